@@ -1,0 +1,136 @@
+/*
+ * seedplane_cuda.h -- C ABI of the B200 (sm_100a) Qwen2 decode engine.
+ *
+ * This is the native boundary that replaces SeedPlane's Vulkan runtime (`qwen_vk`), which the
+ * reference drives through a JSON-lines subprocess (seedplane/native.py:25-90 ->
+ * native/vulkan_decode/qwen_vk.cpp:810-855). Plain pointers and sizes only; no C++ or torch types.
+ *
+ * Conventions
+ *   - Every entry point returns 0 (SP_OK) or a negative SP_ERR_* code; the message of the last
+ *     failure on the calling thread is sp_last_error(). Nothing calls exit() or throws across the
+ *     ABI (the reference aborted the process on Vulkan errors, qwen_vk.cpp:52-53).
+ *   - "dev" pointers are CUDA device pointers on the engine's device; "host" pointers are host
+ *     memory. Token ids and positions are int32, logits fp32.
+ *   - Work is queued on the caller's stream (`stream`, a cudaStream_t; NULL = legacy default
+ *     stream). No call synchronizes the device except where documented.
+ *   - One engine per device. Calls on one engine come from one host thread at a time.
+ *     Engines on different devices are independent and may run concurrently.
+ */
+#ifndef SEEDPLANE_CUDA_H
+#define SEEDPLANE_CUDA_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SP_OK               0
+#define SP_ERR_INVALID     -1   /* bad argument, shape or layout */
+#define SP_ERR_CUDA        -2   /* a CUDA runtime call failed (message names it) */
+#define SP_ERR_CAPACITY    -3   /* KV cache / position / node limit exceeded */
+#define SP_ERR_UNSUPPORTED -4   /* shape not supported by the kernels */
+#define SP_ERR_DEVICE      -5   /* a kernel reported an error status (bounded wait, bad index) */
+
+#define SP_WEIGHTS_F16       0  /* fp16 matrices (seedplane-bundle/2 layout)                    */
+#define SP_WEIGHTS_I8_B32    1  /* int8 matrices + one fp16 scale per 32 inputs along K          */
+
+/* Architecture. Mirrors the `arch` block of a seedplane-bundle/2 manifest
+ * (seedplane/native_bundle.py:129-131) and Qwen2Engine's config reads (qwen_engine.py:44-53). */
+typedef struct sp_config {
+    int32_t layers, hidden, heads, kv_heads, head_dim, intermediate, vocab;
+    int32_t max_positions;     /* RoPE table length (positions are original position ids)      */
+    float   rope_theta, rms_norm_eps;
+    int32_t tied_embeddings;   /* 1: LM head = embedding matrix                                 */
+    int32_t weight_format;     /* SP_WEIGHTS_*                                                  */
+} sp_config;
+
+/* One layer's tensors, device pointers in the bundle-v2 layouts (native_bundle.py:112-120):
+ * row-major [out, in]. qkv_w rows are q (heads*head_dim), then k, then v (kv_heads*head_dim each).
+ * For SP_WEIGHTS_I8_B32 every matrix is int8 and its `_s` pointer holds fp16 scales
+ * [out, in/32]; for SP_WEIGHTS_F16 the `_s` pointers are ignored. */
+typedef struct sp_layer_weights {
+    const void *qkv_w, *qkv_s;   const float *qkv_b;
+    const void *o_w, *o_s;
+    const void *gate_w, *gate_s;
+    const void *up_w, *up_s;
+    const void *down_w, *down_s;
+    const float *in_norm, *post_norm;
+} sp_layer_weights;
+
+typedef struct sp_weights {
+    const void *embed;                 /* [vocab, hidden] fp16, device                          */
+    const void *lm_head, *lm_head_s;   /* untied head (fp16, or int8 + scales); NULL when tied  */
+    const float *final_norm;           /* [hidden] fp32, device                                 */
+    const sp_layer_weights *layers;    /* HOST array of `layers` entries                        */
+    const float *rope_host;            /* optional HOST table [max_positions][head_dim/2][2] of
+                                          (cos, sin) fp32; NULL = computed in double precision  */
+} sp_weights;
+
+typedef struct sp_engine sp_engine;
+typedef struct sp_kv sp_kv;
+
+/* Last error message of the calling thread ("" if none). */
+const char *sp_last_error(void);
+/* Library version string. */
+const char *sp_version(void);
+
+/* Create an engine on `device`. The library copies the weights into its own arena in the packed
+ * layouts its kernels stream (the caller may free its copies on return) and owns all workspace.
+ * Replaces qwen_vk's Engine::init (qwen_vk.cpp:283-342). Synchronizes the device. */
+int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_engine **out);
+void sp_engine_destroy(sp_engine *e);
+/* Bytes of device memory the engine holds (weights arena + workspace). */
+int64_t sp_engine_device_bytes(const sp_engine *e);
+
+/* KV cache of `capacity` slots, fp16 [layers][kv_heads][capacity][head_dim] for K and for V.
+ * Replaces KVCache.allocate / Qwen2Engine.new_cache (qwen_engine.py:18-29,82-85). */
+int sp_kv_create(sp_engine *e, int32_t capacity, sp_kv **out);
+void sp_kv_destroy(sp_kv *kv);
+int32_t sp_kv_length(const sp_kv *kv);
+int32_t sp_kv_capacity(const sp_kv *kv);
+/* Truncate (rollback) the committed length, like `cache.length = n` in the reference's linear
+ * verifier (experiments/hive_scaling/benchmark_speculative.py:119,127). */
+int sp_kv_set_length(sp_kv *kv, int32_t length);
+
+/* Run `n` tokens through the model at cache slots [len, len+n), exactly Qwen2Engine.forward
+ * (qwen_engine.py:105-144): tokens_dev[n] int32, positions_dev[n] int32 RoPE positions (NULL =
+ * the slots). Token i attends to slots [0, len+i]. Advances the cache length by n.
+ * logits_dev: NULL, or fp32 [n][vocab] when all_logits else [vocab] (last token only).
+ * argmax_dev: NULL, or int32 [n] greedy token after each input token (lowest index on ties). */
+int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t *positions_dev,
+               int32_t n, float *logits_dev, int32_t all_logits, int32_t *argmax_dev, void *stream);
+
+/* Greedy decode: feed `token` at position `pos` (slot = current length), then feed back each
+ * argmax on the device, for `n_steps` steps without host round trips. out_tokens_dev[n_steps]
+ * receives the argmax of every step (out[i] is fed at step i+1). logits_dev: NULL or fp32
+ * [vocab] = logits of the last step. Advances the cache length by n_steps. Replaces qwen_vk's
+ * per-token Session::step + argmax loop (qwen_vk.cpp:519-565,588-613). */
+int sp_decode(sp_engine *e, sp_kv *kv, int32_t token, int32_t pos, int32_t n_steps,
+              int32_t *out_tokens_dev, float *logits_dev, void *stream);
+
+/* Speculative tree verification (no counterpart kernel in the reference; semantics of
+ * seedplane/speculative.py:55-92). n nodes in an ancestor-closed order (parent index < own index;
+ * -1 = child of the committed prefix). Node i is written to scratch slot len+i at RoPE position
+ * base_pos + depth_i - 1 and attends to the committed slots [0, len) and to its ancestors and
+ * itself. The cache length is NOT advanced (see sp_kv_commit).
+ * argmax_dev[n]: target argmax after each node. logits_dev: NULL or fp32 [n][vocab]. */
+int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const int32_t *parents_host,
+                   int32_t n, int32_t base_pos, float *logits_dev, int32_t *argmax_dev, void *stream);
+
+/* Move the K/V of accepted scratch slots into place: for i < n, slot src_slots_host[i] is copied
+ * to slot len+i of every layer, then the length becomes len+n. Replaces the reference's KV
+ * rollback by truncation (benchmark_speculative.py:119,127) for tree-shaped drafts. */
+int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stream);
+
+/* Wait for `stream`, then report (and clear) a device-side error status recorded by a kernel since
+ * the last call: SP_ERR_DEVICE with a message, or SP_OK. Kernels never trap; a bad token id, an
+ * out-of-table position or an expired bounded wait is recorded here instead. */
+int sp_device_status(sp_engine *e, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SEEDPLANE_CUDA_H */

@@ -1,0 +1,657 @@
+// Host side of the C ABI (include/seedplane_cuda.h): weight arena and packing, workspace, the
+// per-step kernel chain, CUDA-graph replay of that chain, and the forward / decode / verify /
+// commit entry points.
+//
+// A step is the fixed chain  QKV(l) -> attention(l) -> O(l) -> gate_up(l) -> down(l)  for every
+// layer, then the LM head. All per-step values (token, position, slot, tree mask, output
+// pointers) live in a device-side DevState that the LM head advances, so one captured graph per
+// KV cache serves decode, teacher-forced prefill and tree verification. This replaces qwen_vk's
+// pre-recorded one-token command buffer (native/vulkan_decode/qwen_vk.cpp:349-412) and its
+// per-token submit + fence wait (qwen_vk.cpp:141-147, 519-565).
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/seedplane_cuda.h"
+#include "kernels.cuh"
+
+using namespace sp;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define SP_CUDA(call)                                                                            \
+    do {                                                                                         \
+        cudaError_t e_ = (call);                                                                 \
+        if (e_ != cudaSuccess) return fail(SP_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct LayerDev {
+    const uint8_t *qkv, *o, *gate_up, *down;
+    const __half *qkv_s, *o_s, *gate_up_s, *down_s;
+    const float *qkv_b, *in_norm, *post_norm;
+};
+
+// Stage ring per GEMV CTA. Two CTAs of consecutive kernels share an SM under programmatic
+// dependent launch, so each ring stays below half of the 227 KB shared memory.
+constexpr int kRingBytes = 96 * 1024;
+constexpr int kAttnMaxSplit = 64;
+constexpr int kAttnMinChunk = 32;
+
+}  // namespace
+
+struct sp_kv {
+    sp_engine *e;
+    int32_t capacity;
+    int32_t length;
+    __half *k, *v;
+};
+
+struct sp_engine {
+    sp_config c{};
+    int device = 0;
+    int num_sms = 0;
+    bool pdl = true;
+    bool use_graph = true;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0;
+    uint8_t *ws = nullptr;
+    size_t ws_bytes = 0;
+    const __half *embed = nullptr;
+    const uint8_t *head = nullptr;
+    const __half *head_s = nullptr;
+    int head_fmt = WF_F16;
+    const float *final_norm = nullptr;
+    const float *rope = nullptr;
+    std::vector<LayerDev> layers;
+    // workspace
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *apart = nullptr;
+    unsigned *acnt = nullptr, *lm_cnt = nullptr;
+    float *lm_val = nullptr;
+    int *lm_idx = nullptr;
+    DevState *st = nullptr;
+    // planned GEMV geometry (pointers filled per layer at record time)
+    GemvParams g_qkv{}, g_o{}, g_gu{}, g_down{}, g_head{};
+    cudaStream_t cap_stream = nullptr;
+    std::map<sp_kv *, cudaGraphExec_t> graphs;
+    std::vector<sp_kv *> caches;
+};
+
+namespace {
+
+int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
+    const sp_config &c = e->c;
+    const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
+    for (int l = 0; l < c.layers; ++l) {
+        const LayerDev &L = e->layers[l];
+        LaunchCfg lc{s, e->pdl && l > 0};
+        GemvParams p = e->g_qkv;
+        p.w = L.qkv;
+        p.ws = L.qkv_s;
+        p.xin = e->x;
+        p.gain = L.in_norm;
+        p.bias = L.qkv_b;
+        p.out = e->q;
+        p.kc = kv->k + l * kv_layer;
+        p.vc = kv->v + l * kv_layer;
+        p.cap = kv->capacity;
+        const int pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM;
+        SP_CUDA(launch_gemv(pro, EPI_QKV, p, lc));
+        lc.pdl = e->pdl;
+
+        AttnParams a{};
+        a.q = e->q;
+        a.kc = kv->k + l * kv_layer;
+        a.vc = kv->v + l * kv_layer;
+        a.out = e->attn;
+        a.part = e->apart;
+        a.counter = e->acnt;
+        a.nh = c.heads;
+        a.nkv = c.kv_heads;
+        a.hd = c.head_dim;
+        a.cap = kv->capacity;
+        a.max_split = kAttnMaxSplit;
+        a.min_chunk = kAttnMinChunk;
+        a.scale = 1.0f / sqrtf((float)c.head_dim);
+        a.st = e->st;
+        SP_CUDA(launch_attention(a, lc));
+
+        p = e->g_o;
+        p.w = L.o;
+        p.ws = L.o_s;
+        p.xin = e->attn;
+        p.out = e->x;
+        SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
+
+        p = e->g_gu;
+        p.w = L.gate_up;
+        p.ws = L.gate_up_s;
+        p.xin = e->x;
+        p.gain = L.post_norm;
+        p.out = e->act;
+        SP_CUDA(launch_gemv(PRO_NORM, EPI_SWIGLU, p, lc));
+
+        p = e->g_down;
+        p.w = L.down;
+        p.ws = L.down_s;
+        p.xin = e->act;
+        p.out = e->x;
+        SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
+    }
+    LaunchCfg lc{s, e->pdl};
+    GemvParams p = e->g_head;
+    p.xin = e->x;
+    p.gain = e->final_norm;
+    SP_CUDA(launch_gemv(PRO_NORM, EPI_LMHEAD, p, lc));
+    return SP_OK;
+}
+
+int get_graph(sp_engine *e, sp_kv *kv, cudaGraphExec_t *out) {
+    auto it = e->graphs.find(kv);
+    if (it != e->graphs.end()) {
+        *out = it->second;
+        return SP_OK;
+    }
+    cudaGraph_t g = nullptr;
+    SP_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(e, kv, e->cap_stream);
+    cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
+    if (rc != SP_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+    e->graphs[kv] = ex;
+    *out = ex;
+    return SP_OK;
+}
+
+int run_steps(sp_engine *e, sp_kv *kv, const DevState &init, int n, cudaStream_t s) {
+    SP_CUDA(launch_set_state(e->st, init, s));
+    if (e->use_graph) {
+        cudaGraphExec_t ex;
+        int rc = get_graph(e, kv, &ex);
+        if (rc != SP_OK) return rc;
+        for (int i = 0; i < n; ++i) SP_CUDA(cudaGraphLaunch(ex, s));
+    } else {
+        for (int i = 0; i < n; ++i) {
+            int rc = record_step(e, kv, s);
+            if (rc != SP_OK) return rc;
+        }
+    }
+    return SP_OK;
+}
+
+DevState base_state() {
+    DevState d;
+    memset(&d, 0, sizeof(d));
+    d.tree_base = 0x7fffffff;
+    return d;
+}
+
+bool env_flag(const char *name, bool dflt) {
+    const char *v = getenv(name);
+    if (!v || !*v) return dflt;
+    return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *sp_last_error(void) { return g_err.c_str(); }
+
+const char *sp_version(void) { return "seedplane-b200 0.1 (sm_100a)"; }
+
+int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_engine **out) {
+    if (!cfg || !w || !out) return fail(SP_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const sp_config c = *cfg;
+    if (c.layers <= 0 || c.hidden <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.vocab <= 0 || c.intermediate <= 0)
+        return fail(SP_ERR_INVALID, "non-positive dimension in config");
+    if (c.hidden % c.heads || c.heads % c.kv_heads || c.head_dim != c.hidden / c.heads)
+        return fail(SP_ERR_INVALID, "invalid Qwen2 head configuration");
+    if (c.head_dim != 64 && c.head_dim != 128) return fail(SP_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (c.heads / c.kv_heads > 8) return fail(SP_ERR_UNSUPPORTED, "more than 8 q heads per kv head");
+    if (c.hidden % 16 || c.intermediate % 16) return fail(SP_ERR_UNSUPPORTED, "hidden/intermediate must be multiples of 16");
+    if (c.weight_format == SP_WEIGHTS_I8_B32 && (c.hidden % 256 || c.intermediate % 256))
+        return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights need hidden/intermediate multiples of 256");
+    if (c.weight_format != SP_WEIGHTS_F16 && c.weight_format != SP_WEIGHTS_I8_B32)
+        return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
+    if (c.max_positions <= 0) return fail(SP_ERR_INVALID, "max_positions must be positive");
+    if (!w->embed || !w->final_norm || !w->layers) return fail(SP_ERR_INVALID, "missing tensors");
+    if (!c.tied_embeddings && !w->lm_head) return fail(SP_ERR_INVALID, "untied model without lm_head");
+
+    SP_CUDA(cudaSetDevice(device));
+    sp_engine *e = new sp_engine();
+    e->c = c;
+    e->device = device;
+    e->pdl = env_flag("SEEDPLANE_PDL", true);
+    e->use_graph = env_flag("SEEDPLANE_GRAPH", true);
+    cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
+
+    const int H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
+    const int QR = (c.heads + 2 * c.kv_heads) * HD;
+    const bool i8 = c.weight_format == SP_WEIGHTS_I8_B32;
+    const size_t eb = i8 ? 1 : 2;
+    // ---- arena layout ------------------------------------------------------------------------
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+    const size_t o_embed = take((size_t)V * H * 2);
+    size_t o_head = 0, o_head_s = 0;
+    if (!c.tied_embeddings) {
+        o_head = take((size_t)V * H * eb);
+        if (i8) o_head_s = take((size_t)V * (H / 32) * 2);
+    }
+    const size_t o_fnorm = take((size_t)H * 4);
+    const size_t o_rope = take((size_t)c.max_positions * (HD / 2) * 2 * 4);
+    struct LOff { size_t qkv, qkv_s, qkv_b, o, o_s, gu, gu_s, dn, dn_s, inn, post; };
+    std::vector<LOff> lo(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        lo[l].qkv = take((size_t)QR * H * eb);
+        lo[l].qkv_s = i8 ? take((size_t)QR * (H / 32) * 2) : 0;
+        lo[l].qkv_b = take((size_t)QR * 4);
+        lo[l].o = take((size_t)H * H * eb);
+        lo[l].o_s = i8 ? take((size_t)H * (H / 32) * 2) : 0;
+        lo[l].gu = take((size_t)2 * I * H * eb);
+        lo[l].gu_s = i8 ? take((size_t)2 * I * (H / 32) * 2) : 0;
+        lo[l].dn = take((size_t)H * I * eb);
+        lo[l].dn_s = i8 ? take((size_t)H * (I / 32) * 2) : 0;
+        lo[l].inn = take((size_t)H * 4);
+        lo[l].post = take((size_t)H * 4);
+    }
+    e->arena_bytes = off;
+    cudaError_t ce = cudaMalloc(&e->arena, e->arena_bytes);
+    if (ce != cudaSuccess) {
+        delete e;
+        return fail(SP_ERR_CUDA, "weight arena of %zu bytes: %s", off, cudaGetErrorString(ce));
+    }
+    uint8_t *A = e->arena;
+    cudaStream_t s = nullptr;
+    int rc = SP_OK;
+    int *d_perm = nullptr, *d_iota = nullptr;
+    auto bail = [&](int code) { cudaFree(d_perm); cudaFree(d_iota); if (s) cudaStreamDestroy(s); sp_engine_destroy(e); return code; };
+#define SP_TRY(call)                                                                                 \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return bail(fail(SP_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_))); \
+    } while (0)
+    SP_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    // ---- pack -----------------------------------------------------------------------------
+    // QKV rows are reordered so that the two rows of a RoPE pair (d, d + head_dim/2) of a head
+    // are adjacent: packed row hh*HD + 2*j + t  <-  fused row hh*HD + j + t*HD/2.
+    std::vector<int> perm(QR), iota(std::max(I, QR));
+    for (int r = 0; r < QR; ++r) {
+        const int hh = r / HD, j = r % HD;
+        perm[r] = hh * HD + (j / 2) + (j % 2) * (HD / 2);
+    }
+    for (size_t i = 0; i < iota.size(); ++i) iota[i] = (int)i;
+    SP_TRY(cudaMalloc(&d_perm, perm.size() * 4));
+    SP_TRY(cudaMalloc(&d_iota, iota.size() * 4));
+    SP_TRY(cudaMemcpy(d_perm, perm.data(), perm.size() * 4, cudaMemcpyHostToDevice));
+    SP_TRY(cudaMemcpy(d_iota, iota.data(), iota.size() * 4, cudaMemcpyHostToDevice));
+    SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, (size_t)V * H * 2, cudaMemcpyDeviceToDevice, s));
+    if (!c.tied_embeddings) {
+        SP_TRY(cudaMemcpyAsync(A + o_head, w->lm_head, (size_t)V * H * eb, cudaMemcpyDeviceToDevice, s));
+        if (i8) {
+            if (!w->lm_head_s) return bail(fail(SP_ERR_INVALID, "int8 lm_head without scales"));
+            SP_TRY(cudaMemcpyAsync(A + o_head_s, w->lm_head_s, (size_t)V * (H / 32) * 2, cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+    for (int l = 0; l < c.layers; ++l) {
+        const sp_layer_weights &Lw = w->layers[l];
+        if (!Lw.qkv_w || !Lw.qkv_b || !Lw.o_w || !Lw.gate_w || !Lw.up_w || !Lw.down_w || !Lw.in_norm || !Lw.post_norm)
+            return bail(fail(SP_ERR_INVALID, "layer %d: missing tensor", l));
+        if (i8 && (!Lw.qkv_s || !Lw.o_s || !Lw.gate_s || !Lw.up_s || !Lw.down_s))
+            return bail(fail(SP_ERR_INVALID, "layer %d: int8 matrix without scales", l));
+        const uint8_t *src;
+        SP_TRY(launch_gather_rows(A + lo[l].qkv, (const uint8_t *)Lw.qkv_w, d_perm, QR, (int)(H * eb), 1, 0, s));
+        SP_TRY(launch_gather_rows(A + lo[l].gu, (const uint8_t *)Lw.gate_w, d_iota, I, (int)(H * eb), 2, 0, s));
+        SP_TRY(launch_gather_rows(A + lo[l].gu, (const uint8_t *)Lw.up_w, d_iota, I, (int)(H * eb), 2, 1, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].o, Lw.o_w, (size_t)H * H * eb, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].dn, Lw.down_w, (size_t)H * I * eb, cudaMemcpyDeviceToDevice, s));
+        if (i8) {
+            const int srH = (H / 32) * 2, srI = (I / 32) * 2;
+            SP_TRY(launch_gather_rows(A + lo[l].qkv_s, (const uint8_t *)Lw.qkv_s, d_perm, QR, srH, 1, 0, s));
+            SP_TRY(launch_gather_rows(A + lo[l].gu_s, (const uint8_t *)Lw.gate_s, d_iota, I, srH, 2, 0, s));
+            SP_TRY(launch_gather_rows(A + lo[l].gu_s, (const uint8_t *)Lw.up_s, d_iota, I, srH, 2, 1, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].o_s, Lw.o_s, (size_t)H * srH, cudaMemcpyDeviceToDevice, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].dn_s, Lw.down_s, (size_t)H * srI, cudaMemcpyDeviceToDevice, s));
+        }
+        src = (const uint8_t *)Lw.qkv_b;
+        SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, src, (size_t)QR * 4, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+        LayerDev L;
+        L.qkv = A + lo[l].qkv;
+        L.o = A + lo[l].o;
+        L.gate_up = A + lo[l].gu;
+        L.down = A + lo[l].dn;
+        L.qkv_s = i8 ? (const __half *)(A + lo[l].qkv_s) : nullptr;
+        L.o_s = i8 ? (const __half *)(A + lo[l].o_s) : nullptr;
+        L.gate_up_s = i8 ? (const __half *)(A + lo[l].gu_s) : nullptr;
+        L.down_s = i8 ? (const __half *)(A + lo[l].dn_s) : nullptr;
+        L.qkv_b = (const float *)(A + lo[l].qkv_b);
+        L.in_norm = (const float *)(A + lo[l].inn);
+        L.post_norm = (const float *)(A + lo[l].post);
+        e->layers.push_back(L);
+    }
+    // RoPE table: the caller's (computed like the reference, qwen_engine.py:52,99-103), else double precision.
+    {
+        std::vector<float> rope;
+        const float *host = w->rope_host;
+        if (!host) {
+            rope.resize((size_t)c.max_positions * (HD / 2) * 2);
+            for (int pos = 0; pos < c.max_positions; ++pos)
+                for (int i = 0; i < HD / 2; ++i) {
+                    const float inv = (float)(1.0 / pow((double)c.rope_theta, (double)(2 * i) / (double)HD));
+                    const float ph = (float)pos * inv;
+                    rope[((size_t)pos * (HD / 2) + i) * 2] = (float)cos((double)ph);
+                    rope[((size_t)pos * (HD / 2) + i) * 2 + 1] = (float)sin((double)ph);
+                }
+            host = rope.data();
+        }
+        SP_TRY(cudaMemcpy(A + o_rope, host, (size_t)c.max_positions * (HD / 2) * 2 * 4, cudaMemcpyHostToDevice));
+    }
+    SP_TRY(cudaStreamSynchronize(s));
+    cudaFree(d_perm);
+    cudaFree(d_iota);
+    d_perm = d_iota = nullptr;
+    e->embed = (const __half *)(A + o_embed);
+    e->final_norm = (const float *)(A + o_fnorm);
+    e->rope = (const float *)(A + o_rope);
+    if (c.tied_embeddings) {
+        e->head = A + o_embed;
+        e->head_fmt = WF_F16;
+    } else {
+        e->head = A + o_head;
+        e->head_s = i8 ? (const __half *)(A + o_head_s) : nullptr;
+        e->head_fmt = i8 ? WF_I8 : WF_F16;
+    }
+
+    // ---- GEMV plans -------------------------------------------------------------------------
+    const int fmt = i8 ? WF_I8 : WF_F16;
+    auto base = [&](int N, int K, int f) {
+        GemvParams p{};
+        p.N = N;
+        p.K = K;
+        p.fmt = f;
+        p.eps = c.rms_norm_eps;
+        p.vocab = V;
+        p.rope = e->rope;
+        p.max_pos = c.max_positions;
+        p.nh = c.heads;
+        p.nkv = c.kv_heads;
+        p.hd = HD;
+        return p;
+    };
+    e->g_qkv = base(QR, H, fmt);
+    plan_gemv(e->g_qkv, 2, e->num_sms, kRingBytes);
+    e->g_o = base(H, H, fmt);
+    plan_gemv(e->g_o, 1, e->num_sms, kRingBytes);
+    e->g_gu = base(2 * I, H, fmt);
+    plan_gemv(e->g_gu, 2, e->num_sms, kRingBytes);
+    e->g_down = base(H, I, fmt);
+    plan_gemv(e->g_down, 1, e->num_sms, kRingBytes);
+    e->g_head = base(V, H, e->head_fmt);
+    plan_gemv(e->g_head, 1, e->num_sms, kRingBytes);
+
+    // ---- workspace ------------------------------------------------------------------------
+    size_t woff = 0;
+    auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
+    const size_t w_x = wtake((size_t)H * 4), w_q = wtake((size_t)c.heads * HD * 4);
+    const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake((size_t)I * 4);
+    const size_t w_apart = wtake((size_t)c.heads * kAttnMaxSplit * (HD + 2) * 4);
+    const size_t w_acnt = wtake((size_t)c.kv_heads * 4), w_lmcnt = wtake(4);
+    const size_t w_lmval = wtake((size_t)e->g_head.grid * 4), w_lmidx = wtake((size_t)e->g_head.grid * 4);
+    const size_t w_st = wtake(sizeof(DevState));
+    e->ws_bytes = woff;
+    SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
+    SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
+    e->x = (float *)(e->ws + w_x);
+    e->q = (float *)(e->ws + w_q);
+    e->attn = (float *)(e->ws + w_attn);
+    e->act = (float *)(e->ws + w_act);
+    e->apart = (float *)(e->ws + w_apart);
+    e->acnt = (unsigned *)(e->ws + w_acnt);
+    e->lm_cnt = (unsigned *)(e->ws + w_lmcnt);
+    e->lm_val = (float *)(e->ws + w_lmval);
+    e->lm_idx = (int *)(e->ws + w_lmidx);
+    e->st = (DevState *)(e->ws + w_st);
+    e->g_head.w = e->head;
+    e->g_head.ws = e->head_s;
+    e->g_head.part_val = e->lm_val;
+    e->g_head.part_idx = e->lm_idx;
+    e->g_head.counter = e->lm_cnt;
+    for (GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head}) p->st = e->st;
+    e->g_qkv.embed = e->embed;
+    e->g_qkv.x_init = e->x;
+    SP_TRY(prepare_gemv(PRO_NORM, EPI_QKV, e->g_qkv));
+    SP_TRY(prepare_gemv(PRO_EMBED_NORM, EPI_QKV, e->g_qkv));
+    SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_o));
+    SP_TRY(prepare_gemv(PRO_NORM, EPI_SWIGLU, e->g_gu));
+    SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_down));
+    SP_TRY(prepare_gemv(PRO_NORM, EPI_LMHEAD, e->g_head));
+    for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
+        if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
+    e->cap_stream = s;
+    s = nullptr;
+    (void)rc;
+#undef SP_TRY
+    *out = e;
+    return SP_OK;
+}
+
+void sp_engine_destroy(sp_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (sp_kv *kv : e->caches) kv->e = nullptr;
+    if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+    cudaFree(e->arena);
+    cudaFree(e->ws);
+    delete e;
+}
+
+int64_t sp_engine_device_bytes(const sp_engine *e) { return e ? (int64_t)(e->arena_bytes + e->ws_bytes) : 0; }
+
+int sp_kv_create(sp_engine *e, int32_t capacity, sp_kv **out) {
+    if (!e || !out) return fail(SP_ERR_INVALID, "null argument");
+    if (capacity < 1) return fail(SP_ERR_INVALID, "cache capacity must be positive");
+    SP_CUDA(cudaSetDevice(e->device));
+    const size_t n = (size_t)e->c.layers * e->c.kv_heads * capacity * e->c.head_dim;
+    sp_kv *kv = new sp_kv();
+    kv->e = e;
+    kv->capacity = capacity;
+    kv->length = 0;
+    cudaError_t ce = cudaMalloc(&kv->k, n * 2);
+    if (ce == cudaSuccess) ce = cudaMalloc(&kv->v, n * 2);
+    if (ce == cudaSuccess) ce = cudaMemset(kv->k, 0, n * 2);
+    if (ce == cudaSuccess) ce = cudaMemset(kv->v, 0, n * 2);
+    if (ce != cudaSuccess) {
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+        delete kv;
+        return fail(SP_ERR_CUDA, "KV cache of %d slots: %s", capacity, cudaGetErrorString(ce));
+    }
+    e->caches.push_back(kv);
+    *out = kv;
+    return SP_OK;
+}
+
+void sp_kv_destroy(sp_kv *kv) {
+    if (!kv) return;
+    if (kv->e) {
+        sp_engine *e = kv->e;
+        cudaSetDevice(e->device);
+        auto it = e->graphs.find(kv);
+        if (it != e->graphs.end()) {
+            cudaGraphExecDestroy(it->second);
+            e->graphs.erase(it);
+        }
+        for (size_t i = 0; i < e->caches.size(); ++i)
+            if (e->caches[i] == kv) { e->caches.erase(e->caches.begin() + i); break; }
+    }
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+}
+
+int32_t sp_kv_length(const sp_kv *kv) { return kv ? kv->length : -1; }
+int32_t sp_kv_capacity(const sp_kv *kv) { return kv ? kv->capacity : -1; }
+
+int sp_kv_set_length(sp_kv *kv, int32_t length) {
+    if (!kv) return fail(SP_ERR_INVALID, "null cache");
+    if (length < 0 || length > kv->capacity) return fail(SP_ERR_CAPACITY, "length %d outside [0, %d]", length, kv->capacity);
+    kv->length = length;
+    return SP_OK;
+}
+
+static int check_engine_kv(sp_engine *e, sp_kv *kv) {
+    if (!e || !kv) return fail(SP_ERR_INVALID, "null engine or cache");
+    if (kv->e != e) return fail(SP_ERR_INVALID, "cache belongs to another engine");
+    cudaError_t ce = cudaSetDevice(e->device);
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(ce));
+    return SP_OK;
+}
+
+int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t *positions_dev, int32_t n,
+               float *logits_dev, int32_t all_logits, int32_t *argmax_dev, void *stream) {
+    int rc = check_engine_kv(e, kv);
+    if (rc) return rc;
+    if (n <= 0 || !tokens_dev) return fail(SP_ERR_INVALID, "input_ids cannot be empty");
+    if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    DevState d = base_state();
+    d.n_forced = n;
+    d.slot0 = kv->length;
+    d.slot = kv->length;
+    d.f_tok = tokens_dev;
+    d.f_pos = positions_dev;
+    d.logits = logits_dev;
+    d.logits_stride = all_logits ? (long long)e->c.vocab : 0;
+    d.logits_from = all_logits ? 0 : n - 1;
+    d.out_tokens = argmax_dev;
+    rc = run_steps(e, kv, d, n, (cudaStream_t)stream);
+    if (rc) return rc;
+    kv->length += n;
+    return SP_OK;
+}
+
+int sp_decode(sp_engine *e, sp_kv *kv, int32_t token, int32_t pos, int32_t n_steps, int32_t *out_tokens_dev,
+              float *logits_dev, void *stream) {
+    int rc = check_engine_kv(e, kv);
+    if (rc) return rc;
+    if (n_steps <= 0) return fail(SP_ERR_INVALID, "n_steps must be positive");
+    if (token < 0 || token >= e->c.vocab) return fail(SP_ERR_INVALID, "token %d outside the vocabulary", token);
+    if (kv->length + n_steps > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    if (pos < 0 || pos + n_steps > e->c.max_positions)
+        return fail(SP_ERR_CAPACITY, "positions %d..%d outside the RoPE table", pos, pos + n_steps - 1);
+    DevState d = base_state();
+    d.token = token;
+    d.pos = pos;
+    d.slot = kv->length;
+    d.slot0 = kv->length;
+    d.logits = logits_dev;
+    d.logits_from = n_steps - 1;
+    d.out_tokens = out_tokens_dev;
+    rc = run_steps(e, kv, d, n_steps, (cudaStream_t)stream);
+    if (rc) return rc;
+    kv->length += n_steps;
+    return SP_OK;
+}
+
+int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
+                   int32_t base_pos, float *logits_dev, int32_t *argmax_dev, void *stream) {
+    int rc = check_engine_kv(e, kv);
+    if (rc) return rc;
+    if (n <= 0 || !tokens_host || !parents_host) return fail(SP_ERR_INVALID, "empty tree");
+    if (n > kSmallNodes) return fail(SP_ERR_CAPACITY, "tree of %d nodes exceeds %d", n, kSmallNodes);
+    if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    DevState d = base_state();
+    int depth[kSmallNodes];
+    for (int i = 0; i < n; ++i) {
+        const int par = parents_host[i];
+        if (par >= i || par < -1) return fail(SP_ERR_INVALID, "node %d: parent %d is not an earlier node", i, par);
+        if (tokens_host[i] < 0 || tokens_host[i] >= e->c.vocab) return fail(SP_ERR_INVALID, "node %d: bad token", i);
+        depth[i] = par < 0 ? 1 : depth[par] + 1;
+        d.small_mask[i] = (par < 0 ? 0ull : d.small_mask[par]) | (1ull << i);
+        d.small_tok[i] = tokens_host[i];
+        d.small_pos[i] = base_pos + depth[i] - 1;
+        if (d.small_pos[i] < 0 || d.small_pos[i] >= e->c.max_positions)
+            return fail(SP_ERR_CAPACITY, "node %d: position outside the RoPE table", i);
+    }
+    d.use_small = 1;
+    d.n_forced = n;
+    d.slot0 = kv->length;
+    d.tree_base = kv->length;
+    d.token = d.small_tok[0];
+    d.pos = d.small_pos[0];
+    d.slot = kv->length;
+    d.logits = logits_dev;
+    d.logits_stride = e->c.vocab;
+    d.out_tokens = argmax_dev;
+    return run_steps(e, kv, d, n, (cudaStream_t)stream);
+}
+
+int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stream) {
+    if (!kv || !kv->e) return fail(SP_ERR_INVALID, "null or orphaned cache");
+    if (n < 0 || n > kSmallNodes) return fail(SP_ERR_CAPACITY, "commit of %d slots", n);
+    if (n == 0) return SP_OK;
+    if (!src_slots_host) return fail(SP_ERR_INVALID, "null slot list");
+    if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    for (int i = 0; i < n; ++i) {
+        if (src_slots_host[i] < kv->length + i || src_slots_host[i] >= kv->capacity)
+            return fail(SP_ERR_INVALID, "commit slot %d = %d outside [len+i, capacity)", i, src_slots_host[i]);
+        if (i && src_slots_host[i] <= src_slots_host[i - 1])
+            return fail(SP_ERR_INVALID, "commit slots must be increasing");
+    }
+    sp_engine *e = kv->e;
+    SP_CUDA(cudaSetDevice(e->device));
+    SP_CUDA(launch_kv_commit(kv->k, kv->v, e->c.layers, e->c.kv_heads, kv->capacity, e->c.head_dim, src_slots_host, n,
+                             kv->length, (cudaStream_t)stream));
+    kv->length += n;
+    return SP_OK;
+}
+
+int sp_device_status(sp_engine *e, void *stream) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    SP_CUDA(cudaSetDevice(e->device));
+    int err = 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    SP_CUDA(cudaMemcpyAsync(&err, &e->st->err, 4, cudaMemcpyDeviceToHost, s));
+    SP_CUDA(cudaStreamSynchronize(s));
+    if (err) {
+        SP_CUDA(cudaMemsetAsync(&e->st->err, 0, 4, s));
+        SP_CUDA(cudaStreamSynchronize(s));
+        const char *what = err == kErrMbarTimeout ? "a weight stage never arrived (bounded wait expired)"
+                         : err == kErrBadToken    ? "token id outside the vocabulary"
+                         : err == kErrBadSlot     ? "position or slot outside its table"
+                                                  : "unknown";
+        return fail(SP_ERR_DEVICE, "device error %d: %s", err, what);
+    }
+    return SP_OK;
+}
+
+}  // extern "C"
