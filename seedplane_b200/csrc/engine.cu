@@ -8,7 +8,9 @@
 // KV cache serves decode, teacher-forced prefill and tree verification. This replaces qwen_vk's
 // pre-recorded one-token command buffer (native/vulkan_decode/qwen_vk.cpp:349-412) and its
 // per-token submit + fence wait (qwen_vk.cpp:141-147, 519-565).
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -44,14 +46,15 @@ int fail(int code, const char *fmt, ...) {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct LayerDev {
-    const uint8_t *qkv, *o, *gate_up, *down;
-    const __half *qkv_s, *o_s, *gate_up_s, *down_s;
+    const uint8_t *qkv, *o, *gate_up, *down;       // fragment-packed fp16, contiguous in the stream
     const float *qkv_b, *in_norm, *post_norm;
+    size_t off_qkv, off_o, off_gu, off_dn;          // offsets in the weight stream
 };
 
-// Stage ring per GEMV CTA. Two CTAs of consecutive kernels share an SM under programmatic
-// dependent launch, so each ring stays below half of the 227 KB shared memory.
-constexpr int kRingBytes = 96 * 1024;
+// Stage ring per GEMV CTA. CTAs of consecutive kernels share an SM under programmatic dependent
+// launch, so ring + input fragments stay near half of the 227 KB of shared memory.
+constexpr int kRingBytes = 80 * 1024;
+constexpr int kMaxUnitBytes = 32 * 1024;
 constexpr int kAttnMaxSplit = 64;
 constexpr int kAttnMinChunk = 32;
 
@@ -74,15 +77,22 @@ struct sp_engine {
     size_t arena_bytes = 0;
     uint8_t *ws = nullptr;
     size_t ws_bytes = 0;
-    const __half *embed = nullptr;
-    const uint8_t *head = nullptr;
-    const __half *head_s = nullptr;
-    int head_fmt = WF_F16;
+    // The per-token weight stream: every layer's [qkv | o | gate_up | down], then the LM head, in
+    // consumption order and contiguous, so prefetching "D bytes ahead" is one address window.
+    const uint8_t *stream = nullptr;
+    size_t stream_bytes = 0;
+    size_t prefetch_ahead = 0;
+    bool evict_first = false;
+    const __half *embed = nullptr;          // row-major embedding (token gathers)
+    const uint8_t *head = nullptr;          // fragment-packed LM head (tied: a packed copy of embed)
+    size_t off_head = 0;
     const float *final_norm = nullptr;
     const float *rope = nullptr;
     std::vector<LayerDev> layers;
     // workspace
     float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *apart = nullptr;
+    float *partial = nullptr;
+    unsigned *strip_cnt = nullptr;
     unsigned *acnt = nullptr, *lm_cnt = nullptr;
     float *lm_val = nullptr;
     int *lm_idx = nullptr;
@@ -96,15 +106,33 @@ struct sp_engine {
 
 namespace {
 
+// L2 prefetch window of a kernel that streams [off, off + bytes) of the weight stream: the same
+// number of bytes, `prefetch_ahead` further on (wrapping into the next token's first layers).
+void set_prefetch(const sp_engine *e, GemvParams &p, size_t off, size_t bytes) {
+    p.pf_n = 0;
+    p.evict_first = e->evict_first ? 1 : 0;
+    if (!e->prefetch_ahead || !e->stream_bytes) return;
+    size_t beg = (off + e->prefetch_ahead) % e->stream_bytes;
+    size_t left = std::min(bytes, e->stream_bytes);
+    while (left && p.pf_n < kMaxPrefetch) {
+        const size_t n = std::min(left, e->stream_bytes - beg);
+        p.pf_ptr[p.pf_n] = e->stream + beg;
+        p.pf_bytes[p.pf_n] = n;
+        ++p.pf_n;
+        left -= n;
+        beg = 0;
+    }
+}
+
 int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     const sp_config &c = e->c;
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
+    const size_t H = c.hidden, I = c.intermediate, QR = (size_t)(c.heads + 2 * c.kv_heads) * c.head_dim;
     for (int l = 0; l < c.layers; ++l) {
         const LayerDev &L = e->layers[l];
         LaunchCfg lc{s, e->pdl && l > 0};
         GemvParams p = e->g_qkv;
         p.w = L.qkv;
-        p.ws = L.qkv_s;
         p.xin = e->x;
         p.gain = L.in_norm;
         p.bias = L.qkv_b;
@@ -112,6 +140,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.kc = kv->k + l * kv_layer;
         p.vc = kv->v + l * kv_layer;
         p.cap = kv->capacity;
+        set_prefetch(e, p, L.off_qkv, QR * H * 2);
         const int pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM;
         SP_CUDA(launch_gemv(pro, EPI_QKV, p, lc));
         lc.pdl = e->pdl;
@@ -135,30 +164,31 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
 
         p = e->g_o;
         p.w = L.o;
-        p.ws = L.o_s;
         p.xin = e->attn;
         p.out = e->x;
+        set_prefetch(e, p, L.off_o, H * H * 2);
         SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
 
         p = e->g_gu;
         p.w = L.gate_up;
-        p.ws = L.gate_up_s;
         p.xin = e->x;
         p.gain = L.post_norm;
         p.out = e->act;
+        set_prefetch(e, p, L.off_gu, 2 * I * H * 2);
         SP_CUDA(launch_gemv(PRO_NORM, EPI_SWIGLU, p, lc));
 
         p = e->g_down;
         p.w = L.down;
-        p.ws = L.down_s;
         p.xin = e->act;
         p.out = e->x;
+        set_prefetch(e, p, L.off_dn, H * I * 2);
         SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
     }
     LaunchCfg lc{s, e->pdl};
     GemvParams p = e->g_head;
     p.xin = e->x;
     p.gain = e->final_norm;
+    set_prefetch(e, p, e->off_head, (size_t)c.vocab * H * 2);
     SP_CUDA(launch_gemv(PRO_NORM, EPI_LMHEAD, p, lc));
     return SP_OK;
 }
@@ -216,13 +246,19 @@ bool env_flag(const char *name, bool dflt) {
     return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
 }
 
+long env_long(const char *name, long dflt) {
+    const char *v = getenv(name);
+    if (!v || !*v) return dflt;
+    return strtol(v, nullptr, 10);
+}
+
 }  // namespace
 
 extern "C" {
 
 const char *sp_last_error(void) { return g_err.c_str(); }
 
-const char *sp_version(void) { return "seedplane-b200 0.1 (sm_100a)"; }
+const char *sp_version(void) { return "seedplane-b200 0.2 (sm_100a)"; }
 
 int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_engine **out) {
     if (!cfg || !w || !out) return fail(SP_ERR_INVALID, "null argument");
@@ -234,14 +270,19 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         return fail(SP_ERR_INVALID, "invalid Qwen2 head configuration");
     if (c.head_dim != 64 && c.head_dim != 128) return fail(SP_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
     if (c.heads / c.kv_heads > 8) return fail(SP_ERR_UNSUPPORTED, "more than 8 q heads per kv head");
-    if (c.hidden % 16 || c.intermediate % 16) return fail(SP_ERR_UNSUPPORTED, "hidden/intermediate must be multiples of 16");
-    if (c.weight_format == SP_WEIGHTS_I8_B32 && (c.hidden % 256 || c.intermediate % 256))
-        return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights need hidden/intermediate multiples of 256");
-    if (c.weight_format != SP_WEIGHTS_F16 && c.weight_format != SP_WEIGHTS_I8_B32)
-        return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
+    if (c.hidden % 16 || c.intermediate % 16 || c.vocab % 16)
+        return fail(SP_ERR_UNSUPPORTED, "hidden, intermediate and vocab must be multiples of 16");
+    if (c.weight_format == SP_WEIGHTS_I8_B32)
+        return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights are not built in this version");
+    if (c.weight_format != SP_WEIGHTS_F16) return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
     if (c.max_positions <= 0) return fail(SP_ERR_INVALID, "max_positions must be positive");
     if (!w->embed || !w->final_norm || !w->layers) return fail(SP_ERR_INVALID, "missing tensors");
     if (!c.tied_embeddings && !w->lm_head) return fail(SP_ERR_INVALID, "untied model without lm_head");
+    for (int l = 0; l < c.layers; ++l) {
+        const sp_layer_weights &Lw = w->layers[l];
+        if (!Lw.qkv_w || !Lw.qkv_b || !Lw.o_w || !Lw.gate_w || !Lw.up_w || !Lw.down_w || !Lw.in_norm || !Lw.post_norm)
+            return fail(SP_ERR_INVALID, "layer %d: missing tensor", l);
+    }
 
     SP_CUDA(cudaSetDevice(device));
     sp_engine *e = new sp_engine();
@@ -249,37 +290,32 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->device = device;
     e->pdl = env_flag("SEEDPLANE_PDL", true);
     e->use_graph = env_flag("SEEDPLANE_GRAPH", true);
+    e->prefetch_ahead = (size_t)std::max(0L, env_long("SEEDPLANE_L2_PREFETCH_MB", 0)) << 20;
+    e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", false);
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
-    const int H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
-    const int QR = (c.heads + 2 * c.kv_heads) * HD;
-    const bool i8 = c.weight_format == SP_WEIGHTS_I8_B32;
-    const size_t eb = i8 ? 1 : 2;
-    // ---- arena layout ------------------------------------------------------------------------
+    const size_t H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
+    const size_t QR = (size_t)(c.heads + 2 * c.kv_heads) * HD;
+    // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
-    const size_t o_embed = take((size_t)V * H * 2);
-    size_t o_head = 0, o_head_s = 0;
-    if (!c.tied_embeddings) {
-        o_head = take((size_t)V * H * eb);
-        if (i8) o_head_s = take((size_t)V * (H / 32) * 2);
-    }
-    const size_t o_fnorm = take((size_t)H * 4);
-    const size_t o_rope = take((size_t)c.max_positions * (HD / 2) * 2 * 4);
-    struct LOff { size_t qkv, qkv_s, qkv_b, o, o_s, gu, gu_s, dn, dn_s, inn, post; };
+    struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post; };
     std::vector<LOff> lo(c.layers);
+    for (int l = 0; l < c.layers; ++l) {     // matrix sizes are multiples of 512 B: no gaps
+        lo[l].qkv = take(QR * H * 2);
+        lo[l].o = take(H * H * 2);
+        lo[l].gu = take(2 * I * H * 2);
+        lo[l].dn = take(H * I * 2);
+    }
+    const size_t o_head = take(V * H * 2);
+    const size_t stream_end = off;
+    const size_t o_embed = take(V * H * 2);
+    const size_t o_fnorm = take(H * 4);
+    const size_t o_rope = take((size_t)c.max_positions * (HD / 2) * 2 * 4);
     for (int l = 0; l < c.layers; ++l) {
-        lo[l].qkv = take((size_t)QR * H * eb);
-        lo[l].qkv_s = i8 ? take((size_t)QR * (H / 32) * 2) : 0;
-        lo[l].qkv_b = take((size_t)QR * 4);
-        lo[l].o = take((size_t)H * H * eb);
-        lo[l].o_s = i8 ? take((size_t)H * (H / 32) * 2) : 0;
-        lo[l].gu = take((size_t)2 * I * H * eb);
-        lo[l].gu_s = i8 ? take((size_t)2 * I * (H / 32) * 2) : 0;
-        lo[l].dn = take((size_t)H * I * eb);
-        lo[l].dn_s = i8 ? take((size_t)H * (I / 32) * 2) : 0;
-        lo[l].inn = take((size_t)H * 4);
-        lo[l].post = take((size_t)H * 4);
+        lo[l].qkv_b = take(QR * 4);
+        lo[l].inn = take(H * 4);
+        lo[l].post = take(H * 4);
     }
     e->arena_bytes = off;
     cudaError_t ce = cudaMalloc(&e->arena, e->arena_bytes);
@@ -289,73 +325,58 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     }
     uint8_t *A = e->arena;
     cudaStream_t s = nullptr;
-    int rc = SP_OK;
-    int *d_perm = nullptr, *d_iota = nullptr;
-    auto bail = [&](int code) { cudaFree(d_perm); cudaFree(d_iota); if (s) cudaStreamDestroy(s); sp_engine_destroy(e); return code; };
+    int *d_idx = nullptr;
+    auto bail = [&](int code) { cudaFree(d_idx); if (s) cudaStreamDestroy(s); sp_engine_destroy(e); return code; };
 #define SP_TRY(call)                                                                                 \
     do {                                                                                             \
         cudaError_t e_ = (call);                                                                     \
         if (e_ != cudaSuccess) return bail(fail(SP_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_))); \
     } while (0)
     SP_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-    // ---- pack -----------------------------------------------------------------------------
-    // QKV rows are reordered so that the two rows of a RoPE pair (d, d + head_dim/2) of a head
-    // are adjacent: packed row hh*HD + 2*j + t  <-  fused row hh*HD + j + t*HD/2.
-    std::vector<int> perm(QR), iota(std::max(I, QR));
-    for (int r = 0; r < QR; ++r) {
-        const int hh = r / HD, j = r % HD;
-        perm[r] = hh * HD + (j / 2) + (j % 2) * (HD / 2);
+    // ---- pack ------------------------------------------------------------------------------
+    // Row maps (packed row -> source row): QKV rows are reordered so the two rows of a RoPE pair
+    // (d, d + head_dim/2) of a head are adjacent; gate and up rows are interleaved (gate_i, up_i).
+    const size_t n_iota = std::max(std::max(V, 2 * I), std::max(QR, H));
+    std::vector<int> idx(QR + 2 * I + n_iota);
+    int *h_perm = idx.data(), *h_gu = idx.data() + QR, *h_iota = idx.data() + QR + 2 * I;
+    for (size_t r = 0; r < QR; ++r) {
+        const size_t hh = r / HD, j = r % HD;
+        h_perm[r] = (int)(hh * HD + (j / 2) + (j % 2) * (HD / 2));
     }
-    for (size_t i = 0; i < iota.size(); ++i) iota[i] = (int)i;
-    SP_TRY(cudaMalloc(&d_perm, perm.size() * 4));
-    SP_TRY(cudaMalloc(&d_iota, iota.size() * 4));
-    SP_TRY(cudaMemcpy(d_perm, perm.data(), perm.size() * 4, cudaMemcpyHostToDevice));
-    SP_TRY(cudaMemcpy(d_iota, iota.data(), iota.size() * 4, cudaMemcpyHostToDevice));
-    SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, (size_t)V * H * 2, cudaMemcpyDeviceToDevice, s));
-    if (!c.tied_embeddings) {
-        SP_TRY(cudaMemcpyAsync(A + o_head, w->lm_head, (size_t)V * H * eb, cudaMemcpyDeviceToDevice, s));
-        if (i8) {
-            if (!w->lm_head_s) return bail(fail(SP_ERR_INVALID, "int8 lm_head without scales"));
-            SP_TRY(cudaMemcpyAsync(A + o_head_s, w->lm_head_s, (size_t)V * (H / 32) * 2, cudaMemcpyDeviceToDevice, s));
-        }
+    for (size_t i = 0; i < I; ++i) {
+        h_gu[2 * i] = (int)i;
+        h_gu[2 * i + 1] = (int)(I + i);
     }
-    SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+    for (size_t i = 0; i < n_iota; ++i) h_iota[i] = (int)i;
+    SP_TRY(cudaMalloc(&d_idx, idx.size() * 4));
+    SP_TRY(cudaMemcpy(d_idx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice));
+    const int *d_perm = d_idx, *d_gu = d_idx + QR, *d_iota = d_idx + QR + 2 * I;
+    SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
+    const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
+    SP_TRY(launch_pack_fragments(A + o_head, head_src, (int)V, nullptr, d_iota, (int)V, (int)H, s));
+    SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
-        if (!Lw.qkv_w || !Lw.qkv_b || !Lw.o_w || !Lw.gate_w || !Lw.up_w || !Lw.down_w || !Lw.in_norm || !Lw.post_norm)
-            return bail(fail(SP_ERR_INVALID, "layer %d: missing tensor", l));
-        if (i8 && (!Lw.qkv_s || !Lw.o_s || !Lw.gate_s || !Lw.up_s || !Lw.down_s))
-            return bail(fail(SP_ERR_INVALID, "layer %d: int8 matrix without scales", l));
-        const uint8_t *src;
-        SP_TRY(launch_gather_rows(A + lo[l].qkv, (const uint8_t *)Lw.qkv_w, d_perm, QR, (int)(H * eb), 1, 0, s));
-        SP_TRY(launch_gather_rows(A + lo[l].gu, (const uint8_t *)Lw.gate_w, d_iota, I, (int)(H * eb), 2, 0, s));
-        SP_TRY(launch_gather_rows(A + lo[l].gu, (const uint8_t *)Lw.up_w, d_iota, I, (int)(H * eb), 2, 1, s));
-        SP_TRY(cudaMemcpyAsync(A + lo[l].o, Lw.o_w, (size_t)H * H * eb, cudaMemcpyDeviceToDevice, s));
-        SP_TRY(cudaMemcpyAsync(A + lo[l].dn, Lw.down_w, (size_t)H * I * eb, cudaMemcpyDeviceToDevice, s));
-        if (i8) {
-            const int srH = (H / 32) * 2, srI = (I / 32) * 2;
-            SP_TRY(launch_gather_rows(A + lo[l].qkv_s, (const uint8_t *)Lw.qkv_s, d_perm, QR, srH, 1, 0, s));
-            SP_TRY(launch_gather_rows(A + lo[l].gu_s, (const uint8_t *)Lw.gate_s, d_iota, I, srH, 2, 0, s));
-            SP_TRY(launch_gather_rows(A + lo[l].gu_s, (const uint8_t *)Lw.up_s, d_iota, I, srH, 2, 1, s));
-            SP_TRY(cudaMemcpyAsync(A + lo[l].o_s, Lw.o_s, (size_t)H * srH, cudaMemcpyDeviceToDevice, s));
-            SP_TRY(cudaMemcpyAsync(A + lo[l].dn_s, Lw.down_s, (size_t)H * srI, cudaMemcpyDeviceToDevice, s));
-        }
-        src = (const uint8_t *)Lw.qkv_b;
-        SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, src, (size_t)QR * 4, cudaMemcpyDeviceToDevice, s));
-        SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
-        SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(launch_pack_fragments(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QR, (int)H, s));
+        SP_TRY(launch_pack_fragments(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)H, (int)H, s));
+        SP_TRY(launch_pack_fragments(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu,
+                                     (int)(2 * I), (int)H, s));
+        SP_TRY(launch_pack_fragments(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)H, (int)I, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
+        SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         LayerDev L;
         L.qkv = A + lo[l].qkv;
         L.o = A + lo[l].o;
         L.gate_up = A + lo[l].gu;
         L.down = A + lo[l].dn;
-        L.qkv_s = i8 ? (const __half *)(A + lo[l].qkv_s) : nullptr;
-        L.o_s = i8 ? (const __half *)(A + lo[l].o_s) : nullptr;
-        L.gate_up_s = i8 ? (const __half *)(A + lo[l].gu_s) : nullptr;
-        L.down_s = i8 ? (const __half *)(A + lo[l].dn_s) : nullptr;
         L.qkv_b = (const float *)(A + lo[l].qkv_b);
         L.in_norm = (const float *)(A + lo[l].inn);
         L.post_norm = (const float *)(A + lo[l].post);
+        L.off_qkv = lo[l].qkv;
+        L.off_o = lo[l].o;
+        L.off_gu = lo[l].gu;
+        L.off_dn = lo[l].dn;
         e->layers.push_back(L);
     }
     // RoPE table: the caller's (computed like the reference, qwen_engine.py:52,99-103), else double precision.
@@ -365,7 +386,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         if (!host) {
             rope.resize((size_t)c.max_positions * (HD / 2) * 2);
             for (int pos = 0; pos < c.max_positions; ++pos)
-                for (int i = 0; i < HD / 2; ++i) {
+                for (size_t i = 0; i < HD / 2; ++i) {
                     const float inv = (float)(1.0 / pow((double)c.rope_theta, (double)(2 * i) / (double)HD));
                     const float ph = (float)pos * inv;
                     rope[((size_t)pos * (HD / 2) + i) * 2] = (float)cos((double)ph);
@@ -376,54 +397,53 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(cudaMemcpy(A + o_rope, host, (size_t)c.max_positions * (HD / 2) * 2 * 4, cudaMemcpyHostToDevice));
     }
     SP_TRY(cudaStreamSynchronize(s));
-    cudaFree(d_perm);
-    cudaFree(d_iota);
-    d_perm = d_iota = nullptr;
+    cudaFree(d_idx);
+    d_idx = nullptr;
+    e->stream = A;
+    e->stream_bytes = stream_end;
     e->embed = (const __half *)(A + o_embed);
+    e->head = A + o_head;
+    e->off_head = o_head;
     e->final_norm = (const float *)(A + o_fnorm);
     e->rope = (const float *)(A + o_rope);
-    if (c.tied_embeddings) {
-        e->head = A + o_embed;
-        e->head_fmt = WF_F16;
-    } else {
-        e->head = A + o_head;
-        e->head_s = i8 ? (const __half *)(A + o_head_s) : nullptr;
-        e->head_fmt = i8 ? WF_I8 : WF_F16;
-    }
 
     // ---- GEMV plans -------------------------------------------------------------------------
-    const int fmt = i8 ? WF_I8 : WF_F16;
-    auto base = [&](int N, int K, int f) {
+    auto base = [&](size_t N, size_t K) {
         GemvParams p{};
-        p.N = N;
-        p.K = K;
-        p.fmt = f;
+        p.N = (int)N;
+        p.K = (int)K;
+        p.fmt = WF_F16;
         p.eps = c.rms_norm_eps;
-        p.vocab = V;
+        p.vocab = (int)V;
         p.rope = e->rope;
         p.max_pos = c.max_positions;
         p.nh = c.heads;
         p.nkv = c.kv_heads;
-        p.hd = HD;
+        p.hd = (int)HD;
+        plan_gemv(p, e->num_sms, kRingBytes, kMaxUnitBytes);
         return p;
     };
-    e->g_qkv = base(QR, H, fmt);
-    plan_gemv(e->g_qkv, 2, e->num_sms, kRingBytes);
-    e->g_o = base(H, H, fmt);
-    plan_gemv(e->g_o, 1, e->num_sms, kRingBytes);
-    e->g_gu = base(2 * I, H, fmt);
-    plan_gemv(e->g_gu, 2, e->num_sms, kRingBytes);
-    e->g_down = base(H, I, fmt);
-    plan_gemv(e->g_down, 1, e->num_sms, kRingBytes);
-    e->g_head = base(V, H, e->head_fmt);
-    plan_gemv(e->g_head, 1, e->num_sms, kRingBytes);
+    e->g_qkv = base(QR, H);
+    e->g_o = base(H, H);
+    e->g_gu = base(2 * I, H);
+    e->g_down = base(H, I);
+    e->g_head = base(V, H);
 
     // ---- workspace ------------------------------------------------------------------------
+    size_t n_partial = 0, n_strips = 0;
+    for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head}) {
+        if (p->ks > 1) {
+            n_partial = std::max(n_partial, (size_t)p->N * p->ks);
+            n_strips = std::max(n_strips, (size_t)p->N / 16);
+        }
+    }
     size_t woff = 0;
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
-    const size_t w_x = wtake((size_t)H * 4), w_q = wtake((size_t)c.heads * HD * 4);
-    const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake((size_t)I * 4);
+    const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
+    const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
     const size_t w_apart = wtake((size_t)c.heads * kAttnMaxSplit * (HD + 2) * 4);
+    const size_t w_partial = wtake(std::max<size_t>(n_partial, 1) * 4);
+    const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_acnt = wtake((size_t)c.kv_heads * 4), w_lmcnt = wtake(4);
     const size_t w_lmval = wtake((size_t)e->g_head.grid * 4), w_lmidx = wtake((size_t)e->g_head.grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
@@ -435,17 +455,22 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->attn = (float *)(e->ws + w_attn);
     e->act = (float *)(e->ws + w_act);
     e->apart = (float *)(e->ws + w_apart);
+    e->partial = (float *)(e->ws + w_partial);
+    e->strip_cnt = (unsigned *)(e->ws + w_scnt);
     e->acnt = (unsigned *)(e->ws + w_acnt);
     e->lm_cnt = (unsigned *)(e->ws + w_lmcnt);
     e->lm_val = (float *)(e->ws + w_lmval);
     e->lm_idx = (int *)(e->ws + w_lmidx);
     e->st = (DevState *)(e->ws + w_st);
     e->g_head.w = e->head;
-    e->g_head.ws = e->head_s;
     e->g_head.part_val = e->lm_val;
     e->g_head.part_idx = e->lm_idx;
     e->g_head.counter = e->lm_cnt;
-    for (GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head}) p->st = e->st;
+    for (GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head}) {
+        p->st = e->st;
+        p->partial = e->partial;
+        p->strip_cnt = e->strip_cnt;
+    }
     e->g_qkv.embed = e->embed;
     e->g_qkv.x_init = e->x;
     SP_TRY(prepare_gemv(PRO_NORM, EPI_QKV, e->g_qkv));
@@ -458,7 +483,6 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
     e->cap_stream = s;
     s = nullptr;
-    (void)rc;
 #undef SP_TRY
     *out = e;
     return SP_OK;

@@ -28,133 +28,176 @@ namespace sp {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxTasks = 32;
-constexpr int kTargetStage = 24 * 1024;
 
 SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
 }
 
-SP_DEVINL float dot16_i8(const uint4 q, const float4 *x, float acc) {
-    const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float4 a = x[j];
-        const uint32_t w = wds[j];
-        acc = fmaf((float)(int8_t)(w & 0xff), a.x, acc);
-        acc = fmaf((float)(int8_t)((w >> 8) & 0xff), a.y, acc);
-        acc = fmaf((float)(int8_t)((w >> 16) & 0xff), a.z, acc);
-        acc = fmaf((float)(int8_t)(w >> 24), a.w, acc);
-    }
-    return acc;
+// D += A(16x16 fp16) . B(16x8 fp16), fp32 accumulation (tensor cores). Used as a dot-product
+// engine: B column 0 holds the fp16 "hi" part of the fp32 input, column 1 the "lo" remainder,
+// so y = D[:,0] + D[:,1] carries ~22 bits of the fp32 activation (products are exact).
+SP_DEVINL void mma_16816(float (&d)[4], const uint4 a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
-// Dot product of one staged row segment [v0, v0 + nv) (16-byte vectors) with the input vector.
-template <int FMT>
-SP_DEVINL float dot_segment(const uint8_t *stage, int r, int R, int K, int v0, int nv, const float *xs, int lane) {
-    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-    float a0 = 0.f, a1 = 0.f;
-    if constexpr (FMT == WF_F16) {
-        const uint4 *wr = reinterpret_cast<const uint4 *>(stage + (size_t)r * K * 2);
-        int v = v0 + lane;
-        const int ve = v0 + nv;
-        for (; v + 32 < ve; v += 64) {
-            a0 = dot8_f16(wr[v], x4[2 * v], x4[2 * v + 1], a0);
-            a1 = dot8_f16(wr[v + 32], x4[2 * v + 64], x4[2 * v + 65], a1);
-        }
-        if (v < ve) a0 = dot8_f16(wr[v], x4[2 * v], x4[2 * v + 1], a0);
-    } else {
-        const uint4 *wr = reinterpret_cast<const uint4 *>(stage + (size_t)r * K);
-        const __half *sc = reinterpret_cast<const __half *>(stage + (size_t)R * K) + (size_t)r * (K / 32);
-        for (int v = v0 + lane; v < v0 + nv; v += 32) {
-            const float t = dot16_i8(wr[v], x4 + 4 * v, 0.f);
-            a0 = fmaf(__half2float(sc[v >> 1]), t, a0);
-        }
-    }
-    return a0 + a1;
+SP_DEVINL uint32_t pack_half2(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
 template <int PRO, int EPI, int FMT>
 __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
+    static_assert(FMT == WF_F16, "fragment GEMV streams fp16 weights");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_val[kWarps];
     __shared__ int s_idx[kWarps];
     __shared__ int s_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int S = p.stages, SB = p.stage_bytes, K = p.K, R = p.rows_per_chunk, SPLIT = p.split;
+    const int S = p.stages, K = p.K, NT = p.nt, KS = p.ks;
+    const int KT = K / 16;
+    const int unit_bytes = NT * kTileBytes;
     uint8_t *ring = smem;
-    float *xs = reinterpret_cast<float *>(smem + (size_t)S * SB);
-    float *red = xs + K;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * kMaxTasks);
+    uint32_t *xb = reinterpret_cast<uint32_t *>(smem + (size_t)S * unit_bytes);   // KT x 16 words
+    float *red = reinterpret_cast<float *>(xb + (size_t)KT * 16);                  // 2 x 8 warps x 16
+    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * kWarps * 16);
 
-    constexpr int RG = (EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 1;
     const int C = gridDim.x, c = blockIdx.x;
-    const int ngroups = p.N / RG;
-    const int r0 = (int)((long long)ngroups * c / C) * RG;
-    const int r1 = (int)((long long)ngroups * (c + 1) / C) * RG;
-    const int nch = (r1 - r0 + R - 1) / R;
-    const size_t row_bytes = FMT == WF_F16 ? (size_t)K * 2 : (size_t)K;
-    const size_t srow_bytes = FMT == WF_I8 ? (size_t)(K / 32) * 2 : 0;
+    const int U = (p.N / 16) * KS;
+    const int u0 = (int)((long long)U * c / C), u1 = (int)((long long)U * (c + 1) / C);
+    const int nu = u1 - u0;
+    uint64_t policy = 0;
+    if (p.evict_first) policy = policy_evict_first();
 
     auto issue = [&](int i) {
-        const int s = i % S;
-        const int cr0 = r0 + i * R;
-        const int nr = min(R, r1 - cr0);
-        uint8_t *dst = ring + (size_t)s * SB;
-        const uint32_t wbytes = (uint32_t)(nr * row_bytes);
-        const uint32_t sbytes = (uint32_t)(nr * srow_bytes);
-        mbar_arrive_expect_tx(&bars[s], wbytes + sbytes);
-        bulk_g2s(dst, p.w + (size_t)cr0 * row_bytes, wbytes, &bars[s]);
-        if constexpr (FMT == WF_I8)
-            bulk_g2s(dst + (size_t)R * row_bytes, reinterpret_cast<const uint8_t *>(p.ws) + (size_t)cr0 * srow_bytes,
-                     sbytes, &bars[s]);
+        const int u = u0 + i, st_ = i % S;
+        const int strip = u / KS, seg = u - strip * KS;
+        const uint8_t *src = p.w + ((size_t)strip * KT + (size_t)seg * NT) * kTileBytes;
+        mbar_arrive_expect_tx(&bars[st_], (uint32_t)unit_bytes);
+        if (p.evict_first) bulk_g2s_hint(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &bars[st_], policy);
+        else bulk_g2s(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &bars[st_]);
     };
 
-    // Weights do not depend on the previous kernel: start streaming them before the dependency wait.
+    // Weights do not depend on the previous kernel: start streaming them, and warm L2 with the
+    // weight stream further ahead, before the dependency wait.
     if (tid == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+        for (int i = 0; i < S; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
-        for (int i = 0; i < min(S, nch); ++i) issue(i);
+        for (int i = 0; i < min(S, nu); ++i) issue(i);
+    }
+    if (tid == 32) {
+        for (int r = 0; r < p.pf_n; ++r) {
+            const unsigned long long share = (p.pf_bytes[r] / C + 15) & ~15ull;
+            const unsigned long long beg = share * c;
+            if (beg >= p.pf_bytes[r]) continue;
+            const unsigned long long end = min(beg + share, p.pf_bytes[r]) & ~15ull;
+            for (unsigned long long o = beg; o < end; o += 32768)
+                prefetch_l2(p.pf_ptr[r] + o, (uint32_t)min(32768ull, end - o));
+        }
     }
     __syncthreads();
     griddep_wait();
     griddep_launch_dependents();
 
     DevState *st = p.st;
-    // ---- prologue: fp32 input vector in shared memory --------------------------------------
+    // ---- prologue: fp32 input -> RMSNorm -> hi/lo fp16 B fragments in shared memory ----------
+    // Pass A stores the raw fp32 input at its natural index in the fragment buffer (K floats fill
+    // it exactly) with coalesced loads; pass B turns each k-tile's 16 floats (64 bytes) into that
+    // tile's 64-byte fragment in place: lanes 0-3 hold the fp16 "hi" column, lanes 4-7 the "lo".
+    float *xs = reinterpret_cast<float *>(xb);
+    float ss = 0.f;
     if constexpr (PRO == PRO_EMBED_NORM) {
         int tok = st->token;
         if (tok < 0 || tok >= p.vocab) {
             if (tid == 0) atomicCAS(&st->err, 0, kErrBadToken);
             tok = 0;
         }
-        const __half2 *e = reinterpret_cast<const __half2 *>(p.embed + (size_t)tok * K);
-        for (int k = tid; k < K / 2; k += kThreads) {
-            const float2 f = __half22float2(e[k]);
-            xs[2 * k] = f.x;
-            xs[2 * k + 1] = f.y;
-            if (c == 0) {
-                p.x_init[2 * k] = f.x;
-                p.x_init[2 * k + 1] = f.y;
+        const uint4 *e4 = reinterpret_cast<const uint4 *>(p.embed + (size_t)tok * K);
+        for (int v = tid; v < K / 8; v += kThreads) {
+            const uint4 raw = e4[v];
+            const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 t2 = __half22float2(h2[j]);
+                f[2 * j] = t2.x;
+                f[2 * j + 1] = t2.y;
             }
+            float4 *dst = reinterpret_cast<float4 *>(xs + 8 * v);
+            dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+            dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+            if (c == 0) {
+                float4 *xi = reinterpret_cast<float4 *>(p.x_init + 8 * v);
+                xi[0] = dst[0];
+                xi[1] = dst[1];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
         }
     } else {
-        for (int k = tid * 4; k < K; k += kThreads * 4)
-            *reinterpret_cast<float4 *>(xs + k) = *reinterpret_cast<const float4 *>(p.xin + k);
+        const float4 *x4 = reinterpret_cast<const float4 *>(p.xin);
+        for (int v = tid; v < K / 4; v += kThreads) {
+            const float4 f = x4[v];
+            reinterpret_cast<float4 *>(xs)[v] = f;
+            if constexpr (PRO != PRO_PLAIN) {
+                ss = fmaf(f.x, f.x, ss);
+                ss = fmaf(f.y, f.y, ss);
+                ss = fmaf(f.z, f.z, ss);
+                ss = fmaf(f.w, f.w, ss);
+            }
+        }
     }
+    float inv = 1.f;
     if constexpr (PRO != PRO_PLAIN) {
-        __syncthreads();
-        float ss = 0.f;
-        for (int k = tid; k < K; k += kThreads) ss = fmaf(xs[k], xs[k], ss);
         ss = warp_sum(ss);
         if (lane == 0) s_val[warp] = ss;
-        __syncthreads();
+    }
+    __syncthreads();
+    if constexpr (PRO != PRO_PLAIN) {
         float tot = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) tot += s_val[w];
-        const float inv = 1.0f / sqrtf(tot / (float)K + p.eps);
-        for (int k = tid; k < K; k += kThreads) xs[k] = (xs[k] * inv) * p.gain[k];
+        inv = 1.0f / sqrtf(tot / (float)K + p.eps);
+    }
+    for (int t = tid; t < KT; t += kThreads) {
+        float v[16];
+        const float4 *src = reinterpret_cast<const float4 *>(xs + 16 * t);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 f = src[j];
+            v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+        }
+        if constexpr (PRO != PRO_PLAIN) {
+            const float4 *g4 = reinterpret_cast<const float4 *>(p.gain + 16 * t);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 g = g4[j];
+                v[4 * j] = (v[4 * j] * inv) * g.x;
+                v[4 * j + 1] = (v[4 * j + 1] * inv) * g.y;
+                v[4 * j + 2] = (v[4 * j + 2] * inv) * g.z;
+                v[4 * j + 3] = (v[4 * j + 3] * inv) * g.w;
+            }
+        }
+        __half hi[16], lo[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            hi[j] = __float2half_rn(v[j]);
+            lo[j] = __float2half_rn(v[j] - __half2float(hi[j]));
+        }
+        uint32_t wds[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            const int k0 = 2 * cc;
+            wds[cc * 2] = pack_half2(hi[k0], hi[k0 + 1]);
+            wds[cc * 2 + 1] = pack_half2(hi[k0 + 8], hi[k0 + 9]);
+            wds[8 + cc * 2] = pack_half2(lo[k0], lo[k0 + 1]);
+            wds[8 + cc * 2 + 1] = pack_half2(lo[k0 + 8], lo[k0 + 9]);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(xb + (size_t)t * 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[j] = make_uint4(wds[4 * j], wds[4 * j + 1], wds[4 * j + 2], wds[4 * j + 3]);
     }
     __syncthreads();
 
@@ -176,93 +219,102 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     }
     float bv = -INFINITY;
     int bi = INT_MAX;
-
-    const int vec_per_row = FMT == WF_F16 ? K / 8 : K / 16;
-    const int segv = vec_per_row / SPLIT;
     const int half_hd = p.hd / 2;
 
-    for (int i = 0; i < nch; ++i) {
-        const int s = i % S;
+    for (int i = 0; i < nu; ++i) {
+        const int sidx = i % S;
         const uint32_t par = (uint32_t)(i / S) & 1u;
-        const bool ok = mbar_wait_bounded(&bars[s], par);
-        const uint8_t *stage = ring + (size_t)s * SB;
-        const int cr0 = r0 + i * R;
-        const int nr = min(R, r1 - cr0);
-        float *rb = red + (i & 1) * kMaxTasks;
+        const int u = u0 + i;
+        const int strip = u / KS, seg = u - strip * KS;
+        const bool ok = mbar_wait_bounded(&bars[sidx], par);
+        float *rb = red + (i & 1) * kWarps * 16;
         if (ok) {
-            const int ntask = nr * SPLIT;
-            for (int t = warp; t < ntask; t += kWarps) {
-                const int r = t / SPLIT, sg = t - r * SPLIT;
-                float acc = dot_segment<FMT>(stage, r, R, K, sg * segv, segv, xs, lane);
-                acc = warp_sum(acc);
-                if (lane == 0) rb[t] = acc;
+            const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
+            const uint32_t *xw = xb + (size_t)seg * NT * 16;
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int j = warp; j < NT; j += kWarps) {
+                const uint4 a = *reinterpret_cast<const uint4 *>(stage + (size_t)j * kTileBytes + lane * 16);
+                uint2 b = make_uint2(0u, 0u);
+                if (lane < 8) b = *reinterpret_cast<const uint2 *>(xw + j * 16 + lane * 2);
+                mma_16816(d, a, b.x, b.y);
+            }
+            if ((lane & 3) == 0) {
+                rb[warp * 16 + (lane >> 2)] = d[0] + d[1];
+                rb[warp * 16 + (lane >> 2) + 8] = d[2] + d[3];
             }
         }
         if (!__syncthreads_and(ok)) {
             // A stage never arrived: record it, wait (bounded) for copies still in flight, leave.
             if (tid == 0) {
                 atomicCAS(&st->err, 0, kErrMbarTimeout);
-                for (int j = i; j < min(i + S, nch); ++j) mbar_wait_bounded(&bars[j % S], (uint32_t)(j / S) & 1u);
+                for (int j = i; j < min(i + S, nu); ++j) mbar_wait_bounded(&bars[j % S], (uint32_t)(j / S) & 1u);
             }
             __syncthreads();
             return;
         }
-        if (tid == 0 && i + S < nch) issue(i + S);
+        if (tid == 0 && i + S < nu) issue(i + S);
 
-        // ---- epilogue for the rows of this chunk ------------------------------------------
-        if constexpr (EPI == EPI_RESID) {
-            if (tid < nr) {
-                float y = 0.f;
-                for (int sg = 0; sg < SPLIT; ++sg) y += rb[tid * SPLIT + sg];
-                const int row = cr0 + tid;
-                p.out[row] = p.out[row] + y;
+        if (warp == 0) {
+            float y = 0.f;
+            if (lane < 16) {
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) y += rb[w * 16 + lane];
             }
-        } else if constexpr (EPI == EPI_LMHEAD) {
-            if (tid < nr) {
-                float y = 0.f;
-                for (int sg = 0; sg < SPLIT; ++sg) y += rb[tid * SPLIT + sg];
-                const int row = cr0 + tid;
-                if (lg) lg[row] = y;
-                if (y > bv) { bv = y; bi = row; }
-            }
-        } else if constexpr (EPI == EPI_SWIGLU) {
-            if (tid < nr / 2) {
-                float g = 0.f, u = 0.f;
-                for (int sg = 0; sg < SPLIT; ++sg) {
-                    g += rb[(2 * tid) * SPLIT + sg];
-                    u += rb[(2 * tid + 1) * SPLIT + sg];
+            bool fin = true;
+            if (KS > 1) {
+                if (lane < 16) p.partial[((size_t)strip * KS + seg) * 16 + lane] = y;
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) last = atomicAdd(p.strip_cnt + strip, 1u) == (unsigned)(KS - 1);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                fin = last != 0;
+                if (fin) {
+                    __threadfence();
+                    y = 0.f;
+                    if (lane < 16)
+                        for (int k2 = 0; k2 < KS; ++k2) y += __ldcg(p.partial + ((size_t)strip * KS + k2) * 16 + lane);
+                    if (lane == 0) p.strip_cnt[strip] = 0u;
                 }
-                p.out[cr0 / 2 + tid] = (g / (1.0f + expf(-g))) * u;
             }
-        } else {  // EPI_QKV: packed rows come in RoPE pairs (d, d + hd/2) of one head
-            if (tid < nr / 2) {
-                float y0 = 0.f, y1 = 0.f;
-                for (int sg = 0; sg < SPLIT; ++sg) {
-                    y0 += rb[(2 * tid) * SPLIT + sg];
-                    y1 += rb[(2 * tid + 1) * SPLIT + sg];
-                }
-                const int P = cr0 / 2 + tid;
-                const int hh = P / half_hd, d = P - hh * half_hd;
-                const int lo = hh * p.hd + d, hi = lo + half_hd;
-                y0 += p.bias[lo];
-                y1 += p.bias[hi];
-                if (hh < p.nh + p.nkv) {
-                    const float cs = p.rope[((size_t)pos * half_hd + d) * 2];
-                    const float sn = p.rope[((size_t)pos * half_hd + d) * 2 + 1];
-                    const float o0 = __fadd_rn(__fmul_rn(y0, cs), -__fmul_rn(y1, sn));
-                    const float o1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
-                    if (hh < p.nh) {
-                        p.out[lo] = o0;
-                        p.out[hi] = o1;
-                    } else {
-                        __half *kr = p.kc + ((size_t)(hh - p.nh) * p.cap + slot) * p.hd;
-                        kr[d] = __float2half_rn(o0);
-                        kr[d + half_hd] = __float2half_rn(o1);
+            if (fin) {
+                const int row = strip * 16 + lane;
+                const float other = __shfl_xor_sync(0xffffffffu, y, 1);   // pair partner (row ^ 1)
+                if constexpr (EPI == EPI_RESID) {
+                    if (lane < 16) p.out[row] = p.out[row] + y;
+                } else if constexpr (EPI == EPI_LMHEAD) {
+                    if (lane < 16) {
+                        if (lg) lg[row] = y;
+                        if (y > bv) { bv = y; bi = row; }
                     }
-                } else {
-                    __half *vr = p.vc + ((size_t)(hh - p.nh - p.nkv) * p.cap + slot) * p.hd;
-                    vr[d] = __float2half_rn(y0);
-                    vr[d + half_hd] = __float2half_rn(y1);
+                } else if constexpr (EPI == EPI_SWIGLU) {
+                    if (lane < 16 && (lane & 1) == 0) p.out[row / 2] = (y / (1.0f + expf(-y))) * other;
+                } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
+                    if (lane < 16 && (lane & 1) == 0) {
+                        const int P = row / 2;
+                        const int hh = P / half_hd, dd = P - hh * half_hd;
+                        const int lo = hh * p.hd + dd, hi = lo + half_hd;
+                        const float y0 = y + p.bias[lo], y1 = other + p.bias[hi];
+                        if (hh < p.nh + p.nkv) {
+                            const float cs = p.rope[((size_t)pos * half_hd + dd) * 2];
+                            const float sn = p.rope[((size_t)pos * half_hd + dd) * 2 + 1];
+                            const float o0 = __fadd_rn(__fmul_rn(y0, cs), -__fmul_rn(y1, sn));
+                            const float o1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
+                            if (hh < p.nh) {
+                                p.out[lo] = o0;
+                                p.out[hi] = o1;
+                            } else {
+                                __half *kr = p.kc + ((size_t)(hh - p.nh) * p.cap + slot) * p.hd;
+                                kr[dd] = __float2half_rn(o0);
+                                kr[dd + half_hd] = __float2half_rn(o1);
+                            }
+                        } else {
+                            __half *vr = p.vc + ((size_t)(hh - p.nh - p.nkv) * p.cap + slot) * p.hd;
+                            vr[dd] = __float2half_rn(y0);
+                            vr[dd + half_hd] = __float2half_rn(y1);
+                        }
+                    }
                 }
             }
         }
@@ -419,10 +471,15 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
                 A = fmaf(sm_acc[w][h][d], f, A);
             }
         }
+        if (nsplit == 1) {       // the whole context in one CTA: no partials to merge
+            p.out[(g * G + h) * HD + d] = A / L;
+            continue;
+        }
         float *pr = p.part + ((size_t)(g * G + h) * p.max_split + c) * stride;
         pr[d] = A;
         if (d == 0) { pr[HD] = M; pr[HD + 1] = L; }
     }
+    if (nsplit == 1) return;
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -480,6 +537,30 @@ __global__ void k_gather_rows(uint8_t *dst, const uint8_t *src, const int *src_r
     for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = s[i];
 }
 
+// One warp per 16x16 tile; lane l writes its A-fragment registers a0..a3 (16 bytes):
+// a0 = (row g, cols 2c, 2c+1), a1 = (row g+8, same cols), a2 = (row g, cols 2c+8, 2c+9), a3 = (row g+8, ...),
+// with g = l/4, c = l%4 (the mma.m16n8k16 row-major A layout).
+__global__ void k_pack_fragments(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
+                                 int N, int K) {
+    const int KT = K / 16;
+    const long long tile = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (tile >= (long long)(N / 16) * KT) return;
+    const int lane = threadIdx.x & 31, g = lane >> 2, cc = lane & 3;
+    const int s = (int)(tile / KT), t = (int)(tile % KT);
+    auto row_ptr = [&](int r) {
+        const int src = row_of[r];
+        return src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
+    };
+    const __half *r0 = row_ptr(16 * s + g), *r1 = row_ptr(16 * s + g + 8);
+    const int k0 = 16 * t + 2 * cc;
+    uint4 v;
+    v.x = *reinterpret_cast<const uint32_t *>(r0 + k0);
+    v.y = *reinterpret_cast<const uint32_t *>(r1 + k0);
+    v.z = *reinterpret_cast<const uint32_t *>(r0 + k0 + 8);
+    v.w = *reinterpret_cast<const uint32_t *>(r1 + k0 + 8);
+    *reinterpret_cast<uint4 *>(dst + ((size_t)tile * 32 + lane) * 16) = v;
+}
+
 struct CommitSlots {
     int src[kSmallNodes];
 };
@@ -516,27 +597,29 @@ static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-void plan_gemv(GemvParams &p, int rg, int num_sms, int ring_bytes) {
-    const size_t row = p.fmt == WF_F16 ? (size_t)p.K * 2 : (size_t)p.K + (size_t)(p.K / 32) * 2;
-    const int nvec = p.fmt == WF_F16 ? p.K / 8 : p.K / 16;
-    int R = (int)(kTargetStage / row);
-    R = R / rg * rg;
-    R = std::max(rg, std::min(16, R));
-    int split = 1;
-    if (R < kWarps) {
-        split = kWarps / R;
-        while (split > 1 && nvec % split) --split;
+void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
+    // Choose tiles per unit (a divisor of K/16) minimising the tiles streamed by the busiest CTA;
+    // split strips (ks > 1) cost a little extra (partials), larger units win ties.
+    const int KT = p.K / 16, strips = p.N / 16;
+    double best = 1e300;
+    for (int nt = 1; nt <= KT; ++nt) {
+        if (KT % nt || nt * kTileBytes > max_unit_bytes) continue;
+        const long long U = (long long)strips * (KT / nt);
+        const long long C = std::min<long long>(num_sms, U);
+        const double cost = (double)((U + C - 1) / C) * nt * (KT / nt > 1 ? 1.01 : 1.0);
+        if (cost < best - 1e-9 || (std::abs(cost - best) <= 1e-9 && nt > p.nt)) {
+            best = cost;
+            p.nt = nt;
+        }
     }
-    p.rows_per_chunk = R;
-    p.split = split;
-    p.stage_bytes = (int)((R * row + 127) / 128 * 128);
-    p.stages = std::max(2, std::min(8, ring_bytes / p.stage_bytes));
-    const int groups = p.N / rg;
-    p.grid = std::max(1, std::min(num_sms, groups));
+    p.ks = KT / p.nt;
+    const long long U = (long long)strips * p.ks;
+    p.grid = (int)std::min<long long>(num_sms, U);
+    p.stages = std::max(2, std::min(8, ring_bytes / (p.nt * kTileBytes)));
 }
 
 size_t gemv_smem_bytes(const GemvParams &p) {
-    return (size_t)p.stages * p.stage_bytes + (size_t)p.K * 4 + 2 * kMaxTasks * 4 + (size_t)p.stages * 8;
+    return (size_t)p.stages * p.nt * kTileBytes + (size_t)(p.K / 16) * 64 + 2 * kWarps * 16 * 4 + (size_t)p.stages * 8;
 }
 
 template <int PRO, int EPI, int FMT>
@@ -550,7 +633,7 @@ static cudaError_t gemv_t(const GemvParams &p, const LaunchCfg *lc) {
 static cudaError_t gemv_dispatch(int pro, int epi, const GemvParams &p, const LaunchCfg *lc) {
 #define SP_CASE(PRO, EPI)                                                                    \
     if (pro == PRO && epi == EPI)                                                            \
-        return p.fmt == WF_F16 ? gemv_t<PRO, EPI, WF_F16>(p, lc) : gemv_t<PRO, EPI, WF_I8>(p, lc);
+        return p.fmt == WF_F16 ? gemv_t<PRO, EPI, WF_F16>(p, lc) : cudaErrorNotSupported;
     SP_CASE(PRO_NORM, EPI_QKV)
     SP_CASE(PRO_EMBED_NORM, EPI_QKV)
     SP_CASE(PRO_PLAIN, EPI_RESID)
@@ -584,6 +667,16 @@ cudaError_t launch_gather_rows(uint8_t *dst, const uint8_t *src, const int *src_
     if (rows <= 0) return cudaSuccess;
     if (row_bytes % 16) return cudaErrorInvalidValue;
     k_gather_rows<<<rows, 128, 0, s>>>(dst, src, src_row, row_bytes, dst_mul, dst_add);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_fragments(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
+                                  int N, int K, cudaStream_t s) {
+    if (N % 16 || K % 16) return cudaErrorInvalidValue;
+    const long long tiles = (long long)(N / 16) * (K / 16);
+    const int per_block = 8;
+    k_pack_fragments<<<(unsigned)((tiles + per_block - 1) / per_block), per_block * 32, 0, s>>>(dst, a, rows_a, b, row_of,
+                                                                                            N, K);
     return cudaGetLastError();
 }
 

@@ -9,20 +9,26 @@ enum Prologue : int { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
 enum Epilogue : int { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LMHEAD = 3 };
 enum WeightFmt : int { WF_F16 = 0, WF_I8 = 1 };
 
+// Bytes of one fragment tile: 16 rows x 16 inputs of fp16, stored in mma.m16n8k16 A-fragment
+// order (lane l's 16 bytes are its registers a0..a3), so one 16-byte shared load per lane feeds
+// one tensor-core MMA.
+constexpr int kTileBytes = 512;
+constexpr int kMaxPrefetch = 4;
+
 // One weight-streaming GEMV y = W . in(x) with a fused prologue and epilogue.
-//   W is packed row-major [N][K] (fp16, or int8 + fp16 scales [N][K/32]); each CTA owns a
-//   contiguous range of rows, streams it through a ring of shared-memory stages with 1-D bulk
-//   copies (TMA engine), and reduces rows with warps (fp32 accumulation).
+//   W is fragment-packed: strip s (rows 16s..16s+15) and k-tile t (inputs 16t..16t+15) is the
+//   512-byte tile at (s * K/16 + t) * 512. Work is split into units = (strip, k segment of nt
+//   tiles); each CTA streams a contiguous range of units through a ring of shared-memory stages
+//   with 1-D bulk copies, the 8 warps share a unit's tiles, and units of one strip that end in
+//   different CTAs are summed by the last CTA to finish the strip (fixed order, deterministic).
 struct GemvParams {
     const uint8_t *w;
-    const __half *ws;
     int N, K;
-    int fmt;                 // WeightFmt
-    int rows_per_chunk;      // R: rows per stage (multiple of the epilogue's row group)
-    int split;               // segments per row (K/8 divisible by split)
+    int fmt;                 // WeightFmt (fp16 only in the fragment kernels)
+    int nt;                  // k-tiles per unit
+    int ks;                  // units per strip = (K/16) / nt
     int stages;              // ring depth
-    int stage_bytes;         // bytes per stage (128-aligned)
-    int grid;                // CTAs (row ranges)
+    int grid;                // CTAs
     // prologue
     const float *xin;
     const float *gain;
@@ -38,11 +44,19 @@ struct GemvParams {
     const float *rope;
     int max_pos;
     int nh, nkv, hd;
+    // split-K partials (strips x ks x 16) and per-strip arrival counters
+    float *partial;
+    unsigned *strip_cnt;
     // LM head
     float *part_val;
     int *part_idx;
     unsigned *counter;
     DevState *st;
+    // L2 prefetch of the weight stream ahead of this kernel (issued before the dependency wait)
+    const uint8_t *pf_ptr[kMaxPrefetch];
+    unsigned long long pf_bytes[kMaxPrefetch];
+    int pf_n;
+    int evict_first;         // stream weights with an L2 evict-first hint
 };
 
 struct AttnParams {
@@ -62,8 +76,8 @@ struct LaunchCfg {
     bool pdl;                // launch with programmatic stream serialization
 };
 
-// Plan R / split / stages for a GEMV of N x K rows (row group `rg`); fills the geometry fields.
-void plan_gemv(GemvParams &p, int rg, int num_sms, int ring_bytes);
+// Plan units / stages / grid for a GEMV of N x K; fills the geometry fields.
+void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes);
 size_t gemv_smem_bytes(const GemvParams &p);
 // Set the dynamic shared-memory limit of the kernel instance (call before any stream capture).
 cudaError_t prepare_gemv(int pro, int epi, const GemvParams &p);
@@ -75,6 +89,10 @@ cudaError_t launch_set_state(DevState *st, const DevState &init, cudaStream_t s)
 // dst row (r * dst_mul + dst_add) = src row src_row[r], for r < rows.
 cudaError_t launch_gather_rows(uint8_t *dst, const uint8_t *src, const int *src_row, int rows, int row_bytes,
                                int dst_mul, int dst_add, cudaStream_t s);
+// Fragment-pack an fp16 matrix of N x K: packed row r is source row row_of[r] of `a` when
+// row_of[r] < rows_a, else row row_of[r] - rows_a of `b` (gate/up interleave, RoPE pairing).
+cudaError_t launch_pack_fragments(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
+                                  int N, int K, cudaStream_t s);
 cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap, int hd, const int *src_slots,
                              int n, int dst0, cudaStream_t s);
 

@@ -1,0 +1,78 @@
+"""Short decode runs for profiling and launch-mode comparisons.
+
+    python -m seedplane_b200.profile_decode --model qwen2-1.5b --prompt 16 --tokens 8 [--modes graph+pdl,graph,eager+pdl]
+
+Prints, per launch mode, the device time per decoded token (CUDA events) and the host time spent
+enqueueing the step launches. With `--modes graph+pdl --repeat 0` it is also the small, bounded
+command used under `ncu` (a prefill of `--prompt` tokens and `--tokens` decode steps).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import time
+
+import torch
+
+from .config import PRESETS
+from .randinit import make_weights, random_prompt
+
+MODES = {"graph+pdl": ("1", "1"), "graph": ("1", "0"), "eager+pdl": ("0", "1"), "eager": ("0", "0")}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--model", default="qwen2-1.5b", choices=sorted(PRESETS))
+    ap.add_argument("--prompt", type=int, default=16)
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--repeat", type=int, default=5, help="timed repetitions per mode (0: just run once)")
+    ap.add_argument("--modes", default="graph+pdl")
+    ap.add_argument("--capacity", type=int, default=4096)
+    ap.add_argument("--prefetch-mb", default="0", help="comma list of L2 prefetch distances (MB) to compare")
+    ap.add_argument("--evict-first", default="0", help="comma list of 0/1: stream weights with evict-first")
+    a = ap.parse_args()
+    from .engine import CudaQwen2
+    cfg = PRESETS[a.model]
+    w = make_weights(cfg, seed=0, dtype=torch.float16)
+    prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
+    results = {}
+    variants = [(m, pf, ev) for m in a.modes.split(",") for pf in a.prefetch_mb.split(",")
+                for ev in a.evict_first.split(",")]
+    for mode, pf, ev in variants:
+        graph, pdl = MODES[mode]
+        os.environ["SEEDPLANE_GRAPH"], os.environ["SEEDPLANE_PDL"] = graph, pdl
+        os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
+        label = f"{mode} prefetch={pf}MB evict_first={ev}"
+        eng = CudaQwen2(cfg, w)
+        kv = eng.new_kv(a.capacity)
+        _, am = eng.forward(kv, prompt, want_logits=False)
+        first = int(am[-1])
+        out = torch.empty(a.tokens, dtype=torch.int32, device=eng.device)
+        kv.length = a.prompt
+        eng.decode(kv, first, a.prompt, a.tokens, out=out)
+        torch.cuda.synchronize()
+        eng.status()
+        ref = out.cpu().tolist()
+        if a.repeat:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            host = 0.0
+            s.record()
+            for _ in range(a.repeat):
+                kv.length = a.prompt
+                t0 = time.perf_counter()
+                eng.decode(kv, first, a.prompt, a.tokens, out=out)
+                host += time.perf_counter() - t0
+            e.record()
+            torch.cuda.synchronize()
+            n = a.repeat * a.tokens
+            results[label] = {"device_ms_per_token": s.elapsed_time(e) / n, "host_enqueue_ms_per_token": 1000 * host / n,
+                             "tokens_equal": out.cpu().tolist() == ref}
+        eng.close()
+        del eng, kv
+        torch.cuda.empty_cache()
+    print(json.dumps({"model": a.model, "prompt": a.prompt, "tokens": a.tokens, "results": results}))
+
+
+if __name__ == "__main__":
+    main()
