@@ -188,7 +188,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     GemvParams p = e->g_head;
     p.xin = e->x;
     p.gain = e->final_norm;
-    set_prefetch(e, p, e->off_head, (size_t)c.vocab * H * 2);
+    set_prefetch(e, p, e->off_head, align_up(c.vocab, 16) * H * 2);
     SP_CUDA(launch_gemv(PRO_NORM, EPI_LMHEAD, p, lc));
     return SP_OK;
 }
@@ -270,8 +270,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         return fail(SP_ERR_INVALID, "invalid Qwen2 head configuration");
     if (c.head_dim != 64 && c.head_dim != 128) return fail(SP_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
     if (c.heads / c.kv_heads > 8) return fail(SP_ERR_UNSUPPORTED, "more than 8 q heads per kv head");
-    if (c.hidden % 16 || c.intermediate % 16 || c.vocab % 16)
-        return fail(SP_ERR_UNSUPPORTED, "hidden, intermediate and vocab must be multiples of 16");
+    if (c.hidden % 16 || c.intermediate % 16)
+        return fail(SP_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 16");
     if (c.weight_format == SP_WEIGHTS_I8_B32)
         return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights are not built in this version");
     if (c.weight_format != SP_WEIGHTS_F16) return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
@@ -295,6 +295,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
     const size_t H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
+    const size_t VP = align_up(V, 16);      // LM head rows padded to whole 16-row strips
     const size_t QR = (size_t)(c.heads + 2 * c.kv_heads) * HD;
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
@@ -307,7 +308,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         lo[l].gu = take(2 * I * H * 2);
         lo[l].dn = take(H * I * 2);
     }
-    const size_t o_head = take(V * H * 2);
+    const size_t o_head = take(VP * H * 2);
     const size_t stream_end = off;
     const size_t o_embed = take(V * H * 2);
     const size_t o_fnorm = take(H * 4);
@@ -336,7 +337,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // ---- pack ------------------------------------------------------------------------------
     // Row maps (packed row -> source row): QKV rows are reordered so the two rows of a RoPE pair
     // (d, d + head_dim/2) of a head are adjacent; gate and up rows are interleaved (gate_i, up_i).
-    const size_t n_iota = std::max(std::max(V, 2 * I), std::max(QR, H));
+    const size_t n_iota = std::max(std::max(VP, 2 * I), std::max(QR, H));
     std::vector<int> idx(QR + 2 * I + n_iota);
     int *h_perm = idx.data(), *h_gu = idx.data() + QR, *h_iota = idx.data() + QR + 2 * I;
     for (size_t r = 0; r < QR; ++r) {
@@ -348,12 +349,16 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         h_gu[2 * i + 1] = (int)(I + i);
     }
     for (size_t i = 0; i < n_iota; ++i) h_iota[i] = (int)i;
+    std::vector<int> head_rows(VP);
+    for (size_t i = 0; i < VP; ++i) head_rows[i] = i < V ? (int)i : -1;
+    idx.insert(idx.end(), head_rows.begin(), head_rows.end());
     SP_TRY(cudaMalloc(&d_idx, idx.size() * 4));
     SP_TRY(cudaMemcpy(d_idx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice));
+    const int *d_head_rows = d_idx + QR + 2 * I + n_iota;
     const int *d_perm = d_idx, *d_gu = d_idx + QR, *d_iota = d_idx + QR + 2 * I;
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
-    SP_TRY(launch_pack_fragments(A + o_head, head_src, (int)V, nullptr, d_iota, (int)V, (int)H, s));
+    SP_TRY(launch_pack_fragments(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H, s));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
@@ -427,7 +432,15 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->g_o = base(H, H);
     e->g_gu = base(2 * I, H);
     e->g_down = base(H, I);
-    e->g_head = base(V, H);
+    e->g_head = base(VP, H);
+    e->g_head.n_valid = (int)V;
+    if (env_flag("SEEDPLANE_VERBOSE", false)) {
+        const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
+        int k = 0;
+        for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
+            fprintf(stderr, "[seedplane] gemv %-8s N=%d K=%d tiles/unit=%d units/strip=%d stages=%d grid=%d smem=%zu\n",
+                    names[k++], p->N, p->K, p->nt, p->ks, p->stages, p->grid, gemv_smem_bytes(*p));
+    }
 
     // ---- workspace ------------------------------------------------------------------------
     size_t n_partial = 0, n_strips = 0;

@@ -28,6 +28,8 @@ namespace sp {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kMaxUnitsPerCta = 256;      // bounds the per-CTA array of unit row sums (16 KB)
+constexpr int kMaxStages = 16;
 
 SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
@@ -47,6 +49,14 @@ SP_DEVINL uint32_t pack_half2(__half lo, __half hi) {
     return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
+// The CTA whose unit range [floor(U*c/C), floor(U*(c+1)/C)) contains unit u.
+SP_DEVINL int cta_of(int u, int U, int C) {
+    int c = (int)(((long long)u * C) / U);
+    while (c > 0 && (long long)U * c / C > u) --c;
+    while (c + 1 < C && (long long)U * (c + 1) / C <= u) ++c;
+    return c;
+}
+
 template <int PRO, int EPI, int FMT>
 __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     static_assert(FMT == WF_F16, "fragment GEMV streams fp16 weights");
@@ -62,12 +72,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     uint8_t *ring = smem;
     uint32_t *xb = reinterpret_cast<uint32_t *>(smem + (size_t)S * unit_bytes);   // KT x 16 words
     float *red = reinterpret_cast<float *>(xb + (size_t)KT * 16);                  // 2 x 8 warps x 16
-    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * kWarps * 16);
-
     const int C = gridDim.x, c = blockIdx.x;
     const int U = (p.N / 16) * KS;
     const int u0 = (int)((long long)U * c / C), u1 = (int)((long long)U * (c + 1) / C);
     const int nu = u1 - u0;
+    const int upc = (U + C - 1) / C;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * kWarps * 16 + upc * 16);
     uint64_t policy = 0;
     if (p.evict_first) policy = policy_evict_first();
 
@@ -221,11 +231,11 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     int bi = INT_MAX;
     const int half_hd = p.hd / 2;
 
+    float *ysm = red + 2 * kWarps * 16;      // per-unit row sums of this CTA: nu x 16
     for (int i = 0; i < nu; ++i) {
         const int sidx = i % S;
         const uint32_t par = (uint32_t)(i / S) & 1u;
-        const int u = u0 + i;
-        const int strip = u / KS, seg = u - strip * KS;
+        const int seg = (u0 + i) % KS;
         const bool ok = mbar_wait_bounded(&bars[sidx], par);
         float *rb = red + (i & 1) * kWarps * 16;
         if (ok) {
@@ -254,67 +264,86 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
             return;
         }
         if (tid == 0 && i + S < nu) issue(i + S);
-
-        if (warp == 0) {
+        // Warp 2 (it issues no bulk copies) folds the 8 warp sums of this unit; warps may run one
+        // unit ahead because `red` is double buffered.
+        if (warp == 2 && lane < 16) {
             float y = 0.f;
-            if (lane < 16) {
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w) y += rb[w * 16 + lane];
+            for (int w = 0; w < kWarps; ++w) y += rb[w * 16 + lane];
+            ysm[i * 16 + lane] = y;
+        }
+    }
+    __syncthreads();
+
+    // ---- epilogues: every strip this CTA touched, 16 rows per half-warp -----------------------
+    // Units of one strip are summed in unit order. A strip whose units all lie in this CTA is
+    // finished here; a strip shared with neighbouring CTAs (at most the first and the last) posts
+    // its contribution and the last contributor sums all of them in segment order.
+    const int sA = u0 / KS, sB = (u1 - 1) / KS;
+    const int rows_here = (sB - sA + 1) * 16;
+    const unsigned half_mask = 0xffffu << (lane & 16);
+    for (int base = 0; base < rows_here; base += kThreads) {
+        const int t = base + tid;
+        if (t >= rows_here) continue;       // whole half-warps drop out together
+        const int r = t & 15, strip = sA + (t >> 4);
+        const int ua = max(u0, strip * KS), ub = min(u1, (strip + 1) * KS);
+        float y = 0.f;
+        for (int u = ua; u < ub; ++u) y += ysm[(u - u0) * 16 + r];
+        if (ua != strip * KS || ub != (strip + 1) * KS) {
+            float *slot = p.partial + ((size_t)strip * KS + (ua - strip * KS)) * 16;
+            slot[r] = y;
+            __threadfence();
+            __syncwarp(half_mask);
+            unsigned last = 0;
+            if (r == 0) {
+                const int need = cta_of(strip * KS + KS - 1, U, C) - cta_of(strip * KS, U, C) + 1;
+                last = atomicAdd(p.strip_cnt + strip, 1u) == (unsigned)(need - 1);
             }
-            bool fin = true;
-            if (KS > 1) {
-                if (lane < 16) p.partial[((size_t)strip * KS + seg) * 16 + lane] = y;
-                __threadfence();
-                __syncwarp();
-                unsigned last = 0;
-                if (lane == 0) last = atomicAdd(p.strip_cnt + strip, 1u) == (unsigned)(KS - 1);
-                last = __shfl_sync(0xffffffffu, last, 0);
-                fin = last != 0;
-                if (fin) {
-                    __threadfence();
-                    y = 0.f;
-                    if (lane < 16)
-                        for (int k2 = 0; k2 < KS; ++k2) y += __ldcg(p.partial + ((size_t)strip * KS + k2) * 16 + lane);
-                    if (lane == 0) p.strip_cnt[strip] = 0u;
-                }
+            last = __shfl_sync(half_mask, last, lane & 16);
+            if (!last) continue;
+            __threadfence();
+            float* all = p.partial + (size_t)strip * KS * 16;
+            y = 0.f;
+            for (int k2 = 0; k2 < KS; ++k2) {
+                y += __ldcg(all + k2 * 16 + r);
+                all[k2 * 16 + r] = 0.f;      // leave the slots zeroed for the next launch
             }
-            if (fin) {
-                const int row = strip * 16 + lane;
-                const float other = __shfl_xor_sync(0xffffffffu, y, 1);   // pair partner (row ^ 1)
-                if constexpr (EPI == EPI_RESID) {
-                    if (lane < 16) p.out[row] = p.out[row] + y;
-                } else if constexpr (EPI == EPI_LMHEAD) {
-                    if (lane < 16) {
-                        if (lg) lg[row] = y;
-                        if (y > bv) { bv = y; bi = row; }
+            if (r == 0) p.strip_cnt[strip] = 0u;
+        }
+        const int row = strip * 16 + r;
+        const float other = __shfl_xor_sync(half_mask, y, 1);   // pair partner (row ^ 1)
+        if constexpr (EPI == EPI_RESID) {
+            p.out[row] = p.out[row] + y;
+        } else if constexpr (EPI == EPI_LMHEAD) {
+            if (row < p.n_valid) {
+                if (lg) lg[row] = y;
+                if (y > bv) { bv = y; bi = row; }
+            }
+        } else if constexpr (EPI == EPI_SWIGLU) {
+            if ((r & 1) == 0) p.out[row / 2] = (y / (1.0f + expf(-y))) * other;
+        } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
+            if ((r & 1) == 0) {
+                const int P = row / 2;
+                const int hh = P / half_hd, dd = P - hh * half_hd;
+                const int lo = hh * p.hd + dd, hi = lo + half_hd;
+                const float y0 = y + p.bias[lo], y1 = other + p.bias[hi];
+                if (hh < p.nh + p.nkv) {
+                    const float cs = p.rope[((size_t)pos * half_hd + dd) * 2];
+                    const float sn = p.rope[((size_t)pos * half_hd + dd) * 2 + 1];
+                    const float o0 = __fadd_rn(__fmul_rn(y0, cs), -__fmul_rn(y1, sn));
+                    const float o1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
+                    if (hh < p.nh) {
+                        p.out[lo] = o0;
+                        p.out[hi] = o1;
+                    } else {
+                        __half *kr = p.kc + ((size_t)(hh - p.nh) * p.cap + slot) * p.hd;
+                        kr[dd] = __float2half_rn(o0);
+                        kr[dd + half_hd] = __float2half_rn(o1);
                     }
-                } else if constexpr (EPI == EPI_SWIGLU) {
-                    if (lane < 16 && (lane & 1) == 0) p.out[row / 2] = (y / (1.0f + expf(-y))) * other;
-                } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
-                    if (lane < 16 && (lane & 1) == 0) {
-                        const int P = row / 2;
-                        const int hh = P / half_hd, dd = P - hh * half_hd;
-                        const int lo = hh * p.hd + dd, hi = lo + half_hd;
-                        const float y0 = y + p.bias[lo], y1 = other + p.bias[hi];
-                        if (hh < p.nh + p.nkv) {
-                            const float cs = p.rope[((size_t)pos * half_hd + dd) * 2];
-                            const float sn = p.rope[((size_t)pos * half_hd + dd) * 2 + 1];
-                            const float o0 = __fadd_rn(__fmul_rn(y0, cs), -__fmul_rn(y1, sn));
-                            const float o1 = __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn));
-                            if (hh < p.nh) {
-                                p.out[lo] = o0;
-                                p.out[hi] = o1;
-                            } else {
-                                __half *kr = p.kc + ((size_t)(hh - p.nh) * p.cap + slot) * p.hd;
-                                kr[dd] = __float2half_rn(o0);
-                                kr[dd + half_hd] = __float2half_rn(o1);
-                            }
-                        } else {
-                            __half *vr = p.vc + ((size_t)(hh - p.nh - p.nkv) * p.cap + slot) * p.hd;
-                            vr[dd] = __float2half_rn(y0);
-                            vr[dd + half_hd] = __float2half_rn(y1);
-                        }
-                    }
+                } else {
+                    __half *vr = p.vc + ((size_t)(hh - p.nh - p.nkv) * p.cap + slot) * p.hd;
+                    vr[dd] = __float2half_rn(y0);
+                    vr[dd + half_hd] = __float2half_rn(y1);
                 }
             }
         }
@@ -358,7 +387,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
         if (tid == 0) {
             for (int w = 1; w < kWarps; ++w) argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
             int tok = s_idx[0];
-            if (tok < 0 || tok >= p.N) {
+            if (tok < 0 || tok >= p.n_valid) {
                 atomicCAS(&st->err, 0, kErrBadToken);
                 tok = 0;
             }
@@ -547,17 +576,21 @@ __global__ void k_pack_fragments(uint8_t *dst, const __half *a, int rows_a, cons
     if (tile >= (long long)(N / 16) * KT) return;
     const int lane = threadIdx.x & 31, g = lane >> 2, cc = lane & 3;
     const int s = (int)(tile / KT), t = (int)(tile % KT);
-    auto row_ptr = [&](int r) {
+    auto row_ptr = [&](int r) -> const __half * {
         const int src = row_of[r];
+        if (src < 0) return nullptr;
         return src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
+    };
+    auto pair = [](const __half *row, int k) -> uint32_t {
+        return row ? *reinterpret_cast<const uint32_t *>(row + k) : 0u;
     };
     const __half *r0 = row_ptr(16 * s + g), *r1 = row_ptr(16 * s + g + 8);
     const int k0 = 16 * t + 2 * cc;
     uint4 v;
-    v.x = *reinterpret_cast<const uint32_t *>(r0 + k0);
-    v.y = *reinterpret_cast<const uint32_t *>(r1 + k0);
-    v.z = *reinterpret_cast<const uint32_t *>(r0 + k0 + 8);
-    v.w = *reinterpret_cast<const uint32_t *>(r1 + k0 + 8);
+    v.x = pair(r0, k0);
+    v.y = pair(r1, k0);
+    v.z = pair(r0, k0 + 8);
+    v.w = pair(r1, k0 + 8);
     *reinterpret_cast<uint4 *>(dst + ((size_t)tile * 32 + lane) * 16) = v;
 }
 
@@ -597,16 +630,31 @@ static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// Units per CTA the busiest CTA streams.
+static long long max_units_per_cta(long long U, long long C) { return (U + C - 1) / C; }
+
 void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
-    // Choose tiles per unit (a divisor of K/16) minimising the tiles streamed by the busiest CTA;
-    // split strips (ks > 1) cost a little extra (partials), larger units win ties.
+    // Pick tiles per unit (a divisor of K/16). Model, in SM cycles: a unit costs the larger of its
+    // HBM share (~23 bytes/cycle/SM at the measured copy bandwidth) and its issue time (about 60
+    // cycles per MMA round of the 8 warps plus ~100 of per-unit overhead); strips split across
+    // CTAs add a cross-CTA merge (~4000 cycles). Units per CTA are capped by the shared array.
+    // The ring must also keep ~48 KB per SM in flight (latency x bandwidth) when the CTA has that
+    // much to stream.
     const int KT = p.K / 16, strips = p.N / 16;
     double best = 1e300;
+    p.nt = 0;
     for (int nt = 1; nt <= KT; ++nt) {
         if (KT % nt || nt * kTileBytes > max_unit_bytes) continue;
         const long long U = (long long)strips * (KT / nt);
         const long long C = std::min<long long>(num_sms, U);
-        const double cost = (double)((U + C - 1) / C) * nt * (KT / nt > 1 ? 1.01 : 1.0);
+        const long long upc = max_units_per_cta(U, C);
+        if (upc > kMaxUnitsPerCta) continue;
+        const long long unit_bytes = (long long)nt * kTileBytes;
+        const long long stages = std::min<long long>(kMaxStages, ring_bytes / unit_bytes);
+        if (stages < 2) continue;
+        if (stages * unit_bytes < std::min<long long>(48 * 1024, upc * unit_bytes)) continue;
+        const double unit = std::max(unit_bytes / 23.0, 60.0 * ((nt + kWarps - 1) / kWarps) + 100.0) + 60.0;
+        const double cost = upc * unit + (KT / nt > 1 ? 2000.0 : 0.0);
         if (cost < best - 1e-9 || (std::abs(cost - best) <= 1e-9 && nt > p.nt)) {
             best = cost;
             p.nt = nt;
@@ -615,11 +663,14 @@ void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
     p.ks = KT / p.nt;
     const long long U = (long long)strips * p.ks;
     p.grid = (int)std::min<long long>(num_sms, U);
-    p.stages = std::max(2, std::min(8, ring_bytes / (p.nt * kTileBytes)));
+    p.stages = std::max(2, std::min(kMaxStages, ring_bytes / (p.nt * kTileBytes)));
 }
 
 size_t gemv_smem_bytes(const GemvParams &p) {
-    return (size_t)p.stages * p.nt * kTileBytes + (size_t)(p.K / 16) * 64 + 2 * kWarps * 16 * 4 + (size_t)p.stages * 8;
+    const long long U = (long long)(p.N / 16) * p.ks;
+    const size_t upc = (size_t)max_units_per_cta(U, p.grid);
+    return (size_t)p.stages * p.nt * kTileBytes + (size_t)(p.K / 16) * 64 + 2 * kWarps * 16 * 4 + upc * 16 * 4 +
+           (size_t)p.stages * 8;
 }
 
 template <int PRO, int EPI, int FMT>

@@ -48,6 +48,7 @@ struct GemvParams {
     float *partial;
     unsigned *strip_cnt;
     // LM head
+    int n_valid;             // rows >= n_valid are zero padding (vocab rounded up to 16)
     float *part_val;
     int *part_idx;
     unsigned *counter;
@@ -90,7 +91,8 @@ cudaError_t launch_set_state(DevState *st, const DevState &init, cudaStream_t s)
 cudaError_t launch_gather_rows(uint8_t *dst, const uint8_t *src, const int *src_row, int rows, int row_bytes,
                                int dst_mul, int dst_add, cudaStream_t s);
 // Fragment-pack an fp16 matrix of N x K: packed row r is source row row_of[r] of `a` when
-// row_of[r] < rows_a, else row row_of[r] - rows_a of `b` (gate/up interleave, RoPE pairing).
+// row_of[r] < rows_a, else row row_of[r] - rows_a of `b` (gate/up interleave, RoPE pairing);
+// row_of[r] < 0 is a zero row (padding).
 cudaError_t launch_pack_fragments(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
                                   int N, int K, cudaStream_t s);
 cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap, int hd, const int *src_slots,
