@@ -676,8 +676,14 @@ size_t gemv_smem_bytes(const GemvParams &p) {
 template <int PRO, int EPI, int FMT>
 static cudaError_t gemv_t(const GemvParams &p, const LaunchCfg *lc) {
     const size_t smem = gemv_smem_bytes(p);
-    if (lc == nullptr)
+    if (lc == nullptr) {
+        // One instantiation serves several matrices (O and down): only ever raise its opt-in.
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<PRO, EPI, FMT>);
+        if (e != cudaSuccess) return e;
+        if ((size_t)fa.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
         return cudaFuncSetAttribute(k_gemv<PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
     return launch_ex(k_gemv<PRO, EPI, FMT>, dim3(p.grid), dim3(kThreads), smem, *lc, p);
 }
 
