@@ -53,7 +53,7 @@ struct LayerDev {
 
 // Stage ring per GEMV CTA. CTAs of consecutive kernels share an SM under programmatic dependent
 // launch, so ring + input fragments stay near half of the 227 KB of shared memory.
-constexpr int kRingBytes = 80 * 1024;
+constexpr int kRingBytes = 96 * 1024;
 constexpr int kMaxUnitBytes = 32 * 1024;
 constexpr int kAttnMaxSplit = 64;
 constexpr int kAttnMinChunk = 32;
@@ -492,6 +492,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     SP_TRY(prepare_gemv(PRO_NORM, EPI_SWIGLU, e->g_gu));
     SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_down));
     SP_TRY(prepare_gemv(PRO_NORM, EPI_LMHEAD, e->g_head));
+    SP_TRY(prepare_attention());
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
     e->cap_stream = s;

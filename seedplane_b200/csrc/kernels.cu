@@ -30,6 +30,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxUnitsPerCta = 256;      // bounds the per-CTA array of unit row sums (16 KB)
 constexpr int kMaxStages = 16;
+constexpr int kMaxUnitTiles = 64;         // tiles per unit (32 KB): 8 per warp, held in registers
 
 SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
@@ -232,26 +233,28 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     const int half_hd = p.hd / 2;
 
     float *ysm = red + 2 * kWarps * 16;      // per-unit row sums of this CTA: nu x 16
+    // Per unit: each warp copies its tiles (A fragments) and the matching B fragments to registers,
+    // one barrier, and the stage is refilled BEFORE the MMAs run, so the copy engine never waits
+    // for tensor-core work. The 8 warp sums of unit i are folded by warp 2 (it issues no bulk
+    // copies) after the next barrier; `red` is double buffered for that.
+    constexpr int kMaxTPW = kMaxUnitTiles / kWarps;     // tiles per warp per unit
     for (int i = 0; i < nu; ++i) {
         const int sidx = i % S;
         const uint32_t par = (uint32_t)(i / S) & 1u;
         const int seg = (u0 + i) % KS;
         const bool ok = mbar_wait_bounded(&bars[sidx], par);
-        float *rb = red + (i & 1) * kWarps * 16;
-        if (ok) {
-            const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
-            const uint32_t *xw = xb + (size_t)seg * NT * 16;
-            float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-            for (int j = warp; j < NT; j += kWarps) {
-                const uint4 a = *reinterpret_cast<const uint4 *>(stage + (size_t)j * kTileBytes + lane * 16);
-                uint2 b = make_uint2(0u, 0u);
-                if (lane < 8) b = *reinterpret_cast<const uint2 *>(xw + j * 16 + lane * 2);
-                mma_16816(d, a, b.x, b.y);
-            }
-            if ((lane & 3) == 0) {
-                rb[warp * 16 + (lane >> 2)] = d[0] + d[1];
-                rb[warp * 16 + (lane >> 2) + 8] = d[2] + d[3];
+        uint4 af[kMaxTPW];
+        uint2 bf[kMaxTPW];
+        const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
+        const uint32_t *xw = xb + (size_t)seg * NT * 16;
+#pragma unroll
+        for (int q = 0; q < kMaxTPW; ++q) {
+            const int j = warp + q * kWarps;
+            af[q] = make_uint4(0u, 0u, 0u, 0u);
+            bf[q] = make_uint2(0u, 0u);
+            if (ok && j < NT) {
+                af[q] = *reinterpret_cast<const uint4 *>(stage + (size_t)j * kTileBytes + lane * 16);
+                if (lane < 8) bf[q] = *reinterpret_cast<const uint2 *>(xw + j * 16 + lane * 2);
             }
         }
         if (!__syncthreads_and(ok)) {
@@ -264,14 +267,32 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
             return;
         }
         if (tid == 0 && i + S < nu) issue(i + S);
-        // Warp 2 (it issues no bulk copies) folds the 8 warp sums of this unit; warps may run one
-        // unit ahead because `red` is double buffered.
-        if (warp == 2 && lane < 16) {
+        if (warp == 2 && lane < 16 && i > 0) {       // fold unit i-1 (all its sums are written)
+            const float *rp = red + ((i - 1) & 1) * kWarps * 16;
             float y = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) y += rb[w * 16 + lane];
-            ysm[i * 16 + lane] = y;
+            for (int w = 0; w < kWarps; ++w) y += rp[w * 16 + lane];
+            ysm[(i - 1) * 16 + lane] = y;
         }
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < kMaxTPW; q += 2) {
+            if (warp + q * kWarps < NT) mma_16816(d0, af[q], bf[q].x, bf[q].y);
+            if (q + 1 < kMaxTPW && warp + (q + 1) * kWarps < NT) mma_16816(d1, af[q + 1], bf[q + 1].x, bf[q + 1].y);
+        }
+        float *rb = red + (i & 1) * kWarps * 16;
+        if ((lane & 3) == 0) {
+            rb[warp * 16 + (lane >> 2)] = (d0[0] + d0[1]) + (d1[0] + d1[1]);
+            rb[warp * 16 + (lane >> 2) + 8] = (d0[2] + d0[3]) + (d1[2] + d1[3]);
+        }
+    }
+    __syncthreads();
+    if (warp == 2 && lane < 16 && nu > 0) {
+        const float *rp = red + ((nu - 1) & 1) * kWarps * 16;
+        float y = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) y += rp[w * 16 + lane];
+        ysm[(nu - 1) * 16 + lane] = y;
     }
     __syncthreads();
 
@@ -644,7 +665,7 @@ void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
     double best = 1e300;
     p.nt = 0;
     for (int nt = 1; nt <= KT; ++nt) {
-        if (KT % nt || nt * kTileBytes > max_unit_bytes) continue;
+        if (KT % nt || nt * kTileBytes > max_unit_bytes || nt > kMaxUnitTiles) continue;
         const long long U = (long long)strips * (KT / nt);
         const long long C = std::min<long long>(num_sms, U);
         const long long upc = max_units_per_cta(U, C);
@@ -679,7 +700,10 @@ static cudaError_t gemv_t(const GemvParams &p, const LaunchCfg *lc) {
     if (lc == nullptr) {
         // One instantiation serves several matrices (O and down): only ever raise its opt-in.
         cudaFuncAttributes fa;
-        cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<PRO, EPI, FMT>);
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<PRO, EPI, FMT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncGetAttributes(&fa, k_gemv<PRO, EPI, FMT>);
         if (e != cudaSuccess) return e;
         if ((size_t)fa.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
         return cudaFuncSetAttribute(k_gemv<PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -704,6 +728,14 @@ cudaError_t prepare_gemv(int pro, int epi, const GemvParams &p) { return gemv_di
 
 cudaError_t launch_gemv(int pro, int epi, const GemvParams &p, const LaunchCfg &lc) {
     return gemv_dispatch(pro, epi, p, &lc);
+}
+
+cudaError_t prepare_attention() {
+    cudaError_t e = cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
 }
 
 cudaError_t launch_attention(const AttnParams &p, const LaunchCfg &lc) {

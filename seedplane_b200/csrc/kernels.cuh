@@ -83,6 +83,7 @@ size_t gemv_smem_bytes(const GemvParams &p);
 // Set the dynamic shared-memory limit of the kernel instance (call before any stream capture).
 cudaError_t prepare_gemv(int pro, int epi, const GemvParams &p);
 cudaError_t launch_gemv(int pro, int epi, const GemvParams &p, const LaunchCfg &lc);
+cudaError_t prepare_attention();
 cudaError_t launch_attention(const AttnParams &p, const LaunchCfg &lc);
 
 // Host-side launches of small utility kernels.
