@@ -124,6 +124,14 @@ int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const in
  * rollback by truncation (benchmark_speculative.py:119,127) for tree-shaped drafts. */
 int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stream);
 
+/* Kernel timeline of the last step, when the engine was created with SEEDPLANE_TRACE=1: for each
+ * GEMV of the step (4 per layer, then the LM head) and each CTA, kernel-start / dependency-wait /
+ * prologue / stream / epilogue stamps and per-unit issue and ready stamps of %globaltimer (ns).
+ * host_out NULL: returns the number of 64-bit words; else copies them (synchronizes the device)
+ * and returns the count. Returns 0 when tracing is off. The reference had no GPU timestamps
+ * (experiments/v18/RESULTS.md:29-30). */
+int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity);
+
 /* Wait for `stream`, then report (and clear) a device-side error status recorded by a kernel since
  * the last call: SP_ERR_DEVICE with a message, or SP_OK. Kernels never trap; a bad token id, an
  * out-of-table position or an expired bounded wait is recorded here instead. */

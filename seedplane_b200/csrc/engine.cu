@@ -97,6 +97,8 @@ struct sp_engine {
     float *lm_val = nullptr;
     int *lm_idx = nullptr;
     DevState *st = nullptr;
+    unsigned long long *trace = nullptr;    // [kernel of the step][CTA][kTraceWords], SEEDPLANE_TRACE=1
+    int trace_kernels = 0;
     // planned GEMV geometry (pointers filled per layer at record time)
     GemvParams g_qkv{}, g_o{}, g_gu{}, g_down{}, g_head{};
     cudaStream_t cap_stream = nullptr;
@@ -124,8 +126,13 @@ void set_prefetch(const sp_engine *e, GemvParams &p, size_t off, size_t bytes) {
     }
 }
 
+unsigned long long *trace_slot(sp_engine *e, int k) {
+    return e->trace ? e->trace + (size_t)k * e->num_sms * kTraceWords : nullptr;
+}
+
 int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     const sp_config &c = e->c;
+    int kidx = 0;       // GEMV index within the step (trace slot)
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const size_t H = c.hidden, I = c.intermediate, QR = (size_t)(c.heads + 2 * c.kv_heads) * c.head_dim;
     for (int l = 0; l < c.layers; ++l) {
@@ -141,6 +148,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.vc = kv->v + l * kv_layer;
         p.cap = kv->capacity;
         set_prefetch(e, p, L.off_qkv, QR * H * 2);
+        p.trace = trace_slot(e, kidx++);
         const int pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM;
         SP_CUDA(launch_gemv(pro, EPI_QKV, p, lc));
         lc.pdl = e->pdl;
@@ -167,6 +175,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.xin = e->attn;
         p.out = e->x;
         set_prefetch(e, p, L.off_o, H * H * 2);
+        p.trace = trace_slot(e, kidx++);
         SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
 
         p = e->g_gu;
@@ -175,6 +184,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.gain = L.post_norm;
         p.out = e->act;
         set_prefetch(e, p, L.off_gu, 2 * I * H * 2);
+        p.trace = trace_slot(e, kidx++);
         SP_CUDA(launch_gemv(PRO_NORM, EPI_SWIGLU, p, lc));
 
         p = e->g_down;
@@ -182,6 +192,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.xin = e->act;
         p.out = e->x;
         set_prefetch(e, p, L.off_dn, H * I * 2);
+        p.trace = trace_slot(e, kidx++);
         SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
     }
     LaunchCfg lc{s, e->pdl};
@@ -189,6 +200,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     p.xin = e->x;
     p.gain = e->final_norm;
     set_prefetch(e, p, e->off_head, align_up(c.vocab, 16) * H * 2);
+    p.trace = trace_slot(e, kidx++);
     SP_CUDA(launch_gemv(PRO_NORM, EPI_LMHEAD, p, lc));
     return SP_OK;
 }
@@ -495,6 +507,11 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     SP_TRY(prepare_attention());
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
+    if (env_flag("SEEDPLANE_TRACE", false)) {
+        e->trace_kernels = 4 * c.layers + 1;
+        SP_TRY(cudaMalloc(&e->trace, (size_t)e->trace_kernels * e->num_sms * kTraceWords * 8));
+        SP_TRY(cudaMemset(e->trace, 0, (size_t)e->trace_kernels * e->num_sms * kTraceWords * 8));
+    }
     e->cap_stream = s;
     s = nullptr;
 #undef SP_TRY
@@ -510,6 +527,7 @@ void sp_engine_destroy(sp_engine *e) {
     if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
     cudaFree(e->arena);
     cudaFree(e->ws);
+    cudaFree(e->trace);
     delete e;
 }
 
@@ -671,6 +689,19 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
                              kv->length, (cudaStream_t)stream));
     kv->length += n;
     return SP_OK;
+}
+
+int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    if (!e->trace) return 0;
+    const int64_t n = (int64_t)e->trace_kernels * e->num_sms * kTraceWords;
+    if (!host_out) return n;
+    if (capacity < n) return fail(SP_ERR_CAPACITY, "trace needs %lld words", (long long)n);
+    cudaError_t ce = cudaSetDevice(e->device);
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    if (ce == cudaSuccess) ce = cudaMemcpy(host_out, e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "trace copy: %s", cudaGetErrorString(ce));
+    return n;
 }
 
 int sp_device_status(sp_engine *e, void *stream) {

@@ -82,7 +82,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     uint64_t policy = 0;
     if (p.evict_first) policy = policy_evict_first();
 
+    unsigned long long *tr = p.trace ? p.trace + (size_t)c * kTraceWords : nullptr;
+    if (tr && tid == 0) tr[0] = globaltimer();
     auto issue = [&](int i) {
+        if (tr && i < kTraceUnits) tr[8 + i] = globaltimer();
         const int u = u0 + i, st_ = i % S;
         const int strip = u / KS, seg = u - strip * KS;
         const uint8_t *src = p.w + ((size_t)strip * KT + (size_t)seg * NT) * kTileBytes;
@@ -111,6 +114,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     __syncthreads();
     griddep_wait();
     griddep_launch_dependents();
+    if (tr && tid == 0) tr[1] = globaltimer();
 
     DevState *st = p.st;
     // ---- prologue: fp32 input -> RMSNorm -> hi/lo fp16 B fragments in shared memory ----------
@@ -212,6 +216,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     }
     __syncthreads();
 
+    if (tr && tid == 0) tr[2] = globaltimer();
     // ---- per-step values --------------------------------------------------------------------
     int pos = 0, slot = 0;
     float *lg = nullptr;
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
         const uint32_t par = (uint32_t)(i / S) & 1u;
         const int seg = (u0 + i) % KS;
         const bool ok = mbar_wait_bounded(&bars[sidx], par);
+        if (tr && tid == 0 && i < kTraceUnits) tr[8 + kTraceUnits + i] = globaltimer();
         uint4 af[kMaxTPW];
         uint2 bf[kMaxTPW];
         const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
@@ -287,6 +293,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
         }
     }
     __syncthreads();
+    if (tr && tid == 0) tr[3] = globaltimer();
     if (warp == 2 && lane < 16 && nu > 0) {
         const float *rp = red + ((nu - 1) & 1) * kWarps * 16;
         float y = 0.f;
@@ -370,6 +377,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
         }
     }
 
+    if (tr) {
+        __syncthreads();
+        if (tid == 0) tr[4] = globaltimer();
+    }
     if constexpr (EPI == EPI_LMHEAD) {
         // CTA argmax (lowest index among equal maxima), then the last CTA reduces all CTAs.
 #pragma unroll

@@ -58,7 +58,15 @@ struct GemvParams {
     unsigned long long pf_bytes[kMaxPrefetch];
     int pf_n;
     int evict_first;         // stream weights with an L2 evict-first hint
+    // Optional trace (null = off): per CTA kTraceWords %globaltimer stamps, see kTrace* below.
+    unsigned long long *trace;
 };
+
+// Trace layout per CTA: [0] kernel start, [1] dependency wait returned, [2] prologue done,
+// [3] stream loop done, [4] epilogues done, [8 + i] unit i issued, [8 + kTraceUnits + i] unit i
+// ready (i < kTraceUnits).
+constexpr int kTraceUnits = 24;
+constexpr int kTraceWords = 8 + 2 * kTraceUnits;
 
 struct AttnParams {
     const float *q;          // [NH*HD] fp32 (RoPE applied)

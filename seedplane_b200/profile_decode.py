@@ -21,6 +21,47 @@ from .randinit import make_weights, random_prompt
 MODES = {"graph+pdl": ("1", "1"), "graph": ("1", "0"), "eager+pdl": ("0", "1"), "eager": ("0", "0")}
 
 
+KERNELS = ("qkv", "o", "gate_up", "down")
+
+
+def trace_summary(eng, layers_shown=(0, 1, 13)):
+    """Per-GEMV timeline of the last step from the %globaltimer stamps (microseconds)."""
+    import ctypes as C
+    import numpy as np
+    from . import _native as N
+    lib = N.load()
+    n = lib.sp_trace_read(eng.handle, None, 0)
+    if n <= 0:
+        return {}
+    buf = (C.c_uint64 * n)()
+    N.check(0 if lib.sp_trace_read(eng.handle, buf, n) == n else -2)
+    words = 8 + 2 * 24
+    t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(-1, torch.cuda.get_device_properties(
+        eng.device).multi_processor_count, words)
+    t0 = t[t > 0].min()
+    t = np.where(t > 0, (t - t0) / 1000.0, np.nan)
+    out, prev_end = [], None
+    nk = t.shape[0]
+    for k in range(nk):
+        layer, kind = (k // 4, KERNELS[k % 4]) if k < nk - 1 else (-1, "lm_head")
+        start, wait, pro, loop, epi = (t[k, :, j] for j in range(5))
+        issue, ready = t[k, :, 8:32], t[k, :, 32:56]
+        lat = ready - issue
+        row = {"k": k, "layer": layer, "kind": kind,
+               "start_min": np.nanmin(start), "start_max": np.nanmax(start),
+               "wait_ret_max": np.nanmax(wait), "prologue_med": np.nanmedian(pro - wait),
+               "stream_med": np.nanmedian(loop - pro), "stream_max": np.nanmax(loop - pro),
+               "epilogue_med": np.nanmedian(epi - loop), "end_max": np.nanmax(epi),
+               "unit_latency_med": np.nanmedian(lat), "ready_gap_med": np.nanmedian(np.diff(ready, axis=1)),
+               "gap_from_prev_end": None if prev_end is None else np.nanmin(start) - prev_end}
+        prev_end = np.nanmax(epi)
+        if layer in layers_shown or layer == -1:
+            out.append({key: (round(float(v), 2) if v is not None else None) if not isinstance(v, str) else v
+                        for key, v in row.items()})
+    total = float(np.nanmax(t[nk - 1, :, 4]) - np.nanmin(t[0, :, 0]))
+    return {"step_span_us": round(total, 1), "kernels": out}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model", default="qwen2-1.5b", choices=sorted(PRESETS))
@@ -31,6 +72,7 @@ def main():
     ap.add_argument("--capacity", type=int, default=4096)
     ap.add_argument("--prefetch-mb", default="0", help="comma list of L2 prefetch distances (MB) to compare")
     ap.add_argument("--evict-first", default="0", help="comma list of 0/1: stream weights with evict-first")
+    ap.add_argument("--trace", action="store_true", help="print the kernel timeline of the last decode step")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
@@ -43,6 +85,7 @@ def main():
         graph, pdl = MODES[mode]
         os.environ["SEEDPLANE_GRAPH"], os.environ["SEEDPLANE_PDL"] = graph, pdl
         os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
+        os.environ["SEEDPLANE_TRACE"] = "1" if a.trace else "0"
         label = f"{mode} prefetch={pf}MB evict_first={ev}"
         eng = CudaQwen2(cfg, w)
         kv = eng.new_kv(a.capacity)
@@ -68,6 +111,8 @@ def main():
             n = a.repeat * a.tokens
             results[label] = {"device_ms_per_token": s.elapsed_time(e) / n, "host_enqueue_ms_per_token": 1000 * host / n,
                              "tokens_equal": out.cpu().tolist() == ref}
+        if a.trace:
+            results[label + " trace"] = trace_summary(eng)
         eng.close()
         del eng, kv
         torch.cuda.empty_cache()
