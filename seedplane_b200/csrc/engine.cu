@@ -55,8 +55,6 @@ struct LayerDev {
 // launch, so ring + input fragments stay near half of the 227 KB of shared memory.
 constexpr int kRingBytes = 96 * 1024;
 constexpr int kMaxUnitBytes = 32 * 1024;
-constexpr int kAttnMaxSplit = 64;
-constexpr int kAttnMinChunk = 32;
 
 }  // namespace
 
@@ -90,10 +88,10 @@ struct sp_engine {
     const float *rope = nullptr;
     std::vector<LayerDev> layers;
     // workspace
-    float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *apart = nullptr;
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
     float *partial = nullptr;
     unsigned *strip_cnt = nullptr;
-    unsigned *acnt = nullptr, *lm_cnt = nullptr;
+    unsigned *lm_cnt = nullptr;
     float *lm_val = nullptr;
     int *lm_idx = nullptr;
     DevState *st = nullptr;
@@ -158,14 +156,10 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         a.kc = kv->k + l * kv_layer;
         a.vc = kv->v + l * kv_layer;
         a.out = e->attn;
-        a.part = e->apart;
-        a.counter = e->acnt;
         a.nh = c.heads;
         a.nkv = c.kv_heads;
         a.hd = c.head_dim;
         a.cap = kv->capacity;
-        a.max_split = kAttnMaxSplit;
-        a.min_chunk = kAttnMinChunk;
         a.scale = 1.0f / sqrtf((float)c.head_dim);
         a.st = e->st;
         SP_CUDA(launch_attention(a, lc));
@@ -466,10 +460,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
-    const size_t w_apart = wtake((size_t)c.heads * kAttnMaxSplit * (HD + 2) * 4);
     const size_t w_partial = wtake(std::max<size_t>(n_partial, 1) * 4);
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
-    const size_t w_acnt = wtake((size_t)c.kv_heads * 4), w_lmcnt = wtake(4);
+    const size_t w_lmcnt = wtake(4);
     const size_t w_lmval = wtake((size_t)e->g_head.grid * 4), w_lmidx = wtake((size_t)e->g_head.grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
     e->ws_bytes = woff;
@@ -479,10 +472,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->q = (float *)(e->ws + w_q);
     e->attn = (float *)(e->ws + w_attn);
     e->act = (float *)(e->ws + w_act);
-    e->apart = (float *)(e->ws + w_apart);
     e->partial = (float *)(e->ws + w_partial);
     e->strip_cnt = (unsigned *)(e->ws + w_scnt);
-    e->acnt = (unsigned *)(e->ws + w_acnt);
     e->lm_cnt = (unsigned *)(e->ws + w_lmcnt);
     e->lm_val = (float *)(e->ws + w_lmval);
     e->lm_idx = (int *)(e->ws + w_lmidx);

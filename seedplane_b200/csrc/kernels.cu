@@ -12,25 +12,35 @@
 //              Replaces the Vulkan gemv/swiglu/rope_kv/argmax shaders
 //              (native/vulkan_decode/shaders/gemv.comp:23-51, swiglu.comp:20-44,
 //              rope_kv.comp:14-32, argmax.comp:8-22).
-// k_attn_decode -- GQA decode attention, split-K over the context: one CTA per (kv head, chunk)
-//              serves all q heads of its group, partial (max, sum, acc) per chunk, and the last CTA
-//              of a group to finish merges the partials (log-sum-exp) and writes the output.
+// k_attn_decode -- GQA decode attention, split over the context inside one thread-block cluster
+//              per kv head: each CTA of the cluster serves all q heads of the group over 1/8 of
+//              the positions (online softmax, fp32), then the partials (max, sum, acc) are merged
+//              by log-sum-exp through distributed shared memory, with no global round trip.
 //              Replaces attn_part.comp:15-44 + attn_combine.comp:8-19; the mask is the
 //              reference's `slot <= own slot` (qwen_engine.py:131-135) or a tree-ancestor mask.
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <type_traits>
 #include <utility>
+
+#include <cooperative_groups.h>
 
 #include "kernels.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace sp {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;            // consumer threads (8 warps) of a GEMV; other kernels' block
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxUnitsPerCta = 256;      // bounds the per-CTA array of unit row sums (16 KB)
+constexpr int kGemvThreads = kThreads + 32;   // + the producer warp
+constexpr int kMaxUnitsPerCta = 1024;     // bounds the per-CTA array of unit row sums (64 KB)
 constexpr int kMaxStages = 16;
-constexpr int kMaxUnitTiles = 64;         // tiles per unit (32 KB): 8 per warp, held in registers
+constexpr int kUnitTiles = 16;            // tiles per unit at most (8 KB): one warp holds them in registers
+
+// Barrier among the 8 consumer warps of a GEMV CTA (the producer warp does not take part).
+SP_DEVINL void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 
 SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
@@ -50,6 +60,10 @@ SP_DEVINL uint32_t pack_half2(__half lo, __half hi) {
     return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
+SP_DEVINL void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // The CTA whose unit range [floor(U*c/C), floor(U*(c+1)/C)) contains unit u.
 SP_DEVINL int cta_of(int u, int U, int C) {
     int c = (int)(((long long)u * C) / U);
@@ -59,7 +73,7 @@ SP_DEVINL int cta_of(int u, int U, int C) {
 }
 
 template <int PRO, int EPI, int FMT>
-__global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvParams p) {
     static_assert(FMT == WF_F16, "fragment GEMV streams fp16 weights");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_val[kWarps];
@@ -67,156 +81,215 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     __shared__ int s_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool producer = warp == kWarps;        // warp 8 issues the bulk copies
     const int S = p.stages, K = p.K, NT = p.nt, KS = p.ks;
     const int KT = K / 16;
     const int unit_bytes = NT * kTileBytes;
-    uint8_t *ring = smem;
-    uint32_t *xb = reinterpret_cast<uint32_t *>(smem + (size_t)S * unit_bytes);   // KT x 16 words
-    float *red = reinterpret_cast<float *>(xb + (size_t)KT * 16);                  // 2 x 8 warps x 16
     const int C = gridDim.x, c = blockIdx.x;
     const int U = (p.N / 16) * KS;
     const int u0 = (int)((long long)U * c / C), u1 = (int)((long long)U * (c + 1) / C);
     const int nu = u1 - u0;
     const int upc = (U + C - 1) / C;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * kWarps * 16 + upc * 16);
-    uint64_t policy = 0;
-    if (p.evict_first) policy = policy_evict_first();
+    uint8_t *ring = smem;
+    uint32_t *xb = reinterpret_cast<uint32_t *>(smem + (size_t)S * unit_bytes);   // KT x 16 words
+    float *ysm = reinterpret_cast<float *>(xb + (size_t)KT * 16);                  // upc x 16 row sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(ysm + (size_t)upc * 16);
+    uint64_t *empty = full + S;
 
     unsigned long long *tr = p.trace ? p.trace + (size_t)c * kTraceWords : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer();
-    auto issue = [&](int i) {
+    auto issue = [&](int i, uint64_t policy) {
         if (tr && i < kTraceUnits) tr[8 + i] = globaltimer();
         const int u = u0 + i, st_ = i % S;
         const int strip = u / KS, seg = u - strip * KS;
         const uint8_t *src = p.w + ((size_t)strip * KT + (size_t)seg * NT) * kTileBytes;
-        mbar_arrive_expect_tx(&bars[st_], (uint32_t)unit_bytes);
-        if (p.evict_first) bulk_g2s_hint(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &bars[st_], policy);
-        else bulk_g2s(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &bars[st_]);
+        mbar_arrive_expect_tx(&full[st_], (uint32_t)unit_bytes);
+        if (p.evict_first) bulk_g2s_hint(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &full[st_], policy);
+        else bulk_g2s(ring + (size_t)st_ * unit_bytes, src, (uint32_t)unit_bytes, &full[st_]);
     };
 
-    // Weights do not depend on the previous kernel: start streaming them, and warm L2 with the
-    // weight stream further ahead, before the dependency wait.
     if (tid == 0) {
-        for (int i = 0; i < S; ++i) mbar_init(&bars[i], 1);
-        fence_mbar_init();
-        for (int i = 0; i < min(S, nu); ++i) issue(i);
-    }
-    if (tid == 32) {
-        for (int r = 0; r < p.pf_n; ++r) {
-            const unsigned long long share = (p.pf_bytes[r] / C + 15) & ~15ull;
-            const unsigned long long beg = share * c;
-            if (beg >= p.pf_bytes[r]) continue;
-            const unsigned long long end = min(beg + share, p.pf_bytes[r]) & ~15ull;
-            for (unsigned long long o = beg; o < end; o += 32768)
-                prefetch_l2(p.pf_ptr[r] + o, (uint32_t)min(32768ull, end - o));
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
         }
+        fence_mbar_init();
     }
     __syncthreads();
-    griddep_wait();
-    griddep_launch_dependents();
-    if (tr && tid == 0) tr[1] = globaltimer();
-
     DevState *st = p.st;
-    // ---- prologue: fp32 input -> RMSNorm -> hi/lo fp16 B fragments in shared memory ----------
-    // Pass A stores the raw fp32 input at its natural index in the fragment buffer (K floats fill
-    // it exactly) with coalesced loads; pass B turns each k-tile's 16 floats (64 bytes) into that
-    // tile's 64-byte fragment in place: lanes 0-3 hold the fp16 "hi" column, lanes 4-7 the "lo".
-    float *xs = reinterpret_cast<float *>(xb);
-    float ss = 0.f;
-    if constexpr (PRO == PRO_EMBED_NORM) {
-        int tok = st->token;
-        if (tok < 0 || tok >= p.vocab) {
-            if (tid == 0) atomicCAS(&st->err, 0, kErrBadToken);
-            tok = 0;
-        }
-        const uint4 *e4 = reinterpret_cast<const uint4 *>(p.embed + (size_t)tok * K);
-        for (int v = tid; v < K / 8; v += kThreads) {
-            const uint4 raw = e4[v];
-            const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-            float f[8];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 t2 = __half22float2(h2[j]);
-                f[2 * j] = t2.x;
-                f[2 * j + 1] = t2.y;
+
+    if (producer) {
+        // ---- producer warp: weights do not depend on the previous kernel, so the ring is filled
+        // and L2 is warmed with the weight stream further ahead before any dependency wait. ------
+        if (lane == 0) {
+            const uint64_t policy = p.evict_first ? policy_evict_first() : 0ull;
+            for (int i = 0; i < min(S, nu); ++i) issue(i, policy);
+            for (int r = 0; r < p.pf_n; ++r) {
+                const unsigned long long share = (p.pf_bytes[r] / C + 15) & ~15ull;
+                const unsigned long long beg = share * c;
+                if (beg >= p.pf_bytes[r]) continue;
+                const unsigned long long end = min(beg + share, p.pf_bytes[r]) & ~15ull;
+                for (unsigned long long o = beg; o < end; o += 32768)
+                    prefetch_l2(p.pf_ptr[r] + o, (uint32_t)min(32768ull, end - o));
             }
-            float4 *dst = reinterpret_cast<float4 *>(xs + 8 * v);
-            dst[0] = make_float4(f[0], f[1], f[2], f[3]);
-            dst[1] = make_float4(f[4], f[5], f[6], f[7]);
-            if (c == 0) {
-                float4 *xi = reinterpret_cast<float4 *>(p.x_init + 8 * v);
-                xi[0] = dst[0];
-                xi[1] = dst[1];
+            for (int i = S; i < nu; ++i) {
+                // stage i % S is free once its previous unit (i - S) has been read by its warp
+                if (!mbar_wait_bounded(&empty[i % S], (uint32_t)(i / S - 1) & 1u)) {
+                    atomicCAS(&st->err, 0, kErrMbarTimeout);
+                    break;
+                }
+                issue(i, policy);
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
         }
     } else {
-        const float4 *x4 = reinterpret_cast<const float4 *>(p.xin);
-        for (int v = tid; v < K / 4; v += kThreads) {
-            const float4 f = x4[v];
-            reinterpret_cast<float4 *>(xs)[v] = f;
-            if constexpr (PRO != PRO_PLAIN) {
-                ss = fmaf(f.x, f.x, ss);
-                ss = fmaf(f.y, f.y, ss);
-                ss = fmaf(f.z, f.z, ss);
-                ss = fmaf(f.w, f.w, ss);
+        griddep_wait();
+        griddep_launch_dependents();
+        if (tr && tid == 0) tr[1] = globaltimer();
+        // ---- prologue: fp32 input -> RMSNorm -> hi/lo fp16 B fragments in shared memory ------
+        // Pass A stores the raw fp32 input at its natural index in the fragment buffer (K floats
+        // fill it exactly) with coalesced loads; pass B turns each k-tile's 16 floats (64 bytes)
+        // into that tile's 64-byte fragment in place: lanes 0-3 hold the fp16 "hi" column,
+        // lanes 4-7 the "lo" remainder.
+        float *xs = reinterpret_cast<float *>(xb);
+        float ss = 0.f;
+        if constexpr (PRO == PRO_EMBED_NORM) {
+            int tok = st->token;
+            if (tok < 0 || tok >= p.vocab) {
+                if (tid == 0) atomicCAS(&st->err, 0, kErrBadToken);
+                tok = 0;
+            }
+            const uint4 *e4 = reinterpret_cast<const uint4 *>(p.embed + (size_t)tok * K);
+            for (int v = tid; v < K / 8; v += kThreads) {
+                const uint4 raw = e4[v];
+                const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                float f[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 t2 = __half22float2(h2[j]);
+                    f[2 * j] = t2.x;
+                    f[2 * j + 1] = t2.y;
+                }
+                float4 *dst = reinterpret_cast<float4 *>(xs + 8 * v);
+                dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+                dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+                if (c == 0) {
+                    float4 *xi = reinterpret_cast<float4 *>(p.x_init + 8 * v);
+                    xi[0] = dst[0];
+                    xi[1] = dst[1];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+            }
+        } else {
+            const float4 *x4 = reinterpret_cast<const float4 *>(p.xin);
+            for (int v = tid; v < K / 4; v += kThreads) {
+                const float4 f = x4[v];
+                reinterpret_cast<float4 *>(xs)[v] = f;
+                if constexpr (PRO != PRO_PLAIN) {
+                    ss = fmaf(f.x, f.x, ss);
+                    ss = fmaf(f.y, f.y, ss);
+                    ss = fmaf(f.z, f.z, ss);
+                    ss = fmaf(f.w, f.w, ss);
+                }
             }
         }
-    }
-    float inv = 1.f;
-    if constexpr (PRO != PRO_PLAIN) {
-        ss = warp_sum(ss);
-        if (lane == 0) s_val[warp] = ss;
-    }
-    __syncthreads();
-    if constexpr (PRO != PRO_PLAIN) {
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) tot += s_val[w];
-        inv = 1.0f / sqrtf(tot / (float)K + p.eps);
-    }
-    for (int t = tid; t < KT; t += kThreads) {
-        float v[16];
-        const float4 *src = reinterpret_cast<const float4 *>(xs + 16 * t);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 f = src[j];
-            v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
-        }
+        float inv = 1.f;
         if constexpr (PRO != PRO_PLAIN) {
-            const float4 *g4 = reinterpret_cast<const float4 *>(p.gain + 16 * t);
+            ss = warp_sum(ss);
+            if (lane == 0) s_val[warp] = ss;
+        }
+        consumer_sync();
+        if constexpr (PRO != PRO_PLAIN) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) tot += s_val[w];
+            inv = 1.0f / sqrtf(tot / (float)K + p.eps);
+        }
+        for (int t = tid; t < KT; t += kThreads) {
+            float v[16];
+            const float4 *src = reinterpret_cast<const float4 *>(xs + 16 * t);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float4 g = g4[j];
-                v[4 * j] = (v[4 * j] * inv) * g.x;
-                v[4 * j + 1] = (v[4 * j + 1] * inv) * g.y;
-                v[4 * j + 2] = (v[4 * j + 2] * inv) * g.z;
-                v[4 * j + 3] = (v[4 * j + 3] * inv) * g.w;
+                const float4 f = src[j];
+                v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+            }
+            if constexpr (PRO != PRO_PLAIN) {
+                const float4 *g4 = reinterpret_cast<const float4 *>(p.gain + 16 * t);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 gg = g4[j];
+                    v[4 * j] = (v[4 * j] * inv) * gg.x;
+                    v[4 * j + 1] = (v[4 * j + 1] * inv) * gg.y;
+                    v[4 * j + 2] = (v[4 * j + 2] * inv) * gg.z;
+                    v[4 * j + 3] = (v[4 * j + 3] * inv) * gg.w;
+                }
+            }
+            __half hi[16], lo[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                hi[j] = __float2half_rn(v[j]);
+                lo[j] = __float2half_rn(v[j] - __half2float(hi[j]));
+            }
+            uint32_t wds[16];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const int k0 = 2 * cc;
+                wds[cc * 2] = pack_half2(hi[k0], hi[k0 + 1]);
+                wds[cc * 2 + 1] = pack_half2(hi[k0 + 8], hi[k0 + 9]);
+                wds[8 + cc * 2] = pack_half2(lo[k0], lo[k0 + 1]);
+                wds[8 + cc * 2 + 1] = pack_half2(lo[k0 + 8], lo[k0 + 9]);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(xb + (size_t)t * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_uint4(wds[4 * j], wds[4 * j + 1], wds[4 * j + 2], wds[4 * j + 3]);
+        }
+        consumer_sync();
+        if (tr && tid == 0) tr[2] = globaltimer();
+
+        // ---- stream: warp w takes units w, w+8, ... Each unit: wait for its stage, copy the
+        // unit's A fragments to registers, release the stage to the producer, then run the MMAs
+        // with the B fragments of the unit's k-tiles. The unit's 16 row sums land in ysm. -------
+        for (int i = warp; i < nu; i += kWarps) {
+            const int sidx = i % S;
+            if (!mbar_wait_bounded(&full[sidx], (uint32_t)(i / S) & 1u)) {
+                if (lane == 0) atomicCAS(&st->err, 0, kErrMbarTimeout);
+                break;
+            }
+            if (tr && lane == 0 && i < kTraceUnits) tr[8 + kTraceUnits + i] = globaltimer();
+            const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
+            uint4 af[kUnitTiles];
+#pragma unroll
+            for (int q = 0; q < kUnitTiles; ++q)
+                af[q] = q < NT ? *reinterpret_cast<const uint4 *>(stage + (size_t)q * kTileBytes + lane * 16)
+                               : make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[sidx]);
+            const int seg = (u0 + i) % KS;
+            const uint32_t *xw = xb + (size_t)seg * NT * 16;
+            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int q = 0; q < kUnitTiles; q += 2) {
+                if (q < NT) {
+                    uint2 b = make_uint2(0u, 0u);
+                    if (lane < 8) b = *reinterpret_cast<const uint2 *>(xw + q * 16 + lane * 2);
+                    mma_16816(d0, af[q], b.x, b.y);
+                }
+                if (q + 1 < NT) {
+                    uint2 b = make_uint2(0u, 0u);
+                    if (lane < 8) b = *reinterpret_cast<const uint2 *>(xw + (q + 1) * 16 + lane * 2);
+                    mma_16816(d1, af[q + 1], b.x, b.y);
+                }
+            }
+            if ((lane & 3) == 0) {
+                ysm[i * 16 + (lane >> 2)] = (d0[0] + d0[1]) + (d1[0] + d1[1]);
+                ysm[i * 16 + (lane >> 2) + 8] = (d0[2] + d0[3]) + (d1[2] + d1[3]);
             }
         }
-        __half hi[16], lo[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            hi[j] = __float2half_rn(v[j]);
-            lo[j] = __float2half_rn(v[j] - __half2float(hi[j]));
-        }
-        uint32_t wds[16];
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-            const int k0 = 2 * cc;
-            wds[cc * 2] = pack_half2(hi[k0], hi[k0 + 1]);
-            wds[cc * 2 + 1] = pack_half2(hi[k0 + 8], hi[k0 + 9]);
-            wds[8 + cc * 2] = pack_half2(lo[k0], lo[k0 + 1]);
-            wds[8 + cc * 2 + 1] = pack_half2(lo[k0 + 8], lo[k0 + 9]);
-        }
-        uint4 *dst = reinterpret_cast<uint4 *>(xb + (size_t)t * 16);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = make_uint4(wds[4 * j], wds[4 * j + 1], wds[4 * j + 2], wds[4 * j + 3]);
     }
     __syncthreads();
+    if (tr && tid == 0) tr[3] = globaltimer();
+    if (producer) return;
 
-    if (tr && tid == 0) tr[2] = globaltimer();
     // ---- per-step values --------------------------------------------------------------------
     int pos = 0, slot = 0;
     float *lg = nullptr;
@@ -236,72 +309,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     float bv = -INFINITY;
     int bi = INT_MAX;
     const int half_hd = p.hd / 2;
-
-    float *ysm = red + 2 * kWarps * 16;      // per-unit row sums of this CTA: nu x 16
-    // Per unit: each warp copies its tiles (A fragments) and the matching B fragments to registers,
-    // one barrier, and the stage is refilled BEFORE the MMAs run, so the copy engine never waits
-    // for tensor-core work. The 8 warp sums of unit i are folded by warp 2 (it issues no bulk
-    // copies) after the next barrier; `red` is double buffered for that.
-    constexpr int kMaxTPW = kMaxUnitTiles / kWarps;     // tiles per warp per unit
-    for (int i = 0; i < nu; ++i) {
-        const int sidx = i % S;
-        const uint32_t par = (uint32_t)(i / S) & 1u;
-        const int seg = (u0 + i) % KS;
-        const bool ok = mbar_wait_bounded(&bars[sidx], par);
-        if (tr && tid == 0 && i < kTraceUnits) tr[8 + kTraceUnits + i] = globaltimer();
-        uint4 af[kMaxTPW];
-        uint2 bf[kMaxTPW];
-        const uint8_t *stage = ring + (size_t)sidx * unit_bytes;
-        const uint32_t *xw = xb + (size_t)seg * NT * 16;
-#pragma unroll
-        for (int q = 0; q < kMaxTPW; ++q) {
-            const int j = warp + q * kWarps;
-            af[q] = make_uint4(0u, 0u, 0u, 0u);
-            bf[q] = make_uint2(0u, 0u);
-            if (ok && j < NT) {
-                af[q] = *reinterpret_cast<const uint4 *>(stage + (size_t)j * kTileBytes + lane * 16);
-                if (lane < 8) bf[q] = *reinterpret_cast<const uint2 *>(xw + j * 16 + lane * 2);
-            }
-        }
-        if (!__syncthreads_and(ok)) {
-            // A stage never arrived: record it, wait (bounded) for copies still in flight, leave.
-            if (tid == 0) {
-                atomicCAS(&st->err, 0, kErrMbarTimeout);
-                for (int j = i; j < min(i + S, nu); ++j) mbar_wait_bounded(&bars[j % S], (uint32_t)(j / S) & 1u);
-            }
-            __syncthreads();
-            return;
-        }
-        if (tid == 0 && i + S < nu) issue(i + S);
-        if (warp == 2 && lane < 16 && i > 0) {       // fold unit i-1 (all its sums are written)
-            const float *rp = red + ((i - 1) & 1) * kWarps * 16;
-            float y = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) y += rp[w * 16 + lane];
-            ysm[(i - 1) * 16 + lane] = y;
-        }
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int q = 0; q < kMaxTPW; q += 2) {
-            if (warp + q * kWarps < NT) mma_16816(d0, af[q], bf[q].x, bf[q].y);
-            if (q + 1 < kMaxTPW && warp + (q + 1) * kWarps < NT) mma_16816(d1, af[q + 1], bf[q + 1].x, bf[q + 1].y);
-        }
-        float *rb = red + (i & 1) * kWarps * 16;
-        if ((lane & 3) == 0) {
-            rb[warp * 16 + (lane >> 2)] = (d0[0] + d0[1]) + (d1[0] + d1[1]);
-            rb[warp * 16 + (lane >> 2) + 8] = (d0[2] + d0[3]) + (d1[2] + d1[3]);
-        }
-    }
-    __syncthreads();
-    if (tr && tid == 0) tr[3] = globaltimer();
-    if (warp == 2 && lane < 16 && nu > 0) {
-        const float *rp = red + ((nu - 1) & 1) * kWarps * 16;
-        float y = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) y += rp[w * 16 + lane];
-        ysm[(nu - 1) * 16 + lane] = y;
-    }
-    __syncthreads();
 
     // ---- epilogues: every strip this CTA touched, 16 rows per half-warp -----------------------
     // Units of one strip are summed in unit order. A strip whose units all lie in this CTA is
@@ -378,7 +385,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
     }
 
     if (tr) {
-        __syncthreads();
+        consumer_sync();
         if (tid == 0) tr[4] = globaltimer();
     }
     if constexpr (EPI == EPI_LMHEAD) {
@@ -390,7 +397,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
             argmax_merge(bv, bi, ov, oi);
         }
         if (lane == 0) { s_val[warp] = bv; s_idx[warp] = bi; }
-        __syncthreads();
+        consumer_sync();
         if (tid == 0) {
             float v = s_val[0];
             int ix = s_idx[0];
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
             const unsigned old = atomicAdd(p.counter, 1u);
             s_flag = (old == (unsigned)C - 1u);
         }
-        __syncthreads();
+        consumer_sync();
         if (!s_flag) return;
         __threadfence();
         float v = -INFINITY;
@@ -413,9 +420,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
             const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
             argmax_merge(v, ix, ov, oi);
         }
-        __syncthreads();
+        consumer_sync();
         if (lane == 0) { s_val[warp] = v; s_idx[warp] = ix; }
-        __syncthreads();
+        consumer_sync();
         if (tid == 0) {
             for (int w = 1; w < kWarps; ++w) argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
             int tok = s_idx[0];
@@ -442,31 +449,33 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// GQA decode attention
+// GQA decode attention: one thread-block cluster of kAttnCluster CTAs per kv head
 // ---------------------------------------------------------------------------------------------
 constexpr int kMaxGroup = 8;
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
-    constexpr int DPL = HD / 32;
+    constexpr int DPL = HD / 32;                 // dims per lane
+    constexpr int PB = 4;                        // positions loaded per batch
     __shared__ float sm_m[kWarps][kMaxGroup], sm_l[kWarps][kMaxGroup];
     __shared__ float sm_acc[kWarps][kMaxGroup][HD];
-    __shared__ int s_flag;
+    __shared__ float c_m[kMaxGroup], c_l[kMaxGroup];   // this CTA's partial, read by the cluster
+    __shared__ float c_acc[kMaxGroup][HD];
 
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int nrank = (int)cluster.num_blocks();
     griddep_wait();
     griddep_launch_dependents();
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.y, c = blockIdx.x;
+    const int g = blockIdx.y;
     const DevState *st = p.st;
     const int slot = st->slot, tree_base = st->tree_base;
     const unsigned long long mask = slot >= tree_base ? st->small_mask[slot - tree_base] : 0ull;
     const int ctx = min(slot + 1, p.cap);
-    int nsplit = (ctx + p.min_chunk - 1) / p.min_chunk;
-    nsplit = max(1, min(nsplit, p.max_split));
-    const int chunk = (ctx + nsplit - 1) / nsplit;
-    if (c >= nsplit) return;
-    const int j0 = c * chunk, j1 = min(ctx, j0 + chunk);
+    const int chunk = (ctx + nrank - 1) / nrank;
+    const int j0 = min(ctx, rank * chunk), j1 = min(ctx, j0 + chunk);
     const int G = p.nh / p.nkv;
 
     float qr[kMaxGroup][DPL], m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][DPL];
@@ -482,31 +491,44 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
     }
     const __half *kb = p.kc + (size_t)g * p.cap * HD;
     const __half *vb = p.vc + (size_t)g * p.cap * HD;
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        if (j >= tree_base && !((mask >> (j - tree_base)) & 1ull)) continue;
-        float kf[DPL], vf[DPL];
-        const __half2 *kp = reinterpret_cast<const __half2 *>(kb + (size_t)j * HD + lane * DPL);
-        const __half2 *vp = reinterpret_cast<const __half2 *>(vb + (size_t)j * HD + lane * DPL);
+    using Vec = typename std::conditional<DPL == 4, uint2, uint32_t>::type;
+    for (int jb = j0 + warp * PB; jb < j1; jb += kWarps * PB) {
+        Vec kraw[PB], vraw[PB];
 #pragma unroll
-        for (int e = 0; e < DPL / 2; ++e) {
-            const float2 a = __half22float2(kp[e]), b = __half22float2(vp[e]);
-            kf[2 * e] = a.x; kf[2 * e + 1] = a.y;
-            vf[2 * e] = b.x; vf[2 * e + 1] = b.y;
+        for (int b = 0; b < PB; ++b) {           // issue the batch's loads together
+            const int j = min(jb + b, j1 - 1);
+            kraw[b] = *reinterpret_cast<const Vec *>(kb + (size_t)j * HD + lane * DPL);
+            vraw[b] = *reinterpret_cast<const Vec *>(vb + (size_t)j * HD + lane * DPL);
         }
 #pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            if (h < G) {
-                float s = 0.f;
+        for (int b = 0; b < PB; ++b) {
+            const int j = jb + b;
+            if (j >= j1) break;
+            if (j >= tree_base && !((mask >> (j - tree_base)) & 1ull)) continue;
+            float kf[DPL], vf[DPL];
+            const __half2 *kh = reinterpret_cast<const __half2 *>(&kraw[b]);
+            const __half2 *vh = reinterpret_cast<const __half2 *>(&vraw[b]);
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) s = fmaf(qr[h][e], kf[e], s);
-                s = warp_sum(s) * p.scale;
-                const float mn = fmaxf(m[h], s);
-                const float corr = expf(m[h] - mn);
-                const float pe = expf(s - mn);
-                l[h] = l[h] * corr + pe;
+            for (int e = 0; e < DPL / 2; ++e) {
+                const float2 a = __half22float2(kh[e]), c2 = __half22float2(vh[e]);
+                kf[2 * e] = a.x; kf[2 * e + 1] = a.y;
+                vf[2 * e] = c2.x; vf[2 * e + 1] = c2.y;
+            }
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(acc[h][e], corr, pe * vf[e]);
-                m[h] = mn;
+            for (int h = 0; h < kMaxGroup; ++h) {
+                if (h < G) {
+                    float s = 0.f;
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) s = fmaf(qr[h][e], kf[e], s);
+                    s = warp_sum(s) * p.scale;
+                    const float mn = fmaxf(m[h], s);
+                    const float corr = expf(m[h] - mn);
+                    const float pe = expf(s - mn);
+                    l[h] = l[h] * corr + pe;
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(acc[h][e], corr, pe * vf[e]);
+                    m[h] = mn;
+                }
             }
         }
     }
@@ -519,7 +541,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
         }
     }
     __syncthreads();
-    const int stride = HD + 2;
+    // This CTA's partial over its positions (a CTA with no visible position has m = -inf, l = 0).
     for (int idx = tid; idx < G * HD; idx += kThreads) {
         const int h = idx / HD, d = idx - h * HD;
         float M = -INFINITY;
@@ -532,40 +554,28 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
                 A = fmaf(sm_acc[w][h][d], f, A);
             }
         }
-        if (nsplit == 1) {       // the whole context in one CTA: no partials to merge
-            p.out[(g * G + h) * HD + d] = A / L;
-            continue;
-        }
-        float *pr = p.part + ((size_t)(g * G + h) * p.max_split + c) * stride;
-        pr[d] = A;
-        if (d == 0) { pr[HD] = M; pr[HD + 1] = L; }
+        c_acc[h][d] = A;
+        if (d == 0) { c_m[h] = M; c_l[h] = L; }
     }
-    if (nsplit == 1) return;
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(p.counter + g, 1u);
-        s_flag = (old == (unsigned)nsplit - 1u);
-    }
-    __syncthreads();
-    if (!s_flag) return;
-    __threadfence();
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
-        const int h = idx / HD, d = idx - h * HD;
-        const float *base = p.part + (size_t)(g * G + h) * p.max_split * stride;
+    cluster.sync();
+    // Log-sum-exp merge of the cluster's partials through distributed shared memory; each CTA
+    // finishes a 1/nrank share of the group's outputs.
+    const int E = G * HD, per = (E + nrank - 1) / nrank;
+    for (int e = rank * per + tid; e < min(E, (rank + 1) * per); e += kThreads) {
+        const int h = e / HD, d = e - h * HD;
         float M = -INFINITY;
-        for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(base + (size_t)k * stride + HD));
+        for (int r = 0; r < nrank; ++r) M = fmaxf(M, *cluster.map_shared_rank(&c_m[h], r));
         float L = 0.f, A = 0.f;
-        for (int k = 0; k < nsplit; ++k) {
-            const float mk = __ldcg(base + (size_t)k * stride + HD);
-            if (mk == -INFINITY) continue;
-            const float f = expf(mk - M);
-            L = fmaf(__ldcg(base + (size_t)k * stride + HD + 1), f, L);
-            A = fmaf(__ldcg(base + (size_t)k * stride + d), f, A);
+        for (int r = 0; r < nrank; ++r) {
+            const float mr = *cluster.map_shared_rank(&c_m[h], r);
+            if (mr == -INFINITY) continue;
+            const float f = expf(mr - M);
+            L = fmaf(*cluster.map_shared_rank(&c_l[h], r), f, L);
+            A = fmaf(*cluster.map_shared_rank(&c_acc[h][d], r), f, A);
         }
         p.out[(g * G + h) * HD + d] = A / L;
     }
-    if (tid == 0) p.counter[g] = 0u;
+    cluster.sync();      // keep this CTA's shared memory alive until the cluster has read it
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -666,32 +676,14 @@ static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size
 static long long max_units_per_cta(long long U, long long C) { return (U + C - 1) / C; }
 
 void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
-    // Pick tiles per unit (a divisor of K/16). Model, in SM cycles: a unit costs the larger of its
-    // HBM share (~23 bytes/cycle/SM at the measured copy bandwidth) and its issue time (about 60
-    // cycles per MMA round of the 8 warps plus ~100 of per-unit overhead); strips split across
-    // CTAs add a cross-CTA merge (~4000 cycles). Units per CTA are capped by the shared array.
-    // The ring must also keep ~48 KB per SM in flight (latency x bandwidth) when the CTA has that
-    // much to stream.
+    // A unit is one warp's work item: the largest divisor of K/16 up to kUnitTiles tiles (8 KB),
+    // so a 12-deep ring of units keeps ~96 KB per SM in flight; units are spread evenly over
+    // one CTA per SM.
+    (void)max_unit_bytes;
     const int KT = p.K / 16, strips = p.N / 16;
-    double best = 1e300;
-    p.nt = 0;
-    for (int nt = 1; nt <= KT; ++nt) {
-        if (KT % nt || nt * kTileBytes > max_unit_bytes || nt > kMaxUnitTiles) continue;
-        const long long U = (long long)strips * (KT / nt);
-        const long long C = std::min<long long>(num_sms, U);
-        const long long upc = max_units_per_cta(U, C);
-        if (upc > kMaxUnitsPerCta) continue;
-        const long long unit_bytes = (long long)nt * kTileBytes;
-        const long long stages = std::min<long long>(kMaxStages, ring_bytes / unit_bytes);
-        if (stages < 2) continue;
-        if (stages * unit_bytes < std::min<long long>(48 * 1024, upc * unit_bytes)) continue;
-        const double unit = std::max(unit_bytes / 23.0, 60.0 * ((nt + kWarps - 1) / kWarps) + 100.0) + 60.0;
-        const double cost = upc * unit + (KT / nt > 1 ? 2000.0 : 0.0);
-        if (cost < best - 1e-9 || (std::abs(cost - best) <= 1e-9 && nt > p.nt)) {
-            best = cost;
-            p.nt = nt;
-        }
-    }
+    p.nt = 1;
+    for (int nt = std::min(KT, kUnitTiles); nt >= 1; --nt)
+        if (KT % nt == 0) { p.nt = nt; break; }
     p.ks = KT / p.nt;
     const long long U = (long long)strips * p.ks;
     p.grid = (int)std::min<long long>(num_sms, U);
@@ -701,8 +693,7 @@ void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
 size_t gemv_smem_bytes(const GemvParams &p) {
     const long long U = (long long)(p.N / 16) * p.ks;
     const size_t upc = (size_t)max_units_per_cta(U, p.grid);
-    return (size_t)p.stages * p.nt * kTileBytes + (size_t)(p.K / 16) * 64 + 2 * kWarps * 16 * 4 + upc * 16 * 4 +
-           (size_t)p.stages * 8;
+    return (size_t)p.stages * p.nt * kTileBytes + (size_t)(p.K / 16) * 64 + upc * 16 * 4 + (size_t)p.stages * 16;
 }
 
 template <int PRO, int EPI, int FMT>
@@ -719,7 +710,7 @@ static cudaError_t gemv_t(const GemvParams &p, const LaunchCfg *lc) {
         if ((size_t)fa.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
         return cudaFuncSetAttribute(k_gemv<PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     }
-    return launch_ex(k_gemv<PRO, EPI, FMT>, dim3(p.grid), dim3(kThreads), smem, *lc, p);
+    return launch_ex(k_gemv<PRO, EPI, FMT>, dim3(p.grid), dim3(kGemvThreads), smem, *lc, p);
 }
 
 static cudaError_t gemv_dispatch(int pro, int epi, const GemvParams &p, const LaunchCfg *lc) {
@@ -749,11 +740,29 @@ cudaError_t prepare_attention() {
                                 (int)cudaSharedmemCarveoutMaxShared);
 }
 
+template <int HD>
+static cudaError_t launch_attention_t(const AttnParams &p, const LaunchCfg &lc) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kAttnCluster, p.nkv);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = lc.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAttnCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = lc.pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k_attn_decode<HD>, p);
+}
+
 cudaError_t launch_attention(const AttnParams &p, const LaunchCfg &lc) {
     if (p.nh / p.nkv > kMaxGroup) return cudaErrorInvalidValue;
-    const dim3 grid(p.max_split, p.nkv);
-    if (p.hd == 128) return launch_ex(k_attn_decode<128>, grid, dim3(kThreads), 0, lc, p);
-    if (p.hd == 64) return launch_ex(k_attn_decode<64>, grid, dim3(kThreads), 0, lc, p);
+    if (p.hd == 128) return launch_attention_t<128>(p, lc);
+    if (p.hd == 64) return launch_attention_t<64>(p, lc);
     return cudaErrorInvalidValue;
 }
 

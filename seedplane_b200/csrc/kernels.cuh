@@ -68,14 +68,13 @@ struct GemvParams {
 constexpr int kTraceUnits = 24;
 constexpr int kTraceWords = 8 + 2 * kTraceUnits;
 
+constexpr int kAttnCluster = 8;      // CTAs per kv head (one thread-block cluster)
+
 struct AttnParams {
     const float *q;          // [NH*HD] fp32 (RoPE applied)
     const __half *kc, *vc;   // this layer's caches [NKV][cap][HD]
     float *out;              // [NH*HD] fp32
-    float *part;             // [NH][max_split][HD+2] partial (m, l, acc)
-    unsigned *counter;       // [NKV]
     int nh, nkv, hd, cap;
-    int max_split, min_chunk;
     float scale;
     DevState *st;
 };
