@@ -37,6 +37,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kGemvThreads = kThreads + 32;   // + the producer warp
 constexpr int kMaxUnitsPerCta = 1024;     // bounds the per-CTA array of unit row sums (64 KB)
 constexpr int kMaxStages = 16;
+static_assert(kMaxStages % 8 == 0, "GEMV stage counts are multiples of the 8 consumer warps");
 constexpr int kUnitTiles = 16;            // tiles per unit at most (8 KB): one warp holds them in registers
 
 // Barrier among the 8 consumer warps of a GEMV CTA (the producer warp does not take part).
@@ -687,7 +688,11 @@ void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes) {
     p.ks = KT / p.nt;
     const long long U = (long long)strips * p.ks;
     p.grid = (int)std::min<long long>(num_sms, U);
-    p.stages = std::max(2, std::min(kMaxStages, ring_bytes / (p.nt * kTileBytes)));
+    // Unit i lives in stage i % S and is consumed by warp i % 8. S must be a multiple of 8 so a
+    // stage is always consumed by the same warp, in order: a warp then never waits on a stage's
+    // full barrier more than one phase ahead (a parity wait cannot tell phase k+1 from k-1).
+    const int fit = std::min(kMaxStages, ring_bytes / (p.nt * kTileBytes));
+    p.stages = std::max(kWarps, fit / kWarps * kWarps);
 }
 
 size_t gemv_smem_bytes(const GemvParams &p) {
@@ -714,6 +719,7 @@ static cudaError_t gemv_t(const GemvParams &p, const LaunchCfg *lc) {
 }
 
 static cudaError_t gemv_dispatch(int pro, int epi, const GemvParams &p, const LaunchCfg *lc) {
+    if (p.stages % kWarps || p.stages > kMaxStages || p.nt > kUnitTiles) return cudaErrorInvalidValue;
 #define SP_CASE(PRO, EPI)                                                                    \
     if (pro == PRO && epi == EPI)                                                            \
         return p.fmt == WF_F16 ? gemv_t<PRO, EPI, WF_F16>(p, lc) : cudaErrorNotSupported;
