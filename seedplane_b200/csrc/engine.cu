@@ -55,6 +55,8 @@ struct LayerDev {
 // launch, so ring + input fragments stay near half of the 227 KB of shared memory.
 constexpr int kRingBytes = 96 * 1024;
 constexpr int kMaxUnitBytes = 32 * 1024;
+constexpr int kTcRingBytes = 64 * 1024;     // 4 stages of 16 KB per tensor-core GEMV CTA
+constexpr int kTcBBudget = 64 * 1024;       // B operand (hi/lo activation rows) per CTA
 
 }  // namespace
 
@@ -98,7 +100,9 @@ struct sp_engine {
     unsigned long long *trace = nullptr;    // [kernel of the step][CTA][kTraceWords], SEEDPLANE_TRACE=1
     int trace_kernels = 0;
     // planned GEMV geometry (pointers filled per layer at record time)
+    bool tc = true;                         // tcgen05 GEMVs (else the mma.sync fragment GEMVs)
     GemvParams g_qkv{}, g_o{}, g_gu{}, g_down{}, g_head{};
+    TcGemvParams t_qkv{}, t_o{}, t_gu{}, t_down{}, t_head{};
     cudaStream_t cap_stream = nullptr;
     std::map<sp_kv *, cudaGraphExec_t> graphs;
     std::vector<sp_kv *> caches;
@@ -128,6 +132,35 @@ unsigned long long *trace_slot(sp_engine *e, int k) {
     return e->trace ? e->trace + (size_t)k * e->num_sms * kTraceWords : nullptr;
 }
 
+// The same GEMV call on the tensor-core kernel: copy the call-site fields across.
+cudaError_t launch_tc_from(sp_engine *e, const TcGemvParams &plan, int pro, int epi, const GemvParams &g,
+                           const LaunchCfg &lc) {
+    TcGemvParams t = plan;
+    t.w = g.w;
+    t.xin = g.xin;
+    t.gain = g.gain;
+    t.embed = g.embed;
+    t.x_init = g.x_init;
+    t.bias = g.bias;
+    t.out = g.out;
+    t.kc = g.kc;
+    t.vc = g.vc;
+    t.cap = g.cap;
+    for (int i = 0; i < kMaxPrefetch; ++i) {
+        t.pf_ptr[i] = g.pf_ptr[i];
+        t.pf_bytes[i] = g.pf_bytes[i];
+    }
+    t.pf_n = g.pf_n;
+    t.trace = g.trace;
+    return launch_gemv_tc(pro, epi, t, lc);
+}
+
+cudaError_t launch_any_gemv(sp_engine *e, int which, int pro, int epi, const GemvParams &g, const LaunchCfg &lc) {
+    if (!e->tc) return launch_gemv(pro, epi, g, lc);
+    const TcGemvParams *plans[] = {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head};
+    return launch_tc_from(e, *plans[which], pro, epi, g, lc);
+}
+
 int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     const sp_config &c = e->c;
     int kidx = 0;       // GEMV index within the step (trace slot)
@@ -148,7 +181,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         set_prefetch(e, p, L.off_qkv, QR * H * 2);
         p.trace = trace_slot(e, kidx++);
         const int pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM;
-        SP_CUDA(launch_gemv(pro, EPI_QKV, p, lc));
+        SP_CUDA(launch_any_gemv(e, 0, pro, EPI_QKV, p, lc));
         lc.pdl = e->pdl;
 
         AttnParams a{};
@@ -170,7 +203,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.out = e->x;
         set_prefetch(e, p, L.off_o, H * H * 2);
         p.trace = trace_slot(e, kidx++);
-        SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
+        SP_CUDA(launch_any_gemv(e, 1, PRO_PLAIN, EPI_RESID, p, lc));
 
         p = e->g_gu;
         p.w = L.gate_up;
@@ -179,7 +212,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.out = e->act;
         set_prefetch(e, p, L.off_gu, 2 * I * H * 2);
         p.trace = trace_slot(e, kidx++);
-        SP_CUDA(launch_gemv(PRO_NORM, EPI_SWIGLU, p, lc));
+        SP_CUDA(launch_any_gemv(e, 2, PRO_NORM, EPI_SWIGLU, p, lc));
 
         p = e->g_down;
         p.w = L.down;
@@ -187,15 +220,15 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.out = e->x;
         set_prefetch(e, p, L.off_dn, H * I * 2);
         p.trace = trace_slot(e, kidx++);
-        SP_CUDA(launch_gemv(PRO_PLAIN, EPI_RESID, p, lc));
+        SP_CUDA(launch_any_gemv(e, 3, PRO_PLAIN, EPI_RESID, p, lc));
     }
     LaunchCfg lc{s, e->pdl};
     GemvParams p = e->g_head;
     p.xin = e->x;
     p.gain = e->final_norm;
-    set_prefetch(e, p, e->off_head, align_up(c.vocab, 16) * H * 2);
+    set_prefetch(e, p, e->off_head, align_up(c.vocab, e->tc ? 128 : 16) * H * 2);
     p.trace = trace_slot(e, kidx++);
-    SP_CUDA(launch_gemv(PRO_NORM, EPI_LMHEAD, p, lc));
+    SP_CUDA(launch_any_gemv(e, 4, PRO_NORM, EPI_LMHEAD, p, lc));
     return SP_OK;
 }
 
@@ -298,10 +331,19 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->use_graph = env_flag("SEEDPLANE_GRAPH", true);
     e->prefetch_ahead = (size_t)std::max(0L, env_long("SEEDPLANE_L2_PREFETCH_MB", 0)) << 20;
     e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", false);
+    {
+        const char *g = getenv("SEEDPLANE_GEMV");
+        e->tc = !(g && strcmp(g, "hmma") == 0);
+    }
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
     const size_t H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
-    const size_t VP = align_up(V, 16);      // LM head rows padded to whole 16-row strips
+    // LM head rows padded to whole strips (128 rows for the tensor-core GEMV, 16 otherwise)
+    const size_t VP = align_up(V, e->tc ? 128 : 16);
+    if (e->tc && ((size_t)(c.heads + 2 * c.kv_heads) * c.head_dim % 128 || c.hidden % 128 || (2 * (size_t)c.intermediate) % 128)) {
+        delete e;
+        return fail(SP_ERR_UNSUPPORTED, "tensor-core GEMV needs qkv rows, hidden and 2*intermediate in multiples of 128");
+    }
     const size_t QR = (size_t)(c.heads + 2 * c.kv_heads) * HD;
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
@@ -364,15 +406,18 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const int *d_perm = d_idx, *d_gu = d_idx + QR, *d_iota = d_idx + QR + 2 * I;
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
-    SP_TRY(launch_pack_fragments(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H, s));
+    auto pack = [&](uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K) {
+        return e->tc ? launch_pack_tc(dst, a, rows_a, b, row_of, N, K, s)
+                     : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
+    };
+    SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
-        SP_TRY(launch_pack_fragments(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QR, (int)H, s));
-        SP_TRY(launch_pack_fragments(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)H, (int)H, s));
-        SP_TRY(launch_pack_fragments(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu,
-                                     (int)(2 * I), (int)H, s));
-        SP_TRY(launch_pack_fragments(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)H, (int)I, s));
+        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QR, (int)H));
+        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)H, (int)H));
+        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)(2 * I), (int)H));
+        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)H, (int)I));
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
@@ -440,7 +485,41 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->g_down = base(H, I);
     e->g_head = base(VP, H);
     e->g_head.n_valid = (int)V;
-    if (env_flag("SEEDPLANE_VERBOSE", false)) {
+    auto tbase = [&](size_t N, size_t K, int n_valid) {
+        TcGemvParams t{};
+        t.N = (int)N;
+        t.K = (int)K;
+        t.n_valid = n_valid;
+        t.eps = c.rms_norm_eps;
+        t.vocab = (int)V;
+        t.rope = e->rope;
+        t.max_pos = c.max_positions;
+        t.nh = c.heads;
+        t.nkv = c.kv_heads;
+        t.hd = (int)HD;
+        plan_gemv_tc(t, e->num_sms, kTcRingBytes, kTcBBudget);
+        return t;
+    };
+    if (e->tc) {
+        e->t_qkv = tbase(QR, H, (int)QR);
+        e->t_o = tbase(H, H, (int)H);
+        e->t_gu = tbase(2 * I, H, (int)(2 * I));
+        e->t_down = tbase(H, I, (int)H);
+        e->t_head = tbase(VP, H, (int)V);
+        for (const TcGemvParams *t : {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head})
+            if (t->max_items > gemv_tc_max_items() || gemv_tc_smem_bytes(*t) > 227 * 1024)
+                return bail(fail(SP_ERR_UNSUPPORTED, "tensor-core GEMV plan for N=%d K=%d does not fit (%d strips per CTA, %zu B smem)",
+                                 t->N, t->K, t->max_items, gemv_tc_smem_bytes(*t)));
+    }
+    if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc) {
+        const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
+        int k = 0;
+        for (const TcGemvParams *t : {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head})
+            fprintf(stderr, "[seedplane] tc gemv %-8s N=%d K=%d grid=%d stages=%d b_full=%d b_tiles=%d contrib<=%d items<=%d smem=%zu\n",
+                    names[k++], t->N, t->K, t->grid, t->stages, t->b_full, t->b_tiles, t->max_contrib, t->max_items,
+                    gemv_tc_smem_bytes(*t));
+    }
+    if (env_flag("SEEDPLANE_VERBOSE", false) && !e->tc) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
         for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
@@ -456,6 +535,11 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             n_strips = std::max(n_strips, (size_t)p->N / 16);
         }
     }
+    if (e->tc)
+        for (const TcGemvParams *t : {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head}) {
+            n_partial = std::max(n_partial, (size_t)t->N * t->max_contrib);
+            n_strips = std::max(n_strips, (size_t)t->N / 128);
+        }
     size_t woff = 0;
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
@@ -463,7 +547,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_partial = wtake(std::max<size_t>(n_partial, 1) * 4);
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
-    const size_t w_lmval = wtake((size_t)e->g_head.grid * 4), w_lmidx = wtake((size_t)e->g_head.grid * 4);
+    const size_t lm_grid = std::max((size_t)e->g_head.grid, (size_t)e->t_head.grid);
+    const size_t w_lmval = wtake(lm_grid * 4), w_lmidx = wtake(lm_grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
@@ -489,6 +574,15 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     }
     e->g_qkv.embed = e->embed;
     e->g_qkv.x_init = e->x;
+    for (TcGemvParams *t : {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head}) {
+        t->st = e->st;
+        t->partial = e->partial;
+        t->strip_cnt = e->strip_cnt;
+    }
+    e->t_head.part_val = e->lm_val;
+    e->t_head.part_idx = e->lm_idx;
+    e->t_head.counter = e->lm_cnt;
+    e->t_head.w = e->head;
     SP_TRY(prepare_gemv(PRO_NORM, EPI_QKV, e->g_qkv));
     SP_TRY(prepare_gemv(PRO_EMBED_NORM, EPI_QKV, e->g_qkv));
     SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_o));
@@ -496,6 +590,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_down));
     SP_TRY(prepare_gemv(PRO_NORM, EPI_LMHEAD, e->g_head));
     SP_TRY(prepare_attention());
+    if (e->tc) {
+        SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_QKV, e->t_qkv));
+        SP_TRY(prepare_gemv_tc(PRO_EMBED_NORM, EPI_QKV, e->t_qkv));
+        SP_TRY(prepare_gemv_tc(PRO_PLAIN, EPI_RESID, e->t_o));
+        SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_SWIGLU, e->t_gu));
+        SP_TRY(prepare_gemv_tc(PRO_PLAIN, EPI_RESID, e->t_down));
+        SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_LMHEAD, e->t_head));
+    }
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
     if (env_flag("SEEDPLANE_TRACE", false)) {

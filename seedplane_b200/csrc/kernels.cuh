@@ -84,6 +84,55 @@ struct LaunchCfg {
     bool pdl;                // launch with programmatic stream serialization
 };
 
+// ---- tensor-core (tcgen05 + TMEM) weight-streaming GEMV: gemv_tc.cu ------------------------
+constexpr int kTcTileBytes = 4096;       // 128 rows x 16 inputs of fp16, canonical K-major layout
+
+struct TcGemvParams {
+    const uint8_t *w;        // tiles (strip s, k-tile t) at (s * K/16 + t) * 4096
+    int N, K;                // N multiple of 128 (zero padded), K multiple of 16
+    int n_valid;             // rows >= n_valid are padding
+    int grid, stages;
+    int b_full;              // B operand holds all K/16 k-tiles (else the CTA's tiles)
+    int b_tiles;             // B operand tiles in shared memory
+    int max_contrib;         // CTAs that may share one strip
+    int max_items;           // strips a CTA may touch
+    // prologue
+    const float *xin;
+    const float *gain;
+    const __half *embed;
+    float *x_init;
+    float eps;
+    int vocab;
+    // epilogue
+    const float *bias;
+    float *out;
+    __half *kc, *vc;
+    int cap;
+    const float *rope;
+    int max_pos;
+    int nh, nkv, hd;
+    float *partial;          // [strips][max_contrib][128]
+    unsigned *strip_cnt;     // [strips]
+    float *part_val;
+    int *part_idx;
+    unsigned *counter;
+    DevState *st;
+    const uint8_t *pf_ptr[kMaxPrefetch];
+    unsigned long long pf_bytes[kMaxPrefetch];
+    int pf_n;
+    unsigned long long *trace;
+};
+
+void plan_gemv_tc(TcGemvParams &p, int num_sms, int ring_bytes, int b_budget_bytes);
+size_t gemv_tc_smem_bytes(const TcGemvParams &p);
+int gemv_tc_max_items();
+cudaError_t prepare_gemv_tc(int pro, int epi, const TcGemvParams &p);
+cudaError_t launch_gemv_tc(int pro, int epi, const TcGemvParams &p, const LaunchCfg &lc);
+// Pack an fp16 N x K matrix (packed row r = source row row_of[r] of a / b as in
+// launch_pack_fragments, < 0 = zero) into 128 x 16 canonical K-major tiles.
+cudaError_t launch_pack_tc(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
+                           cudaStream_t s);
+
 // Plan units / stages / grid for a GEMV of N x K; fills the geometry fields.
 void plan_gemv(GemvParams &p, int num_sms, int ring_bytes, int max_unit_bytes);
 size_t gemv_smem_bytes(const GemvParams &p);
