@@ -195,6 +195,10 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         a.cap = kv->capacity;
         a.scale = 1.0f / sqrtf((float)c.head_dim);
         a.st = e->st;
+        // the attention kernels of layer 0 and of the middle layer are traced after the GEMV slots
+        a.trace = (e->trace && (l == 0 || l == c.layers / 2))
+                      ? e->trace + (size_t)(e->trace_kernels + (l == 0 ? 0 : 1)) * e->num_sms * kTraceWords
+                      : nullptr;
         SP_CUDA(launch_attention(a, lc));
 
         p = e->g_o;
@@ -601,9 +605,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
     if (env_flag("SEEDPLANE_TRACE", false)) {
-        e->trace_kernels = 4 * c.layers + 1;
-        SP_TRY(cudaMalloc(&e->trace, (size_t)e->trace_kernels * e->num_sms * kTraceWords * 8));
-        SP_TRY(cudaMemset(e->trace, 0, (size_t)e->trace_kernels * e->num_sms * kTraceWords * 8));
+        e->trace_kernels = 4 * c.layers + 1;       // + 2 attention slots after the GEMVs
+        SP_TRY(cudaMalloc(&e->trace, (size_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords * 8));
+        SP_TRY(cudaMemset(e->trace, 0, (size_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords * 8));
     }
     e->cap_stream = s;
     s = nullptr;
@@ -787,7 +791,7 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
 int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity) {
     if (!e) return fail(SP_ERR_INVALID, "null engine");
     if (!e->trace) return 0;
-    const int64_t n = (int64_t)e->trace_kernels * e->num_sms * kTraceWords;
+    const int64_t n = (int64_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords;
     if (!host_out) return n;
     if (capacity < n) return fail(SP_ERR_CAPACITY, "trace needs %lld words", (long long)n);
     cudaError_t ce = cudaSetDevice(e->device);

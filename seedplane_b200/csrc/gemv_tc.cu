@@ -181,29 +181,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemv_tc(const TcGemvParams p)
         bready_sync();
         tc_fence_after();
         if (lane == 0) {
+            // Walk the tiles with running (item, k-tile) counters: no division on the issue path.
             const uint32_t ring_addr = smem_u32(ring), b_addr = smem_u32(bbuf);
-            int item = 0;
-            bool ok = true;
-            for (int i = 0; i < nstage && ok; ++i) {
-                const int s = i % S;
-                if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+            int item = 0, t = it_a[0];
+            uint32_t b_tile = (uint32_t)it_boff[0];      // B tile of the current k-tile
+            int s = 0, par = 0;
+            for (int i = 0; i < nstage; ++i) {
+                if (!mbar_wait_bounded(&full[s], (uint32_t)par)) {
                     atomicCAS(&st->err, 0, kErrMbarTimeout);
-                    ok = false;
                     break;
                 }
                 tc_fence_after();
                 if (tr && i < kTraceUnits) tr[8 + kTraceUnits + i] = globaltimer();
                 const int n = min((int)kTcStageTiles, ntiles - i * (int)kTcStageTiles);
+                uint32_t a_addr = ring_addr + (uint32_t)(s * kTcStageBytes);
                 for (int q = 0; q < n; ++q) {
-                    const long long g = g0 + (long long)i * kTcStageTiles + q;
-                    const int t = (int)(g % KT);
-                    while (item + 1 < nitems && t == it_a[item + 1] && (int)(g / KT) == it_strip[item + 1]) ++item;
-                    const uint64_t ad = smem_desc(ring_addr + (uint32_t)(s * kTcStageBytes + q * kTcTileBytes), 128, 256);
-                    const uint64_t bd = smem_desc(b_addr + (uint32_t)((it_boff[item] + t - it_a[item]) * 256), 128, 256);
+                    const uint64_t ad = smem_desc(a_addr, 128, 256);
+                    const uint64_t bd = smem_desc(b_addr + b_tile * 256u, 128, 256);
                     mma_f16(tmem + (uint32_t)(item * 8), ad, bd, t != it_a[item] ? 1u : 0u);
-                    if (t == it_b[item] - 1) mma_commit(&accf[item]);   // accumulator complete
+                    a_addr += kTcTileBytes;
+                    ++t;
+                    ++b_tile;
+                    if (t == it_b[item]) {                      // accumulator complete
+                        mma_commit(&accf[item]);
+                        if (item + 1 < nitems) {
+                            ++item;
+                            t = it_a[item];
+                            b_tile = (uint32_t)it_boff[item];
+                        }
+                    }
                 }
                 mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+                if (++s == S) {
+                    s = 0;
+                    par ^= 1;
+                }
             }
         }
         __syncwarp();

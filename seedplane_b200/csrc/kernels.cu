@@ -466,8 +466,12 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int nrank = (int)cluster.num_blocks();
+    unsigned long long *tr =
+        p.trace ? p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * kTraceWords : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = globaltimer();
     griddep_wait();
     griddep_launch_dependents();
+    if (tr && threadIdx.x == 0) tr[1] = globaltimer();
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = blockIdx.y;
@@ -533,6 +537,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
             }
         }
     }
+    if (tr && tid == 0) tr[2] = globaltimer();
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
         if (h < G) {
@@ -558,7 +563,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
         c_acc[h][d] = A;
         if (d == 0) { c_m[h] = M; c_l[h] = L; }
     }
+    if (tr && tid == 0) tr[3] = globaltimer();
     cluster.sync();
+    if (tr && tid == 0) tr[4] = globaltimer();
     // Log-sum-exp merge of the cluster's partials through distributed shared memory; each CTA
     // finishes a 1/nrank share of the group's outputs.
     const int E = G * HD, per = (E + nrank - 1) / nrank;
@@ -576,6 +583,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
         }
         p.out[(g * G + h) * HD + d] = A / L;
     }
+    if (tr && tid == 0) tr[5] = globaltimer();
     cluster.sync();      // keep this CTA's shared memory alive until the cluster has read it
 }
 

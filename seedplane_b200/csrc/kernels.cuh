@@ -77,6 +77,9 @@ struct AttnParams {
     int nh, nkv, hd, cap;
     float scale;
     DevState *st;
+    // Optional trace (null = off): per CTA [0] start, [1] wait returned, [2] positions done,
+    // [3] CTA partial written, [4] first cluster barrier passed, [5] merged.
+    unsigned long long *trace;
 };
 
 struct LaunchCfg {

@@ -42,8 +42,8 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
     t = np.where(t > 0, (t - t0) / 1000.0, np.nan)
     out, prev_end = [], None
     nk = t.shape[0]
-    for k in range(nk):
-        layer, kind = (k // 4, KERNELS[k % 4]) if k < nk - 1 else (-1, "lm_head")
+    for k in range(nk - 2):
+        layer, kind = (k // 4, KERNELS[k % 4]) if k < nk - 3 else (-1, "lm_head")
         start, wait, pro, loop, epi = (t[k, :, j] for j in range(5))
         issue, ready = t[k, :, 8:32], t[k, :, 32:56]
         lat = ready - issue
@@ -58,8 +58,20 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
         if layer in layers_shown or layer == -1:
             out.append({key: (round(float(v), 2) if v is not None else None) if not isinstance(v, str) else v
                         for key, v in row.items()})
-    total = float(np.nanmax(t[nk - 1, :, 4]) - np.nanmin(t[0, :, 0]))
-    return {"step_span_us": round(total, 1), "kernels": out}
+    gemv_k = nk - 2                                          # the last two slots are attention kernels
+    total = float(np.nanmax(t[gemv_k - 1, :, 4]) - np.nanmin(t[0, :, 0]))
+    attn = []
+    for k in (gemv_k, gemv_k + 1):
+        row = t[k]
+        if np.isnan(row[:, 0]).all():
+            continue
+        attn.append({"slot": "layer 0" if k == gemv_k else "middle layer",
+                     "start": round(float(np.nanmin(row[:, 0])), 2), "wait_ret": round(float(np.nanmax(row[:, 1])), 2),
+                     "positions_done": round(float(np.nanmax(row[:, 2])), 2),
+                     "partial_done": round(float(np.nanmax(row[:, 3])), 2),
+                     "cluster_sync": round(float(np.nanmax(row[:, 4])), 2),
+                     "merged": round(float(np.nanmax(row[:, 5])), 2)})
+    return {"step_span_us": round(total, 1), "kernels": out, "attention": attn}
 
 
 def main():
