@@ -36,6 +36,7 @@ constexpr int kTcStageTiles = 4;          // 16 KB per stage
 constexpr int kTcStageBytes = kTcStageTiles * kTcTileBytes;
 constexpr int kTcMaxItems = 16;           // TMEM accumulators per CTA (8 columns each)
 constexpr int kTcTmemCols = kTcMaxItems * 8;
+constexpr int kMaxPairs = 4;              // B pairs (k-tile, half) per prologue thread: K/8 <= 512
 
 SP_DEVINL void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 // warps 0-3 + the MMA warp: the B operand is ready
@@ -221,6 +222,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemv_tc(const TcGemvParams p)
         __syncwarp();
     } else {
         // ---- warps 0-3: input vector -> B operand (rows hi / lo / 0 x 6) ----------------------
+        // One L2 round trip: every thread first loads the 8 inputs (and 8 norm gains) of each of
+        // its B "pairs" (k-tile, half), plus, when the B operand covers only part of K, its share
+        // of the whole vector for the RMSNorm sum of squares; then one reduction, then the fp16
+        // hi / lo rows are built from registers.
         griddep_wait();
         griddep_launch_dependents();
         if (tr && tid == 0) tr[1] = globaltimer();
@@ -233,91 +238,121 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemv_tc(const TcGemvParams p)
             }
             erow = p.embed + (size_t)tok * K;
         }
-        float inv = 1.f;
-        if constexpr (PRO != PRO_PLAIN) {
-            float ss = 0.f;
-            if constexpr (PRO == PRO_EMBED_NORM) {
-                const uint4 *e4 = reinterpret_cast<const uint4 *>(erow);
-                for (int v = tid; v < K / 8; v += kEpiThreads) {
-                    const uint4 raw = e4[v];
+        const int nb = p.b_full ? KT : ntiles;
+        const int npairs = nb * 2;
+        float v[kMaxPairs][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxPairs; ++q) {
+            const int idx = tid + q * kEpiThreads;
+            if (idx < npairs) {
+                const int bt = idx >> 1, h = idx & 1;
+                int t = bt;                                  // k-tile of this B tile
+                if (!p.b_full) {
+                    int j = 0;
+                    while (j + 1 < nitems && bt >= it_boff[j + 1]) ++j;
+                    t = it_a[j] + (bt - it_boff[j]);
+                }
+                const int k0 = 16 * t + 8 * h;
+                if constexpr (PRO == PRO_EMBED_NORM) {
+                    const uint4 raw = *reinterpret_cast<const uint4 *>(erow + k0);
                     const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-                    float f[8];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const float2 t2 = __half22float2(h2[j]);
-                        f[2 * j] = t2.x;
-                        f[2 * j + 1] = t2.y;
+                        v[q][2 * j] = t2.x;
+                        v[q][2 * j + 1] = t2.y;
                     }
-                    if (c == 0) {
-                        float4 *xi = reinterpret_cast<float4 *>(p.x_init + 8 * v);
-                        xi[0] = make_float4(f[0], f[1], f[2], f[3]);
-                        xi[1] = make_float4(f[4], f[5], f[6], f[7]);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+                } else {
+                    const float4 x0 = *reinterpret_cast<const float4 *>(p.xin + k0);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(p.xin + k0 + 4);
+                    v[q][0] = x0.x; v[q][1] = x0.y; v[q][2] = x0.z; v[q][3] = x0.w;
+                    v[q][4] = x1.x; v[q][5] = x1.y; v[q][6] = x1.z; v[q][7] = x1.w;
                 }
-            } else {
-                const float4 *x4 = reinterpret_cast<const float4 *>(p.xin);
-                for (int v = tid; v < K / 4; v += kEpiThreads) {
-                    const float4 f = x4[v];
-                    ss = fmaf(f.x, f.x, ss);
-                    ss = fmaf(f.y, f.y, ss);
-                    ss = fmaf(f.z, f.z, ss);
-                    ss = fmaf(f.w, f.w, ss);
+                if (PRO != PRO_PLAIN && p.b_full) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) ss = fmaf(v[q][j], v[q][j], ss);
                 }
             }
+        }
+        if constexpr (PRO != PRO_PLAIN) {
+            if (!p.b_full || (PRO == PRO_EMBED_NORM && c == 0)) {
+                // the whole vector: sum of squares (B covers part of K) and / or the residual init
+                if constexpr (PRO == PRO_EMBED_NORM) {
+                    const uint4 *e4 = reinterpret_cast<const uint4 *>(erow);
+                    for (int vv = tid; vv < K / 8; vv += kEpiThreads) {
+                        const uint4 raw = e4[vv];
+                        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                        float f[8];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 t2 = __half22float2(h2[j]);
+                            f[2 * j] = t2.x;
+                            f[2 * j + 1] = t2.y;
+                        }
+                        if (c == 0) {
+                            float4 *xi = reinterpret_cast<float4 *>(p.x_init + 8 * vv);
+                            xi[0] = make_float4(f[0], f[1], f[2], f[3]);
+                            xi[1] = make_float4(f[4], f[5], f[6], f[7]);
+                        }
+                        if (!p.b_full) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+                        }
+                    }
+                } else {
+                    const float4 *x4 = reinterpret_cast<const float4 *>(p.xin);
+                    for (int vv = tid; vv < K / 4; vv += kEpiThreads) {
+                        const float4 f = x4[vv];
+                        ss = fmaf(f.x, f.x, ss);
+                        ss = fmaf(f.y, f.y, ss);
+                        ss = fmaf(f.z, f.z, ss);
+                        ss = fmaf(f.w, f.w, ss);
+                    }
+                }
+            }
+        }
+        float inv = 1.f;
+        if constexpr (PRO != PRO_PLAIN) {
             ss = warp_sum(ss);
             if (lane == 0) s_val[warp] = ss;
             epi_sync();
             inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
         }
-        // One (k-tile, half) core pair per step: 8 inputs -> a hi row, a lo row and 6 zero rows.
-        const int nb = p.b_full ? KT : ntiles;
-        for (int idx = tid; idx < nb * 2; idx += kEpiThreads) {
-            const int bt = idx >> 1, h = idx & 1;
-            int t = bt;                                // k-tile of this B tile
-            if (!p.b_full) {
-                int j = 0;
-                while (j + 1 < nitems && bt >= it_boff[j + 1]) ++j;
-                t = it_a[j] + (bt - it_boff[j]);
-            }
-            const int k0 = 16 * t + 8 * h;
-            float v[8];
-            if constexpr (PRO == PRO_EMBED_NORM) {
-                const uint4 raw = *reinterpret_cast<const uint4 *>(erow + k0);
-                const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int q = 0; q < kMaxPairs; ++q) {
+            const int idx = tid + q * kEpiThreads;
+            if (idx < npairs) {
+                const int bt = idx >> 1, h = idx & 1;
+                if constexpr (PRO != PRO_PLAIN) {
+                    int t = bt;
+                    if (!p.b_full) {
+                        int j = 0;
+                        while (j + 1 < nitems && bt >= it_boff[j + 1]) ++j;
+                        t = it_a[j] + (bt - it_boff[j]);
+                    }
+                    const int k0 = 16 * t + 8 * h;
+                    const float4 ga = *reinterpret_cast<const float4 *>(p.gain + k0);
+                    const float4 gb = *reinterpret_cast<const float4 *>(p.gain + k0 + 4);
+                    const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[q][j] = (v[q][j] * inv) * gg[j];
+                }
+                uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float2 t2 = __half22float2(h2[j]);
-                    v[2 * j] = t2.x;
-                    v[2 * j + 1] = t2.y;
+                    const __half h0 = __float2half_rn(v[q][2 * j]), h1 = __float2half_rn(v[q][2 * j + 1]);
+                    const __half l0 = __float2half_rn(v[q][2 * j] - __half2float(h0));
+                    const __half l1 = __float2half_rn(v[q][2 * j + 1] - __half2float(h1));
+                    hi[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                    lo[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
                 }
-            } else {
-                const float4 a = *reinterpret_cast<const float4 *>(p.xin + k0);
-                const float4 b = *reinterpret_cast<const float4 *>(p.xin + k0 + 4);
-                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            }
-            if constexpr (PRO != PRO_PLAIN) {
-                const float4 ga = *reinterpret_cast<const float4 *>(p.gain + k0);
-                const float4 gb = *reinterpret_cast<const float4 *>(p.gain + k0 + 4);
-                const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+                uint4 *core = reinterpret_cast<uint4 *>(bbuf + (size_t)bt * 256 + h * 128);
+                core[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                core[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = (v[j] * inv) * gg[j];
+                for (int r = 2; r < 8; ++r) core[r] = make_uint4(0u, 0u, 0u, 0u);
             }
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
-                const __half l0 = __float2half_rn(v[2 * j] - __half2float(h0));
-                const __half l1 = __float2half_rn(v[2 * j + 1] - __half2float(h1));
-                hi[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-                lo[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-            }
-            uint4 *core = reinterpret_cast<uint4 *>(bbuf + (size_t)bt * 256 + h * 128);
-            core[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            core[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-#pragma unroll
-            for (int r = 2; r < 8; ++r) core[r] = make_uint4(0u, 0u, 0u, 0u);
         }
         fence_proxy_async_smem();   // generic-proxy writes -> visible to the tensor core
         bready_sync();
@@ -501,6 +536,8 @@ void plan_gemv_tc(TcGemvParams &p, int num_sms, int ring_bytes, int b_budget_byt
     p.max_items = (int)(per / KT + 2);
 }
 
+int gemv_tc_max_pairs() { return kMaxPairs * kEpiThreads; }
+
 size_t gemv_tc_smem_bytes(const TcGemvParams &p) {
     return (size_t)p.stages * kTcStageBytes + (size_t)p.b_tiles * 256 + (size_t)(2 * p.stages + kTcMaxItems) * 8;
 }
@@ -534,7 +571,8 @@ static cudaError_t gemv_tc_t(const TcGemvParams &p, const LaunchCfg *lc) {
 }
 
 static cudaError_t gemv_tc_dispatch(int pro, int epi, const TcGemvParams &p, const LaunchCfg *lc) {
-    if (p.max_items > kTcMaxItems || p.N % 128 || p.K % 16) return cudaErrorInvalidValue;
+    if (p.max_items > kTcMaxItems || p.N % 128 || p.K % 16 || p.b_tiles * 2 > kMaxPairs * kEpiThreads)
+        return cudaErrorInvalidValue;
 #define SP_CASE(PRO, EPI) \
     if (pro == PRO && epi == EPI) return gemv_tc_t<PRO, EPI>(p, lc);
     SP_CASE(PRO_NORM, EPI_QKV)

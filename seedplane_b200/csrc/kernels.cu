@@ -12,23 +12,14 @@
 //              Replaces the Vulkan gemv/swiglu/rope_kv/argmax shaders
 //              (native/vulkan_decode/shaders/gemv.comp:23-51, swiglu.comp:20-44,
 //              rope_kv.comp:14-32, argmax.comp:8-22).
-// k_attn_decode -- GQA decode attention, split over the context inside one thread-block cluster
-//              per kv head: each CTA of the cluster serves all q heads of the group over 1/8 of
-//              the positions (online softmax, fp32), then the partials (max, sum, acc) are merged
-//              by log-sum-exp through distributed shared memory, with no global round trip.
-//              Replaces attn_part.comp:15-44 + attn_combine.comp:8-19; the mask is the
-//              reference's `slot <= own slot` (qwen_engine.py:131-135) or a tree-ancestor mask.
+// (The decode attention kernel is in attention.cu, the tensor-core GEMV in gemv_tc.cu.)
 #include <algorithm>
 #include <climits>
 #include <cmath>
 #include <type_traits>
 #include <utility>
 
-#include <cooperative_groups.h>
-
 #include "kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace sp {
 
@@ -450,144 +441,6 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// GQA decode attention: one thread-block cluster of kAttnCluster CTAs per kv head
-// ---------------------------------------------------------------------------------------------
-constexpr int kMaxGroup = 8;
-
-template <int HD>
-__global__ void __launch_bounds__(kThreads) k_attn_decode(const AttnParams p) {
-    constexpr int DPL = HD / 32;                 // dims per lane
-    constexpr int PB = 4;                        // positions loaded per batch
-    __shared__ float sm_m[kWarps][kMaxGroup], sm_l[kWarps][kMaxGroup];
-    __shared__ float sm_acc[kWarps][kMaxGroup][HD];
-    __shared__ float c_m[kMaxGroup], c_l[kMaxGroup];   // this CTA's partial, read by the cluster
-    __shared__ float c_acc[kMaxGroup][HD];
-
-    cg::cluster_group cluster = cg::this_cluster();
-    const int rank = (int)cluster.block_rank();
-    const int nrank = (int)cluster.num_blocks();
-    unsigned long long *tr =
-        p.trace ? p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * kTraceWords : nullptr;
-    if (tr && threadIdx.x == 0) tr[0] = globaltimer();
-    griddep_wait();
-    griddep_launch_dependents();
-    if (tr && threadIdx.x == 0) tr[1] = globaltimer();
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.y;
-    const DevState *st = p.st;
-    const int slot = st->slot, tree_base = st->tree_base;
-    const unsigned long long mask = slot >= tree_base ? st->small_mask[slot - tree_base] : 0ull;
-    const int ctx = min(slot + 1, p.cap);
-    const int chunk = (ctx + nrank - 1) / nrank;
-    const int j0 = min(ctx, rank * chunk), j1 = min(ctx, j0 + chunk);
-    const int G = p.nh / p.nkv;
-
-    float qr[kMaxGroup][DPL], m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][DPL];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) {
-            acc[h][e] = 0.f;
-            qr[h][e] = h < G ? p.q[(g * G + h) * HD + lane * DPL + e] : 0.f;
-        }
-    }
-    const __half *kb = p.kc + (size_t)g * p.cap * HD;
-    const __half *vb = p.vc + (size_t)g * p.cap * HD;
-    using Vec = typename std::conditional<DPL == 4, uint2, uint32_t>::type;
-    for (int jb = j0 + warp * PB; jb < j1; jb += kWarps * PB) {
-        Vec kraw[PB], vraw[PB];
-#pragma unroll
-        for (int b = 0; b < PB; ++b) {           // issue the batch's loads together
-            const int j = min(jb + b, j1 - 1);
-            kraw[b] = *reinterpret_cast<const Vec *>(kb + (size_t)j * HD + lane * DPL);
-            vraw[b] = *reinterpret_cast<const Vec *>(vb + (size_t)j * HD + lane * DPL);
-        }
-#pragma unroll
-        for (int b = 0; b < PB; ++b) {
-            const int j = jb + b;
-            if (j >= j1) break;
-            if (j >= tree_base && !((mask >> (j - tree_base)) & 1ull)) continue;
-            float kf[DPL], vf[DPL];
-            const __half2 *kh = reinterpret_cast<const __half2 *>(&kraw[b]);
-            const __half2 *vh = reinterpret_cast<const __half2 *>(&vraw[b]);
-#pragma unroll
-            for (int e = 0; e < DPL / 2; ++e) {
-                const float2 a = __half22float2(kh[e]), c2 = __half22float2(vh[e]);
-                kf[2 * e] = a.x; kf[2 * e + 1] = a.y;
-                vf[2 * e] = c2.x; vf[2 * e + 1] = c2.y;
-            }
-#pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) {
-                if (h < G) {
-                    float s = 0.f;
-#pragma unroll
-                    for (int e = 0; e < DPL; ++e) s = fmaf(qr[h][e], kf[e], s);
-                    s = warp_sum(s) * p.scale;
-                    const float mn = fmaxf(m[h], s);
-                    const float corr = expf(m[h] - mn);
-                    const float pe = expf(s - mn);
-                    l[h] = l[h] * corr + pe;
-#pragma unroll
-                    for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(acc[h][e], corr, pe * vf[e]);
-                    m[h] = mn;
-                }
-            }
-        }
-    }
-    if (tr && tid == 0) tr[2] = globaltimer();
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-        if (h < G) {
-            if (lane == 0) { sm_m[warp][h] = m[h]; sm_l[warp][h] = l[h]; }
-#pragma unroll
-            for (int e = 0; e < DPL; ++e) sm_acc[warp][h][lane * DPL + e] = acc[h][e];
-        }
-    }
-    __syncthreads();
-    // This CTA's partial over its positions (a CTA with no visible position has m = -inf, l = 0).
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
-        const int h = idx / HD, d = idx - h * HD;
-        float M = -INFINITY;
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][h]);
-        float L = 0.f, A = 0.f;
-        if (M != -INFINITY) {
-            for (int w = 0; w < kWarps; ++w) {
-                const float f = expf(sm_m[w][h] - M);
-                L = fmaf(sm_l[w][h], f, L);
-                A = fmaf(sm_acc[w][h][d], f, A);
-            }
-        }
-        c_acc[h][d] = A;
-        if (d == 0) { c_m[h] = M; c_l[h] = L; }
-    }
-    if (tr && tid == 0) tr[3] = globaltimer();
-    cluster.sync();
-    if (tr && tid == 0) tr[4] = globaltimer();
-    // Log-sum-exp merge of the cluster's partials through distributed shared memory; each CTA
-    // finishes a 1/nrank share of the group's outputs.
-    const int E = G * HD, per = (E + nrank - 1) / nrank;
-    for (int e = rank * per + tid; e < min(E, (rank + 1) * per); e += kThreads) {
-        const int h = e / HD, d = e - h * HD;
-        float M = -INFINITY;
-        for (int r = 0; r < nrank; ++r) M = fmaxf(M, *cluster.map_shared_rank(&c_m[h], r));
-        float L = 0.f, A = 0.f;
-        for (int r = 0; r < nrank; ++r) {
-            const float mr = *cluster.map_shared_rank(&c_m[h], r);
-            if (mr == -INFINITY) continue;
-            const float f = expf(mr - M);
-            L = fmaf(*cluster.map_shared_rank(&c_l[h], r), f, L);
-            A = fmaf(*cluster.map_shared_rank(&c_acc[h][d], r), f, A);
-        }
-        p.out[(g * G + h) * HD + d] = A / L;
-    }
-    if (tr && tid == 0) tr[5] = globaltimer();
-    cluster.sync();      // keep this CTA's shared memory alive until the cluster has read it
-}
-
-// ---------------------------------------------------------------------------------------------
 // Utility kernels
 // ---------------------------------------------------------------------------------------------
 // Writes the state of a step sequence; a forced sequence takes step 0's token and position from
@@ -744,40 +597,6 @@ cudaError_t prepare_gemv(int pro, int epi, const GemvParams &p) { return gemv_di
 
 cudaError_t launch_gemv(int pro, int epi, const GemvParams &p, const LaunchCfg &lc) {
     return gemv_dispatch(pro, epi, p, &lc);
-}
-
-cudaError_t prepare_attention() {
-    cudaError_t e = cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                         (int)cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                (int)cudaSharedmemCarveoutMaxShared);
-}
-
-template <int HD>
-static cudaError_t launch_attention_t(const AttnParams &p, const LaunchCfg &lc) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kAttnCluster, p.nkv);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = lc.stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kAttnCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = lc.pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, k_attn_decode<HD>, p);
-}
-
-cudaError_t launch_attention(const AttnParams &p, const LaunchCfg &lc) {
-    if (p.nh / p.nkv > kMaxGroup) return cudaErrorInvalidValue;
-    if (p.hd == 128) return launch_attention_t<128>(p, lc);
-    if (p.hd == 64) return launch_attention_t<64>(p, lc);
-    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_set_state(DevState *st, const DevState &init, cudaStream_t s) {
