@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         cp_async16(qs + 4 * i, p.q + (size_t)g * G * HD + 4 * i);
     cp_async_wait_all();
     __syncthreads();
+    if (tr && tid == 0) tr[6] = globaltimer();
 
     const int E = G * HD;                   // outputs of this group, thread t owns t, t+256, ...
     float acc[kMaxGroup * HD / kAttnThreads];
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
             for (int h = 0; h < kMaxGroup; ++h) sc[jl * kMaxGroup + h] = vis ? s[h] * p.scale : -INFINITY;
         }
         __syncthreads();
+        if (tr && tid == 0 && a == j0) tr[7] = globaltimer();
         // ---- softmax statistics: warp h owns head h ----------------------------------------------
         if (warp < G) {
             const int h = warp;
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
             }
         }
         __syncthreads();
+        if (tr && tid == 0 && a == j0) tr[8] = globaltimer();
         // ---- values: thread = output element ----------------------------------------------------
 #pragma unroll
         for (int k = 0; k < kMaxGroup * HD / kAttnThreads; ++k) {

@@ -315,8 +315,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemv_tc(const TcGemvParams p)
         float inv = 1.f;
         if constexpr (PRO != PRO_PLAIN) {
             ss = warp_sum(ss);
+            if (tr && tid == 0) tr[5] = globaltimer();
             if (lane == 0) s_val[warp] = ss;
             epi_sync();
+            if (tr && tid == 0) tr[6] = globaltimer();
             inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
         }
 #pragma unroll

@@ -53,6 +53,7 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
                "stream_med": np.nanmedian(loop - pro), "stream_max": np.nanmax(loop - pro),
                "epilogue_med": np.nanmedian(epi - loop), "end_max": np.nanmax(epi),
                "unit_latency_med": np.nanmedian(lat), "ready_gap_med": np.nanmedian(np.diff(ready, axis=1)),
+               "x_loaded_med": np.nanmedian(t[k, :, 5] - wait), "reduced_med": np.nanmedian(t[k, :, 6] - wait),
                "gap_from_prev_end": None if prev_end is None else np.nanmin(start) - prev_end}
         prev_end = np.nanmax(epi)
         if layer in layers_shown or layer == -1:
@@ -70,7 +71,10 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
                      "positions_done": round(float(np.nanmax(row[:, 2])), 2),
                      "partial_done": round(float(np.nanmax(row[:, 3])), 2),
                      "cluster_sync": round(float(np.nanmax(row[:, 4])), 2),
-                     "merged": round(float(np.nanmax(row[:, 5])), 2)})
+                     "merged": round(float(np.nanmax(row[:, 5])), 2),
+                     "staged_max": round(float(np.nanmax(row[:, 6])), 2),
+                     "scores_max": round(float(np.nanmax(row[:, 7])), 2),
+                     "softmax_max": round(float(np.nanmax(row[:, 8])), 2)})
     return {"step_span_us": round(total, 1), "kernels": out, "attention": attn}
 
 
