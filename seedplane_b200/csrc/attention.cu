@@ -6,9 +6,11 @@
 // and `slot` itself is advanced by the previous step), so they are fetched BEFORE the
 // programmatic-dependent-launch wait, overlapping the QKV projection. After the wait the CTA
 // fetches q and the current row, then per sub-chunk of up to 128 positions:
-//   scores  s[j][h] = scale * q_h . k_j   (lane = position, q broadcast from shared memory)
-//   softmax running max / sum per head (fp32, online across sub-chunks)
-//   values  acc[h][d] += p[j][h] v_j[d]    (thread = output element)
+//   scores  s[j][h] = scale * q_h . k_j   (warp = position, lane = HD/32 dims, q in registers;
+//                                          a 3-step butterfly leaves head lane/4 in each lane)
+//   softmax running max / sum per head (fp32, online across sub-chunks; warp = head)
+//   values  acc[h][d] += p[j][h] v_j[d]    (warp = head, lane = HD/32 dims, 4 partial sums)
+// Heads of the group beyond G are computed on a zero q (branch-free inner loops) and dropped.
 // The CTAs' partials (max, sum, acc) are merged by log-sum-exp through distributed shared memory.
 // Mask: the reference's `key slot <= own slot` (seedplane/qwen_engine.py:131-135), or, for
 // speculative nodes (slot >= tree_base), the node's ancestor-or-self bits.
@@ -27,8 +29,9 @@ namespace {
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kMaxGroup = 8;          // q heads per kv head
+constexpr int kMaxGroup = 8;          // q heads per kv head (== kAttnWarps: softmax/values use warp = head)
 constexpr int kSub = 128;             // positions per shared-memory sub-chunk
+static_assert(kMaxGroup == kAttnWarps, "one warp per head of the group");
 
 SP_DEVINL void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -39,11 +42,10 @@ SP_DEVINL void cp_async_wait_all() {
 
 template <int HD>
 struct AttnSmem {
-    static constexpr int kRow = HD * 2 + 16;              // padded K row (bank-conflict-free lane-per-row reads)
-    static constexpr int vRow = HD * 2;
+    static constexpr int kRow = HD * 2;                   // K and V rows, fp16, unpadded
     static constexpr size_t kOff = 0;
     static constexpr size_t vOff = kOff + (size_t)kSub * kRow;
-    static constexpr size_t qOff = vOff + (size_t)kSub * vRow;
+    static constexpr size_t qOff = vOff + (size_t)kSub * kRow;
     static constexpr size_t sOff = qOff + (size_t)kMaxGroup * HD * 4;
     static constexpr size_t bytes = sOff + (size_t)kSub * kMaxGroup * 4;
 };
@@ -61,8 +63,47 @@ SP_DEVINL void stage_rows(uint8_t *sm, const __half *kb, const __half *vb, int b
         if (which == 0)
             cp_async16(sm + L::kOff + (size_t)(j - base) * L::kRow + ch * 16, kb + (size_t)j * HD + ch * 8);
         else
-            cp_async16(sm + L::vOff + (size_t)(j - base) * L::vRow + ch * 16, vb + (size_t)j * HD + ch * 8);
+            cp_async16(sm + L::vOff + (size_t)(j - base) * L::kRow + ch * 16, vb + (size_t)j * HD + ch * 8);
     }
+}
+
+// DL consecutive fp16 values at `p` (8- or 4-byte aligned) as fp32.
+template <int DL>
+SP_DEVINL void load_dims(const uint8_t *p, float (&f)[DL]) {
+    static_assert(DL == 4 || DL == 2, "head_dim 128 or 64");
+    if constexpr (DL == 4) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(p);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+    } else {
+        const uint32_t u = *reinterpret_cast<const uint32_t *>(p);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u));
+        f[0] = a.x; f[1] = a.y;
+    }
+}
+
+// Sum v[h] over the 32 lanes for all 8 heads; lane l returns the sum of head l / 4.
+// Three exchange steps halve the values each lane carries (xor 16, 8, 4), two plain steps
+// (xor 2, 1) finish the sums: 9 shuffles instead of 40. The summation order is fixed.
+SP_DEVINL float reduce_heads(const float (&v)[kMaxGroup], int lane) {
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float w[4], x[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float send = b4 ? v[i] : v[i + 4], keep = b4 ? v[i + 4] : v[i];
+        w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? w[i] : w[i + 2], keep = b3 ? w[i + 2] : w[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    const float send = b2 ? x[0] : x[1], keep = b2 ? x[1] : x[0];
+    float y = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    y += __shfl_xor_sync(0xffffffffu, y, 2);
+    y += __shfl_xor_sync(0xffffffffu, y, 1);
+    return y;
 }
 
 }  // namespace
@@ -70,6 +111,7 @@ SP_DEVINL void stage_rows(uint8_t *sm, const __half *kb, const __half *vb, int b
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p) {
     using L = AttnSmem<HD>;
+    constexpr int DL = HD / 32;             // dims per lane
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ float m_run[kMaxGroup], l_run[kMaxGroup], corr[kMaxGroup];
     __shared__ float c_m[kMaxGroup], c_l[kMaxGroup];     // this CTA's partial, read by the cluster
@@ -99,6 +141,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         m_run[tid] = -INFINITY;
         l_run[tid] = 0.f;
     }
+    for (int i = G * HD + tid; i < kMaxGroup * HD; i += kAttnThreads) qs[i] = 0.f;
     // first sub-chunk: every row except the current one can be fetched before the wait
     const int s1 = min(j1, j0 + kSub);
     stage_rows<HD>(sm, kb, vb, j0, j0, min(s1, slot), tid);
@@ -112,10 +155,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     __syncthreads();
     if (tr && tid == 0) tr[6] = globaltimer();
 
-    const int E = G * HD;                   // outputs of this group, thread t owns t, t+256, ...
-    float acc[kMaxGroup * HD / kAttnThreads];
+    float qr[kMaxGroup][DL];                // this lane's dims of every head's q
 #pragma unroll
-    for (int k = 0; k < kMaxGroup * HD / kAttnThreads; ++k) acc[k] = 0.f;
+    for (int h = 0; h < kMaxGroup; ++h)
+#pragma unroll
+        for (int i = 0; i < DL; ++i) qr[h][i] = qs[h * HD + DL * lane + i];
+    float acc[DL];                          // warp = head (< G), lane = dims [DL*lane, DL*lane + DL)
+#pragma unroll
+    for (int i = 0; i < DL; ++i) acc[i] = 0.f;
 
     for (int a = j0; a < j1; a += kSub) {
         const int b = min(j1, a + kSub), nj = b - a;
@@ -124,40 +171,41 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
             cp_async_wait_all();
             __syncthreads();
         }
-        // ---- scores: lane = position -----------------------------------------------------------
-        const int jl = warp * 32 + lane;
-        if (jl < nj) {
-            float s[kMaxGroup];
+        // ---- scores: warp = position, two positions in flight --------------------------------------
+        for (int jl = warp; jl < nj; jl += 2 * kAttnWarps) {
+            const int jl2 = jl + kAttnWarps;
+            const bool has2 = jl2 < nj;     // warp-uniform
+            float k1[DL], k2[DL];
+            load_dims<DL>(sm + L::kOff + (size_t)jl * L::kRow + lane * DL * 2, k1);
+            if (has2) {
+                load_dims<DL>(sm + L::kOff + (size_t)jl2 * L::kRow + lane * DL * 2, k2);
+            } else {
 #pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) s[h] = 0.f;
-            const uint4 *krow = reinterpret_cast<const uint4 *>(sm + L::kOff + (size_t)jl * L::kRow);
-#pragma unroll 4
-            for (int c8 = 0; c8 < HD / 8; ++c8) {
-                const uint4 kv = krow[c8];
-                const __half2 *kh = reinterpret_cast<const __half2 *>(&kv);
-                float kf[8];
+                for (int i = 0; i < DL; ++i) k2[i] = 0.f;
+            }
+            float v1[kMaxGroup], v2[kMaxGroup];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(kh[e]);
-                    kf[2 * e] = f.x;
-                    kf[2 * e + 1] = f.y;
+            for (int h = 0; h < kMaxGroup; ++h) {
+                float t1 = qr[h][0] * k1[0], t2 = qr[h][0] * k2[0];
+#pragma unroll
+                for (int i = 1; i < DL; ++i) {
+                    t1 = fmaf(qr[h][i], k1[i], t1);
+                    t2 = fmaf(qr[h][i], k2[i], t2);
                 }
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h) {
-                    if (h < G) {
-                        const float4 q0 = *reinterpret_cast<const float4 *>(qs + h * HD + 8 * c8);
-                        const float4 q1 = *reinterpret_cast<const float4 *>(qs + h * HD + 8 * c8 + 4);
-                        float t = s[h];
-                        t = fmaf(q0.x, kf[0], t); t = fmaf(q0.y, kf[1], t); t = fmaf(q0.z, kf[2], t); t = fmaf(q0.w, kf[3], t);
-                        t = fmaf(q1.x, kf[4], t); t = fmaf(q1.y, kf[5], t); t = fmaf(q1.z, kf[6], t); t = fmaf(q1.w, kf[7], t);
-                        s[h] = t;
-                    }
+                v1[h] = t1;
+                v2[h] = t2;
+            }
+            const float s1v = reduce_heads(v1, lane), s2v = reduce_heads(v2, lane);
+            if ((lane & 3) == 0) {
+                const int h = lane >> 2;
+                const int j = a + jl, j2 = a + jl2;
+                const bool vis1 = !(j >= tree_base && !((mask >> (j - tree_base)) & 1ull));
+                sc[jl * kMaxGroup + h] = vis1 ? s1v * p.scale : -INFINITY;
+                if (has2) {
+                    const bool vis2 = !(j2 >= tree_base && !((mask >> (j2 - tree_base)) & 1ull));
+                    sc[jl2 * kMaxGroup + h] = vis2 ? s2v * p.scale : -INFINITY;
                 }
             }
-            const int j = a + jl;
-            const bool vis = !(j >= tree_base && !((mask >> (j - tree_base)) & 1ull));
-#pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) sc[jl * kMaxGroup + h] = vis ? s[h] * p.scale : -INFINITY;
         }
         __syncthreads();
         if (tr && tid == 0 && a == j0) tr[7] = globaltimer();
@@ -185,26 +233,44 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         }
         __syncthreads();
         if (tr && tid == 0 && a == j0) tr[8] = globaltimer();
-        // ---- values: thread = output element ----------------------------------------------------
+        // ---- values: warp h owns head h, four independent partial sums ---------------------------
+        if (warp < G) {
+            const int h = warp;
+            float part[4][DL];
 #pragma unroll
-        for (int k = 0; k < kMaxGroup * HD / kAttnThreads; ++k) {
-            const int e = tid + k * kAttnThreads;
-            if (e < E) {
-                const int h = e / HD, d = e - h * HD;
-                float t = acc[k] * corr[h];
-                const __half *vcol = reinterpret_cast<const __half *>(sm + L::vOff) + d;
-                for (int q = 0; q < nj; ++q) t = fmaf(sc[q * kMaxGroup + h], __half2float(vcol[(size_t)q * HD]), t);
-                acc[k] = t;
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int i = 0; i < DL; ++i) part[u][i] = 0.f;
+            const uint8_t *vrow = sm + L::vOff + lane * DL * 2;
+            int q = 0;
+            for (; q + 4 <= nj; q += 4) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float pe = sc[(q + u) * kMaxGroup + h];
+                    float vf[DL];
+                    load_dims<DL>(vrow + (size_t)(q + u) * L::kRow, vf);
+#pragma unroll
+                    for (int i = 0; i < DL; ++i) part[u][i] = fmaf(pe, vf[i], part[u][i]);
+                }
             }
+            for (; q < nj; ++q) {
+                const float pe = sc[q * kMaxGroup + h];
+                float vf[DL];
+                load_dims<DL>(vrow + (size_t)q * L::kRow, vf);
+#pragma unroll
+                for (int i = 0; i < DL; ++i) part[0][i] = fmaf(pe, vf[i], part[0][i]);
+            }
+            const float cf = corr[h];
+#pragma unroll
+            for (int i = 0; i < DL; ++i) acc[i] = fmaf(acc[i], cf, (part[0][i] + part[1][i]) + (part[2][i] + part[3][i]));
         }
         __syncthreads();
     }
     if (tr && tid == 0) tr[2] = globaltimer();
     // ---- this CTA's partial, then the cluster merge ------------------------------------------------
+    if (warp < G) {
 #pragma unroll
-    for (int k = 0; k < kMaxGroup * HD / kAttnThreads; ++k) {
-        const int e = tid + k * kAttnThreads;
-        if (e < E) c_acc[e / HD][e % HD] = acc[k];
+        for (int i = 0; i < DL; ++i) c_acc[warp][DL * lane + i] = acc[i];
     }
     if (tid < G) {
         c_m[tid] = m_run[tid];
@@ -213,18 +279,26 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     if (tr && tid == 0) tr[3] = globaltimer();
     cluster.sync();
     if (tr && tid == 0) tr[4] = globaltimer();
-    const int per = (E + nrank - 1) / nrank;
+    const int E = G * HD;
+    const int per = (E + kAttnCluster - 1) / kAttnCluster;
     for (int e = rank * per + tid; e < min(E, (rank + 1) * per); e += kAttnThreads) {
         const int h = e / HD, d = e - h * HD;
+        float mr[kAttnCluster], lr[kAttnCluster], ar[kAttnCluster];
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            mr[r] = *cluster.map_shared_rank(&c_m[h], r);
+            lr[r] = *cluster.map_shared_rank(&c_l[h], r);
+            ar[r] = *cluster.map_shared_rank(&c_acc[h][d], r);
+        }
         float M = -INFINITY;
-        for (int r = 0; r < nrank; ++r) M = fmaxf(M, *cluster.map_shared_rank(&c_m[h], r));
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, mr[r]);
         float Ls = 0.f, A = 0.f;
-        for (int r = 0; r < nrank; ++r) {
-            const float mr = *cluster.map_shared_rank(&c_m[h], r);
-            if (mr == -INFINITY) continue;
-            const float f = expf(mr - M);
-            Ls = fmaf(*cluster.map_shared_rank(&c_l[h], r), f, Ls);
-            A = fmaf(*cluster.map_shared_rank(&c_acc[h][d], r), f, A);
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            const float f = mr[r] == -INFINITY ? 0.f : expf(mr[r] - M);
+            Ls = fmaf(lr[r], f, Ls);
+            A = fmaf(ar[r], f, A);
         }
         p.out[(g * G + h) * HD + d] = A / Ls;
     }
