@@ -304,7 +304,7 @@ def run_decode(args, world, rank, local):
         L = cfg.layers
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
                 "config": {"workload": f"qwen2-1.5b greedy decode: {DECODE} tokens per step after a {PROMPT}-token "
                                        "prompt, random-init fp16 weights (seed 0), fp16 KV cache",
                            "decode_tokens_per_step": DECODE, "prompt": PROMPT, "kv_capacity": CAPACITY,
@@ -324,7 +324,7 @@ def run_decode(args, world, rank, local):
                 "token_sha256": __import__("hashlib").sha256(json.dumps(tokens_ref).encode()).hexdigest()}
         if world == 1 and not args.no_cpu_baseline:
             threads = physical_cores()
-            n = 8
+            n = 200    # about 10 s of CPU work on a 16-core host
             val, toks, dt = cpu_oracle_sample(cfg, w, prompt, n, threads)
             line["cpu_baseline"] = {"value": val, "unit": "tok/s", "cores": threads, "kind": "port",
                                     "sample": f"{n} greedy tokens after the same 512-token prompt (prefill "
