@@ -124,6 +124,14 @@ int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const in
  * rollback by truncation (benchmark_speculative.py:119,127) for tree-shaped drafts. */
 int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stream);
 
+/* Greedy argmax of each row of fp32 logits [rows][ld] (device) over the first `cols` columns:
+ * argmax_dev[rows] int32, lowest index on ties (NaN is never selected). For logits produced
+ * outside the fused LM head, e.g. all-logits verification. Replaces `Qwen2Engine.sample`
+ * (qwen_engine.py:147-148) and argmax.comp:8-22. Uses the engine's scratch: calls on one engine
+ * are ordered by their stream (one stream per engine). */
+int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
+              void *stream);
+
 /* Kernel timeline of the last step, when the engine was created with SEEDPLANE_TRACE=1: for each
  * GEMV of the step (4 per layer, then the LM head) and each CTA, kernel-start / dependency-wait /
  * prologue / stream / epilogue stamps and per-unit issue and ready stamps of %globaltimer (ns).

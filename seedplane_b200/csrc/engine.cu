@@ -57,6 +57,7 @@ constexpr int kRingBytes = 96 * 1024;
 constexpr int kMaxUnitBytes = 32 * 1024;
 constexpr int kTcRingBytes = 64 * 1024;     // 4 stages of 16 KB per tensor-core GEMV CTA
 constexpr int kTcBBudget = 64 * 1024;       // B operand (hi/lo activation rows) per CTA
+constexpr int kArgmaxChunkRows = 64;        // sp_argmax rows per launch (engine scratch is sized for it)
 
 }  // namespace
 
@@ -97,6 +98,7 @@ struct sp_engine {
     float *lm_val = nullptr;
     int *lm_idx = nullptr;
     DevState *st = nullptr;
+    ArgmaxScratch am{};                     // sp_argmax: kArgmaxChunkRows rows per launch
     unsigned long long *trace = nullptr;    // [kernel of the step][CTA][kTraceWords], SEEDPLANE_TRACE=1
     int trace_kernels = 0;
     // planned GEMV geometry (pointers filled per layer at record time)
@@ -554,6 +556,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t lm_grid = std::max((size_t)e->g_head.grid, (size_t)e->t_head.grid);
     const size_t w_lmval = wtake(lm_grid * 4), w_lmidx = wtake(lm_grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
+    const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
@@ -567,6 +570,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->lm_val = (float *)(e->ws + w_lmval);
     e->lm_idx = (int *)(e->ws + w_lmidx);
     e->st = (DevState *)(e->ws + w_st);
+    e->am = argmax_scratch_at(e->ws + w_am, kArgmaxChunkRows);
     e->g_head.w = e->head;
     e->g_head.part_val = e->lm_val;
     e->g_head.part_idx = e->lm_idx;
@@ -785,6 +789,22 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
     SP_CUDA(launch_kv_commit(kv->k, kv->v, e->c.layers, e->c.kv_heads, kv->capacity, e->c.head_dim, src_slots_host, n,
                              kv->length, (cudaStream_t)stream));
     kv->length += n;
+    return SP_OK;
+}
+
+int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
+              void *stream) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    if (!logits_dev || !argmax_dev) return fail(SP_ERR_INVALID, "null logits or output");
+    if (rows <= 0 || cols <= 0 || ld < cols) return fail(SP_ERR_INVALID, "bad shape rows=%d cols=%d ld=%lld", rows, cols,
+                                                         (long long)ld);
+    SP_CUDA(cudaSetDevice(e->device));
+    // rows in chunks: the chunks share the engine's scratch in stream order
+    for (int32_t r0 = 0; r0 < rows; r0 += kArgmaxChunkRows) {
+        const int n = std::min<int32_t>(kArgmaxChunkRows, rows - r0);
+        SP_CUDA(launch_argmax_rows(logits_dev + (size_t)r0 * ld, n, cols, ld, argmax_dev + r0, e->am,
+                                   (cudaStream_t)stream));
+    }
     return SP_OK;
 }
 

@@ -158,4 +158,19 @@ cudaError_t launch_pack_fragments(uint8_t *dst, const __half *a, int rows_a, con
 cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap, int hd, const int *src_slots,
                              int n, int dst0, cudaStream_t s);
 
+// Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
+// (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per
+// row, which must be zero when the kernel starts and is zero again when it ends.
+constexpr int kArgmaxMaxCtas = 32;
+struct ArgmaxScratch {
+    float *val;
+    int *idx;
+    unsigned *cnt;
+};
+int argmax_ctas(int cols);
+size_t argmax_scratch_bytes(int rows);
+ArgmaxScratch argmax_scratch_at(void *base, int rows);
+cudaError_t launch_argmax_rows(const float *logits, int rows, int cols, long long ld, int *out, const ArgmaxScratch &sc,
+                               cudaStream_t s);
+
 }  // namespace sp

@@ -241,3 +241,13 @@ class CudaQwen2:
     def kv_commit(self, kv: DeviceKV, src_slots: Sequence[int]):
         N.check(N.load().sp_kv_commit(kv.handle, N.int_array(src_slots), len(src_slots),
                                       C.c_void_p(_stream(self.device))))
+
+    def argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        """Row-wise greedy argmax (lowest index on ties) of fp32 logits [rows, V] on this device."""
+        if logits.device != self.device or logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise ValueError("fp32 logits [rows, V] with unit column stride on the engine's device expected")
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=self.device)
+        N.check(N.load().sp_argmax(self.handle, C.c_void_p(logits.data_ptr()), logits.shape[0], logits.shape[1],
+                                   logits.stride(0), C.c_void_p(out.data_ptr()), C.c_void_p(_stream(self.device))))
+        return out
+

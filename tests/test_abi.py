@@ -45,6 +45,7 @@ def test_null_arguments_are_rejected_with_messages(lib):
     assert lib.sp_kv_set_length(None, 0) == N.SP_ERR_INVALID
     assert lib.sp_kv_commit(None, None, 0, None) == N.SP_ERR_INVALID
     assert lib.sp_device_status(None, None) == N.SP_ERR_INVALID
+    assert lib.sp_argmax(None, None, 1, 1, 1, None, None) == N.SP_ERR_INVALID
     with pytest.raises(ValueError):
         N.check(N.SP_ERR_INVALID)
 

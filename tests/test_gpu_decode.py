@@ -172,3 +172,31 @@ def test_qwen2engine_surface_generate(tiny):
     with pytest.raises(ValueError):
         e.forward([1, 2], cache, positions=[1])
     e.engine.close()
+
+
+def argmax_cases(seed=0):
+    """Logit matrices with planted ties and maxima at chunk edges; numpy's argmax (first index of
+    the maximum) is the oracle, as torch.argmax / `sample` in the reference."""
+    g = np.random.default_rng(seed)
+    cases = []
+    for rows, cols, ld in ((1, 151936, 151936), (3, 1000, 1000), (70, 1200, 1204), (5, 8193, 8195), (2, 7, 7)):
+        x = g.standard_normal((rows, ld)).astype(np.float32)
+        for r in range(rows):
+            j = int(g.integers(0, cols))
+            x[r, j] = 9.0
+            k = int(g.integers(0, cols))
+            x[r, k] = 9.0                       # a tie: the lower index must win
+            if r % 3 == 0:
+                x[r, cols - 1] = 9.5            # maximum in the last column of the row
+            x[r, cols:] = 100.0                 # padding beyond `cols` must be ignored
+        cases.append((x, cols))
+    return cases
+
+
+def test_argmax_rows_first_index(tiny):
+    cfg, w, eng, o = tiny
+    for x, cols in argmax_cases():
+        dev = torch.from_numpy(x).to(eng.device)
+        got = eng.argmax(dev[:, :cols]).cpu().numpy()
+        want = np.argmax(x[:, :cols], axis=1)
+        assert (got == want).all()
