@@ -132,6 +132,20 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
 int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
               void *stream);
 
+/* sp_argmax without an engine and without any allocation (no reference counterpart: the
+ * reference allocates nothing on this path; this entry point exists for callers that must not
+ * allocate device memory, e.g. inside a memory-capped serving process or before an engine
+ * exists). Same result as sp_argmax. Runs on `device` (it calls cudaSetDevice). Its scratch is
+ * a fixed 33,280-byte __device__ array of the library (one per device), so:
+ *   - rows <= 128, else SP_ERR_CAPACITY (nothing is launched);
+ *   - it clears the row counters it uses (a memset on `stream`) before each launch;
+ *   - calls that overlap in time on one device (different streams or threads) race on the same
+ *     scratch: order them on one stream;
+ *   - the first call on a device looks the scratch up (cudaGetSymbolAddress): make it before any
+ *     stream capture; later calls may be captured. */
+int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld,
+                      int32_t *argmax_dev, void *stream);
+
 /* Kernel timeline of the last step, when the engine was created with SEEDPLANE_TRACE=1: for each
  * GEMV of the step (4 per layer, then the LM head) and each CTA, kernel-start / dependency-wait /
  * prologue / stream / epilogue stamps and per-unit issue and ready stamps of %globaltimer (ns).

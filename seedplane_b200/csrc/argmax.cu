@@ -103,6 +103,20 @@ ArgmaxScratch argmax_scratch_at(void *base, int rows) {
     return s;
 }
 
+// Scratch of the allocation-free entry point (sp_argmax_noalloc): a fixed array in the module's
+// global memory, sized for kNoAllocMaxRows rows (val / idx [128][32] + 128 counters = 33,280 B).
+// Zero at module load; the caller clears the counters it uses before each launch.
+namespace {
+constexpr int kNoAllocMaxRows = 128;
+constexpr size_t kNoAllocScratchBytes =
+    2 * (size_t)kNoAllocMaxRows * kArgmaxMaxCtas * 4 + (size_t)kNoAllocMaxRows * 4;
+static __device__ __align__(256) uint8_t g_argmax_scratch[kNoAllocScratchBytes];
+}  // namespace
+
+int argmax_noalloc_max_rows() { return kNoAllocMaxRows; }
+size_t argmax_noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
+cudaError_t argmax_noalloc_scratch(void **base) { return cudaGetSymbolAddress(base, g_argmax_scratch); }
+
 cudaError_t launch_argmax_rows(const float *logits, int rows, int cols, long long ld, int *out, const ArgmaxScratch &sc,
                                cudaStream_t s) {
     if (rows <= 0 || rows > 65535 || cols <= 0 || ld < cols) return cudaErrorInvalidValue;

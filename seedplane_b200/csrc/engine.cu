@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -58,6 +59,7 @@ constexpr int kMaxUnitBytes = 32 * 1024;
 constexpr int kTcRingBytes = 64 * 1024;     // 4 stages of 16 KB per tensor-core GEMV CTA
 constexpr int kTcBBudget = 64 * 1024;       // B operand (hi/lo activation rows) per CTA
 constexpr int kArgmaxChunkRows = 64;        // sp_argmax rows per launch (engine scratch is sized for it)
+constexpr int kMaxDevices = 64;             // sp_argmax_noalloc: per-device scratch addresses
 
 }  // namespace
 
@@ -805,6 +807,37 @@ int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols,
         SP_CUDA(launch_argmax_rows(logits_dev + (size_t)r0 * ld, n, cols, ld, argmax_dev + r0, e->am,
                                    (cudaStream_t)stream));
     }
+    return SP_OK;
+}
+
+int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
+                      void *stream) {
+    if (!logits_dev || !argmax_dev) return fail(SP_ERR_INVALID, "null logits or output");
+    if (rows <= 0 || cols <= 0 || ld < cols) return fail(SP_ERR_INVALID, "bad shape rows=%d cols=%d ld=%lld", rows, cols,
+                                                         (long long)ld);
+    if (rows > argmax_noalloc_max_rows())
+        return fail(SP_ERR_CAPACITY, "%d rows exceed the fixed scratch (at most %d rows)", rows, argmax_noalloc_max_rows());
+    if (device < 0 || device >= kMaxDevices) return fail(SP_ERR_INVALID, "device %d", device);
+    SP_CUDA(cudaSetDevice(device));
+    // Per-device address of the module's scratch array, looked up once (before any stream capture).
+    static std::mutex mu;
+    static void *base[kMaxDevices] = {};
+    void *b = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!base[device]) {
+            void *p = nullptr;
+            SP_CUDA(argmax_noalloc_scratch(&p));
+            if (!p) return fail(SP_ERR_CUDA, "no address for the argmax scratch on device %d", device);
+            base[device] = p;
+        }
+        b = base[device];
+    }
+    if (argmax_scratch_bytes(rows) > argmax_noalloc_scratch_bytes())
+        return fail(SP_ERR_CAPACITY, "argmax scratch of %zu bytes is too small", argmax_noalloc_scratch_bytes());
+    const ArgmaxScratch sc = argmax_scratch_at(b, rows);
+    SP_CUDA(cudaMemsetAsync(sc.cnt, 0, (size_t)rows * sizeof(unsigned), (cudaStream_t)stream));   // counters start at 0
+    SP_CUDA(launch_argmax_rows(logits_dev, rows, cols, ld, argmax_dev, sc, (cudaStream_t)stream));
     return SP_OK;
 }
 

@@ -172,5 +172,9 @@ size_t argmax_scratch_bytes(int rows);
 ArgmaxScratch argmax_scratch_at(void *base, int rows);
 cudaError_t launch_argmax_rows(const float *logits, int rows, int cols, long long ld, int *out, const ArgmaxScratch &sc,
                                cudaStream_t s);
+// The fixed scratch of sp_argmax_noalloc on the current device (a __device__ array, no allocation).
+int argmax_noalloc_max_rows();
+size_t argmax_noalloc_scratch_bytes();
+cudaError_t argmax_noalloc_scratch(void **base);
 
 }  // namespace sp

@@ -251,3 +251,15 @@ class CudaQwen2:
                                    logits.stride(0), C.c_void_p(out.data_ptr()), C.c_void_p(_stream(self.device))))
         return out
 
+
+def argmax_noalloc(logits: torch.Tensor) -> torch.Tensor:
+    """Row-wise greedy argmax of fp32 logits [rows <= 128, V] through `sp_argmax_noalloc`: no engine
+    and no device allocation in the library (its scratch is a fixed device array). Calls on one
+    device must not overlap in time; the first call on a device must precede any stream capture."""
+    if logits.device.type != "cuda" or logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("fp32 CUDA logits [rows, V] with unit column stride expected")
+    out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    N.check(N.load().sp_argmax_noalloc(logits.device.index, C.c_void_p(logits.data_ptr()), logits.shape[0],
+                                       logits.shape[1], logits.stride(0), C.c_void_p(out.data_ptr()),
+                                       C.c_void_p(_stream(logits.device))))
+    return out

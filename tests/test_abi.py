@@ -46,6 +46,9 @@ def test_null_arguments_are_rejected_with_messages(lib):
     assert lib.sp_kv_commit(None, None, 0, None) == N.SP_ERR_INVALID
     assert lib.sp_device_status(None, None) == N.SP_ERR_INVALID
     assert lib.sp_argmax(None, None, 1, 1, 1, None, None) == N.SP_ERR_INVALID
+    assert lib.sp_argmax_noalloc(0, None, 1, 1, 1, None, None) == N.SP_ERR_INVALID
+    # more rows than the fixed scratch holds: rejected before any CUDA call
+    assert lib.sp_argmax_noalloc(0, C.c_void_p(256), 129, 8, 8, C.c_void_p(256), None) == N.SP_ERR_CAPACITY
     with pytest.raises(ValueError):
         N.check(N.SP_ERR_INVALID)
 
