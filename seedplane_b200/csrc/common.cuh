@@ -145,5 +145,6 @@ SP_DEVINL float dot8_f16(const uint4 w, const float4 a, const float4 b, float ac
 constexpr int kErrMbarTimeout = 1;
 constexpr int kErrBadToken = 2;
 constexpr int kErrBadSlot = 3;
+constexpr int kErrDepTimeout = 4;        // a cross-CTA dependency counter never reached its target
 
 }  // namespace sp

@@ -80,6 +80,7 @@ struct sp_engine {
     size_t arena_bytes = 0;
     uint8_t *ws = nullptr;
     size_t ws_bytes = 0;
+    size_t ws_clear_bytes = 0;              // prefix of ws holding counters and split-strip state
     // The per-token weight stream: every layer's [qkv | o | gate_up | down], then the LM head, in
     // consumption order and contiguous, so prefetching "D bytes ahead" is one address window.
     const uint8_t *stream = nullptr;
@@ -101,6 +102,18 @@ struct sp_engine {
     int *lm_idx = nullptr;
     DevState *st = nullptr;
     ArgmaxScratch am{};                     // sp_argmax: kArgmaxChunkRows rows per launch
+    // persistent step kernel (default; SEEDPLANE_STEP=chain selects the kernel-per-op chain)
+    bool step_kernel = true;
+    StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (256 x 64 tiles)
+    int step_stages = 0, step_a_blocks = 0, step_max_chunks = 0;
+    size_t step_smem = 0;
+    unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
+    unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
+    int n_cnt = 0;
+    float *attn_ml = nullptr, *attn_acc = nullptr;
+    std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
+    int n_step_ops = 0;
+    unsigned long long *step_trace = nullptr;
     unsigned long long *trace = nullptr;    // [kernel of the step][CTA][kTraceWords], SEEDPLANE_TRACE=1
     int trace_kernels = 0;
     // planned GEMV geometry (pointers filled per layer at record time)
@@ -165,8 +178,126 @@ cudaError_t launch_any_gemv(sp_engine *e, int which, int pro, int epi, const Gem
     return launch_tc_from(e, *plans[which], pro, epi, g, lc);
 }
 
+// The step's op table for one cache: per layer QKV, attention, O, gate_up, down; then the LM head.
+// Counter 5l+0: QKV strips finished, +1: attention (one per CTA), +2: O strips, +3: gate_up
+// strips, +4: down strips (the residual x of layer l+1 is complete).
+std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
+    const sp_config &c = e->c;
+    const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
+    const int H = c.hidden, I = c.intermediate, QR = (c.heads + 2 * c.kv_heads) * c.head_dim;
+    const int grid = e->num_sms;
+    std::vector<StepOp> ops;
+    auto gemv = [&](const StepOp &plan, const uint8_t *w, int pro, int epi, int dep, int dep_n, int sig) {
+        StepOp o = plan;
+        o.kind = OP_GEMV;
+        o.w = w;
+        o.pro = pro;
+        o.epi = epi;
+        o.dep = dep;
+        o.dep_n = dep_n;
+        o.sig = sig;
+        return o;
+    };
+    const int sx = e->s_o.N / 256, sq = e->s_qkv.N / 256, sgu = e->s_gu.N / 256;   // strips signalled per op
+    for (int l = 0; l < c.layers; ++l) {
+        const LayerDev &L = e->layers[l];
+        __half *kc = kv->k + l * kv_layer, *vc = kv->v + l * kv_layer;
+        StepOp o = gemv(e->s_qkv, L.qkv, l == 0 ? PRO_EMBED_NORM : PRO_NORM, EPI_QKV, l == 0 ? -1 : 5 * (l - 1) + 4,
+                        sx, 5 * l + 0);
+        o.xin = e->x;
+        o.gain = L.in_norm;
+        o.bias = L.qkv_b;
+        o.out = e->q;
+        o.kc = kc;
+        o.vc = vc;
+        ops.push_back(o);
+        StepOp a{};
+        a.kind = OP_ATTN;
+        a.kc = kc;
+        a.vc = vc;
+        a.dep = 5 * l + 0;
+        a.dep_n = sq;
+        a.sig = 5 * l + 1;
+        ops.push_back(a);
+        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, grid, 5 * l + 2);
+        o.out = e->x;
+        o.resid_embed = l == 0;
+        ops.push_back(o);
+        o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU, 5 * l + 2, sx, 5 * l + 3);
+        o.xin = e->x;
+        o.gain = L.post_norm;
+        o.out = e->act;
+        ops.push_back(o);
+        o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID, 5 * l + 3, sgu, 5 * l + 4);
+        o.xin = e->act;
+        o.out = e->x;
+        ops.push_back(o);
+    }
+    StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD, 5 * (c.layers - 1) + 4, sx, -1);
+    o.xin = e->x;
+    o.gain = e->final_norm;
+    ops.push_back(o);
+    return ops;
+}
+
+int ensure_step_ops(sp_engine *e, sp_kv *kv, StepOp **out) {
+    auto it = e->step_ops.find(kv);
+    if (it != e->step_ops.end()) {
+        *out = it->second;
+        return SP_OK;
+    }
+    const std::vector<StepOp> ops = build_step_ops(e, kv);
+    StepOp *d = nullptr;
+    SP_CUDA(cudaMalloc(&d, ops.size() * sizeof(StepOp)));
+    cudaError_t ce = cudaMemcpy(d, ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        cudaFree(d);
+        return fail(SP_ERR_CUDA, "step op table: %s", cudaGetErrorString(ce));
+    }
+    e->n_step_ops = (int)ops.size();
+    e->step_ops[kv] = d;
+    *out = d;
+    return SP_OK;
+}
+
 int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     const sp_config &c = e->c;
+    if (e->step_kernel) {
+        StepOp *ops = nullptr;
+        int rc = ensure_step_ops(e, kv, &ops);
+        if (rc != SP_OK) return rc;
+        StepParams p{};
+        p.ops = ops;
+        p.n_ops = e->n_step_ops;
+        p.stages = e->step_stages;
+        p.a_blocks = e->step_a_blocks;
+        p.nh = c.heads;
+        p.nkv = c.kv_heads;
+        p.hd = c.head_dim;
+        p.cap = kv->capacity;
+        p.max_pos = c.max_positions;
+        p.vocab = c.vocab;
+        p.hidden = c.hidden;
+        p.max_chunks = e->step_max_chunks;
+        p.eps = c.rms_norm_eps;
+        p.scale = 1.0f / sqrtf((float)c.head_dim);
+        p.rope = e->rope;
+        p.embed = e->embed;
+        p.q = e->q;
+        p.attn_ml = e->attn_ml;
+        p.attn_acc = e->attn_acc;
+        p.partial = e->partial;
+        p.strip_cnt = e->strip_cnt;
+        p.part_val = e->lm_val;
+        p.part_idx = e->lm_idx;
+        p.lm_cnt = e->lm_cnt;
+        p.cnt = e->cnt;
+        p.epoch = e->epoch;
+        p.st = e->st;
+        p.trace = e->step_trace;
+        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_smem, s, e->pdl));
+        return SP_OK;
+    }
     int kidx = 0;       // GEMV index within the step (trace slot)
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const size_t H = c.hidden, I = c.intermediate, QR = (size_t)(c.heads + 2 * c.kv_heads) * c.head_dim;
@@ -265,6 +396,11 @@ int get_graph(sp_engine *e, sp_kv *kv, cudaGraphExec_t *out) {
 }
 
 int run_steps(sp_engine *e, sp_kv *kv, const DevState &init, int n, cudaStream_t s) {
+    if (e->step_kernel) {
+        StepOp *ops = nullptr;                // built outside any stream capture
+        int rc = ensure_step_ops(e, kv, &ops);
+        if (rc != SP_OK) return rc;
+    }
     SP_CUDA(launch_set_state(e->st, init, s));
     if (e->use_graph) {
         cudaGraphExec_t ex;
@@ -342,27 +478,35 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     {
         const char *g = getenv("SEEDPLANE_GEMV");
         e->tc = !(g && strcmp(g, "hmma") == 0);
+        const char *st = getenv("SEEDPLANE_STEP");
+        e->step_kernel = e->tc && !(st && strcmp(st, "chain") == 0);
     }
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
     const size_t H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
-    // LM head rows padded to whole strips (128 rows for the tensor-core GEMV, 16 otherwise)
-    const size_t VP = align_up(V, e->tc ? 128 : 16);
-    if (e->tc && ((size_t)(c.heads + 2 * c.kv_heads) * c.head_dim % 128 || c.hidden % 128 || (2 * (size_t)c.intermediate) % 128)) {
+    if (e->step_kernel && (c.hidden % 64 || c.intermediate % 64)) e->step_kernel = false;   // K in 64-input blocks
+    // Output rows padded to whole strips with zero rows: 256 (step kernel), 128 (kernel-per-op
+    // tensor-core GEMV) or 16 (fragment GEMV); the LM head always, the others only in step mode.
+    const size_t rowpad = e->step_kernel ? 256 : (e->tc ? 128 : 16);
+    const size_t VP = align_up(V, rowpad);
+    if (e->tc && !e->step_kernel &&
+        ((size_t)(c.heads + 2 * c.kv_heads) * c.head_dim % 128 || c.hidden % 128 || (2 * (size_t)c.intermediate) % 128)) {
         delete e;
         return fail(SP_ERR_UNSUPPORTED, "tensor-core GEMV needs qkv rows, hidden and 2*intermediate in multiples of 128");
     }
     const size_t QR = (size_t)(c.heads + 2 * c.kv_heads) * HD;
+    const size_t padq = e->step_kernel ? rowpad : 1;
+    const size_t QRp = align_up(QR, padq), Hp = align_up(H, padq), GUp = align_up(2 * I, padq);
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
     struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post; };
     std::vector<LOff> lo(c.layers);
     for (int l = 0; l < c.layers; ++l) {     // matrix sizes are multiples of 512 B: no gaps
-        lo[l].qkv = take(QR * H * 2);
-        lo[l].o = take(H * H * 2);
-        lo[l].gu = take(2 * I * H * 2);
-        lo[l].dn = take(H * I * 2);
+        lo[l].qkv = take(QRp * H * 2);
+        lo[l].o = take(Hp * H * 2);
+        lo[l].gu = take(GUp * H * 2);
+        lo[l].dn = take(Hp * I * 2);
     }
     const size_t o_head = take(VP * H * 2);
     const size_t stream_end = off;
@@ -393,9 +537,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // ---- pack ------------------------------------------------------------------------------
     // Row maps (packed row -> source row): QKV rows are reordered so the two rows of a RoPE pair
     // (d, d + head_dim/2) of a head are adjacent; gate and up rows are interleaved (gate_i, up_i).
-    const size_t n_iota = std::max(std::max(VP, 2 * I), std::max(QR, H));
-    std::vector<int> idx(QR + 2 * I + n_iota);
-    int *h_perm = idx.data(), *h_gu = idx.data() + QR, *h_iota = idx.data() + QR + 2 * I;
+    // (padded rows map to -1 = zero row)
+    const size_t n_iota = std::max(std::max(VP, GUp), std::max(QRp, Hp));
+    std::vector<int> idx(QRp + GUp + n_iota, -1);
+    int *h_perm = idx.data(), *h_gu = idx.data() + QRp, *h_iota = idx.data() + QRp + GUp;
     for (size_t r = 0; r < QR; ++r) {
         const size_t hh = r / HD, j = r % HD;
         h_perm[r] = (int)(hh * HD + (j / 2) + (j % 2) * (HD / 2));
@@ -404,28 +549,29 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         h_gu[2 * i] = (int)i;
         h_gu[2 * i + 1] = (int)(I + i);
     }
-    for (size_t i = 0; i < n_iota; ++i) h_iota[i] = (int)i;
+    for (size_t i = 0; i < n_iota; ++i) h_iota[i] = i < H ? (int)i : -1;
     std::vector<int> head_rows(VP);
     for (size_t i = 0; i < VP; ++i) head_rows[i] = i < V ? (int)i : -1;
     idx.insert(idx.end(), head_rows.begin(), head_rows.end());
     SP_TRY(cudaMalloc(&d_idx, idx.size() * 4));
     SP_TRY(cudaMemcpy(d_idx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice));
-    const int *d_head_rows = d_idx + QR + 2 * I + n_iota;
-    const int *d_perm = d_idx, *d_gu = d_idx + QR, *d_iota = d_idx + QR + 2 * I;
+    const int *d_head_rows = d_idx + QRp + GUp + n_iota;
+    const int *d_perm = d_idx, *d_gu = d_idx + QRp, *d_iota = d_idx + QRp + GUp;
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
     auto pack = [&](uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K) {
-        return e->tc ? launch_pack_tc(dst, a, rows_a, b, row_of, N, K, s)
-                     : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
+        return e->step_kernel ? launch_pack_sw128(dst, a, rows_a, b, row_of, N, K, s)
+               : e->tc        ? launch_pack_tc(dst, a, rows_a, b, row_of, N, K, s)
+                              : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
     };
     SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
-        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QR, (int)H));
-        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)H, (int)H));
-        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)(2 * I), (int)H));
-        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)H, (int)I));
+        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QRp, (int)H));
+        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)Hp, (int)H));
+        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)GUp, (int)H));
+        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)Hp, (int)I));
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
@@ -519,6 +665,33 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
                 return bail(fail(SP_ERR_UNSUPPORTED, "tensor-core GEMV plan for N=%d K=%d does not fit (%d strips per CTA, %zu B smem)",
                                  t->N, t->K, t->max_items, gemv_tc_smem_bytes(*t)));
     }
+    if (e->step_kernel) {
+        auto sbase = [&](size_t N, size_t K, size_t n_valid) {
+            StepOp o{};
+            o.kind = OP_GEMV;
+            o.N = (int)N;
+            o.K = (int)K;
+            o.n_valid = (int)n_valid;
+            plan_step_gemv(o, e->num_sms);
+            return o;
+        };
+        e->s_qkv = sbase(QRp, H, QR);
+        e->s_o = sbase(Hp, H, H);
+        e->s_gu = sbase(GUp, H, 2 * I);
+        e->s_down = sbase(Hp, I, H);
+        e->s_head = sbase(VP, H, V);
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
+            if (o->max_items > step_max_items() || o->a_blocks > step_max_a_blocks())
+                return bail(fail(SP_ERR_UNSUPPORTED, "step GEMV plan for N=%d K=%d does not fit (%d strips, %d atoms per CTA)",
+                                 o->N, o->K, o->max_items, o->a_blocks));
+    }
+    if (env_flag("SEEDPLANE_VERBOSE", false) && e->step_kernel) {
+        const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
+        int k = 0;
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
+            fprintf(stderr, "[seedplane] step gemv %-8s N=%d K=%d grid=%d b_full=%d atoms=%d contrib<=%d items<=%d\n",
+                    names[k++], o->N, o->K, o->grid, o->b_full, o->a_blocks, o->max_contrib, o->max_items);
+    }
     if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
@@ -548,17 +721,29 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             n_partial = std::max(n_partial, (size_t)t->N * t->max_contrib);
             n_strips = std::max(n_strips, (size_t)t->N / 128);
         }
+    if (e->step_kernel)
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) {
+            n_partial = std::max(n_partial, (size_t)o->N * o->max_contrib);
+            n_strips = std::max(n_strips, (size_t)o->N / 256);
+        }
     size_t woff = 0;
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
+    // counters and split-strip state first: a device error clears exactly this prefix
+    e->n_cnt = 5 * c.layers;
+    e->step_max_chunks = std::min(kStepMaxChunks, e->num_sms / c.kv_heads);
+    const size_t w_cnt = wtake((size_t)e->n_cnt * 8), w_epoch = wtake(8);
+    const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
+    const size_t w_lmcnt = wtake(4);
+    const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
+    e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
     const size_t w_partial = wtake(std::max<size_t>(n_partial, 1) * 4);
-    const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
-    const size_t w_lmcnt = wtake(4);
-    const size_t lm_grid = std::max((size_t)e->g_head.grid, (size_t)e->t_head.grid);
+    const size_t lm_grid = std::max({(size_t)e->g_head.grid, (size_t)e->t_head.grid, (size_t)e->num_sms});
     const size_t w_lmval = wtake(lm_grid * 4), w_lmidx = wtake(lm_grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
-    const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
+    const size_t w_ml = wtake((size_t)c.heads * e->step_max_chunks * 2 * 4);
+    const size_t w_acc = wtake((size_t)c.heads * e->step_max_chunks * HD * 4);
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
@@ -573,6 +758,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->lm_idx = (int *)(e->ws + w_lmidx);
     e->st = (DevState *)(e->ws + w_st);
     e->am = argmax_scratch_at(e->ws + w_am, kArgmaxChunkRows);
+    e->cnt = (unsigned long long *)(e->ws + w_cnt);
+    e->epoch = (unsigned long long *)(e->ws + w_epoch);
+    e->attn_ml = (float *)(e->ws + w_ml);
+    e->attn_acc = (float *)(e->ws + w_acc);
     e->g_head.w = e->head;
     e->g_head.part_val = e->lm_val;
     e->g_head.part_idx = e->lm_idx;
@@ -608,9 +797,27 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(prepare_gemv_tc(PRO_PLAIN, EPI_RESID, e->t_down));
         SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_LMHEAD, e->t_head));
     }
+    if (e->step_kernel) {
+        int ab = 0;
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) ab = std::max(ab, o->a_blocks);
+        e->step_a_blocks = ab;
+        e->step_stages = step_stages_for(ab, (int)HD);
+        if (e->step_stages < 2 || c.kv_heads * e->step_max_chunks > e->num_sms)
+            return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (%d activation atoms, %d stages)", ab,
+                             e->step_stages));
+        e->step_smem = step_smem_bytes(e->step_stages, ab, (int)HD);
+        SP_TRY(prepare_step((int)HD, e->step_smem));
+        if (env_flag("SEEDPLANE_VERBOSE", false))
+            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d atoms=%d smem=%zu max_chunks=%d\n", e->num_sms,
+                    e->step_stages, ab, e->step_smem, e->step_max_chunks);
+    }
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
-    if (env_flag("SEEDPLANE_TRACE", false)) {
+    if (env_flag("SEEDPLANE_TRACE", false) && e->step_kernel) {
+        const size_t words = (size_t)(5 * c.layers + 1) * e->num_sms * kStepTraceWords;
+        SP_TRY(cudaMalloc(&e->step_trace, words * 8));
+        SP_TRY(cudaMemset(e->step_trace, 0, words * 8));
+    } else if (env_flag("SEEDPLANE_TRACE", false)) {
         e->trace_kernels = 4 * c.layers + 1;       // + 2 attention slots after the GEMVs
         SP_TRY(cudaMalloc(&e->trace, (size_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords * 8));
         SP_TRY(cudaMemset(e->trace, 0, (size_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords * 8));
@@ -626,6 +833,8 @@ void sp_engine_destroy(sp_engine *e) {
     if (!e) return;
     cudaSetDevice(e->device);
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto &kv : e->step_ops) cudaFree(kv.second);
+    cudaFree(e->step_trace);
     for (sp_kv *kv : e->caches) kv->e = nullptr;
     if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
     cudaFree(e->arena);
@@ -669,6 +878,11 @@ void sp_kv_destroy(sp_kv *kv) {
         if (it != e->graphs.end()) {
             cudaGraphExecDestroy(it->second);
             e->graphs.erase(it);
+        }
+        auto so = e->step_ops.find(kv);
+        if (so != e->step_ops.end()) {
+            cudaFree(so->second);
+            e->step_ops.erase(so);
         }
         for (size_t i = 0; i < e->caches.size(); ++i)
             if (e->caches[i] == kv) { e->caches.erase(e->caches.begin() + i); break; }
@@ -843,13 +1057,14 @@ int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t
 
 int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity) {
     if (!e) return fail(SP_ERR_INVALID, "null engine");
-    if (!e->trace) return 0;
-    const int64_t n = (int64_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords;
+    if (!e->trace && !e->step_trace) return 0;
+    const int64_t n = e->step_trace ? (int64_t)(5 * e->c.layers + 1) * e->num_sms * kStepTraceWords
+                                    : (int64_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords;
     if (!host_out) return n;
     if (capacity < n) return fail(SP_ERR_CAPACITY, "trace needs %lld words", (long long)n);
     cudaError_t ce = cudaSetDevice(e->device);
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
-    if (ce == cudaSuccess) ce = cudaMemcpy(host_out, e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess) ce = cudaMemcpy(host_out, e->step_trace ? e->step_trace : e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost);
     if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "trace copy: %s", cudaGetErrorString(ce));
     return n;
 }
@@ -862,6 +1077,8 @@ int sp_device_status(sp_engine *e, void *stream) {
     SP_CUDA(cudaMemcpyAsync(&err, &e->st->err, 4, cudaMemcpyDeviceToHost, s));
     SP_CUDA(cudaStreamSynchronize(s));
     if (err) {
+        // a step that gave up left counters and split-strip state undefined: start them afresh
+        SP_CUDA(cudaMemsetAsync(e->ws, 0, e->ws_clear_bytes, s));
         SP_CUDA(cudaMemsetAsync(&e->st->err, 0, 4, s));
         SP_CUDA(cudaStreamSynchronize(s));
         const char *what = err == kErrMbarTimeout ? "a weight stage never arrived (bounded wait expired)"

@@ -22,6 +22,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "tc.cuh"
 
 namespace sp {
 
@@ -41,49 +42,6 @@ constexpr int kMaxPairs = 4;              // B pairs (k-tile, half) per prologue
 SP_DEVINL void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 // warps 0-3 + the MMA warp: the B operand is ready
 SP_DEVINL void bready_sync() { asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads + 32) : "memory"); }
-
-SP_DEVINL uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);   // version 1, no swizzle
-}
-
-// kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N = 8.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
-
-SP_DEVINL void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
-}
-SP_DEVINL void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-SP_DEVINL void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-SP_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-SP_DEVINL void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-SP_DEVINL void tc_argmax_merge(float &v, int &i, float ov, int oi) {
-    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
-}
-
-// The CTA whose tile range [floor(T*c/C), floor(T*(c+1)/C)) contains tile g.
-SP_DEVINL int tc_cta_of(long long g, long long T, int C) {
-    int c = (int)((g * C) / T);
-    while (c > 0 && T * c / C > g) --c;
-    while (c + 1 < C && T * (c + 1) / C <= g) ++c;
-    return c;
-}
 
 }  // namespace
 

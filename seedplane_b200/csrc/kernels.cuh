@@ -158,6 +158,78 @@ cudaError_t launch_pack_fragments(uint8_t *dst, const __half *a, int rows_a, con
 cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap, int hd, const int *src_slots,
                              int n, int dst0, cudaStream_t s);
 
+// ---- persistent decode step: step.cu -----------------------------------------------------------
+// One launch per token runs the whole step on one CTA per SM. The ops of the step (GEMVs with
+// fused prologues/epilogues, and attention) are a table in device memory; every CTA owns a fixed
+// tile range of every GEMV, streams all of its tiles through one ring without waiting for data,
+// and meets the other CTAs only through 64-bit dependency counters in global memory: an op's
+// consumers wait until its counter reaches units x (epoch + 1), where `epoch` counts finished
+// steps (advanced by the LM head's last CTA) and `units` is the number of strips (or CTAs) that
+// signal it once per step.
+enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
+constexpr int PRO_ATTN = 3;              // O-projection prologue: merge the attention partials
+constexpr int kStepAttnRows = 32;        // attention positions staged per sub-chunk
+constexpr int kStepMaxChunks = 64;       // attention chunks per kv head (partials merged by O)
+constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, B ready, done, first / last accumulator
+
+struct StepOp {
+    const uint8_t *w;        // packed tiles (GEMV)
+    const float *xin;        // prologue input (PRO_NORM / PRO_PLAIN)
+    const float *gain;       // RMSNorm gains
+    const float *bias;       // QKV bias
+    float *out;              // epilogue output (q / x / act)
+    __half *kc, *vc;         // this layer's K/V cache (QKV epilogue, attention)
+    int kind;                // StepOpKind
+    int pro, epi;
+    int N, K, n_valid;
+    int b_full;              // B covers all K/16 k-tiles (else the CTA's tiles)
+    int max_contrib;         // CTAs that may share a strip (partial stride)
+    int dep, dep_n;          // wait until cnt[dep] >= dep_n * (epoch + 1); dep < 0: none
+    int sig;                 // cnt[sig] += finished strips (GEMV) / 1 per CTA (attention); < 0: none
+    int resid_embed;         // EPI_RESID: the residual base is the token's embedding row
+    int grid;                // CTAs sharing this GEMV: min(grid, tiles); CTAs beyond own nothing
+    int a_blocks;            // activation atoms this op needs per CTA (plan)
+    int max_items;           // strips a CTA may touch (plan)
+};
+
+struct StepParams {
+    const StepOp *ops;
+    int n_ops;
+    int stages, a_blocks;    // shared-memory layout: ring stages of 32 KB, activation atoms of 1 KB
+    int nh, nkv, hd, cap, max_pos, vocab, hidden;
+    int max_chunks;          // attention chunks per kv head at most (nkv * max_chunks <= grid)
+    float eps, scale;
+    const float *rope;
+    const __half *embed;
+    float *q;                // [nh * hd] fp32 (RoPE applied)
+    float *attn_ml;          // [nh][max_chunks][2]  (running max, sum) per attention chunk
+    float *attn_acc;         // [nh][max_chunks][hd] unnormalised outputs per chunk
+    float *partial;          // split strips [strips][max_contrib][128]
+    unsigned *strip_cnt;     // [strips]
+    float *part_val;         // LM head: per-CTA argmax
+    int *part_idx;
+    unsigned *lm_cnt;
+    unsigned long long *cnt; // dependency counters
+    unsigned long long *epoch;
+    DevState *st;
+    unsigned long long *trace;   // [n_ops][grid][kStepTraceWords] or null
+};
+
+// Weight tiles of the step kernel: 256 output rows x 64 inputs (32 KB), 128B-swizzled K-major.
+// N must be a multiple of 256 (zero-padded rows) and K of 64.
+void plan_step_gemv(StepOp &o, int num_sms);    // fills grid, b_full, a_blocks, max_contrib, max_items
+int step_max_items();
+int step_max_a_blocks();
+cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
+                              cudaStream_t s);
+size_t step_attn_smem_bytes(int hd);
+int step_stages_for(int a_blocks, int hd);
+size_t step_smem_bytes(int stages, int a_blocks, int hd);
+cudaError_t prepare_step(int hd, size_t smem);
+// pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
+// resident at once (one CTA per SM), so the launch is cooperative.
+cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl);
+
 // Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
 // (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per
 // row, which must be zero when the kernel starts and is zero again when it ends.

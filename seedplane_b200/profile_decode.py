@@ -19,9 +19,40 @@ from .config import PRESETS
 from .randinit import make_weights, random_prompt
 
 MODES = {"graph+pdl": ("1", "1"), "graph": ("1", "0"), "eager+pdl": ("0", "1"), "eager": ("0", "0")}
+# --step chain|step: the kernel-per-op chain or the persistent step kernel
 
 
 KERNELS = ("qkv", "o", "gate_up", "down")
+
+
+STEP_OPS = ("qkv", "attn", "o", "gate_up", "down")
+
+
+def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
+    """Timeline of the persistent step kernel from its per-op, per-CTA stamps (microseconds):
+    [0] the CTA reached the op, [1] its dependency was met, [2] activation ready, [3] op done,
+    [4] first accumulator ready, [5] last accumulator ready."""
+    import numpy as np
+    t0 = t[t > 0].min()
+    t = np.where(t > 0, (t - t0) / 1000.0, np.nan)
+    rows, prev_done = [], 0.0
+    for k in range(t.shape[0]):
+        layer, kind = (k // 5, STEP_OPS[k % 5]) if k < 5 * layers else (-1, "lm_head")
+        done = float(np.nanmax(t[k, :, 3]))
+        row = {"k": k, "layer": layer, "kind": kind,
+               "dep_met_max": float(np.nanmax(t[k, :, 1])) if kind != "attn" else None,
+               "bready_med": float(np.nanmedian(t[k, :, 2])) if kind != "attn" else None,
+               "acc_first_med": float(np.nanmedian(t[k, :, 4])) if kind != "attn" else None,
+               "acc_last_med": float(np.nanmedian(t[k, :, 5])) if kind != "attn" else None,
+               "acc_last_max": float(np.nanmax(t[k, :, 5])) if kind != "attn" else None,
+               "done_med": float(np.nanmedian(t[k, :, 3])), "done_max": done, "since_prev_done": done - prev_done}
+        prev_done = done
+        if layer in layers_shown or layer == -1:
+            rows.append({key: (round(v, 2) if isinstance(v, float) else v) for key, v in row.items()})
+    span = float(np.nanmax(t[:, :, 3]))
+    per_layer = [float(np.nanmax(t[5 * l + 4, :, 3]) - (np.nanmax(t[5 * l - 1, :, 3]) if l else 0.0))
+                 for l in range(layers)]
+    return {"step_span_us": round(span, 1), "layer_us_median": round(float(np.median(per_layer)), 2), "ops": rows}
 
 
 def trace_summary(eng, layers_shown=(0, 1, 13)):
@@ -35,6 +66,10 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
         return {}
     buf = (C.c_uint64 * n)()
     N.check(0 if lib.sp_trace_read(eng.handle, buf, n) == n else -2)
+    sms = torch.cuda.get_device_properties(eng.device).multi_processor_count
+    if n == (5 * eng.cfg.layers + 1) * sms * 8:        # persistent step kernel
+        return step_trace_summary(np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(-1, sms, 8),
+                                  eng.cfg.layers, layers_shown)
     words = 8 + 2 * 24
     t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(-1, torch.cuda.get_device_properties(
         eng.device).multi_processor_count, words)
@@ -89,20 +124,22 @@ def main():
     ap.add_argument("--prefetch-mb", default="0", help="comma list of L2 prefetch distances (MB) to compare")
     ap.add_argument("--evict-first", default="0", help="comma list of 0/1: stream weights with evict-first")
     ap.add_argument("--trace", action="store_true", help="print the kernel timeline of the last decode step")
+    ap.add_argument("--step", default="step", help="comma list of step implementations: step (persistent), chain")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
     w = make_weights(cfg, seed=0, dtype=torch.float16)
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
     results = {}
-    variants = [(m, pf, ev) for m in a.modes.split(",") for pf in a.prefetch_mb.split(",")
+    variants = [(m, pf, ev, sk) for sk in a.step.split(",") for m in a.modes.split(",") for pf in a.prefetch_mb.split(",")
                 for ev in a.evict_first.split(",")]
-    for mode, pf, ev in variants:
+    for mode, pf, ev, sk in variants:
         graph, pdl = MODES[mode]
         os.environ["SEEDPLANE_GRAPH"], os.environ["SEEDPLANE_PDL"] = graph, pdl
+        os.environ["SEEDPLANE_STEP"] = sk
         os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
         os.environ["SEEDPLANE_TRACE"] = "1" if a.trace else "0"
-        label = f"{mode} prefetch={pf}MB evict_first={ev}"
+        label = f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
         eng = CudaQwen2(cfg, w)
         kv = eng.new_kv(a.capacity)
         _, am = eng.forward(kv, prompt, want_logits=False)
