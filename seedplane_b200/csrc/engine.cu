@@ -106,6 +106,7 @@ struct sp_engine {
     bool step_kernel = true;
     StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (256 x 64 tiles)
     int step_stages = 0, step_a_blocks = 0, step_max_chunks = 0;
+    int step_l2_ahead = 0;                  // SEEDPLANE_L2_AHEAD tiles (32 KB each) per CTA
     size_t step_smem = 0;
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
@@ -279,6 +280,8 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.vocab = c.vocab;
         p.hidden = c.hidden;
         p.max_chunks = e->step_max_chunks;
+        p.l2_ahead = e->step_l2_ahead;
+        p.evict_first = e->evict_first ? 1 : 0;
         p.eps = c.rms_norm_eps;
         p.scale = 1.0f / sqrtf((float)c.head_dim);
         p.rope = e->rope;
@@ -474,7 +477,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->pdl = env_flag("SEEDPLANE_PDL", true);
     e->use_graph = env_flag("SEEDPLANE_GRAPH", true);
     e->prefetch_ahead = (size_t)std::max(0L, env_long("SEEDPLANE_L2_PREFETCH_MB", 0)) << 20;
-    e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", false);
+    e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", true);
+    e->step_l2_ahead = (int)std::max(0L, std::min(64L, env_long("SEEDPLANE_L2_AHEAD", 0)));
     {
         const char *g = getenv("SEEDPLANE_GEMV");
         e->tc = !(g && strcmp(g, "hmma") == 0);
@@ -801,11 +805,11 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         int ab = 0;
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) ab = std::max(ab, o->a_blocks);
         e->step_a_blocks = ab;
-        e->step_stages = step_stages_for(ab, (int)HD);
+        e->step_stages = step_stages_for(ab, (int)HD, 5 * c.layers + 1);
         if (e->step_stages < 2 || c.kv_heads * e->step_max_chunks > e->num_sms)
             return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (%d activation atoms, %d stages)", ab,
                              e->step_stages));
-        e->step_smem = step_smem_bytes(e->step_stages, ab, (int)HD);
+        e->step_smem = step_smem_bytes(e->step_stages, ab, (int)HD, 5 * c.layers + 1);
         SP_TRY(prepare_step((int)HD, e->step_smem));
         if (env_flag("SEEDPLANE_VERBOSE", false))
             fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d atoms=%d smem=%zu max_chunks=%d\n", e->num_sms,

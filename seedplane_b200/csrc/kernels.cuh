@@ -190,7 +190,9 @@ struct StepOp {
     int grid;                // CTAs sharing this GEMV: min(grid, tiles); CTAs beyond own nothing
     int a_blocks;            // activation atoms this op needs per CTA (plan)
     int max_items;           // strips a CTA may touch (plan)
+    int pad_[3];
 };
+static_assert(sizeof(StepOp) % 16 == 0, "the op table is copied to shared memory in 16-byte words");
 
 struct StepParams {
     const StepOp *ops;
@@ -198,6 +200,8 @@ struct StepParams {
     int stages, a_blocks;    // shared-memory layout: ring stages of 32 KB, activation atoms of 1 KB
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
     int max_chunks;          // attention chunks per kv head at most (nkv * max_chunks <= grid)
+    int l2_ahead;            // weight tiles the producer warms L2 with ahead of its ring (0: off)
+    int evict_first;         // ring copies carry an L2 evict-first hint
     float eps, scale;
     const float *rope;
     const __half *embed;
@@ -223,8 +227,8 @@ int step_max_a_blocks();
 cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
                               cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
-int step_stages_for(int a_blocks, int hd);
-size_t step_smem_bytes(int stages, int a_blocks, int hd);
+int step_stages_for(int a_blocks, int hd, int n_ops);
+size_t step_smem_bytes(int stages, int a_blocks, int hd, int n_ops);
 cudaError_t prepare_step(int hd, size_t smem);
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
 // resident at once (one CTA per SM), so the launch is cooperative.

@@ -50,7 +50,10 @@ constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kTileRows = 256;              // output rows per weight tile (MMA N)
 constexpr int kTileK = 64;                  // inputs per weight tile (one 128-byte swizzled row)
-constexpr int kStepTileBytes = kTileRows * kTileK * 2;    // 32 KB = one ring stage
+constexpr int kStepTileBytes = kTileRows * kTileK * 2;    // 32 KB per weight tile
+constexpr int kStageTiles = 2;              // tiles per ring stage: one 64 KB bulk copy (a bulk copy costs
+                                            // about the same time whatever its size, so big ones ingest faster)
+constexpr int kStageBytes = kStageTiles * kStepTileBytes;
 constexpr int kABlockBytes = 1024;          // activation atom (8 rows x 64 inputs) per k-block
 constexpr int kMaxItems = 16;               // strips a CTA may touch in one op
 constexpr int kTmemCols = 512;              // two accumulators of 256 fp32 columns
@@ -69,6 +72,18 @@ SP_DEVINL unsigned long long ld_acquire_u64(const unsigned long long *p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Cross-CTA hand-off. The writers of a CTA meet at a barrier, then one thread publishes with
+// release semantics (cumulative over the writes the barrier ordered before it); a consumer thread
+// acquires, then its CTA's barrier orders the other threads' reads after the acquire.
+SP_DEVINL unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+SP_DEVINL void red_add_release(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 SP_DEVINL void cp_async16(void *dst, const void *src) {
@@ -109,7 +124,7 @@ SP_DEVINL bool wait_counter(const unsigned long long *cnt, unsigned long long ta
                 *ab.flag = 1;
                 return false;
             }
-            __nanosleep(64);
+            if (i >= 1024u) __nanosleep(64);      // back off only after the first ~1k polls
         }
     }
     ab.raise(kErrDepTimeout);
@@ -189,6 +204,32 @@ SP_DEVINL int attn_chunks(int ctx, int max_chunks) {
 
 SP_DEVINL void stamp(unsigned long long *tr, int k, int C, int c, int i) {
     if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + i] = globaltimer();
+}
+
+
+
+SP_DEVINL void prefetch_line_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// While op k waits for its inputs, the epilogue warps warm L2 with this CTA's weight tiles that the
+// ring cannot hold yet: op k's tiles beyond the ring's depth, then the next GEMV op's, at most
+// `budget` tiles. Plain line prefetches (load/store path), so the copy engine keeps serving the ring;
+// the ring's later bulk copies of these tiles then hit L2.
+SP_DEVINL void warm_l2_for(const StepParams &p, const StepOp *ops, int k, int c, int tid, int skip, int budget) {
+    for (int kk = k; kk < p.n_ops && budget > 0; ++kk) {
+        const StepOp &op = ops[kk];
+        if (op.kind != OP_GEMV) continue;
+        if (c < op.grid) {
+            const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
+            long long g0 = T * c / op.grid;
+            const long long g1 = T * (c + 1) / op.grid;
+            if (kk == k) g0 += skip;
+            for (long long g = g0; g < g1 && budget > 0; ++g, --budget) {
+                const uint8_t *t = op.w + (size_t)g * kStepTileBytes;
+                for (int line = tid; line < kStepTileBytes / 128; line += kEpiThreads) prefetch_line_l2(t + (size_t)line * 128);
+            }
+        }
+        if (kk != k) break;              // this op and the next GEMV op only
+    }
 }
 
 // Per-step values every epilogue thread reads once (after the dependency on the previous step).
@@ -412,11 +453,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     const int C = gridDim.x, c = blockIdx.x;
     const int S = p.stages;
     uint8_t *ring = smem;
-    uint8_t *abuf = smem + (size_t)S * kStepTileBytes;                      // activation atoms, 1 KB per 64 inputs
+    uint8_t *abuf = smem + (size_t)S * kStageBytes;                         // activation atoms, 1 KB per 64 inputs
     uint8_t *am = abuf + (size_t)p.a_blocks * kABlockBytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(am + AttnRegion<HD>::bytes);
+    StepOp *ops = reinterpret_cast<StepOp *>(am + AttnRegion<HD>::bytes);   // the op table, copied once
+    uint64_t *full = reinterpret_cast<uint64_t *>(ops + p.n_ops);
     uint64_t *empty = full + S;
     const Abort ab{&s_abort, p.st};
+
+    // Every role reads op descriptors on its critical path: keep them in shared memory.
+    for (int i = tid; i < p.n_ops * (int)(sizeof(StepOp) / 16); i += kThreads)
+        reinterpret_cast<uint4 *>(ops)[i] = __ldg(reinterpret_cast<const uint4 *>(p.ops) + i);
 
     if (tid == 0) {
         s_abort = 0;
@@ -450,18 +496,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         // ---- producer: every tile of the step, in op order; waits only for free stages ----------
         if (lane == 0) {
             int s = 0, round = 0, issued = 0;
+            const uint64_t pol = policy_evict_first();
             for (int k = 0; k < p.n_ops && !ab.on(); ++k) {
-                const StepOp &op = p.ops[k];
+                const StepOp &op = ops[k];
                 if (op.kind != OP_GEMV) continue;
                 const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
                 const int Cg = op.grid;
                 if (c >= Cg) continue;
                 const long long g0 = T * c / Cg, g1 = T * (c + 1) / Cg;
-                for (long long g = g0; g < g1; ++g) {
+                for (long long g = g0; g < g1; g += kStageTiles) {
                     if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)kStepTileBytes);
-                    bulk_g2s(ring + (size_t)s * kStepTileBytes, op.w + (size_t)g * kStepTileBytes,
-                             (uint32_t)kStepTileBytes, &full[s]);
+                    const int n = (int)(g1 - g < kStageTiles ? g1 - g : kStageTiles);
+                    const uint32_t nb = (uint32_t)(n * kStepTileBytes);
+                    mbar_arrive_expect_tx(&full[s], nb);
+                    if (p.evict_first)
+                        bulk_g2s_hint(ring + (size_t)s * kStageBytes, op.w + (size_t)g * kStepTileBytes, nb, &full[s], pol);
+                    else
+                        bulk_g2s(ring + (size_t)s * kStageBytes, op.w + (size_t)g * kStepTileBytes, nb, &full[s]);
                     ++issued;
                     if (++s == S) {
                         s = 0;
@@ -477,12 +528,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         int s = 0, round = 0, gi = 0, consumed = 0;
         uint32_t gj = 0;                      // items of the step so far (accumulator = gj & 1)
         for (int k = 0; k < p.n_ops; ++k) {
-            const StepOp &op = p.ops[k];
+            const StepOp &op = ops[k];
             if (op.kind != OP_GEMV) continue;
             const int buf = gi & 1;
             ++gi;
             bready_sync();
             tc_fence_after();
+            if (lane == 0 && p.trace) p.trace[((size_t)k * C + c) * kStepTraceWords + 6] = globaltimer();
             if (lane == 0 && !ab.on()) {
                 const int nitems = s_nitems[buf];
                 const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
@@ -491,28 +543,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 int item = 0, t = it_a[buf][0];
                 uint32_t a_blk = (uint32_t)it_boff[buf][0];
                 bool ok = ntiles == 0 || gj < 2 || wait_bar(&tfree[gj & 1], ((gj >> 1) - 1) & 1u, ab);
-                for (int i = 0; i < ntiles && ok; ++i) {
+                for (int i = 0; i < ntiles && ok; i += kStageTiles) {
                     if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
+                    if (i == 0 && p.trace) p.trace[((size_t)k * C + c) * kStepTraceWords + 7] = globaltimer();
                     ++consumed;
                     tc_fence_after();
-                    const uint32_t d = tmem + (gj & 1u) * 256u;
-                    const uint32_t b_addr = ring_addr + (uint32_t)(s * kStepTileBytes);
-                    const uint32_t a_addr = a_addr0 + a_blk * (uint32_t)kABlockBytes;
-                    const bool first = t == it_a[buf][item];
+                    const int n = ntiles - i < kStageTiles ? ntiles - i : kStageTiles;
+                    for (int q = 0; q < n && ok; ++q) {
+                        const uint32_t d = tmem + (gj & 1u) * 256u;
+                        const uint32_t b_addr = ring_addr + (uint32_t)(s * kStageBytes + q * kStepTileBytes);
+                        const uint32_t a_addr = a_addr0 + a_blk * (uint32_t)kABlockBytes;
+                        const bool first = t == it_a[buf][item];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        mma_f16_id(d, smem_desc_sw128(a_addr + 32u * j, 0u), smem_desc_sw128(b_addr + 32u * j, 1024u),
-                                   kIdescM128N256, (first && j == 0) ? 0u : 1u);
-                    ++t;
-                    ++a_blk;
-                    if (t == it_b[buf][item]) {
-                        mma_commit(&accf[gj & 1u]);
-                        ++gj;
-                        if (item + 1 < nitems) {
-                            ++item;
-                            t = it_a[buf][item];
-                            a_blk = (uint32_t)it_boff[buf][item];
-                            if (gj >= 2 && !wait_bar(&tfree[gj & 1u], ((gj >> 1) - 1) & 1u, ab)) ok = false;
+                        for (int j = 0; j < 4; ++j)
+                            mma_f16_id(d, smem_desc_sw128(a_addr + 32u * j, 0u), smem_desc_sw128(b_addr + 32u * j, 1024u),
+                                       kIdescM128N256, (first && j == 0) ? 0u : 1u);
+                        ++t;
+                        ++a_blk;
+                        if (t == it_b[buf][item]) {
+                            mma_commit(&accf[gj & 1u]);
+                            ++gj;
+                            if (item + 1 < nitems) {
+                                ++item;
+                                t = it_a[buf][item];
+                                a_blk = (uint32_t)it_boff[buf][item];
+                                if (gj >= 2 && !wait_bar(&tfree[gj & 1u], ((gj >> 1) - 1) & 1u, ab)) ok = false;
+                            }
                         }
                     }
                     mma_commit(&empty[s]);
@@ -558,15 +614,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         int gi = 0;
 
         for (int k = 0; k < p.n_ops; ++k) {
-            const StepOp &op = p.ops[k];
+            const StepOp &op = ops[k];
             stamp(p.trace, k, C, c, 0);
             if (op.kind == OP_ATTN) {
                 const int items = p.nkv * n_chunks;
                 if (c < items && !ab.on()) attention_item<HD>(p, op, ss, am, c, n_chunks, rows_per, ctx, ab);
-                __threadfence();
                 epi_sync();
                 stamp(p.trace, k, C, c, 3);
-                if (tid == 0 && op.sig >= 0) atomicAdd(p.cnt + op.sig, 1ull);
+                if (tid == 0 && op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
                 continue;
             }
             const int buf = gi & 1;
@@ -593,9 +648,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     ++n;
                 }
                 s_nitems[buf] = n;
-                if (op.dep >= 0 && !ab.on())
-                    wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
             }
+            if (p.l2_ahead > 0 && op.dep >= 0) warm_l2_for(p, ops, k, c, tid, S * kStageTiles, p.l2_ahead);
+            if (tid == 0 && op.dep >= 0 && !ab.on())
+                wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
             epi_sync();
             stamp(p.trace, k, C, c, 1);
             const int nitems = s_nitems[buf];
@@ -710,7 +766,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             float bv = -INFINITY;
             int bi = INT_MAX;
             int n_final = 0;
+            const int col = 64 * warp + 2 * lane;   // this thread's row pair (col, col + 1) of a strip
             for (int j = 0; j < nitems; ++j) {
+                // epilogue operands that do not depend on the accumulator: load them before waiting
+                const int strip = it_strip[buf][j];
+                const int row = strip * kTileRows + col;
+                float pre0 = 0.f, pre1 = 0.f, pcs = 1.f, psn = 0.f;
+                if (row < op.n_valid) {
+                    if (op.epi == EPI_RESID) {
+                        if (op.resid_embed) {
+                            const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
+                            pre0 = __low2float(e2);
+                            pre1 = __high2float(e2);
+                        } else {
+                            const float2 b2 = __ldcg(reinterpret_cast<const float2 *>(op.out + row));
+                            pre0 = b2.x;
+                            pre1 = b2.y;
+                        }
+                    } else if (op.epi == EPI_QKV) {
+                        const int P = row / 2, hh = P / half_hd, dd = P - hh * half_hd;
+                        pre0 = __ldg(op.bias + hh * HD + dd);
+                        pre1 = __ldg(op.bias + hh * HD + dd + half_hd);
+                        if (hh < p.nh + p.nkv) {
+                            const float2 r2 = __ldg(reinterpret_cast<const float2 *>(p.rope + ((size_t)ss.pos * half_hd + dd) * 2));
+                            pcs = r2.x;
+                            psn = r2.y;
+                        }
+                    }
+                }
                 const uint32_t tb = gj & 1u;
                 const bool ok = !ab.on() && wait_bar(&accf[tb], (gj >> 1) & 1u, ab);
                 ++gj;
@@ -744,20 +827,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 const float2 lv = *reinterpret_cast<const float2 *>(&ystage[warp][1][2 * lane]);
                 __syncwarp();
                 float y0 = hv.x + lv.x, y1 = hv.y + lv.y;
-                const int strip = it_strip[buf][j];
-                const int col = 64 * warp + 2 * lane;   // row pair (col, col + 1) of the strip
                 if (it_a[buf][j] != 0 || it_b[buf][j] != KB) {
                     // strip shared with other CTAs: post this part; the last contributor sums all
                     const long long first = (long long)strip * KB;
                     const int cf = tc_cta_of(first, T, Cg), cl = tc_cta_of(first + KB - 1, T, Cg);
                     float *slotp = p.partial + ((size_t)strip * op.max_contrib + (c - cf)) * kTileRows;
                     *reinterpret_cast<float2 *>(slotp + col) = make_float2(y0, y1);
-                    __threadfence();
                     epi_sync();
-                    if (tid == 0) s_flag = atomicAdd(p.strip_cnt + strip, 1u) == (unsigned)(cl - cf);
+                    if (tid == 0) s_flag = atom_add_acq_rel(p.strip_cnt + strip, 1u) == (unsigned)(cl - cf);
                     epi_sync();
                     if (!s_flag) continue;
-                    __threadfence();
                     const float *all = p.partial + (size_t)strip * op.max_contrib * kTileRows + col;
                     y0 = 0.f;
                     y1 = 0.f;
@@ -778,15 +857,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     if (tid == 0) p.strip_cnt[strip] = 0u;
                 }
                 ++n_final;
-                const int row = strip * kTileRows + col;
                 if (row >= op.n_valid) continue;
                 if (op.epi == EPI_RESID) {
-                    const float b0 = op.resid_embed ? __half2float(p.embed[(size_t)ss.token * p.hidden + row])
-                                                    : __ldcg(op.out + row);
-                    const float b1 = op.resid_embed ? __half2float(p.embed[(size_t)ss.token * p.hidden + row + 1])
-                                                    : __ldcg(op.out + row + 1);
-                    op.out[row] = b0 + y0;
-                    op.out[row + 1] = b1 + y1;
+                    *reinterpret_cast<float2 *>(op.out + row) = make_float2(pre0 + y0, pre1 + y1);
                 } else if (op.epi == EPI_LMHEAD) {
                     if (lg) lg[row] = y0;
                     if (y0 > bv) {
@@ -806,10 +879,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     const int P = row / 2;
                     const int hh = P / half_hd, dd = P - hh * half_hd;
                     const int lo = hh * HD + dd, hi = lo + half_hd;
-                    const float a0 = y0 + __ldg(op.bias + lo), a1 = y1 + __ldg(op.bias + hi);
+                    const float a0 = y0 + pre0, a1 = y1 + pre1;
                     if (hh < p.nh + p.nkv) {
-                        const float cs = __ldg(p.rope + ((size_t)ss.pos * half_hd + dd) * 2);
-                        const float sn = __ldg(p.rope + ((size_t)ss.pos * half_hd + dd) * 2 + 1);
+                        const float cs = pcs, sn = psn;
                         const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
                         const float o1 = __fadd_rn(__fmul_rn(a1, cs), __fmul_rn(a0, sn));
                         if (hh < p.nh) {
@@ -846,12 +918,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     for (int w = 1; w < 4; ++w) tc_argmax_merge(vb, ib, s_val[w], s_idx[w]);
                     p.part_val[c] = vb;
                     p.part_idx[c] = ib;
-                    __threadfence();
-                    s_flag = atomicAdd(p.lm_cnt, 1u) == (unsigned)C - 1u;
+                    s_flag = atom_add_acq_rel(p.lm_cnt, 1u) == (unsigned)C - 1u;
                 }
                 epi_sync();
                 if (s_flag) {
-                    __threadfence();
                     float vb = -INFINITY;
                     int ib = INT_MAX;
                     for (int j = tid; j < C; j += kEpiThreads)
@@ -893,9 +963,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     }
                 }
             } else if (op.sig >= 0) {
-                __threadfence();
                 epi_sync();
-                if (tid == 0 && n_final > 0) atomicAdd(p.cnt + op.sig, (unsigned long long)n_final);
+                if (tid == 0 && n_final > 0) red_add_release(p.cnt + op.sig, (unsigned long long)n_final);
             }
             stamp(p.trace, k, C, c, 3);
         }
@@ -961,16 +1030,16 @@ size_t step_attn_smem_bytes(int hd) { return hd == 64 ? AttnRegion<64>::bytes : 
 
 static size_t step_static_reserve() { return 4096; }   // static shared memory of k_step, rounded up
 
-size_t step_smem_bytes(int stages, int a_blocks, int hd) {
-    return (size_t)stages * kStepTileBytes + (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd) +
-           (size_t)(2 * stages) * 8;
+size_t step_smem_bytes(int stages, int a_blocks, int hd, int n_ops) {
+    return (size_t)stages * kStageBytes + (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd) +
+           (size_t)n_ops * sizeof(StepOp) + (size_t)(2 * stages) * 8;
 }
 
-int step_stages_for(int a_blocks, int hd) {
+int step_stages_for(int a_blocks, int hd, int n_ops) {
     const size_t budget = 227 * 1024 - step_static_reserve();
-    const size_t fixed = (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd);
+    const size_t fixed = (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp);
     if (fixed >= budget) return 0;
-    return (int)((budget - fixed) / (kStepTileBytes + 16));
+    return (int)((budget - fixed) / (kStageBytes + 16));
 }
 
 cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,

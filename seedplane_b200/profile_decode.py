@@ -31,7 +31,8 @@ STEP_OPS = ("qkv", "attn", "o", "gate_up", "down")
 def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
     """Timeline of the persistent step kernel from its per-op, per-CTA stamps (microseconds):
     [0] the CTA reached the op, [1] its dependency was met, [2] activation ready, [3] op done,
-    [4] first accumulator ready, [5] last accumulator ready."""
+    [4] first accumulator ready, [5] last accumulator ready, [6] MMA warp starts the op, [7] the op's first
+    ring stage is available to the MMA warp."""
     import numpy as np
     t0 = t[t > 0].min()
     t = np.where(t > 0, (t - t0) / 1000.0, np.nan)
@@ -42,6 +43,8 @@ def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
         row = {"k": k, "layer": layer, "kind": kind,
                "dep_met_max": float(np.nanmax(t[k, :, 1])) if kind != "attn" else None,
                "bready_med": float(np.nanmedian(t[k, :, 2])) if kind != "attn" else None,
+               "mma_start_med": float(np.nanmedian(t[k, :, 6])) if kind != "attn" else None,
+               "tile0_med": float(np.nanmedian(t[k, :, 7])) if kind != "attn" else None,
                "acc_first_med": float(np.nanmedian(t[k, :, 4])) if kind != "attn" else None,
                "acc_last_med": float(np.nanmedian(t[k, :, 5])) if kind != "attn" else None,
                "acc_last_max": float(np.nanmax(t[k, :, 5])) if kind != "attn" else None,
@@ -125,21 +128,23 @@ def main():
     ap.add_argument("--evict-first", default="0", help="comma list of 0/1: stream weights with evict-first")
     ap.add_argument("--trace", action="store_true", help="print the kernel timeline of the last decode step")
     ap.add_argument("--step", default="step", help="comma list of step implementations: step (persistent), chain")
+    ap.add_argument("--l2-ahead", default="0", help="comma list: weight tiles the step kernel warms L2 with ahead")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
     w = make_weights(cfg, seed=0, dtype=torch.float16)
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
     results = {}
-    variants = [(m, pf, ev, sk) for sk in a.step.split(",") for m in a.modes.split(",") for pf in a.prefetch_mb.split(",")
-                for ev in a.evict_first.split(",")]
-    for mode, pf, ev, sk in variants:
+    variants = [(m, pf, ev, sk, la) for sk in a.step.split(",") for m in a.modes.split(",")
+                for pf in a.prefetch_mb.split(",") for ev in a.evict_first.split(",") for la in a.l2_ahead.split(",")]
+    for mode, pf, ev, sk, la in variants:
         graph, pdl = MODES[mode]
         os.environ["SEEDPLANE_GRAPH"], os.environ["SEEDPLANE_PDL"] = graph, pdl
         os.environ["SEEDPLANE_STEP"] = sk
+        os.environ["SEEDPLANE_L2_AHEAD"] = la
         os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
         os.environ["SEEDPLANE_TRACE"] = "1" if a.trace else "0"
-        label = f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
+        label = f"{sk} {mode} l2_ahead={la} evict_first={ev}" if sk == "step" else f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
         eng = CudaQwen2(cfg, w)
         kv = eng.new_kv(a.capacity)
         _, am = eng.forward(kv, prompt, want_logits=False)
