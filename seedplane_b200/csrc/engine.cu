@@ -107,6 +107,7 @@ struct sp_engine {
     StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (256 x 64 tiles)
     int step_stages = 0, step_a_blocks = 0, step_max_chunks = 0;
     int step_l2_ahead = 0;                  // SEEDPLANE_L2_AHEAD tiles (32 KB each) per CTA
+    int step_min_tiles = 4;                 // SEEDPLANE_STEP_MIN_TILES: tiles per CTA at least (narrow GEMVs)
     size_t step_smem = 0;
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
@@ -479,6 +480,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->prefetch_ahead = (size_t)std::max(0L, env_long("SEEDPLANE_L2_PREFETCH_MB", 0)) << 20;
     e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", true);
     e->step_l2_ahead = (int)std::max(0L, std::min(64L, env_long("SEEDPLANE_L2_AHEAD", 0)));
+    e->step_min_tiles = (int)std::max(1L, std::min(64L, env_long("SEEDPLANE_STEP_MIN_TILES", 4)));
     {
         const char *g = getenv("SEEDPLANE_GEMV");
         e->tc = !(g && strcmp(g, "hmma") == 0);
@@ -676,7 +678,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             o.N = (int)N;
             o.K = (int)K;
             o.n_valid = (int)n_valid;
-            plan_step_gemv(o, e->num_sms);
+            plan_step_gemv(o, e->num_sms, e->step_min_tiles);
             return o;
         };
         e->s_qkv = sbase(QRp, H, QR);

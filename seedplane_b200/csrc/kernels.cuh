@@ -221,7 +221,7 @@ struct StepParams {
 
 // Weight tiles of the step kernel: 256 output rows x 64 inputs (32 KB), 128B-swizzled K-major.
 // N must be a multiple of 256 (zero-padded rows) and K of 64.
-void plan_step_gemv(StepOp &o, int num_sms);    // fills grid, b_full, a_blocks, max_contrib, max_items
+void plan_step_gemv(StepOp &o, int num_sms, int min_tiles);   // fills grid, b_full, a_blocks, max_contrib, max_items
 int step_max_items();
 int step_max_a_blocks();
 cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,

@@ -617,8 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             const StepOp &op = ops[k];
             stamp(p.trace, k, C, c, 0);
             if (op.kind == OP_ATTN) {
-                const int items = p.nkv * n_chunks;
-                if (c < items && !ab.on()) attention_item<HD>(p, op, ss, am, c, n_chunks, rows_per, ctx, ab);
+                // items on the last CTAs: narrow GEMVs use the first ones, so these arrive early and
+                // stage their K/V rows while the QKV projection is still running
+                const int items = p.nkv * n_chunks, item = C - 1 - c;
+                if (item < items && !ab.on()) attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab);
                 epi_sync();
                 stamp(p.trace, k, C, c, 3);
                 if (tid == 0 && op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
@@ -841,15 +843,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     y0 = 0.f;
                     y1 = 0.f;
                     const int ncon = cl - cf + 1;
-                    for (int k2 = 0; k2 < ncon; k2 += 8) {
-                        // eight contributors' loads in flight, summed in contributor order
-                        float2 pv[8];
+                    for (int k2 = 0; k2 < ncon; k2 += 16) {
+                        // sixteen contributors' loads in flight, summed in contributor order
+                        float2 pv[16];
 #pragma unroll
-                        for (int u = 0; u < 8; ++u)
+                        for (int u = 0; u < 16; ++u)
                             pv[u] = k2 + u < ncon ? __ldcg(reinterpret_cast<const float2 *>(all + (size_t)(k2 + u) * kTileRows))
                                                   : make_float2(0.f, 0.f);
 #pragma unroll
-                        for (int u = 0; u < 8; ++u) {
+                        for (int u = 0; u < 16; ++u) {
                             y0 += pv[u].x;
                             y1 += pv[u].y;
                         }
@@ -1011,10 +1013,12 @@ __global__ void k_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-void plan_step_gemv(StepOp &o, int num_sms) {
+void plan_step_gemv(StepOp &o, int num_sms, int min_tiles) {
     const int KB = o.K / kTileK;
     const long long T = (long long)(o.N / kTileRows) * KB;
-    o.grid = (int)std::min<long long>(num_sms, T);
+    // at least `min_tiles` tiles per CTA: fewer CTAs share a strip, so its last contributor sums
+    // fewer partials and waits for fewer CTAs
+    o.grid = (int)std::max<long long>(1, std::min<long long>(num_sms, T / std::max(1, min_tiles)));
     const long long per = (T + o.grid - 1) / o.grid;
     o.b_full = per >= KB ? 1 : 0;
     o.a_blocks = o.b_full ? KB : (int)per;
