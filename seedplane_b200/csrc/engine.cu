@@ -104,15 +104,14 @@ struct sp_engine {
     ArgmaxScratch am{};                     // sp_argmax: kArgmaxChunkRows rows per launch
     // persistent step kernel (default; SEEDPLANE_STEP=chain selects the kernel-per-op chain)
     bool step_kernel = true;
-    StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (256 x 64 tiles)
-    int step_stages = 0, step_a_blocks = 0, step_max_chunks = 0;
-    int step_l2_ahead = 0;                  // SEEDPLANE_L2_AHEAD tiles (32 KB each) per CTA
-    int step_min_tiles = 4;                 // SEEDPLANE_STEP_MIN_TILES: tiles per CTA at least (narrow GEMVs)
+    StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (row blocks)
+    int step_stages = 0, step_xmax = 0, step_max_chunks = 0;
     size_t step_smem = 0;
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
     int n_cnt = 0;
-    float *attn_ml = nullptr, *attn_acc = nullptr;
+    float *attn_ml = nullptr, *attn_acc = nullptr, *attn_out = nullptr;
+    unsigned *grp_cnt = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
     unsigned long long *step_trace = nullptr;
@@ -200,12 +199,12 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.sig = sig;
         return o;
     };
-    const int sx = e->s_o.N / 256, sq = e->s_qkv.N / 256, sgu = e->s_gu.N / 256;   // strips signalled per op
+    // signals per step: one per CTA owning rows of a GEMV, one per kv head for attention
     for (int l = 0; l < c.layers; ++l) {
         const LayerDev &L = e->layers[l];
         __half *kc = kv->k + l * kv_layer, *vc = kv->v + l * kv_layer;
         StepOp o = gemv(e->s_qkv, L.qkv, l == 0 ? PRO_EMBED_NORM : PRO_NORM, EPI_QKV, l == 0 ? -1 : 5 * (l - 1) + 4,
-                        sx, 5 * l + 0);
+                        e->s_down.grid, 5 * l + 0);
         o.xin = e->x;
         o.gain = L.in_norm;
         o.bias = L.qkv_b;
@@ -218,24 +217,24 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         a.kc = kc;
         a.vc = vc;
         a.dep = 5 * l + 0;
-        a.dep_n = sq;
+        a.dep_n = e->s_qkv.grid;
         a.sig = 5 * l + 1;
         ops.push_back(a);
-        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, grid, 5 * l + 2);
+        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, c.kv_heads, 5 * l + 2);
         o.out = e->x;
         o.resid_embed = l == 0;
         ops.push_back(o);
-        o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU, 5 * l + 2, sx, 5 * l + 3);
+        o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU, 5 * l + 2, e->s_o.grid, 5 * l + 3);
         o.xin = e->x;
         o.gain = L.post_norm;
         o.out = e->act;
         ops.push_back(o);
-        o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID, 5 * l + 3, sgu, 5 * l + 4);
+        o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID, 5 * l + 3, e->s_gu.grid, 5 * l + 4);
         o.xin = e->act;
         o.out = e->x;
         ops.push_back(o);
     }
-    StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD, 5 * (c.layers - 1) + 4, sx, -1);
+    StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD, 5 * (c.layers - 1) + 4, e->s_down.grid, -1);
     o.xin = e->x;
     o.gain = e->final_norm;
     ops.push_back(o);
@@ -272,7 +271,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.ops = ops;
         p.n_ops = e->n_step_ops;
         p.stages = e->step_stages;
-        p.a_blocks = e->step_a_blocks;
+        p.xmax = e->step_xmax;
         p.nh = c.heads;
         p.nkv = c.kv_heads;
         p.hd = c.head_dim;
@@ -281,7 +280,6 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.vocab = c.vocab;
         p.hidden = c.hidden;
         p.max_chunks = e->step_max_chunks;
-        p.l2_ahead = e->step_l2_ahead;
         p.evict_first = e->evict_first ? 1 : 0;
         p.eps = c.rms_norm_eps;
         p.scale = 1.0f / sqrtf((float)c.head_dim);
@@ -290,8 +288,8 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.q = e->q;
         p.attn_ml = e->attn_ml;
         p.attn_acc = e->attn_acc;
-        p.partial = e->partial;
-        p.strip_cnt = e->strip_cnt;
+        p.attn_out = e->attn_out;
+        p.grp_cnt = e->grp_cnt;
         p.part_val = e->lm_val;
         p.part_idx = e->lm_idx;
         p.lm_cnt = e->lm_cnt;
@@ -479,8 +477,6 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->use_graph = env_flag("SEEDPLANE_GRAPH", true);
     e->prefetch_ahead = (size_t)std::max(0L, env_long("SEEDPLANE_L2_PREFETCH_MB", 0)) << 20;
     e->evict_first = env_flag("SEEDPLANE_EVICT_FIRST", true);
-    e->step_l2_ahead = (int)std::max(0L, std::min(64L, env_long("SEEDPLANE_L2_AHEAD", 0)));
-    e->step_min_tiles = (int)std::max(1L, std::min(64L, env_long("SEEDPLANE_STEP_MIN_TILES", 4)));
     {
         const char *g = getenv("SEEDPLANE_GEMV");
         e->tc = !(g && strcmp(g, "hmma") == 0);
@@ -490,10 +486,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
     const size_t H = c.hidden, I = c.intermediate, V = c.vocab, HD = c.head_dim;
-    if (e->step_kernel && (c.hidden % 64 || c.intermediate % 64)) e->step_kernel = false;   // K in 64-input blocks
-    // Output rows padded to whole strips with zero rows: 256 (step kernel), 128 (kernel-per-op
-    // tensor-core GEMV) or 16 (fragment GEMV); the LM head always, the others only in step mode.
-    const size_t rowpad = e->step_kernel ? 256 : (e->tc ? 128 : 16);
+    // Output rows padded with zero rows to whole strips of the kernel-per-op GEMVs: 128 (tensor
+    // core) or 16 (fragment GEMV); the step kernel only needs row pairs.
+    const size_t rowpad = e->step_kernel ? 2 : (e->tc ? 128 : 16);
     const size_t VP = align_up(V, rowpad);
     if (e->tc && !e->step_kernel &&
         ((size_t)(c.heads + 2 * c.kv_heads) * c.head_dim % 128 || c.hidden % 128 || (2 * (size_t)c.intermediate) % 128)) {
@@ -503,6 +498,29 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t QR = (size_t)(c.heads + 2 * c.kv_heads) * HD;
     const size_t padq = e->step_kernel ? rowpad : 1;
     const size_t QRp = align_up(QR, padq), Hp = align_up(H, padq), GUp = align_up(2 * I, padq);
+    if (e->step_kernel) {
+        // row-block plans (the packing depends on them)
+        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro) {
+            StepOp o{};
+            o.kind = OP_GEMV;
+            o.pro = pro;
+            o.N = (int)N;
+            o.K = (int)K;
+            o.n_valid = (int)n_valid;
+            plan_step_gemv(o, e->num_sms);
+            return o;
+        };
+        e->s_qkv = sbase(QRp, H, QR, PRO_NORM);
+        e->s_o = sbase(Hp, H, H, PRO_ATTN);
+        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM);
+        e->s_down = sbase(Hp, I, H, PRO_PLAIN);
+        e->s_head = sbase(VP, H, V, PRO_NORM);
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
+            if (!step_gemv_supported(*o)) {
+                delete e;
+                return fail(SP_ERR_UNSUPPORTED, "step GEMV of N=%d K=%d is not supported", o->N, o->K);
+            }
+    }
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
@@ -565,19 +583,21 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const int *d_perm = d_idx, *d_gu = d_idx + QRp, *d_iota = d_idx + QRp + GUp;
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
-    auto pack = [&](uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K) {
-        return e->step_kernel ? launch_pack_sw128(dst, a, rows_a, b, row_of, N, K, s)
+    auto pack = [&](uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
+                    const StepOp &plan) {
+        return e->step_kernel ? launch_pack_rows(dst, a, rows_a, b, row_of, plan, s)
                : e->tc        ? launch_pack_tc(dst, a, rows_a, b, row_of, N, K, s)
                               : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
     };
-    SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H));
+    SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H, e->s_head));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
-        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QRp, (int)H));
-        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)Hp, (int)H));
-        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)GUp, (int)H));
-        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)Hp, (int)I));
+        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QRp, (int)H, e->s_qkv));
+        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)Hp, (int)H, e->s_o));
+        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)GUp, (int)H,
+                    e->s_gu));
+        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)Hp, (int)I, e->s_down));
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
@@ -660,7 +680,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         plan_gemv_tc(t, e->num_sms, kTcRingBytes, kTcBBudget);
         return t;
     };
-    if (e->tc) {
+    if (e->tc && !e->step_kernel) {
         e->t_qkv = tbase(QR, H, (int)QR);
         e->t_o = tbase(H, H, (int)H);
         e->t_gu = tbase(2 * I, H, (int)(2 * I));
@@ -671,34 +691,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
                 return bail(fail(SP_ERR_UNSUPPORTED, "tensor-core GEMV plan for N=%d K=%d does not fit (%d strips per CTA, %zu B smem)",
                                  t->N, t->K, t->max_items, gemv_tc_smem_bytes(*t)));
     }
-    if (e->step_kernel) {
-        auto sbase = [&](size_t N, size_t K, size_t n_valid) {
-            StepOp o{};
-            o.kind = OP_GEMV;
-            o.N = (int)N;
-            o.K = (int)K;
-            o.n_valid = (int)n_valid;
-            plan_step_gemv(o, e->num_sms, e->step_min_tiles);
-            return o;
-        };
-        e->s_qkv = sbase(QRp, H, QR);
-        e->s_o = sbase(Hp, H, H);
-        e->s_gu = sbase(GUp, H, 2 * I);
-        e->s_down = sbase(Hp, I, H);
-        e->s_head = sbase(VP, H, V);
-        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            if (o->max_items > step_max_items() || o->a_blocks > step_max_a_blocks())
-                return bail(fail(SP_ERR_UNSUPPORTED, "step GEMV plan for N=%d K=%d does not fit (%d strips, %d atoms per CTA)",
-                                 o->N, o->K, o->max_items, o->a_blocks));
-    }
     if (env_flag("SEEDPLANE_VERBOSE", false) && e->step_kernel) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            fprintf(stderr, "[seedplane] step gemv %-8s N=%d K=%d grid=%d b_full=%d atoms=%d contrib<=%d items<=%d\n",
-                    names[k++], o->N, o->K, o->grid, o->b_full, o->a_blocks, o->max_contrib, o->max_items);
+            fprintf(stderr, "[seedplane] step gemv %-8s N=%d K=%d grid=%d pass_rows=%d chunk=%d\n", names[k++], o->N,
+                    o->K, o->grid, o->pass_rows, o->chunk_w);
     }
-    if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc) {
+    if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc && !e->step_kernel) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
         for (const TcGemvParams *t : {&e->t_qkv, &e->t_o, &e->t_gu, &e->t_down, &e->t_head})
@@ -727,11 +727,6 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             n_partial = std::max(n_partial, (size_t)t->N * t->max_contrib);
             n_strips = std::max(n_strips, (size_t)t->N / 128);
         }
-    if (e->step_kernel)
-        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) {
-            n_partial = std::max(n_partial, (size_t)o->N * o->max_contrib);
-            n_strips = std::max(n_strips, (size_t)o->N / 256);
-        }
     size_t woff = 0;
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
     // counters and split-strip state first: a device error clears exactly this prefix
@@ -741,6 +736,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
     const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
+    const size_t w_grp = wtake((size_t)c.kv_heads * 4);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
@@ -750,6 +746,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_st = wtake(sizeof(DevState));
     const size_t w_ml = wtake((size_t)c.heads * e->step_max_chunks * 2 * 4);
     const size_t w_acc = wtake((size_t)c.heads * e->step_max_chunks * HD * 4);
+    const size_t w_aout = wtake((size_t)c.heads * HD * 4);
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
@@ -768,6 +765,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->epoch = (unsigned long long *)(e->ws + w_epoch);
     e->attn_ml = (float *)(e->ws + w_ml);
     e->attn_acc = (float *)(e->ws + w_acc);
+    e->attn_out = (float *)(e->ws + w_aout);
+    e->grp_cnt = (unsigned *)(e->ws + w_grp);
     e->g_head.w = e->head;
     e->g_head.part_val = e->lm_val;
     e->g_head.part_idx = e->lm_idx;
@@ -788,14 +787,16 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->t_head.part_idx = e->lm_idx;
     e->t_head.counter = e->lm_cnt;
     e->t_head.w = e->head;
-    SP_TRY(prepare_gemv(PRO_NORM, EPI_QKV, e->g_qkv));
-    SP_TRY(prepare_gemv(PRO_EMBED_NORM, EPI_QKV, e->g_qkv));
-    SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_o));
-    SP_TRY(prepare_gemv(PRO_NORM, EPI_SWIGLU, e->g_gu));
-    SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_down));
-    SP_TRY(prepare_gemv(PRO_NORM, EPI_LMHEAD, e->g_head));
+    if (!e->tc) {
+        SP_TRY(prepare_gemv(PRO_NORM, EPI_QKV, e->g_qkv));
+        SP_TRY(prepare_gemv(PRO_EMBED_NORM, EPI_QKV, e->g_qkv));
+        SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_o));
+        SP_TRY(prepare_gemv(PRO_NORM, EPI_SWIGLU, e->g_gu));
+        SP_TRY(prepare_gemv(PRO_PLAIN, EPI_RESID, e->g_down));
+        SP_TRY(prepare_gemv(PRO_NORM, EPI_LMHEAD, e->g_head));
+    }
     SP_TRY(prepare_attention());
-    if (e->tc) {
+    if (e->tc && !e->step_kernel) {
         SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_QKV, e->t_qkv));
         SP_TRY(prepare_gemv_tc(PRO_EMBED_NORM, EPI_QKV, e->t_qkv));
         SP_TRY(prepare_gemv_tc(PRO_PLAIN, EPI_RESID, e->t_o));
@@ -804,21 +805,19 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_LMHEAD, e->t_head));
     }
     if (e->step_kernel) {
-        int ab = 0;
-        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) ab = std::max(ab, o->a_blocks);
-        e->step_a_blocks = ab;
-        e->step_stages = step_stages_for(ab, (int)HD, 5 * c.layers + 1);
+        e->step_xmax = (int)align_up(std::max(H, I), 4);
+        e->step_stages = step_stages_for(e->step_xmax, (int)HD, 5 * c.layers + 1);
         if (e->step_stages < 2 || c.kv_heads * e->step_max_chunks > e->num_sms)
-            return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (%d activation atoms, %d stages)", ab,
-                             e->step_stages));
-        e->step_smem = step_smem_bytes(e->step_stages, ab, (int)HD, 5 * c.layers + 1);
+            return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (input vector of %d floats, %d stages)",
+                             e->step_xmax, e->step_stages));
+        e->step_smem = step_smem_bytes(e->step_stages, e->step_xmax, (int)HD, 5 * c.layers + 1);
         SP_TRY(prepare_step((int)HD, e->step_smem));
         if (env_flag("SEEDPLANE_VERBOSE", false))
-            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d atoms=%d smem=%zu max_chunks=%d\n", e->num_sms,
-                    e->step_stages, ab, e->step_smem, e->step_max_chunks);
+            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d xmax=%d smem=%zu max_chunks=%d\n", e->num_sms,
+                    e->step_stages, e->step_xmax, e->step_smem, e->step_max_chunks);
     }
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
-        if (gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
+        if (!e->tc && gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));
     if (env_flag("SEEDPLANE_TRACE", false) && e->step_kernel) {
         const size_t words = (size_t)(5 * c.layers + 1) * e->num_sms * kStepTraceWords;
         SP_TRY(cudaMalloc(&e->step_trace, words * 8));

@@ -160,20 +160,22 @@ cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap,
 
 // ---- persistent decode step: step.cu -----------------------------------------------------------
 // One launch per token runs the whole step on one CTA per SM. The ops of the step (GEMVs with
-// fused prologues/epilogues, and attention) are a table in device memory; every CTA owns a fixed
-// tile range of every GEMV, streams all of its tiles through one ring without waiting for data,
-// and meets the other CTAs only through 64-bit dependency counters in global memory: an op's
-// consumers wait until its counter reaches units x (epoch + 1), where `epoch` counts finished
-// steps (advanced by the LM head's last CTA) and `units` is the number of strips (or CTAs) that
-// signal it once per step.
+// fused prologues/epilogues, and attention) are a table in device memory. Every CTA owns whole
+// output rows of every GEMV (no split-K), streams all of its weight units through one ring
+// without waiting for data, and meets the other CTAs only through 64-bit dependency counters in
+// global memory: an op's consumers wait until its counter reaches units x (epoch + 1), where
+// `epoch` counts finished steps (advanced by the LM head's last CTA) and `units` is the number of
+// CTAs (GEMVs) or kv heads (attention) that signal it once per step.
 enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
-constexpr int PRO_ATTN = 3;              // O-projection prologue: merge the attention partials
+constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged attention output
 constexpr int kStepAttnRows = 32;        // attention positions staged per sub-chunk
-constexpr int kStepMaxChunks = 64;       // attention chunks per kv head (partials merged by O)
-constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, B ready, done, first / last accumulator
+constexpr int kStepMaxChunks = 64;       // attention chunks per kv head
+constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
+constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, input ready, done,
+                                         // first unit available, rows finished
 
 struct StepOp {
-    const uint8_t *w;        // packed tiles (GEMV)
+    const uint8_t *w;        // row-block packed weights (GEMV), see k_pack_rows
     const float *xin;        // prologue input (PRO_NORM / PRO_PLAIN)
     const float *gain;       // RMSNorm gains
     const float *bias;       // QKV bias
@@ -181,26 +183,24 @@ struct StepOp {
     __half *kc, *vc;         // this layer's K/V cache (QKV epilogue, attention)
     int kind;                // StepOpKind
     int pro, epi;
-    int N, K, n_valid;
-    int b_full;              // B covers all K/16 k-tiles (else the CTA's tiles)
-    int max_contrib;         // CTAs that may share a strip (partial stride)
+    int N, K, n_valid;       // N even: rows come in pairs
+    int grid;                // CTAs owning rows: CTA c owns pairs [P c / grid, P (c + 1) / grid)
+    int pass_rows;           // rows per pass (even, <= kStepPassRows)
+    int chunk_w;             // inputs per unit (multiple of 256, or all of K)
     int dep, dep_n;          // wait until cnt[dep] >= dep_n * (epoch + 1); dep < 0: none
-    int sig;                 // cnt[sig] += finished strips (GEMV) / 1 per CTA (attention); < 0: none
+    int sig;                 // cnt[sig] += 1 per CTA (GEMV) / per kv head (attention); < 0: none
     int resid_embed;         // EPI_RESID: the residual base is the token's embedding row
-    int grid;                // CTAs sharing this GEMV: min(grid, tiles); CTAs beyond own nothing
-    int a_blocks;            // activation atoms this op needs per CTA (plan)
-    int max_items;           // strips a CTA may touch (plan)
-    int pad_[3];
+    int pad_[1];
 };
 static_assert(sizeof(StepOp) % 16 == 0, "the op table is copied to shared memory in 16-byte words");
 
 struct StepParams {
     const StepOp *ops;
     int n_ops;
-    int stages, a_blocks;    // shared-memory layout: ring stages of 32 KB, activation atoms of 1 KB
+    int stages;              // ring stages of 64 KB
+    int xmax;                // floats of the shared input vector (largest K, multiple of 4)
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
     int max_chunks;          // attention chunks per kv head at most (nkv * max_chunks <= grid)
-    int l2_ahead;            // weight tiles the producer warms L2 with ahead of its ring (0: off)
     int evict_first;         // ring copies carry an L2 evict-first hint
     float eps, scale;
     const float *rope;
@@ -208,8 +208,8 @@ struct StepParams {
     float *q;                // [nh * hd] fp32 (RoPE applied)
     float *attn_ml;          // [nh][max_chunks][2]  (running max, sum) per attention chunk
     float *attn_acc;         // [nh][max_chunks][hd] unnormalised outputs per chunk
-    float *partial;          // split strips [strips][max_contrib][128]
-    unsigned *strip_cnt;     // [strips]
+    float *attn_out;         // [nh * hd] merged attention output (the O projection's input)
+    unsigned *grp_cnt;       // [nkv] attention chunks finished per kv head (last one merges)
     float *part_val;         // LM head: per-CTA argmax
     int *part_idx;
     unsigned *lm_cnt;
@@ -219,16 +219,15 @@ struct StepParams {
     unsigned long long *trace;   // [n_ops][grid][kStepTraceWords] or null
 };
 
-// Weight tiles of the step kernel: 256 output rows x 64 inputs (32 KB), 128B-swizzled K-major.
-// N must be a multiple of 256 (zero-padded rows) and K of 64.
-void plan_step_gemv(StepOp &o, int num_sms, int min_tiles);   // fills grid, b_full, a_blocks, max_contrib, max_items
-int step_max_items();
-int step_max_a_blocks();
-cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
-                              cudaStream_t s);
+void plan_step_gemv(StepOp &o, int num_sms);     // fills grid, pass_rows, chunk_w from N, K
+bool step_gemv_supported(const StepOp &o);
+// Pack an fp16 N x K matrix (packed row r = source row row_of[r] of a / b as in
+// launch_pack_fragments, < 0 = zero) into the plan's row-block layout.
+cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
+                             const StepOp &plan, cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
-int step_stages_for(int a_blocks, int hd, int n_ops);
-size_t step_smem_bytes(int stages, int a_blocks, int hd, int n_ops);
+int step_stages_for(int xmax, int hd, int n_ops);
+size_t step_smem_bytes(int stages, int xmax, int hd, int n_ops);
 cudaError_t prepare_step(int hd, size_t smem);
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
 // resident at once (one CTA per SM), so the launch is cooperative.

@@ -1,33 +1,27 @@
 // Persistent decode step for sm_100a: one launch per token, one CTA per SM.
 //
 // The kernel walks the step's op table (per layer: QKV GEMV, attention, O GEMV, gate_up GEMV,
-// down GEMV; then the LM head). Weights are packed as tiles of 256 output rows x 64 inputs (32 KB,
-// 128B-swizzled K-major rows); every CTA owns the tile range [T*c/C, T*(c+1)/C) of every GEMV.
-// The weight tile is the B operand of tcgen05.mma (N = 256, K = 16, four per tile) and the
-// activation is the A operand (M = 128): one 1 KB swizzle atom per 64 inputs holds row 0 = fp16(x)
-// and row 1 = fp16(x - fp16(x)), and the descriptor's 8-row-group stride is 0, so every group of
-// the 128 rows re-reads that atom. D rows 0 and 1 (and their copies in every warp's TMEM quarter)
-// then hold W.hi and W.lo; y = their sum carries ~22 bits of the fp32 activation. Carrying 8 KB
-// of weights per MMA instruction is what lets the tensor core keep up with HBM (measured: 4 KB
-// per instruction as the A operand streams at about half the rate). Roles:
+// down GEMV; then the LM head). Batch-1 decode reads every weight once per token and is bound by
+// HBM bandwidth, so the GEMVs run on the CUDA cores from shared memory and the design is about
+// moving bytes and hiding latency:
 //
-//   warp 4 (producer)  streams ALL of the CTA's tiles of the step, op after op, through one ring
-//                      of 32 KB stages with 1-D bulk copies. It never waits for data, only for a
-//                      free stage, so weight traffic continues while the other warps wait for
-//                      activations (the ring then fills with the next ops' tiles).
-//   warp 5 (MMA)       per GEMV op: waits until the activation atoms of that op are built, then
-//                      issues four MMAs per tile into one of two 256-column TMEM accumulators
-//                      (double-buffered with the epilogue: one accumulator per strip item).
-//   warps 0-3          per GEMV op: wait on the op's dependency counter, build the activation
-//                      atoms (RMSNorm fused), hand them to the MMA warp, then read the
-//                      accumulators (warp w: columns 64w..64w+63) and run the epilogue on row pairs
-//                      (bias + RoPE + K/V write / residual add / SwiGLU / logits + argmax). A strip
-//                      split between CTAs is summed by its last contributor in fixed order.
-//                      Finished strips are counted into the op's counter (fence, then atomic add).
-//                      Attention: the epilogue warps of the first nkv * chunks CTAs each compute
-//                      one (kv head, context chunk) item and publish an unnormalised partial
-//                      (max, sum, acc); the O projection's prologue merges, per input it needs,
-//                      the partials of that head (log-sum-exp, fixed chunk order).
+//   rows       every CTA owns whole output rows of every GEMV (row pairs, so a RoPE pair or a
+//              gate/up pair stays in one warp): no split-K, no cross-CTA partial sums. Its rows
+//              are packed as units of (up to 64 rows) x (a chunk of the inputs), at most 64 KB each.
+//   warp 4     (producer) streams ALL of the CTA's units of the step, op after op, through a
+//              ring of 64 KB stages with 1-D bulk copies (one copy per unit). It never waits for
+//              data, only for a free stage, so weights stream while the other warps wait for
+//              activations.
+//   warps 0-3  per GEMV op: wait on the op's dependency counter, build the fp32 input vector in
+//              shared memory (RMSNorm fused), then multiply each unit: lane = 8 consecutive
+//              inputs, warp = every fourth row pair, fp16 x fp32 -> fp32 FMA chains; per row pass a
+//              butterfly reduction leaves each row sum in a lane pair, which runs the epilogue
+//              (bias + RoPE + K/V write / residual add / SwiGLU / logits + argmax). Then one
+//              release-add on the op's counter.
+//              Attention: the first nkv * chunks CTAs from the top each compute one (kv head,
+//              context chunk) item and publish an unnormalised partial (max, sum, acc); the last
+//              item of a kv head merges the head's chunks (log-sum-exp, fixed order) into the
+//              attention output the O projection reads.
 //
 // Counters are 64-bit and never reset: an op's consumers wait for units * (epoch + 1). All data
 // another CTA produced is read through L2 (ld.global.cg / cp.async.cg), never from L1. Every
@@ -38,35 +32,115 @@
 #include <cmath>
 
 #include "kernels.cuh"
-#include "tc.cuh"
 
 namespace sp {
 
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;            // warps 0-3: TMEM lanes 0-127
+constexpr int kEpiThreads = 128;            // warps 0-3: compute, epilogues, attention
 constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kTileRows = 256;              // output rows per weight tile (MMA N)
-constexpr int kTileK = 64;                  // inputs per weight tile (one 128-byte swizzled row)
-constexpr int kStepTileBytes = kTileRows * kTileK * 2;    // 32 KB per weight tile
-constexpr int kStageTiles = 2;              // tiles per ring stage: one 64 KB bulk copy (a bulk copy costs
-                                            // about the same time whatever its size, so big ones ingest faster)
-constexpr int kStageBytes = kStageTiles * kStepTileBytes;
-constexpr int kABlockBytes = 1024;          // activation atom (8 rows x 64 inputs) per k-block
-constexpr int kMaxItems = 16;               // strips a CTA may touch in one op
-constexpr int kTmemCols = 512;              // two accumulators of 256 fp32 columns
-constexpr int kMaxUnits = 4;                // activation chunks (8 inputs) per epilogue thread
+constexpr int kThreads = kEpiThreads + 32;
+constexpr int kStageBytes = 64 * 1024;      // one unit per stage (a bulk copy costs about the same
+                                            // time whatever its size, so big ones ingest faster)
+constexpr int kPassRows = kStepPassRows;    // rows per pass: 16 per warp
 constexpr int kGroup = 8;                   // q heads per kv head, padded (zero q beyond G)
+constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
 constexpr uint32_t kDepSpinLimit = 1u << 22;
+
+SP_DEVINL void ldmatrix_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                 : "r"(addr));
+}
+// D (16x8 fp32) += A (16x16 fp16, row-major) * B (16x8 fp16, column-major)
+SP_DEVINL void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// x[k .. k + 3] -> hi = fp16(x), lo = fp16(x - hi)
+SP_DEVINL void store_hilo4(__half *xh, __half *xl, int k, float4 v) {
+    const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v.x - f01.x, v.y - f01.y), l23 = __floats2half2_rn(v.z - f23.x, v.w - f23.y);
+    *reinterpret_cast<__half2 *>(xh + k) = h01;
+    *reinterpret_cast<__half2 *>(xh + k + 2) = h23;
+    *reinterpret_cast<__half2 *>(xl + k) = l01;
+    *reinterpret_cast<__half2 *>(xl + k + 2) = l23;
+}
+
+// One weight unit of a pass through the tensor cores. This warp takes k-steps warp, warp + 4, ...
+// in groups of U (= 4 / row tiles): accumulator slot sl = rt * U + u holds row tile rt's sum over
+// the group's u-th k-step, so four independent MMA chains run and four ldmatrix are in flight.
+template <int U>
+SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int rows_p, int nrt, int q0, const __half *xh,
+                        const __half *xl, int warp, int lane) {
+    const int lm = lane >> 3, lr = lane & 7;               // ldmatrix: matrix, row within it
+    for (int ks = warp; ks < nks; ks += 4 * U) {
+        uint32_t b[U][2];
+        uint32_t a[4][4];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            b[u][0] = 0u;
+            b[u][1] = 0u;
+            const int kk = ks + 4 * u;
+            if (kk < nks && lane < 8) {                     // B column 0 = hi, column 1 = lo
+                const __half *xv = lane < 4 ? xh : xl;
+                const int kr = q0 + 16 * kk + 2 * (lane & 3);
+                b[u][0] = *reinterpret_cast<const uint32_t *>(xv + kr);
+                b[u][1] = *reinterpret_cast<const uint32_t *>(xv + kr + 8);
+            }
+        }
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl) {
+            const int rt = sl / U, kk = ks + 4 * (sl % U);
+            if (rt < nrt && kk < nks) {
+                const int r = min(rt * 16 + ((lm & 1) << 3) + lr, rows_p - 1);
+                const int j = 2 * kk + (lm >> 1);           // 16-byte chunk of the row
+                const int pj = (j & ~7) | ((j & 7) ^ (r & 7));
+                ldmatrix_x4(unit + (uint32_t)(r * rs + pj * 16), a[sl][0], a[sl][1], a[sl][2], a[sl][3]);
+            }
+        }
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl) {
+            const int rt = sl / U, kk = ks + 4 * (sl % U);
+            if (rt < nrt && kk < nks) mma_16816(d[sl], a[sl][0], a[sl][1], a[sl][2], a[sl][3], b[sl % U][0], b[sl % U][1]);
+        }
+    }
+}
+
+// Row sums of a pass from the accumulator slots (lanes 4i: rows i and i + 8 of each tile; columns
+// 0 = hi, 1 = lo), tile rt's U slots added in slot order.
+template <int U>
+SP_DEVINL void rows_from_acc(const float (&d)[4][4], float *red_w, int nrt, int lane) {
+#pragma unroll
+    for (int rt = 0; rt < 4 / U; ++rt) {
+        if (rt < nrt) {
+            float ya = 0.f, yb = 0.f;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                ya += d[rt * U + u][0] + d[rt * U + u][1];
+                yb += d[rt * U + u][2] + d[rt * U + u][3];
+            }
+            red_w[rt * 16 + (lane >> 2)] = ya;
+            red_w[rt * 16 + (lane >> 2) + 8] = yb;
+        }
+    }
+}
+
+SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
+    if (ov > v || (ov == v && oi < i)) {
+        v = ov;
+        i = oi;
+    }
+}
 
 SP_DEVINL void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 SP_DEVINL void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
-SP_DEVINL void bready_sync() { asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads + 32) : "memory"); }
 
 SP_DEVINL unsigned long long ld_acquire_u64(const unsigned long long *p) {
     unsigned long long v;
@@ -208,30 +282,6 @@ SP_DEVINL void stamp(unsigned long long *tr, int k, int C, int c, int i) {
 
 
 
-SP_DEVINL void prefetch_line_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
-
-// While op k waits for its inputs, the epilogue warps warm L2 with this CTA's weight tiles that the
-// ring cannot hold yet: op k's tiles beyond the ring's depth, then the next GEMV op's, at most
-// `budget` tiles. Plain line prefetches (load/store path), so the copy engine keeps serving the ring;
-// the ring's later bulk copies of these tiles then hit L2.
-SP_DEVINL void warm_l2_for(const StepParams &p, const StepOp *ops, int k, int c, int tid, int skip, int budget) {
-    for (int kk = k; kk < p.n_ops && budget > 0; ++kk) {
-        const StepOp &op = ops[kk];
-        if (op.kind != OP_GEMV) continue;
-        if (c < op.grid) {
-            const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
-            long long g0 = T * c / op.grid;
-            const long long g1 = T * (c + 1) / op.grid;
-            if (kk == k) g0 += skip;
-            for (long long g = g0; g < g1 && budget > 0; ++g, --budget) {
-                const uint8_t *t = op.w + (size_t)g * kStepTileBytes;
-                for (int line = tid; line < kStepTileBytes / 128; line += kEpiThreads) prefetch_line_l2(t + (size_t)line * 128);
-            }
-        }
-        if (kk != k) break;              // this op and the next GEMV op only
-    }
-}
-
 // Per-step values every epilogue thread reads once (after the dependency on the previous step).
 struct StepState {
     unsigned long long epoch;
@@ -240,6 +290,23 @@ struct StepState {
 };
 
 // ---- attention item of one CTA: (kv head g, chunk ch) ------------------------------------------
+// Staging that does not depend on the step: zero q of the padded heads and copy the first
+// sub-chunk's K/V rows other than the current one. Issued before the QKV projection's wait.
+template <int HD>
+__device__ void attn_prestage(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
+                              int n_chunks, int rows_per, int ctx) {
+    using L = AttnRegion<HD>;
+    const int tid = threadIdx.x;
+    const int G = p.nh / p.nkv;
+    const int g = item / n_chunks, ch = item - g * n_chunks;
+    const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
+    float *qs = reinterpret_cast<float *>(am + L::qOff);
+    for (int i = G * HD + tid; i < kGroup * HD; i += kEpiThreads) qs[i] = 0.f;
+    const int s1 = min(j1, j0 + kStepAttnRows);
+    stage_rows<HD>(am, op.kc + (size_t)g * p.cap * HD, op.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot), tid);
+    cp_async_commit();
+}
+
 template <int HD>
 __device__ void attention_item(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
                                int n_chunks, int rows_per, int ctx, const Abort &ab) {
@@ -255,11 +322,8 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     float *sc = reinterpret_cast<float *>(am + L::sOff);
     const int slot = ss.slot;
 
-    for (int i = G * HD + tid; i < kGroup * HD; i += kEpiThreads) qs[i] = 0.f;
-    // rows other than the current one do not depend on this step: stage them before the wait
+    // rows other than the current one were staged by attn_prestage (they do not depend on this step)
     const int s1 = min(j1, j0 + kStepAttnRows);
-    stage_rows<HD>(am, kb, vb, j0, j0, min(s1, slot), tid);
-    cp_async_commit();
     if (tid == 0 && op.dep >= 0) wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
     epi_sync();
     if (slot >= j0 && slot < s1) stage_rows<HD>(am, kb, vb, j0, slot, slot + 1, tid);
@@ -402,34 +466,54 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     }
 }
 
-// ---- B operand: 8 inputs of one pair (k-tile t, half h) ------------------------------------------
-// Merged attention output dims [k0, k0 + 8) (all inside one head): log-sum-exp over the chunks in
-// fixed order. Two passes whose loads are independent of each other's arithmetic (max of the chunk
-// maxima, then the weighted sums), so each pass costs about one L2 round trip.
+
+// The last attention item of kv head g merges the head's chunks: out[h][d] for the G q heads of
+// the group = sum_c w_c acc_c[d] with w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), in chunk order.
+// `scratch` (shared, >= 2 * kGroup * max_chunks floats) holds the per-(head, chunk) weights.
 template <int HD>
-SP_DEVINL void merge_attention(const StepParams &p, int k0, int n_chunks, float (&v)[8]) {
-    const int hq = k0 / HD, d0 = k0 - hq * HD;
-    const float *ml = p.attn_ml + (size_t)hq * p.max_chunks * 2;
-    const float *ac = p.attn_acc + (size_t)hq * p.max_chunks * HD + d0;
-    float M = -INFINITY;
-#pragma unroll 16
-    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, __ldcg(ml + 2 * c));
-    float Ls = 0.f;
-    float A[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) A[i] = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < n_chunks; ++c) {
-        const float2 mlc = __ldcg(reinterpret_cast<const float2 *>(ml + 2 * c));
-        const float4 a0 = ldcg4(ac + (size_t)c * HD), a1 = ldcg4(ac + (size_t)c * HD + 4);
-        const float f = mlc.x == -INFINITY ? 0.f : expf(mlc.x - M);
-        Ls = fmaf(mlc.y, f, Ls);
-        A[0] = fmaf(a0.x, f, A[0]); A[1] = fmaf(a0.y, f, A[1]); A[2] = fmaf(a0.z, f, A[2]); A[3] = fmaf(a0.w, f, A[3]);
-        A[4] = fmaf(a1.x, f, A[4]); A[5] = fmaf(a1.y, f, A[5]); A[6] = fmaf(a1.z, f, A[6]); A[7] = fmaf(a1.w, f, A[7]);
+__device__ void merge_group(const StepParams &p, int g, int n_chunks, float *scratch) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = p.nh / p.nkv;
+    float *wts = scratch;                                  // [G][n_chunks]
+    for (int i = tid; i < G * n_chunks; i += kEpiThreads) {
+        const int hh = i / n_chunks, c = i - hh * n_chunks;
+        wts[i] = __ldcg(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2);
     }
-    const float inv = 1.f / Ls;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = A[i] * inv;
+    epi_sync();
+    for (int hh = warp; hh < G; hh += 4) {
+        float M = -INFINITY;
+        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, wts[hh * n_chunks + c]);
+        M = warp_max(M);
+        float L = 0.f;
+        for (int c = lane; c < n_chunks; c += 32) {
+            const float m = wts[hh * n_chunks + c];
+            const float l = __ldcg(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2 + 1);
+            L = fmaf(l, m == -INFINITY ? 0.f : expf(m - M), L);
+        }
+        L = warp_sum(L);
+        __syncwarp();
+        for (int c = lane; c < n_chunks; c += 32) {
+            const float m = wts[hh * n_chunks + c];
+            wts[hh * n_chunks + c] = m == -INFINITY ? 0.f : expf(m - M) / L;
+        }
+    }
+    epi_sync();
+    // four outputs per thread and step, up to 16 chunks' loads in flight
+    for (int e4 = tid; e4 < G * HD / 4; e4 += kEpiThreads) {
+        const int e = 4 * e4, hh = e / HD, d = e - hh * HD, h = g * G + hh;
+        const float *ac = p.attn_acc + (size_t)h * p.max_chunks * HD + d;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 16
+        for (int c = 0; c < n_chunks; ++c) {
+            const float w = wts[hh * n_chunks + c];
+            const float4 a = ldcg4(ac + (size_t)c * HD);
+            A.x = fmaf(w, a.x, A.x);
+            A.y = fmaf(w, a.y, A.y);
+            A.z = fmaf(w, a.z, A.z);
+            A.w = fmaf(w, a.w, A.w);
+        }
+        *reinterpret_cast<float4 *>(p.attn_out + (size_t)h * HD + d) = A;
+    }
 }
 
 }  // namespace
@@ -437,156 +521,76 @@ SP_DEVINL void merge_attention(const StepParams &p, int k0, int n_chunks, float 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint32_t s_tmem;
     __shared__ float s_val[4];
     __shared__ int s_idx[4];
     __shared__ int s_flag;
     __shared__ int s_abort;
-    __shared__ int s_issued, s_consumed;      // stages the producer issued / the MMA warp consumed
-    __shared__ __align__(8) uint64_t s_drain; // MMA completion before TMEM is released
-    __shared__ __align__(8) uint64_t accf[2], tfree[2];   // accumulator full (MMA -> epilogue) / free
-    __shared__ int it_strip[2][kMaxItems], it_a[2][kMaxItems], it_b[2][kMaxItems], it_boff[2][kMaxItems];
-    __shared__ int s_nitems[2];
-    __shared__ __align__(16) float ystage[4][2][64];    // per warp: hi and lo rows of its 64 columns
+    __shared__ int s_issued, s_consumed;      // stages the producer issued / the compute warps consumed
+    __shared__ float red[4][kPassRows];       // per-warp row partials of a pass (k-steps split over warps)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, c = blockIdx.x;
     const int S = p.stages;
     uint8_t *ring = smem;
-    uint8_t *abuf = smem + (size_t)S * kStageBytes;                         // activation atoms, 1 KB per 64 inputs
-    uint8_t *am = abuf + (size_t)p.a_blocks * kABlockBytes;
-    StepOp *ops = reinterpret_cast<StepOp *>(am + AttnRegion<HD>::bytes);   // the op table, copied once
+    // input vector as two fp16 vectors: hi = fp16(x), lo = fp16(x - hi) (~22 bits of x)
+    __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * kStageBytes);
+    __half *xl = xh + p.xmax;
+    uint8_t *am = reinterpret_cast<uint8_t *>(xl + p.xmax);                     // attention region
+    StepOp *ops = reinterpret_cast<StepOp *>(am + AttnRegion<HD>::bytes);        // the op table
     uint64_t *full = reinterpret_cast<uint64_t *>(ops + p.n_ops);
     uint64_t *empty = full + S;
     const Abort ab{&s_abort, p.st};
-
-    // Every role reads op descriptors on its critical path: keep them in shared memory.
-    for (int i = tid; i < p.n_ops * (int)(sizeof(StepOp) / 16); i += kThreads)
-        reinterpret_cast<uint4 *>(ops)[i] = __ldg(reinterpret_cast<const uint4 *>(p.ops) + i);
 
     if (tid == 0) {
         s_abort = 0;
         s_issued = 0;
         s_consumed = 0;
-        mbar_init(&s_drain, 1);
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&accf[i], 1);
-            mbar_init(&tfree[i], 4);        // one arrival per epilogue warp
-        }
         fence_mbar_init();
     }
-    // rows 2-7 of every activation atom stay zero; rows 0/1 are rewritten per op
-    for (int i = tid; i < p.a_blocks * kABlockBytes / 16; i += kThreads)
-        reinterpret_cast<uint4 *>(abuf)[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    tc_fence_before();
+    // every role reads op descriptors on its critical path: keep them in shared memory
+    for (int i = tid; i < p.n_ops * (int)(sizeof(StepOp) / 16); i += kThreads)
+        reinterpret_cast<uint4 *>(ops)[i] = __ldg(reinterpret_cast<const uint4 *>(p.ops) + i);
     __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = s_tmem;
 
     if (warp == kProducerWarp) {
-        // ---- producer: every tile of the step, in op order; waits only for free stages ----------
+        // ---- producer: every unit of the step, in op order; waits only for free stages ----------
         if (lane == 0) {
             int s = 0, round = 0, issued = 0;
             const uint64_t pol = policy_evict_first();
             for (int k = 0; k < p.n_ops && !ab.on(); ++k) {
                 const StepOp &op = ops[k];
-                if (op.kind != OP_GEMV) continue;
-                const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
-                const int Cg = op.grid;
-                if (c >= Cg) continue;
-                const long long g0 = T * c / Cg, g1 = T * (c + 1) / Cg;
-                for (long long g = g0; g < g1; g += kStageTiles) {
-                    if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
-                    const int n = (int)(g1 - g < kStageTiles ? g1 - g : kStageTiles);
-                    const uint32_t nb = (uint32_t)(n * kStepTileBytes);
-                    mbar_arrive_expect_tx(&full[s], nb);
-                    if (p.evict_first)
-                        bulk_g2s_hint(ring + (size_t)s * kStageBytes, op.w + (size_t)g * kStepTileBytes, nb, &full[s], pol);
-                    else
-                        bulk_g2s(ring + (size_t)s * kStageBytes, op.w + (size_t)g * kStepTileBytes, nb, &full[s]);
-                    ++issued;
-                    if (++s == S) {
-                        s = 0;
-                        ++round;
+                if (op.kind != OP_GEMV || c >= op.grid) continue;
+                const int P = op.N / 2;
+                const int R0 = 2 * (int)((long long)P * c / op.grid);
+                const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
+                const uint8_t *src = op.w + (size_t)R0 * op.K * 2;
+                for (int p0 = 0; p0 < R && !ab.on(); p0 += op.pass_rows) {
+                    const int rows = min(op.pass_rows, R - p0);
+                    for (int q0 = 0; q0 < op.K; q0 += op.chunk_w) {
+                        const uint32_t nb = (uint32_t)(rows * min(op.chunk_w, op.K - q0) * 2);
+                        if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
+                        mbar_arrive_expect_tx(&full[s], nb);
+                        if (p.evict_first)
+                            bulk_g2s_hint(ring + (size_t)s * kStageBytes, src, nb, &full[s], pol);
+                        else
+                            bulk_g2s(ring + (size_t)s * kStageBytes, src, nb, &full[s]);
+                        src += nb;
+                        ++issued;
+                        if (++s == S) {
+                            s = 0;
+                            ++round;
+                        }
                     }
                 }
             }
             s_issued = issued;
         }
-    } else if (warp == kMmaWarp) {
-        // ---- MMA issuer: per tile 4 x (M=128, N=256, K=16); accumulators double-buffered ----------
-        const uint32_t ring_addr = smem_u32(ring), a_addr0 = smem_u32(abuf);
-        int s = 0, round = 0, gi = 0, consumed = 0;
-        uint32_t gj = 0;                      // items of the step so far (accumulator = gj & 1)
-        for (int k = 0; k < p.n_ops; ++k) {
-            const StepOp &op = ops[k];
-            if (op.kind != OP_GEMV) continue;
-            const int buf = gi & 1;
-            ++gi;
-            bready_sync();
-            tc_fence_after();
-            if (lane == 0 && p.trace) p.trace[((size_t)k * C + c) * kStepTraceWords + 6] = globaltimer();
-            if (lane == 0 && !ab.on()) {
-                const int nitems = s_nitems[buf];
-                const long long T = (long long)(op.N / kTileRows) * (op.K / kTileK);
-                const int Cg = op.grid;
-                const int ntiles = c < Cg ? (int)(T * (c + 1) / Cg - T * c / Cg) : 0;
-                int item = 0, t = it_a[buf][0];
-                uint32_t a_blk = (uint32_t)it_boff[buf][0];
-                bool ok = ntiles == 0 || gj < 2 || wait_bar(&tfree[gj & 1], ((gj >> 1) - 1) & 1u, ab);
-                for (int i = 0; i < ntiles && ok; i += kStageTiles) {
-                    if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
-                    if (i == 0 && p.trace) p.trace[((size_t)k * C + c) * kStepTraceWords + 7] = globaltimer();
-                    ++consumed;
-                    tc_fence_after();
-                    const int n = ntiles - i < kStageTiles ? ntiles - i : kStageTiles;
-                    for (int q = 0; q < n && ok; ++q) {
-                        const uint32_t d = tmem + (gj & 1u) * 256u;
-                        const uint32_t b_addr = ring_addr + (uint32_t)(s * kStageBytes + q * kStepTileBytes);
-                        const uint32_t a_addr = a_addr0 + a_blk * (uint32_t)kABlockBytes;
-                        const bool first = t == it_a[buf][item];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            mma_f16_id(d, smem_desc_sw128(a_addr + 32u * j, 0u), smem_desc_sw128(b_addr + 32u * j, 1024u),
-                                       kIdescM128N256, (first && j == 0) ? 0u : 1u);
-                        ++t;
-                        ++a_blk;
-                        if (t == it_b[buf][item]) {
-                            mma_commit(&accf[gj & 1u]);
-                            ++gj;
-                            if (item + 1 < nitems) {
-                                ++item;
-                                t = it_a[buf][item];
-                                a_blk = (uint32_t)it_boff[buf][item];
-                                if (gj >= 2 && !wait_bar(&tfree[gj & 1u], ((gj >> 1) - 1) & 1u, ab)) ok = false;
-                            }
-                        }
-                    }
-                    mma_commit(&empty[s]);
-                    if (++s == S) {
-                        s = 0;
-                        ++round;
-                    }
-                }
-            }
-            __syncwarp();
-        }
-        if (lane == 0) {
-            s_consumed = consumed;
-            mma_commit(&s_drain);    // arrives once every MMA this thread issued has completed
-        }
-        __syncwarp();
     } else {
-        // ---- warps 0-3: dependencies, prologues, epilogues, attention -----------------------------
+        // ---- warps 0-3: dependencies, prologues, GEMV compute, epilogues, attention ---------------
         griddep_wait();
         griddep_launch_dependents();
         DevState *st = p.st;
@@ -610,171 +614,108 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         const int n_chunks = attn_chunks(ctx, p.max_chunks);
         const int rows_per = (ctx + n_chunks - 1) / n_chunks;
         const int half_hd = HD / 2;
-        uint32_t gj = 0;                // items of the step so far (accumulator = gj & 1)
-        int gi = 0;
+        int s = 0, round = 0, consumed = 0;       // ring position of the compute warps
 
         for (int k = 0; k < p.n_ops; ++k) {
             const StepOp &op = ops[k];
             stamp(p.trace, k, C, c, 0);
             if (op.kind == OP_ATTN) {
-                // items on the last CTAs: narrow GEMVs use the first ones, so these arrive early and
-                // stage their K/V rows while the QKV projection is still running
+                // items on the last CTAs (the first ones own the first rows of every GEMV), so
+                // they stage their K/V rows early
                 const int items = p.nkv * n_chunks, item = C - 1 - c;
-                if (item < items && !ab.on()) attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab);
-                epi_sync();
+                if (item < items && !ab.on()) {
+                    attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab);
+                    const int g = item / n_chunks;
+                    epi_sync();
+                    if (tid == 0) s_flag = atom_add_acq_rel(p.grp_cnt + g, 1u) == (unsigned)(n_chunks - 1);
+                    epi_sync();
+                    if (s_flag) {      // the head's last chunk: merge all of them
+                        merge_group<HD>(p, g, n_chunks, reinterpret_cast<float *>(am));
+                        epi_sync();
+                        if (tid == 0) {
+                            p.grp_cnt[g] = 0u;
+                            if (op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
+                        }
+                    }
+                }
                 stamp(p.trace, k, C, c, 3);
-                if (tid == 0 && op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
                 continue;
             }
-            const int buf = gi & 1;
-            ++gi;
-            const int K = op.K, KB = K / kTileK;
-            const long long T = (long long)(op.N / kTileRows) * KB;
-            const int Cg = op.grid;          // CTAs c >= Cg own no tile of this GEMV
-            const long long g0 = c < Cg ? T * c / Cg : T, g1 = c < Cg ? T * (c + 1) / Cg : T;
-            const int ntiles = (int)(g1 - g0);
-            if (tid == 0) {
-                // items: the CTA's tiles split at strip boundaries (at most kMaxItems, host-checked)
-                int n = 0, boff = 0;
-                long long gg = g0;
-                while (gg < g1 && n < kMaxItems) {
-                    const int s = (int)(gg / KB), a = (int)(gg % KB);
-                    const long long rest = (long long)a + (g1 - gg);
-                    const int b = rest < KB ? (int)rest : KB;
-                    it_strip[buf][n] = s;
-                    it_a[buf][n] = a;
-                    it_b[buf][n] = b;
-                    it_boff[buf][n] = op.b_full ? a : boff;
-                    boff += b - a;
-                    gg += b - a;
-                    ++n;
-                }
-                s_nitems[buf] = n;
+            if (op.epi == EPI_QKV && k + 1 < p.n_ops && ops[k + 1].kind == OP_ATTN) {
+                // this CTA's attention item of the layer: stage its immutable K/V rows now
+                const int item = C - 1 - c;
+                if (item < p.nkv * n_chunks)
+                    attn_prestage<HD>(p, ops[k + 1], ss, am, item, n_chunks, rows_per, ctx);
             }
-            if (p.l2_ahead > 0 && op.dep >= 0) warm_l2_for(p, ops, k, c, tid, S * kStageTiles, p.l2_ahead);
+            if (c >= op.grid) continue;          // no rows of this GEMV
+            const int K = op.K;
             if (tid == 0 && op.dep >= 0 && !ab.on())
                 wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
             epi_sync();
             stamp(p.trace, k, C, c, 1);
-            const int nitems = s_nitems[buf];
 
-            // ---- prologue: activation atoms (row 0 fp16 hi, row 1 fp16 lo) from one L2 round trip ---
-            const int nb = op.b_full ? KB : ntiles;
-            const int nunits = nb * 8;          // 8 inputs (one 16-byte chunk of a row) per unit
-            float v[kMaxUnits][8], gg8[kMaxUnits][8];
-            float sq = 0.f;
+            // ---- prologue: the fp32 input vector in shared memory (RMSNorm fused) -------------------
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
-            const __half *erow = p.embed + (size_t)ss.token * K;
-#pragma unroll
-            for (int q = 0; q < kMaxUnits; ++q) {
-                const int u = tid + q * kEpiThreads;
-                if (u >= nunits) continue;
-                const int bt = u >> 3, ch = u & 7;
-                int t = bt;
-                if (!op.b_full) {
-                    int j = 0;
-                    while (j + 1 < nitems && bt >= it_boff[buf][j + 1]) ++j;
-                    t = it_a[buf][j] + (bt - it_boff[buf][j]);
-                }
-                const int k0 = kTileK * t + 8 * ch;
-                if (op.pro == PRO_EMBED_NORM) {
-                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(erow + k0));
-                    const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 t2 = __half22float2(h2[j]);
-                        v[q][2 * j] = t2.x;
-                        v[q][2 * j + 1] = t2.y;
-                    }
-                } else if (op.pro == PRO_ATTN) {
-                    merge_attention<HD>(p, k0, n_chunks, v[q]);
-                } else {
-                    const float4 x0 = ldcg4(op.xin + k0), x1 = ldcg4(op.xin + k0 + 4);
-                    v[q][0] = x0.x; v[q][1] = x0.y; v[q][2] = x0.z; v[q][3] = x0.w;
-                    v[q][4] = x1.x; v[q][5] = x1.y; v[q][6] = x1.z; v[q][7] = x1.w;
-                }
-                if (norm) {
-                    const float4 ga = __ldg(reinterpret_cast<const float4 *>(op.gain + k0));
-                    const float4 gb = __ldg(reinterpret_cast<const float4 *>(op.gain + k0 + 4));
-                    gg8[q][0] = ga.x; gg8[q][1] = ga.y; gg8[q][2] = ga.z; gg8[q][3] = ga.w;
-                    gg8[q][4] = gb.x; gg8[q][5] = gb.y; gg8[q][6] = gb.z; gg8[q][7] = gb.w;
-                    if (op.b_full) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) sq = fmaf(v[q][j], v[q][j], sq);
-                    }
-                }
-            }
-            float inv = 1.f;
             if (norm) {
-                if (!op.b_full) {
-                    // the sum of squares needs the whole vector
-                    if (op.pro == PRO_EMBED_NORM) {
-                        for (int vv = tid; vv < K / 8; vv += kEpiThreads) {
-                            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(erow) + vv);
-                            const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                // K <= kNormRegs * 4 * kEpiThreads (host-checked): each thread holds its float4s in registers
+                float4 v[kNormRegs], gn[kNormRegs];
+                float sq = 0.f;
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float2 t2 = __half22float2(h2[j]);
-                                sq = fmaf(t2.x, t2.x, sq);
-                                sq = fmaf(t2.y, t2.y, sq);
-                            }
+                for (int q = 0; q < kNormRegs; ++q) {
+                    const int i = tid + q * kEpiThreads;
+                    if (4 * i < K) {
+                        if (op.pro == PRO_EMBED_NORM) {
+                            const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(p.embed + (size_t)ss.token * K) + i);
+                            const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                            const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                            v[q] = make_float4(a.x, a.y, b.x, b.y);
+                        } else {
+                            v[q] = ldcg4(op.xin + 4 * i);
                         }
-                    } else {
-                        for (int vv = tid; vv < K / 4; vv += kEpiThreads) {
-                            const float4 f = ldcg4(op.xin + 4 * vv);
-                            sq = fmaf(f.x, f.x, sq);
-                            sq = fmaf(f.y, f.y, sq);
-                            sq = fmaf(f.z, f.z, sq);
-                            sq = fmaf(f.w, f.w, sq);
-                        }
+                        gn[q] = __ldg(reinterpret_cast<const float4 *>(op.gain) + i);
+                        sq = fmaf(v[q].x, v[q].x, sq);
+                        sq = fmaf(v[q].y, v[q].y, sq);
+                        sq = fmaf(v[q].z, v[q].z, sq);
+                        sq = fmaf(v[q].w, v[q].w, sq);
                     }
                 }
                 sq = warp_sum(sq);
                 if (lane == 0) s_val[warp] = sq;
                 epi_sync();
-                inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
-            }
+                const float inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
 #pragma unroll
-            for (int q = 0; q < kMaxUnits; ++q) {
-                const int u = tid + q * kEpiThreads;
-                if (u >= nunits) continue;
-                const int bt = u >> 3, ch = u & 7;
-                if (norm) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[q][j] = (v[q][j] * inv) * gg8[q][j];
+                for (int q = 0; q < kNormRegs; ++q) {
+                    const int i = tid + q * kEpiThreads;
+                    if (4 * i < K)
+                        store_hilo4(xh, xl, 4 * i,
+                                    make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
+                                                (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w));
                 }
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const __half h0 = __float2half_rn(v[q][2 * j]), h1 = __float2half_rn(v[q][2 * j + 1]);
-                    const __half l0 = __float2half_rn(v[q][2 * j] - __half2float(h0));
-                    const __half l1 = __float2half_rn(v[q][2 * j + 1] - __half2float(h1));
-                    hi[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-                    lo[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-                }
-                // row 0 (hi) keeps chunk ch at position ch, row 1 (lo) at position ch ^ 1
-                uint8_t *atom = abuf + (size_t)bt * kABlockBytes;
-                *reinterpret_cast<uint4 *>(atom + ch * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(atom + 128 + (ch ^ 1) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            } else {
+                const float *src = op.pro == PRO_ATTN ? p.attn_out : op.xin;
+                for (int i = tid; i < K / 4; i += kEpiThreads) store_hilo4(xh, xl, 4 * i, ldcg4(src + 4 * i));
             }
-            fence_proxy_async_smem();
-            bready_sync();
+            epi_sync();
             stamp(p.trace, k, C, c, 2);
 
-            // ---- epilogue: warp w takes columns [64w, 64w + 64) of the item's 256 output rows ---------
+            // ---- rows: passes of up to kPassRows rows, each over all inputs in chunks ---------------
+            const int P = op.N / 2;
+            const int R0 = 2 * (int)((long long)P * c / op.grid);
+            const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
             float *lg = nullptr;
             if (op.epi == EPI_LMHEAD && st->logits != nullptr && st->step >= st->logits_from)
                 lg = st->logits + st->logits_stride * (long long)st->step;
             float bv = -INFINITY;
             int bi = INT_MAX;
-            int n_final = 0;
-            const int col = 64 * warp + 2 * lane;   // this thread's row pair (col, col + 1) of a strip
-            for (int j = 0; j < nitems; ++j) {
-                // epilogue operands that do not depend on the accumulator: load them before waiting
-                const int strip = it_strip[buf][j];
-                const int row = strip * kTileRows + col;
+            for (int p0 = 0; p0 < R && !ab.on(); p0 += op.pass_rows) {
+                const int rows_p = min(op.pass_rows, R - p0), npairs = rows_p / 2;
+                const int nrt = (rows_p + 15) >> 4;                 // 16-row tiles of the pass (<= 4)
+                // epilogue operands that do not depend on the products: thread t < npairs finishes
+                // pair t (rows 2t, 2t + 1 of the pass)
+                const int row = R0 + p0 + 2 * tid;                  // packed row (row, row + 1)
+                const bool mine = tid < npairs && row < op.n_valid;
                 float pre0 = 0.f, pre1 = 0.f, pcs = 1.f, psn = 0.f;
-                if (row < op.n_valid) {
+                if (mine) {
                     if (op.epi == EPI_RESID) {
                         if (op.resid_embed) {
                             const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
@@ -786,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                             pre1 = b2.y;
                         }
                     } else if (op.epi == EPI_QKV) {
-                        const int P = row / 2, hh = P / half_hd, dd = P - hh * half_hd;
+                        const int P2 = row / 2, hh = P2 / half_hd, dd = P2 - hh * half_hd;
                         pre0 = __ldg(op.bias + hh * HD + dd);
                         pre1 = __ldg(op.bias + hh * HD + dd + half_hd);
                         if (hh < p.nh + p.nkv) {
@@ -796,70 +737,51 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         }
                     }
                 }
-                const uint32_t tb = gj & 1u;
-                const bool ok = !ab.on() && wait_bar(&accf[tb], (gj >> 1) & 1u, ab);
-                ++gj;
-                if (!ok) continue;
-                if (j == 0) stamp(p.trace, k, C, c, 4);
-                if (j == nitems - 1) stamp(p.trace, k, C, c, 5);
-                tc_fence_after();
-                {
-                    uint32_t r0[32], r1[32];
-                    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + tb * 256u + (uint32_t)(warp * 64);
-                    tmem_ld32_nowait(taddr, r0);
-                    tmem_ld32_nowait(taddr + 32u, r1);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tfree[tb]);     // this warp's columns are read
-                    if (lane < 2) {
-                        float4 *dst = reinterpret_cast<float4 *>(&ystage[warp][lane][0]);
+                // tensor-core products: A = 16 weight rows x 16 inputs (ldmatrix from the swizzled
+                // unit), B column 0 = hi, column 1 = lo of the inputs, fp32 accumulators; warp w
+                // takes k-steps w, w + 4, ... of every row tile
+                float d[4][4];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            dst[i] = make_float4(__uint_as_float(r0[4 * i]), __uint_as_float(r0[4 * i + 1]),
-                                                 __uint_as_float(r0[4 * i + 2]), __uint_as_float(r0[4 * i + 3]));
+                for (int i = 0; i < 4; ++i)
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            dst[8 + i] = make_float4(__uint_as_float(r1[4 * i]), __uint_as_float(r1[4 * i + 1]),
-                                                     __uint_as_float(r1[4 * i + 2]), __uint_as_float(r1[4 * i + 3]));
+                    for (int j = 0; j < 4; ++j) d[i][j] = 0.f;
+                const int lm = lane >> 3, lr = lane & 7;            // ldmatrix: matrix, row within it
+                for (int q0 = 0; q0 < K; q0 += op.chunk_w) {
+                    const int wq = min(op.chunk_w, K - q0);
+                    if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
+                    if (p0 == 0 && q0 == 0) stamp(p.trace, k, C, c, 4);
+                    const uint32_t unit = smem_u32(ring + (size_t)s * kStageBytes);
+                    const int rs = wq * 2;                          // row stride (bytes) inside the unit
+                    const int nks = wq >> 4;
+                    if (nrt == 1)
+                        unit_mma<4>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
+                    else if (nrt == 2)
+                        unit_mma<2>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
+                    else
+                        unit_mma<1>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
+                    epi_sync();                                     // every warp is done with the unit
+                    if (tid == 0) mbar_arrive(&empty[s]);
+                    ++consumed;
+                    if (++s == S) {
+                        s = 0;
+                        ++round;
                     }
                 }
-                __syncwarp();
-                const float2 hv = *reinterpret_cast<const float2 *>(&ystage[warp][0][2 * lane]);
-                const float2 lv = *reinterpret_cast<const float2 *>(&ystage[warp][1][2 * lane]);
-                __syncwarp();
-                float y0 = hv.x + lv.x, y1 = hv.y + lv.y;
-                if (it_a[buf][j] != 0 || it_b[buf][j] != KB) {
-                    // strip shared with other CTAs: post this part; the last contributor sums all
-                    const long long first = (long long)strip * KB;
-                    const int cf = tc_cta_of(first, T, Cg), cl = tc_cta_of(first + KB - 1, T, Cg);
-                    float *slotp = p.partial + ((size_t)strip * op.max_contrib + (c - cf)) * kTileRows;
-                    *reinterpret_cast<float2 *>(slotp + col) = make_float2(y0, y1);
-                    epi_sync();
-                    if (tid == 0) s_flag = atom_add_acq_rel(p.strip_cnt + strip, 1u) == (unsigned)(cl - cf);
-                    epi_sync();
-                    if (!s_flag) continue;
-                    const float *all = p.partial + (size_t)strip * op.max_contrib * kTileRows + col;
-                    y0 = 0.f;
-                    y1 = 0.f;
-                    const int ncon = cl - cf + 1;
-                    for (int k2 = 0; k2 < ncon; k2 += 16) {
-                        // sixteen contributors' loads in flight, summed in contributor order
-                        float2 pv[16];
-#pragma unroll
-                        for (int u = 0; u < 16; ++u)
-                            pv[u] = k2 + u < ncon ? __ldcg(reinterpret_cast<const float2 *>(all + (size_t)(k2 + u) * kTileRows))
-                                                  : make_float2(0.f, 0.f);
-#pragma unroll
-                        for (int u = 0; u < 16; ++u) {
-                            y0 += pv[u].x;
-                            y1 += pv[u].y;
-                        }
-                    }
-                    if (tid == 0) p.strip_cnt[strip] = 0u;
+                // row sums: lanes 4i hold rows i and i + 8 of each tile (columns 0 = hi, 1 = lo);
+                // tile rt's U accumulator slots are summed in slot order
+                if ((lane & 3) == 0) {
+                    if (nrt == 1)
+                        rows_from_acc<4>(d, red[warp], nrt, lane);
+                    else if (nrt == 2)
+                        rows_from_acc<2>(d, red[warp], nrt, lane);
+                    else
+                        rows_from_acc<1>(d, red[warp], nrt, lane);
                 }
-                ++n_final;
-                if (row >= op.n_valid) continue;
+                epi_sync();
+                if (!mine) continue;
+                const int r2 = 2 * tid;
+                const float y0 = ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
+                const float y1 = ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
                 if (op.epi == EPI_RESID) {
                     *reinterpret_cast<float2 *>(op.out + row) = make_float2(pre0 + y0, pre1 + y1);
                 } else if (op.epi == EPI_LMHEAD) {
@@ -878,14 +800,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 } else if (op.epi == EPI_SWIGLU) {
                     op.out[row / 2] = (y0 / (1.0f + expf(-y0))) * y1;
                 } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
-                    const int P = row / 2;
-                    const int hh = P / half_hd, dd = P - hh * half_hd;
+                    const int P2 = row / 2;
+                    const int hh = P2 / half_hd, dd = P2 - hh * half_hd;
                     const int lo = hh * HD + dd, hi = lo + half_hd;
                     const float a0 = y0 + pre0, a1 = y1 + pre1;
                     if (hh < p.nh + p.nkv) {
-                        const float cs = pcs, sn = psn;
-                        const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
-                        const float o1 = __fadd_rn(__fmul_rn(a1, cs), __fmul_rn(a0, sn));
+                        const float o0 = __fadd_rn(__fmul_rn(a0, pcs), -__fmul_rn(a1, psn));
+                        const float o1 = __fadd_rn(__fmul_rn(a1, pcs), __fmul_rn(a0, psn));
                         if (hh < p.nh) {
                             op.out[lo] = o0;
                             op.out[hi] = o1;
@@ -901,13 +822,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     }
                 }
             }
+            epi_sync();                                             // `red` is reused by the next op
+            stamp(p.trace, k, C, c, 5);
 
             if (op.epi == EPI_LMHEAD) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    tc_argmax_merge(bv, bi, ov, oi);
+                    argmax_merge(bv, bi, ov, oi);
                 }
                 if (lane == 0) {
                     s_val[warp] = bv;
@@ -917,22 +840,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 if (tid == 0) {
                     float vb = s_val[0];
                     int ib = s_idx[0];
-                    for (int w = 1; w < 4; ++w) tc_argmax_merge(vb, ib, s_val[w], s_idx[w]);
+                    for (int w = 1; w < 4; ++w) argmax_merge(vb, ib, s_val[w], s_idx[w]);
                     p.part_val[c] = vb;
                     p.part_idx[c] = ib;
-                    s_flag = atom_add_acq_rel(p.lm_cnt, 1u) == (unsigned)C - 1u;
+                    s_flag = atom_add_acq_rel(p.lm_cnt, 1u) == (unsigned)op.grid - 1u;
                 }
                 epi_sync();
                 if (s_flag) {
                     float vb = -INFINITY;
                     int ib = INT_MAX;
-                    for (int j = tid; j < C; j += kEpiThreads)
-                        tc_argmax_merge(vb, ib, __ldcg(p.part_val + j), __ldcg(p.part_idx + j));
+                    for (int j = tid; j < op.grid; j += kEpiThreads)
+                        argmax_merge(vb, ib, __ldcg(p.part_val + j), __ldcg(p.part_idx + j));
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
                         const float ov = __shfl_xor_sync(0xffffffffu, vb, o);
                         const int oi = __shfl_xor_sync(0xffffffffu, ib, o);
-                        tc_argmax_merge(vb, ib, ov, oi);
+                        argmax_merge(vb, ib, ov, oi);
                     }
                     epi_sync();
                     if (lane == 0) {
@@ -941,7 +864,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     }
                     epi_sync();
                     if (tid == 0) {
-                        for (int w = 1; w < 4; ++w) tc_argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
+                        for (int w = 1; w < 4; ++w) argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
                         int tok = s_idx[0];
                         if (tok < 0 || tok >= op.n_valid) {
                             atomicCAS(&st->err, 0, kErrBadToken);
@@ -966,91 +889,100 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 }
             } else if (op.sig >= 0) {
                 epi_sync();
-                if (tid == 0 && n_final > 0) red_add_release(p.cnt + op.sig, (unsigned long long)n_final);
+                if (tid == 0) red_add_release(p.cnt + op.sig, 1ull);
             }
             stamp(p.trace, k, C, c, 3);
         }
+        if (tid == 0) s_consumed = consumed;
     }
 
-    // producer and MMA warps are done; all TMEM reads are fenced: release TMEM
     __syncthreads();
     if (warp == kProducerWarp && lane == 0) {
         // after an abort, stages may still be in flight: let their copies land before exiting
         for (int i = s_consumed; i < s_issued; ++i) mbar_wait_bounded(&full[i % S], (uint32_t)(i / S) & 1u);
     }
-    if (warp == kMmaWarp) {
-        if (lane == 0) mbar_wait_bounded(&s_drain, 0u);
-        __syncwarp();
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
-    }
 }
 
-// Pack an fp16 N x K matrix into 256 x 64 tiles of 128B-swizzled K-major rows: tile (strip s, k-block
-// t) at (s * K/64 + t) * 32 KB; inside it row r (0..255) at r * 128 B with input chunk c (8 inputs)
-// at chunk position c ^ (r & 7). Packed row `row` is source row row_of[row] of `a` (< rows_a) or of
-// `b` (row_of - rows_a); row_of < 0 is a zero row. One thread per 16-byte chunk.
-__global__ void k_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K) {
-    const int KB = K / kTileK;
+// Pack an fp16 N x K matrix into the row-block layout of the step kernel. Packed row r is source
+// row row_of[r] of `a` (< rows_a) or of `b` (row_of - rows_a); row_of < 0 is a zero row. The rows
+// of CTA c are [R0, R0 + R) (R0 = 2 floor(P c / grid), P = N / 2), stored from byte R0 * K * 2 as
+// units in (pass, chunk) order: pass i covers rows [i * pass_rows, ...) of the CTA, chunk j inputs
+// [j * chunk_w, ...); a unit is [its rows][its inputs] fp16 in which the 16-byte chunks of each
+// 128-byte segment of row r are XOR-permuted by r & 7 (8 rows read by one ldmatrix hit 8 different
+// bank groups). One thread per 8 inputs of a row.
+__global__ void k_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
+                            int grid, int pass_rows, int chunk_w) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long total = (long long)N * K / 8;
     if (idx >= total) return;
-    const long long tile = idx >> 11;                 // 2048 chunks of 16 B per 32 KB tile
-    const int within = (int)(idx & 2047);
-    const int r = within >> 3, pc = within & 7;
-    const int ch = pc ^ (r & 7);
-    const int s = (int)(tile / KB), t = (int)(tile % KB);
-    const int row = kTileRows * s + r;
+    const int row = (int)(idx / (K / 8));
+    const int k = (int)(idx - (long long)row * (K / 8)) * 8;
+    const int P = N / 2, pair = row / 2;
+    int c = (int)(((long long)pair * grid) / P);
+    while (c > 0 && (long long)P * c / grid > pair) --c;
+    while (c + 1 < grid && (long long)P * (c + 1) / grid <= pair) ++c;
+    const int R0 = 2 * (int)((long long)P * c / grid);
+    const int R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+    const int lr = row - R0;
+    const int pi = lr / pass_rows;
+    const int rows_p = min(pass_rows, R - pi * pass_rows);
+    const int qi = k / chunk_w;
+    const int wq = min(chunk_w, K - qi * chunk_w);
+    const int r = lr - pi * pass_rows;                    // row within the unit
+    const int j = (k - qi * chunk_w) / 8;                   // 16-byte chunk within the unit's row
+    const int pj = (j & ~7) | ((j & 7) ^ (r & 7));          // 128-byte segments XOR-swizzled by row
+    const size_t off = (size_t)R0 * K * 2 + (size_t)pi * pass_rows * K * 2 + (size_t)rows_p * qi * chunk_w * 2 +
+                       (size_t)r * wq * 2 + (size_t)pj * 16;
     const int src = row_of[row];
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (src >= 0) {
         const __half *rp = src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
-        v = *reinterpret_cast<const uint4 *>(rp + kTileK * t + 8 * ch);
+        v = *reinterpret_cast<const uint4 *>(rp + k);
     }
-    *reinterpret_cast<uint4 *>(dst + (size_t)idx * 16) = v;
+    *reinterpret_cast<uint4 *>(dst + off) = v;
 }
 
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-void plan_step_gemv(StepOp &o, int num_sms, int min_tiles) {
-    const int KB = o.K / kTileK;
-    const long long T = (long long)(o.N / kTileRows) * KB;
-    // at least `min_tiles` tiles per CTA: fewer CTAs share a strip, so its last contributor sums
-    // fewer partials and waits for fewer CTAs
-    o.grid = (int)std::max<long long>(1, std::min<long long>(num_sms, T / std::max(1, min_tiles)));
-    const long long per = (T + o.grid - 1) / o.grid;
-    o.b_full = per >= KB ? 1 : 0;
-    o.a_blocks = o.b_full ? KB : (int)per;
-    const long long minper = std::max<long long>(1, T / o.grid);
-    o.max_contrib = (int)((KB + minper - 1) / minper + 1);
-    o.max_items = (int)(per / KB + 2);
+void plan_step_gemv(StepOp &o, int num_sms) {
+    const int P = o.N / 2;
+    o.grid = std::max(1, std::min(num_sms, P));
+    const int rmax = 2 * ((P + o.grid - 1) / o.grid);                       // rows of the busiest CTA
+    o.pass_rows = std::min(kPassRows, rmax);
+    int w = (kStageBytes / (o.pass_rows * 2)) / 256 * 256;                  // units of at most one stage
+    o.chunk_w = std::max(256, w) >= o.K ? o.K : std::max(256, w);
 }
 
-int step_max_items() { return kMaxItems; }
-int step_max_a_blocks() { return kMaxUnits * kEpiThreads / 8; }
+bool step_gemv_supported(const StepOp &o) {
+    return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows <= kPassRows &&
+           (size_t)o.pass_rows * o.chunk_w * 2 <= (size_t)kStageBytes &&
+           (o.chunk_w == o.K || o.chunk_w % 256 == 0) &&
+           (o.pro == PRO_NORM || o.pro == PRO_EMBED_NORM ? o.K <= kNormRegs * 4 * kEpiThreads : true);
+}
 
 size_t step_attn_smem_bytes(int hd) { return hd == 64 ? AttnRegion<64>::bytes : AttnRegion<128>::bytes; }
 
-static size_t step_static_reserve() { return 4096; }   // static shared memory of k_step, rounded up
+static size_t step_static_reserve() { return 2048; }   // static shared memory of k_step, rounded up
 
-size_t step_smem_bytes(int stages, int a_blocks, int hd, int n_ops) {
-    return (size_t)stages * kStageBytes + (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd) +
-           (size_t)n_ops * sizeof(StepOp) + (size_t)(2 * stages) * 8;
+size_t step_smem_bytes(int stages, int xmax, int hd, int n_ops) {
+    return (size_t)stages * kStageBytes + (size_t)xmax * 4 + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp) +
+           (size_t)(2 * stages) * 8;
 }
 
-int step_stages_for(int a_blocks, int hd, int n_ops) {
+int step_stages_for(int xmax, int hd, int n_ops) {
     const size_t budget = 227 * 1024 - step_static_reserve();
-    const size_t fixed = (size_t)a_blocks * kABlockBytes + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp);
+    const size_t fixed = (size_t)xmax * 4 + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp);
     if (fixed >= budget) return 0;
     return (int)((budget - fixed) / (kStageBytes + 16));
 }
 
-cudaError_t launch_pack_sw128(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
-                              cudaStream_t s) {
-    if (N % kTileRows || K % kTileK) return cudaErrorInvalidValue;
-    const long long total = (long long)N * K / 8;
-    k_pack_sw128<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(dst, a, rows_a, b, row_of, N, K);
+cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
+                             const StepOp &plan, cudaStream_t s) {
+    if (plan.N % 2 || plan.K % 8) return cudaErrorInvalidValue;
+    const long long total = (long long)plan.N * plan.K / 8;
+    k_pack_rows<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(dst, a, rows_a, b, row_of, plan.N, plan.K, plan.grid,
+                                                                plan.pass_rows, plan.chunk_w);
     return cudaGetLastError();
 }
 
@@ -1089,8 +1021,7 @@ cudaError_t prepare_step(int hd, size_t smem) {
 }
 
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    if (p.stages < 2 || p.a_blocks > step_max_a_blocks() || p.nh / p.nkv > kGroup || p.nkv * p.max_chunks > grid ||
-        p.max_chunks > kStepMaxChunks)
+    if (p.stages < 2 || p.nh / p.nkv > kGroup || p.nkv * p.max_chunks > grid || p.max_chunks > kStepMaxChunks)
         return cudaErrorInvalidValue;
     if (hd == 128) return step_launch_t<128>(&p, grid, smem, s, pdl);
     if (hd == 64) return step_launch_t<64>(&p, grid, smem, s, pdl);

@@ -30,24 +30,21 @@ STEP_OPS = ("qkv", "attn", "o", "gate_up", "down")
 
 def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
     """Timeline of the persistent step kernel from its per-op, per-CTA stamps (microseconds):
-    [0] the CTA reached the op, [1] its dependency was met, [2] activation ready, [3] op done,
-    [4] first accumulator ready, [5] last accumulator ready, [6] MMA warp starts the op, [7] the op's first
-    ring stage is available to the MMA warp."""
+    [0] the CTA reached the op, [1] its dependency was met, [2] input vector ready, [3] op done,
+    [4] first weight unit available, [5] all rows finished."""
     import numpy as np
     t0 = t[t > 0].min()
     t = np.where(t > 0, (t - t0) / 1000.0, np.nan)
     rows, prev_done = [], 0.0
+    gemv = lambda x: x if True else None
     for k in range(t.shape[0]):
         layer, kind = (k // 5, STEP_OPS[k % 5]) if k < 5 * layers else (-1, "lm_head")
         done = float(np.nanmax(t[k, :, 3]))
-        row = {"k": k, "layer": layer, "kind": kind,
-               "dep_met_max": float(np.nanmax(t[k, :, 1])) if kind != "attn" else None,
-               "bready_med": float(np.nanmedian(t[k, :, 2])) if kind != "attn" else None,
-               "mma_start_med": float(np.nanmedian(t[k, :, 6])) if kind != "attn" else None,
-               "tile0_med": float(np.nanmedian(t[k, :, 7])) if kind != "attn" else None,
-               "acc_first_med": float(np.nanmedian(t[k, :, 4])) if kind != "attn" else None,
-               "acc_last_med": float(np.nanmedian(t[k, :, 5])) if kind != "attn" else None,
-               "acc_last_max": float(np.nanmax(t[k, :, 5])) if kind != "attn" else None,
+        g = kind != "attn"
+        med = lambda j: float(np.nanmedian(t[k, :, j])) if g else None
+        mx = lambda j: float(np.nanmax(t[k, :, j])) if g else None
+        row = {"k": k, "layer": layer, "kind": kind, "dep_met_max": mx(1), "input_med": med(2),
+               "unit0_med": med(4), "rows_med": med(5), "rows_max": mx(5),
                "done_med": float(np.nanmedian(t[k, :, 3])), "done_max": done, "since_prev_done": done - prev_done}
         prev_done = done
         if layer in layers_shown or layer == -1:
