@@ -309,7 +309,7 @@ __device__ void attn_prestage(const StepParams &p, const StepOp &op, const StepS
 
 template <int HD>
 __device__ void attention_item(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
-                               int n_chunks, int rows_per, int ctx, const Abort &ab) {
+                               int n_chunks, int rows_per, int ctx, const Abort &ab, int k) {
     using L = AttnRegion<HD>;
     constexpr int DL = HD / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -326,11 +326,13 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     const int s1 = min(j1, j0 + kStepAttnRows);
     if (tid == 0 && op.dep >= 0) wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
     epi_sync();
+    stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
     if (slot >= j0 && slot < s1) stage_rows<HD>(am, kb, vb, j0, slot, slot + 1, tid);
     for (int i = tid; i < G * HD / 4; i += kEpiThreads) cp_async16(qs + 4 * i, p.q + (size_t)g * G * HD + 4 * i);
     cp_async_commit();
     cp_async_wait_all();
     epi_sync();
+    stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
 
     float qr[kGroup][DL];
 #pragma unroll
@@ -390,6 +392,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
             }
         }
         epi_sync();
+        if (a == j0) stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
         // softmax (online) and values: this warp's heads only, so the warp needs no CTA barrier
         float corr[2];
 #pragma unroll
@@ -450,6 +453,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
                 for (int i = 0; i < DL; ++i) acc[u][i] = fmaf(acc[u][i], corr[u], part[u][0][i] + part[u][1][i]);
         }
     }
+    stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
     // publish this chunk's partial for each of this warp's heads
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -469,31 +473,30 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
 
 // The last attention item of kv head g merges the head's chunks: out[h][d] for the G q heads of
 // the group = sum_c w_c acc_c[d] with w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), in chunk order.
-// `scratch` (shared, >= 2 * kGroup * max_chunks floats) holds the per-(head, chunk) weights.
+// `scratch` (shared, >= 3 * kGroup * kStepMaxChunks floats) holds the per-(head, chunk) weights.
 template <int HD>
 __device__ void merge_group(const StepParams &p, int g, int n_chunks, float *scratch) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.nh / p.nkv;
-    float *wts = scratch;                                  // [G][n_chunks]
+    float *wts = scratch;                                  // [G][n_chunks] weights
+    float2 *mls = reinterpret_cast<float2 *>(scratch + kGroup * kStepMaxChunks);   // [G][n_chunks] (max, sum)
     for (int i = tid; i < G * n_chunks; i += kEpiThreads) {
         const int hh = i / n_chunks, c = i - hh * n_chunks;
-        wts[i] = __ldcg(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2);
+        mls[i] = __ldcg(reinterpret_cast<const float2 *>(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2));
     }
     epi_sync();
     for (int hh = warp; hh < G; hh += 4) {
         float M = -INFINITY;
-        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, wts[hh * n_chunks + c]);
+        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, mls[hh * n_chunks + c].x);
         M = warp_max(M);
         float L = 0.f;
         for (int c = lane; c < n_chunks; c += 32) {
-            const float m = wts[hh * n_chunks + c];
-            const float l = __ldcg(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2 + 1);
-            L = fmaf(l, m == -INFINITY ? 0.f : expf(m - M), L);
+            const float2 ml = mls[hh * n_chunks + c];
+            L = fmaf(ml.y, ml.x == -INFINITY ? 0.f : expf(ml.x - M), L);
         }
         L = warp_sum(L);
-        __syncwarp();
         for (int c = lane; c < n_chunks; c += 32) {
-            const float m = wts[hh * n_chunks + c];
+            const float m = mls[hh * n_chunks + c].x;
             wts[hh * n_chunks + c] = m == -INFINITY ? 0.f : expf(m - M) / L;
         }
     }
@@ -624,14 +627,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 // they stage their K/V rows early
                 const int items = p.nkv * n_chunks, item = C - 1 - c;
                 if (item < items && !ab.on()) {
-                    attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab);
+                    attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
                     const int g = item / n_chunks;
                     epi_sync();
                     if (tid == 0) s_flag = atom_add_acq_rel(p.grp_cnt + g, 1u) == (unsigned)(n_chunks - 1);
                     epi_sync();
                     if (s_flag) {      // the head's last chunk: merge all of them
+                        stamp(p.trace, k, C, c, 6);
                         merge_group<HD>(p, g, n_chunks, reinterpret_cast<float *>(am));
                         epi_sync();
+                        stamp(p.trace, k, C, c, 7);
                         if (tid == 0) {
                             p.grp_cnt[g] = 0u;
                             if (op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);

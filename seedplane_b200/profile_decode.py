@@ -43,6 +43,16 @@ def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
         g = kind != "attn"
         med = lambda j: float(np.nanmedian(t[k, :, j])) if g else None
         mx = lambda j: float(np.nanmax(t[k, :, j])) if g else None
+        if kind == "attn":       # item CTAs only: [1] QKV ready, [2] staged, [4] computed, [6]/[7] merge
+            a = lambda j, f: float(f(t[k, :, j])) if not np.isnan(t[k, :, j]).all() else None
+            row = {"k": k, "layer": layer, "kind": kind, "qkv_seen_max": a(1, np.nanmax), "staged_max": a(2, np.nanmax),
+                   "scores_max": a(5, np.nanmax), "computed_med": a(4, np.nanmedian), "computed_max": a(4, np.nanmax),
+                   "merge_start_max": a(6, np.nanmax), "merge_end_max": a(7, np.nanmax),
+                   "done_max": float(np.nanmax(t[k, :, 3])), "since_prev_done": float(np.nanmax(t[k, :, 3])) - prev_done}
+            prev_done = row["done_max"]
+            if layer in layers_shown:
+                rows.append({key: (round(v, 2) if isinstance(v, float) else v) for key, v in row.items()})
+            continue
         row = {"k": k, "layer": layer, "kind": kind, "dep_met_max": mx(1), "input_med": med(2),
                "unit0_med": med(4), "rows_med": med(5), "rows_max": mx(5),
                "done_med": float(np.nanmedian(t[k, :, 3])), "done_max": done, "since_prev_done": done - prev_done}

@@ -1,0 +1,222 @@
+"""Speculative decoding surface of the B200 engine (drop-in for `seedplane.speculative`).
+
+Same types and the same decisions as the reference prototype (`seedplane/speculative.py`):
+
+* `SpeculativeForest.build` / `node_count` -- trie of draft branches, empty branches skipped,
+  `paths` kept in input order (speculative.py:18-43).
+* `verify_greedy(committed, forest, target_logits)` -- every path walked in input order; the
+  target token is the first index of the maximum; the first mismatch emits the target token and
+  rejects; the path with the largest (accepted_draft_tokens, len(emitted)) wins, the earliest on
+  ties (strict '>'); no bonus token on full acceptance; an empty forest yields one target token
+  (speculative.py:55-92).
+* `CommitLedger` -- the committed frontier moves only on commit (speculative.py:95-111).
+
+Added for the GPU:
+
+* `SpeculativeForest.flatten()` -- the trie as arrays (token, parent, depth) in first-visit order
+  of the paths, and each path as a list of node indices: the layout `sp_verify_tree` takes.
+* `verify_tree(engine, kv, forest, root_pred, base_pos)` -- ONE batched target pass over the whole
+  forest on the device (every node attends to the committed prefix and its own ancestors), then
+  the same selection rule applied to the per-node argmaxes. Returns the same `Verification` as
+  `verify_greedy` would with the engine's logits, plus the data needed to commit.
+* `commit_tree(engine, kv, tree, verification)` -- moves the accepted nodes' K/V into place.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple
+
+
+@dataclass
+class ForestNode:
+    token: int
+    children: Dict[int, "ForestNode"] = field(default_factory=dict)
+
+
+@dataclass
+class SpeculativeForest:
+    roots: Dict[int, ForestNode] = field(default_factory=dict)
+    paths: List[Tuple[int, ...]] = field(default_factory=list)
+
+    @classmethod
+    def build(cls, branches: Iterable[Iterable[int]]) -> "SpeculativeForest":
+        forest = cls()
+        for branch in branches:
+            path = tuple(int(token) for token in branch)
+            if not path:
+                continue
+            forest.paths.append(path)
+            children = forest.roots
+            for token in path:
+                node = children.get(token)
+                if node is None:
+                    node = children[token] = ForestNode(token)
+                children = node.children
+        return forest
+
+    @property
+    def node_count(self) -> int:
+        def count(children):
+            return sum(1 + count(node.children) for node in children.values())
+        return count(self.roots)
+
+    def flatten(self) -> "FlatForest":
+        index: Dict[Tuple[int, ...], int] = {}
+        tokens: List[int] = []
+        parents: List[int] = []
+        depths: List[int] = []
+        node_paths: List[List[int]] = []
+        for path in self.paths:
+            ids = []
+            for d in range(1, len(path) + 1):
+                key = path[:d]
+                if key not in index:
+                    index[key] = len(tokens)
+                    tokens.append(path[d - 1])
+                    parents.append(index[path[:d - 1]] if d > 1 else -1)
+                    depths.append(d)
+                ids.append(index[key])
+            node_paths.append(ids)
+        return FlatForest(tuple(tokens), tuple(parents), tuple(depths), tuple(tuple(p) for p in node_paths),
+                          tuple(self.paths))
+
+
+@dataclass(frozen=True)
+class FlatForest:
+    tokens: Tuple[int, ...]          # node tokens, first-visit order
+    parents: Tuple[int, ...]         # parent node index, -1 = child of the committed prefix
+    depths: Tuple[int, ...]          # 1 = first draft token
+    node_paths: Tuple[Tuple[int, ...], ...]
+    paths: Tuple[Tuple[int, ...], ...]
+
+
+@dataclass(frozen=True)
+class Verification:
+    emitted: Tuple[int, ...]
+    accepted_draft_tokens: int
+    rejected: bool
+    target_steps: int
+    branch: Tuple[int, ...]
+
+
+def _first_argmax(values: Sequence[float]) -> int:
+    return max(range(len(values)), key=values.__getitem__)
+
+
+def verify_greedy(committed: Sequence[int], forest: SpeculativeForest,
+                  target_logits: Callable[[Tuple[int, ...]], Sequence[float]]) -> Verification:
+    """Verify every draft path with one target call per (path, depth), then choose the longest
+    exact greedy continuation (the reference's sequential rule, kept for callers with a logits
+    callback; the GPU path is `verify_tree`)."""
+    base = tuple(int(t) for t in committed)
+    if not forest.paths:
+        logits = target_logits(base)
+        if not len(logits):
+            raise ValueError("target returned empty logits")
+        return Verification((_first_argmax(logits),), 0, False, 1, ())
+    best = None
+    for path in forest.paths:
+        accepted: List[int] = []
+        steps = 0
+        rejected = False
+        for draft_token in path:
+            logits = target_logits(base + tuple(accepted))
+            if not len(logits):
+                raise ValueError("target returned empty logits")
+            target_token = _first_argmax(logits)
+            steps += 1
+            if draft_token != target_token:
+                accepted.append(target_token)
+                rejected = True
+                break
+            accepted.append(draft_token)
+        result = Verification(tuple(accepted), len(accepted) - int(rejected), rejected, steps, path)
+        if best is None or (result.accepted_draft_tokens, len(result.emitted)) > \
+                (best.accepted_draft_tokens, len(best.emitted)):
+            best = result
+    return best
+
+
+def accept_greedy(flat: FlatForest, root_pred: int, node_pred: Sequence[int]) -> Tuple[Verification, Tuple[int, ...]]:
+    """`verify_greedy`'s decision from the target argmax after the committed prefix (`root_pred`)
+    and after each node (`node_pred[i]`). Returns the verification and the accepted draft nodes
+    of the chosen path (their K/V is what a commit keeps)."""
+    if not flat.paths:
+        return Verification((int(root_pred),), 0, False, 1, ()), ()
+    best, best_nodes = None, ()
+    for path, ids in zip(flat.paths, flat.node_paths):
+        emitted: List[int] = []
+        nodes: List[int] = []
+        steps = 0
+        rejected = False
+        prev = -1
+        for nid in ids:
+            target = int(root_pred) if prev < 0 else int(node_pred[prev])
+            steps += 1
+            if flat.tokens[nid] != target:
+                emitted.append(target)
+                rejected = True
+                break
+            emitted.append(flat.tokens[nid])
+            nodes.append(nid)
+            prev = nid
+        result = Verification(tuple(emitted), len(emitted) - int(rejected), rejected, steps, tuple(path))
+        if best is None or (result.accepted_draft_tokens, len(result.emitted)) > \
+                (best.accepted_draft_tokens, len(best.emitted)):
+            best, best_nodes = result, tuple(nodes)
+    return best, best_nodes
+
+
+@dataclass(frozen=True)
+class TreeResult:
+    verification: Verification
+    accepted_nodes: Tuple[int, ...]  # node indices of the accepted draft tokens, in order
+    node_pred: Tuple[int, ...]       # target argmax after every node
+    next_pred: Optional[int]         # target argmax after the emitted tokens, when known (full acceptance)
+    flat: FlatForest
+
+
+def verify_tree(engine, kv, forest: SpeculativeForest, root_pred: int, base_pos: int,
+                want_logits: bool = False) -> TreeResult:
+    """One batched target pass over the whole forest (`sp_verify_tree`) and the reference's
+    selection rule on its argmaxes.
+
+    `root_pred` is the target's greedy token after the committed prefix (the caller has it from
+    the previous step); `base_pos` is the position of the first draft token. The cache length is
+    not advanced; `commit_tree` keeps the accepted nodes."""
+    flat = forest.flatten()
+    if not flat.tokens:
+        return TreeResult(Verification((int(root_pred),), 0, False, 1, ()), (), (), None, flat)
+    argmax, _ = engine.verify_tree(kv, list(flat.tokens), list(flat.parents), base_pos, want_logits=want_logits)
+    node_pred = tuple(int(t) for t in argmax.cpu().tolist())
+    ver, nodes = accept_greedy(flat, root_pred, node_pred)
+    next_pred = node_pred[nodes[-1]] if (nodes and not ver.rejected) else None
+    return TreeResult(ver, nodes, node_pred, next_pred, flat)
+
+
+def commit_tree(engine, kv, result: TreeResult) -> int:
+    """Keep the K/V of the accepted draft nodes (they were written at scratch slots len + i) and
+    advance the cache length by their number. Returns the new length."""
+    base = kv.length
+    slots = [base + i for i in result.accepted_nodes]
+    engine.kv_commit(kv, slots)
+    return kv.length
+
+
+@dataclass
+class CommitLedger:
+    """Committed token frontier; speculative state never mutates it pre-commit."""
+    tokens: List[int] = field(default_factory=list)
+    commits: int = 0
+
+    @property
+    def frontier(self) -> int:
+        return len(self.tokens)
+
+    def commit(self, verification: Verification) -> Tuple[int, ...]:
+        if not verification.emitted:
+            raise ValueError("cannot commit an empty verification")
+        committed = verification.emitted
+        self.tokens.extend(committed)
+        self.commits += 1
+        return committed

@@ -200,3 +200,43 @@ def test_argmax_rows_first_index(tiny):
         got = eng.argmax(dev[:, :cols]).cpu().numpy()
         want = np.argmax(x[:, :cols], axis=1)
         assert (got == want).all()
+
+
+def test_speculative_surface_verify_tree_and_commit(tiny):
+    """`speculative.verify_tree` (one batched device pass) takes the same decision as the
+    reference's sequential `verify_greedy` with the oracle as target; after `commit_tree` the
+    cache continues exactly like the oracle on the committed tokens."""
+    from seedplane_b200.speculative import SpeculativeForest, commit_tree, verify_greedy, verify_tree
+    cfg, w, eng, o = tiny
+    prompt = random_prompt(cfg.vocab, 10, seed=3)
+    greedy, _ = o.greedy(prompt, 6, capacity=64)
+    V = cfg.vocab
+
+    def target(prefix):
+        lg, _ = o.forward(list(prefix), o.new_cache(64))
+        return lg[-1].tolist()
+
+    for branches in ([greedy[:4], greedy[:2] + [(greedy[2] + 1) % V], [(greedy[0] + 3) % V], greedy[:3]],
+                     [[(greedy[0] + 1) % V, greedy[1]], greedy[:1] + [(greedy[1] + 7) % V]],
+                     [greedy[:5]]):
+        kv = eng.new_kv(64)
+        _, am = eng.forward(kv, prompt, want_logits=False)
+        root = int(am[-1])
+        assert root == greedy[0]
+        forest = SpeculativeForest.build(branches)
+        res = verify_tree(eng, kv, forest, root_pred=root, base_pos=len(prompt))
+        assert res.verification == verify_greedy(prompt, forest, target)
+        n_acc = res.verification.accepted_draft_tokens
+        assert commit_tree(eng, kv, res) == len(prompt) + n_acc
+        # continue from the committed prefix: feed the last emitted token (correction or last
+        # accepted) unless it is already in the cache
+        emitted = list(res.verification.emitted)
+        if res.verification.rejected:
+            toks, _ = eng.decode(kv, emitted[-1], len(prompt) + n_acc, 2)
+            want, _ = o.greedy(prompt + emitted, 2, capacity=64)
+        else:
+            assert res.next_pred == greedy[len(emitted)]
+            toks, _ = eng.decode(kv, res.next_pred, len(prompt) + n_acc, 2)
+            want, _ = o.greedy(prompt + emitted + [res.next_pred], 2, capacity=64)
+        assert toks.cpu().tolist() == want
+        kv.close()
