@@ -110,7 +110,8 @@ struct sp_engine {
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
     int n_cnt = 0;
-    float *attn_ml = nullptr, *attn_acc = nullptr, *attn_out = nullptr;
+    float *attn_ml = nullptr, *attn_acc = nullptr;
+    __half *attn_h = nullptr, *attn_l = nullptr, *act_h = nullptr, *act_l = nullptr;
     unsigned *grp_cnt = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
@@ -220,17 +221,19 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         a.dep_n = e->s_qkv.grid;
         a.sig = 5 * l + 1;
         ops.push_back(a);
-        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, c.kv_heads, 5 * l + 2);
+        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, c.heads, 5 * l + 2);
         o.out = e->x;
         o.resid_embed = l == 0;
         ops.push_back(o);
         o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU, 5 * l + 2, e->s_o.grid, 5 * l + 3);
         o.xin = e->x;
         o.gain = L.post_norm;
-        o.out = e->act;
+        o.out_h = e->act_h;
+        o.out_l = e->act_l;
         ops.push_back(o);
         o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID, 5 * l + 3, e->s_gu.grid, 5 * l + 4);
-        o.xin = e->act;
+        o.xin_h = e->act_h;
+        o.xin_l = e->act_l;
         o.out = e->x;
         ops.push_back(o);
     }
@@ -288,7 +291,8 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.q = e->q;
         p.attn_ml = e->attn_ml;
         p.attn_acc = e->attn_acc;
-        p.attn_out = e->attn_out;
+        p.attn_h = e->attn_h;
+        p.attn_l = e->attn_l;
         p.grp_cnt = e->grp_cnt;
         p.part_val = e->lm_val;
         p.part_idx = e->lm_idx;
@@ -731,12 +735,12 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
     // counters and split-strip state first: a device error clears exactly this prefix
     e->n_cnt = 5 * c.layers;
-    e->step_max_chunks = std::min(kStepMaxChunks, e->num_sms / c.kv_heads);
+    e->step_max_chunks = std::min(kStepMaxChunks, e->num_sms / c.heads);
     const size_t w_cnt = wtake((size_t)e->n_cnt * 8), w_epoch = wtake(8);
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
     const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
-    const size_t w_grp = wtake((size_t)c.kv_heads * 4);
+    const size_t w_grp = wtake((size_t)c.heads * 4);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
@@ -747,6 +751,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_ml = wtake((size_t)c.heads * e->step_max_chunks * 2 * 4);
     const size_t w_acc = wtake((size_t)c.heads * e->step_max_chunks * HD * 4);
     const size_t w_aout = wtake((size_t)c.heads * HD * 4);
+    const size_t w_acth = wtake(I * 4);
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
@@ -765,7 +770,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->epoch = (unsigned long long *)(e->ws + w_epoch);
     e->attn_ml = (float *)(e->ws + w_ml);
     e->attn_acc = (float *)(e->ws + w_acc);
-    e->attn_out = (float *)(e->ws + w_aout);
+    e->attn_h = (__half *)(e->ws + w_aout);
+    e->attn_l = e->attn_h + (size_t)c.heads * HD;
+    e->act_h = (__half *)(e->ws + w_acth);
+    e->act_l = e->act_h + I;
     e->grp_cnt = (unsigned *)(e->ws + w_grp);
     e->g_head.w = e->head;
     e->g_head.part_val = e->lm_val;
@@ -807,7 +815,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     if (e->step_kernel) {
         e->step_xmax = (int)align_up(std::max(H, I), 4);
         e->step_stages = step_stages_for(e->step_xmax, (int)HD, 5 * c.layers + 1);
-        if (e->step_stages < 2 || c.kv_heads * e->step_max_chunks > e->num_sms)
+        if (e->step_stages < 2 || e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms)
             return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (input vector of %d floats, %d stages)",
                              e->step_xmax, e->step_stages));
         e->step_smem = step_smem_bytes(e->step_stages, e->step_xmax, (int)HD, 5 * c.layers + 1);

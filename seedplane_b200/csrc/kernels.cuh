@@ -165,21 +165,23 @@ cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap,
 // without waiting for data, and meets the other CTAs only through 64-bit dependency counters in
 // global memory: an op's consumers wait until its counter reaches units x (epoch + 1), where
 // `epoch` counts finished steps (advanced by the LM head's last CTA) and `units` is the number of
-// CTAs (GEMVs) or kv heads (attention) that signal it once per step.
+// CTAs (GEMVs) or q heads (attention) that signal it once per step.
 enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged attention output
-constexpr int kStepAttnRows = 32;        // attention positions staged per sub-chunk
-constexpr int kStepMaxChunks = 64;       // attention chunks per kv head
+constexpr int kStepAttnRows = 64;        // attention positions staged per sub-chunk
+constexpr int kStepMaxChunks = 64;       // attention chunks per q head
 constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
 constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, input ready, done,
                                          // first unit available, rows finished
 
 struct StepOp {
     const uint8_t *w;        // row-block packed weights (GEMV), see k_pack_rows
-    const float *xin;        // prologue input (PRO_NORM / PRO_PLAIN)
+    const float *xin;        // prologue input (PRO_NORM): fp32 vector
+    const __half *xin_h, *xin_l;   // prologue input (PRO_PLAIN): fp16 hi / lo vectors
     const float *gain;       // RMSNorm gains
     const float *bias;       // QKV bias
-    float *out;              // epilogue output (q / x / act)
+    float *out;              // epilogue output (q / x)
+    __half *out_h, *out_l;   // EPI_SWIGLU output as fp16 hi / lo vectors
     __half *kc, *vc;         // this layer's K/V cache (QKV epilogue, attention)
     int kind;                // StepOpKind
     int pro, epi;
@@ -188,7 +190,7 @@ struct StepOp {
     int pass_rows;           // rows per pass (even, <= kStepPassRows)
     int chunk_w;             // inputs per unit (multiple of 256, or all of K)
     int dep, dep_n;          // wait until cnt[dep] >= dep_n * (epoch + 1); dep < 0: none
-    int sig;                 // cnt[sig] += 1 per CTA (GEMV) / per kv head (attention); < 0: none
+    int sig;                 // cnt[sig] += 1 per CTA (GEMV) / per q head (attention); < 0: none
     int resid_embed;         // EPI_RESID: the residual base is the token's embedding row
     int pad_[1];
 };
@@ -200,7 +202,7 @@ struct StepParams {
     int stages;              // ring stages of 64 KB
     int xmax;                // floats of the shared input vector (largest K, multiple of 4)
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
-    int max_chunks;          // attention chunks per kv head at most (nkv * max_chunks <= grid)
+    int max_chunks;          // attention chunks per q head at most (nh * max_chunks <= grid)
     int evict_first;         // ring copies carry an L2 evict-first hint
     float eps, scale;
     const float *rope;
@@ -208,8 +210,8 @@ struct StepParams {
     float *q;                // [nh * hd] fp32 (RoPE applied)
     float *attn_ml;          // [nh][max_chunks][2]  (running max, sum) per attention chunk
     float *attn_acc;         // [nh][max_chunks][hd] unnormalised outputs per chunk
-    float *attn_out;         // [nh * hd] merged attention output (the O projection's input)
-    unsigned *grp_cnt;       // [nkv] attention chunks finished per kv head (last one merges)
+    __half *attn_h, *attn_l; // [nh * hd] merged attention output as fp16 hi / lo (the O projection's input)
+    unsigned *grp_cnt;       // [nh] attention chunks finished per q head (the last one merges)
     float *part_val;         // LM head: per-CTA argmax
     int *part_idx;
     unsigned *lm_cnt;

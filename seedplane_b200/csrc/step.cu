@@ -43,7 +43,7 @@ constexpr int kThreads = kEpiThreads + 32;
 constexpr int kStageBytes = 64 * 1024;      // one unit per stage (a bulk copy costs about the same
                                             // time whatever its size, so big ones ingest faster)
 constexpr int kPassRows = kStepPassRows;    // rows per pass: 16 per warp
-constexpr int kGroup = 8;                   // q heads per kv head, padded (zero q beyond G)
+constexpr int kGroup = 8;                   // q heads per kv head at most
 constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
 constexpr uint32_t kDepSpinLimit = 1u << 22;
 
@@ -205,16 +205,17 @@ SP_DEVINL bool wait_counter(const unsigned long long *cnt, unsigned long long ta
     return false;
 }
 
-// Attention staging region: K and V rows of one sub-chunk (fp16), q of the group (fp32, padded
-// to kGroup heads), scores [rows][kGroup].
+// Attention staging region of one (q head, chunk) item: K and V rows of one sub-chunk (fp16), the
+// scores, q (fp32) and the four warps' value sums.
 template <int HD>
 struct AttnRegion {
     static constexpr int kRow = HD * 2;
-    static constexpr size_t kOff = 0;
-    static constexpr size_t vOff = kOff + (size_t)kStepAttnRows * kRow;
-    static constexpr size_t qOff = vOff + (size_t)kStepAttnRows * kRow;
-    static constexpr size_t sOff = qOff + (size_t)kGroup * HD * 4;
-    static constexpr size_t bytes = sOff + (size_t)kStepAttnRows * kGroup * 4;
+    static constexpr size_t kOff = 0;                                   // K rows of the sub-chunk
+    static constexpr size_t vOff = kOff + (size_t)kStepAttnRows * kRow; // V rows
+    static constexpr size_t sOff = vOff + (size_t)kStepAttnRows * kRow; // scores / probabilities [rows]
+    static constexpr size_t qOff = sOff + (size_t)kStepAttnRows * 4;    // q of the head [HD] fp32
+    static constexpr size_t rOff = qOff + (size_t)HD * 4;               // per-warp PV partials [4][HD]
+    static constexpr size_t bytes = rOff + (size_t)4 * HD * 4;
 };
 
 // cp.async K/V rows [lo, hi) of one kv head into the sub-chunk buffers (row j -> local j - base).
@@ -248,28 +249,6 @@ SP_DEVINL void load_dims(const uint8_t *q, float (&f)[DL]) {
     }
 }
 
-// Sum v[h] over the 32 lanes for 8 heads; lane l returns head l / 4 (exchange steps xor 16, 8, 4
-// halve the values per lane, then xor 2, 1 finish the sums; fixed order).
-SP_DEVINL float reduce_heads(const float (&v)[kGroup], int lane) {
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-    float w[4], x[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float send = b4 ? v[i] : v[i + 4], keep = b4 ? v[i + 4] : v[i];
-        w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const float send = b3 ? w[i] : w[i + 2], keep = b3 ? w[i + 2] : w[i];
-        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-    const float send = b2 ? x[0] : x[1], keep = b2 ? x[1] : x[0];
-    float y = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    y += __shfl_xor_sync(0xffffffffu, y, 2);
-    y += __shfl_xor_sync(0xffffffffu, y, 1);
-    return y;
-}
-
 // Attention chunking of the visible context [0, ctx): the same in the attention op and in the
 // O projection's merge.
 SP_DEVINL int attn_chunks(int ctx, int max_chunks) {
@@ -289,24 +268,27 @@ struct StepState {
     unsigned long long mask;
 };
 
-// ---- attention item of one CTA: (kv head g, chunk ch) ------------------------------------------
-// Staging that does not depend on the step: zero q of the padded heads and copy the first
-// sub-chunk's K/V rows other than the current one. Issued before the QKV projection's wait.
+// ---- attention item of one CTA: (q head h, context chunk ch) -----------------------------------
+// Staging that does not depend on the step: the first sub-chunk's K/V rows other than the current
+// one (only the step's QKV projection writes row `slot`). Issued before the QKV projection's wait.
 template <int HD>
 __device__ void attn_prestage(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
                               int n_chunks, int rows_per, int ctx) {
-    using L = AttnRegion<HD>;
-    const int tid = threadIdx.x;
     const int G = p.nh / p.nkv;
-    const int g = item / n_chunks, ch = item - g * n_chunks;
+    const int h = item / n_chunks, ch = item - h * n_chunks, g = h / G;
     const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
-    float *qs = reinterpret_cast<float *>(am + L::qOff);
-    for (int i = G * HD + tid; i < kGroup * HD; i += kEpiThreads) qs[i] = 0.f;
     const int s1 = min(j1, j0 + kStepAttnRows);
-    stage_rows<HD>(am, op.kc + (size_t)g * p.cap * HD, op.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot), tid);
+    stage_rows<HD>(am, op.kc + (size_t)g * p.cap * HD, op.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot),
+                   threadIdx.x);
     cp_async_commit();
 }
 
+// One q head over one chunk of the context, in sub-chunks of up to kStepAttnRows positions:
+//   scores  warp = position (four in flight), lane = HD/32 dims, q in registers, warp sum
+//   softmax one warp, running max / sum across sub-chunks (fp32)
+//   values  warp = every fourth position, lane = HD/32 dims; the four warps' sums meet in shared
+//           memory and thread t < HD keeps output dim t
+// Publishes the chunk's unnormalised partial (max, sum, acc[HD]).
 template <int HD>
 __device__ void attention_item(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
                                int n_chunks, int rows_per, int ctx, const Abort &ab, int k) {
@@ -314,209 +296,161 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     constexpr int DL = HD / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.nh / p.nkv;
-    const int g = item / n_chunks, ch = item - g * n_chunks;
+    const int h = item / n_chunks, ch = item - h * n_chunks, g = h / G;
     const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
     const __half *kb = op.kc + (size_t)g * p.cap * HD;
     const __half *vb = op.vc + (size_t)g * p.cap * HD;
     float *qs = reinterpret_cast<float *>(am + L::qOff);
     float *sc = reinterpret_cast<float *>(am + L::sOff);
+    float *rd = reinterpret_cast<float *>(am + L::rOff);
+    __shared__ float s_corr;
     const int slot = ss.slot;
-
-    // rows other than the current one were staged by attn_prestage (they do not depend on this step)
     const int s1 = min(j1, j0 + kStepAttnRows);
     if (tid == 0 && op.dep >= 0) wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
     epi_sync();
     stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
     if (slot >= j0 && slot < s1) stage_rows<HD>(am, kb, vb, j0, slot, slot + 1, tid);
-    for (int i = tid; i < G * HD / 4; i += kEpiThreads) cp_async16(qs + 4 * i, p.q + (size_t)g * G * HD + 4 * i);
+    for (int i = tid; i < HD / 4; i += kEpiThreads) cp_async16(qs + 4 * i, p.q + (size_t)h * HD + 4 * i);
     cp_async_commit();
     cp_async_wait_all();
     epi_sync();
     stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
 
-    float qr[kGroup][DL];
+    float qr[DL];
 #pragma unroll
-    for (int h = 0; h < kGroup; ++h)
-#pragma unroll
-        for (int i = 0; i < DL; ++i) qr[h][i] = qs[h * HD + DL * lane + i];
-    // this warp's heads: warp and warp + 4 (of the group)
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    float acc[2][DL];
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int i = 0; i < DL; ++i) acc[u][i] = 0.f;
+    for (int i = 0; i < DL; ++i) qr[i] = qs[DL * lane + i];
+    float m_run = -INFINITY, l_run = 0.f;       // warp 0 (lane-uniform)
+    float acc = 0.f;                            // thread t < HD: output dim t
 
     for (int a = j0; a < j1; a += kStepAttnRows) {
         const int b = min(j1, a + kStepAttnRows), nj = b - a;
         if (a != j0) {
-            epi_sync();                       // everyone is done with the previous sub-chunk
+            epi_sync();                         // everyone is done with the previous sub-chunk
             stage_rows<HD>(am, kb, vb, a, a, b, tid);
             cp_async_commit();
             cp_async_wait_all();
             epi_sync();
         }
-        // scores: warp = position (two in flight), lane = HD/32 dims, all 8 heads
-        for (int jl = warp; jl < nj; jl += 8) {
-            const int jl2 = jl + 4;
-            const bool has2 = jl2 < nj;
-            float k1[DL], k2[DL];
-            load_dims<DL>(am + L::kOff + (size_t)jl * L::kRow + lane * DL * 2, k1);
-            if (has2) {
-                load_dims<DL>(am + L::kOff + (size_t)jl2 * L::kRow + lane * DL * 2, k2);
-            } else {
+        // scores: four positions per warp in flight
+        for (int jl = warp; jl < nj; jl += 16) {
+            float t[4];
 #pragma unroll
-                for (int i = 0; i < DL; ++i) k2[i] = 0.f;
-            }
-            float v1[kGroup], v2[kGroup];
+            for (int u = 0; u < 4; ++u) {
+                const int j = jl + 4 * u;
+                float kf[DL];
+                if (j < nj) {
+                    load_dims<DL>(am + L::kOff + (size_t)j * L::kRow + lane * DL * 2, kf);
+                } else {
 #pragma unroll
-            for (int h = 0; h < kGroup; ++h) {
-                float t1 = qr[h][0] * k1[0], t2 = qr[h][0] * k2[0];
-#pragma unroll
-                for (int i = 1; i < DL; ++i) {
-                    t1 = fmaf(qr[h][i], k1[i], t1);
-                    t2 = fmaf(qr[h][i], k2[i], t2);
+                    for (int i = 0; i < DL; ++i) kf[i] = 0.f;
                 }
-                v1[h] = t1;
-                v2[h] = t2;
+                float v = qr[0] * kf[0];
+#pragma unroll
+                for (int i = 1; i < DL; ++i) v = fmaf(qr[i], kf[i], v);
+                t[u] = v;
             }
-            const float r1 = reduce_heads(v1, lane), r2 = reduce_heads(v2, lane);
-            if ((lane & 3) == 0) {
-                const int h = lane >> 2, j = a + jl, j2 = a + jl2;
-                const bool vis1 = !(j >= ss.tree_base && !((ss.mask >> (j - ss.tree_base)) & 1ull));
-                sc[jl * kGroup + h] = vis1 ? r1 * p.scale : -INFINITY;
-                if (has2) {
-                    const bool vis2 = !(j2 >= ss.tree_base && !((ss.mask >> (j2 - ss.tree_base)) & 1ull));
-                    sc[jl2 * kGroup + h] = vis2 ? r2 * p.scale : -INFINITY;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) t[u] += __shfl_xor_sync(0xffffffffu, t[u], o);
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = jl + 4 * u, jj = a + j;
+                    if (j < nj) {
+                        const bool vis = !(jj >= ss.tree_base && !((ss.mask >> (jj - ss.tree_base)) & 1ull));
+                        sc[j] = vis ? t[u] * p.scale : -INFINITY;
+                    }
                 }
             }
         }
         epi_sync();
         if (a == j0) stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
-        // softmax (online) and values: this warp's heads only, so the warp needs no CTA barrier
-        float corr[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int hh = warp + 4 * u;
-            corr[u] = 1.f;
-            if (hh >= G) continue;
-            const float sv = lane < nj ? sc[lane * kGroup + hh] : -INFINITY;
-            const float mx = warp_max(sv);
-            const float mnew = fmaxf(m_run[u], mx);
-            const float pe = mnew == -INFINITY ? 0.f : expf(sv - mnew);
-            const float ls = warp_sum(lane < nj ? pe : 0.f);
-            corr[u] = m_run[u] == -INFINITY ? 0.f : expf(m_run[u] - mnew);
-            l_run[u] = l_run[u] * corr[u] + ls;
-            m_run[u] = mnew;
-            if (lane < nj) sc[lane * kGroup + hh] = pe;
+        if (warp == 0) {                        // softmax statistics over the sub-chunk
+            const float v0 = lane < nj ? sc[lane] : -INFINITY;
+            const float v1 = lane + 32 < nj ? sc[lane + 32] : -INFINITY;
+            const float mnew = fmaxf(m_run, warp_max(fmaxf(v0, v1)));
+            const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
+            const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
+            const float ls = warp_sum((lane < nj ? p0 : 0.f) + (lane + 32 < nj ? p1 : 0.f));
+            const float corr = m_run == -INFINITY ? 0.f : expf(m_run - mnew);
+            l_run = l_run * corr + ls;
+            m_run = mnew;
+            if (lane < nj) sc[lane] = p0;
+            if (lane + 32 < nj) sc[lane + 32] = p1;
+            if (lane == 0) s_corr = corr;
         }
-        __syncwarp();
-        float part[2][2][DL];
+        epi_sync();
+        // values: warp w sums positions w, w + 4, ...; lane = DL output dims
+        float pa[DL];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-            for (int v = 0; v < 2; ++v)
-#pragma unroll
-                for (int i = 0; i < DL; ++i) part[u][v][i] = 0.f;
+        for (int i = 0; i < DL; ++i) pa[i] = 0.f;
         const uint8_t *vrow = am + L::vOff + lane * DL * 2;
-        const bool two = warp + 4 < G;
-        if (warp < G) {
-            int q = 0;
-            for (; q + 2 <= nj; q += 2) {
+        for (int j = warp; j < nj; j += 4) {
+            float vf[DL];
+            load_dims<DL>(vrow + (size_t)j * L::kRow, vf);
+            const float pj = sc[j];
 #pragma unroll
-                for (int v = 0; v < 2; ++v) {
-                    float vf[DL];
-                    load_dims<DL>(vrow + (size_t)(q + v) * L::kRow, vf);
-                    const float pa = sc[(q + v) * kGroup + warp];
-                    const float pb = two ? sc[(q + v) * kGroup + warp + 4] : 0.f;
-#pragma unroll
-                    for (int i = 0; i < DL; ++i) {
-                        part[0][v][i] = fmaf(pa, vf[i], part[0][v][i]);
-                        part[1][v][i] = fmaf(pb, vf[i], part[1][v][i]);
-                    }
-                }
-            }
-            if (q < nj) {
-                float vf[DL];
-                load_dims<DL>(vrow + (size_t)q * L::kRow, vf);
-                const float pa = sc[q * kGroup + warp];
-                const float pb = two ? sc[q * kGroup + warp + 4] : 0.f;
-#pragma unroll
-                for (int i = 0; i < DL; ++i) {
-                    part[0][0][i] = fmaf(pa, vf[i], part[0][0][i]);
-                    part[1][0][i] = fmaf(pb, vf[i], part[1][0][i]);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int i = 0; i < DL; ++i) acc[u][i] = fmaf(acc[u][i], corr[u], part[u][0][i] + part[u][1][i]);
+            for (int i = 0; i < DL; ++i) pa[i] = fmaf(pj, vf[i], pa[i]);
         }
+#pragma unroll
+        for (int i = 0; i < DL; ++i) rd[warp * HD + DL * lane + i] = pa[i];
+        epi_sync();
+        if (tid < HD) acc = fmaf(acc, s_corr, ((rd[tid] + rd[HD + tid]) + rd[2 * HD + tid]) + rd[3 * HD + tid]);
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
-    // publish this chunk's partial for each of this warp's heads
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int hh = warp + 4 * u;
-        if (hh >= G) continue;
-        const int h = g * G + hh;
-        float *dst = p.attn_acc + ((size_t)h * p.max_chunks + ch) * HD + DL * lane;
-#pragma unroll
-        for (int i = 0; i < DL; ++i) dst[i] = acc[u][i];
-        if (lane == 0) {
-            p.attn_ml[((size_t)h * p.max_chunks + ch) * 2] = m_run[u];
-            p.attn_ml[((size_t)h * p.max_chunks + ch) * 2 + 1] = l_run[u];
-        }
+    if (tid < HD) p.attn_acc[((size_t)h * p.max_chunks + ch) * HD + tid] = acc;
+    if (tid == 0) {
+        p.attn_ml[((size_t)h * p.max_chunks + ch) * 2] = m_run;
+        p.attn_ml[((size_t)h * p.max_chunks + ch) * 2 + 1] = l_run;
     }
 }
 
+// The last item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
+// w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), chunks in a fixed order. Thread d < HD loads a batch
+// of kMergeBatch chunks' (max, sum) pairs and acc_c[d] at once (one L2 round trip per batch; the
+// common case is a single batch) and folds it into a running (M, sum, acc) with rescaling.
+// The output is written as fp16 hi / lo vectors (the O projection's input, ready to copy).
+constexpr int kMergeBatch = 16;
 
-// The last attention item of kv head g merges the head's chunks: out[h][d] for the G q heads of
-// the group = sum_c w_c acc_c[d] with w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), in chunk order.
-// `scratch` (shared, >= 3 * kGroup * kStepMaxChunks floats) holds the per-(head, chunk) weights.
 template <int HD>
-__device__ void merge_group(const StepParams &p, int g, int n_chunks, float *scratch) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = p.nh / p.nkv;
-    float *wts = scratch;                                  // [G][n_chunks] weights
-    float2 *mls = reinterpret_cast<float2 *>(scratch + kGroup * kStepMaxChunks);   // [G][n_chunks] (max, sum)
-    for (int i = tid; i < G * n_chunks; i += kEpiThreads) {
-        const int hh = i / n_chunks, c = i - hh * n_chunks;
-        mls[i] = __ldcg(reinterpret_cast<const float2 *>(p.attn_ml + ((size_t)(g * G + hh) * p.max_chunks + c) * 2));
-    }
-    epi_sync();
-    for (int hh = warp; hh < G; hh += 4) {
-        float M = -INFINITY;
-        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, mls[hh * n_chunks + c].x);
-        M = warp_max(M);
-        float L = 0.f;
-        for (int c = lane; c < n_chunks; c += 32) {
-            const float2 ml = mls[hh * n_chunks + c];
-            L = fmaf(ml.y, ml.x == -INFINITY ? 0.f : expf(ml.x - M), L);
+__device__ void merge_head(const StepParams &p, int h, int n_chunks) {
+    const int tid = threadIdx.x;
+    if (tid >= HD) return;
+    const float2 *ml = reinterpret_cast<const float2 *>(p.attn_ml) + (size_t)h * p.max_chunks;
+    const float *ac = p.attn_acc + (size_t)h * p.max_chunks * HD + tid;
+    float M = -INFINITY, Ls = 0.f, A = 0.f;
+    for (int c0 = 0; c0 < n_chunks; c0 += kMergeBatch) {
+        float2 mc[kMergeBatch];
+        float av[kMergeBatch];
+#pragma unroll
+        for (int c = 0; c < kMergeBatch; ++c) {
+            mc[c] = make_float2(-INFINITY, 0.f);
+            av[c] = 0.f;
+            if (c0 + c < n_chunks) {
+                mc[c] = __ldcg(ml + c0 + c);
+                av[c] = __ldcg(ac + (size_t)(c0 + c) * HD);
+            }
         }
-        L = warp_sum(L);
-        for (int c = lane; c < n_chunks; c += 32) {
-            const float m = mls[hh * n_chunks + c].x;
-            wts[hh * n_chunks + c] = m == -INFINITY ? 0.f : expf(m - M) / L;
+        float Mb = M;
+#pragma unroll
+        for (int c = 0; c < kMergeBatch; ++c) Mb = fmaxf(Mb, mc[c].x);
+        if (Mb == -INFINITY) continue;
+        const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+        Ls *= r;
+        A *= r;
+#pragma unroll
+        for (int c = 0; c < kMergeBatch; ++c) {
+            const float f = mc[c].x == -INFINITY ? 0.f : expf(mc[c].x - Mb);
+            Ls = fmaf(mc[c].y, f, Ls);
+            A = fmaf(av[c], f, A);
         }
+        M = Mb;
     }
-    epi_sync();
-    // four outputs per thread and step, up to 16 chunks' loads in flight
-    for (int e4 = tid; e4 < G * HD / 4; e4 += kEpiThreads) {
-        const int e = 4 * e4, hh = e / HD, d = e - hh * HD, h = g * G + hh;
-        const float *ac = p.attn_acc + (size_t)h * p.max_chunks * HD + d;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 16
-        for (int c = 0; c < n_chunks; ++c) {
-            const float w = wts[hh * n_chunks + c];
-            const float4 a = ldcg4(ac + (size_t)c * HD);
-            A.x = fmaf(w, a.x, A.x);
-            A.y = fmaf(w, a.y, A.y);
-            A.z = fmaf(w, a.z, A.z);
-            A.w = fmaf(w, a.w, A.w);
-        }
-        *reinterpret_cast<float4 *>(p.attn_out + (size_t)h * HD + d) = A;
-    }
+    const float o = A / Ls;
+    const __half hi = __float2half_rn(o);
+    p.attn_h[(size_t)h * HD + tid] = hi;
+    p.attn_l[(size_t)h * HD + tid] = __float2half_rn(o - __half2float(hi));
 }
 
 }  // namespace
@@ -623,22 +557,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             const StepOp &op = ops[k];
             stamp(p.trace, k, C, c, 0);
             if (op.kind == OP_ATTN) {
-                // items on the last CTAs (the first ones own the first rows of every GEMV), so
-                // they stage their K/V rows early
-                const int items = p.nkv * n_chunks, item = C - 1 - c;
+                // items on the last CTAs: (q head, context chunk), one per CTA
+                const int items = p.nh * n_chunks, item = C - 1 - c;
                 if (item < items && !ab.on()) {
                     attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
-                    const int g = item / n_chunks;
+                    const int h = item / n_chunks;
                     epi_sync();
-                    if (tid == 0) s_flag = atom_add_acq_rel(p.grp_cnt + g, 1u) == (unsigned)(n_chunks - 1);
+                    if (tid == 0) s_flag = atom_add_acq_rel(p.grp_cnt + h, 1u) == (unsigned)(n_chunks - 1);
                     epi_sync();
                     if (s_flag) {      // the head's last chunk: merge all of them
                         stamp(p.trace, k, C, c, 6);
-                        merge_group<HD>(p, g, n_chunks, reinterpret_cast<float *>(am));
+                        merge_head<HD>(p, h, n_chunks);
                         epi_sync();
                         stamp(p.trace, k, C, c, 7);
                         if (tid == 0) {
-                            p.grp_cnt[g] = 0u;
+                            p.grp_cnt[h] = 0u;
                             if (op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
                         }
                     }
@@ -649,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             if (op.epi == EPI_QKV && k + 1 < p.n_ops && ops[k + 1].kind == OP_ATTN) {
                 // this CTA's attention item of the layer: stage its immutable K/V rows now
                 const int item = C - 1 - c;
-                if (item < p.nkv * n_chunks)
+                if (item < p.nh * n_chunks)
                     attn_prestage<HD>(p, ops[k + 1], ss, am, item, n_chunks, rows_per, ctx);
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
@@ -697,8 +630,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                                                 (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w));
                 }
             } else {
-                const float *src = op.pro == PRO_ATTN ? p.attn_out : op.xin;
-                for (int i = tid; i < K / 4; i += kEpiThreads) store_hilo4(xh, xl, 4 * i, ldcg4(src + 4 * i));
+                // the producer of this input wrote it as fp16 hi / lo vectors: copy them
+                const __half *sh = op.pro == PRO_ATTN ? p.attn_h : op.xin_h;
+                const __half *sl = op.pro == PRO_ATTN ? p.attn_l : op.xin_l;
+                for (int i = tid; i < K / 8; i += kEpiThreads) {
+                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(sh) + i);
+                    const uint4 lv = __ldcg(reinterpret_cast<const uint4 *>(sl) + i);
+                    reinterpret_cast<uint4 *>(xh)[i] = hv;
+                    reinterpret_cast<uint4 *>(xl)[i] = lv;
+                }
             }
             epi_sync();
             stamp(p.trace, k, C, c, 2);
@@ -803,7 +743,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         }
                     }
                 } else if (op.epi == EPI_SWIGLU) {
-                    op.out[row / 2] = (y0 / (1.0f + expf(-y0))) * y1;
+                    const float a = (y0 / (1.0f + expf(-y0))) * y1;
+                    const __half ah = __float2half_rn(a);
+                    op.out_h[row / 2] = ah;
+                    op.out_l[row / 2] = __float2half_rn(a - __half2float(ah));
                 } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
                     const int P2 = row / 2;
                     const int hh = P2 / half_hd, dd = P2 - hh * half_hd;
@@ -1026,7 +969,7 @@ cudaError_t prepare_step(int hd, size_t smem) {
 }
 
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    if (p.stages < 2 || p.nh / p.nkv > kGroup || p.nkv * p.max_chunks > grid || p.max_chunks > kStepMaxChunks)
+    if (p.stages < 2 || p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks)
         return cudaErrorInvalidValue;
     if (hd == 128) return step_launch_t<128>(&p, grid, smem, s, pdl);
     if (hd == 64) return step_launch_t<64>(&p, grid, smem, s, pdl);
