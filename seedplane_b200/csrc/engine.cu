@@ -105,14 +105,17 @@ struct sp_engine {
     // persistent step kernel (default; SEEDPLANE_STEP=chain selects the kernel-per-op chain)
     bool step_kernel = true;
     StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (row blocks)
-    int step_stages = 0, step_xmax = 0, step_max_chunks = 0;
-    size_t step_smem = 0;
+    StepLayout step_lay{};                  // shared memory of the step kernel
+    int step_xmax = 0, step_max_chunks = 0;
+    int step_inflight = 0;                  // ring copies in flight at most (0: all stages)
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
     int n_cnt = 0;
-    float *attn_ml = nullptr, *attn_acc = nullptr;
-    __half *attn_h = nullptr, *attn_l = nullptr, *act_h = nullptr, *act_l = nullptr;
-    unsigned *grp_cnt = nullptr;
+    // step hand-offs, two of each (layer parity): LL words of the residual stream after O (xo) and
+    // after down (xd), q, the new K/V rows, attention partials and output; the SwiGLU activation
+    uint64_t *ll_xo = nullptr, *ll_xd = nullptr, *ll_q = nullptr, *ll_kv = nullptr, *ll_part = nullptr,
+             *ll_attn = nullptr;
+    __half *act_h = nullptr, *act_l = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
     unsigned long long *step_trace = nullptr;
@@ -180,36 +183,40 @@ cudaError_t launch_any_gemv(sp_engine *e, int which, int pro, int epi, const Gem
     return launch_tc_from(e, *plans[which], pro, epi, g, lc);
 }
 
-// The step's op table for one cache: per layer QKV, attention, O, gate_up, down; then the LM head.
-// Counter 5l+0: QKV strips finished, +1: attention (one per CTA), +2: O strips, +3: gate_up
-// strips, +4: down strips (the residual x of layer l+1 is complete).
+// The step's op table for one cache: per layer QKV, attention, O, gate_up, down (ops 5l .. 5l + 4);
+// then the LM head. Layer l uses hand-off buffers of parity l & 1; the residual stream the QKV
+// projection and the LM head read is the previous down projection's output. Counter 5l + 3
+// counts the gate_up CTAs of layer l (the only counted hand-off).
 std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
     const sp_config &c = e->c;
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
-    const int H = c.hidden, I = c.intermediate, QR = (c.heads + 2 * c.kv_heads) * c.head_dim;
-    const int grid = e->num_sms;
+    const size_t H = c.hidden, I = c.intermediate, HD = c.head_dim;
+    const size_t nq = (size_t)c.heads * HD, nkv = (size_t)c.kv_heads * HD;
+    const size_t npart = (size_t)c.heads * e->step_max_chunks * (HD + 2);
     std::vector<StepOp> ops;
-    auto gemv = [&](const StepOp &plan, const uint8_t *w, int pro, int epi, int dep, int dep_n, int sig) {
+    auto gemv = [&](const StepOp &plan, const uint8_t *w, int pro, int epi) {
         StepOp o = plan;
         o.kind = OP_GEMV;
         o.w = w;
         o.pro = pro;
         o.epi = epi;
-        o.dep = dep;
-        o.dep_n = dep_n;
-        o.sig = sig;
+        o.dep = -1;
+        o.sig = -1;
         return o;
     };
-    // signals per step: one per CTA owning rows of a GEMV, one per kv head for attention
     for (int l = 0; l < c.layers; ++l) {
         const LayerDev &L = e->layers[l];
+        const int par = l & 1, prev = par ^ 1;
         __half *kc = kv->k + l * kv_layer, *vc = kv->v + l * kv_layer;
-        StepOp o = gemv(e->s_qkv, L.qkv, l == 0 ? PRO_EMBED_NORM : PRO_NORM, EPI_QKV, l == 0 ? -1 : 5 * (l - 1) + 4,
-                        e->s_down.grid, 5 * l + 0);
-        o.xin = e->x;
+        StepOp o = gemv(e->s_qkv, L.qkv, l == 0 ? PRO_EMBED_NORM : PRO_NORM, EPI_QKV);
+        if (l > 0) {
+            o.lin = e->ll_xd + prev * H;
+            o.lin_k = 5 * (l - 1) + 4;
+        }
         o.gain = L.in_norm;
         o.bias = L.qkv_b;
-        o.out = e->q;
+        o.lout = e->ll_q + par * nq;
+        o.lkv = e->ll_kv + par * nkv;
         o.kc = kc;
         o.vc = vc;
         ops.push_back(o);
@@ -217,28 +224,44 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         a.kind = OP_ATTN;
         a.kc = kc;
         a.vc = vc;
-        a.dep = 5 * l + 0;
-        a.dep_n = e->s_qkv.grid;
-        a.sig = 5 * l + 1;
+        a.lin = e->ll_q + par * nq;
+        a.lin_k = 5 * l;
+        a.lkv = e->ll_kv + par * nkv;
+        a.lpart = e->ll_part + par * npart;
+        a.lout = e->ll_attn + par * nq;
+        a.dep = -1;
+        a.sig = -1;
         ops.push_back(a);
-        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID, 5 * l + 1, c.heads, 5 * l + 2);
-        o.out = e->x;
-        o.resid_embed = l == 0;
+        o = gemv(e->s_o, L.o, PRO_ATTN, EPI_RESID);
+        o.lin = e->ll_attn + par * nq;
+        o.lin_k = 5 * l + 1;
+        if (l > 0) {                       // layer 0: the residual base is the token's embedding row
+            o.lres = e->ll_xd + prev * H;
+            o.lres_k = 5 * (l - 1) + 4;
+        }
+        o.lout = e->ll_xo + par * H;
         ops.push_back(o);
-        o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU, 5 * l + 2, e->s_o.grid, 5 * l + 3);
-        o.xin = e->x;
+        o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU);
+        o.lin = e->ll_xo + par * H;
+        o.lin_k = 5 * l + 2;
         o.gain = L.post_norm;
-        o.out_h = e->act_h;
-        o.out_l = e->act_l;
+        o.out_h = e->act_h + par * 2 * I;
+        o.out_l = e->act_l + par * 2 * I;
+        o.sig = 5 * l + 3;
         ops.push_back(o);
-        o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID, 5 * l + 3, e->s_gu.grid, 5 * l + 4);
-        o.xin_h = e->act_h;
-        o.xin_l = e->act_l;
-        o.out = e->x;
+        o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID);
+        o.xin_h = e->act_h + par * 2 * I;
+        o.xin_l = e->act_l + par * 2 * I;
+        o.dep = 5 * l + 3;
+        o.dep_n = e->s_gu.grid;
+        o.lres = e->ll_xo + par * H;
+        o.lres_k = 5 * l + 2;
+        o.lout = e->ll_xd + par * H;
         ops.push_back(o);
     }
-    StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD, 5 * (c.layers - 1) + 4, e->s_down.grid, -1);
-    o.xin = e->x;
+    StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD);
+    o.lin = e->ll_xd + ((c.layers - 1) & 1) * H;
+    o.lin_k = 5 * (c.layers - 1) + 4;
     o.gain = e->final_norm;
     ops.push_back(o);
     return ops;
@@ -273,8 +296,10 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         StepParams p{};
         p.ops = ops;
         p.n_ops = e->n_step_ops;
-        p.stages = e->step_stages;
-        p.xmax = e->step_xmax;
+        p.stages = e->step_lay.stages;
+        p.stage_bytes = e->step_lay.stage_bytes;
+        p.vec_bytes = e->step_lay.vec_bytes;
+        p.attn_off = e->step_lay.attn_off;
         p.nh = c.heads;
         p.nkv = c.kv_heads;
         p.hd = c.head_dim;
@@ -284,16 +309,11 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.hidden = c.hidden;
         p.max_chunks = e->step_max_chunks;
         p.evict_first = e->evict_first ? 1 : 0;
+        p.max_inflight = e->step_inflight;
         p.eps = c.rms_norm_eps;
         p.scale = 1.0f / sqrtf((float)c.head_dim);
         p.rope = e->rope;
         p.embed = e->embed;
-        p.q = e->q;
-        p.attn_ml = e->attn_ml;
-        p.attn_acc = e->attn_acc;
-        p.attn_h = e->attn_h;
-        p.attn_l = e->attn_l;
-        p.grp_cnt = e->grp_cnt;
         p.part_val = e->lm_val;
         p.part_idx = e->lm_idx;
         p.lm_cnt = e->lm_cnt;
@@ -301,7 +321,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.epoch = e->epoch;
         p.st = e->st;
         p.trace = e->step_trace;
-        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_smem, s, e->pdl));
+        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_lay.smem, s, e->pdl));
         return SP_OK;
     }
     int kidx = 0;       // GEMV index within the step (trace slot)
@@ -503,7 +523,18 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t padq = e->step_kernel ? rowpad : 1;
     const size_t QRp = align_up(QR, padq), Hp = align_up(H, padq), GUp = align_up(2 * I, padq);
     if (e->step_kernel) {
-        // row-block plans (the packing depends on them)
+        // shared-memory layout first (its stage size bounds the units), then the row-block plans
+        // (the packing depends on them)
+        e->step_xmax = (int)align_up(std::max({H, I, (size_t)c.heads * HD}), 8);
+        const int want = (int)env_long("SEEDPLANE_STEP_STAGES", 3);
+        e->step_inflight = (int)env_long("SEEDPLANE_STEP_INFLIGHT", 0);
+        e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, std::max(2, want));
+        if (e->step_lay.stage_bytes < 16 * 1024 && want > 2) e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, 2);
+        if (e->step_lay.stage_bytes < 16 * 1024) {
+            delete e;
+            return fail(SP_ERR_UNSUPPORTED, "step kernel: the input vector of %d floats leaves no room for the ring",
+                        e->step_xmax);
+        }
         auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro) {
             StepOp o{};
             o.kind = OP_GEMV;
@@ -511,7 +542,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             o.N = (int)N;
             o.K = (int)K;
             o.n_valid = (int)n_valid;
-            plan_step_gemv(o, e->num_sms);
+            plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes);
             return o;
         };
         e->s_qkv = sbase(QRp, H, QR, PRO_NORM);
@@ -520,7 +551,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->s_down = sbase(Hp, I, H, PRO_PLAIN);
         e->s_head = sbase(VP, H, V, PRO_NORM);
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            if (!step_gemv_supported(*o)) {
+            if (!step_gemv_supported(*o, e->step_lay.stage_bytes)) {
                 delete e;
                 return fail(SP_ERR_UNSUPPORTED, "step GEMV of N=%d K=%d is not supported", o->N, o->K);
             }
@@ -740,7 +771,11 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
     const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
-    const size_t w_grp = wtake((size_t)c.heads * 4);
+    // step hand-off words (a step after a device error must not see tags of the failed one)
+    const size_t n_part = (size_t)c.heads * e->step_max_chunks * (HD + 2);
+    const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
+    const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
+    const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
@@ -748,10 +783,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t lm_grid = std::max({(size_t)e->g_head.grid, (size_t)e->t_head.grid, (size_t)e->num_sms});
     const size_t w_lmval = wtake(lm_grid * 4), w_lmidx = wtake(lm_grid * 4);
     const size_t w_st = wtake(sizeof(DevState));
-    const size_t w_ml = wtake((size_t)c.heads * e->step_max_chunks * 2 * 4);
-    const size_t w_acc = wtake((size_t)c.heads * e->step_max_chunks * HD * 4);
-    const size_t w_aout = wtake((size_t)c.heads * HD * 4);
-    const size_t w_acth = wtake(I * 4);
+    const size_t w_acth = wtake(4 * I * 2);
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
@@ -768,13 +800,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->am = argmax_scratch_at(e->ws + w_am, kArgmaxChunkRows);
     e->cnt = (unsigned long long *)(e->ws + w_cnt);
     e->epoch = (unsigned long long *)(e->ws + w_epoch);
-    e->attn_ml = (float *)(e->ws + w_ml);
-    e->attn_acc = (float *)(e->ws + w_acc);
-    e->attn_h = (__half *)(e->ws + w_aout);
-    e->attn_l = e->attn_h + (size_t)c.heads * HD;
-    e->act_h = (__half *)(e->ws + w_acth);
+    e->ll_xo = (uint64_t *)(e->ws + w_llxo);
+    e->ll_xd = (uint64_t *)(e->ws + w_llxd);
+    e->ll_q = (uint64_t *)(e->ws + w_llq);
+    e->ll_kv = (uint64_t *)(e->ws + w_llkv);
+    e->ll_part = (uint64_t *)(e->ws + w_llpart);
+    e->ll_attn = (uint64_t *)(e->ws + w_llattn);
+    e->act_h = (__half *)(e->ws + w_acth);        // parity p: hi at [2p I, 2p I + I), lo right after
     e->act_l = e->act_h + I;
-    e->grp_cnt = (unsigned *)(e->ws + w_grp);
     e->g_head.w = e->head;
     e->g_head.part_val = e->lm_val;
     e->g_head.part_idx = e->lm_idx;
@@ -813,16 +846,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_LMHEAD, e->t_head));
     }
     if (e->step_kernel) {
-        e->step_xmax = (int)align_up(std::max(H, I), 4);
-        e->step_stages = step_stages_for(e->step_xmax, (int)HD, 5 * c.layers + 1);
-        if (e->step_stages < 2 || e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms)
-            return bail(fail(SP_ERR_UNSUPPORTED, "step kernel plan does not fit (input vector of %d floats, %d stages)",
-                             e->step_xmax, e->step_stages));
-        e->step_smem = step_smem_bytes(e->step_stages, e->step_xmax, (int)HD, 5 * c.layers + 1);
-        SP_TRY(prepare_step((int)HD, e->step_smem));
+        if (e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms)
+            return bail(fail(SP_ERR_UNSUPPORTED, "step kernel: %d q heads do not fit one attention item per CTA",
+                             c.heads));
+        SP_TRY(prepare_step((int)HD, e->step_lay.smem));
         if (env_flag("SEEDPLANE_VERBOSE", false))
-            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d xmax=%d smem=%zu max_chunks=%d\n", e->num_sms,
-                    e->step_stages, e->step_xmax, e->step_smem, e->step_max_chunks);
+            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d x %d B xmax=%d smem=%zu max_chunks=%d\n",
+                    e->num_sms, e->step_lay.stages, e->step_lay.stage_bytes, e->step_xmax, e->step_lay.smem,
+                    e->step_max_chunks);
     }
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (!e->tc && gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));

@@ -161,27 +161,32 @@ cudaError_t launch_kv_commit(__half *k, __half *v, int layers, int nkv, int cap,
 // ---- persistent decode step: step.cu -----------------------------------------------------------
 // One launch per token runs the whole step on one CTA per SM. The ops of the step (GEMVs with
 // fused prologues/epilogues, and attention) are a table in device memory. Every CTA owns whole
-// output rows of every GEMV (no split-K), streams all of its weight units through one ring
-// without waiting for data, and meets the other CTAs only through 64-bit dependency counters in
-// global memory: an op's consumers wait until its counter reaches units x (epoch + 1), where
-// `epoch` counts finished steps (advanced by the LM head's last CTA) and `units` is the number of
-// CTAs (GEMVs) or q heads (attention) that signal it once per step.
+// output rows of every GEMV (no split-K) and streams all of its weight units through one ring
+// without waiting for data. Vectors pass between ops as LL words (a 64-bit store of a 32-bit
+// payload and the 32-bit tag of the writing op and step, polled by the readers); the SwiGLU
+// activation passes through a 64-bit counter whose readers wait until it reaches CTAs x
+// (epoch + 1), where `epoch` counts finished steps (advanced by the LM head's last CTA).
 enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged attention output
-constexpr int kStepAttnRows = 64;        // attention positions staged per sub-chunk
+constexpr int kStepAttnRows = 48;        // attention positions staged per sub-chunk
 constexpr int kStepMaxChunks = 64;       // attention chunks per q head
 constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
 constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, input ready, done,
-                                         // first unit available, rows finished
+                                         // first unit available, rows finished, merge start / end
 
 struct StepOp {
     const uint8_t *w;        // row-block packed weights (GEMV), see k_pack_rows
-    const float *xin;        // prologue input (PRO_NORM): fp32 vector
-    const __half *xin_h, *xin_l;   // prologue input (PRO_PLAIN): fp16 hi / lo vectors
+    const uint64_t *lin;     // LL input: the residual stream (norm prologues), the merged attention
+                             // output (PRO_ATTN), q (attention)
+    const uint64_t *lres;    // EPI_RESID: LL residual base; null: the token's embedding row
+    uint64_t *lout;          // LL output: q (QKV), the residual stream (EPI_RESID), the merged
+                             // attention output (attention)
+    uint64_t *lkv;           // QKV / attention: the step's new K/V rows, [nkv][k | v][hd / 2] fp16 pairs
+    uint64_t *lpart;         // attention: per (q head, chunk) partials [nh][max_chunks][hd + 2]
+    const __half *xin_h, *xin_l;   // PRO_PLAIN input: fp16 hi / lo vectors behind counter `dep`
+    __half *out_h, *out_l;   // EPI_SWIGLU output: fp16 hi / lo vectors
     const float *gain;       // RMSNorm gains
     const float *bias;       // QKV bias
-    float *out;              // epilogue output (q / x)
-    __half *out_h, *out_l;   // EPI_SWIGLU output as fp16 hi / lo vectors
     __half *kc, *vc;         // this layer's K/V cache (QKV epilogue, attention)
     int kind;                // StepOpKind
     int pro, epi;
@@ -189,29 +194,27 @@ struct StepOp {
     int grid;                // CTAs owning rows: CTA c owns pairs [P c / grid, P (c + 1) / grid)
     int pass_rows;           // rows per pass (even, <= kStepPassRows)
     int chunk_w;             // inputs per unit (multiple of 256, or all of K)
+    int lin_k, lres_k;       // ops whose tags lin / lres carry
     int dep, dep_n;          // wait until cnt[dep] >= dep_n * (epoch + 1); dep < 0: none
-    int sig;                 // cnt[sig] += 1 per CTA (GEMV) / per q head (attention); < 0: none
-    int resid_embed;         // EPI_RESID: the residual base is the token's embedding row
-    int pad_[1];
+    int sig;                 // cnt[sig] += 1 per CTA; < 0: none
+    int pad_[2];
 };
-static_assert(sizeof(StepOp) % 16 == 0, "the op table is copied to shared memory in 16-byte words");
+static_assert(sizeof(StepOp) % 16 == 0, "ops are copied to shared memory in 16-byte words");
 
 struct StepParams {
     const StepOp *ops;
     int n_ops;
-    int stages;              // ring stages of 64 KB
-    int xmax;                // floats of the shared input vector (largest K, multiple of 4)
+    int stages;              // ring stages
+    int stage_bytes;         // bytes per stage (multiple of 1024, <= 64 KB)
+    int vec_bytes;           // shared input-vector region (GEMV input halves, attention staging)
+    int attn_off;            // attention staging offset in it (after the QKV projection's input)
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
     int max_chunks;          // attention chunks per q head at most (nh * max_chunks <= grid)
     int evict_first;         // ring copies carry an L2 evict-first hint
+    int max_inflight;        // ring copies in flight at most (0: stages)
     float eps, scale;
     const float *rope;
     const __half *embed;
-    float *q;                // [nh * hd] fp32 (RoPE applied)
-    float *attn_ml;          // [nh][max_chunks][2]  (running max, sum) per attention chunk
-    float *attn_acc;         // [nh][max_chunks][hd] unnormalised outputs per chunk
-    __half *attn_h, *attn_l; // [nh * hd] merged attention output as fp16 hi / lo (the O projection's input)
-    unsigned *grp_cnt;       // [nh] attention chunks finished per q head (the last one merges)
     float *part_val;         // LM head: per-CTA argmax
     int *part_idx;
     unsigned *lm_cnt;
@@ -221,15 +224,20 @@ struct StepParams {
     unsigned long long *trace;   // [n_ops][grid][kStepTraceWords] or null
 };
 
-void plan_step_gemv(StepOp &o, int num_sms);     // fills grid, pass_rows, chunk_w from N, K
-bool step_gemv_supported(const StepOp &o);
+struct StepLayout {
+    int stages = 0, stage_bytes = 0, vec_bytes = 0, attn_off = 0;
+    size_t smem = 0;         // dynamic shared memory; stage_bytes == 0: does not fit
+};
+
+void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes);   // fills grid, pass_rows, chunk_w from N, K
+bool step_gemv_supported(const StepOp &o, int stage_bytes);
 // Pack an fp16 N x K matrix (packed row r = source row row_of[r] of a / b as in
 // launch_pack_fragments, < 0 = zero) into the plan's row-block layout.
 cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
                              const StepOp &plan, cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
-int step_stages_for(int xmax, int hd, int n_ops);
-size_t step_smem_bytes(int stages, int xmax, int hd, int n_ops);
+// xmax: the largest GEMV input (multiple of 8); hidden: the QKV projection's input.
+StepLayout step_layout(int hidden, int xmax, int hd, int stages);
 cudaError_t prepare_step(int hd, size_t smem);
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
 // resident at once (one CTA per SM), so the launch is cooperative.

@@ -1,32 +1,39 @@
 // Persistent decode step for sm_100a: one launch per token, one CTA per SM.
 //
 // The kernel walks the step's op table (per layer: QKV GEMV, attention, O GEMV, gate_up GEMV,
-// down GEMV; then the LM head). Batch-1 decode reads every weight once per token and is bound by
-// HBM bandwidth, so the GEMVs run on the CUDA cores from shared memory and the design is about
-// moving bytes and hiding latency:
+// down GEMV; then the LM head). Batch-1 decode reads every weight once per token; it is bound by
+// HBM bandwidth and by the latency of the hand-offs between ops, so the design is about moving
+// bytes and hiding latency:
 //
 //   rows       every CTA owns whole output rows of every GEMV (row pairs, so a RoPE pair or a
-//              gate/up pair stays in one warp): no split-K, no cross-CTA partial sums. Its rows
-//              are packed as units of (up to 64 rows) x (a chunk of the inputs), at most 64 KB each.
+//              gate/up pair stays in one thread): no split-K, no cross-CTA partial sums. Its rows
+//              are packed as units of (up to 64 rows) x (a chunk of the inputs), one ring stage
+//              at most.
 //   warp 4     (producer) streams ALL of the CTA's units of the step, op after op, through a
-//              ring of 64 KB stages with 1-D bulk copies (one copy per unit). It never waits for
-//              data, only for a free stage, so weights stream while the other warps wait for
-//              activations.
-//   warps 0-3  per GEMV op: wait on the op's dependency counter, build the fp32 input vector in
-//              shared memory (RMSNorm fused), then multiply each unit: lane = 8 consecutive
-//              inputs, warp = every fourth row pair, fp16 x fp32 -> fp32 FMA chains; per row pass a
-//              butterfly reduction leaves each row sum in a lane pair, which runs the epilogue
-//              (bias + RoPE + K/V write / residual add / SwiGLU / logits + argmax). Then one
-//              release-add on the op's counter.
-//              Attention: the first nkv * chunks CTAs from the top each compute one (kv head,
-//              context chunk) item and publish an unnormalised partial (max, sum, acc); the last
-//              item of a kv head merges the head's chunks (log-sum-exp, fixed order) into the
-//              attention output the O projection reads.
+//              ring of stages with 1-D bulk copies (one copy per unit). It never waits for data,
+//              only for a free stage, so weights stream while the other warps wait for
+//              activations; it starts while the previous step is still finishing (programmatic
+//              dependent launch).
+//   warps 0-3  per GEMV op: build the input vector in shared memory as fp16 hi / lo halves
+//              (RMSNorm fused), multiply each unit on the tensor cores (mma.sync m16n8k16:
+//              A = 16 weight rows from the swizzled unit, B = the hi / lo columns), add up the
+//              four warps' k-step partials in shared memory and run the pair epilogue (bias +
+//              RoPE + K/V write / residual add / SwiGLU / logits + argmax).
+//              Attention: the last nh * chunks CTAs each compute one (q head, context chunk)
+//              item and publish an unnormalised partial (max, sum, acc); the chunk-0 item of a
+//              head merges the head's chunks (log-sum-exp, fixed order).
 //
-// Counters are 64-bit and never reset: an op's consumers wait for units * (epoch + 1). All data
-// another CTA produced is read through L2 (ld.global.cg / cp.async.cg), never from L1. Every
-// wait is bounded; on expiry the CTA records an error in DevState::err, sets its abort flag and
-// runs to the end without waiting again, so the kernel always terminates.
+// Hand-offs. The vectors that the CTAs of the next op read (the residual stream x, q, the new
+// K/V rows, attention partials and the attention output) are LL words: one 64-bit store carries
+// a 32-bit payload and the 32-bit tag of the writing op and step. A reader polls the words
+// themselves until every tag matches, so a hand-off costs about one L2 round trip and no fence.
+// The SwiGLU activation (the largest vector, read whole by every down-projection CTA) is plain
+// fp16 hi / lo published through a 64-bit counter: its writers meet at a barrier, one thread
+// release-adds, a reader acquires. Counters never reset: the target is CTAs x (epoch + 1), where
+// the epoch counts finished steps (advanced by the LM head's last CTA). Buffers alternate by
+// layer parity. All data another CTA produced is read through L2. Every wait is bounded; on
+// expiry the CTA records an error in DevState::err, sets its abort flag and runs to the end
+// without waiting again, so the kernel always terminates.
 #include <algorithm>
 #include <climits>
 #include <cmath>
@@ -40,12 +47,16 @@ namespace {
 constexpr int kEpiThreads = 128;            // warps 0-3: compute, epilogues, attention
 constexpr int kProducerWarp = 4;
 constexpr int kThreads = kEpiThreads + 32;
-constexpr int kStageBytes = 64 * 1024;      // one unit per stage (a bulk copy costs about the same
+constexpr int kMaxStageBytes = 64 * 1024;   // one unit per stage (a bulk copy costs about the same
                                             // time whatever its size, so big ones ingest faster)
 constexpr int kPassRows = kStepPassRows;    // rows per pass: 16 per warp
 constexpr int kGroup = 8;                   // q heads per kv head at most
 constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
+constexpr int kLLBatch = 7;                 // LL word pairs per thread in flight (plain prologues, merge)
+constexpr int kMergeBatch = 32;            // attention chunks merged per batch (staged in shared memory)
 constexpr uint32_t kDepSpinLimit = 1u << 22;
+constexpr int kOpWords = (int)(sizeof(StepOp) / 16);
+static_assert(kLLBatch <= 32, "poll masks are 32-bit");
 
 SP_DEVINL void ldmatrix_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -205,6 +216,115 @@ SP_DEVINL bool wait_counter(const unsigned long long *cnt, unsigned long long ta
     return false;
 }
 
+// ---- LL words: (payload, tag) in one single-copy-atomic 64-bit store -------------------------
+// Tag of the words op k writes in the step of `epoch`: never 0 (zeroed buffers never match) and
+// different for every op of the last 2^31 / n_ops steps.
+SP_DEVINL uint32_t ll_tag(unsigned long long epoch, int n_ops, int k) {
+    return 0x80000000u | (((uint32_t)epoch * (uint32_t)n_ops + (uint32_t)k) & 0x7fffffffu);
+}
+SP_DEVINL uint64_t ll_word(uint32_t payload, uint32_t tag) { return ((uint64_t)tag << 32) | payload; }
+SP_DEVINL uint64_t ll_wordf(float v, uint32_t tag) { return ll_word(__float_as_uint(v), tag); }
+SP_DEVINL float ll_f(uint64_t w) { return __uint_as_float((uint32_t)w); }
+SP_DEVINL bool ll_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+SP_DEVINL void ll_st1(uint64_t *p, uint64_t a) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+SP_DEVINL void ll_st2(uint64_t *p, uint64_t a, uint64_t b) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+SP_DEVINL void ll_ld2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
+}
+// fp16 hi = fp16(x) in the low half, lo = fp16(x - hi) in the high half
+SP_DEVINL uint32_t hilo_bits(float x) {
+    const __half h = __float2half_rn(x);
+    const __half l = __float2half_rn(x - __half2float(h));
+    return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+}
+SP_DEVINL uint32_t half2_bits(float a, float b) {
+    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+
+// Polls the word pairs j < N with bit j of `valid` set (pair j at addr(j), 16-byte aligned) until
+// both words of every pair carry `tag`; the words are left in w. Every round re-loads all pending
+// pairs at once (the pairs of one thread come from different writers), so the poll ends about
+// one round trip after the last writer's words land. Bounded; false when the CTA aborts.
+template <int N, typename Addr>
+SP_DEVINL bool ll_poll(uint64_t (&w)[N][2], uint32_t valid, Addr addr, uint32_t tag, const Abort &ab) {
+    uint32_t pend = valid, todo = valid;
+    for (uint32_t it = 0; pend != 0u; ++it) {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if ((todo >> j) & 1u) ll_ld2(addr(j), w[j][0], w[j][1]);
+        uint32_t got = 0u;
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (((todo >> j) & 1u) && ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag)) got |= 1u << j;
+        pend &= ~got;
+        todo = pend;
+        if ((it & 63u) == 63u && pend != 0u) {
+            if (ab.on() || *reinterpret_cast<volatile int *>(&ab.st->err) != 0) {
+                *ab.flag = 1;
+                return false;
+            }
+            if (it >= kDepSpinLimit) {
+                ab.raise(kErrDepTimeout);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Prologue input of a norm op: this thread's float4s q of the residual stream (elements
+// 4 (tid + q kEpiThreads) ..., K <= 4 x kNormRegs x kEpiThreads) from LL words, kNormRound
+// float4s (2 kNormRound word pairs) per round trip.
+constexpr int kNormRound = 3;
+SP_DEVINL bool ll_norm_input(float4 (&v)[kNormRegs], const uint64_t *lin, int K, uint32_t tag, const Abort &ab) {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int q0 = 0; q0 < kNormRegs; q0 += kNormRound) {
+        if (4 * (tid + q0 * kEpiThreads) >= K) break;
+        uint64_t w[2 * kNormRound][2];
+        uint32_t valid = 0u;
+#pragma unroll
+        for (int j = 0; j < 2 * kNormRound; ++j)
+            if (q0 + (j >> 1) < kNormRegs && 4 * (tid + (q0 + (j >> 1)) * kEpiThreads) < K) valid |= 1u << j;
+        if (!ll_poll<2 * kNormRound>(
+                w, valid, [&](int j) { return lin + 4 * (tid + (q0 + (j >> 1)) * kEpiThreads) + 2 * (j & 1); }, tag, ab))
+            return false;
+#pragma unroll
+        for (int q = 0; q < kNormRound; ++q)
+            if (q0 + q < kNormRegs)
+                v[q0 + q] = make_float4(ll_f(w[2 * q][0]), ll_f(w[2 * q][1]), ll_f(w[2 * q + 1][0]), ll_f(w[2 * q + 1][1]));
+    }
+    return true;
+}
+
+// Prologue input of the O projection: the merged attention output, LL words whose payload is the
+// fp16 hi / lo pair, into the shared hi / lo vectors.
+SP_DEVINL void ll_hilo_input(__half *xh, __half *xl, const uint64_t *lin, int K, uint32_t tag,
+                                           const Abort &ab) {
+    const int tid = threadIdx.x;
+    for (int b0 = 0; b0 < K; b0 += 2 * kEpiThreads * kLLBatch) {
+        uint64_t w[kLLBatch][2];
+        uint32_t valid = 0u;
+#pragma unroll
+        for (int j = 0; j < kLLBatch; ++j)
+            if (b0 + 2 * (tid + j * kEpiThreads) < K) valid |= 1u << j;
+        if (!ll_poll<kLLBatch>(w, valid, [&](int j) { return lin + b0 + 2 * (tid + j * kEpiThreads); }, tag, ab)) return;
+#pragma unroll
+        for (int j = 0; j < kLLBatch; ++j) {
+            if ((valid >> j) & 1u) {
+                const int e = b0 + 2 * (tid + j * kEpiThreads);
+                const uint32_t u0 = (uint32_t)w[j][0], u1 = (uint32_t)w[j][1];
+                *reinterpret_cast<uint32_t *>(xh + e) = (u0 & 0xffffu) | (u1 << 16);
+                *reinterpret_cast<uint32_t *>(xl + e) = (u0 >> 16) | (u1 & 0xffff0000u);
+            }
+        }
+    }
+}
+
 // Attention staging region of one (q head, chunk) item: K and V rows of one sub-chunk (fp16), the
 // scores, q (fp32) and the four warps' value sums.
 template <int HD>
@@ -249,8 +369,7 @@ SP_DEVINL void load_dims(const uint8_t *q, float (&f)[DL]) {
     }
 }
 
-// Attention chunking of the visible context [0, ctx): the same in the attention op and in the
-// O projection's merge.
+// Attention chunking of the visible context [0, ctx), the same in every CTA.
 SP_DEVINL int attn_chunks(int ctx, int max_chunks) {
     return max(1, min(max_chunks, (ctx + kStepAttnRows - 1) / kStepAttnRows));
 }
@@ -258,8 +377,6 @@ SP_DEVINL int attn_chunks(int ctx, int max_chunks) {
 SP_DEVINL void stamp(unsigned long long *tr, int k, int C, int c, int i) {
     if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + i] = globaltimer();
 }
-
-
 
 // Per-step values every epilogue thread reads once (after the dependency on the previous step).
 struct StepState {
@@ -270,15 +387,16 @@ struct StepState {
 
 // ---- attention item of one CTA: (q head h, context chunk ch) -----------------------------------
 // Staging that does not depend on the step: the first sub-chunk's K/V rows other than the current
-// one (only the step's QKV projection writes row `slot`). Issued before the QKV projection's wait.
+// one (only the step's QKV projection writes row `slot`). Issued before the QKV projection's
+// input is ready; `qkv` is that projection's op (same layer caches).
 template <int HD>
-__device__ void attn_prestage(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
+__device__ void attn_prestage(const StepParams &p, const StepOp &qkv, const StepState &ss, uint8_t *am, int item,
                               int n_chunks, int rows_per, int ctx) {
     const int G = p.nh / p.nkv;
     const int h = item / n_chunks, ch = item - h * n_chunks, g = h / G;
     const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
     const int s1 = min(j1, j0 + kStepAttnRows);
-    stage_rows<HD>(am, op.kc + (size_t)g * p.cap * HD, op.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot),
+    stage_rows<HD>(am, qkv.kc + (size_t)g * p.cap * HD, qkv.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot),
                    threadIdx.x);
     cp_async_commit();
 }
@@ -288,7 +406,7 @@ __device__ void attn_prestage(const StepParams &p, const StepOp &op, const StepS
 //   softmax one warp, running max / sum across sub-chunks (fp32)
 //   values  warp = every fourth position, lane = HD/32 dims; the four warps' sums meet in shared
 //           memory and thread t < HD keeps output dim t
-// Publishes the chunk's unnormalised partial (max, sum, acc[HD]).
+// Publishes the chunk's unnormalised partial (max, sum, acc[HD]) as LL words.
 template <int HD>
 __device__ void attention_item(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
                                int n_chunks, int rows_per, int ctx, const Abort &ab, int k) {
@@ -306,12 +424,31 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     __shared__ float s_corr;
     const int slot = ss.slot;
     const int s1 = min(j1, j0 + kStepAttnRows);
-    if (tid == 0 && op.dep >= 0) wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
-    epi_sync();
-    stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
-    if (slot >= j0 && slot < s1) stage_rows<HD>(am, kb, vb, j0, slot, slot + 1, tid);
-    for (int i = tid; i < HD / 4; i += kEpiThreads) cp_async16(qs + 4 * i, p.q + (size_t)h * HD + 4 * i);
-    cp_async_commit();
+    {
+        // q of the head and, when the first sub-chunk holds the step's position, its new K / V
+        // row: LL words of the QKV projection (thread t < HD / 2: one pair of each)
+        const bool cur = slot >= j0 && slot < s1;
+        const uint64_t *qw = op.lin + (size_t)h * HD + 2 * tid;
+        const uint64_t *kw = op.lkv + (size_t)g * HD + 2 * tid;
+        uint64_t w[2][2];
+        const uint32_t valid = tid < HD / 2 ? (cur ? 3u : 1u) : 0u;
+        ll_poll<2>(w, valid, [&](int j) { return j == 0 ? qw : kw; }, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
+        stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
+        if (tid < HD / 2) {
+            qs[2 * tid] = ll_f(w[0][0]);
+            qs[2 * tid + 1] = ll_f(w[0][1]);
+            if (cur) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int i = 2 * tid + e, which = i / (HD / 2), dd = i - which * (HD / 2);
+                    __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)(slot - j0) * L::kRow);
+                    const uint32_t u = (uint32_t)w[1][e];
+                    row[dd] = __ushort_as_half((unsigned short)(u & 0xffffu));
+                    row[dd + HD / 2] = __ushort_as_half((unsigned short)(u >> 16));
+                }
+            }
+        }
+    }
     cp_async_wait_all();
     epi_sync();
     stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
@@ -399,58 +536,69 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
         if (tid < HD) acc = fmaf(acc, s_corr, ((rd[tid] + rd[HD + tid]) + rd[2 * HD + tid]) + rd[3 * HD + tid]);
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
-    if (tid < HD) p.attn_acc[((size_t)h * p.max_chunks + ch) * HD + tid] = acc;
-    if (tid == 0) {
-        p.attn_ml[((size_t)h * p.max_chunks + ch) * 2] = m_run;
-        p.attn_ml[((size_t)h * p.max_chunks + ch) * 2 + 1] = l_run;
-    }
+    uint64_t *pw = op.lpart + ((size_t)h * p.max_chunks + ch) * (HD + 2);
+    const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
+    if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc, tag));
+    if (tid == 0) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
 }
 
-// The last item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
-// w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), chunks in a fixed order. Thread d < HD loads a batch
-// of kMergeBatch chunks' (max, sum) pairs and acc_c[d] at once (one L2 round trip per batch; the
-// common case is a single batch) and folds it into a running (M, sum, acc) with rescaling.
-// The output is written as fp16 hi / lo vectors (the O projection's input, ready to copy).
-constexpr int kMergeBatch = 16;
-
+// The chunk-0 item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
+// w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), chunks in a fixed order. In batches of up to
+// kMergeBatch chunks, all epilogue threads poll the batch's LL words (max, sum, acc[HD] per
+// chunk; one round trip) into the free K staging rows, then thread d < HD folds the batch into a
+// running (M, sum, acc[d]). The output goes out as LL words whose payload is the fp16 hi / lo pair
+// the O projection multiplies.
 template <int HD>
-__device__ void merge_head(const StepParams &p, int h, int n_chunks) {
+__device__ void merge_head(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int h,
+                           int n_chunks, int k, const Abort &ab) {
+    using L = AttnRegion<HD>;
+    constexpr int kW = HD + 2;                  // words per chunk
     const int tid = threadIdx.x;
-    if (tid >= HD) return;
-    const float2 *ml = reinterpret_cast<const float2 *>(p.attn_ml) + (size_t)h * p.max_chunks;
-    const float *ac = p.attn_acc + (size_t)h * p.max_chunks * HD + tid;
+    const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
+    const uint64_t *base = op.lpart + (size_t)h * p.max_chunks * kW;
+    static_assert((size_t)kMergeBatch * kW * 4 <= L::sOff, "a merge batch fits the K/V staging rows");
+    float *mp = reinterpret_cast<float *>(am + L::kOff);
     float M = -INFINITY, Ls = 0.f, A = 0.f;
     for (int c0 = 0; c0 < n_chunks; c0 += kMergeBatch) {
-        float2 mc[kMergeBatch];
-        float av[kMergeBatch];
+        const int nc = min(kMergeBatch, n_chunks - c0);
+        const int nw = nc * kW;                 // even
+        const uint64_t *bw = base + (size_t)c0 * kW;
+        for (int b0 = 0; b0 < nw; b0 += 2 * kEpiThreads * kLLBatch) {
+            uint64_t w[kLLBatch][2];
+            uint32_t valid = 0u;
 #pragma unroll
-        for (int c = 0; c < kMergeBatch; ++c) {
-            mc[c] = make_float2(-INFINITY, 0.f);
-            av[c] = 0.f;
-            if (c0 + c < n_chunks) {
-                mc[c] = __ldcg(ml + c0 + c);
-                av[c] = __ldcg(ac + (size_t)(c0 + c) * HD);
+            for (int j = 0; j < kLLBatch; ++j)
+                if (b0 + 2 * (tid + j * kEpiThreads) < nw) valid |= 1u << j;
+            if (!ll_poll<kLLBatch>(w, valid, [&](int j) { return bw + b0 + 2 * (tid + j * kEpiThreads); }, tag, ab))
+                return;
+#pragma unroll
+            for (int j = 0; j < kLLBatch; ++j) {
+                if ((valid >> j) & 1u) {
+                    const int e = b0 + 2 * (tid + j * kEpiThreads);
+                    *reinterpret_cast<float2 *>(mp + e) = make_float2(ll_f(w[j][0]), ll_f(w[j][1]));
+                }
             }
         }
-        float Mb = M;
-#pragma unroll
-        for (int c = 0; c < kMergeBatch; ++c) Mb = fmaxf(Mb, mc[c].x);
-        if (Mb == -INFINITY) continue;
-        const float r = M == -INFINITY ? 0.f : expf(M - Mb);
-        Ls *= r;
-        A *= r;
-#pragma unroll
-        for (int c = 0; c < kMergeBatch; ++c) {
-            const float f = mc[c].x == -INFINITY ? 0.f : expf(mc[c].x - Mb);
-            Ls = fmaf(mc[c].y, f, Ls);
-            A = fmaf(av[c], f, A);
+        epi_sync();
+        if (tid < HD) {
+            float Mb = M;
+            for (int cc = 0; cc < nc; ++cc) Mb = fmaxf(Mb, mp[cc * kW]);
+            if (Mb != -INFINITY) {
+                const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+                Ls *= r;
+                A *= r;
+                for (int cc = 0; cc < nc; ++cc) {
+                    const float mc = mp[cc * kW];
+                    const float f = mc == -INFINITY ? 0.f : expf(mc - Mb);
+                    Ls = fmaf(mp[cc * kW + 1], f, Ls);
+                    A = fmaf(mp[cc * kW + 2 + tid], f, A);
+                }
+                M = Mb;
+            }
         }
-        M = Mb;
+        epi_sync();                             // the staging rows are reused by the next batch
     }
-    const float o = A / Ls;
-    const __half hi = __float2half_rn(o);
-    p.attn_h[(size_t)h * HD + tid] = hi;
-    p.attn_l[(size_t)h * HD + tid] = __float2half_rn(o - __half2float(hi));
+    if (tid < HD) ll_st1(op.lout + (size_t)h * HD + tid, ll_word(hilo_bits(A / Ls), tag));
 }
 
 }  // namespace
@@ -468,13 +616,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, c = blockIdx.x;
     const int S = p.stages;
+    const int SB = p.stage_bytes;
     uint8_t *ring = smem;
-    // input vector as two fp16 vectors: hi = fp16(x), lo = fp16(x - hi) (~22 bits of x)
-    __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * kStageBytes);
-    __half *xl = xh + p.xmax;
-    uint8_t *am = reinterpret_cast<uint8_t *>(xl + p.xmax);                     // attention region
-    StepOp *ops = reinterpret_cast<StepOp *>(am + AttnRegion<HD>::bytes);        // the op table
-    uint64_t *full = reinterpret_cast<uint64_t *>(ops + p.n_ops);
+    // the input vector of a GEMV as two fp16 vectors: hi = fp16(x) at xh, lo = fp16(x - hi) at
+    // xh + K (~22 bits of x); the attention region follows the QKV projection's input
+    uint8_t *vec = smem + (size_t)S * SB;
+    __half *xh = reinterpret_cast<__half *>(vec);
+    uint8_t *am = vec + p.attn_off;
+    StepOp *opc = reinterpret_cast<StepOp *>(vec + p.vec_bytes);     // ops k and k + 1 (warps 0-3)
+    uint64_t *full = reinterpret_cast<uint64_t *>(opc + 2);
     uint64_t *empty = full + S;
     const Abort ab{&s_abort, p.st};
 
@@ -488,46 +638,77 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         }
         fence_mbar_init();
     }
-    // every role reads op descriptors on its critical path: keep them in shared memory
-    for (int i = tid; i < p.n_ops * (int)(sizeof(StepOp) / 16); i += kThreads)
-        reinterpret_cast<uint4 *>(ops)[i] = __ldg(reinterpret_cast<const uint4 *>(p.ops) + i);
+    if (tid < kOpWords) cp_async16(reinterpret_cast<uint4 *>(opc) + tid, reinterpret_cast<const uint4 *>(p.ops) + tid);
+    cp_async_commit();
+    cp_async_wait_all();
     __syncthreads();
 
     if (warp == kProducerWarp) {
         // ---- producer: every unit of the step, in op order; waits only for free stages ----------
         if (lane == 0) {
             int s = 0, round = 0, issued = 0;
+            const int F = p.max_inflight > 0 ? min(p.max_inflight, S) : S;
             const uint64_t pol = policy_evict_first();
+            // the fields of op k, read one op ahead from the table in global memory
+            int kind = __ldg(&p.ops[0].kind), grid = __ldg(&p.ops[0].grid), N = __ldg(&p.ops[0].N),
+                K = __ldg(&p.ops[0].K), prw = __ldg(&p.ops[0].pass_rows), cw = __ldg(&p.ops[0].chunk_w);
+            const uint8_t *w = reinterpret_cast<const uint8_t *>(
+                __ldg(reinterpret_cast<const unsigned long long *>(&p.ops[0].w)));
             for (int k = 0; k < p.n_ops && !ab.on(); ++k) {
-                const StepOp &op = ops[k];
-                if (op.kind != OP_GEMV || c >= op.grid) continue;
-                const int P = op.N / 2;
-                const int R0 = 2 * (int)((long long)P * c / op.grid);
-                const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
-                const uint8_t *src = op.w + (size_t)R0 * op.K * 2;
-                for (int p0 = 0; p0 < R && !ab.on(); p0 += op.pass_rows) {
-                    const int rows = min(op.pass_rows, R - p0);
-                    for (int q0 = 0; q0 < op.K; q0 += op.chunk_w) {
-                        const uint32_t nb = (uint32_t)(rows * min(op.chunk_w, op.K - q0) * 2);
-                        if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
-                        mbar_arrive_expect_tx(&full[s], nb);
-                        if (p.evict_first)
-                            bulk_g2s_hint(ring + (size_t)s * kStageBytes, src, nb, &full[s], pol);
-                        else
-                            bulk_g2s(ring + (size_t)s * kStageBytes, src, nb, &full[s]);
-                        src += nb;
-                        ++issued;
-                        if (++s == S) {
-                            s = 0;
-                            ++round;
+                int nkind = OP_ATTN, ngrid = 0, nN = 0, nK = 0, nprw = 0, ncw = 0;
+                const uint8_t *nw = nullptr;
+                if (k + 1 < p.n_ops) {
+                    const StepOp *o = p.ops + k + 1;
+                    nkind = __ldg(&o->kind);
+                    ngrid = __ldg(&o->grid);
+                    nN = __ldg(&o->N);
+                    nK = __ldg(&o->K);
+                    nprw = __ldg(&o->pass_rows);
+                    ncw = __ldg(&o->chunk_w);
+                    nw = reinterpret_cast<const uint8_t *>(__ldg(reinterpret_cast<const unsigned long long *>(&o->w)));
+                }
+                if (kind == OP_GEMV && c < grid) {
+                    const int P = N / 2;
+                    const int R0 = 2 * (int)((long long)P * c / grid);
+                    const int R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+                    const uint8_t *src = w + (size_t)R0 * K * 2;
+                    for (int p0 = 0; p0 < R && !ab.on(); p0 += prw) {
+                        const int rows = min(prw, R - p0);
+                        for (int q0 = 0; q0 < K; q0 += cw) {
+                            const uint32_t nb = (uint32_t)(rows * min(cw, K - q0) * 2);
+                            if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
+                            // at most F copies in flight: unit issued - F must have landed (its stage
+                            // is not refilled before this one is issued, so its phase parity is exact)
+                            if (issued >= F) {
+                                const int u = issued - F;
+                                if (!wait_bar(&full[u % S], (uint32_t)(u / S) & 1u, ab)) break;
+                            }
+                            mbar_arrive_expect_tx(&full[s], nb);
+                            if (p.evict_first)
+                                bulk_g2s_hint(ring + (size_t)s * SB, src, nb, &full[s], pol);
+                            else
+                                bulk_g2s(ring + (size_t)s * SB, src, nb, &full[s]);
+                            src += nb;
+                            ++issued;
+                            if (++s == S) {
+                                s = 0;
+                                ++round;
+                            }
                         }
                     }
                 }
+                kind = nkind;
+                grid = ngrid;
+                N = nN;
+                K = nK;
+                prw = nprw;
+                cw = ncw;
+                w = nw;
             }
             s_issued = issued;
         }
     } else {
-        // ---- warps 0-3: dependencies, prologues, GEMV compute, epilogues, attention ---------------
+        // ---- warps 0-3: hand-offs, prologues, GEMV compute, epilogues, attention ------------------
         griddep_wait();
         griddep_launch_dependents();
         DevState *st = p.st;
@@ -554,63 +735,78 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         int s = 0, round = 0, consumed = 0;       // ring position of the compute warps
 
         for (int k = 0; k < p.n_ops; ++k) {
-            const StepOp &op = ops[k];
+            cp_async_wait_all();
+            epi_sync();                           // op k is in opc[k & 1]; everyone is done with op k - 1
+            const StepOp &op = opc[k & 1];
+            if (k + 1 < p.n_ops && tid < kOpWords)
+                cp_async16(reinterpret_cast<uint4 *>(opc + ((k + 1) & 1)) + tid,
+                           reinterpret_cast<const uint4 *>(p.ops + k + 1) + tid);
+            cp_async_commit();
             stamp(p.trace, k, C, c, 0);
+            const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
             if (op.kind == OP_ATTN) {
                 // items on the last CTAs: (q head, context chunk), one per CTA
                 const int items = p.nh * n_chunks, item = C - 1 - c;
                 if (item < items && !ab.on()) {
                     attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
                     const int h = item / n_chunks;
-                    epi_sync();
-                    if (tid == 0) s_flag = atom_add_acq_rel(p.grp_cnt + h, 1u) == (unsigned)(n_chunks - 1);
-                    epi_sync();
-                    if (s_flag) {      // the head's last chunk: merge all of them
+                    if (item == h * n_chunks) {          // chunk 0 of the head: merge all of them
                         stamp(p.trace, k, C, c, 6);
-                        merge_head<HD>(p, h, n_chunks);
-                        epi_sync();
+                        merge_head<HD>(p, op, ss, am, h, n_chunks, k, ab);
                         stamp(p.trace, k, C, c, 7);
-                        if (tid == 0) {
-                            p.grp_cnt[h] = 0u;
-                            if (op.sig >= 0) red_add_release(p.cnt + op.sig, 1ull);
-                        }
                     }
                 }
                 stamp(p.trace, k, C, c, 3);
                 continue;
             }
-            if (op.epi == EPI_QKV && k + 1 < p.n_ops && ops[k + 1].kind == OP_ATTN) {
+            if (op.epi == EPI_QKV) {
                 // this CTA's attention item of the layer: stage its immutable K/V rows now
                 const int item = C - 1 - c;
-                if (item < p.nh * n_chunks)
-                    attn_prestage<HD>(p, ops[k + 1], ss, am, item, n_chunks, rows_per, ctx);
+                if (item < p.nh * n_chunks) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             const int K = op.K;
-            if (tid == 0 && op.dep >= 0 && !ab.on())
-                wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
-            epi_sync();
-            stamp(p.trace, k, C, c, 1);
-
-            // ---- prologue: the fp32 input vector in shared memory (RMSNorm fused) -------------------
+            __half *xl = xh + K;
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
+            float4 gn[kNormRegs];
             if (norm) {
-                // K <= kNormRegs * 4 * kEpiThreads (host-checked): each thread holds its float4s in registers
-                float4 v[kNormRegs], gn[kNormRegs];
-                float sq = 0.f;
 #pragma unroll
                 for (int q = 0; q < kNormRegs; ++q) {
                     const int i = tid + q * kEpiThreads;
-                    if (4 * i < K) {
-                        if (op.pro == PRO_EMBED_NORM) {
+                    gn[q] = 4 * i < K ? __ldg(reinterpret_cast<const float4 *>(op.gain) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            if (op.dep >= 0) {
+                if (tid == 0 && !ab.on())
+                    wait_counter(p.cnt + op.dep, (unsigned long long)op.dep_n * (ss.epoch + 1), ab);
+                epi_sync();
+            }
+            stamp(p.trace, k, C, c, 1);
+
+            // ---- prologue: the input vector in shared memory as hi / lo halves ----------------------
+            if (norm) {
+                // K <= kNormRegs * 4 * kEpiThreads (host-checked): each thread holds its float4s in registers
+                float4 v[kNormRegs];
+#pragma unroll
+                for (int q = 0; q < kNormRegs; ++q) v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (op.pro == PRO_EMBED_NORM) {
+#pragma unroll
+                    for (int q = 0; q < kNormRegs; ++q) {
+                        const int i = tid + q * kEpiThreads;
+                        if (4 * i < K) {
                             const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(p.embed + (size_t)ss.token * K) + i);
                             const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
                             const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
                             v[q] = make_float4(a.x, a.y, b.x, b.y);
-                        } else {
-                            v[q] = ldcg4(op.xin + 4 * i);
                         }
-                        gn[q] = __ldg(reinterpret_cast<const float4 *>(op.gain) + i);
+                    }
+                } else {
+                    ll_norm_input(v, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
+                }
+                float sq = 0.f;
+#pragma unroll
+                for (int q = 0; q < kNormRegs; ++q) {
+                    if (4 * (tid + q * kEpiThreads) < K) {
                         sq = fmaf(v[q].x, v[q].x, sq);
                         sq = fmaf(v[q].y, v[q].y, sq);
                         sq = fmaf(v[q].z, v[q].z, sq);
@@ -629,13 +825,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                                     make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
                                                 (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w));
                 }
+            } else if (op.pro == PRO_ATTN) {
+                ll_hilo_input(xh, xl, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
             } else {
-                // the producer of this input wrote it as fp16 hi / lo vectors: copy them
-                const __half *sh = op.pro == PRO_ATTN ? p.attn_h : op.xin_h;
-                const __half *sl = op.pro == PRO_ATTN ? p.attn_l : op.xin_l;
+                // PRO_PLAIN: fp16 hi / lo vectors behind the dependency counter: copy them
                 for (int i = tid; i < K / 8; i += kEpiThreads) {
-                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(sh) + i);
-                    const uint4 lv = __ldcg(reinterpret_cast<const uint4 *>(sl) + i);
+                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(op.xin_h) + i);
+                    const uint4 lv = __ldcg(reinterpret_cast<const uint4 *>(op.xin_l) + i);
                     reinterpret_cast<uint4 *>(xh)[i] = hv;
                     reinterpret_cast<uint4 *>(xl)[i] = lv;
                 }
@@ -653,23 +849,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             float bv = -INFINITY;
             int bi = INT_MAX;
             for (int p0 = 0; p0 < R && !ab.on(); p0 += op.pass_rows) {
-                const int rows_p = min(op.pass_rows, R - p0), npairs = rows_p / 2;
+                const int rows_p = min(op.pass_rows, R - p0);
                 const int nrt = (rows_p + 15) >> 4;                 // 16-row tiles of the pass (<= 4)
                 // epilogue operands that do not depend on the products: thread t < npairs finishes
                 // pair t (rows 2t, 2t + 1 of the pass)
                 const int row = R0 + p0 + 2 * tid;                  // packed row (row, row + 1)
-                const bool mine = tid < npairs && row < op.n_valid;
+                const bool mine = tid < rows_p / 2 && row < op.n_valid;
                 float pre0 = 0.f, pre1 = 0.f, pcs = 1.f, psn = 0.f;
                 if (mine) {
                     if (op.epi == EPI_RESID) {
-                        if (op.resid_embed) {
+                        if (op.lres == nullptr) {                   // layer 0: the token's embedding row
                             const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
                             pre0 = __low2float(e2);
                             pre1 = __high2float(e2);
                         } else {
-                            const float2 b2 = __ldcg(reinterpret_cast<const float2 *>(op.out + row));
-                            pre0 = b2.x;
-                            pre1 = b2.y;
+                            uint64_t w[1][2];
+                            ll_poll<1>(w, 1u, [&](int) { return op.lres + row; }, ll_tag(ss.epoch, p.n_ops, op.lres_k), ab);
+                            pre0 = ll_f(w[0][0]);
+                            pre1 = ll_f(w[0][1]);
                         }
                     } else if (op.epi == EPI_QKV) {
                         const int P2 = row / 2, hh = P2 / half_hd, dd = P2 - hh * half_hd;
@@ -690,12 +887,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) d[i][j] = 0.f;
-                const int lm = lane >> 3, lr = lane & 7;            // ldmatrix: matrix, row within it
                 for (int q0 = 0; q0 < K; q0 += op.chunk_w) {
                     const int wq = min(op.chunk_w, K - q0);
                     if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
                     if (p0 == 0 && q0 == 0) stamp(p.trace, k, C, c, 4);
-                    const uint32_t unit = smem_u32(ring + (size_t)s * kStageBytes);
+                    const uint32_t unit = smem_u32(ring + (size_t)s * SB);
                     const int rs = wq * 2;                          // row stride (bytes) inside the unit
                     const int nks = wq >> 4;
                     if (nrt == 1)
@@ -728,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 const float y0 = ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
                 const float y1 = ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
                 if (op.epi == EPI_RESID) {
-                    *reinterpret_cast<float2 *>(op.out + row) = make_float2(pre0 + y0, pre1 + y1);
+                    ll_st2(op.lout + row, ll_wordf(pre0 + y0, tag), ll_wordf(pre1 + y1, tag));
                 } else if (op.epi == EPI_LMHEAD) {
                     if (lg) lg[row] = y0;
                     if (y0 > bv) {
@@ -750,23 +946,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 } else {  // EPI_QKV: packed rows (2q, 2q+1) are dims (d, d + hd/2) of one head
                     const int P2 = row / 2;
                     const int hh = P2 / half_hd, dd = P2 - hh * half_hd;
-                    const int lo = hh * HD + dd, hi = lo + half_hd;
                     const float a0 = y0 + pre0, a1 = y1 + pre1;
                     if (hh < p.nh + p.nkv) {
                         const float o0 = __fadd_rn(__fmul_rn(a0, pcs), -__fmul_rn(a1, psn));
                         const float o1 = __fadd_rn(__fmul_rn(a1, pcs), __fmul_rn(a0, psn));
                         if (hh < p.nh) {
-                            op.out[lo] = o0;
-                            op.out[hi] = o1;
+                            ll_st1(op.lout + hh * HD + dd, ll_wordf(o0, tag));
+                            ll_st1(op.lout + hh * HD + dd + half_hd, ll_wordf(o1, tag));
                         } else {
-                            __half *kr = op.kc + ((size_t)(hh - p.nh) * p.cap + ss.slot) * HD;
+                            const int g = hh - p.nh;
+                            __half *kr = op.kc + ((size_t)g * p.cap + ss.slot) * HD;
                             kr[dd] = __float2half_rn(o0);
                             kr[dd + half_hd] = __float2half_rn(o1);
+                            ll_st1(op.lkv + (size_t)g * HD + dd, ll_word(half2_bits(o0, o1), tag));
                         }
                     } else {
-                        __half *vr = op.vc + ((size_t)(hh - p.nh - p.nkv) * p.cap + ss.slot) * HD;
+                        const int g = hh - p.nh - p.nkv;
+                        __half *vr = op.vc + ((size_t)g * p.cap + ss.slot) * HD;
                         vr[dd] = __float2half_rn(a0);
                         vr[dd + half_hd] = __float2half_rn(a1);
+                        ll_st1(op.lkv + (size_t)g * HD + half_hd + dd, ll_word(half2_bits(a0, a1), tag));
                     }
                 }
             }
@@ -836,11 +1035,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     }
                 }
             } else if (op.sig >= 0) {
-                epi_sync();
-                if (tid == 0) red_add_release(p.cnt + op.sig, 1ull);
+                if (tid == 0) red_add_release(p.cnt + op.sig, 1ull);   // after the barrier above
             }
             stamp(p.trace, k, C, c, 3);
         }
+        cp_async_wait_all();
         if (tid == 0) s_consumed = consumed;
     }
 
@@ -893,18 +1092,35 @@ __global__ void k_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __h
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-void plan_step_gemv(StepOp &o, int num_sms) {
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
+// pass), each unit at most one stage.
+void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
     const int P = o.N / 2;
     o.grid = std::max(1, std::min(num_sms, P));
     const int rmax = 2 * ((P + o.grid - 1) / o.grid);                       // rows of the busiest CTA
-    o.pass_rows = std::min(kPassRows, rmax);
-    int w = (kStageBytes / (o.pass_rows * 2)) / 256 * 256;                  // units of at most one stage
-    o.chunk_w = std::max(256, w) >= o.K ? o.K : std::max(256, w);
+    long long best = -1;
+    for (int pr = std::min(kPassRows, rmax); pr >= 2; pr -= 2) {
+        int w = (stage_bytes / (pr * 2)) / 256 * 256;
+        if (w >= o.K) w = o.K;
+        if (w < 256 && w != o.K) continue;
+        const long long units = (long long)((rmax + pr - 1) / pr) * ((o.K + w - 1) / w);
+        if (best < 0 || units < best) {
+            best = units;
+            o.pass_rows = pr;
+            o.chunk_w = w;
+        }
+    }
+    if (best < 0) {
+        o.pass_rows = 2;
+        o.chunk_w = 256;
+    }
 }
 
-bool step_gemv_supported(const StepOp &o) {
-    return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows <= kPassRows &&
-           (size_t)o.pass_rows * o.chunk_w * 2 <= (size_t)kStageBytes &&
+bool step_gemv_supported(const StepOp &o, int stage_bytes) {
+    return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 && o.pass_rows <= kPassRows &&
+           (size_t)o.pass_rows * o.chunk_w * 2 <= (size_t)stage_bytes &&
            (o.chunk_w == o.K || o.chunk_w % 256 == 0) &&
            (o.pro == PRO_NORM || o.pro == PRO_EMBED_NORM ? o.K <= kNormRegs * 4 * kEpiThreads : true);
 }
@@ -913,16 +1129,20 @@ size_t step_attn_smem_bytes(int hd) { return hd == 64 ? AttnRegion<64>::bytes : 
 
 static size_t step_static_reserve() { return 2048; }   // static shared memory of k_step, rounded up
 
-size_t step_smem_bytes(int stages, int xmax, int hd, int n_ops) {
-    return (size_t)stages * kStageBytes + (size_t)xmax * 4 + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp) +
-           (size_t)(2 * stages) * 8;
-}
-
-int step_stages_for(int xmax, int hd, int n_ops) {
+// Dynamic shared memory: ring [stages x stage_bytes] | vector region | ops k, k + 1 | barriers.
+// The vector region holds a GEMV's input halves (4 K bytes) and, from attn_off on (after the QKV
+// projection's input, 4 hidden bytes), the attention staging region.
+StepLayout step_layout(int hidden, int xmax, int hd, int stages) {
+    StepLayout L{};
+    L.stages = stages;
+    L.attn_off = (int)align_up((size_t)hidden * 4, 128);
+    L.vec_bytes = (int)align_up(std::max((size_t)xmax * 4, (size_t)L.attn_off + step_attn_smem_bytes(hd)), 128);
+    const size_t fixed = (size_t)L.vec_bytes + 2 * sizeof(StepOp) + (size_t)stages * 16;
     const size_t budget = 227 * 1024 - step_static_reserve();
-    const size_t fixed = (size_t)xmax * 4 + step_attn_smem_bytes(hd) + (size_t)n_ops * sizeof(StepOp);
-    if (fixed >= budget) return 0;
-    return (int)((budget - fixed) / (kStageBytes + 16));
+    if (stages < 2 || fixed >= budget) return L;
+    L.stage_bytes = (int)std::min<size_t>(kMaxStageBytes, (budget - fixed) / stages / 1024 * 1024);
+    L.smem = (size_t)stages * L.stage_bytes + fixed;
+    return L;
 }
 
 cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
@@ -969,7 +1189,9 @@ cudaError_t prepare_step(int hd, size_t smem) {
 }
 
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    if (p.stages < 2 || p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks)
+    if (p.stages < 2 || p.stage_bytes < 1024 || p.stage_bytes % 1024 || p.stage_bytes > kMaxStageBytes ||
+        p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks || p.attn_off % 128 ||
+        p.vec_bytes % 128 || (size_t)p.attn_off + step_attn_smem_bytes(hd) > (size_t)p.vec_bytes)
         return cudaErrorInvalidValue;
     if (hd == 128) return step_launch_t<128>(&p, grid, smem, s, pdl);
     if (hd == 64) return step_launch_t<64>(&p, grid, smem, s, pdl);
