@@ -260,12 +260,14 @@ def run_decode(args, world, rank, local):
     value = total_tokens / (ms_max / 1000.0)
     ms_per_token = ms / (args.steps * DECODE)
 
-    # roofline of the per-token step (one CUDA-graph launch of the fused kernel chain)
+    # roofline of the per-token step: one launch of the persistent step kernel per token (the
+    # kernel-per-op chain, SEEDPLANE_STEP=chain, launches 5 L + 1 kernels per token instead)
     hbm, peak_kind = peaks()
     avg_ctx = PROMPT + DECODE / 2
     alg_bytes = cfg.weight_bytes_per_token(2) + cfg.kv_bytes_per_position(2) * avg_ctx
     achieved = alg_bytes / (ms_per_token / 1000.0) / 1e9
     traffic = traffic_per_token()
+    step_kernel = os.environ.get("SEEDPLANE_STEP", "step") != "chain"
 
     # e2e through the public API: host prompt (pinned) -> device, prefill, decode, tokens -> host
     from seedplane_b200.qwen_engine import KVCache
@@ -314,12 +316,13 @@ def run_decode(args, world, rank, local):
                            "ms_per_token": ms_per_token},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
-                             "kernel": "one decode step (CUDA graph of the fused GEMV/attention chain)",
+                             "kernel": ("k_step: persistent per-token decode kernel, one launch per token"
+                                        if step_kernel else "one decode step: the GEMV / attention kernel chain"),
                              "algorithmic_bytes_per_launch": alg_bytes, "peak_kind": peak_kind},
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                         "d2h_bytes_per_step": DECODE * 4 + 4,
                         "note": "public API per step: pinned prompt H2D, prefill, 256-token decode, tokens D2H"},
-                "gpu_launches": args.steps * (DECODE * (5 * L + 1) + 1),
+                "gpu_launches": args.steps * (DECODE * (1 if step_kernel else 5 * L + 1) + 1),
                 "clocks": clocks.summary(),
                 "token_sha256": __import__("hashlib").sha256(json.dumps(tokens_ref).encode()).hexdigest()}
         if world == 1 and not args.no_cpu_baseline:
