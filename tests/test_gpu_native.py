@@ -1,0 +1,63 @@
+"""`NativeEngine` and the per-GPU HIVE executor on the GPU: greedy tokens identical to the oracle,
+the reference's `last` fields, stop-token cut with cache rollback, reset."""
+import pytest
+import torch
+
+from oracle.qwen_oracle import OracleQwen2
+from seedplane_b200.config import PRESETS
+from seedplane_b200.randinit import TEST_INIT, make_weights, random_prompt
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def bundle(tmp_path_factory):
+    from safetensors.torch import save_file
+    import json
+    cfg = PRESETS["tiny-hd128"]
+    w = make_weights(cfg, seed=0, dtype=torch.float16, **TEST_INIT)
+    d = tmp_path_factory.mktemp("tiny-bundle")
+    (d / "config.json").write_text(json.dumps(cfg.to_hf()))
+    save_file({k: v.contiguous() for k, v in w.items()}, str(d / "model.safetensors"))
+    return d, cfg, w
+
+
+def test_native_engine_generate_matches_oracle(bundle):
+    from seedplane_b200.native import NativeEngine
+    d, cfg, w = bundle
+    prompt = random_prompt(cfg.vocab, 11, seed=5)
+    want = OracleQwen2(cfg, w, kv_fp16=True).greedy(prompt, 40)[0]
+    with NativeEngine(d, ctx=256) as eng:
+        assert eng.info["ready"] and eng.info["mode"] == "full" and eng.info["positions"] == 256
+        pieces = list(eng.generate(ids=prompt, max_new_tokens=40))
+        assert pieces == []                       # no tokenizer.json: ids only
+        assert eng.last_tokens == want
+        last = eng.last
+        assert last["done"] and last["reason"] == "length" and last["generated"] == 40
+        assert last["prompt_tokens"] == len(prompt) and last["position"] == len(prompt) + 39
+        # a stop token cuts the output and rolls the cache back to the emitted tokens
+        list(eng.generate(ids=prompt, max_new_tokens=40, stop=[want[5]]))
+        assert eng.last_tokens == want[:5] and eng.last["reason"] == "stop"
+        assert eng.state()["position"] == len(prompt) + 5
+        # reset=True starts over: same tokens again
+        list(eng.generate(ids=prompt, max_new_tokens=7))
+        assert eng.last_tokens == want[:7]
+        with pytest.raises(RuntimeError):
+            list(eng.generate(ids=prompt, temperature=0.7))
+        with pytest.raises(RuntimeError):
+            eng.tokenize("hello")
+
+
+def test_gpu_agent_executor_matches_oracle(bundle):
+    from seedplane_b200.engine import CudaQwen2
+    from seedplane_b200.hive.agent import GreedyExecutor, token_sha256
+    d, cfg, w = bundle
+    eng = CudaQwen2(cfg, w, device="cuda:0")
+    ex = GreedyExecutor(eng, 128)
+    o = OracleQwen2(cfg, w, kv_fp16=True)
+    for seed in (1, 2):
+        prompt = random_prompt(cfg.vocab, 20 + seed, seed=seed)
+        r = ex({"ids": prompt, "max_new_tokens": 9})
+        want = o.greedy(prompt, 9)[0]
+        assert r["tokens"] == want and r["token_sha256"] == token_sha256(want)
+    eng.close()
