@@ -50,6 +50,7 @@ struct LayerDev {
     const uint8_t *qkv, *o, *gate_up, *down;       // fragment-packed fp16, contiguous in the stream
     const float *qkv_b, *in_norm, *post_norm;
     size_t off_qkv, off_o, off_gu, off_dn;          // offsets in the weight stream
+    PrefillLayer pf{};                              // row-major copies for the batched prompt pass
 };
 
 // Stage ring per GEMV CTA. CTAs of consecutive kernels share an SM under programmatic dependent
@@ -127,6 +128,14 @@ struct sp_engine {
     TcGemvParams t_qkv{}, t_o{}, t_gu{}, t_down{}, t_head{};
     cudaStream_t cap_stream = nullptr;
     std::map<sp_kv *, cudaGraphExec_t> graphs;
+    // batched prompt pass (prefill.cu); off with SEEDPLANE_PREFILL=steps
+    bool prefill = false;
+    void *blas = nullptr;                   // cublasHandle_t
+    PrefillDims pf_dims{};
+    PrefillScratch pf{};
+    uint8_t *pf_mem = nullptr;
+    size_t pf_bytes = 0;
+    const __half *head_rm = nullptr;        // row-major LM head (the embedding when tied)
     std::vector<sp_kv *> caches;
 };
 
@@ -559,7 +568,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
-    struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post; };
+    struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post, rqkv, ro, rgu, rdn; };
     std::vector<LOff> lo(c.layers);
     for (int l = 0; l < c.layers; ++l) {     // matrix sizes are multiples of 512 B: no gaps
         lo[l].qkv = take(QRp * H * 2);
@@ -576,6 +585,18 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         lo[l].qkv_b = take(QR * 4);
         lo[l].inn = take(H * 4);
         lo[l].post = take(H * 4);
+    }
+    // row-major copies for the batched prompt pass
+    e->prefill = !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
+    size_t o_head_rm = 0;
+    if (e->prefill) {
+        for (int l = 0; l < c.layers; ++l) {
+            lo[l].rqkv = take(QR * H * 2);
+            lo[l].ro = take(H * (size_t)c.heads * HD * 2);
+            lo[l].rgu = take(2 * I * H * 2);
+            lo[l].rdn = take(H * I * 2);
+        }
+        if (!c.tied_embeddings) o_head_rm = take(V * H * 2);
     }
     e->arena_bytes = off;
     cudaError_t ce = cudaMalloc(&e->arena, e->arena_bytes);
@@ -625,6 +646,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
                               : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
     };
     SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H, e->s_head));
+    if (e->prefill && !c.tied_embeddings)
+        SP_TRY(cudaMemcpyAsync(A + o_head_rm, w->lm_head, V * H * 2, cudaMemcpyDeviceToDevice, s));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
@@ -636,6 +659,13 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
+        if (e->prefill) {
+            SP_TRY(cudaMemcpyAsync(A + lo[l].rqkv, Lw.qkv_w, QR * H * 2, cudaMemcpyDeviceToDevice, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].ro, Lw.o_w, H * (size_t)c.heads * HD * 2, cudaMemcpyDeviceToDevice, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].rgu, Lw.gate_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].rgu + I * H * 2, Lw.up_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
+            SP_TRY(cudaMemcpyAsync(A + lo[l].rdn, Lw.down_w, H * I * 2, cudaMemcpyDeviceToDevice, s));
+        }
         LayerDev L;
         L.qkv = A + lo[l].qkv;
         L.o = A + lo[l].o;
@@ -648,6 +678,15 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         L.off_o = lo[l].o;
         L.off_gu = lo[l].gu;
         L.off_dn = lo[l].dn;
+        if (e->prefill) {
+            L.pf.qkv = (const __half *)(A + lo[l].rqkv);
+            L.pf.o = (const __half *)(A + lo[l].ro);
+            L.pf.gate_up = (const __half *)(A + lo[l].rgu);
+            L.pf.down = (const __half *)(A + lo[l].rdn);
+            L.pf.qkv_b = L.qkv_b;
+            L.pf.in_norm = L.in_norm;
+            L.pf.post_norm = L.post_norm;
+        }
         e->layers.push_back(L);
     }
     // RoPE table: the caller's (computed like the reference, qwen_engine.py:52,99-103), else double precision.
@@ -677,6 +716,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->off_head = o_head;
     e->final_norm = (const float *)(A + o_fnorm);
     e->rope = (const float *)(A + o_rope);
+    e->head_rm = c.tied_embeddings ? e->embed : (const __half *)(A + o_head_rm);
 
     // ---- GEMV plans -------------------------------------------------------------------------
     auto base = [&](size_t N, size_t K) {
@@ -787,6 +827,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->ws_bytes = woff;
     SP_TRY(cudaMalloc(&e->ws, e->ws_bytes));
     SP_TRY(cudaMemset(e->ws, 0, e->ws_bytes));
+    if (e->prefill) {
+        e->pf_dims = PrefillDims{(int)H, (int)I, c.heads, c.kv_heads, (int)HD, (int)V, c.max_positions,
+                                 kPrefillMaxTokens, c.rms_norm_eps};
+        e->pf_bytes = prefill_scratch_bytes(e->pf_dims);
+        SP_TRY(cudaMalloc(&e->pf_mem, e->pf_bytes));
+        e->pf = prefill_scratch_at(e->pf_mem, e->pf_dims);
+        SP_TRY(prefill_blas_create(&e->blas));
+    }
     e->x = (float *)(e->ws + w_x);
     e->q = (float *)(e->ws + w_q);
     e->attn = (float *)(e->ws + w_attn);
@@ -884,10 +932,14 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->arena);
     cudaFree(e->ws);
     cudaFree(e->trace);
+    cudaFree(e->pf_mem);
+    prefill_blas_destroy(e->blas);
     delete e;
 }
 
-int64_t sp_engine_device_bytes(const sp_engine *e) { return e ? (int64_t)(e->arena_bytes + e->ws_bytes) : 0; }
+int64_t sp_engine_device_bytes(const sp_engine *e) {
+    return e ? (int64_t)(e->arena_bytes + e->ws_bytes + e->pf_bytes) : 0;
+}
 
 int sp_kv_create(sp_engine *e, int32_t capacity, sp_kv **out) {
     if (!e || !out) return fail(SP_ERR_INVALID, "null argument");
@@ -954,12 +1006,48 @@ static int check_engine_kv(sp_engine *e, sp_kv *kv) {
     return SP_OK;
 }
 
+// The batched prompt pass: chunks of up to kPrefillMaxTokens tokens through all layers at once
+// (prefill.cu), then the head in blocks of kPrefillLogitRows rows: logits (all rows, or the last
+// row) and every row's argmax. The K/V of the chunk's tokens land at slots length .. length + n.
+static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const int32_t *pos, int32_t n, float *logits,
+                    bool all_logits, int32_t *argmax, cudaStream_t s) {
+    const sp_config &c = e->c;
+    const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
+    const float scale = 1.0f / sqrtf((float)c.head_dim);
+    SP_CUDA(prefill_blas_stream(e->blas, s));
+    for (int32_t b0 = 0; b0 < n; b0 += kPrefillMaxTokens) {
+        const int T = std::min<int32_t>(kPrefillMaxTokens, n - b0);
+        const int slot0 = kv->length + b0;
+        SP_CUDA(launch_prefill_embed(e->pf_dims, e->pf, e->embed, tok + b0, T, e->st, s));
+        for (int l = 0; l < c.layers; ++l) {
+            const PrefillLayer &L = e->layers[l].pf;
+            SP_CUDA(launch_prefill_layer_front(e->pf_dims, L, e->pf, T, pos ? pos + b0 : nullptr, kv->k + l * kv_layer,
+                                               kv->v + l * kv_layer, kv->capacity, slot0, scale, e->rope, e->st,
+                                               e->blas, s));
+            SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->blas, s));
+        }
+        for (int r0 = 0; r0 < T; r0 += kPrefillLogitRows) {
+            const int rows = std::min(kPrefillLogitRows, T - r0);
+            float *out = all_logits && logits ? logits + (size_t)(b0 + r0) * c.vocab : e->pf.logits;
+            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_rm, r0, rows, out, e->blas, s));
+            SP_CUDA(launch_argmax_rows(out, rows, c.vocab, c.vocab, argmax + b0 + r0, e->am, s));
+            if (!all_logits && logits && b0 + r0 + rows == n)
+                SP_CUDA(cudaMemcpyAsync(logits, out + (size_t)(rows - 1) * c.vocab, (size_t)c.vocab * 4,
+                                        cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    kv->length += n;
+    return SP_OK;
+}
+
 int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t *positions_dev, int32_t n,
                float *logits_dev, int32_t all_logits, int32_t *argmax_dev, void *stream) {
     int rc = check_engine_kv(e, kv);
     if (rc) return rc;
     if (n <= 0 || !tokens_dev) return fail(SP_ERR_INVALID, "input_ids cannot be empty");
     if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    if (e->prefill && n >= kPrefillMin) return forward_batched(e, kv, tokens_dev, positions_dev, n, logits_dev,
+                                                               all_logits != 0, argmax_dev, (cudaStream_t)stream);
     DevState d = base_state();
     d.n_forced = n;
     d.slot0 = kv->length;

@@ -243,6 +243,50 @@ cudaError_t prepare_step(int hd, size_t smem);
 // resident at once (one CTA per SM), so the launch is cooperative.
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl);
 
+// ---- batched prompt pass: prefill.cu ------------------------------------------------------------
+// T prompt tokens per chunk through all layers at once: cuBLAS GEMMs (fp16 x fp16 -> fp32) on
+// row-major weight copies with the activation split into fp16 hi / lo halves, and this engine's
+// kernels for the norms, RoPE + K/V write, causal attention and SwiGLU.
+constexpr int kPrefillMin = 8;           // shorter inputs run as step launches
+constexpr int kPrefillMaxTokens = 512;   // tokens per chunk (scratch size)
+constexpr int kPrefillLogitRows = 64;    // logits rows per head GEMM (argmax scratch rows)
+
+struct PrefillDims {
+    int hidden, inter, heads, kv_heads, head_dim, vocab, max_pos, max_tokens;
+    float eps;
+};
+struct PrefillLayer {                    // row-major fp16 weights
+    const __half *qkv;                   // [(heads + 2 kv_heads) * head_dim, hidden], natural row order
+    const __half *o;                     // [hidden, heads * head_dim]
+    const __half *gate_up;               // [2 inter, hidden]: gate rows, then up rows
+    const __half *down;                  // [hidden, inter]
+    const float *qkv_b, *in_norm, *post_norm;
+};
+struct PrefillScratch {
+    float *x;                            // [T, hidden] residual stream
+    __half *xh, *xl;                     // [T, max(hidden, inter, heads * head_dim)] GEMM inputs
+    float *y;                            // [T, max(qkv rows, 2 inter)] GEMM outputs
+    float *q;                            // [T, heads * head_dim]
+    float *logits;                       // [kPrefillLogitRows, vocab]
+};
+size_t prefill_scratch_bytes(const PrefillDims &d);
+PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d);
+cudaError_t prefill_blas_create(void **handle);
+cudaError_t prefill_blas_stream(void *handle, cudaStream_t s);
+void prefill_blas_destroy(void *handle);
+cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,
+                                 const int32_t *tok, int T, DevState *st, cudaStream_t stream);
+// RMSNorm, QKV GEMM, bias + RoPE + K/V write at slots slot0 .., causal attention, O GEMM (+= x)
+cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
+                                       const int32_t *pos, __half *kc, __half *vc, int cap, int slot0, float scale,
+                                       const float *rope, DevState *st, void *cublas, cudaStream_t stream);
+// RMSNorm, gate_up GEMM, SwiGLU, down GEMM (+= x)
+cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
+                                     void *cublas, cudaStream_t stream);
+// final RMSNorm of rows [r0, r0 + n) and the head GEMM into out [n, vocab]
+cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
+                                  const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream);
+
 // Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
 // (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per
 // row, which must be zero when the kernel starts and is zero again when it ends.

@@ -1,0 +1,321 @@
+// Batched prompt pass (prefill) for sm_100a: T prompt tokens per chunk through all layers at once.
+//
+// The projections of T tokens are plain GEMMs, [T, K] x [K, N], compute-bound at prompt lengths,
+// so they go to cuBLAS (fp16 operands, fp32 accumulation and output) on row-major copies of the
+// weights. Everything around them is this file's kernels: embedding gather, RMSNorm to fp16
+// hi / lo halves, bias + RoPE + K/V cache write, causal GQA attention over the cache, SwiGLU.
+// The activation of every GEMM is split like the decode step's: hi = fp16(x), lo = fp16(x - hi),
+// and the GEMM runs once on each (W x = W hi + W lo), so the products carry ~22 bits of the fp32
+// activation against the fp16 weights — the decode step's precision, which greedy token identity
+// with the fp32 reference depends on. The residual stream stays fp32 (the O and down GEMMs
+// accumulate into it with beta = 1).
+#include <cublas_v2.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "kernels.cuh"
+
+namespace sp {
+
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kAttnQ = 16;                  // queries per attention CTA (4 per warp)
+constexpr int kAttnKeys = 32;               // keys per staged tile (one per lane)
+
+__device__ __forceinline__ void set_err(DevState *st, int code) {
+    if (st) atomicCAS(&st->err, 0, code);
+}
+
+// x[t] = embedding row of token t (ids outside the vocabulary record an error and read row 0)
+__global__ void k_embed_rows(float *x, const __half *embed, const int32_t *tok, int H, int vocab, DevState *st) {
+    const int t = blockIdx.x;
+    int id = tok[t];
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) set_err(st, kErrBadToken);
+        id = 0;
+    }
+    const __half *row = embed + (size_t)id * H;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) x[(size_t)t * H + j] = __half2float(row[j]);
+}
+
+// hi / lo halves of RMSNorm(x[t]) * gain: v = (x * inv) * g, inv = 1 / sqrt(mean(x^2) + eps)
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __half *xl, const float *x,
+                                                                const float *gain, int H, float eps) {
+    const int t = blockIdx.x;
+    const float *r = x + (size_t)t * H;
+    __shared__ float s_part[kNormThreads / 32];
+    float sq = 0.f;
+    for (int j = threadIdx.x; j < H; j += kNormThreads) sq = fmaf(r[j], r[j], sq);
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += s_part[w];
+    const float inv = 1.0f / sqrtf(tot / (float)H + eps);
+    for (int j = threadIdx.x; j < H; j += kNormThreads) {
+        const float v = (r[j] * inv) * gain[j];
+        const __half h = __float2half_rn(v);
+        xh[(size_t)t * H + j] = h;
+        xl[(size_t)t * H + j] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+// y[t] = [q heads | k heads | v heads] (natural row order): bias, RoPE on q and k with the
+// position of token t, q -> fp32, k and v -> the fp16 cache at slot slot0 + t.
+__global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, const float *bias, const float *rope,
+                              const int32_t *pos, int nh, int nkv, int hd, int cap, int slot0, int max_pos,
+                              DevState *st) {
+    const int t = blockIdx.x, half_hd = hd / 2, heads = nh + 2 * nkv;
+    int p = pos ? pos[t] : slot0 + t;
+    if (p < 0 || p >= max_pos) {
+        if (threadIdx.x == 0) set_err(st, kErrBadSlot);
+        p = min(max(p, 0), max_pos - 1);
+    }
+    const float *yr = y + (size_t)t * heads * hd;
+    const int slot = slot0 + t;
+    for (int i = threadIdx.x; i < heads * half_hd; i += blockDim.x) {
+        const int hh = i / half_hd, d = i - hh * half_hd;
+        const int lo = hh * hd + d, hi = lo + half_hd;
+        const float a0 = yr[lo] + bias[lo], a1 = yr[hi] + bias[hi];
+        if (hh < nh + nkv) {
+            const float cs = rope[((size_t)p * half_hd + d) * 2], sn = rope[((size_t)p * half_hd + d) * 2 + 1];
+            const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
+            const float o1 = __fadd_rn(__fmul_rn(a1, cs), __fmul_rn(a0, sn));
+            if (hh < nh) {
+                q[(size_t)t * nh * hd + lo] = o0;
+                q[(size_t)t * nh * hd + hi] = o1;
+            } else {
+                __half *kr = kc + ((size_t)(hh - nh) * cap + slot) * hd;
+                kr[d] = __float2half_rn(o0);
+                kr[d + half_hd] = __float2half_rn(o1);
+            }
+        } else {
+            __half *vr = vc + ((size_t)(hh - nh - nkv) * cap + slot) * hd;
+            vr[d] = __float2half_rn(a0);
+            vr[d + half_hd] = __float2half_rn(a1);
+        }
+    }
+}
+
+// Causal GQA attention of T queries (slots slot0 .. slot0 + T - 1) over the cache: query t sees
+// slots [0, slot0 + t]. CTA = (q head, 16 queries), warp = 4 queries; keys in tiles of 32 staged
+// in shared memory (K rows padded by 4 bytes: lane j reads row j without bank conflicts). Scores,
+// online softmax (running max / sum per query) and the value sums in fp32; the output goes out as
+// fp16 hi / lo halves (the O projection's input).
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, const float *q, const __half *kc,
+                                                      const __half *vc, int T, int nh, int nkv, int cap, int slot0,
+                                                      float scale) {
+    constexpr int DL = HD / 32;                       // output dims per lane
+    constexpr int KROW = HD * 2 + 4;                  // padded K row (bytes)
+    __shared__ __align__(16) float qs[kAttnQ][HD];
+    __shared__ __align__(16) uint8_t ks[kAttnKeys * KROW];
+    __shared__ __align__(16) __half vs[kAttnKeys][HD];
+    const int h = blockIdx.x, q0 = blockIdx.y * kAttnQ;
+    const int g = h / (nh / nkv);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kAttnQ * HD; i += 128) {
+        const int qq = i / HD, d = i - qq * HD;
+        qs[qq][d] = q0 + qq < T ? q[(size_t)(q0 + qq) * nh * HD + h * HD + d] * scale : 0.f;
+    }
+    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
+    float m[4], l[4], acc[4][DL];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[i][d] = 0.f;
+    }
+    const int last = slot0 + min(T, q0 + kAttnQ) - 1;    // the last key any query of this CTA sees
+    for (int k0 = 0; k0 <= last; k0 += kAttnKeys) {
+        __syncthreads();                                  // previous tile consumed (and q staged)
+        for (int i = threadIdx.x; i < kAttnKeys * (HD / 8); i += 128) {
+            const int j = i / (HD / 8), c = i - j * (HD / 8);
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
+            if (k0 + j <= last) {
+                kv = *reinterpret_cast<const uint4 *>(kb + (size_t)(k0 + j) * HD + c * 8);
+                vv = *reinterpret_cast<const uint4 *>(vb + (size_t)(k0 + j) * HD + c * 8);
+            }
+            uint32_t *kd = reinterpret_cast<uint32_t *>(ks + (size_t)j * KROW + c * 16);
+            kd[0] = kv.x;
+            kd[1] = kv.y;
+            kd[2] = kv.z;
+            kd[3] = kv.w;
+            *reinterpret_cast<uint4 *>(&vs[j][c * 8]) = vv;
+        }
+        __syncthreads();
+        // scores: lane = key k0 + lane, four queries of this warp
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint8_t *kr = ks + (size_t)lane * KROW;
+#pragma unroll 8
+        for (int d = 0; d < HD; d += 2) {
+            const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(kr + d * 2));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 qf = *reinterpret_cast<const float2 *>(&qs[warp * 4 + i][d]);
+                s[i] = fmaf(qf.x, kf.x, s[i]);
+                s[i] = fmaf(qf.y, kf.y, s[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int t = q0 + warp * 4 + i;
+            const int key = k0 + lane;
+            const bool vis = t < T && key <= slot0 + t;
+            const float sv = vis ? s[i] : -INFINITY;
+            const float mnew = fmaxf(m[i], warp_max(sv));
+            const float p = mnew == -INFINITY ? 0.f : expf(sv - mnew);
+            const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
+            l[i] = l[i] * corr + warp_sum(p);
+            m[i] = mnew;
+#pragma unroll
+            for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
+            for (int j = 0; j < kAttnKeys; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, p, j);
+                if (pj != 0.f) {
+#pragma unroll
+                    for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, __half2float(vs[j][lane * DL + d]), acc[i][d]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = q0 + warp * 4 + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) {
+            const float o = acc[i][d] / l[i];
+            const __half hv = __float2half_rn(o);
+            const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
+            oh[idx] = hv;
+            ol[idx] = __float2half_rn(o - __half2float(hv));
+        }
+    }
+}
+
+// act = SiLU(gate) * up as fp16 hi / lo; y[t] = [gate (I) | up (I)]
+__global__ void k_swiglu_hilo(__half *ah, __half *al, const float *y, int I) {
+    const int t = blockIdx.x;
+    const float *g = y + (size_t)t * 2 * I, *u = g + I;
+    for (int j = threadIdx.x; j < I; j += blockDim.x) {
+        const float y0 = g[j], y1 = u[j];
+        const float a = (y0 / (1.0f + expf(-y0))) * y1;
+        const __half hv = __float2half_rn(a);
+        ah[(size_t)t * I + j] = hv;
+        al[(size_t)t * I + j] = __float2half_rn(a - __half2float(hv));
+    }
+}
+
+// Y[T, N] (row-major, ldy) = beta * Y + W[N, K] (row-major) . (Xh + Xl)[T, K]^T, in two GEMMs
+cublasStatus_t gemm_hilo(cublasHandle_t hb, const __half *w, int N, int K, const __half *xh, const __half *xl, int T,
+                         float *y, int ldy, float beta) {
+    const float one = 1.0f;
+    cublasStatus_t s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16F, K, xh, CUDA_R_16F, K,
+                                    &beta, y, CUDA_R_32F, ldy, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    if (s != CUBLAS_STATUS_SUCCESS) return s;
+    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16F, K, xl, CUDA_R_16F, K, &one, y,
+                        CUDA_R_32F, ldy, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+}  // namespace
+
+size_t prefill_scratch_bytes(const PrefillDims &d) {
+    const size_t T = d.max_tokens;
+    const size_t kmax = std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
+    const size_t nmax = std::max((size_t)(d.heads + 2 * d.kv_heads) * d.head_dim, 2 * (size_t)d.inter);
+    return T * d.hidden * 4 + 2 * T * kmax * 2 + T * nmax * 4 + T * d.heads * d.head_dim * 4 +
+           (size_t)kPrefillLogitRows * d.vocab * 4 + 5 * 256;
+}
+
+PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
+    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+    const size_t T = d.max_tokens;
+    const size_t kmax = std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
+    const size_t nmax = std::max((size_t)(d.heads + 2 * d.kv_heads) * d.head_dim, 2 * (size_t)d.inter);
+    uint8_t *p = static_cast<uint8_t *>(base);
+    PrefillScratch s{};
+    s.x = reinterpret_cast<float *>(p);
+    p += up(T * d.hidden * 4);
+    s.xh = reinterpret_cast<__half *>(p);
+    p += up(T * kmax * 2);
+    s.xl = reinterpret_cast<__half *>(p);
+    p += up(T * kmax * 2);
+    s.y = reinterpret_cast<float *>(p);
+    p += up(T * nmax * 4);
+    s.q = reinterpret_cast<float *>(p);
+    p += up(T * d.heads * d.head_dim * 4);
+    s.logits = reinterpret_cast<float *>(p);
+    return s;
+}
+
+cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
+                                       const int32_t *pos, __half *kc, __half *vc, int cap, int slot0, float scale,
+                                       const float *rope, DevState *st, void *cublas, cudaStream_t stream) {
+    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
+    const int H = d.hidden, QR = (d.heads + 2 * d.kv_heads) * d.head_dim;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x, L.in_norm, H, d.eps);
+    if (gemm_hilo(hb, L.qkv, QR, H, s.xh, s.xl, T, s.y, QR, 0.0f) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_qkv_rope_kv<<<T, 256, 0, stream>>>(s.q, kc, vc, s.y, L.qkv_b, rope, pos, d.heads, d.kv_heads, d.head_dim, cap,
+                                         slot0, d.max_pos, st);
+    const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
+    if (d.head_dim == 128)
+        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xh, s.xl, s.q, kc, vc, T, d.heads, d.kv_heads, cap, slot0, scale);
+    else
+        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xh, s.xl, s.q, kc, vc, T, d.heads, d.kv_heads, cap, slot0, scale);
+    // O projection into the residual stream
+    if (gemm_hilo(hb, L.o, H, d.heads * d.head_dim, s.xh, s.xl, T, s.x, H, 1.0f) != CUBLAS_STATUS_SUCCESS)
+        return cudaErrorUnknown;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
+                                     void *cublas, cudaStream_t stream) {
+    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
+    const int H = d.hidden, I = d.inter;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x, L.post_norm, H, d.eps);
+    if (gemm_hilo(hb, L.gate_up, 2 * I, H, s.xh, s.xl, T, s.y, 2 * I, 0.0f) != CUBLAS_STATUS_SUCCESS)
+        return cudaErrorUnknown;
+    k_swiglu_hilo<<<T, 256, 0, stream>>>(s.xh, s.xl, s.y, I);
+    if (gemm_hilo(hb, L.down, H, I, s.xh, s.xl, T, s.x, H, 1.0f) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,
+                                 const int32_t *tok, int T, DevState *st, cudaStream_t stream) {
+    k_embed_rows<<<T, 256, 0, stream>>>(s.x, embed, tok, d.hidden, d.vocab, st);
+    return cudaGetLastError();
+}
+
+// Logits of rows [r0, r0 + n) of the chunk (n <= kPrefillLogitRows) into `out` (row stride vocab):
+// final RMSNorm, then the head GEMM.
+cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
+                                  const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream) {
+    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
+    const int H = d.hidden;
+    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x + (size_t)r0 * H, final_norm, H, d.eps);
+    if (gemm_hilo(hb, head, d.vocab, H, s.xh, s.xl, n, out, d.vocab, 0.0f) != CUBLAS_STATUS_SUCCESS)
+        return cudaErrorUnknown;
+    return cudaGetLastError();
+}
+
+cudaError_t prefill_blas_create(void **handle) {
+    cublasHandle_t h = nullptr;
+    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    *handle = h;
+    return cudaSuccess;
+}
+
+cudaError_t prefill_blas_stream(void *handle, cudaStream_t s) {
+    return cublasSetStream(static_cast<cublasHandle_t>(handle), s) == CUBLAS_STATUS_SUCCESS ? cudaSuccess
+                                                                                             : cudaErrorUnknown;
+}
+
+void prefill_blas_destroy(void *handle) {
+    if (handle) cublasDestroy(static_cast<cublasHandle_t>(handle));
+}
+
+}  // namespace sp
