@@ -337,6 +337,76 @@ def run_decode(args, world, rank, local):
     return line
 
 
+def run_verify(args, world, rank, local):
+    """Tree-verify latency (the cfg2 shapes): Qwen2-0.5B-shaped fp16 target, a 128-token prompt, a
+    16-node draft tree of depth 4 (branching 4, 2, 1, 1 cut to 16 nodes); one batched device pass
+    per verify. `value` = microseconds per verify pass (device, CUDA events on the stream); `e2e`
+    adds the host side: tree arrays to the device and the 16 argmaxes back."""
+    import random
+    from seedplane_b200.config import QWEN2_0_5B
+    from seedplane_b200.engine import CudaQwen2
+    from seedplane_b200.randinit import make_weights, random_prompt
+    cfg = QWEN2_0_5B
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = make_weights(cfg, seed=0, dtype=torch.float16)
+    eng = CudaQwen2(cfg, w, device=dev)
+    del w
+    prompt = random_prompt(cfg.vocab, 128, seed=0)
+    kv = eng.new_kv(1024)
+    eng.forward(kv, prompt, want_logits=False)
+    # branching [4, 2, 1, 1] cut to 16 nodes in breadth-first order
+    rng = random.Random(0)
+    tokens, parents, level = [], [], [-1]
+    for width in (4, 2, 1, 1):
+        nxt = []
+        for par in level:
+            for _ in range(width):
+                if len(tokens) < 16:
+                    tokens.append(rng.randrange(cfg.vocab))
+                    parents.append(par)
+                    nxt.append(len(tokens) - 1)
+        level = nxt
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        am, _ = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+    torch.cuda.synchronize(dev)
+    eng.status()
+    ref = am.cpu().tolist()
+    reps = max(10, args.steps * 20)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler([local]) as clocks:
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(reps):
+            am, _ = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    assert am.cpu().tolist() == ref, "verify is not deterministic"
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        am, _ = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+        host = am.cpu().tolist()
+    e2e_us = (time.perf_counter() - t0) * 1e6 / reps
+    eng.status()
+    eng.close()
+    if rank != 0:
+        return None
+    flops = 2.0 * cfg.weight_bytes_per_token(2) / 2 * len(tokens)
+    return {"metric": "tree verify us (16 nodes, Qwen2-0.5B-shaped target)", "value": us, "unit": "us",
+            "n_gpus": 1, "steps": reps, "warmup": max(3, args.warmup), "ms_per_step": us / 1000.0,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "one batched verify pass of a 16-node depth-4 draft tree (branching 4,2,1,1 cut "
+                                   "to 16) after a 128-token prompt, qwen2-0.5b random-init fp16 target",
+                       "nodes": len(tokens), "prompt": len(prompt),
+                       "tensor_tflops": flops / (us * 1e-6) / 1e12,
+                       "l2": "inputs larger than L2: 0.99 GB of weights per pass"},
+            "e2e": {"value": e2e_us, "unit": "us", "h2d_bytes_per_step": len(tokens) * 16,
+                    "d2h_bytes_per_step": len(tokens) * 4},
+            "clocks": clocks.summary(), "argmax": host}
+
+
 def run_burst(args, world, rank, local):
     from seedplane_b200.hive.burst import run_burst_bench
     return run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barrier, peaks)
@@ -348,7 +418,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "burst"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "burst", "verify"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -358,7 +428,8 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        line = (run_burst if args.workload == "burst" else run_decode)(args, world, rank, local)
+        run = {"burst": run_burst, "verify": run_verify}.get(args.workload, run_decode)
+        line = run(args, world, rank, local)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -46,6 +46,15 @@ int fail(int code, const char *fmt, ...) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Inputs of one batched block that a captured verify graph reads from fixed device memory.
+struct VerifyIn {
+    int32_t slot0;                          // first cache slot of the block
+    int32_t pad_;
+    int32_t tok[kSmallNodes];
+    int32_t pos[kSmallNodes];
+    uint64_t mask[kSmallNodes];             // ancestor-or-self bits of node i
+};
+
 struct LayerDev {
     const uint8_t *qkv, *o, *gate_up, *down;       // fragment-packed fp16, contiguous in the stream
     const float *qkv_b, *in_norm, *post_norm;
@@ -136,6 +145,10 @@ struct sp_engine {
     uint8_t *pf_mem = nullptr;
     size_t pf_bytes = 0;
     const __half *head_rm = nullptr;        // row-major LM head (the embedding when tied)
+    VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
+    int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
+    void *blas_ws = nullptr;
+    std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
     std::vector<sp_kv *> caches;
 };
 
@@ -833,7 +846,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->pf_bytes = prefill_scratch_bytes(e->pf_dims);
         SP_TRY(cudaMalloc(&e->pf_mem, e->pf_bytes));
         e->pf = prefill_scratch_at(e->pf_mem, e->pf_dims);
-        SP_TRY(prefill_blas_create(&e->blas));
+        SP_TRY(cudaMalloc(&e->blas_ws, kPrefillBlasWorkspace));
+        SP_TRY(prefill_blas_create(&e->blas, e->blas_ws, kPrefillBlasWorkspace));
+        SP_TRY(cudaMalloc(&e->vt, sizeof(VerifyIn) + kSmallNodes * sizeof(int32_t)));
+        e->vt_argmax = reinterpret_cast<int32_t *>(e->vt + 1);
     }
     e->x = (float *)(e->ws + w_x);
     e->q = (float *)(e->ws + w_q);
@@ -932,8 +948,11 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->arena);
     cudaFree(e->ws);
     cudaFree(e->trace);
+    for (auto &g : e->vgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->pf_mem);
+    cudaFree(e->vt);
     prefill_blas_destroy(e->blas);
+    cudaFree(e->blas_ws);
     delete e;
 }
 
@@ -980,6 +999,14 @@ void sp_kv_destroy(sp_kv *kv) {
             cudaFree(so->second);
             e->step_ops.erase(so);
         }
+        for (auto vg = e->vgraphs.begin(); vg != e->vgraphs.end();) {
+            if (vg->first.first == kv) {
+                cudaGraphExecDestroy(vg->second);
+                vg = e->vgraphs.erase(vg);
+            } else {
+                ++vg;
+            }
+        }
         for (size_t i = 0; i < e->caches.size(); ++i)
             if (e->caches[i] == kv) { e->caches.erase(e->caches.begin() + i); break; }
     }
@@ -1006,24 +1033,26 @@ static int check_engine_kv(sp_engine *e, sp_kv *kv) {
     return SP_OK;
 }
 
-// The batched prompt pass: chunks of up to kPrefillMaxTokens tokens through all layers at once
+// The batched pass: chunks of up to kPrefillMaxTokens tokens through all layers at once
 // (prefill.cu), then the head in blocks of kPrefillLogitRows rows: logits (all rows, or the last
-// row) and every row's argmax. The K/V of the chunk's tokens land at slots length .. length + n.
-static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const int32_t *pos, int32_t n, float *logits,
-                    bool all_logits, int32_t *argmax, cudaStream_t s) {
+// row) and every row's argmax. The K/V of the block land at slots *slot_base + 0 .. n - 1 (the
+// base is read on the device, so a captured graph serves any cache length). `mask`: tree-verify
+// ancestor masks (n <= kSmallNodes), else causal.
+static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const int32_t *pos, const uint64_t *mask,
+                           const int32_t *slot_base, int32_t n, float *logits, bool all_logits, int32_t *argmax,
+                           cudaStream_t s) {
     const sp_config &c = e->c;
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const float scale = 1.0f / sqrtf((float)c.head_dim);
     SP_CUDA(prefill_blas_stream(e->blas, s));
     for (int32_t b0 = 0; b0 < n; b0 += kPrefillMaxTokens) {
         const int T = std::min<int32_t>(kPrefillMaxTokens, n - b0);
-        const int slot0 = kv->length + b0;
         SP_CUDA(launch_prefill_embed(e->pf_dims, e->pf, e->embed, tok + b0, T, e->st, s));
         for (int l = 0; l < c.layers; ++l) {
             const PrefillLayer &L = e->layers[l].pf;
-            SP_CUDA(launch_prefill_layer_front(e->pf_dims, L, e->pf, T, pos ? pos + b0 : nullptr, kv->k + l * kv_layer,
-                                               kv->v + l * kv_layer, kv->capacity, slot0, scale, e->rope, e->st,
-                                               e->blas, s));
+            SP_CUDA(launch_prefill_layer_front(e->pf_dims, L, e->pf, T, pos ? pos + b0 : nullptr,
+                                               mask ? mask + b0 : nullptr, kv->k + l * kv_layer, kv->v + l * kv_layer,
+                                               kv->capacity, slot_base, b0, scale, e->rope, e->st, e->blas, s));
             SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->blas, s));
         }
         for (int r0 = 0; r0 < T; r0 += kPrefillLogitRows) {
@@ -1036,7 +1065,34 @@ static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const in
                                         cudaMemcpyDeviceToDevice, s));
         }
     }
-    kv->length += n;
+    return SP_OK;
+}
+
+// One verify pass of n tree nodes as a CUDA graph per (cache, n): inputs in e->vt, argmaxes out
+// in e->vt_argmax.
+static int verify_graph(sp_engine *e, sp_kv *kv, int n, cudaGraphExec_t *out) {
+    auto key = std::make_pair(kv, n);
+    auto it = e->vgraphs.find(key);
+    if (it != e->vgraphs.end()) {
+        *out = it->second;
+        return SP_OK;
+    }
+    cudaGraph_t g = nullptr;
+    SP_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = forward_batched(e, kv, e->vt->tok, e->vt->pos, e->vt->mask, &e->vt->slot0, n, nullptr, false,
+                             e->vt_argmax, e->cap_stream);
+    cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
+    if (rc != SP_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "verify graph capture: %s", cudaGetErrorString(ce));
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "verify graph instantiate: %s", cudaGetErrorString(ce));
+    e->vgraphs[key] = ex;
+    *out = ex;
     return SP_OK;
 }
 
@@ -1046,8 +1102,16 @@ int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t
     if (rc) return rc;
     if (n <= 0 || !tokens_dev) return fail(SP_ERR_INVALID, "input_ids cannot be empty");
     if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
-    if (e->prefill && n >= kPrefillMin) return forward_batched(e, kv, tokens_dev, positions_dev, n, logits_dev,
-                                                               all_logits != 0, argmax_dev, (cudaStream_t)stream);
+    if (e->prefill && n >= kPrefillMin) {
+        cudaStream_t s = (cudaStream_t)stream;
+        const int32_t base = kv->length;
+        SP_CUDA(cudaMemcpyAsync(&e->vt->slot0, &base, sizeof(base), cudaMemcpyHostToDevice, s));
+        rc = forward_batched(e, kv, tokens_dev, positions_dev, nullptr, &e->vt->slot0, n, logits_dev, all_logits != 0,
+                             argmax_dev, s);
+        if (rc) return rc;
+        kv->length += n;
+        return SP_OK;
+    }
     DevState d = base_state();
     d.n_forced = n;
     d.slot0 = kv->length;
@@ -1106,6 +1170,28 @@ int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const in
         d.small_pos[i] = base_pos + depth[i] - 1;
         if (d.small_pos[i] < 0 || d.small_pos[i] >= e->c.max_positions)
             return fail(SP_ERR_CAPACITY, "node %d: position outside the RoPE table", i);
+    }
+    if (e->prefill) {
+        // one batched pass over the tree: node i at scratch slot length + i, its ancestors' bits as
+        // the attention mask; the cache length does not move (sp_kv_commit keeps accepted nodes).
+        // Inputs go to the device in one copy; without logits the pass replays a captured graph.
+        cudaStream_t s = (cudaStream_t)stream;
+        VerifyIn in;
+        memset(&in, 0, sizeof(in));
+        in.slot0 = kv->length;
+        memcpy(in.tok, d.small_tok, n * sizeof(int32_t));
+        memcpy(in.pos, d.small_pos, n * sizeof(int32_t));
+        memcpy(in.mask, d.small_mask, n * sizeof(uint64_t));
+        SP_CUDA(cudaMemcpyAsync(e->vt, &in, sizeof(in), cudaMemcpyHostToDevice, s));
+        if (logits_dev)
+            return forward_batched(e, kv, e->vt->tok, e->vt->pos, e->vt->mask, &e->vt->slot0, n, logits_dev, true,
+                                   argmax_dev, s);
+        cudaGraphExec_t ex;
+        rc = verify_graph(e, kv, n, &ex);
+        if (rc) return rc;
+        SP_CUDA(cudaGraphLaunch(ex, s));
+        SP_CUDA(cudaMemcpyAsync(argmax_dev, e->vt_argmax, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+        return SP_OK;
     }
     d.use_small = 1;
     d.n_forced = n;

@@ -264,22 +264,25 @@ struct PrefillLayer {                    // row-major fp16 weights
 };
 struct PrefillScratch {
     float *x;                            // [T, hidden] residual stream
-    __half *xh, *xl;                     // [T, max(hidden, inter, heads * head_dim)] GEMM inputs
-    float *y;                            // [T, max(qkv rows, 2 inter)] GEMM outputs
+    __half *xh, *xl;                     // GEMM inputs [2T, K]: hi rows then lo rows (xl unused)
+    float *y;                            // [2T, max(qkv rows, 2 inter)] GEMM outputs (hi rows, lo rows)
     float *q;                            // [T, heads * head_dim]
     float *logits;                       // [kPrefillLogitRows, vocab]
 };
 size_t prefill_scratch_bytes(const PrefillDims &d);
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d);
-cudaError_t prefill_blas_create(void **handle);
+constexpr size_t kPrefillBlasWorkspace = 32u << 20;
+cudaError_t prefill_blas_create(void **handle, void *workspace, size_t workspace_bytes);
 cudaError_t prefill_blas_stream(void *handle, cudaStream_t s);
 void prefill_blas_destroy(void *handle);
 cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,
                                  const int32_t *tok, int T, DevState *st, cudaStream_t stream);
-// RMSNorm, QKV GEMM, bias + RoPE + K/V write at slots slot0 .., causal attention, O GEMM (+= x)
+// RMSNorm, QKV GEMM, bias + RoPE + K/V write at slots *slot_base + slot_off .., attention
+// (causal, or the tree of ancestor masks `mask` [T], T <= 64), O GEMM (+= x)
 cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
-                                       const int32_t *pos, __half *kc, __half *vc, int cap, int slot0, float scale,
-                                       const float *rope, DevState *st, void *cublas, cudaStream_t stream);
+                                       const int32_t *pos, const uint64_t *mask, __half *kc, __half *vc, int cap,
+                                       const int *slot_base, int slot_off, float scale, const float *rope,
+                                       DevState *st, void *cublas, cudaStream_t stream);
 // RMSNorm, gate_up GEMM, SwiGLU, down GEMM (+= x)
 cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
                                      void *cublas, cudaStream_t stream);

@@ -5,10 +5,13 @@
 // weights. Everything around them is this file's kernels: embedding gather, RMSNorm to fp16
 // hi / lo halves, bias + RoPE + K/V cache write, causal GQA attention over the cache, SwiGLU.
 // The activation of every GEMM is split like the decode step's: hi = fp16(x), lo = fp16(x - hi),
-// and the GEMM runs once on each (W x = W hi + W lo), so the products carry ~22 bits of the fp32
-// activation against the fp16 weights — the decode step's precision, which greedy token identity
-// with the fp32 reference depends on. The residual stream stays fp32 (the O and down GEMMs
-// accumulate into it with beta = 1).
+// stacked as 2T columns [hi rows; lo rows] so ONE GEMM reads the weights once, and the epilogues
+// add the two halves (W x = W hi + W lo): the products carry ~22 bits of the fp32 activation
+// against the fp16 weights — the decode step's precision, which greedy token identity with the
+// fp32 reference depends on. The residual stream stays fp32.
+//
+// The same pass verifies a draft tree: the T tokens are tree nodes (K/V at scratch slots) and
+// node t attends to the committed prefix and to the nodes whose bits its ancestor mask holds.
 #include <cublas_v2.h>
 
 #include <algorithm>
@@ -26,6 +29,17 @@ constexpr int kAttnKeys = 32;               // keys per staged tile (one per lan
 
 __device__ __forceinline__ void set_err(DevState *st, int code) {
     if (st) atomicCAS(&st->err, 0, code);
+}
+
+// First cache slot of the block: device-side base (so a captured graph serves any cache length)
+// plus the chunk offset; a block that would not fit the cache records an error and is clamped.
+__device__ __forceinline__ int block_slot0(const int *slot_base, int slot_off, int T, int cap, DevState *st) {
+    int s0 = *slot_base + slot_off;
+    if (s0 < 0 || s0 + T > cap) {
+        if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_err(st, kErrBadSlot);
+        s0 = min(max(s0, 0), max(cap - T, 0));
+    }
+    return s0;
 }
 
 // x[t] = embedding row of token t (ids outside the vocabulary record an error and read row 0)
@@ -65,20 +79,21 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __hal
 // y[t] = [q heads | k heads | v heads] (natural row order): bias, RoPE on q and k with the
 // position of token t, q -> fp32, k and v -> the fp16 cache at slot slot0 + t.
 __global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, const float *bias, const float *rope,
-                              const int32_t *pos, int nh, int nkv, int hd, int cap, int slot0, int max_pos,
-                              DevState *st) {
+                              const int32_t *pos, int T, int nh, int nkv, int hd, int cap, const int *slot_base,
+                              int slot_off, int max_pos, DevState *st) {
     const int t = blockIdx.x, half_hd = hd / 2, heads = nh + 2 * nkv;
+    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     int p = pos ? pos[t] : slot0 + t;
     if (p < 0 || p >= max_pos) {
         if (threadIdx.x == 0) set_err(st, kErrBadSlot);
         p = min(max(p, 0), max_pos - 1);
     }
-    const float *yr = y + (size_t)t * heads * hd;
+    const float *yr = y + (size_t)t * heads * hd, *yl = y + (size_t)(T + t) * heads * hd;
     const int slot = slot0 + t;
     for (int i = threadIdx.x; i < heads * half_hd; i += blockDim.x) {
         const int hh = i / half_hd, d = i - hh * half_hd;
         const int lo = hh * hd + d, hi = lo + half_hd;
-        const float a0 = yr[lo] + bias[lo], a1 = yr[hi] + bias[hi];
+        const float a0 = (yr[lo] + yl[lo]) + bias[lo], a1 = (yr[hi] + yl[hi]) + bias[hi];
         if (hh < nh + nkv) {
             const float cs = rope[((size_t)p * half_hd + d) * 2], sn = rope[((size_t)p * half_hd + d) * 2 + 1];
             const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
@@ -99,15 +114,19 @@ __global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, 
     }
 }
 
-// Causal GQA attention of T queries (slots slot0 .. slot0 + T - 1) over the cache: query t sees
-// slots [0, slot0 + t]. CTA = (q head, 16 queries), warp = 4 queries; keys in tiles of 32 staged
+// GQA attention of T queries (slots slot0 .. slot0 + T - 1) over the cache. Query t sees the slots
+// before slot0 and, among the block's own slots, [slot0, slot0 + t] (causal, mask == null) or the
+// slots slot0 + j whose bit j its ancestor mask holds (tree, T <= 64). CTA = (q head, 16 queries),
+// warp = 4 queries; keys in tiles of 32 staged
 // in shared memory (K rows padded by 4 bytes: lane j reads row j without bank conflicts). Scores,
 // online softmax (running max / sum per query) and the value sums in fp32; the output goes out as
 // fp16 hi / lo halves (the O projection's input).
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, const float *q, const __half *kc,
-                                                      const __half *vc, int T, int nh, int nkv, int cap, int slot0,
-                                                      float scale) {
+                                                      const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
+                                                      int cap, const int *slot_base, int slot_off, float scale,
+                                                      DevState *st) {
+    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     constexpr int DL = HD / 32;                       // output dims per lane
     constexpr int KROW = HD * 2 + 4;                  // padded K row (bytes)
     __shared__ __align__(16) float qs[kAttnQ][HD];
@@ -164,7 +183,8 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
         for (int i = 0; i < 4; ++i) {
             const int t = q0 + warp * 4 + i;
             const int key = k0 + lane;
-            const bool vis = t < T && key <= slot0 + t;
+            bool vis = t < T && key <= slot0 + t;
+            if (mask && vis && key >= slot0) vis = (mask[t] >> (key - slot0)) & 1ull;
             const float sv = vis ? s[i] : -INFINITY;
             const float mnew = fmaxf(m[i], warp_max(sv));
             const float p = mnew == -INFINITY ? 0.f : expf(sv - mnew);
@@ -197,17 +217,39 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
     }
 }
 
-// act = SiLU(gate) * up as fp16 hi / lo; y[t] = [gate (I) | up (I)]
-__global__ void k_swiglu_hilo(__half *ah, __half *al, const float *y, int I) {
+// act = SiLU(gate) * up as fp16 hi / lo; rows t and T + t of y are the two halves of [gate | up]
+__global__ void k_swiglu_hilo(__half *ah, __half *al, const float *y, int T, int I) {
     const int t = blockIdx.x;
     const float *g = y + (size_t)t * 2 * I, *u = g + I;
+    const float *gl = y + (size_t)(T + t) * 2 * I, *ul = gl + I;
     for (int j = threadIdx.x; j < I; j += blockDim.x) {
-        const float y0 = g[j], y1 = u[j];
+        const float y0 = g[j] + gl[j], y1 = u[j] + ul[j];
         const float a = (y0 / (1.0f + expf(-y0))) * y1;
         const __half hv = __float2half_rn(a);
         ah[(size_t)t * I + j] = hv;
         al[(size_t)t * I + j] = __float2half_rn(a - __half2float(hv));
     }
+}
+
+// out[t] = y[t] + y[n + t] (rows of `cols`); in place when out == y
+__global__ void k_sum_halves(float *out, const float *y, int n, int cols) {
+    const int t = blockIdx.y;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += gridDim.x * blockDim.x)
+        out[(size_t)t * cols + j] = y[(size_t)t * cols + j] + y[(size_t)(n + t) * cols + j];
+}
+
+// x[t] += y[t] + y[T + t]: the two halves of a projection into the residual stream
+__global__ void k_resid_add(float *x, const float *y, int T, int H) {
+    const int t = blockIdx.x;
+    for (int j = threadIdx.x; j < H; j += blockDim.x)
+        x[(size_t)t * H + j] += y[(size_t)t * H + j] + y[(size_t)(T + t) * H + j];
+}
+
+// Y2[2T, N] (row-major) = W[N, K] (row-major) . X2[2T, K]^T, X2 = [hi rows; lo rows]: one GEMM
+cublasStatus_t gemm_stacked(cublasHandle_t hb, const __half *w, int N, int K, const __half *x2, int T, float *y2) {
+    const float one = 1.0f, zero = 0.0f;
+    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &one, w, CUDA_R_16F, K, x2, CUDA_R_16F, K, &zero,
+                        y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
 // Y[T, N] (row-major, ldy) = beta * Y + W[N, K] (row-major) . (Xh + Xl)[T, K]^T, in two GEMMs
@@ -227,7 +269,7 @@ size_t prefill_scratch_bytes(const PrefillDims &d) {
     const size_t T = d.max_tokens;
     const size_t kmax = std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
     const size_t nmax = std::max((size_t)(d.heads + 2 * d.kv_heads) * d.head_dim, 2 * (size_t)d.inter);
-    return T * d.hidden * 4 + 2 * T * kmax * 2 + T * nmax * 4 + T * d.heads * d.head_dim * 4 +
+    return T * d.hidden * 4 + 2 * T * kmax * 2 + 2 * T * nmax * 4 + T * d.heads * d.head_dim * 4 +
            (size_t)kPrefillLogitRows * d.vocab * 4 + 5 * 256;
 }
 
@@ -240,12 +282,11 @@ PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
     PrefillScratch s{};
     s.x = reinterpret_cast<float *>(p);
     p += up(T * d.hidden * 4);
-    s.xh = reinterpret_cast<__half *>(p);
-    p += up(T * kmax * 2);
-    s.xl = reinterpret_cast<__half *>(p);
-    p += up(T * kmax * 2);
+    s.xh = reinterpret_cast<__half *>(p);      // [2T, kmax] halves: hi rows, then lo rows
+    p += up(2 * T * kmax * 2);
+    s.xl = nullptr;
     s.y = reinterpret_cast<float *>(p);
-    p += up(T * nmax * 4);
+    p += up(2 * T * nmax * 4);
     s.q = reinterpret_cast<float *>(p);
     p += up(T * d.heads * d.head_dim * 4);
     s.logits = reinterpret_cast<float *>(p);
@@ -253,22 +294,25 @@ PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
 }
 
 cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
-                                       const int32_t *pos, __half *kc, __half *vc, int cap, int slot0, float scale,
-                                       const float *rope, DevState *st, void *cublas, cudaStream_t stream) {
+                                       const int32_t *pos, const uint64_t *mask, __half *kc, __half *vc, int cap,
+                                       const int *slot_base, int slot_off, float scale, const float *rope,
+                                       DevState *st, void *cublas, cudaStream_t stream) {
     cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
-    const int H = d.hidden, QR = (d.heads + 2 * d.kv_heads) * d.head_dim;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x, L.in_norm, H, d.eps);
-    if (gemm_hilo(hb, L.qkv, QR, H, s.xh, s.xl, T, s.y, QR, 0.0f) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-    k_qkv_rope_kv<<<T, 256, 0, stream>>>(s.q, kc, vc, s.y, L.qkv_b, rope, pos, d.heads, d.kv_heads, d.head_dim, cap,
-                                         slot0, d.max_pos, st);
+    const int H = d.hidden, QR = (d.heads + 2 * d.kv_heads) * d.head_dim, A = d.heads * d.head_dim;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)T * H, s.x, L.in_norm, H, d.eps);
+    if (gemm_stacked(hb, L.qkv, QR, H, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_qkv_rope_kv<<<T, 256, 0, stream>>>(s.q, kc, vc, s.y, L.qkv_b, rope, pos, T, d.heads, d.kv_heads, d.head_dim,
+                                         cap, slot_base, slot_off, d.max_pos, st);
     const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
     if (d.head_dim == 128)
-        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xh, s.xl, s.q, kc, vc, T, d.heads, d.kv_heads, cap, slot0, scale);
+        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xh, s.xh + (size_t)T * A, s.q, kc, vc, mask, T, d.heads,
+                                                      d.kv_heads, cap, slot_base, slot_off, scale, st);
     else
-        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xh, s.xl, s.q, kc, vc, T, d.heads, d.kv_heads, cap, slot0, scale);
+        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xh, s.xh + (size_t)T * A, s.q, kc, vc, mask, T, d.heads,
+                                                     d.kv_heads, cap, slot_base, slot_off, scale, st);
     // O projection into the residual stream
-    if (gemm_hilo(hb, L.o, H, d.heads * d.head_dim, s.xh, s.xl, T, s.x, H, 1.0f) != CUBLAS_STATUS_SUCCESS)
-        return cudaErrorUnknown;
+    if (gemm_stacked(hb, L.o, H, A, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_resid_add<<<T, 256, 0, stream>>>(s.x, s.y, T, H);
     return cudaGetLastError();
 }
 
@@ -276,11 +320,11 @@ cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L
                                      void *cublas, cudaStream_t stream) {
     cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
     const int H = d.hidden, I = d.inter;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x, L.post_norm, H, d.eps);
-    if (gemm_hilo(hb, L.gate_up, 2 * I, H, s.xh, s.xl, T, s.y, 2 * I, 0.0f) != CUBLAS_STATUS_SUCCESS)
-        return cudaErrorUnknown;
-    k_swiglu_hilo<<<T, 256, 0, stream>>>(s.xh, s.xl, s.y, I);
-    if (gemm_hilo(hb, L.down, H, I, s.xh, s.xl, T, s.x, H, 1.0f) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)T * H, s.x, L.post_norm, H, d.eps);
+    if (gemm_stacked(hb, L.gate_up, 2 * I, H, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_swiglu_hilo<<<T, 256, 0, stream>>>(s.xh, s.xh + (size_t)T * I, s.y, T, I);
+    if (gemm_stacked(hb, L.down, H, I, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    k_resid_add<<<T, 256, 0, stream>>>(s.x, s.y, T, H);
     return cudaGetLastError();
 }
 
@@ -296,15 +340,27 @@ cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s,
                                   const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream) {
     cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
     const int H = d.hidden;
-    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xh, s.xl, s.x + (size_t)r0 * H, final_norm, H, d.eps);
-    if (gemm_hilo(hb, head, d.vocab, H, s.xh, s.xl, n, out, d.vocab, 0.0f) != CUBLAS_STATUS_SUCCESS)
+    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)n * H, s.x + (size_t)r0 * H, final_norm, H,
+                                                    d.eps);
+    if (2 * n <= kPrefillLogitRows) {
+        // one pass over the head: [hi rows; lo rows] into the scratch, then the halves summed
+        if (gemm_stacked(hb, head, d.vocab, H, s.xh, n, s.logits) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+        k_sum_halves<<<dim3(64, n), 256, 0, stream>>>(out, s.logits, n, d.vocab);
+    } else if (gemm_hilo(hb, head, d.vocab, H, s.xh, s.xh + (size_t)n * H, n, out, d.vocab, 0.0f) !=
+               CUBLAS_STATUS_SUCCESS) {
         return cudaErrorUnknown;
+    }
     return cudaGetLastError();
 }
 
-cudaError_t prefill_blas_create(void **handle) {
+cudaError_t prefill_blas_create(void **handle, void *workspace, size_t workspace_bytes) {
     cublasHandle_t h = nullptr;
     if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+    // a fixed workspace: no allocation inside a captured graph
+    if (cublasSetWorkspace(h, workspace, workspace_bytes) != CUBLAS_STATUS_SUCCESS) {
+        cublasDestroy(h);
+        return cudaErrorUnknown;
+    }
     *handle = h;
     return cudaSuccess;
 }
