@@ -118,6 +118,7 @@ struct sp_engine {
     StepLayout step_lay{};                  // shared memory of the step kernel
     int step_xmax = 0, step_max_chunks = 0;
     int step_inflight = 0;                  // ring copies in flight at most (0: all stages)
+    int step_l2_ahead = 0;                  // bytes per CTA prefetched into L2 ahead of the ring
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
     unsigned long long *epoch = nullptr;    // finished steps (never reset by set-state)
     int n_cnt = 0;
@@ -332,6 +333,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.max_chunks = e->step_max_chunks;
         p.evict_first = e->evict_first ? 1 : 0;
         p.max_inflight = e->step_inflight;
+        p.l2_ahead = e->step_l2_ahead;
         p.eps = c.rms_norm_eps;
         p.scale = 1.0f / sqrtf((float)c.head_dim);
         p.rope = e->rope;
@@ -550,6 +552,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->step_xmax = (int)align_up(std::max({H, I, (size_t)c.heads * HD}), 8);
         const int want = (int)env_long("SEEDPLANE_STEP_STAGES", 3);
         e->step_inflight = (int)env_long("SEEDPLANE_STEP_INFLIGHT", 0);
+        e->step_l2_ahead = (int)env_long("SEEDPLANE_STEP_L2_KB", 0) * 1024;
         e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, std::max(2, want));
         if (e->step_lay.stage_bytes < 16 * 1024 && want > 2) e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, 2);
         if (e->step_lay.stage_bytes < 16 * 1024) {

@@ -171,8 +171,9 @@ constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged at
 constexpr int kStepAttnRows = 48;        // attention positions staged per sub-chunk
 constexpr int kStepMaxChunks = 64;       // attention chunks per q head
 constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
-constexpr int kStepTraceWords = 8;       // per op and CTA: reached, dep met, input ready, done,
-                                         // first unit available, rows finished, merge start / end
+constexpr int kStepTraceWords = 16;      // per op and CTA: [0..7] %globaltimer: reached, dep met, input
+                                         // ready, done, first unit available, rows finished, merge
+                                         // start / end; [8..15] clock64 at the op's phase boundaries
 
 struct StepOp {
     const uint8_t *w;        // row-block packed weights (GEMV), see k_pack_rows
@@ -212,6 +213,7 @@ struct StepParams {
     int max_chunks;          // attention chunks per q head at most (nh * max_chunks <= grid)
     int evict_first;         // ring copies carry an L2 evict-first hint
     int max_inflight;        // ring copies in flight at most (0: stages)
+    int l2_ahead;            // bytes of its next units a CTA prefetches into L2 while its ring is full
     float eps, scale;
     const float *rope;
     const __half *embed;

@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
             *reinterpret_cast<uint4 *>(&vs[j][c * 8]) = vv;
         }
         __syncthreads();
+        __syncwarp();                                     // reconverged before the shuffles below
         // scores: lane = key k0 + lane, four queries of this warp
         float s[4] = {0.f, 0.f, 0.f, 0.f};
         const uint8_t *kr = ks + (size_t)lane * KROW;

@@ -151,6 +151,11 @@ SP_DEVINL void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// The compute warps' barrier. A warp can leave bar.sync with its lanes still split (they arrived
+// from divergent code), and a warp-collective instruction after that (shuffle reductions) then
+// pays a resynchronisation of hundreds of cycles: code that reduces across a warp right after
+// divergent code reconverges first with __syncwarp() (measured: the softmax phase 2900 -> 550
+// cycles). It is not added here or to the ring wait: measured, that costs more than it saves.
 SP_DEVINL void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
 SP_DEVINL unsigned long long ld_acquire_u64(const unsigned long long *p) {
@@ -177,7 +182,6 @@ SP_DEVINL void cp_async16(void *dst, const void *src) {
 SP_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 SP_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-SP_DEVINL float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
 // Abort state of the CTA: set on the first expired wait, after which no thread waits again.
 struct Abort {
@@ -339,6 +343,8 @@ struct AttnRegion {
 };
 
 // cp.async K/V rows [lo, hi) of one kv head into the sub-chunk buffers (row j -> local j - base).
+// In K rows the 16-byte chunks are XOR-permuted by (local row & 7): a thread per row reads chunk c
+// of 8 consecutive rows from 8 different bank groups. V rows keep their order.
 template <int HD>
 SP_DEVINL void stage_rows(uint8_t *am, const __half *kb, const __half *vb, int base, int lo, int hi, int tid) {
     using L = AttnRegion<HD>;
@@ -349,7 +355,7 @@ SP_DEVINL void stage_rows(uint8_t *am, const __half *kb, const __half *vb, int b
         const int r = (i - which * n * kChunks) / kChunks, ch = i % kChunks;
         const int j = lo + r;
         if (which == 0)
-            cp_async16(am + L::kOff + (size_t)(j - base) * L::kRow + ch * 16, kb + (size_t)j * HD + ch * 8);
+            cp_async16(am + L::kOff + (size_t)(j - base) * L::kRow + (ch ^ ((j - base) & 7)) * 16, kb + (size_t)j * HD + ch * 8);
         else
             cp_async16(am + L::vOff + (size_t)(j - base) * L::kRow + ch * 16, vb + (size_t)j * HD + ch * 8);
     }
@@ -376,6 +382,10 @@ SP_DEVINL int attn_chunks(int ctx, int max_chunks) {
 
 SP_DEVINL void stamp(unsigned long long *tr, int k, int C, int c, int i) {
     if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + i] = globaltimer();
+}
+// SM clock at phase boundary i (0..7) of op k: cycle-exact durations inside one CTA
+SP_DEVINL void stamp_clk(unsigned long long *tr, int k, int C, int c, int i) {
+    if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + 8 + i] = clock64();
 }
 
 // Per-step values every epilogue thread reads once (after the dependency on the previous step).
@@ -432,8 +442,10 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
         const uint64_t *kw = op.lkv + (size_t)g * HD + 2 * tid;
         uint64_t w[2][2];
         const uint32_t valid = tid < HD / 2 ? (cur ? 3u : 1u) : 0u;
+        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 0);
         ll_poll<2>(w, valid, [&](int j) { return j == 0 ? qw : kw; }, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
         stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
+        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 1);
         if (tid < HD / 2) {
             qs[2 * tid] = ll_f(w[0][0]);
             qs[2 * tid + 1] = ll_f(w[0][1]);
@@ -441,10 +453,14 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int i = 2 * tid + e, which = i / (HD / 2), dd = i - which * (HD / 2);
-                    __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)(slot - j0) * L::kRow);
+                    const int r = slot - j0;
+                    __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)r * L::kRow);
                     const uint32_t u = (uint32_t)w[1][e];
-                    row[dd] = __ushort_as_half((unsigned short)(u & 0xffffu));
-                    row[dd + HD / 2] = __ushort_as_half((unsigned short)(u >> 16));
+                    // dims dd and dd + HD/2; K chunks permuted like stage_rows'
+                    const int d0 = which ? dd : ((((dd >> 3) ^ (r & 7)) << 3) | (dd & 7));
+                    const int d1 = which ? dd + HD / 2 : (((((dd + HD / 2) >> 3) ^ (r & 7)) << 3) | (dd & 7));
+                    row[d0] = __ushort_as_half((unsigned short)(u & 0xffffu));
+                    row[d1] = __ushort_as_half((unsigned short)(u >> 16));
                 }
             }
         }
@@ -452,6 +468,8 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     cp_async_wait_all();
     epi_sync();
     stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 2);
+    __syncwarp();
 
     float qr[DL];
 #pragma unroll
@@ -468,42 +486,41 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
             cp_async_wait_all();
             epi_sync();
         }
-        // scores: four positions per warp in flight
-        for (int jl = warp; jl < nj; jl += 16) {
-            float t[4];
+        // scores: thread t = position t of the sub-chunk (nj <= kStepAttnRows <= kEpiThreads), a
+        // full dot product over HD dims: 16-byte K chunks (permuted by row, conflict-free) against
+        // q from shared memory (the same address in every lane: a broadcast). No shuffles.
+        if (tid < nj) {
+            const uint8_t *kr = am + L::kOff + (size_t)tid * L::kRow;
+            float sv = 0.f;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int j = jl + 4 * u;
-                float kf[DL];
-                if (j < nj) {
-                    load_dims<DL>(am + L::kOff + (size_t)j * L::kRow + lane * DL * 2, kf);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < DL; ++i) kf[i] = 0.f;
-                }
-                float v = qr[0] * kf[0];
-#pragma unroll
-                for (int i = 1; i < DL; ++i) v = fmaf(qr[i], kf[i], v);
-                t[u] = v;
+            for (int c = 0; c < HD / 8; ++c) {
+                const uint4 kq = *reinterpret_cast<const uint4 *>(kr + ((c ^ (tid & 7)) << 4));
+                const float4 qa = *reinterpret_cast<const float4 *>(qs + 8 * c);
+                const float4 qb = *reinterpret_cast<const float4 *>(qs + 8 * c + 4);
+                const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.x));
+                const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.y));
+                const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.z));
+                const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.w));
+                sv = fmaf(qa.x, k0.x, sv);
+                sv = fmaf(qa.y, k0.y, sv);
+                sv = fmaf(qa.z, k1.x, sv);
+                sv = fmaf(qa.w, k1.y, sv);
+                sv = fmaf(qb.x, k2.x, sv);
+                sv = fmaf(qb.y, k2.y, sv);
+                sv = fmaf(qb.z, k3.x, sv);
+                sv = fmaf(qb.w, k3.y, sv);
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int u = 0; u < 4; ++u) t[u] += __shfl_xor_sync(0xffffffffu, t[u], o);
-            if (lane == 0) {
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int j = jl + 4 * u, jj = a + j;
-                    if (j < nj) {
-                        const bool vis = !(jj >= ss.tree_base && !((ss.mask >> (jj - ss.tree_base)) & 1ull));
-                        sc[j] = vis ? t[u] * p.scale : -INFINITY;
-                    }
-                }
-            }
+            const int jj = a + tid;
+            const bool vis = !(jj >= ss.tree_base && !((ss.mask >> (jj - ss.tree_base)) & 1ull));
+            sc[tid] = vis ? sv * p.scale : -INFINITY;
         }
         epi_sync();
-        if (a == j0) stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
+        if (a == j0) {
+            stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
+            stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 3);
+        }
         if (warp == 0) {                        // softmax statistics over the sub-chunk
+            __syncwarp();
             const float v0 = lane < nj ? sc[lane] : -INFINITY;
             const float v1 = lane + 32 < nj ? sc[lane + 32] : -INFINITY;
             const float mnew = fmaxf(m_run, warp_max(fmaxf(v0, v1)));
@@ -518,6 +535,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
             if (lane == 0) s_corr = corr;
         }
         epi_sync();
+        if (a == j0) stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 4);
         // values: warp w sums positions w, w + 4, ...; lane = DL output dims
         float pa[DL];
 #pragma unroll
@@ -536,6 +554,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
         if (tid < HD) acc = fmaf(acc, s_corr, ((rd[tid] + rd[HD + tid]) + rd[2 * HD + tid]) + rd[3 * HD + tid]);
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
     uint64_t *pw = op.lpart + ((size_t)h * p.max_chunks + ch) * (HD + 2);
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
     if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc, tag));
@@ -569,8 +588,9 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
 #pragma unroll
             for (int j = 0; j < kLLBatch; ++j)
                 if (b0 + 2 * (tid + j * kEpiThreads) < nw) valid |= 1u << j;
+            // on abort every thread still passes the barriers below (the results are then unused)
             if (!ll_poll<kLLBatch>(w, valid, [&](int j) { return bw + b0 + 2 * (tid + j * kEpiThreads); }, tag, ab))
-                return;
+                valid = 0u;
 #pragma unroll
             for (int j = 0; j < kLLBatch; ++j) {
                 if ((valid >> j) & 1u) {
@@ -601,14 +621,134 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
     if (tid < HD) ll_st1(op.lout + (size_t)h * HD + tid, ll_word(hilo_bits(A / Ls), tag));
 }
 
+// The LM head's argmax across CTAs (last arriver) and the device state of the next step; once
+// per step, so out of line (it keeps the step's hot code smaller).
+__device__ __noinline__ void lmhead_finish(const StepParams &p, const StepOp &op, const StepState &ss, DevState *st,
+                                           float bv, int bi, int c) {
+    __shared__ float s_val[4];
+    __shared__ int s_idx[4];
+    __shared__ int s_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+    }
+    if (lane == 0) {
+        s_val[warp] = bv;
+        s_idx[warp] = bi;
+    }
+    epi_sync();
+    if (tid == 0) {
+        float vb = s_val[0];
+        int ib = s_idx[0];
+        for (int w = 1; w < 4; ++w) argmax_merge(vb, ib, s_val[w], s_idx[w]);
+        p.part_val[c] = vb;
+        p.part_idx[c] = ib;
+        s_flag = atom_add_acq_rel(p.lm_cnt, 1u) == (unsigned)op.grid - 1u;
+    }
+    epi_sync();
+    if (s_flag) {
+        float vb = -INFINITY;
+        int ib = INT_MAX;
+        for (int j = tid; j < op.grid; j += kEpiThreads)
+            argmax_merge(vb, ib, __ldcg(p.part_val + j), __ldcg(p.part_idx + j));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, vb, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ib, o);
+            argmax_merge(vb, ib, ov, oi);
+        }
+        epi_sync();
+        if (lane == 0) {
+            s_val[warp] = vb;
+            s_idx[warp] = ib;
+        }
+        epi_sync();
+        if (tid == 0) {
+            for (int w = 1; w < 4; ++w) argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
+            int tok = s_idx[0];
+            if (tok < 0 || tok >= op.n_valid) {
+                atomicCAS(&st->err, 0, kErrBadToken);
+                tok = 0;
+            }
+            *p.lm_cnt = 0u;
+            const int step = st->step;
+            if (st->out_tokens) st->out_tokens[step] = tok;
+            const int nxt = step + 1;
+            st->step = nxt;
+            if (nxt < st->n_forced) {
+                st->slot = st->slot0 + nxt;
+                st->token = st->use_small ? st->small_tok[nxt] : st->f_tok[nxt];
+                st->pos = st->use_small ? st->small_pos[nxt] : (st->f_pos ? st->f_pos[nxt] : st->slot0 + nxt);
+            } else {
+                st->token = tok;
+                st->pos += 1;
+                st->slot += 1;
+            }
+            *p.epoch = ss.epoch + 1;
+        }
+    }
+}
+
+// The CTA's weight units of the step in consumption order (op, pass, chunk). A unit's bytes are
+// contiguous and follow the previous unit of the same op (see k_pack_rows). Op fields are read
+// from the table in global memory when the cursor enters an op, lazily (at the next call), so a
+// unit is handed out without waiting for the next op's descriptor.
+struct UnitCursor {
+    const StepOp *ops;
+    int n_ops, c;
+    int k = -1;                     // current op; n_ops: exhausted
+    int K = 0, cw = 0, prw = 0, R = 0, p0 = 0, q0 = 0;
+    bool pending = false;           // the current op is used up: seek the next one first
+    const uint8_t *src = nullptr;
+
+    SP_DEVINL void seek(int from) {
+        for (k = from; k < n_ops; ++k) {
+            const StepOp *o = ops + k;
+            if (__ldg(&o->kind) != OP_GEMV) continue;
+            const int grid = __ldg(&o->grid);
+            if (c >= grid) continue;
+            const int P = __ldg(&o->N) / 2;
+            const int R0 = 2 * (int)((long long)P * c / grid);
+            R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+            if (R <= 0) continue;
+            K = __ldg(&o->K);
+            cw = __ldg(&o->chunk_w);
+            prw = __ldg(&o->pass_rows);
+            src = reinterpret_cast<const uint8_t *>(__ldg(reinterpret_cast<const unsigned long long *>(&o->w))) +
+                  (size_t)R0 * K * 2;
+            p0 = 0;
+            q0 = 0;
+            return;
+        }
+    }
+    SP_DEVINL bool next(const uint8_t *&unit, uint32_t &bytes) {
+        if (pending) {
+            pending = false;
+            seek(k + 1);
+        }
+        if (k >= n_ops) return false;
+        bytes = (uint32_t)(min(prw, R - p0) * min(cw, K - q0) * 2);
+        unit = src;
+        src += bytes;
+        q0 += cw;
+        if (q0 >= K) {
+            q0 = 0;
+            p0 += prw;
+            if (p0 >= R) pending = true;
+        }
+        return true;
+    }
+};
+
 }  // namespace
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ float s_val[4];
-    __shared__ int s_idx[4];
-    __shared__ int s_flag;
     __shared__ int s_abort;
     __shared__ int s_issued, s_consumed;      // stages the producer issued / the compute warps consumed
     __shared__ float red[4][kPassRows];       // per-warp row partials of a pass (k-steps split over warps)
@@ -644,66 +784,74 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     __syncthreads();
 
     if (warp == kProducerWarp) {
-        // ---- producer: every unit of the step, in op order; waits only for free stages ----------
+        // ---- producer: every unit of the step, in op order; waits only for free stages. While it
+        // waits (the ring is full: the other warps are in a hand-off or a small op), it warms L2 with
+        // the CTA's next units, up to p.l2_ahead bytes beyond the issue point, so HBM keeps
+        // streaming through the latency-bound phases and the big ops later read from L2. ---------
         if (lane == 0) {
             int s = 0, round = 0, issued = 0;
             const int F = p.max_inflight > 0 ? min(p.max_inflight, S) : S;
             const uint64_t pol = policy_evict_first();
-            // the fields of op k, read one op ahead from the table in global memory
-            int kind = __ldg(&p.ops[0].kind), grid = __ldg(&p.ops[0].grid), N = __ldg(&p.ops[0].N),
-                K = __ldg(&p.ops[0].K), prw = __ldg(&p.ops[0].pass_rows), cw = __ldg(&p.ops[0].chunk_w);
-            const uint8_t *w = reinterpret_cast<const uint8_t *>(
-                __ldg(reinterpret_cast<const unsigned long long *>(&p.ops[0].w)));
-            for (int k = 0; k < p.n_ops && !ab.on(); ++k) {
-                int nkind = OP_ATTN, ngrid = 0, nN = 0, nK = 0, nprw = 0, ncw = 0;
-                const uint8_t *nw = nullptr;
-                if (k + 1 < p.n_ops) {
-                    const StepOp *o = p.ops + k + 1;
-                    nkind = __ldg(&o->kind);
-                    ngrid = __ldg(&o->grid);
-                    nN = __ldg(&o->N);
-                    nK = __ldg(&o->K);
-                    nprw = __ldg(&o->pass_rows);
-                    ncw = __ldg(&o->chunk_w);
-                    nw = reinterpret_cast<const uint8_t *>(__ldg(reinterpret_cast<const unsigned long long *>(&o->w)));
+            UnitCursor ic{p.ops, p.n_ops, c};
+            ic.seek(0);
+            UnitCursor pc = ic;
+            int pc_idx = 0;                     // units the prefetch cursor has passed
+            uint32_t ahead = 0;                 // bytes prefetched beyond the issue point
+            bool pf_more = p.l2_ahead > 0;
+            const uint8_t *u;
+            uint32_t nb;
+            while (!ab.on() && ic.next(u, nb)) {
+                if (pc_idx <= issued) {         // the prefetch cursor restarts right after this unit
+                    pc = ic;
+                    pc_idx = issued + 1;
+                    ahead = 0;
+                } else {
+                    ahead -= nb;                // this unit was prefetched
                 }
-                if (kind == OP_GEMV && c < grid) {
-                    const int P = N / 2;
-                    const int R0 = 2 * (int)((long long)P * c / grid);
-                    const int R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
-                    const uint8_t *src = w + (size_t)R0 * K * 2;
-                    for (int p0 = 0; p0 < R && !ab.on(); p0 += prw) {
-                        const int rows = min(prw, R - p0);
-                        for (int q0 = 0; q0 < K; q0 += cw) {
-                            const uint32_t nb = (uint32_t)(rows * min(cw, K - q0) * 2);
-                            if (round > 0 && !wait_bar(&empty[s], (uint32_t)(round - 1) & 1u, ab)) break;
-                            // at most F copies in flight: unit issued - F must have landed (its stage
-                            // is not refilled before this one is issued, so its phase parity is exact)
-                            if (issued >= F) {
-                                const int u = issued - F;
-                                if (!wait_bar(&full[u % S], (uint32_t)(u / S) & 1u, ab)) break;
-                            }
-                            mbar_arrive_expect_tx(&full[s], nb);
-                            if (p.evict_first)
-                                bulk_g2s_hint(ring + (size_t)s * SB, src, nb, &full[s], pol);
-                            else
-                                bulk_g2s(ring + (size_t)s * SB, src, nb, &full[s]);
-                            src += nb;
-                            ++issued;
-                            if (++s == S) {
-                                s = 0;
-                                ++round;
+                if (round > 0) {
+                    const uint32_t par = (uint32_t)(round - 1) & 1u;
+                    bool ok = false;
+                    for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+                        // with prefetch budget left, probe without blocking and prefetch in between
+                        const bool pf = pf_more && ahead < (uint32_t)p.l2_ahead;
+                        if (pf ? mbar_test_wait(&empty[s], par) : mbar_try_wait(&empty[s], par)) {
+                            ok = true;
+                            break;
+                        }
+                        if (pf) {
+                            const uint8_t *pu;
+                            uint32_t pnb;
+                            if (pc.next(pu, pnb)) {
+                                prefetch_l2(pu, pnb);
+                                ahead += pnb;
+                                ++pc_idx;
+                            } else {
+                                pf_more = false;
                             }
                         }
+                        if ((i & 255u) == 255u && ab.on()) break;
+                    }
+                    if (!ok) {
+                        if (!ab.on()) ab.raise(kErrMbarTimeout);
+                        break;
                     }
                 }
-                kind = nkind;
-                grid = ngrid;
-                N = nN;
-                K = nK;
-                prw = nprw;
-                cw = ncw;
-                w = nw;
+                // at most F copies in flight: unit issued - F must have landed (its stage is not
+                // refilled before this one is issued, so its phase parity is exact)
+                if (issued >= F) {
+                    const int uu = issued - F;
+                    if (!wait_bar(&full[uu % S], (uint32_t)(uu / S) & 1u, ab)) break;
+                }
+                mbar_arrive_expect_tx(&full[s], nb);
+                if (p.evict_first)
+                    bulk_g2s_hint(ring + (size_t)s * SB, u, nb, &full[s], pol);
+                else
+                    bulk_g2s(ring + (size_t)s * SB, u, nb, &full[s]);
+                ++issued;
+                if (++s == S) {
+                    s = 0;
+                    ++round;
+                }
             }
             s_issued = issued;
         }
@@ -752,8 +900,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     const int h = item / n_chunks;
                     if (item == h * n_chunks) {          // chunk 0 of the head: merge all of them
                         stamp(p.trace, k, C, c, 6);
+                        stamp_clk(p.trace, k, C, c, 6);
                         merge_head<HD>(p, op, ss, am, h, n_chunks, k, ab);
                         stamp(p.trace, k, C, c, 7);
+                        stamp_clk(p.trace, k, C, c, 7);
                     }
                 }
                 stamp(p.trace, k, C, c, 3);
@@ -765,6 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 if (item < p.nh * n_chunks) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
+            stamp_clk(p.trace, k, C, c, 0);
             const int K = op.K;
             __half *xl = xh + K;
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
@@ -803,6 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 } else {
                     ll_norm_input(v, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
                 }
+                __syncwarp();
                 float sq = 0.f;
 #pragma unroll
                 for (int q = 0; q < kNormRegs; ++q) {
@@ -828,16 +980,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             } else if (op.pro == PRO_ATTN) {
                 ll_hilo_input(xh, xl, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
             } else {
-                // PRO_PLAIN: fp16 hi / lo vectors behind the dependency counter: copy them
+                // PRO_PLAIN: fp16 hi / lo vectors behind the dependency counter: every 16-byte piece
+                // in flight at once (cp.async through L2), one wait
                 for (int i = tid; i < K / 8; i += kEpiThreads) {
-                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(op.xin_h) + i);
-                    const uint4 lv = __ldcg(reinterpret_cast<const uint4 *>(op.xin_l) + i);
-                    reinterpret_cast<uint4 *>(xh)[i] = hv;
-                    reinterpret_cast<uint4 *>(xl)[i] = lv;
+                    cp_async16(reinterpret_cast<uint4 *>(xh) + i, reinterpret_cast<const uint4 *>(op.xin_h) + i);
+                    cp_async16(reinterpret_cast<uint4 *>(xl) + i, reinterpret_cast<const uint4 *>(op.xin_l) + i);
                 }
+                cp_async_commit();
+                cp_async_wait_all();
             }
             epi_sync();
             stamp(p.trace, k, C, c, 2);
+            stamp_clk(p.trace, k, C, c, 1);
 
             // ---- rows: passes of up to kPassRows rows, each over all inputs in chunks ---------------
             const int P = op.N / 2;
@@ -879,6 +1033,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         }
                     }
                 }
+                __syncwarp();                                       // after the per-pair preload
                 // tensor-core products: A = 16 weight rows x 16 inputs (ldmatrix from the swizzled
                 // unit), B column 0 = hi, column 1 = lo of the inputs, fp32 accumulators; warp w
                 // takes k-steps w, w + 4, ... of every row tile
@@ -890,14 +1045,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 for (int q0 = 0; q0 < K; q0 += op.chunk_w) {
                     const int wq = min(op.chunk_w, K - q0);
                     if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
-                    if (p0 == 0 && q0 == 0) stamp(p.trace, k, C, c, 4);
+                    if (p0 == 0 && q0 == 0) {
+                        stamp(p.trace, k, C, c, 4);
+                        stamp_clk(p.trace, k, C, c, 2);
+                    }
                     const uint32_t unit = smem_u32(ring + (size_t)s * SB);
                     const int rs = wq * 2;                          // row stride (bytes) inside the unit
                     const int nks = wq >> 4;
                     if (nrt == 1)
                         unit_mma<4>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
-                    else if (nrt == 2)
-                        unit_mma<2>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
                     else
                         unit_mma<1>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
                     epi_sync();                                     // every warp is done with the unit
@@ -908,13 +1064,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         ++round;
                     }
                 }
+                if (p0 == 0) stamp_clk(p.trace, k, C, c, 3);
                 // row sums: lanes 4i hold rows i and i + 8 of each tile (columns 0 = hi, 1 = lo);
                 // tile rt's U accumulator slots are summed in slot order
                 if ((lane & 3) == 0) {
                     if (nrt == 1)
                         rows_from_acc<4>(d, red[warp], nrt, lane);
-                    else if (nrt == 2)
-                        rows_from_acc<2>(d, red[warp], nrt, lane);
                     else
                         rows_from_acc<1>(d, red[warp], nrt, lane);
                 }
@@ -971,73 +1126,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             }
             epi_sync();                                             // `red` is reused by the next op
             stamp(p.trace, k, C, c, 5);
+            stamp_clk(p.trace, k, C, c, 4);
 
             if (op.epi == EPI_LMHEAD) {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    argmax_merge(bv, bi, ov, oi);
-                }
-                if (lane == 0) {
-                    s_val[warp] = bv;
-                    s_idx[warp] = bi;
-                }
-                epi_sync();
-                if (tid == 0) {
-                    float vb = s_val[0];
-                    int ib = s_idx[0];
-                    for (int w = 1; w < 4; ++w) argmax_merge(vb, ib, s_val[w], s_idx[w]);
-                    p.part_val[c] = vb;
-                    p.part_idx[c] = ib;
-                    s_flag = atom_add_acq_rel(p.lm_cnt, 1u) == (unsigned)op.grid - 1u;
-                }
-                epi_sync();
-                if (s_flag) {
-                    float vb = -INFINITY;
-                    int ib = INT_MAX;
-                    for (int j = tid; j < op.grid; j += kEpiThreads)
-                        argmax_merge(vb, ib, __ldcg(p.part_val + j), __ldcg(p.part_idx + j));
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const float ov = __shfl_xor_sync(0xffffffffu, vb, o);
-                        const int oi = __shfl_xor_sync(0xffffffffu, ib, o);
-                        argmax_merge(vb, ib, ov, oi);
-                    }
-                    epi_sync();
-                    if (lane == 0) {
-                        s_val[warp] = vb;
-                        s_idx[warp] = ib;
-                    }
-                    epi_sync();
-                    if (tid == 0) {
-                        for (int w = 1; w < 4; ++w) argmax_merge(s_val[0], s_idx[0], s_val[w], s_idx[w]);
-                        int tok = s_idx[0];
-                        if (tok < 0 || tok >= op.n_valid) {
-                            atomicCAS(&st->err, 0, kErrBadToken);
-                            tok = 0;
-                        }
-                        *p.lm_cnt = 0u;
-                        const int step = st->step;
-                        if (st->out_tokens) st->out_tokens[step] = tok;
-                        const int nxt = step + 1;
-                        st->step = nxt;
-                        if (nxt < st->n_forced) {
-                            st->slot = st->slot0 + nxt;
-                            st->token = st->use_small ? st->small_tok[nxt] : st->f_tok[nxt];
-                            st->pos = st->use_small ? st->small_pos[nxt] : (st->f_pos ? st->f_pos[nxt] : st->slot0 + nxt);
-                        } else {
-                            st->token = tok;
-                            st->pos += 1;
-                            st->slot += 1;
-                        }
-                        *p.epoch = ss.epoch + 1;
-                    }
-                }
+                lmhead_finish(p, op, ss, st, bv, bi, c);
             } else if (op.sig >= 0) {
                 if (tid == 0) red_add_release(p.cnt + op.sig, 1ull);   // after the barrier above
             }
             stamp(p.trace, k, C, c, 3);
+            stamp_clk(p.trace, k, C, c, 5);
         }
         cp_async_wait_all();
         if (tid == 0) s_consumed = consumed;

@@ -65,6 +65,39 @@ def step_trace_summary(t, layers, layers_shown=(0, 1, 13)):
     return {"step_span_us": round(span, 1), "layer_us_median": round(float(np.median(per_layer)), 2), "ops": rows}
 
 
+GEMV_PHASES = ("prologue", "unit_wait", "mma", "epilogue", "signal")
+ATTN_PHASES = ("poll_qkv", "stage", "scores", "softmax", "values", "publish_to_merge", "merge")
+
+
+def step_phase_summary(clk, gt, layers):
+    """Median per-CTA phase durations (microseconds, from clock64 at the SM clock) per op kind over
+    layers 1 .. L-1: GEMV [0] start [1] input ready [2] first unit [3] MMA done [4] epilogue done
+    [5] signalled; attention [0] poll start [1] q/kv seen [2] staged [3] scores [4] softmax
+    [5] values done [6] merge start [7] merge end."""
+    import numpy as np
+    c = clk.astype(np.float64)
+    g = gt.astype(np.float64)
+    # SM clock from the first and the last layer's QKV op: clock64 cycles per %globaltimer ns
+    k1 = 5 * (layers - 1)
+    dc, dt = c[k1, :, 0] - c[0, :, 0], g[k1, :, 0] - g[0, :, 0]
+    ok = (c[k1, :, 0] > 0) & (c[0, :, 0] > 0) & (dt > 0)
+    mhz = float(np.median(dc[ok] / dt[ok])) * 1000.0 if ok.any() else 1965.0
+    out = {}
+    for j, kind in enumerate(STEP_OPS):
+        ks = [5 * l + j for l in range(1, layers)]
+        x = c[ks]                                            # [layers - 1, sms, 8]
+        names = ATTN_PHASES if kind == "attn" else GEMV_PHASES
+        d = {}
+        for i, name in enumerate(names):
+            a, b = x[:, :, i], x[:, :, i + 1]
+            ok = (a > 0) & (b > 0) & (b >= a)
+            if ok.any():
+                d[name] = round(float(np.median((b - a)[ok])) / mhz, 3)
+        out[kind] = d
+    out["sm_mhz"] = round(mhz, 1)
+    return out
+
+
 def trace_summary(eng, layers_shown=(0, 1, 13)):
     """Per-GEMV timeline of the last step from the %globaltimer stamps (microseconds)."""
     import ctypes as C
@@ -77,9 +110,11 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
     buf = (C.c_uint64 * n)()
     N.check(0 if lib.sp_trace_read(eng.handle, buf, n) == n else -2)
     sms = torch.cuda.get_device_properties(eng.device).multi_processor_count
-    if n == (5 * eng.cfg.layers + 1) * sms * 8:        # persistent step kernel
-        return step_trace_summary(np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(-1, sms, 8),
-                                  eng.cfg.layers, layers_shown)
+    if n == (5 * eng.cfg.layers + 1) * sms * 16:       # persistent step kernel
+        raw = np.frombuffer(buf, dtype=np.uint64).reshape(-1, sms, 16)
+        out = step_trace_summary(raw[:, :, :8].astype(np.float64), eng.cfg.layers, layers_shown)
+        out["phases_us"] = step_phase_summary(raw[:, :, 8:], raw[:, :, :8], eng.cfg.layers)
+        return out
     words = 8 + 2 * 24
     t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(-1, torch.cuda.get_device_properties(
         eng.device).multi_processor_count, words)
