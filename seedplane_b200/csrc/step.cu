@@ -919,6 +919,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             const int K = op.K;
             __half *xl = xh + K;
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
+            const int P = op.N / 2;
+            const int R0 = 2 * (int)((long long)P * c / op.grid);
+            const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
+            // epilogue operands that do not depend on the products (residual rows, bias, RoPE
+            // factors): thread t < npairs finishes pair t (rows 2t, 2t + 1) of a pass. Pass 0's are
+            // loaded before the input wait, where their round trip costs nothing.
+            auto preload = [&](int p0, float &pre0, float &pre1, float &pcs, float &psn) {
+                const int rows_p = min(op.pass_rows, R - p0);
+                const int row = R0 + p0 + 2 * tid;                  // packed row (row, row + 1)
+                pre0 = 0.f;
+                pre1 = 0.f;
+                pcs = 1.f;
+                psn = 0.f;
+                if (tid < rows_p / 2 && row < op.n_valid) {
+                    if (op.epi == EPI_RESID) {
+                        if (op.lres == nullptr) {                   // layer 0: the token's embedding row
+                            const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
+                            pre0 = __low2float(e2);
+                            pre1 = __high2float(e2);
+                        } else {
+                            uint64_t w[1][2];
+                            ll_poll<1>(w, 1u, [&](int) { return op.lres + row; }, ll_tag(ss.epoch, p.n_ops, op.lres_k), ab);
+                            pre0 = ll_f(w[0][0]);
+                            pre1 = ll_f(w[0][1]);
+                        }
+                    } else if (op.epi == EPI_QKV) {
+                        const int P2 = row / 2, hh = P2 / half_hd, dd = P2 - hh * half_hd;
+                        pre0 = __ldg(op.bias + hh * HD + dd);
+                        pre1 = __ldg(op.bias + hh * HD + dd + half_hd);
+                        if (hh < p.nh + p.nkv) {
+                            const float2 r2 = __ldg(reinterpret_cast<const float2 *>(p.rope + ((size_t)ss.pos * half_hd + dd) * 2));
+                            pcs = r2.x;
+                            psn = r2.y;
+                        }
+                    }
+                }
+                __syncwarp();                                       // after the per-pair loads
+            };
+            float pre0, pre1, pcs, psn;
+            preload(0, pre0, pre1, pcs, psn);
             float4 gn[kNormRegs];
             if (norm) {
 #pragma unroll
@@ -994,9 +1034,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             stamp_clk(p.trace, k, C, c, 1);
 
             // ---- rows: passes of up to kPassRows rows, each over all inputs in chunks ---------------
-            const int P = op.N / 2;
-            const int R0 = 2 * (int)((long long)P * c / op.grid);
-            const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
             float *lg = nullptr;
             if (op.epi == EPI_LMHEAD && st->logits != nullptr && st->step >= st->logits_from)
                 lg = st->logits + st->logits_stride * (long long)st->step;
@@ -1005,35 +1042,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             for (int p0 = 0; p0 < R && !ab.on(); p0 += op.pass_rows) {
                 const int rows_p = min(op.pass_rows, R - p0);
                 const int nrt = (rows_p + 15) >> 4;                 // 16-row tiles of the pass (<= 4)
-                // epilogue operands that do not depend on the products: thread t < npairs finishes
-                // pair t (rows 2t, 2t + 1 of the pass)
                 const int row = R0 + p0 + 2 * tid;                  // packed row (row, row + 1)
                 const bool mine = tid < rows_p / 2 && row < op.n_valid;
-                float pre0 = 0.f, pre1 = 0.f, pcs = 1.f, psn = 0.f;
-                if (mine) {
-                    if (op.epi == EPI_RESID) {
-                        if (op.lres == nullptr) {                   // layer 0: the token's embedding row
-                            const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
-                            pre0 = __low2float(e2);
-                            pre1 = __high2float(e2);
-                        } else {
-                            uint64_t w[1][2];
-                            ll_poll<1>(w, 1u, [&](int) { return op.lres + row; }, ll_tag(ss.epoch, p.n_ops, op.lres_k), ab);
-                            pre0 = ll_f(w[0][0]);
-                            pre1 = ll_f(w[0][1]);
-                        }
-                    } else if (op.epi == EPI_QKV) {
-                        const int P2 = row / 2, hh = P2 / half_hd, dd = P2 - hh * half_hd;
-                        pre0 = __ldg(op.bias + hh * HD + dd);
-                        pre1 = __ldg(op.bias + hh * HD + dd + half_hd);
-                        if (hh < p.nh + p.nkv) {
-                            const float2 r2 = __ldg(reinterpret_cast<const float2 *>(p.rope + ((size_t)ss.pos * half_hd + dd) * 2));
-                            pcs = r2.x;
-                            psn = r2.y;
-                        }
-                    }
-                }
-                __syncwarp();                                       // after the per-pair preload
+                if (p0 > 0) preload(p0, pre0, pre1, pcs, psn);      // pass 0: preloaded before the input
                 // tensor-core products: A = 16 weight rows x 16 inputs (ldmatrix from the swizzled
                 // unit), B column 0 = hi, column 1 = lo of the inputs, fp32 accumulators; warp w
                 // takes k-steps w, w + 4, ... of every row tile
