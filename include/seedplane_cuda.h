@@ -132,6 +132,13 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
 int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
               void *stream);
 
+/* Per-row top-k of fp32 logits, k in 1..8: indices and values [rows][k] ordered by larger value,
+ * lower index on ties (the greedy argmax's rule), and each row's log-sum-exp, so log-probabilities
+ * are val - lse. Replaces the drafter-side `torch.topk` + `log_softmax` a tree drafter needs; the
+ * reference has no drafter tree (seedplane/speculative.py:18-43 takes given branches). */
+int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t k,
+            int32_t *idx_dev, float *val_dev, float *lse_dev, void *stream);
+
 /* sp_argmax without an engine and without any allocation (no reference counterpart: the
  * reference allocates nothing on this path; this entry point exists for callers that must not
  * allocate device memory, e.g. inside a memory-capped serving process or before an engine

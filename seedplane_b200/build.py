@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libseedplane_cuda.so"
-SOURCES = ["kernels.cu", "gemv_tc.cu", "attention.cu", "argmax.cu", "step.cu", "prefill.cu", "engine.cu"]
+SOURCES = ["kernels.cu", "gemv_tc.cu", "attention.cu", "argmax.cu", "step.cu", "prefill.cu", "sample.cu", "engine.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1245,6 +1245,16 @@ int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols,
     return SP_OK;
 }
 
+int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t k,
+            int32_t *idx_dev, float *val_dev, float *lse_dev, void *stream) {
+    if (!e || !logits_dev || !idx_dev || !val_dev || !lse_dev) return fail(SP_ERR_INVALID, "null argument");
+    if (rows <= 0 || cols <= 0 || ld < cols) return fail(SP_ERR_INVALID, "bad logits shape");
+    if (k < 1 || k > kTopkMax || k > cols) return fail(SP_ERR_INVALID, "k must be in 1..%d and <= cols", kTopkMax);
+    SP_CUDA(cudaSetDevice(e->device));
+    SP_CUDA(launch_topk_rows(logits_dev, rows, cols, ld, k, idx_dev, val_dev, lse_dev, (cudaStream_t)stream));
+    return SP_OK;
+}
+
 int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
                       void *stream) {
     if (!logits_dev || !argmax_dev) return fail(SP_ERR_INVALID, "null logits or output");

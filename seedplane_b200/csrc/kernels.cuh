@@ -292,6 +292,12 @@ cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
                                   const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream);
 
+// Per-row top-k (k <= kTopkMax; larger value first, lower index on ties) and log-sum-exp of fp32
+// logits (sample.cu): idx / val [rows][k], lse [rows].
+constexpr int kTopkMax = 8;
+cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long ld, int k, int *idx, float *val,
+                             float *lse, cudaStream_t s);
+
 // Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
 // (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per
 // row, which must be zero when the kernel starts and is zero again when it ends.

@@ -242,6 +242,21 @@ class CudaQwen2:
         N.check(N.load().sp_kv_commit(kv.handle, N.int_array(src_slots), len(src_slots),
                                       C.c_void_p(_stream(self.device))))
 
+    def topk(self, logits: torch.Tensor, k: int):
+        """Per-row top-k of fp32 logits on the device: (indices int32 [rows, k], values [rows, k],
+        log-sum-exp [rows]); larger value first, lower index on ties."""
+        x = logits if logits.dim() == 2 else logits.reshape(1, -1)
+        if x.dtype != torch.float32 or x.device != self.device or x.stride(1) != 1:
+            raise ValueError("topk wants fp32 logits on the engine's device, rows contiguous")
+        rows, cols = x.shape
+        idx = torch.empty((rows, k), dtype=torch.int32, device=self.device)
+        val = torch.empty((rows, k), dtype=torch.float32, device=self.device)
+        lse = torch.empty(rows, dtype=torch.float32, device=self.device)
+        N.check(N.load().sp_topk(self.handle, C.c_void_p(x.data_ptr()), rows, cols, x.stride(0), k,
+                                 C.c_void_p(idx.data_ptr()), C.c_void_p(val.data_ptr()), C.c_void_p(lse.data_ptr()),
+                                 C.c_void_p(_stream(self.device))))
+        return idx, val, lse
+
     def argmax(self, logits: torch.Tensor) -> torch.Tensor:
         """Row-wise greedy argmax (lowest index on ties) of fp32 logits [rows, V] on this device."""
         if logits.device != self.device or logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:

@@ -220,3 +220,115 @@ class CommitLedger:
         self.tokens.extend(committed)
         self.commits += 1
         return committed
+
+
+# ---- tree drafting and the speculative decode loop (the cfg2 workload) ---------------------------
+def draft_tree(drafter, dkv, root_logits, base_pos: int, branching=(4, 2, 1, 1), max_nodes: int = 16
+               ) -> SpeculativeForest:
+    """A draft tree from a drafter engine whose cache holds the committed prefix.
+
+    Depth d expands every node of depth d - 1 into its drafter top-`branching[d-1]` children (one
+    batched tree pass of the drafter per depth, `verify_tree` with logits, then `topk` on the
+    device). The kept nodes are the `max_nodes` of highest cumulative drafter log-probability
+    (ties: earlier node first), an ancestor-closed set because a child's cumulative log-probability
+    never exceeds its parent's. Returned as a forest of root-to-leaf paths in node order; the
+    drafter cache length is left unchanged (tree nodes sit at scratch slots)."""
+    import torch
+    tokens: List[int] = []
+    parents: List[int] = []
+    cum: List[float] = []
+    idx, val, lse = drafter.topk(root_logits.reshape(1, -1).float().contiguous(), branching[0])
+    frontier = []
+    for t, v in zip(idx[0].tolist(), (val[0] - lse[0]).tolist()):
+        tokens.append(int(t))
+        parents.append(-1)
+        cum.append(float(v))
+        frontier.append(len(tokens) - 1)
+    for width in branching[1:]:
+        if not frontier or len(tokens) >= 4 * max_nodes:
+            break
+        _, logits = drafter.verify_tree(dkv, tokens, parents, base_pos, want_logits=True)
+        rows = logits[torch.tensor(frontier, device=logits.device)].contiguous()
+        idx, val, lse = drafter.topk(rows, width)
+        lp = (val - lse[:, None]).tolist()
+        nxt = []
+        for r, f in enumerate(frontier):
+            for t, v in zip(idx[r].tolist(), lp[r]):
+                tokens.append(int(t))
+                parents.append(f)
+                cum.append(cum[f] + float(v))
+                nxt.append(len(tokens) - 1)
+        frontier = nxt
+    keep = sorted(sorted(range(len(tokens)), key=lambda i: (-cum[i], i))[:max_nodes])
+    pos = {old: new for new, old in enumerate(keep)}
+    k_tokens = [tokens[i] for i in keep]
+    k_parents = [pos[parents[i]] if parents[i] >= 0 else -1 for i in keep]
+    children = [0] * len(keep)
+    for p in k_parents:
+        if p >= 0:
+            children[p] += 1
+    paths = []
+    for i in range(len(keep)):
+        if children[i] == 0:                 # a leaf: its root-to-leaf path
+            path, j = [], i
+            while j >= 0:
+                path.append(k_tokens[j])
+                j = k_parents[j]
+            paths.append(path[::-1])
+    return SpeculativeForest.build(paths)
+
+
+@dataclass
+class SpecStats:
+    rounds: int = 0
+    drafted: int = 0
+    accepted: int = 0
+    verify_ms: List[float] = field(default_factory=list)
+
+
+def speculative_generate(target, drafter, prompt: Sequence[int], n_new: int, branching=(4, 2, 1, 1),
+                         max_nodes: int = 16, capacity: Optional[int] = None):
+    """Greedy speculative decoding: the drafter proposes a tree, the target verifies all of it in one
+    batched pass (`verify_tree`), the reference's selection rule picks the emitted tokens, the
+    accepted nodes' K/V are committed. Lossless: the tokens equal plain greedy decoding of the
+    target. Returns (tokens, SpecStats); `verify_ms` holds the device time of every verify pass."""
+    import torch
+    cap = capacity or len(prompt) + n_new + 8 * max_nodes
+    tkv, dkv = target.new_kv(cap), drafter.new_kv(cap)
+    _, am = target.forward(tkv, list(prompt), want_logits=False)
+    root_pred = int(am[-1])
+    d_logits, _ = drafter.forward(dkv, list(prompt))
+    d_root = d_logits[-1]
+    out: List[int] = []
+    stats = SpecStats()
+    stream = torch.cuda.current_stream(target.device)
+    while len(out) < n_new:
+        base = tkv.length
+        forest = draft_tree(drafter, dkv, d_root, base, branching, max_nodes)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        res = verify_tree(target, tkv, forest, root_pred, base)
+        e1.record(stream)
+        ver = res.verification
+        commit_tree(target, tkv, res)
+        stats.rounds += 1
+        stats.drafted += forest.node_count
+        stats.accepted += ver.accepted_draft_tokens
+        e1.synchronize()
+        stats.verify_ms.append(e0.elapsed_time(e1))
+        emitted = list(ver.emitted)
+        if ver.rejected:                     # the target's own token at the mismatch: feed it
+            _, am = target.forward(tkv, [emitted[-1]], want_logits=False)
+            root_pred = int(am[-1])
+        elif res.next_pred is not None:
+            root_pred = res.next_pred
+        else:                                # empty forest: the emitted token is the root prediction
+            _, am = target.forward(tkv, [emitted[-1]], want_logits=False)
+            root_pred = int(am[-1])
+        dkv.length = base
+        d_logits, _ = drafter.forward(dkv, emitted)
+        d_root = d_logits[-1]
+        out.extend(emitted)
+    tkv.close()
+    dkv.close()
+    return out[:n_new], stats
