@@ -407,6 +407,67 @@ def run_verify(args, world, rank, local):
             "clocks": clocks.summary(), "argmax": host}
 
 
+def run_speculative(args, world, rank, local):
+    """cfg2: greedy speculative decoding with a Qwen2-0.5B-shaped fp16 target and its first two
+    layers as the drafter (+ final norm and LM head), 16-node trees of branching 4, 2, 1, 1, a
+    128-token prompt, 64 output tokens. `value` = output tokens per second of the whole loop (wall
+    clock, host included); the line also carries the device time per verify pass, the accepted
+    draft tokens per round, and whether the tokens equal the target's own greedy decoding."""
+    from seedplane_b200.config import QWEN2_0_5B
+    from seedplane_b200.engine import CudaQwen2
+    from seedplane_b200.randinit import make_weights, random_prompt, truncate
+    from seedplane_b200.speculative import speculative_generate
+    from dataclasses import replace
+    cfg = QWEN2_0_5B
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = make_weights(cfg, seed=0, dtype=torch.float16)
+    target = CudaQwen2(cfg, w, device=dev)
+    drafter = CudaQwen2(replace(cfg, layers=2, name="qwen2-0.5b-draft2"), truncate(w, cfg, 2), device=dev)
+    del w
+    prompt = random_prompt(cfg.vocab, 128, seed=0)
+    n_out = 64
+    # the target's own greedy tokens (prefill + device decode loop)
+    kv = target.new_kv(512)
+    _, am = target.forward(kv, prompt, want_logits=False)
+    first = int(am[-1])
+    rest, _ = target.decode(kv, first, len(prompt), n_out - 1)
+    greedy = [first] + rest.tolist()
+    kv.close()
+    for _ in range(max(1, args.warmup)):
+        speculative_generate(target, drafter, prompt, n_out)
+    torch.cuda.synchronize(dev)
+    times, stats = [], None
+    with ClockSampler([local]) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            toks, stats = speculative_generate(target, drafter, prompt, n_out)
+            torch.cuda.synchronize(dev)
+            times.append(time.perf_counter() - t0)
+    target.status()
+    drafter.status()
+    target.close()
+    drafter.close()
+    if rank != 0:
+        return None
+    best = min(times)
+    return {"metric": "Qwen2-0.5B speculative greedy tok/s (16-node tree verify, 2-layer drafter)",
+            "value": n_out / best, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": max(1, args.warmup), "ms_per_step": 1000 * best, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "cfg2: qwen2-0.5b fp16 target (random-init seed 0), drafter = its first 2 "
+                                   "layers, 16-node draft trees (branching 4,2,1,1 kept by cumulative drafter "
+                                   "log-probability), 128-token prompt, 64 greedy output tokens",
+                       "rounds": stats.rounds, "accepted_per_round": stats.accepted / max(1, stats.rounds),
+                       "verify_us_mean": 1000.0 * statistics.mean(stats.verify_ms),
+                       "verify_us_median": 1000.0 * statistics.median(stats.verify_ms),
+                       "tokens_equal_target_greedy": toks == greedy,
+                       "l2": "inputs larger than L2: 0.99 GB of target weights per verify pass"},
+            "e2e": {"value": n_out / best, "unit": "tok/s", "h2d_bytes_per_step": 128 * 4,
+                    "d2h_bytes_per_step": n_out * 4},
+            "clocks": clocks.summary()}
+
+
 def run_burst(args, world, rank, local):
     from seedplane_b200.hive.burst import run_burst_bench
     return run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barrier, peaks)
@@ -418,7 +479,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "burst", "verify"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "burst", "verify", "speculative"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -428,7 +489,7 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        run = {"burst": run_burst, "verify": run_verify}.get(args.workload, run_decode)
+        run = {"burst": run_burst, "verify": run_verify, "speculative": run_speculative}.get(args.workload, run_decode)
         line = run(args, world, rank, local)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)

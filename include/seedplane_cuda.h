@@ -139,6 +139,19 @@ int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols,
 int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t k,
             int32_t *idx_dev, float *val_dev, float *lse_dev, void *stream);
 
+/* Stochastic acceptance of a draft tree at `temperature` with a counter-based RNG (seed, counter):
+ * recursive rejection sampling (children tried in node order, accept with min(1, p/q), residual
+ * max(p - q, 0) after a rejection, a draw from the residual when every child is rejected). The
+ * reference has no stochastic verifier (seedplane/speculative.py:46-92 is greedy only); the rule
+ * and its fp64 arithmetic are restated bit for bit in the repository's CPU oracle.
+ * target_logits / draft_logits: device fp32 [n + 1][ld], row 0 = after the committed prefix,
+ * row i + 1 = after node i. tokens / parents (host, parents[i] < i, -1 = root child). out_host
+ * [2n + 3]: emitted count, accepted count, emitted tokens [n + 1], accepted node indices [n].
+ * Synchronises `stream`. */
+int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const float *draft_logits_dev, int64_t ld,
+                         int32_t vocab, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
+                         double temperature, uint64_t seed, uint64_t counter, int32_t *out_host, void *stream);
+
 /* sp_argmax without an engine and without any allocation (no reference counterpart: the
  * reference allocates nothing on this path; this entry point exists for callers that must not
  * allocate device memory, e.g. inside a memory-capped serving process or before an engine

@@ -16,6 +16,11 @@ Added for the batched verifier (no counterpart in the reference, checked against
 
 * `flatten_forest` -- the trie as arrays (token, parent, depth) in first-visit order of the input
                       paths, plus each path as a node-index list.
+* `accept_stochastic` -- stochastic tree acceptance (recursive rejection sampling at a
+                      temperature, seeded counter RNG). The reference has NO stochastic verifier:
+                      this restates the repository's own written rule, fp64 operation by
+                      operation (own exp, fixed summation orders, splitmix64), so the GPU kernel's
+                      decisions can be checked bit for bit. Parity unpinned against the reference.
 * `accept_from_predictions` -- the same decision as `verify_greedy`, computed from the target's
                       argmax after the committed prefix (`root_pred`) and after each node
                       (`node_pred`). With consistent logits it returns the identical Verification.
@@ -147,3 +152,119 @@ class Ledger:
         self.tokens.extend(emitted)
         self.commits += 1
         return tuple(emitted)
+
+
+# ---- stochastic tree acceptance (restatement of the GPU rule, bit for bit) ---------------------
+_M64 = (1 << 64) - 1
+_LN2_HI, _LN2_LO, _INV_LN2 = 6.93147180369123816490e-01, 1.90821492927058770002e-10, 1.44269504088896338700e+00
+_INV_FACT = [1.0 / 479001600.0, 1.0 / 39916800.0, 1.0 / 3628800.0, 1.0 / 362880.0, 1.0 / 40320.0, 1.0 / 5040.0,
+             1.0 / 720.0, 1.0 / 120.0, 1.0 / 24.0, 1.0 / 6.0, 0.5, 1.0, 1.0]
+_THREADS = 256
+
+
+def dexp_ref(x):
+    """exp in fp64: Cody-Waite reduction by a two-part ln 2, Taylor series to r^13/13! in Horner
+    form (no fused multiply-add), scaling by 2^k; 0 below -745."""
+    import numpy as np
+    x = np.asarray(x, dtype=np.float64)
+    k = np.rint(x * _INV_LN2)
+    r = (x + (-(k * _LN2_HI))) + (-(k * _LN2_LO))
+    pw = np.full_like(x, 1.0 / 6227020800.0)
+    for c in _INV_FACT:
+        pw = pw * r + c
+    with np.errstate(over="ignore"):
+        out = np.ldexp(pw, np.where(x < -745.0, 0, k).astype(np.int64))
+    return np.where(x < -745.0, 0.0, out)
+
+
+def _block_sums(vals):
+    """Contiguous blocks of ceil(V / 256) entries, each summed in index order, then the block sums
+    in order: (block sums [256], total)."""
+    import numpy as np
+    V = vals.shape[0]
+    B = -(-V // _THREADS)
+    pad = np.zeros(_THREADS * B, dtype=np.float64)
+    pad[:V] = vals
+    blocks = pad.reshape(_THREADS, B)
+    acc = np.zeros(_THREADS, dtype=np.float64)
+    for i in range(B):
+        acc = acc + blocks[:, i]
+    tot = 0.0
+    for t in range(_THREADS):
+        tot = tot + float(acc[t])
+    return acc, tot
+
+
+def _splitmix(state):
+    state = (state + 0x9E3779B97F4A7C15) & _M64
+    z = state
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return state, z ^ (z >> 31)
+
+
+def accept_stochastic(tokens, parents, target_logits, draft_logits, temperature: float, seed: int, counter: int):
+    """The stochastic tree acceptance (see the GPU kernel's description): returns (emitted tokens,
+    accepted node indices). `target_logits` / `draft_logits`: fp32 [n + 1, V], row 0 after the
+    committed prefix, row i + 1 after node i."""
+    import numpy as np
+    tl = np.asarray(target_logits, dtype=np.float32).astype(np.float64)
+    dl = np.asarray(draft_logits, dtype=np.float32).astype(np.float64)
+    n, V = len(tokens), tl.shape[1]
+    inv_t = 1.0 / float(temperature)
+    state = (seed ^ ((counter * 0x9E3779B97F4A7C15) & _M64)) & _M64
+    cur, emitted, accepted = -1, [], []
+    for _ in range(n + 1):
+        zt, zd = tl[cur + 1] * inv_t, dl[cur + 1] * inv_t
+        mt, md = float(np.max(zt)), float(np.max(zd))
+        et, ed = dexp_ref(zt + (-mt)), dexp_ref(zd + (-md))
+        _, St = _block_sums(et)
+        _, Sd = _block_sums(ed)
+        P = et / St
+        qv = ed / Sd
+        nxt = -1
+        for c in range(n):
+            if parents[c] != cur:
+                continue
+            x = tokens[c]
+            state, z = _splitmix(state)
+            u = float(z >> 11) * 2.0 ** -53
+            if u < float(P[x]) / float(qv[x]):
+                nxt = c
+                break
+            res = np.fmax(P + (-qv), 0.0)
+            _, Z = _block_sums(res)
+            if Z > 0.0:
+                P = res / Z
+        if nxt >= 0:
+            emitted.append(int(tokens[nxt]))
+            accepted.append(nxt)
+            cur = nxt
+            if all(p != cur for p in parents):
+                break
+            continue
+        state, z = _splitmix(state)
+        u = float(z >> 11) * 2.0 ** -53
+        blocks, S = _block_sums(P)
+        target = u * S
+        B = -(-V // _THREADS)
+        run, pick, found = 0.0, V - 1, False
+        for t in range(_THREADS):
+            if found:
+                break
+            if run + float(blocks[t]) > target or t == _THREADS - 1:
+                for i in range(B):
+                    j = t * B + i
+                    if j >= V:
+                        break
+                    run = run + float(P[j])
+                    if run > target:
+                        pick, found = j, True
+                        break
+                if not found:
+                    pick, found = min(V - 1, t * B + B - 1), True
+            else:
+                run = run + float(blocks[t])
+        emitted.append(int(pick))
+        break
+    return emitted, accepted

@@ -147,6 +147,8 @@ struct sp_engine {
     size_t pf_bytes = 0;
     const __half *head_rm = nullptr;        // row-major LM head (the embedding when tied)
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
+    double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
+    int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
     void *blas_ws = nullptr;
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
@@ -954,6 +956,7 @@ void sp_engine_destroy(sp_engine *e) {
     for (auto &g : e->vgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->pf_mem);
     cudaFree(e->vt);
+    cudaFree(e->acc_scratch);
     prefill_blas_destroy(e->blas);
     cudaFree(e->blas_ws);
     delete e;
@@ -1252,6 +1255,39 @@ int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, i
     if (k < 1 || k > kTopkMax || k > cols) return fail(SP_ERR_INVALID, "k must be in 1..%d and <= cols", kTopkMax);
     SP_CUDA(cudaSetDevice(e->device));
     SP_CUDA(launch_topk_rows(logits_dev, rows, cols, ld, k, idx_dev, val_dev, lse_dev, (cudaStream_t)stream));
+    return SP_OK;
+}
+
+int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const float *draft_logits_dev, int64_t ld,
+                         int32_t vocab, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
+                         double temperature, uint64_t seed, uint64_t counter, int32_t *out_host, void *stream) {
+    if (!e || !target_logits_dev || !draft_logits_dev || !out_host || (n > 0 && (!tokens_host || !parents_host)))
+        return fail(SP_ERR_INVALID, "null argument");
+    if (n < 0 || n > kSmallNodes) return fail(SP_ERR_CAPACITY, "tree of %d nodes exceeds %d", n, kSmallNodes);
+    if (vocab <= 0 || ld < vocab) return fail(SP_ERR_INVALID, "bad logits shape");
+    if (!(temperature > 0.0)) return fail(SP_ERR_INVALID, "temperature must be positive");
+    for (int i = 0; i < n; ++i) {
+        if (parents_host[i] >= i || parents_host[i] < -1) return fail(SP_ERR_INVALID, "node %d: bad parent", i);
+        if (tokens_host[i] < 0 || tokens_host[i] >= vocab) return fail(SP_ERR_INVALID, "node %d: bad token", i);
+    }
+    SP_CUDA(cudaSetDevice(e->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (e->acc_vocab < vocab) {
+        cudaFree(e->acc_scratch);
+        e->acc_scratch = nullptr;
+        SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)vocab * 8 + (size_t)(4 * kSmallNodes + 8) * 4));
+        e->acc_vocab = vocab;
+    }
+    int32_t *dtok = reinterpret_cast<int32_t *>(e->acc_scratch + e->acc_vocab);
+    int32_t *dpar = dtok + kSmallNodes, *dout = dpar + kSmallNodes;
+    int32_t host[2 * kSmallNodes];
+    memcpy(host, tokens_host, n * 4);
+    memcpy(host + kSmallNodes, parents_host, n * 4);
+    SP_CUDA(cudaMemcpyAsync(dtok, host, sizeof(host), cudaMemcpyHostToDevice, s));
+    SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, temperature, seed,
+                                     counter, e->acc_scratch, dout, s));
+    SP_CUDA(cudaMemcpyAsync(out_host, dout, (size_t)(2 * n + 3) * 4, cudaMemcpyDeviceToHost, s));
+    SP_CUDA(cudaStreamSynchronize(s));
     return SP_OK;
 }
 

@@ -298,6 +298,13 @@ constexpr int kTopkMax = 8;
 cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long ld, int k, int *idx, float *val,
                              float *lse, cudaStream_t s);
 
+// Stochastic acceptance of a draft tree (sample.cu): target / drafter logits [n + 1][ld] (row 0:
+// after the committed prefix, row i + 1: after node i), nodes (token, parent), fp64 scratch [V].
+// out [2n + 3]: emitted count, accepted count, emitted tokens [n + 1], accepted nodes [n].
+cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
+                                     const int *parent, int n, double temperature, unsigned long long seed,
+                                     unsigned long long counter, double *scratch, int *out, cudaStream_t s);
+
 // Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
 // (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per
 // row, which must be zero when the kernel starts and is zero again when it ends.

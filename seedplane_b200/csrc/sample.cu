@@ -145,4 +145,194 @@ cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long 
     return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Stochastic tree acceptance (recursive rejection sampling over a draft tree, temperature T).
+//
+// Rule (written here; the reference has none, so its CPU restatement in
+// oracle/speculative_oracle.py is the oracle): start at the root (row 0 of the logits, the
+// distributions after the committed prefix). At a node with target distribution p and drafter
+// distribution q, try its children in node order: child x is accepted with probability
+// min(1, p(x) / q(x)) (uniform u < p(x) / q(x)); on rejection p becomes max(p - q, 0) normalised
+// (unchanged if that is all zero) and the next child is tried. An accepted child becomes the
+// current node (rows i + 1: the distributions after node i); when it has no children the pass
+// ends with the accepted drafts only. When every child is rejected, one token is drawn from p
+// and the pass ends. Every number is fp64 with a fixed operation order, so decisions are
+// reproducible bit for bit on the CPU:
+//   p_j = e_j / S, e_j = exp((l_j / T) - max), S = sum of e over contiguous blocks of
+//   ceil(V / 256) entries (block b summed in index order, then the 256 block sums in order);
+//   exp: Cody-Waite reduction by ln 2 (two-part constant) and a degree-13 Taylor polynomial in
+//   Horner form, no fused multiply-add, then scaling by 2^k;
+//   u: splitmix64 (Vigna) of seed ^ (counter * 0x9E3779B97F4A7C15) advanced once per draw, the
+//   top 53 bits times 2^-53; a draw from p walks the same blocks: the first index whose running
+//   sum exceeds u * S.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kAccThreads = 256;
+
+SP_DEVINL double dexp_ref(double x) {
+    // Cody-Waite: x = k ln2 + r, |r| <= ln2 / 2 (ln 2 split in two parts, the published values of
+    // fdlibm's e_exp.c); exp(r) by its Taylor series to r^13 / 13!
+    const double ln2_hi = 6.93147180369123816490e-01, ln2_lo = 1.90821492927058770002e-10;
+    const double inv_ln2 = 1.44269504088896338700e+00;
+    if (x < -745.0) return 0.0;
+    const double k = rint(__dmul_rn(x, inv_ln2));
+    const double r = __dadd_rn(__dadd_rn(x, -__dmul_rn(k, ln2_hi)), -__dmul_rn(k, ln2_lo));
+    double pw = 1.0 / 6227020800.0;                 // 1/13!
+    const double inv_fact[13] = {1.0 / 479001600.0, 1.0 / 39916800.0, 1.0 / 3628800.0, 1.0 / 362880.0,
+                                 1.0 / 40320.0,     1.0 / 5040.0,     1.0 / 720.0,      1.0 / 120.0,
+                                 1.0 / 24.0,        1.0 / 6.0,        0.5,              1.0,
+                                 1.0};
+#pragma unroll
+    for (int i = 0; i < 13; ++i) pw = __dadd_rn(__dmul_rn(pw, r), inv_fact[i]);
+    return scalbn(pw, (int)k);
+}
+
+SP_DEVINL unsigned long long splitmix_next(unsigned long long &s) {
+    s += 0x9E3779B97F4A7C15ull;
+    unsigned long long z = s;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+SP_DEVINL double uniform53(unsigned long long &s) { return (double)(splitmix_next(s) >> 11) * 0x1.0p-53; }
+
+// sum over contiguous blocks (block b = thread b), then the block sums in order (thread 0)
+template <typename F>
+SP_DEVINL double block_sum(F f, int V, double *s_part) {
+    const int B = (V + kAccThreads - 1) / kAccThreads;
+    double acc = 0.0;
+    for (int i = 0; i < B; ++i) {
+        const int j = threadIdx.x * B + i;
+        if (j < V) acc = __dadd_rn(acc, f(j));
+    }
+    s_part[threadIdx.x] = acc;
+    __syncthreads();
+    double tot = 0.0;
+    for (int t = 0; t < kAccThreads; ++t) tot = __dadd_rn(tot, s_part[t]);
+    __syncthreads();
+    return tot;
+}
+
+SP_DEVINL double block_max(const float *row, int V, double inv_t, double *s_part) {
+    double m = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += kAccThreads) m = fmax(m, __dmul_rn((double)row[j], inv_t));
+    s_part[threadIdx.x] = m;
+    __syncthreads();
+    double mx = -INFINITY;
+    for (int t = 0; t < kAccThreads; ++t) mx = fmax(mx, s_part[t]);
+    __syncthreads();
+    return mx;
+}
+
+__global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *tlog, const float *dlog, long long ld,
+                                                                   int V, const int *tok, const int *parent, int n,
+                                                                   double inv_t, unsigned long long seed,
+                                                                   unsigned long long counter, double *P, int *out) {
+    __shared__ double s_part[kAccThreads];
+    __shared__ int s_tok;
+    unsigned long long rng = seed ^ (counter * 0x9E3779B97F4A7C15ull);
+    int cur = -1;                                         // -1: the root
+    int n_out = 0, n_acc = 0;
+    for (int depth = 0; depth <= n; ++depth) {
+        const float *tr = tlog + (size_t)(cur + 1) * ld, *dr = dlog + (size_t)(cur + 1) * ld;
+        const double mt = block_max(tr, V, inv_t, s_part), md = block_max(dr, V, inv_t, s_part);
+        const double St = block_sum([&](int j) { return dexp_ref(__dadd_rn(__dmul_rn((double)tr[j], inv_t), -mt)); }, V, s_part);
+        const double Sd = block_sum([&](int j) { return dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)); }, V, s_part);
+        for (int j = threadIdx.x; j < V; j += kAccThreads)
+            P[j] = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)tr[j], inv_t), -mt)), St);
+        __syncthreads();
+        int next = -1;
+        bool any_child = false;
+        for (int c = 0; c < n && next < 0; ++c) {
+            if (parent[c] != cur) continue;
+            any_child = true;
+            const int x = tok[c];
+            const double q = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[x], inv_t), -md)), Sd);
+            const double u = uniform53(rng);                  // the same in every thread
+            const double px = P[x];
+            if (u < __ddiv_rn(px, q)) {
+                next = c;
+            } else {                                          // residual max(p - q, 0), normalised
+                const double Z = block_sum([&](int j) {
+                    const double qj = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)), Sd);
+                    return fmax(__dadd_rn(P[j], -qj), 0.0);
+                }, V, s_part);
+                if (Z > 0.0) {
+                    for (int j = threadIdx.x; j < V; j += kAccThreads) {
+                        const double qj = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)), Sd);
+                        P[j] = __ddiv_rn(fmax(__dadd_rn(P[j], -qj), 0.0), Z);
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (next >= 0) {                                      // accepted: descend
+            if (threadIdx.x == 0) {
+                out[2 + n_out] = tok[next];
+                out[2 + n + 1 + n_acc] = next;
+            }
+            ++n_out;
+            ++n_acc;
+            cur = next;
+            bool leaf = true;
+            for (int c = 0; c < n; ++c) leaf &= parent[c] != cur;
+            if (leaf) break;
+            continue;
+        }
+        // every child rejected (or none): draw from p
+        const double u = uniform53(rng);
+        const double S = block_sum([&](int j) { return P[j]; }, V, s_part);
+        if (threadIdx.x == 0) {
+            const double target = __dmul_rn(u, S);
+            const int B = (V + kAccThreads - 1) / kAccThreads;
+            double run = 0.0;
+            int pick = V - 1;
+            bool found = false;
+            for (int t = 0; t < kAccThreads && !found; ++t) {
+                if (__dadd_rn(run, s_part[t]) > target || t == kAccThreads - 1) {
+                    for (int i = 0; i < B; ++i) {             // inside block t, in index order
+                        const int j = t * B + i;
+                        if (j >= V) break;
+                        run = __dadd_rn(run, P[j]);
+                        if (run > target) {
+                            pick = j;
+                            found = true;
+                            break;
+                        }
+                    }
+                    if (!found) {                             // rounding: the block's last index
+                        pick = min(V - 1, t * B + B - 1);
+                        found = true;
+                    }
+                } else {
+                    run = __dadd_rn(run, s_part[t]);
+                }
+            }
+            s_tok = pick;
+            out[2 + n_out] = pick;
+        }
+        __syncthreads();
+        ++n_out;
+        (void)any_child;
+        break;
+    }
+    if (threadIdx.x == 0) {
+        out[0] = n_out;
+        out[1] = n_acc;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
+                                     const int *parent, int n, double temperature, unsigned long long seed,
+                                     unsigned long long counter, double *scratch, int *out, cudaStream_t s) {
+    if (V <= 0 || n < 0 || !(temperature > 0.0)) return cudaErrorInvalidValue;
+    k_accept_stochastic<<<1, kAccThreads, 0, s>>>(tlog, dlog, ld, V, tok, parent, n, 1.0 / temperature, seed, counter,
+                                                  scratch, out);
+    return cudaGetLastError();
+}
+
 }  // namespace sp

@@ -194,6 +194,30 @@ def verify_tree(engine, kv, forest: SpeculativeForest, root_pred: int, base_pos:
     return TreeResult(ver, nodes, node_pred, next_pred, flat)
 
 
+def accept_stochastic(engine, flat: FlatForest, target_logits, draft_logits, temperature: float, seed: int,
+                      counter: int) -> Tuple[Verification, Tuple[int, ...]]:
+    """Stochastic acceptance of a verified tree on the device (`sp_accept_stochastic`): children
+    tried in node order with min(1, p/q), the residual max(p - q, 0) after each rejection, a draw
+    from the residual when all are rejected; counter-based RNG, so (seed, counter) reproduce a
+    decision. Logits fp32 [n + 1, V] on the engine's device: row 0 after the committed prefix, row
+    i + 1 after node i. Returns the Verification and the accepted node indices."""
+    import ctypes as C
+    from . import _native as N
+    from .engine import _stream
+    n = len(flat.tokens)
+    out = (C.c_int32 * (2 * n + 3))()
+    N.check(N.load().sp_accept_stochastic(engine.handle, C.c_void_p(target_logits.data_ptr()),
+                                          C.c_void_p(draft_logits.data_ptr()), target_logits.stride(0),
+                                          target_logits.shape[1], N.int_array(flat.tokens), N.int_array(flat.parents),
+                                          n, float(temperature), int(seed), int(counter), out,
+                                          C.c_void_p(_stream(engine.device))))
+    n_out, n_acc = out[0], out[1]
+    emitted = tuple(out[2 + i] for i in range(n_out))
+    nodes = tuple(out[2 + n + 1 + i] for i in range(n_acc))
+    path = tuple(flat.tokens[i] for i in nodes)
+    return Verification(emitted, n_acc, n_out > n_acc, n_out, path), nodes
+
+
 def commit_tree(engine, kv, result: TreeResult) -> int:
     """Keep the K/V of the accepted draft nodes (they were written at scratch slots len + i) and
     advance the cache length by their number. Returns the new length."""

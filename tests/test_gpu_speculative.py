@@ -69,3 +69,34 @@ def test_speculative_greedy_is_lossless(pair):
     assert stats.rounds >= 1 and len(stats.verify_ms) == stats.rounds
     target.status()
     drafter.status()
+
+
+@pytest.mark.parametrize("V", [5000, 151936])
+def test_stochastic_accept_matches_oracle(pair, V):
+    """The device's stochastic acceptance takes the oracle's decisions bit for bit (same fp64
+    arithmetic, summation order and RNG), on random trees and logits."""
+    import numpy as np
+    from oracle.speculative_oracle import accept_stochastic as ref
+    from seedplane_b200.speculative import SpeculativeForest, accept_stochastic
+    cfg, w, target, drafter = pair
+    rng = np.random.default_rng(V)
+    cases = 0
+    for trial in range(4):
+        paths = [[int(rng.integers(0, V)) for _ in range(int(rng.integers(1, 5)))] for _ in range(5)]
+        flat = SpeculativeForest.build(paths).flatten()
+        n = len(flat.tokens)
+        t = (rng.normal(size=(n + 1, V)) * 3).astype(np.float32)
+        d = (rng.normal(size=(n + 1, V)) * 3).astype(np.float32)
+        # make the drafts likely under both, so acceptances happen
+        for i, tok in enumerate(flat.tokens):
+            row = flat.parents[i] + 1
+            t[row, tok] += 6.0
+            d[row, tok] += 6.5
+        td, dd = torch.from_numpy(t).cuda(), torch.from_numpy(d).cuda()
+        for seed, counter in ((1, 0), (1, 1), (99, 7), (2 ** 40 + 3, 123)):
+            ver, nodes = accept_stochastic(target, flat, td, dd, 1.0 if trial % 2 == 0 else 0.7, seed, counter)
+            want_tokens, want_nodes = ref(list(flat.tokens), list(flat.parents), t, d,
+                                          1.0 if trial % 2 == 0 else 0.7, seed, counter)
+            assert list(ver.emitted) == want_tokens and list(nodes) == want_nodes
+            cases += 1
+    assert cases == 16
