@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #define SP_DEVINL __device__ __forceinline__
+#define SP_HOSTDEV __host__ __device__ __forceinline__
 
 namespace sp {
 

@@ -347,7 +347,7 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.epoch = e->epoch;
         p.st = e->st;
         p.trace = e->step_trace;
-        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_lay.smem, s, e->pdl));
+        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_lay.smem, s, e->pdl, e->c.weight_format == SP_WEIGHTS_I8_B32));
         return SP_OK;
     }
     int kidx = 0;       // GEMV index within the step (trace slot)
@@ -507,9 +507,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     if (c.heads / c.kv_heads > 8) return fail(SP_ERR_UNSUPPORTED, "more than 8 q heads per kv head");
     if (c.hidden % 16 || c.intermediate % 16)
         return fail(SP_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 16");
-    if (c.weight_format == SP_WEIGHTS_I8_B32)
-        return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights are not built in this version");
-    if (c.weight_format != SP_WEIGHTS_F16) return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
+    if (c.weight_format != SP_WEIGHTS_F16 && c.weight_format != SP_WEIGHTS_I8_B32)
+        return fail(SP_ERR_INVALID, "unknown weight format %d", c.weight_format);
+    const bool i8 = c.weight_format == SP_WEIGHTS_I8_B32;
     if (c.max_positions <= 0) return fail(SP_ERR_INVALID, "max_positions must be positive");
     if (!w->embed || !w->final_norm || !w->layers) return fail(SP_ERR_INVALID, "missing tensors");
     if (!c.tied_embeddings && !w->lm_head) return fail(SP_ERR_INVALID, "untied model without lm_head");
@@ -517,7 +517,12 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         const sp_layer_weights &Lw = w->layers[l];
         if (!Lw.qkv_w || !Lw.qkv_b || !Lw.o_w || !Lw.gate_w || !Lw.up_w || !Lw.down_w || !Lw.in_norm || !Lw.post_norm)
             return fail(SP_ERR_INVALID, "layer %d: missing tensor", l);
+        if (i8 && (!Lw.qkv_s || !Lw.o_s || !Lw.gate_s || !Lw.up_s || !Lw.down_s))
+            return fail(SP_ERR_INVALID, "layer %d: missing int8 block scales", l);
     }
+    if (i8 && !c.tied_embeddings && !w->lm_head_s) return fail(SP_ERR_INVALID, "int8 lm_head without scales");
+    if (i8 && (c.hidden % 128 || c.intermediate % 128))
+        return fail(SP_ERR_UNSUPPORTED, "int8 weights need hidden and intermediate in multiples of 128");
 
     SP_CUDA(cudaSetDevice(device));
     sp_engine *e = new sp_engine();
@@ -532,6 +537,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->tc = !(g && strcmp(g, "hmma") == 0);
         const char *st = getenv("SEEDPLANE_STEP");
         e->step_kernel = e->tc && !(st && strcmp(st, "chain") == 0);
+    }
+    if (i8 && !e->step_kernel) {
+        delete e;
+        return fail(SP_ERR_UNSUPPORTED, "int8 blockwise weights run on the step kernel only");
     }
     cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
 
@@ -562,9 +571,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             return fail(SP_ERR_UNSUPPORTED, "step kernel: the input vector of %d floats leaves no room for the ring",
                         e->step_xmax);
         }
-        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro) {
+        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, bool q8) {
             StepOp o{};
             o.kind = OP_GEMV;
+            o.fmt = q8 ? WF_I8 : WF_F16;
             o.pro = pro;
             o.N = (int)N;
             o.K = (int)K;
@@ -572,11 +582,11 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes);
             return o;
         };
-        e->s_qkv = sbase(QRp, H, QR, PRO_NORM);
-        e->s_o = sbase(Hp, H, H, PRO_ATTN);
-        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM);
-        e->s_down = sbase(Hp, I, H, PRO_PLAIN);
-        e->s_head = sbase(VP, H, V, PRO_NORM);
+        e->s_qkv = sbase(QRp, H, QR, PRO_NORM, i8);
+        e->s_o = sbase(Hp, H, H, PRO_ATTN, i8);
+        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM, i8);
+        e->s_down = sbase(Hp, I, H, PRO_PLAIN, i8);
+        e->s_head = sbase(VP, H, V, PRO_NORM, i8 && !c.tied_embeddings);   // a tied head is the fp16 embedding
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
             if (!step_gemv_supported(*o, e->step_lay.stage_bytes)) {
                 delete e;
@@ -588,13 +598,15 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
     struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post, rqkv, ro, rgu, rdn; };
     std::vector<LOff> lo(c.layers);
-    for (int l = 0; l < c.layers; ++l) {     // matrix sizes are multiples of 512 B: no gaps
-        lo[l].qkv = take(QRp * H * 2);
-        lo[l].o = take(Hp * H * 2);
-        lo[l].gu = take(GUp * H * 2);
-        lo[l].dn = take(Hp * I * 2);
+    // packed matrix bytes: fp16 sizes are multiples of 512 B (no gaps); int8 ones of 32 B
+    auto mbytes = [&](const StepOp &o, size_t N, size_t K) { return e->step_kernel ? step_gemv_bytes(o) : N * K * 2; };
+    for (int l = 0; l < c.layers; ++l) {
+        lo[l].qkv = take(mbytes(e->s_qkv, QRp, H));
+        lo[l].o = take(mbytes(e->s_o, Hp, H));
+        lo[l].gu = take(mbytes(e->s_gu, GUp, H));
+        lo[l].dn = take(mbytes(e->s_down, Hp, I));
     }
-    const size_t o_head = take(VP * H * 2);
+    const size_t o_head = take(mbytes(e->s_head, VP, H));
     const size_t stream_end = off;
     const size_t o_embed = take(V * H * 2);
     const size_t o_fnorm = take(H * 4);
@@ -605,7 +617,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         lo[l].post = take(H * 4);
     }
     // row-major copies for the batched prompt pass
-    e->prefill = !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
+    // (int8 prompts and tree verifies run through the step kernel)
+    e->prefill = !i8 && !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
     size_t o_head_rm = 0;
     if (e->prefill) {
         for (int l = 0; l < c.layers; ++l) {
@@ -657,23 +670,30 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const int *d_perm = d_idx, *d_gu = d_idx + QRp, *d_iota = d_idx + QRp + GUp;
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
-    auto pack = [&](uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of, int N, int K,
-                    const StepOp &plan) {
-        return e->step_kernel ? launch_pack_rows(dst, a, rows_a, b, row_of, plan, s)
-               : e->tc        ? launch_pack_tc(dst, a, rows_a, b, row_of, N, K, s)
-                              : launch_pack_fragments(dst, a, rows_a, b, row_of, N, K, s);
+    auto pack = [&](uint8_t *dst, const void *a, const void *as, int rows_a, const void *b, const void *bs,
+                    const int *row_of, int N, int K, const StepOp &plan) {
+        if (e->step_kernel && plan.fmt == WF_I8) {
+            cudaError_t me = cudaMemsetAsync(dst, 0, step_gemv_bytes(plan), s);
+            if (me != cudaSuccess) return me;
+            return launch_pack_rows_i8(dst, (const int8_t *)a, (const __half *)as, rows_a, (const int8_t *)b,
+                                       (const __half *)bs, row_of, plan, s);
+        }
+        const __half *ah = (const __half *)a, *bh = (const __half *)b;
+        return e->step_kernel ? launch_pack_rows(dst, ah, rows_a, bh, row_of, plan, s)
+               : e->tc        ? launch_pack_tc(dst, ah, rows_a, bh, row_of, N, K, s)
+                              : launch_pack_fragments(dst, ah, rows_a, bh, row_of, N, K, s);
     };
-    SP_TRY(pack(A + o_head, head_src, (int)V, nullptr, d_head_rows, (int)VP, (int)H, e->s_head));
+    SP_TRY(pack(A + o_head, head_src, c.tied_embeddings ? nullptr : w->lm_head_s, (int)V, nullptr, nullptr,
+                d_head_rows, (int)VP, (int)H, e->s_head));
     if (e->prefill && !c.tied_embeddings)
         SP_TRY(cudaMemcpyAsync(A + o_head_rm, w->lm_head, V * H * 2, cudaMemcpyDeviceToDevice, s));
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
-        SP_TRY(pack(A + lo[l].qkv, (const __half *)Lw.qkv_w, (int)QR, nullptr, d_perm, (int)QRp, (int)H, e->s_qkv));
-        SP_TRY(pack(A + lo[l].o, (const __half *)Lw.o_w, (int)H, nullptr, d_iota, (int)Hp, (int)H, e->s_o));
-        SP_TRY(pack(A + lo[l].gu, (const __half *)Lw.gate_w, (int)I, (const __half *)Lw.up_w, d_gu, (int)GUp, (int)H,
-                    e->s_gu));
-        SP_TRY(pack(A + lo[l].dn, (const __half *)Lw.down_w, (int)H, nullptr, d_iota, (int)Hp, (int)I, e->s_down));
+        SP_TRY(pack(A + lo[l].qkv, Lw.qkv_w, Lw.qkv_s, (int)QR, nullptr, nullptr, d_perm, (int)QRp, (int)H, e->s_qkv));
+        SP_TRY(pack(A + lo[l].o, Lw.o_w, Lw.o_s, (int)H, nullptr, nullptr, d_iota, (int)Hp, (int)H, e->s_o));
+        SP_TRY(pack(A + lo[l].gu, Lw.gate_w, Lw.gate_s, (int)I, Lw.up_w, Lw.up_s, d_gu, (int)GUp, (int)H, e->s_gu));
+        SP_TRY(pack(A + lo[l].dn, Lw.down_w, Lw.down_s, (int)H, nullptr, nullptr, d_iota, (int)Hp, (int)I, e->s_down));
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
@@ -788,8 +808,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            fprintf(stderr, "[seedplane] step gemv %-8s N=%d K=%d grid=%d pass_rows=%d chunk=%d\n", names[k++], o->N,
-                    o->K, o->grid, o->pass_rows, o->chunk_w);
+            fprintf(stderr, "[seedplane] step gemv %-8s %s N=%d K=%d grid=%d pass_rows=%d chunk=%d\n", names[k++],
+                    o->fmt == WF_I8 ? "i8" : "f16", o->N, o->K, o->grid, o->pass_rows, o->chunk_w);
     }
     if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc && !e->step_kernel) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
@@ -918,7 +938,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         if (e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms)
             return bail(fail(SP_ERR_UNSUPPORTED, "step kernel: %d q heads do not fit one attention item per CTA",
                              c.heads));
-        SP_TRY(prepare_step((int)HD, e->step_lay.smem));
+        SP_TRY(prepare_step((int)HD, e->step_lay.smem, i8));
         if (env_flag("SEEDPLANE_VERBOSE", false))
             fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d x %d B xmax=%d smem=%zu max_chunks=%d\n",
                     e->num_sms, e->step_lay.stages, e->step_lay.stage_bytes, e->step_xmax, e->step_lay.smem,

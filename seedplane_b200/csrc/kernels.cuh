@@ -194,11 +194,12 @@ struct StepOp {
     int N, K, n_valid;       // N even: rows come in pairs
     int grid;                // CTAs owning rows: CTA c owns pairs [P c / grid, P (c + 1) / grid)
     int pass_rows;           // rows per pass (even, <= kStepPassRows)
-    int chunk_w;             // inputs per unit (multiple of 256, or all of K)
+    int chunk_w;             // inputs per unit (f16: multiple of 256, i8: of 128; or all of K)
     int lin_k, lres_k;       // ops whose tags lin / lres carry
     int dep, dep_n;          // wait until cnt[dep] >= dep_n * (epoch + 1); dep < 0: none
     int sig;                 // cnt[sig] += 1 per CTA; < 0: none
-    int pad_[2];
+    int fmt;                 // WeightFmt of w
+    int cta_bytes;           // WF_I8: bytes of one CTA's rows (CTA c's units start at c * cta_bytes)
 };
 static_assert(sizeof(StepOp) % 16 == 0, "ops are copied to shared memory in 16-byte words");
 
@@ -233,17 +234,22 @@ struct StepLayout {
 
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes);   // fills grid, pass_rows, chunk_w from N, K
 bool step_gemv_supported(const StepOp &o, int stage_bytes);
+size_t step_gemv_bytes(const StepOp &o);                           // packed bytes of a planned GEMV
 // Pack an fp16 N x K matrix (packed row r = source row row_of[r] of a / b as in
 // launch_pack_fragments, < 0 = zero) into the plan's row-block layout.
 cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __half *b, const int *row_of,
                              const StepOp &plan, cudaStream_t s);
+// Blockwise int8 (`a`, `b` int8 [rows][K] with fp16 scales `as`, `bs` [rows][K / 32]); `dst` must
+// be zeroed first (padding scales of partial row tiles are not written).
+cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
+                                const __half *bs, const int *row_of, const StepOp &plan, cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
 // xmax: the largest GEMV input (multiple of 8); hidden: the QKV projection's input.
 StepLayout step_layout(int hidden, int xmax, int hd, int stages);
-cudaError_t prepare_step(int hd, size_t smem);
+cudaError_t prepare_step(int hd, size_t smem, bool q8);   // q8: the build with the int8 unit path
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
 // resident at once (one CTA per SM), so the launch is cooperative.
-cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl);
+cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8);
 
 // ---- batched prompt pass: prefill.cu ------------------------------------------------------------
 // T prompt tokens per chunk through all layers at once: cuBLAS GEMMs (fp16 x fp16 -> fp32) on

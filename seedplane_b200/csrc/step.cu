@@ -121,6 +121,78 @@ SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int ro
     }
 }
 
+// Two offset-binary bytes (u = q + 128, bytes sel of a word) -> fp16 pair q exactly: u placed in
+// the low mantissa bits under exponent bits 0x64 reads as 1024 + u; minus 1152 (0x6480) leaves q.
+// (The magic-number int8 -> fp16 conversion of Kim et al., "Who Says Elephants Can't Run", 2022.)
+SP_DEVINL uint32_t u8x2_to_h2(uint32_t w, uint32_t sel) {
+    const uint32_t h = __byte_perm(w, 0x64646464u, sel);
+    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&h), __halves2half2(__ushort_as_half(0x6480),
+                                                                                   __ushort_as_half(0x6480)));
+    return *reinterpret_cast<const uint32_t *>(&q);
+}
+
+// One blockwise-int8 unit of a pass (see k_pack_rows_i8): rows of offset-binary bytes in 16-byte
+// chunks XOR-swizzled like the fp16 units, then the scales [block][row tile][8] as fp16 pairs
+// (row g, row g + 8). One ldmatrix.x4 gives a 16-row x 32-input block (a lane: 4 consecutive
+// inputs of rows g and g + 8 in each half); the two MMAs take the inputs in the order the bytes
+// arrive (the k-index map 2t, 2t+1, 2t+8, 2t+9 -> 4t .. 4t+3 is applied to the B operand too),
+// summed into a fresh block accumulator that is scaled per row into the running sums in fp32.
+// Warp w takes blocks w, w + 4, ...; slots as in unit_mma.
+template <int U>
+SP_DEVINL void unit_mma_i8(float (&d)[4][4], uint32_t unit, int rs, int nb, int rows_p, int nrt, int q0,
+                           const __half *xh, const __half *xl, int warp, int lane) {
+    const int lm = lane >> 3, lr = lane & 7;
+    const uint32_t scl = unit + (uint32_t)(rows_p * rs);
+    for (int kb = warp; kb < nb; kb += 4 * U) {
+        uint32_t b[U][4];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            b[u][0] = b[u][1] = b[u][2] = b[u][3] = 0u;
+            const int kk = kb + 4 * u;
+            if (kk < nb && lane < 8) {                      // B column 0 = hi, column 1 = lo
+                const __half *xv = (lane < 4 ? xh : xl) + q0 + 32 * kk + 4 * (lane & 3);
+                const uint2 v0 = *reinterpret_cast<const uint2 *>(xv);
+                const uint2 v1 = *reinterpret_cast<const uint2 *>(xv + 16);
+                b[u][0] = v0.x;
+                b[u][1] = v0.y;
+                b[u][2] = v1.x;
+                b[u][3] = v1.y;
+            }
+        }
+        uint32_t a[4][4], sc[4];
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl) {
+            const int rt = sl / U, kk = kb + 4 * (sl % U);
+            if (rt < nrt && kk < nb) {
+                const int r = min(rt * 16 + ((lm & 1) << 3) + lr, rows_p - 1);
+                const int j = 2 * kk + (lm >> 1);
+                const int pj = (j & ~7) | ((j & 7) ^ (r & 7));
+                ldmatrix_x4(unit + (uint32_t)(r * rs + pj * 16), a[sl][0], a[sl][1], a[sl][2], a[sl][3]);
+                asm volatile("ld.shared.b32 %0, [%1];"
+                             : "=r"(sc[sl])
+                             : "r"(scl + (uint32_t)(((kk * nrt + rt) * 8 + (lane >> 2)) * 4)));
+            }
+        }
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl) {
+            const int rt = sl / U, kk = kb + 4 * (sl % U);
+            if (rt < nrt && kk < nb) {
+                float e[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t *bb = b[sl % U];
+                mma_16816(e, u8x2_to_h2(a[sl][0], 0x4140), u8x2_to_h2(a[sl][1], 0x4140), u8x2_to_h2(a[sl][0], 0x4342),
+                          u8x2_to_h2(a[sl][1], 0x4342), bb[0], bb[1]);
+                mma_16816(e, u8x2_to_h2(a[sl][2], 0x4140), u8x2_to_h2(a[sl][3], 0x4140), u8x2_to_h2(a[sl][2], 0x4342),
+                          u8x2_to_h2(a[sl][3], 0x4342), bb[2], bb[3]);
+                const float2 s = __half22float2(*reinterpret_cast<const __half2 *>(&sc[sl]));
+                d[sl][0] = fmaf(s.x, e[0], d[sl][0]);
+                d[sl][1] = fmaf(s.x, e[1], d[sl][1]);
+                d[sl][2] = fmaf(s.y, e[2], d[sl][2]);
+                d[sl][3] = fmaf(s.y, e[3], d[sl][3]);
+            }
+        }
+    }
+}
+
 // Row sums of a pass from the accumulator slots (lanes 4i: rows i and i + 8 of each tile; columns
 // 0 = hi, 1 = lo), tile rt's U slots added in slot order.
 template <int U>
@@ -692,6 +764,12 @@ __device__ __noinline__ void lmhead_finish(const StepParams &p, const StepOp &op
     }
 }
 
+// Bytes of one unit of `rows` rows x `w` inputs: fp16 rows, or int8 rows plus the scales of
+// ceil(rows / 16) row tiles (8 fp16 pairs per tile and 32-input block).
+SP_HOSTDEV uint32_t step_unit_bytes(int fmt, int rows, int w) {
+    return fmt == WF_I8 ? (uint32_t)(rows * w + (w / 32) * ((rows + 15) / 16) * 32) : (uint32_t)(rows * w * 2);
+}
+
 // The CTA's weight units of the step in consumption order (op, pass, chunk). A unit's bytes are
 // contiguous and follow the previous unit of the same op (see k_pack_rows). Op fields are read
 // from the table in global memory when the cursor enters an op, lazily (at the next call), so a
@@ -700,7 +778,7 @@ struct UnitCursor {
     const StepOp *ops;
     int n_ops, c;
     int k = -1;                     // current op; n_ops: exhausted
-    int K = 0, cw = 0, prw = 0, R = 0, p0 = 0, q0 = 0;
+    int K = 0, cw = 0, prw = 0, R = 0, p0 = 0, q0 = 0, fmt = WF_F16;
     bool pending = false;           // the current op is used up: seek the next one first
     const uint8_t *src = nullptr;
 
@@ -717,8 +795,9 @@ struct UnitCursor {
             K = __ldg(&o->K);
             cw = __ldg(&o->chunk_w);
             prw = __ldg(&o->pass_rows);
+            fmt = __ldg(&o->fmt);
             src = reinterpret_cast<const uint8_t *>(__ldg(reinterpret_cast<const unsigned long long *>(&o->w))) +
-                  (size_t)R0 * K * 2;
+                  (fmt == WF_I8 ? (size_t)c * __ldg(&o->cta_bytes) : (size_t)R0 * K * 2);
             p0 = 0;
             q0 = 0;
             return;
@@ -730,7 +809,7 @@ struct UnitCursor {
             seek(k + 1);
         }
         if (k >= n_ops) return false;
-        bytes = (uint32_t)(min(prw, R - p0) * min(cw, K - q0) * 2);
+        bytes = step_unit_bytes(fmt, min(prw, R - p0), min(cw, K - q0));
         unit = src;
         src += bytes;
         q0 += cw;
@@ -745,7 +824,9 @@ struct UnitCursor {
 
 }  // namespace
 
-template <int HD>
+// Q8: the build with the blockwise-int8 unit path (a separate instantiation, so the fp16-only
+// kernel keeps its register allocation).
+template <int HD, bool Q8>
 __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ float s_val[4];
@@ -1061,12 +1142,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         stamp_clk(p.trace, k, C, c, 2);
                     }
                     const uint32_t unit = smem_u32(ring + (size_t)s * SB);
-                    const int rs = wq * 2;                          // row stride (bytes) inside the unit
-                    const int nks = wq >> 4;
-                    if (nrt == 1)
-                        unit_mma<4>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
-                    else
-                        unit_mma<1>(d, unit, rs, nks, rows_p, nrt, q0, xh, xl, warp, lane);
+                    if (Q8 && op.fmt == WF_I8) {                    // row stride wq bytes, 32-input blocks
+                        if (nrt == 1)
+                            unit_mma_i8<2>(d, unit, wq, wq >> 5, rows_p, nrt, q0, xh, xl, warp, lane);
+                        else
+                            unit_mma_i8<1>(d, unit, wq, wq >> 5, rows_p, nrt, q0, xh, xl, warp, lane);
+                    } else {                                        // row stride 2 wq bytes, 16-input k-steps
+                        if (nrt == 1)
+                            unit_mma<4>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
+                        else
+                            unit_mma<1>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
+                    }
                     epi_sync();                                     // every warp is done with the unit
                     if (tid == 0) mbar_arrive(&empty[s]);
                     ++consumed;
@@ -1079,7 +1165,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 // row sums: lanes 4i hold rows i and i + 8 of each tile (columns 0 = hi, 1 = lo);
                 // tile rt's U accumulator slots are summed in slot order
                 if ((lane & 3) == 0) {
-                    if (nrt == 1)
+                    if (Q8 && nrt == 1 && op.fmt == WF_I8)
+                        rows_from_acc<2>(d, red[warp], nrt, lane);
+                    else if (nrt == 1)
                         rows_from_acc<4>(d, red[warp], nrt, lane);
                     else
                         rows_from_acc<1>(d, red[warp], nrt, lane);
@@ -1197,10 +1285,73 @@ __global__ void k_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __h
     *reinterpret_cast<uint4 *>(dst + off) = v;
 }
 
+// Pack a blockwise-int8 N x K matrix (an fp16 scale per row and 32 inputs) into the step kernel's
+// int8 units; rows map as in k_pack_rows. CTA c's units start at c * cta_bytes, in (pass, chunk)
+// order; a unit holds its rows' bytes as offset binary (q + 128) in 16-byte chunks swizzled like
+// the fp16 units, then the scales [block][row tile][8] as fp16 pairs (row g, row g + 8) of the
+// tile. One thread per row and 32-input block.
+__global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
+                               const __half *bs, const int *row_of, int N, int K, int grid, int pass_rows,
+                               int chunk_w, int cta_bytes) {
+    const int nbk = K / 32;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)N * nbk) return;
+    const int row = (int)(idx / nbk);
+    const int k = (int)(idx - (long long)row * nbk) * 32;
+    const int P = N / 2, pair = row / 2;
+    int c = (int)(((long long)pair * grid) / P);
+    while (c > 0 && (long long)P * c / grid > pair) --c;
+    while (c + 1 < grid && (long long)P * (c + 1) / grid <= pair) ++c;
+    const int R0 = 2 * (int)((long long)P * c / grid);
+    const int R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+    const int lr = row - R0;
+    const int pi = lr / pass_rows;
+    const int rows_p = min(pass_rows, R - pi * pass_rows);
+    const int nrt = (rows_p + 15) / 16;
+    const int qi = k / chunk_w;
+    const int wq = min(chunk_w, K - qi * chunk_w);
+    const int r = lr - pi * pass_rows;
+    const size_t pass_full = (size_t)pass_rows * K + (size_t)nbk * ((pass_rows + 15) / 16) * 32;
+    uint8_t *unit = dst + (size_t)c * cta_bytes + (size_t)pi * pass_full +
+                    (size_t)qi * ((size_t)rows_p * chunk_w + (size_t)(chunk_w / 32) * nrt * 32);
+    const int kl = k - qi * chunk_w;                       // first input within the unit
+    uint4 v[2];
+    __half sc = __ushort_as_half(0);
+    v[0] = v[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+    const int src = row_of[row];
+    if (src >= 0) {
+        const int8_t *rp = src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
+        sc = src < rows_a ? as[(size_t)src * nbk + k / 32] : bs[(size_t)(src - rows_a) * nbk + k / 32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(rp + k + 16 * h);
+            v[h] = make_uint4(q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u);
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int j = kl / 16 + h;
+        const int pj = (j & ~7) | ((j & 7) ^ (r & 7));
+        *reinterpret_cast<uint4 *>(unit + (size_t)r * wq + (size_t)pj * 16) = v[h];
+    }
+    const int si = ((kl / 32) * nrt + r / 16) * 8 + (r & 7);
+    reinterpret_cast<__half *>(unit + (size_t)rows_p * wq)[2 * si + ((r >> 3) & 1)] = sc;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Packed int8 bytes of R rows (passes of pass_rows rows, each all K inputs plus its scales).
+static size_t i8_rows_bytes(int R, int K, int pass_rows) {
+    size_t b = 0;
+    for (int p0 = 0; p0 < R; p0 += pass_rows) {
+        const int rp = std::min(pass_rows, R - p0);
+        b += (size_t)rp * K + (size_t)(K / 32) * ((rp + 15) / 16) * 32;
+    }
+    return b;
+}
 
 // Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
 // pass), each unit at most one stage.
@@ -1208,11 +1359,14 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
     const int P = o.N / 2;
     o.grid = std::max(1, std::min(num_sms, P));
     const int rmax = 2 * ((P + o.grid - 1) / o.grid);                       // rows of the busiest CTA
+    const bool i8 = o.fmt == WF_I8;
+    const int gran = i8 ? 128 : 256;                                         // chunk_w granule
     long long best = -1;
     for (int pr = std::min(kPassRows, rmax); pr >= 2; pr -= 2) {
-        int w = (stage_bytes / (pr * 2)) / 256 * 256;
+        // widest unit within a stage: pr * w * 2 bytes (fp16), w * (pr + row tiles) (int8)
+        int w = (i8 ? stage_bytes / (pr + (pr + 15) / 16) : stage_bytes / (pr * 2)) / gran * gran;
         if (w >= o.K) w = o.K;
-        if (w < 256 && w != o.K) continue;
+        if (w < gran && w != o.K) continue;
         const long long units = (long long)((rmax + pr - 1) / pr) * ((o.K + w - 1) / w);
         if (best < 0 || units < best) {
             best = units;
@@ -1222,14 +1376,22 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
     }
     if (best < 0) {
         o.pass_rows = 2;
-        o.chunk_w = 256;
+        o.chunk_w = gran;
     }
+    const size_t cb = i8 ? i8_rows_bytes(rmax, o.K, o.pass_rows) : 0;
+    o.cta_bytes = cb <= (size_t)INT_MAX ? (int)cb : -1;
+}
+
+size_t step_gemv_bytes(const StepOp &o) {
+    return o.fmt == WF_I8 ? (size_t)o.grid * (size_t)std::max(o.cta_bytes, 0) : (size_t)o.N * o.K * 2;
 }
 
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
+    const bool i8 = o.fmt == WF_I8;
+    if (i8 && (o.K % 128 || (o.chunk_w != o.K && o.chunk_w % 128) || o.cta_bytes <= 0)) return false;
+    if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
     return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 && o.pass_rows <= kPassRows &&
-           (size_t)o.pass_rows * o.chunk_w * 2 <= (size_t)stage_bytes &&
-           (o.chunk_w == o.K || o.chunk_w % 256 == 0) &&
+           step_unit_bytes(o.fmt, o.pass_rows, o.chunk_w) <= (uint32_t)stage_bytes &&
            (o.pro == PRO_NORM || o.pro == PRO_EMBED_NORM ? o.K <= kNormRegs * 4 * kEpiThreads : true);
 }
 
@@ -1262,12 +1424,22 @@ cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __
     return cudaGetLastError();
 }
 
-template <int HD>
+cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
+                                const __half *bs, const int *row_of, const StepOp &plan, cudaStream_t s) {
+    if (plan.fmt != WF_I8 || plan.N % 2 || plan.K % 128 || plan.cta_bytes <= 0) return cudaErrorInvalidValue;
+    const long long total = (long long)plan.N * (plan.K / 32);
+    k_pack_rows_i8<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(dst, a, as, rows_a, b, bs, row_of, plan.N, plan.K,
+                                                                   plan.grid, plan.pass_rows, plan.chunk_w,
+                                                                   plan.cta_bytes);
+    return cudaGetLastError();
+}
+
+template <int HD, bool Q8>
 static cudaError_t step_launch_t(const StepParams *p, int grid, size_t smem, cudaStream_t s, bool pdl) {
     if (p == nullptr) {
-        cudaError_t e = cudaFuncSetAttribute(k_step<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_step<HD, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        return cudaFuncSetAttribute(k_step<HD>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        return cudaFuncSetAttribute(k_step<HD, Q8>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     (int)cudaSharedmemCarveoutMaxShared);
     }
     cudaLaunchConfig_t cfg = {};
@@ -1287,23 +1459,27 @@ static cudaError_t step_launch_t(const StepParams *p, int grid, size_t smem, cud
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, k_step<HD>, *p);
+    return cudaLaunchKernelEx(&cfg, k_step<HD, Q8>, *p);
 }
 
-cudaError_t prepare_step(int hd, size_t smem) {
-    if (hd == 128) return step_launch_t<128>(nullptr, 0, smem, nullptr, false);
-    if (hd == 64) return step_launch_t<64>(nullptr, 0, smem, nullptr, false);
+template <bool Q8>
+static cudaError_t step_launch_hd(int hd, const StepParams *p, int grid, size_t smem, cudaStream_t s, bool pdl) {
+    if (hd == 128) return step_launch_t<128, Q8>(p, grid, smem, s, pdl);
+    if (hd == 64) return step_launch_t<64, Q8>(p, grid, smem, s, pdl);
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl) {
+cudaError_t prepare_step(int hd, size_t smem, bool q8) {
+    return q8 ? step_launch_hd<true>(hd, nullptr, 0, smem, nullptr, false)
+              : step_launch_hd<false>(hd, nullptr, 0, smem, nullptr, false);
+}
+
+cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8) {
     if (p.stages < 2 || p.stage_bytes < 1024 || p.stage_bytes % 1024 || p.stage_bytes > kMaxStageBytes ||
         p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks || p.attn_off % 128 ||
         p.vec_bytes % 128 || (size_t)p.attn_off + step_attn_smem_bytes(hd) > (size_t)p.vec_bytes)
         return cudaErrorInvalidValue;
-    if (hd == 128) return step_launch_t<128>(&p, grid, smem, s, pdl);
-    if (hd == 64) return step_launch_t<64>(&p, grid, smem, s, pdl);
-    return cudaErrorInvalidValue;
+    return q8 ? step_launch_hd<true>(hd, &p, grid, smem, s, pdl) : step_launch_hd<false>(hd, &p, grid, smem, s, pdl);
 }
 
 }  // namespace sp
