@@ -216,15 +216,37 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------------------------
+DECODE_SPECS = {
+    # the headline: Qwen2-1.5B fp16, 512-token prompt, 256 greedy tokens per step
+    "decode": dict(preset="qwen2-1.5b", fmt="f16", prompt=PROMPT, decode=DECODE, capacity=CAPACITY, metric=METRIC),
+    # the int8 target architecture: Qwen2.5-7B shapes, blockwise int8 (32-input blocks, fp16 scales)
+    "decode-7b-i8": dict(preset="qwen2.5-7b", fmt="i8", prompt=512, decode=128, capacity=4096,
+                         metric="Qwen2.5-7B int8 decode tok/s"),
+}
+
+
 def run_decode(args, world, rank, local):
-    from seedplane_b200.config import QWEN2_1_5B
+    """Greedy decode on one GPU per rank (replicas): `value` = decoded tokens of all ranks / the
+    slowest rank's device time for the timed steps; each step re-decodes the same tokens after
+    the same prompt (the cache length is reset, the prompt's K/V stay)."""
+    from seedplane_b200.config import PRESETS
     from seedplane_b200.engine import CudaQwen2
-    from seedplane_b200.randinit import make_weights, random_prompt
-    cfg = QWEN2_1_5B
+    from seedplane_b200.randinit import make_int8_blockwise, make_weights, random_prompt
+    spec = DECODE_SPECS[args.workload]
+    cfg = PRESETS[spec["preset"]]
+    PROMPT, DECODE, CAPACITY = spec["prompt"], spec["decode"], spec["capacity"]
+    i8 = spec["fmt"] == "i8"
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    w = make_weights(cfg, seed=0, dtype=torch.float16)
-    eng = CudaQwen2(cfg, w, device=dev)
+    if i8:
+        # drawn on the device (a CUDA generator stream): no CPU oracle runs on these weights
+        w = make_int8_blockwise(cfg, seed=0, device=str(dev))
+        eng = CudaQwen2(cfg, w, device=dev, weight_format="i8")
+        del w
+        torch.cuda.empty_cache()
+    else:
+        w = make_weights(cfg, seed=0, dtype=torch.float16)
+        eng = CudaQwen2(cfg, w, device=dev)
     prompt = random_prompt(cfg.vocab, PROMPT, seed=0)
     kv = eng.new_kv(CAPACITY)
     _, argmax = eng.forward(kv, prompt, want_logits=False)
@@ -264,9 +286,15 @@ def run_decode(args, world, rank, local):
     # kernel-per-op chain, SEEDPLANE_STEP=chain, launches 5 L + 1 kernels per token instead)
     hbm, peak_kind = peaks()
     avg_ctx = PROMPT + DECODE / 2
-    alg_bytes = cfg.weight_bytes_per_token(2) + cfg.kv_bytes_per_position(2) * avg_ctx
+    if i8:      # int8 matrices (1 B + a 2-byte scale per 32) and, when tied, the fp16 head
+        H, I, V = cfg.hidden, cfg.intermediate, cfg.vocab
+        mats = cfg.layers * (cfg.qkv_rows * H + H * H + 3 * I * H) + (0 if cfg.tied_embeddings else V * H)
+        w_bytes = cfg.weight_bytes_per_token(0) + mats * (1 + 2 / 32) + (V * H * 2 if cfg.tied_embeddings else 0)
+    else:
+        w_bytes = cfg.weight_bytes_per_token(2)
+    alg_bytes = w_bytes + cfg.kv_bytes_per_position(2) * avg_ctx
     achieved = alg_bytes / (ms_per_token / 1000.0) / 1e9
-    traffic = traffic_per_token()
+    traffic = traffic_per_token() if not i8 else None
     step_kernel = os.environ.get("SEEDPLANE_STEP", "step") != "chain"
 
     # e2e through the public API: host prompt (pinned) -> device, prefill, decode, tokens -> host
@@ -304,15 +332,16 @@ def run_decode(args, world, rank, local):
     line = None
     if rank == 0:
         L = cfg.layers
-        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        wdesc = "blockwise-int8 (32-input blocks, fp16 scales)" if i8 else "fp16"
+        line = {"metric": spec["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-                "config": {"workload": f"qwen2-1.5b greedy decode: {DECODE} tokens per step after a {PROMPT}-token "
-                                       "prompt, random-init fp16 weights (seed 0), fp16 KV cache",
+                "scaling": "weak", "vs_baseline": None, "dtype": "i8xf16" if i8 else "f16", "data": "synthetic",
+                "config": {"workload": f"{cfg.name} greedy decode: {DECODE} tokens per step after a {PROMPT}-token "
+                                       f"prompt, random-init {wdesc} weights (seed 0), fp16 KV cache",
                            "decode_tokens_per_step": DECODE, "prompt": PROMPT, "kv_capacity": CAPACITY,
-                           "weights": "fp16", "accumulate": "fp32", "kv": "fp16",
+                           "weights": wdesc, "accumulate": "fp32", "kv": "fp16",
                            "parallelism": f"replicas x{world} (independent requests, no collective)",
-                           "l2": "inputs larger than L2: 3.09 GB of weights streamed per token",
+                           "l2": f"inputs larger than L2: {w_bytes / 1e9:.2f} GB of weights streamed per token",
                            "ms_per_token": ms_per_token},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
@@ -321,11 +350,15 @@ def run_decode(args, world, rank, local):
                              "algorithmic_bytes_per_launch": alg_bytes, "peak_kind": peak_kind},
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                         "d2h_bytes_per_step": DECODE * 4 + 4,
-                        "note": "public API per step: pinned prompt H2D, prefill, 256-token decode, tokens D2H"},
+                        "note": f"public API per step: pinned prompt H2D, prefill, {DECODE}-token decode, tokens D2H"},
                 "gpu_launches": args.steps * (DECODE * (1 if step_kernel else 5 * L + 1) + 1),
                 "clocks": clocks.summary(),
                 "token_sha256": __import__("hashlib").sha256(json.dumps(tokens_ref).encode()).hexdigest()}
-        if world == 1 and not args.no_cpu_baseline:
+        if i8:
+            line["cpu_baseline"] = None
+            line["cpu_baseline_note"] = ("not run: the oracle needs the 7B checkpoint dequantized to fp32 (28 GB) "
+                                         "in host memory; int8 parity is covered by the tests on smaller shapes")
+        elif world == 1 and not args.no_cpu_baseline:
             threads = physical_cores()
             n = 200    # about 10 s of CPU work on a 16-core host
             val, toks, dt = cpu_oracle_sample(cfg, w, prompt, n, threads)
@@ -479,7 +512,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "burst", "verify", "speculative"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "decode-7b-i8", "burst", "verify", "speculative"),
+                    default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":

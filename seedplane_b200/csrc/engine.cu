@@ -564,8 +564,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         const int want = (int)env_long("SEEDPLANE_STEP_STAGES", 3);
         e->step_inflight = (int)env_long("SEEDPLANE_STEP_INFLIGHT", 0);
         e->step_l2_ahead = (int)env_long("SEEDPLANE_STEP_L2_KB", 0) * 1024;
-        e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, std::max(2, want));
-        if (e->step_lay.stage_bytes < 16 * 1024 && want > 2) e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, 2);
+        e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, std::max(2, want), i8);
+        if (e->step_lay.stage_bytes < 16 * 1024 && want > 2) e->step_lay = step_layout((int)H, e->step_xmax, (int)HD, 2, i8);
         if (e->step_lay.stage_bytes < 16 * 1024) {
             delete e;
             return fail(SP_ERR_UNSUPPORTED, "step kernel: the input vector of %d floats leaves no room for the ring",

@@ -39,6 +39,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "tc.cuh"
 
 namespace sp {
 
@@ -50,6 +51,10 @@ constexpr int kThreads = kEpiThreads + 32;
 constexpr int kMaxStageBytes = 64 * 1024;   // one unit per stage (a bulk copy costs about the same
                                             // time whatever its size, so big ones ingest faster)
 constexpr int kPassRows = kStepPassRows;    // rows per pass: 16 per warp
+constexpr int kPassRowsI8 = 128;            // int8 passes: one M = 128 tensor-core tile
+constexpr int kUnitBlocksI8 = 32;           // int8 32-input blocks per unit: 8 TMEM columns each
+constexpr uint32_t kStepTmemCols = 2 * 8 * kUnitBlocksI8;   // two unit buffers
+static_assert(kPassRowsI8 <= 4 * kPassRows, "int8 pass rows go through red[]");
 constexpr int kGroup = 8;                   // q heads per kv head at most
 constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
 constexpr int kLLBatch = 7;                 // LL word pairs per thread in flight (plain prologues, merge)
@@ -121,76 +126,101 @@ SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int ro
     }
 }
 
-// Two offset-binary bytes (u = q + 128, bytes sel of a word) -> fp16 pair q exactly: u placed in
-// the low mantissa bits under exponent bits 0x64 reads as 1024 + u; minus 1152 (0x6480) leaves q.
-// (The magic-number int8 -> fp16 conversion of Kim et al., "Who Says Elephants Can't Run", 2022.)
-SP_DEVINL uint32_t u8x2_to_h2(uint32_t w, uint32_t sel) {
-    const uint32_t h = __byte_perm(w, 0x64646464u, sel);
-    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&h), __halves2half2(__ushort_as_half(0x6480),
-                                                                                   __ushort_as_half(0x6480)));
-    return *reinterpret_cast<const uint32_t *>(&q);
+// Integer digits of a GEMV input for int8 weights. A 32-input block with max |x| in [2^E, 2^E+1)
+// gets the scale 2^(E - 26): q = rint(x * 2^(26 - E)) is an integer below 2^27 in magnitude, written
+// as q = d0 2^21 + d1 2^14 + d2 2^7 + d3 with d0 in [-64, 63] and d1..d3 in [0, 127] (the bits of
+// q), so every digit is an int8 and x = scale * q to 2^-28 of the block's largest input. Layout:
+// 128 bytes per block, [half h][digit c][16 inputs] (input k at (k / 32) * 128 + ((k / 16) & 1) *
+// 64 + c * 16 + k % 16): each 16-input half is a K-major 8-row core matrix whose rows 0-3 are the
+// digits (rows 4-7, the next 64 bytes, give output columns that are not read). The block's scale
+// goes to bsc[k / 32]. The 32 inputs of a block are the float4s of 8 consecutive lanes (lane & 7 =
+// position in the block); the whole warp calls this.
+SP_DEVINL void digitize4(float4 x, int k, int8_t *dg, float *bsc) {
+    float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    // biased exponent of m, at least 26 (blocks below 2^-101 become zero: multiplier 2^127)
+    const int eb = max((int)((__float_as_uint(m) >> 23) & 0xffu), 26);
+    const float mul = __uint_as_float((uint32_t)(280 - eb) << 23);           // 2^(153 - eb)
+    if ((threadIdx.x & 7) == 0) bsc[k >> 5] = __uint_as_float((uint32_t)(eb - 26) << 23);   // 2^(eb - 153)
+    uint32_t sp[4];
+    const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int q = __float2int_rn(xv[e] * mul);
+        // bytes (low to high): d3, d2, d1, d0 = q's 7-bit groups, the top one signed
+        sp[e] = ((uint32_t)q & 0x7fu) | (((uint32_t)q << 1) & 0x7f00u) | (((uint32_t)q << 2) & 0x7f0000u) |
+                (((uint32_t)q << 3) & 0xff000000u);
+    }
+    // transpose: word c = byte (3 - c) of the four inputs (c = 0: the top digit)
+    const uint32_t t0 = __byte_perm(sp[0], sp[1], 0x5140), t1 = __byte_perm(sp[0], sp[1], 0x7362);
+    const uint32_t t2 = __byte_perm(sp[2], sp[3], 0x5140), t3 = __byte_perm(sp[2], sp[3], 0x7362);
+    int8_t *w = dg + (k >> 5) * 128 + ((k >> 4) & 1) * 64 + (k & 15);
+    *reinterpret_cast<uint32_t *>(w) = __byte_perm(t1, t3, 0x7632);
+    *reinterpret_cast<uint32_t *>(w + 16) = __byte_perm(t1, t3, 0x5410);
+    *reinterpret_cast<uint32_t *>(w + 32) = __byte_perm(t0, t2, 0x7632);
+    *reinterpret_cast<uint32_t *>(w + 48) = __byte_perm(t0, t2, 0x5410);
 }
 
-// One blockwise-int8 unit of a pass (see k_pack_rows_i8): rows of offset-binary bytes in 16-byte
-// chunks XOR-swizzled like the fp16 units, then the scales [block][row tile][8] as fp16 pairs
-// (row g, row g + 8). One ldmatrix.x4 gives a 16-row x 32-input block (a lane: 4 consecutive
-// inputs of rows g and g + 8 in each half); the two MMAs take the inputs in the order the bytes
-// arrive (the k-index map 2t, 2t+1, 2t+8, 2t+9 -> 4t .. 4t+3 is applied to the B operand too),
-// summed into a fresh block accumulator that is scaled per row into the running sums in fp32.
-// Warp w takes blocks w, w + 4, ...; slots as in unit_mma.
-template <int U>
-SP_DEVINL void unit_mma_i8(float (&d)[4][4], uint32_t unit, int rs, int nb, int rows_p, int nrt, int q0,
-                           const __half *xh, const __half *xl, int warp, int lane) {
-    const int lm = lane >> 3, lr = lane & 7;
-    const uint32_t scl = unit + (uint32_t)(rows_p * rs);
-    for (int kb = warp; kb < nb; kb += 4 * U) {
-        uint32_t b[U][4];
+// The MMAs of one int8 unit (one thread). A unit of rows_p rows x 32 nb inputs holds, per 32-input
+// block b, the rows' 32 bytes as two K-major halves: [half][row][16 bytes] (rows at 16 B, 8-row
+// core groups 128 B apart, halves rows_p * 16 B apart; no padding rows: the rows past rows_p of the
+// M = 128 tile read whatever follows and land in TMEM lanes nobody reads), then the scales
+// [row][block] fp16. Block b: D (TMEM columns 8b .. 8b + 7) = A (128 x 32 s8) * B (the 8-row digit
+// cores of the same 32 inputs), exact s32, not accumulated: every block keeps its own sums.
+// Issued by lane 0 of each compute warp w for blocks w, w + 4, ... (the tensor core takes one such
+// MMA per ~45 cycles whatever the row count; four issuers keep it fed), descriptors advanced in
+// place.
+SP_DEVINL void unit_i8_issue(uint32_t tmem, uint32_t unit, int rows_p, int nb, uint32_t dgb, int b0) {
+    uint64_t ad = smem_desc(unit + (uint32_t)(b0 * rows_p * 32), (uint32_t)(rows_p * 16), 128);
+    uint64_t bd = smem_desc(dgb + (uint32_t)(b0 * 128), 64, 128);
+    const uint64_t da = (uint64_t)((4 * rows_p * 32) >> 4), db = (uint64_t)((4 * 128) >> 4);
+    uint32_t t = tmem + (uint32_t)(8 * b0);
+    for (int b = b0; b < nb; b += 4) {
+        mma_i8(t, ad, bd);
+        ad += da;                                           // start-address field (bits 0-13) only
+        bd += db;
+        t += 32;
+    }
+}
+
+// 16 consecutive TMEM columns of this thread's lane (no wait).
+SP_DEVINL void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+}
+
+// This thread's row (its TMEM lane) of one int8 unit of nb blocks (nb even): sum over blocks b of
+// row scale (sc2: fp16 pairs of blocks 2j, 2j + 1) * input block scale * (2^14 (128 d0 + d1) +
+// (128 d2 + d3)), the d's the block's digit columns 0-3 (the pairs are exact in s32), in fp32 and
+// block order. Whole warp (tcgen05.ld is warp-wide).
+SP_DEVINL float unit_i8_row(uint32_t tmem_lane, const uint32_t (&sc2)[kUnitBlocksI8 / 2], int nb, const float *bsc) {
+    float y = 0.f;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            b[u][0] = b[u][1] = b[u][2] = b[u][3] = 0u;
-            const int kk = kb + 4 * u;
-            if (kk < nb && lane < 8) {                      // B column 0 = hi, column 1 = lo
-                const __half *xv = (lane < 4 ? xh : xl) + q0 + 32 * kk + 4 * (lane & 3);
-                const uint2 v0 = *reinterpret_cast<const uint2 *>(xv);
-                const uint2 v1 = *reinterpret_cast<const uint2 *>(xv + 16);
-                b[u][0] = v0.x;
-                b[u][1] = v0.y;
-                b[u][2] = v1.x;
-                b[u][3] = v1.y;
-            }
-        }
-        uint32_t a[4][4], sc[4];
+    for (int b0 = 0; b0 < kUnitBlocksI8; b0 += 4) {
+        if (b0 < nb) {                                          // warp-uniform
+            uint32_t v[2][16];
+            tmem_ld16_nowait(tmem_lane + (uint32_t)(8 * b0), v[0]);
+            if (b0 + 2 < nb) tmem_ld16_nowait(tmem_lane + (uint32_t)(8 * b0 + 16), v[1]);
+            tmem_wait_ld();
 #pragma unroll
-        for (int sl = 0; sl < 4; ++sl) {
-            const int rt = sl / U, kk = kb + 4 * (sl % U);
-            if (rt < nrt && kk < nb) {
-                const int r = min(rt * 16 + ((lm & 1) << 3) + lr, rows_p - 1);
-                const int j = 2 * kk + (lm >> 1);
-                const int pj = (j & ~7) | ((j & 7) ^ (r & 7));
-                ldmatrix_x4(unit + (uint32_t)(r * rs + pj * 16), a[sl][0], a[sl][1], a[sl][2], a[sl][3]);
-                asm volatile("ld.shared.b32 %0, [%1];"
-                             : "=r"(sc[sl])
-                             : "r"(scl + (uint32_t)(((kk * nrt + rt) * 8 + (lane >> 2)) * 4)));
-            }
-        }
-#pragma unroll
-        for (int sl = 0; sl < 4; ++sl) {
-            const int rt = sl / U, kk = kb + 4 * (sl % U);
-            if (rt < nrt && kk < nb) {
-                float e[4] = {0.f, 0.f, 0.f, 0.f};
-                const uint32_t *bb = b[sl % U];
-                mma_16816(e, u8x2_to_h2(a[sl][0], 0x4140), u8x2_to_h2(a[sl][1], 0x4140), u8x2_to_h2(a[sl][0], 0x4342),
-                          u8x2_to_h2(a[sl][1], 0x4342), bb[0], bb[1]);
-                mma_16816(e, u8x2_to_h2(a[sl][2], 0x4140), u8x2_to_h2(a[sl][3], 0x4140), u8x2_to_h2(a[sl][2], 0x4342),
-                          u8x2_to_h2(a[sl][3], 0x4342), bb[2], bb[3]);
-                const float2 s = __half22float2(*reinterpret_cast<const __half2 *>(&sc[sl]));
-                d[sl][0] = fmaf(s.x, e[0], d[sl][0]);
-                d[sl][1] = fmaf(s.x, e[1], d[sl][1]);
-                d[sl][2] = fmaf(s.y, e[2], d[sl][2]);
-                d[sl][3] = fmaf(s.y, e[3], d[sl][3]);
+            for (int e = 0; e < 4; ++e) {
+                const int b = b0 + e;
+                if (b < nb) {
+                    const uint32_t *r = &v[e >> 1][8 * (e & 1)];
+                    const int hi = (int)r[0] * 128 + (int)r[1], lo = (int)r[2] * 128 + (int)r[3];
+                    const float ds = fmaf(16384.f, (float)hi, (float)lo);
+                    const __half2 s2 = *reinterpret_cast<const __half2 *>(&sc2[b >> 1]);
+                    const float sc = (b & 1) ? __high2float(s2) : __low2float(s2);
+                    y = fmaf(sc * bsc[b], ds, y);
+                }
             }
         }
     }
+    return y;
 }
 
 // Row sums of a pass from the accumulator slots (lanes 4i: rows i and i + 8 of each tile; columns
@@ -355,7 +385,14 @@ SP_DEVINL bool ll_poll(uint64_t (&w)[N][2], uint32_t valid, Addr addr, uint32_t 
 // Prologue input of a norm op: this thread's float4s q of the residual stream (elements
 // 4 (tid + q kEpiThreads) ..., K <= 4 x kNormRegs x kEpiThreads) from LL words, kNormRound
 // float4s (2 kNormRound word pairs) per round trip.
+// HILO: the payloads are fp16 (hi, lo) pairs, x = hi + lo; else fp32.
 constexpr int kNormRound = 3;
+SP_DEVINL float ll_x(uint64_t w, bool hilo) {
+    if (!hilo) return ll_f(w);
+    const uint32_t u = (uint32_t)w;
+    return __half2float(__ushort_as_half((unsigned short)(u & 0xffffu))) + __half2float(__ushort_as_half((unsigned short)(u >> 16)));
+}
+template <bool HILO>
 SP_DEVINL bool ll_norm_input(float4 (&v)[kNormRegs], const uint64_t *lin, int K, uint32_t tag, const Abort &ab) {
     const int tid = threadIdx.x;
 #pragma unroll
@@ -372,7 +409,8 @@ SP_DEVINL bool ll_norm_input(float4 (&v)[kNormRegs], const uint64_t *lin, int K,
 #pragma unroll
         for (int q = 0; q < kNormRound; ++q)
             if (q0 + q < kNormRegs)
-                v[q0 + q] = make_float4(ll_f(w[2 * q][0]), ll_f(w[2 * q][1]), ll_f(w[2 * q + 1][0]), ll_f(w[2 * q + 1][1]));
+                v[q0 + q] = make_float4(ll_x(w[2 * q][0], HILO), ll_x(w[2 * q][1], HILO), ll_x(w[2 * q + 1][0], HILO),
+                                        ll_x(w[2 * q + 1][1], HILO));
     }
     return true;
 }
@@ -396,6 +434,59 @@ SP_DEVINL void ll_hilo_input(__half *xh, __half *xl, const uint64_t *lin, int K,
                 const uint32_t u0 = (uint32_t)w[j][0], u1 = (uint32_t)w[j][1];
                 *reinterpret_cast<uint32_t *>(xh + e) = (u0 & 0xffffu) | (u1 << 16);
                 *reinterpret_cast<uint32_t *>(xl + e) = (u0 >> 16) | (u1 & 0xffff0000u);
+            }
+        }
+    }
+}
+
+// Int8 prologues (out of line: they run once per op and keep the kernel's register budget for
+// the unit loop). The merged attention output (LL words of fp16 hi / lo payloads) into digits:
+__device__ __noinline__ void attn_digits(const uint64_t *lin, int K, uint32_t tag, const Abort &ab, int8_t *dg,
+                                         float *bsc) {
+    // all of this thread's float4s (K <= 4 kNormRegs kEpiThreads) in one round trip
+    const int tid = threadIdx.x;
+    uint64_t w[2 * kNormRegs][2];
+    uint32_t valid = 0u;
+#pragma unroll
+    for (int j = 0; j < 2 * kNormRegs; ++j)
+        if (4 * (tid + (j >> 1) * kEpiThreads) < K) valid |= 1u << j;
+    if (!ll_poll<2 * kNormRegs>(w, valid, [&](int j) { return lin + 4 * (tid + (j >> 1) * kEpiThreads) + 2 * (j & 1); },
+                                tag, ab))
+        return;
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < kNormRegs; ++q)
+        if (4 * (tid + q * kEpiThreads) < K)
+            digitize4(make_float4(ll_x(w[2 * q][0], true), ll_x(w[2 * q][1], true), ll_x(w[2 * q + 1][0], true),
+                                  ll_x(w[2 * q + 1][1], true)),
+                      4 * (tid + q * kEpiThreads), dg, bsc);
+}
+
+// PRO_PLAIN into digits: the fp16 hi / lo vectors behind the counter (written by other CTAs in
+// this launch: loads through L2), kPlainBatch float4s (2 kPlainBatch loads) in flight per thread:
+// the round trip to L2, not the arithmetic, bounds this prologue.
+constexpr int kPlainBatch = 12;
+__device__ __noinline__ void plain_digits(const __half *xin_h, const __half *xin_l, int K, int8_t *dg, float *bsc) {
+    const int tid = threadIdx.x;
+    for (int i0 = tid; 4 * i0 < K; i0 += kPlainBatch * kEpiThreads) {
+        uint2 h[kPlainBatch], l[kPlainBatch];
+#pragma unroll
+        for (int u = 0; u < kPlainBatch; ++u) {
+            const int i = i0 + u * kEpiThreads;
+            if (4 * i < K) {
+                h[u] = __ldcg(reinterpret_cast<const uint2 *>(xin_h) + i);
+                l[u] = __ldcg(reinterpret_cast<const uint2 *>(xin_l) + i);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kPlainBatch; ++u) {
+            const int i = i0 + u * kEpiThreads;
+            if (4 * i < K) {                                        // warp-uniform (K % 128 == 0)
+                const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&h[u].x));
+                const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&h[u].y));
+                const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&l[u].x));
+                const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&l[u].y));
+                digitize4(make_float4(h0.x + l0.x, h0.y + l0.y, h1.x + l1.x, h1.y + l1.y), 4 * i, dg, bsc);
             }
         }
     }
@@ -764,10 +855,10 @@ __device__ __noinline__ void lmhead_finish(const StepParams &p, const StepOp &op
     }
 }
 
-// Bytes of one unit of `rows` rows x `w` inputs: fp16 rows, or int8 rows plus the scales of
-// ceil(rows / 16) row tiles (8 fp16 pairs per tile and 32-input block).
+// Bytes of one unit of `rows` rows x `w` inputs: fp16 rows, or int8 rows plus their fp16 scales
+// (one per row and 32-input block), padded to 16 bytes.
 SP_HOSTDEV uint32_t step_unit_bytes(int fmt, int rows, int w) {
-    return fmt == WF_I8 ? (uint32_t)(rows * w + (w / 32) * ((rows + 15) / 16) * 32) : (uint32_t)(rows * w * 2);
+    return fmt == WF_I8 ? (uint32_t)(rows * w + (((w / 32) * rows * 2 + 15) & ~15)) : (uint32_t)(rows * w * 2);
 }
 
 // The CTA's weight units of the step in consumption order (op, pass, chunk). A unit's bytes are
@@ -833,6 +924,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     __shared__ int s_abort;
     __shared__ int s_issued, s_consumed;      // stages the producer issued / the compute warps consumed
     __shared__ float red[4][kPassRows];       // per-warp row partials of a pass (k-steps split over warps)
+    __shared__ uint64_t s_accb[2];            // Q8: the int8 MMAs of a unit (TMEM buffer 0 / 1) are done
+    __shared__ uint32_t s_tmem;               // Q8: TMEM accumulator base (kStepTmemCols columns)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, c = blockIdx.x;
@@ -857,12 +950,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
+        if (Q8) {                             // one commit from each compute warp's issuing lane
+            mbar_init(&s_accb[0], kEpiThreads / 32);
+            mbar_init(&s_accb[1], kEpiThreads / 32);
+        }
         fence_mbar_init();
+    }
+    if (Q8 && warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(kStepTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid < kOpWords) cp_async16(reinterpret_cast<uint4 *>(opc) + tid, reinterpret_cast<const uint4 *>(p.ops) + tid);
     cp_async_commit();
     cp_async_wait_all();
+    if (Q8) tc_fence_before();
     __syncthreads();
+    if (Q8) tc_fence_after();
+    const uint32_t tmem = Q8 ? s_tmem : 0u;
+    uint32_t acc_par = 0u;                    // Q8: phases of s_accb[0] (bit 0) and s_accb[1] (bit 1)
 
     if (warp == kProducerWarp) {
         // ---- producer: every unit of the step, in op order; waits only for free stages. While it
@@ -999,6 +1105,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             stamp_clk(p.trace, k, C, c, 0);
             const int K = op.K;
             __half *xl = xh + K;
+            // int8 weights: the input's digit rows (stride K + 16 bytes) and block scales instead
+            int8_t *dg = reinterpret_cast<int8_t *>(vec);
+            float *bsc = reinterpret_cast<float *>(vec + 4 * (K + 16));
+            const bool q8 = Q8 && op.fmt == WF_I8;
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
             const int P = op.N / 2;
             const int R0 = 2 * (int)((long long)P * c / op.grid);
@@ -1073,7 +1183,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         }
                     }
                 } else {
-                    ll_norm_input(v, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
+                    ll_norm_input<false>(v, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
                 }
                 __syncwarp();
                 float sq = 0.f;
@@ -1093,13 +1203,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
 #pragma unroll
                 for (int q = 0; q < kNormRegs; ++q) {
                     const int i = tid + q * kEpiThreads;
-                    if (4 * i < K)
-                        store_hilo4(xh, xl, 4 * i,
-                                    make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
-                                                (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w));
+                    if (4 * i < K) {                                // warp-uniform (K % 128 == 0 for int8)
+                        const float4 xn = make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
+                                                      (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w);
+                        if (q8)
+                            digitize4(xn, 4 * i, dg, bsc);
+                        else
+                            store_hilo4(xh, xl, 4 * i, xn);
+                    }
                 }
+            } else if (q8 && op.pro == PRO_ATTN) {
+                attn_digits(op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab, dg, bsc);
             } else if (op.pro == PRO_ATTN) {
                 ll_hilo_input(xh, xl, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
+            } else if (q8) {
+                plain_digits(op.xin_h, op.xin_l, K, dg, bsc);
             } else {
                 // PRO_PLAIN: fp16 hi / lo vectors behind the dependency counter: every 16-byte piece
                 // in flight at once (cp.async through L2), one wait
@@ -1110,6 +1228,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 cp_async_commit();
                 cp_async_wait_all();
             }
+            if (q8) fence_proxy_async_smem();                       // digits -> visible to the tensor core
             epi_sync();
             stamp(p.trace, k, C, c, 2);
             stamp_clk(p.trace, k, C, c, 1);
@@ -1134,6 +1253,62 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) d[i][j] = 0.f;
+                float yrow = 0.f;                                   // int8: this thread's row of the pass
+                if (q8) {
+                    // int8 units on the 5th-generation tensor cores, pipelined: lane 0 of each warp
+                    // issues its share of unit u + 1's block MMAs (TMEM buffer (u + 1) & 1) while
+                    // every thread reads unit u's sums out of TMEM; a unit's stage is free once its
+                    // MMAs are done and its row scales are in registers.
+                    const int nun = (K + op.chunk_w - 1) / op.chunk_w;
+                    auto stage_of = [&](int u, int &su, uint32_t &par) {
+                        const int x = s + u;
+                        su = x % S;
+                        par = (uint32_t)(round + x / S) & 1u;
+                    };
+                    auto issue = [&](int u) {                       // lane 0 of each compute warp
+                        int su;
+                        uint32_t par;
+                        stage_of(u, su, par);
+                        if (!wait_bar(&full[su], par, ab)) return;
+                        tc_fence_after();
+                        const int q0 = u * op.chunk_w;
+                        unit_i8_issue(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8), smem_u32(ring + (size_t)su * SB),
+                                      rows_p, min(op.chunk_w, K - q0) >> 5, smem_u32(dg) + (uint32_t)((q0 >> 5) * 128),
+                                      warp);
+                        mma_commit(&s_accb[u & 1]);
+                    };
+                    if (lane == 0) issue(0);
+                    int u = 0;
+                    for (; u < nun; ++u) {
+                        const int q0 = u * op.chunk_w, wq = min(op.chunk_w, K - q0), nb = wq >> 5;
+                        int su;
+                        uint32_t par;
+                        stage_of(u, su, par);
+                        if (!wait_bar(&s_accb[u & 1], (acc_par >> (u & 1)) & 1u, ab)) break;
+                        acc_par ^= 1u << (u & 1);
+                        tc_fence_after();
+                        if (p0 == 0 && u == 0) {
+                            stamp(p.trace, k, C, c, 4);
+                            stamp_clk(p.trace, k, C, c, 2);
+                        }
+                        // this row's scales: [row][block] fp16 after the unit's weights
+                        uint32_t sc2[kUnitBlocksI8 / 2];
+                        const uint32_t *sr = reinterpret_cast<const uint32_t *>(ring + (size_t)su * SB + (size_t)rows_p * wq) +
+                                             (size_t)min(tid, rows_p - 1) * (nb >> 1);
+#pragma unroll
+                        for (int j = 0; j < kUnitBlocksI8 / 2; ++j) sc2[j] = 2 * j < nb ? sr[j] : 0u;
+                        epi_sync();                                 // the stage is read
+                        if (tid == 0) mbar_arrive(&empty[su]);
+                        if (lane == 0 && u + 1 < nun) issue(u + 1);
+                        yrow += unit_i8_row(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8) + ((uint32_t)(warp * 32) << 16),
+                                            sc2, nb, bsc + (q0 >> 5));
+                        tc_fence_before();
+                    }
+                    consumed += u;
+                    s += u;
+                    round += s / S;
+                    s %= S;
+                } else {
                 for (int q0 = 0; q0 < K; q0 += op.chunk_w) {
                     const int wq = min(op.chunk_w, K - q0);
                     if (!wait_bar(&full[s], (uint32_t)round & 1u, ab)) break;
@@ -1142,17 +1317,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         stamp_clk(p.trace, k, C, c, 2);
                     }
                     const uint32_t unit = smem_u32(ring + (size_t)s * SB);
-                    if (Q8 && op.fmt == WF_I8) {                    // row stride wq bytes, 32-input blocks
-                        if (nrt == 1)
-                            unit_mma_i8<2>(d, unit, wq, wq >> 5, rows_p, nrt, q0, xh, xl, warp, lane);
-                        else
-                            unit_mma_i8<1>(d, unit, wq, wq >> 5, rows_p, nrt, q0, xh, xl, warp, lane);
-                    } else {                                        // row stride 2 wq bytes, 16-input k-steps
-                        if (nrt == 1)
-                            unit_mma<4>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
-                        else
-                            unit_mma<1>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
-                    }
+                    // row stride 2 wq bytes, 16-input k-steps
+                    if (nrt == 1)
+                        unit_mma<4>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
+                    else
+                        unit_mma<1>(d, unit, wq * 2, wq >> 4, rows_p, nrt, q0, xh, xl, warp, lane);
                     epi_sync();                                     // every warp is done with the unit
                     if (tid == 0) mbar_arrive(&empty[s]);
                     ++consumed;
@@ -1161,13 +1330,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                         ++round;
                     }
                 }
+                }
                 if (p0 == 0) stamp_clk(p.trace, k, C, c, 3);
                 // row sums: lanes 4i hold rows i and i + 8 of each tile (columns 0 = hi, 1 = lo);
                 // tile rt's U accumulator slots are summed in slot order
-                if ((lane & 3) == 0) {
-                    if (Q8 && nrt == 1 && op.fmt == WF_I8)
-                        rows_from_acc<2>(d, red[warp], nrt, lane);
-                    else if (nrt == 1)
+                if (q8) {
+                    if (tid < rows_p) (&red[0][0])[tid] = yrow;     // row tid of the pass (<= 128 rows)
+                } else if ((lane & 3) == 0) {
+                    if (nrt == 1)
                         rows_from_acc<4>(d, red[warp], nrt, lane);
                     else
                         rows_from_acc<1>(d, red[warp], nrt, lane);
@@ -1175,8 +1345,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 epi_sync();
                 if (!mine) continue;
                 const int r2 = 2 * tid;
-                const float y0 = ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
-                const float y1 = ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
+                const float y0 = q8 ? (&red[0][0])[r2] : ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
+                const float y1 =
+                    q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
                 if (op.epi == EPI_RESID) {
                     ll_st2(op.lout + row, ll_wordf(pre0 + y0, tag), ll_wordf(pre1 + y1, tag));
                 } else if (op.epi == EPI_LMHEAD) {
@@ -1239,7 +1410,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
         if (tid == 0) s_consumed = consumed;
     }
 
+    if (Q8 && warp < kEpiThreads / 32 && lane == 0) {
+        // every MMA issued has completed (one more commit per issuer tracks all of them) before
+        // TMEM goes back
+        mma_commit(&s_accb[0]);
+        mbar_wait_bounded(&s_accb[0], acc_par & 1u);
+    }
+    if (Q8) tc_fence_before();
     __syncthreads();
+    if (Q8 && warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kStepTmemCols));
+    }
     if (warp == kProducerWarp && lane == 0) {
         // after an abort, stages may still be in flight: let their copies land before exiting
         for (int i = s_consumed; i < s_issued; ++i) mbar_wait_bounded(&full[i % S], (uint32_t)(i / S) & 1u);
@@ -1287,9 +1469,9 @@ __global__ void k_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __h
 
 // Pack a blockwise-int8 N x K matrix (an fp16 scale per row and 32 inputs) into the step kernel's
 // int8 units; rows map as in k_pack_rows. CTA c's units start at c * cta_bytes, in (pass, chunk)
-// order; a unit holds its rows' bytes as offset binary (q + 128) in 16-byte chunks swizzled like
-// the fp16 units, then the scales [block][row tile][8] as fp16 pairs (row g, row g + 8) of the
-// tile. One thread per row and 32-input block.
+// order. A unit of rows_p rows x wq inputs holds, per 32-input block, [half][row][16 bytes] (the
+// tensor core's K-major core matrices, see unit_i8_issue), then the scales [row][block]. One
+// thread per row and 32-input block.
 __global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
                                const __half *bs, const int *row_of, int N, int K, int grid, int pass_rows,
                                int chunk_w, int cta_bytes) {
@@ -1307,35 +1489,27 @@ __global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, 
     const int lr = row - R0;
     const int pi = lr / pass_rows;
     const int rows_p = min(pass_rows, R - pi * pass_rows);
-    const int nrt = (rows_p + 15) / 16;
     const int qi = k / chunk_w;
     const int wq = min(chunk_w, K - qi * chunk_w);
     const int r = lr - pi * pass_rows;
-    const size_t pass_full = (size_t)pass_rows * K + (size_t)nbk * ((pass_rows + 15) / 16) * 32;
+    size_t pass_full = 0;                                  // bytes of a full pass (pass_rows rows)
+    for (int q0 = 0; q0 < K; q0 += chunk_w) pass_full += step_unit_bytes(WF_I8, pass_rows, min(chunk_w, K - q0));
     uint8_t *unit = dst + (size_t)c * cta_bytes + (size_t)pi * pass_full +
-                    (size_t)qi * ((size_t)rows_p * chunk_w + (size_t)(chunk_w / 32) * nrt * 32);
-    const int kl = k - qi * chunk_w;                       // first input within the unit
-    uint4 v[2];
+                    (size_t)qi * step_unit_bytes(WF_I8, rows_p, chunk_w);
+    const int bl = (k - qi * chunk_w) / 32;                // block within the unit
+    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
     __half sc = __ushort_as_half(0);
-    v[0] = v[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
     const int src = row_of[row];
     if (src >= 0) {
         const int8_t *rp = src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
         sc = src < rows_a ? as[(size_t)src * nbk + k / 32] : bs[(size_t)(src - rows_a) * nbk + k / 32];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(rp + k + 16 * h);
-            v[h] = make_uint4(q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u);
-        }
+        v0 = *reinterpret_cast<const uint4 *>(rp + k);
+        v1 = *reinterpret_cast<const uint4 *>(rp + k + 16);
     }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int j = kl / 16 + h;
-        const int pj = (j & ~7) | ((j & 7) ^ (r & 7));
-        *reinterpret_cast<uint4 *>(unit + (size_t)r * wq + (size_t)pj * 16) = v[h];
-    }
-    const int si = ((kl / 32) * nrt + r / 16) * 8 + (r & 7);
-    reinterpret_cast<__half *>(unit + (size_t)rows_p * wq)[2 * si + ((r >> 3) & 1)] = sc;
+    uint8_t *blk = unit + (size_t)bl * rows_p * 32;
+    *reinterpret_cast<uint4 *>(blk + (size_t)r * 16) = v0;
+    *reinterpret_cast<uint4 *>(blk + (size_t)rows_p * 16 + (size_t)r * 16) = v1;
+    reinterpret_cast<__half *>(unit + (size_t)rows_p * wq)[(size_t)r * (wq / 32) + bl] = sc;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1343,13 +1517,12 @@ __global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, 
 // ---------------------------------------------------------------------------------------------
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Packed int8 bytes of R rows (passes of pass_rows rows, each all K inputs plus its scales).
-static size_t i8_rows_bytes(int R, int K, int pass_rows) {
+// Packed int8 bytes of R rows (passes of pass_rows rows, each all K inputs in chunks of chunk_w).
+static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
     size_t b = 0;
-    for (int p0 = 0; p0 < R; p0 += pass_rows) {
-        const int rp = std::min(pass_rows, R - p0);
-        b += (size_t)rp * K + (size_t)(K / 32) * ((rp + 15) / 16) * 32;
-    }
+    for (int p0 = 0; p0 < R; p0 += pass_rows)
+        for (int q0 = 0; q0 < K; q0 += chunk_w)
+            b += step_unit_bytes(WF_I8, std::min(pass_rows, R - p0), std::min(chunk_w, K - q0));
     return b;
 }
 
@@ -1360,13 +1533,15 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
     o.grid = std::max(1, std::min(num_sms, P));
     const int rmax = 2 * ((P + o.grid - 1) / o.grid);                       // rows of the busiest CTA
     const bool i8 = o.fmt == WF_I8;
-    const int gran = i8 ? 128 : 256;                                         // chunk_w granule
+    const int gran = i8 ? 64 : 256;                                          // chunk_w granule (int8: even blocks)
     long long best = -1;
-    for (int pr = std::min(kPassRows, rmax); pr >= 2; pr -= 2) {
-        // widest unit within a stage: pr * w * 2 bytes (fp16), w * (pr + row tiles) (int8)
-        int w = (i8 ? stage_bytes / (pr + (pr + 15) / 16) : stage_bytes / (pr * 2)) / gran * gran;
+    for (int pr = std::min(i8 ? kPassRowsI8 : kPassRows, rmax); pr >= 2; pr -= 2) {
+        // widest unit within a stage (int8: at most kUnitBlocksI8 blocks, one TMEM column group each)
+        int w = i8 ? std::min((stage_bytes - 16) / (pr + pr / 16 + 1), 32 * kUnitBlocksI8) : stage_bytes / (pr * 2);
+        w = w / gran * gran;
         if (w >= o.K) w = o.K;
         if (w < gran && w != o.K) continue;
+        while (i8 && w > gran && step_unit_bytes(WF_I8, pr, w) > (uint32_t)stage_bytes) w -= gran;
         const long long units = (long long)((rmax + pr - 1) / pr) * ((o.K + w - 1) / w);
         if (best < 0 || units < best) {
             best = units;
@@ -1378,7 +1553,7 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
         o.pass_rows = 2;
         o.chunk_w = gran;
     }
-    const size_t cb = i8 ? i8_rows_bytes(rmax, o.K, o.pass_rows) : 0;
+    const size_t cb = i8 ? i8_rows_bytes(rmax, o.K, o.pass_rows, o.chunk_w) : 0;
     o.cta_bytes = cb <= (size_t)INT_MAX ? (int)cb : -1;
 }
 
@@ -1388,11 +1563,13 @@ size_t step_gemv_bytes(const StepOp &o) {
 
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
     const bool i8 = o.fmt == WF_I8;
-    if (i8 && (o.K % 128 || (o.chunk_w != o.K && o.chunk_w % 128) || o.cta_bytes <= 0)) return false;
+    if (i8 && (o.K % 128 || o.chunk_w % 64 || o.chunk_w > 32 * kUnitBlocksI8 || o.cta_bytes <= 0)) return false;
     if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
-    return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 && o.pass_rows <= kPassRows &&
+    return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 &&
+           o.pass_rows <= (i8 ? kPassRowsI8 : kPassRows) &&
            step_unit_bytes(o.fmt, o.pass_rows, o.chunk_w) <= (uint32_t)stage_bytes &&
-           (o.pro == PRO_NORM || o.pro == PRO_EMBED_NORM ? o.K <= kNormRegs * 4 * kEpiThreads : true);
+           (o.pro == PRO_NORM || o.pro == PRO_EMBED_NORM || (i8 && o.pro == PRO_ATTN) ? o.K <= kNormRegs * 4 * kEpiThreads
+                                                                                      : true);
 }
 
 size_t step_attn_smem_bytes(int hd) { return hd == 64 ? AttnRegion<64>::bytes : AttnRegion<128>::bytes; }
@@ -1402,11 +1579,14 @@ static size_t step_static_reserve() { return 2048; }   // static shared memory o
 // Dynamic shared memory: ring [stages x stage_bytes] | vector region | ops k, k + 1 | barriers.
 // The vector region holds a GEMV's input halves (4 K bytes) and, from attn_off on (after the QKV
 // projection's input, 4 hidden bytes), the attention staging region.
-StepLayout step_layout(int hidden, int xmax, int hd, int stages) {
+StepLayout step_layout(int hidden, int xmax, int hd, int stages, bool i8) {
     StepLayout L{};
     L.stages = stages;
-    L.attn_off = (int)align_up((size_t)hidden * 4, 128);
-    L.vec_bytes = (int)align_up(std::max((size_t)xmax * 4, (size_t)L.attn_off + step_attn_smem_bytes(hd)), 128);
+    // a GEMV input of K values: fp16 hi / lo halves (4 K bytes) or, for int8 weights, four digit
+    // rows of K + 16 bytes and K / 32 block scales
+    auto in_bytes = [&](size_t K) { return i8 ? 4 * (K + 16) + K / 8 : 4 * K; };
+    L.attn_off = (int)align_up(in_bytes((size_t)hidden), 128);
+    L.vec_bytes = (int)align_up(std::max(in_bytes((size_t)xmax), (size_t)L.attn_off + step_attn_smem_bytes(hd)), 128);
     const size_t fixed = (size_t)L.vec_bytes + 2 * sizeof(StepOp) + (size_t)stages * 16;
     const size_t budget = 227 * 1024 - step_static_reserve();
     if (stages < 2 || fixed >= budget) return L;

@@ -16,7 +16,7 @@ import time
 import torch
 
 from .config import PRESETS
-from .randinit import make_weights, random_prompt
+from .randinit import make_int8_blockwise, make_weights, random_prompt
 
 MODES = {"graph+pdl": ("1", "1"), "graph": ("1", "0"), "eager+pdl": ("0", "1"), "eager": ("0", "0")}
 # --step chain|step: the kernel-per-op chain or the persistent step kernel
@@ -172,10 +172,15 @@ def main():
     ap.add_argument("--step", default="step", help="comma list of step implementations: step (persistent), chain")
     ap.add_argument("--l2-ahead", default="0", help="comma list: weight tiles the step kernel warms L2 with ahead")
     ap.add_argument("--min-tiles", default="4", help="comma list: weight tiles per CTA at least (step kernel)")
+    ap.add_argument("--int8", action="store_true", help="blockwise-int8 random weights (drawn on the device)")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
-    w = make_weights(cfg, seed=0, dtype=torch.float16)
+    if a.int8:
+        w = make_int8_blockwise(cfg, seed=0, device="cuda")
+    else:
+        w = make_weights(cfg, seed=0, dtype=torch.float16)
+    fmt = "i8" if a.int8 else "f16"
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
     results = {}
     variants = [(m, pf, ev, sk, la, mt) for sk in a.step.split(",") for m in a.modes.split(",")
@@ -190,7 +195,7 @@ def main():
         os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
         os.environ["SEEDPLANE_TRACE"] = "1" if a.trace else "0"
         label = f"{sk} {mode} l2_ahead={la} min_tiles={mt} evict_first={ev}" if sk == "step" else f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
-        eng = CudaQwen2(cfg, w)
+        eng = CudaQwen2(cfg, w, weight_format=fmt)
         kv = eng.new_kv(a.capacity)
         _, am = eng.forward(kv, prompt, want_logits=False)
         first = int(am[-1])
@@ -219,7 +224,7 @@ def main():
         eng.close()
         del eng, kv
         torch.cuda.empty_cache()
-    print(json.dumps({"model": a.model, "prompt": a.prompt, "tokens": a.tokens, "results": results}))
+    print(json.dumps({"model": a.model, "weights": fmt, "prompt": a.prompt, "tokens": a.tokens, "results": results}))
 
 
 if __name__ == "__main__":
