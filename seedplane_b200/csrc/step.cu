@@ -137,6 +137,7 @@ SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int ro
 // position in the block); the whole warp calls this.
 SP_DEVINL void digitize4(float4 x, int k, int8_t *dg, float *bsc) {
     float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+    __syncwarp();                   // a warp left split by earlier divergent code pays ~8x per shuffle
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
