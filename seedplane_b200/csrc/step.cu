@@ -552,6 +552,62 @@ SP_DEVINL void stamp_clk(unsigned long long *tr, int k, int C, int c, int i) {
     if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + 8 + i] = clock64();
 }
 
+// One int8 pass (rows_p rows, all K inputs in units of chunk_w) on the 5th-generation tensor cores,
+// pipelined: lane 0 of each compute warp issues its share of unit u + 1's block MMAs (TMEM buffer
+// (u + 1) & 1) while every thread reads unit u's sums out of TMEM; a unit's stage goes back to the
+// producer once its MMAs are done and its row scales are in registers. Out of line: the loop gets
+// its own register budget instead of the step kernel's. Returns this thread's row sum.
+struct I8Ring {
+    uint8_t *ring;
+    uint64_t *full, *empty, *accb;
+    int S, SB;
+    int s, round, consumed;          // in / out: the ring position
+    uint32_t acc_par;                // in / out: phases of accb[0] (bit 0), accb[1] (bit 1)
+};
+__device__ __noinline__ float i8_pass(I8Ring &rg, uint32_t tmem, const int8_t *dg, const float *bsc, int rows_p, int K,
+                                      int chunk_w, const Abort ab) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = rg.S, SB = rg.SB, s0 = rg.s, round0 = rg.round;
+    uint32_t acc_par = rg.acc_par;
+    const int nun = (K + chunk_w - 1) / chunk_w;
+    auto issue = [&](int u) {                                   // lane 0 of each compute warp
+        const int x = s0 + u, su = x % S;
+        if (!wait_bar(&rg.full[su], (uint32_t)(round0 + x / S) & 1u, ab)) return;
+        tc_fence_after();
+        const int q0 = u * chunk_w;
+        unit_i8_issue(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8), smem_u32(rg.ring + (size_t)su * SB), rows_p,
+                      min(chunk_w, K - q0) >> 5, smem_u32(dg) + (uint32_t)((q0 >> 5) * 128), warp);
+        mma_commit(&rg.accb[u & 1]);
+    };
+    if (lane == 0) issue(0);
+    float y = 0.f;
+    int u = 0;
+    for (; u < nun; ++u) {
+        const int q0 = u * chunk_w, wq = min(chunk_w, K - q0), nb = wq >> 5;
+        const int su = (s0 + u) % S;
+        if (!wait_bar(&rg.accb[u & 1], (acc_par >> (u & 1)) & 1u, ab)) break;
+        acc_par ^= 1u << (u & 1);
+        tc_fence_after();
+        // this row's scales: [row][block] fp16 after the unit's weights
+        uint32_t sc2[kUnitBlocksI8 / 2];
+        const uint32_t *sr = reinterpret_cast<const uint32_t *>(rg.ring + (size_t)su * SB + (size_t)rows_p * wq) +
+                             (size_t)min(tid, rows_p - 1) * (nb >> 1);
+#pragma unroll
+        for (int j = 0; j < kUnitBlocksI8 / 2; ++j) sc2[j] = 2 * j < nb ? sr[j] : 0u;
+        epi_sync();                                             // the stage is read
+        if (tid == 0) mbar_arrive(&rg.empty[su]);
+        if (lane == 0 && u + 1 < nun) issue(u + 1);
+        y += unit_i8_row(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8) + ((uint32_t)(warp * 32) << 16), sc2, nb,
+                         bsc + (q0 >> 5));
+        tc_fence_before();
+    }
+    rg.consumed += u;
+    rg.s = (s0 + u) % S;
+    rg.round = round0 + (s0 + u) / S;
+    rg.acc_par = acc_par;
+    return y;
+}
+
 // Per-step values every epilogue thread reads once (after the dependency on the previous step).
 struct StepState {
     unsigned long long epoch;
@@ -1256,59 +1312,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     for (int j = 0; j < 4; ++j) d[i][j] = 0.f;
                 float yrow = 0.f;                                   // int8: this thread's row of the pass
                 if (q8) {
-                    // int8 units on the 5th-generation tensor cores, pipelined: lane 0 of each warp
-                    // issues its share of unit u + 1's block MMAs (TMEM buffer (u + 1) & 1) while
-                    // every thread reads unit u's sums out of TMEM; a unit's stage is free once its
-                    // MMAs are done and its row scales are in registers.
-                    const int nun = (K + op.chunk_w - 1) / op.chunk_w;
-                    auto stage_of = [&](int u, int &su, uint32_t &par) {
-                        const int x = s + u;
-                        su = x % S;
-                        par = (uint32_t)(round + x / S) & 1u;
-                    };
-                    auto issue = [&](int u) {                       // lane 0 of each compute warp
-                        int su;
-                        uint32_t par;
-                        stage_of(u, su, par);
-                        if (!wait_bar(&full[su], par, ab)) return;
-                        tc_fence_after();
-                        const int q0 = u * op.chunk_w;
-                        unit_i8_issue(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8), smem_u32(ring + (size_t)su * SB),
-                                      rows_p, min(op.chunk_w, K - q0) >> 5, smem_u32(dg) + (uint32_t)((q0 >> 5) * 128),
-                                      warp);
-                        mma_commit(&s_accb[u & 1]);
-                    };
-                    if (lane == 0) issue(0);
-                    int u = 0;
-                    for (; u < nun; ++u) {
-                        const int q0 = u * op.chunk_w, wq = min(op.chunk_w, K - q0), nb = wq >> 5;
-                        int su;
-                        uint32_t par;
-                        stage_of(u, su, par);
-                        if (!wait_bar(&s_accb[u & 1], (acc_par >> (u & 1)) & 1u, ab)) break;
-                        acc_par ^= 1u << (u & 1);
-                        tc_fence_after();
-                        if (p0 == 0 && u == 0) {
-                            stamp(p.trace, k, C, c, 4);
-                            stamp_clk(p.trace, k, C, c, 2);
-                        }
-                        // this row's scales: [row][block] fp16 after the unit's weights
-                        uint32_t sc2[kUnitBlocksI8 / 2];
-                        const uint32_t *sr = reinterpret_cast<const uint32_t *>(ring + (size_t)su * SB + (size_t)rows_p * wq) +
-                                             (size_t)min(tid, rows_p - 1) * (nb >> 1);
-#pragma unroll
-                        for (int j = 0; j < kUnitBlocksI8 / 2; ++j) sc2[j] = 2 * j < nb ? sr[j] : 0u;
-                        epi_sync();                                 // the stage is read
-                        if (tid == 0) mbar_arrive(&empty[su]);
-                        if (lane == 0 && u + 1 < nun) issue(u + 1);
-                        yrow += unit_i8_row(tmem + (uint32_t)((u & 1) * 8 * kUnitBlocksI8) + ((uint32_t)(warp * 32) << 16),
-                                            sc2, nb, bsc + (q0 >> 5));
-                        tc_fence_before();
+                    I8Ring rg{ring, full, empty, s_accb, S, SB, s, round, consumed, acc_par};
+                    if (p0 == 0) {
+                        stamp(p.trace, k, C, c, 4);
+                        stamp_clk(p.trace, k, C, c, 2);
                     }
-                    consumed += u;
-                    s += u;
-                    round += s / S;
-                    s %= S;
+                    yrow = i8_pass(rg, tmem, dg, bsc, rows_p, K, op.chunk_w, ab);
+                    s = rg.s;
+                    round = rg.round;
+                    consumed = rg.consumed;
+                    acc_par = rg.acc_par;
                 } else {
                 for (int q0 = 0; q0 < K; q0 += op.chunk_w) {
                     const int wq = min(op.chunk_w, K - q0);
