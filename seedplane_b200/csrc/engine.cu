@@ -145,7 +145,7 @@ struct sp_engine {
     PrefillScratch pf{};
     uint8_t *pf_mem = nullptr;
     size_t pf_bytes = 0;
-    const __half *head_rm = nullptr;        // row-major LM head (the embedding when tied)
+    PrefillMat head_pf{};                   // row-major LM head for the batched pass (the embedding when tied)
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
     int acc_vocab = 0;
@@ -596,7 +596,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
-    struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post, rqkv, ro, rgu, rdn; };
+    struct LOff { size_t qkv, o, gu, dn, qkv_b, inn, post, rqkv, ro, rgu, rdn, rqkv_lo, ro_lo, rgu_lo, rdn_lo; };
     std::vector<LOff> lo(c.layers);
     // packed matrix bytes: fp16 sizes are multiples of 512 B (no gaps); int8 ones of 32 B
     auto mbytes = [&](const StepOp &o, size_t N, size_t K) { return e->step_kernel ? step_gemv_bytes(o) : N * K * 2; };
@@ -616,18 +616,27 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         lo[l].inn = take(H * 4);
         lo[l].post = take(H * 4);
     }
-    // row-major copies for the batched prompt pass
-    // (int8 prompts and tree verifies run through the step kernel)
-    e->prefill = !i8 && !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
-    size_t o_head_rm = 0;
+    // row-major copies for the batched prompt pass: the fp16 weights, or for int8 checkpoints the
+    // dequantized weights times a power of two as exact fp16 hi / lo halves (4 bytes a weight)
+    e->prefill = !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
+    size_t o_head_rm = 0, o_head_rm_lo = 0;
     if (e->prefill) {
         for (int l = 0; l < c.layers; ++l) {
             lo[l].rqkv = take(QR * H * 2);
             lo[l].ro = take(H * (size_t)c.heads * HD * 2);
             lo[l].rgu = take(2 * I * H * 2);
             lo[l].rdn = take(H * I * 2);
+            if (i8) {
+                lo[l].rqkv_lo = take(QR * H * 2);
+                lo[l].ro_lo = take(H * (size_t)c.heads * HD * 2);
+                lo[l].rgu_lo = take(2 * I * H * 2);
+                lo[l].rdn_lo = take(H * I * 2);
+            }
         }
-        if (!c.tied_embeddings) o_head_rm = take(V * H * 2);
+        if (!c.tied_embeddings) {
+            o_head_rm = take(V * H * 2);
+            if (i8) o_head_rm_lo = take(V * H * 2);
+        }
     }
     e->arena_bytes = off;
     cudaError_t ce = cudaMalloc(&e->arena, e->arena_bytes);
@@ -638,7 +647,14 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     uint8_t *A = e->arena;
     cudaStream_t s = nullptr;
     int *d_idx = nullptr;
-    auto bail = [&](int code) { cudaFree(d_idx); if (s) cudaStreamDestroy(s); sp_engine_destroy(e); return code; };
+    float *d_absmax = nullptr;
+    auto bail = [&](int code) {
+        cudaFree(d_idx);
+        cudaFree(d_absmax);
+        if (s) cudaStreamDestroy(s);
+        sp_engine_destroy(e);
+        return code;
+    };
 #define SP_TRY(call)                                                                                 \
     do {                                                                                             \
         cudaError_t e_ = (call);                                                                     \
@@ -685,8 +701,41 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     };
     SP_TRY(pack(A + o_head, head_src, c.tied_embeddings ? nullptr : w->lm_head_s, (int)V, nullptr, nullptr,
                 d_head_rows, (int)VP, (int)H, e->s_head));
-    if (e->prefill && !c.tied_embeddings)
-        SP_TRY(cudaMemcpyAsync(A + o_head_rm, w->lm_head, V * H * 2, cudaMemcpyDeviceToDevice, s));
+    // int8 row-major copies: exponent k per matrix so that its largest weight times 2^k is near 2^15
+    // (fp16 range, and the lo halves of the large weights stay normal); one alpha = 2^-k per matrix
+    auto dequant = [&](size_t hi_off, size_t lo_off, const void *q1, const void *s1, int rows1, const void *q2,
+                       const void *s2, int rows2, int K, PrefillMat &m) -> cudaError_t {
+        float mx = 0.f, mx2 = 0.f;
+        cudaError_t er = launch_int8_absmax(d_absmax, (const __half *)s1, (long long)rows1 * (K / 32), s);
+        if (er == cudaSuccess) er = cudaMemcpyAsync(&mx, d_absmax, 4, cudaMemcpyDeviceToHost, s);
+        if (er == cudaSuccess && q2) er = launch_int8_absmax(d_absmax, (const __half *)s2, (long long)rows2 * (K / 32), s);
+        if (er == cudaSuccess && q2) er = cudaMemcpyAsync(&mx2, d_absmax, 4, cudaMemcpyDeviceToHost, s);
+        if (er == cudaSuccess) er = cudaStreamSynchronize(s);
+        if (er != cudaSuccess) return er;
+        mx = std::max(mx, mx2);
+        int k = 0;
+        if (mx > 0.f && std::isfinite(mx)) k = std::min(30, std::max(-30, (int)std::floor(std::log2(32768.0 / mx))));
+        __half *hi = (__half *)(A + hi_off), *lw = (__half *)(A + lo_off);
+        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, s);
+        if (er == cudaSuccess && q2)
+            er = launch_dequant_hilo(hi + (size_t)rows1 * K, lw + (size_t)rows1 * K, (const int8_t *)q2,
+                                     (const __half *)s2, rows2, K, k, s);
+        m.hi = hi;
+        m.lo = lw;
+        m.alpha = ldexpf(1.0f, -k);
+        return er;
+    };
+    if (e->prefill && i8) SP_TRY(cudaMalloc(&d_absmax, sizeof(float)));
+    PrefillMat head_pf{c.tied_embeddings ? (const __half *)w->embed : nullptr, nullptr, 1.0f};
+    if (e->prefill && !c.tied_embeddings) {
+        if (i8) {
+            SP_TRY(dequant(o_head_rm, o_head_rm_lo, w->lm_head, w->lm_head_s, (int)V, nullptr, nullptr, 0, (int)H,
+                           head_pf));
+        } else {
+            SP_TRY(cudaMemcpyAsync(A + o_head_rm, w->lm_head, V * H * 2, cudaMemcpyDeviceToDevice, s));
+            head_pf.hi = (const __half *)(A + o_head_rm);
+        }
+    }
     SP_TRY(cudaMemcpyAsync(A + o_fnorm, w->final_norm, H * 4, cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.layers; ++l) {
         const sp_layer_weights &Lw = w->layers[l];
@@ -697,14 +746,25 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(cudaMemcpyAsync(A + lo[l].qkv_b, Lw.qkv_b, QR * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].inn, Lw.in_norm, H * 4, cudaMemcpyDeviceToDevice, s));
         SP_TRY(cudaMemcpyAsync(A + lo[l].post, Lw.post_norm, H * 4, cudaMemcpyDeviceToDevice, s));
-        if (e->prefill) {
+        LayerDev L;
+        if (e->prefill && i8) {
+            const int A_ = c.heads * (int)HD;
+            SP_TRY(dequant(lo[l].rqkv, lo[l].rqkv_lo, Lw.qkv_w, Lw.qkv_s, (int)QR, nullptr, nullptr, 0, (int)H, L.pf.qkv));
+            SP_TRY(dequant(lo[l].ro, lo[l].ro_lo, Lw.o_w, Lw.o_s, (int)H, nullptr, nullptr, 0, A_, L.pf.o));
+            SP_TRY(dequant(lo[l].rgu, lo[l].rgu_lo, Lw.gate_w, Lw.gate_s, (int)I, Lw.up_w, Lw.up_s, (int)I, (int)H,
+                           L.pf.gate_up));
+            SP_TRY(dequant(lo[l].rdn, lo[l].rdn_lo, Lw.down_w, Lw.down_s, (int)H, nullptr, nullptr, 0, (int)I, L.pf.down));
+        } else if (e->prefill) {
             SP_TRY(cudaMemcpyAsync(A + lo[l].rqkv, Lw.qkv_w, QR * H * 2, cudaMemcpyDeviceToDevice, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].ro, Lw.o_w, H * (size_t)c.heads * HD * 2, cudaMemcpyDeviceToDevice, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].rgu, Lw.gate_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].rgu + I * H * 2, Lw.up_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].rdn, Lw.down_w, H * I * 2, cudaMemcpyDeviceToDevice, s));
+            L.pf.qkv = PrefillMat{(const __half *)(A + lo[l].rqkv), nullptr, 1.0f};
+            L.pf.o = PrefillMat{(const __half *)(A + lo[l].ro), nullptr, 1.0f};
+            L.pf.gate_up = PrefillMat{(const __half *)(A + lo[l].rgu), nullptr, 1.0f};
+            L.pf.down = PrefillMat{(const __half *)(A + lo[l].rdn), nullptr, 1.0f};
         }
-        LayerDev L;
         L.qkv = A + lo[l].qkv;
         L.o = A + lo[l].o;
         L.gate_up = A + lo[l].gu;
@@ -717,10 +777,6 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         L.off_gu = lo[l].gu;
         L.off_dn = lo[l].dn;
         if (e->prefill) {
-            L.pf.qkv = (const __half *)(A + lo[l].rqkv);
-            L.pf.o = (const __half *)(A + lo[l].ro);
-            L.pf.gate_up = (const __half *)(A + lo[l].rgu);
-            L.pf.down = (const __half *)(A + lo[l].rdn);
             L.pf.qkv_b = L.qkv_b;
             L.pf.in_norm = L.in_norm;
             L.pf.post_norm = L.post_norm;
@@ -747,6 +803,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     SP_TRY(cudaStreamSynchronize(s));
     cudaFree(d_idx);
     d_idx = nullptr;
+    cudaFree(d_absmax);
+    d_absmax = nullptr;
     e->stream = A;
     e->stream_bytes = stream_end;
     e->embed = (const __half *)(A + o_embed);
@@ -754,7 +812,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->off_head = o_head;
     e->final_norm = (const float *)(A + o_fnorm);
     e->rope = (const float *)(A + o_rope);
-    e->head_rm = c.tied_embeddings ? e->embed : (const __half *)(A + o_head_rm);
+    e->head_pf = head_pf;
+    if (c.tied_embeddings) e->head_pf.hi = e->embed;
 
     // ---- GEMV plans -------------------------------------------------------------------------
     auto base = [&](size_t N, size_t K) {
@@ -1084,7 +1143,7 @@ static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const in
         for (int r0 = 0; r0 < T; r0 += kPrefillLogitRows) {
             const int rows = std::min(kPrefillLogitRows, T - r0);
             float *out = all_logits && logits ? logits + (size_t)(b0 + r0) * c.vocab : e->pf.logits;
-            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_rm, r0, rows, out, e->blas, s));
+            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_pf, r0, rows, out, e->blas, s));
             SP_CUDA(launch_argmax_rows(out, rows, c.vocab, c.vocab, argmax + b0 + r0, e->am, s));
             if (!all_logits && logits && b0 + r0 + rows == n)
                 SP_CUDA(cudaMemcpyAsync(logits, out + (size_t)(rows - 1) * c.vocab, (size_t)c.vocab * 4,

@@ -264,13 +264,24 @@ struct PrefillDims {
     int hidden, inter, heads, kv_heads, head_dim, vocab, max_pos, max_tokens;
     float eps;
 };
-struct PrefillLayer {                    // row-major fp16 weights
-    const __half *qkv;                   // [(heads + 2 kv_heads) * head_dim, hidden], natural row order
-    const __half *o;                     // [hidden, heads * head_dim]
-    const __half *gate_up;               // [2 inter, hidden]: gate rows, then up rows
-    const __half *down;                  // [hidden, inter]
+struct PrefillMat {                      // row-major fp16 weights W = alpha * (hi + lo)
+    const __half *hi;                    // fp16 checkpoints: the weights (alpha 1, no lo)
+    const __half *lo;                    // int8 checkpoints: the dequantized weights times 2^k split in two
+    float alpha;                         // fp16 halves (exact: q * scale has at most 19 significant bits)
+};
+struct PrefillLayer {
+    PrefillMat qkv;                      // [(heads + 2 kv_heads) * head_dim, hidden], natural row order
+    PrefillMat o;                        // [hidden, heads * head_dim]
+    PrefillMat gate_up;                  // [2 inter, hidden]: gate rows, then up rows
+    PrefillMat down;                     // [hidden, inter]
     const float *qkv_b, *in_norm, *post_norm;
 };
+// Dequantize blockwise int8 rows (q [rows][K], fp16 scales [rows][K / 32]) into fp16 hi / lo halves
+// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi).
+cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
+                                cudaStream_t s);
+// Largest |scale| * 127 of a blockwise-int8 matrix (n fp16 scales), into *out (device float).
+cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cudaStream_t s);
 struct PrefillScratch {
     float *x;                            // [T, hidden] residual stream
     __half *xh, *xl;                     // GEMM inputs [2T, K]: hi rows then lo rows (xl unused)
@@ -297,7 +308,7 @@ cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L
                                      void *cublas, cudaStream_t stream);
 // final RMSNorm of rows [r0, r0 + n) and the head GEMM into out [n, vocab]
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
-                                  const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream);
+                                  const PrefillMat &head, int r0, int n, float *out, void *cublas, cudaStream_t stream);
 
 // Per-row top-k (k <= kTopkMax; larger value first, lower index on ties) and log-sum-exp of fp32
 // logits (sample.cu): idx / val [rows][k], lse [rows].

@@ -246,22 +246,66 @@ __global__ void k_resid_add(float *x, const float *y, int T, int H) {
         x[(size_t)t * H + j] += y[(size_t)t * H + j] + y[(size_t)(T + t) * H + j];
 }
 
-// Y2[2T, N] (row-major) = W[N, K] (row-major) . X2[2T, K]^T, X2 = [hi rows; lo rows]: one GEMM
-cublasStatus_t gemm_stacked(cublasHandle_t hb, const __half *w, int N, int K, const __half *x2, int T, float *y2) {
-    const float one = 1.0f, zero = 0.0f;
-    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &one, w, CUDA_R_16F, K, x2, CUDA_R_16F, K, &zero,
-                        y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+// Y2[2T, N] (row-major) = W[N, K] (row-major) . X2[2T, K]^T, X2 = [hi rows; lo rows]: one GEMM per
+// weight half (W = alpha (hi + lo); fp16 checkpoints have no lo half)
+cublasStatus_t gemm_stacked(cublasHandle_t hb, const PrefillMat &w, int N, int K, const __half *x2, int T, float *y2) {
+    const float zero = 0.0f, one = 1.0f;
+    cublasStatus_t st = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &w.alpha, w.hi, CUDA_R_16F, K, x2,
+                                     CUDA_R_16F, K, &zero, y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    if (st != CUBLAS_STATUS_SUCCESS || w.lo == nullptr) return st;
+    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &w.alpha, w.lo, CUDA_R_16F, K, x2, CUDA_R_16F, K,
+                        &one, y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
-// Y[T, N] (row-major, ldy) = beta * Y + W[N, K] (row-major) . (Xh + Xl)[T, K]^T, in two GEMMs
-cublasStatus_t gemm_hilo(cublasHandle_t hb, const __half *w, int N, int K, const __half *xh, const __half *xl, int T,
+// Y[T, N] (row-major, ldy) = beta * Y + W[N, K] (row-major) . (Xh + Xl)[T, K]^T, one GEMM per input
+// half and weight half
+cublasStatus_t gemm_hilo(cublasHandle_t hb, const PrefillMat &w, int N, int K, const __half *xh, const __half *xl, int T,
                          float *y, int ldy, float beta) {
     const float one = 1.0f;
-    cublasStatus_t s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16F, K, xh, CUDA_R_16F, K,
-                                    &beta, y, CUDA_R_32F, ldy, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    if (s != CUBLAS_STATUS_SUCCESS) return s;
-    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16F, K, xl, CUDA_R_16F, K, &one, y,
-                        CUDA_R_32F, ldy, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    const __half *wh[2] = {w.hi, w.lo};
+    const __half *xs[2] = {xh, xl};
+    bool first = true;
+    for (int i = 0; i < 2; ++i) {
+        if (wh[i] == nullptr) continue;
+        for (int j = 0; j < 2; ++j) {
+            cublasStatus_t st = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &w.alpha, wh[i], CUDA_R_16F, K,
+                                             xs[j], CUDA_R_16F, K, first ? &beta : &one, y, CUDA_R_32F, ldy,
+                                             CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+            if (st != CUBLAS_STATUS_SUCCESS) return st;
+            first = false;
+        }
+    }
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+// w = q * scale (exact in fp32), times 2^k (exact), split into fp16 hi = fp16(w') and lo =
+// fp16(w' - hi): hi + lo = w' exactly while w' and its remainder stay in fp16's normal range, which
+// the caller's k arranges for the matrix's largest weights. One thread per 8 inputs of a row.
+__global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, float p2) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)rows * (K / 8)) return;
+    const long long e0 = idx * 8;
+    const float sc = __half2float(scales[e0 / 32]) * p2;
+    const uint2 raw = *reinterpret_cast<const uint2 *>(q + e0);
+    const int8_t *b = reinterpret_cast<const int8_t *>(&raw);
+    __align__(16) __half h[8], l[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float w = (float)b[j] * sc;
+        h[j] = __float2half_rn(w);
+        l[j] = __float2half_rn(w - __half2float(h[j]));
+    }
+    *reinterpret_cast<uint4 *>(hi + e0) = *reinterpret_cast<const uint4 *>(h);
+    *reinterpret_cast<uint4 *>(lo + e0) = *reinterpret_cast<const uint4 *>(l);
+}
+
+// max |scale| over n fp16 scales, times 127, into *out (non-negative floats compare as unsigned)
+__global__ void k_int8_absmax(float *out, const __half *scales, long long n) {
+    float m = 0.f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(__half2float(scales[i])));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned *>(out), __float_as_uint(m * 127.0f));
 }
 
 }  // namespace
@@ -338,7 +382,7 @@ cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, 
 // Logits of rows [r0, r0 + n) of the chunk (n <= kPrefillLogitRows) into `out` (row stride vocab):
 // final RMSNorm, then the head GEMM.
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
-                                  const __half *head, int r0, int n, float *out, void *cublas, cudaStream_t stream) {
+                                  const PrefillMat &head, int r0, int n, float *out, void *cublas, cudaStream_t stream) {
     cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
     const int H = d.hidden;
     k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)n * H, s.x + (size_t)r0 * H, final_norm, H,
@@ -351,6 +395,21 @@ cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s,
                CUBLAS_STATUS_SUCCESS) {
         return cudaErrorUnknown;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
+                                cudaStream_t s) {
+    if (K % 32 || k < -30 || k > 30) return cudaErrorInvalidValue;
+    const long long n = (long long)rows * (K / 8);
+    k_dequant_hilo<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(hi, lo, q, scales, rows, K, ldexpf(1.0f, k));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float), s);
+    if (e != cudaSuccess) return e;
+    k_int8_absmax<<<256, 256, 0, s>>>(out, scales, n);
     return cudaGetLastError();
 }
 

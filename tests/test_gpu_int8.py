@@ -6,8 +6,9 @@ at cache write as the engine stores them. Bars: greedy tokens identical; logits 
 the largest |logit| (fp16 hi/lo activations and fp32 block sums against an fp32 matvec).
 
 The tied tiny models mix formats (int8 layers, fp16 embedding as the LM head); the untied one
-streams an int8 LM head too. Prompts and tree verifies of int8 checkpoints run through the step
-kernel (the batched prompt pass is fp16 only).
+streams an int8 LM head too. Prompts of 8 or more tokens and tree verifies go through the batched
+pass, whose GEMMs use exact fp16 hi / lo halves of the dequantized weights; shorter prompts, decode
+and `SEEDPLANE_PREFILL=steps` go through the step kernel's int8 units.
 """
 import numpy as np
 import pytest
@@ -109,3 +110,23 @@ def test_int8_qwen2_0_5b_shape_greedy():
     d = next((i for i, (x, y) in enumerate(zip(got, want)) if x != y), None)
     assert d is None, f"first divergence at {d}: margin there {margins[d]:.5f}"
 
+
+
+def test_int8_prompt_through_step_kernel_matches_batched(monkeypatch):
+    """The same prompt through the step kernel (one launch per token) and through the batched pass."""
+    from seedplane_b200.engine import CudaQwen2
+    cfg = PRESETS["tiny-untied"]
+    w = make_int8_blockwise(cfg, seed=3, std=0.1)
+    prompt = random_prompt(cfg.vocab, 11, seed=2)
+    eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
+    kv = eng.new_kv(32)
+    batched, _ = eng.forward(kv, prompt, all_logits=True)
+    eng.close()
+    monkeypatch.setenv("SEEDPLANE_PREFILL", "steps")
+    eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
+    kv = eng.new_kv(32)
+    stepped, _ = eng.forward(kv, prompt, all_logits=True)
+    eng.close()
+    want, _ = OracleQwen2(cfg, w, kv_fp16=True).forward(prompt, None, all_logits=True)
+    assert_logits_close(batched, want)
+    assert_logits_close(stepped, want)
