@@ -164,22 +164,23 @@ SP_DEVINL void digitize4(float4 x, int k, int8_t *dg, float *bsc) {
     *reinterpret_cast<uint32_t *>(w + 48) = __byte_perm(t0, t2, 0x5410);
 }
 
-// The MMAs of one int8 unit (one thread). A unit of rows_p rows x 32 nb inputs holds, per 32-input
+// The MMAs of one int8 unit. A unit of rows_p rows x 32 nb inputs holds, per 32-input
 // block b, the rows' 32 bytes as two K-major halves: [half][row][16 bytes] (rows at 16 B, 8-row
 // core groups 128 B apart, halves rows_p * 16 B apart; no padding rows: the rows past rows_p of the
-// M = 128 tile read whatever follows and land in TMEM lanes nobody reads), then the scales
-// [row][block] fp16. Block b: D (TMEM columns 8b .. 8b + 7) = A (128 x 32 s8) * B (the 8-row digit
-// cores of the same 32 inputs), exact s32, not accumulated: every block keeps its own sums.
-// Issued by lane 0 of each compute warp w for blocks w, w + 4, ... (the tensor core takes one such
-// MMA per ~45 cycles whatever the row count; four issuers keep it fed), descriptors advanced in
-// place.
+// M = 64 or 128 tile read whatever follows and land in TMEM lanes nobody reads), then the scales
+// [row][block] fp16. Block b: D (TMEM columns 8b .. 8b + 7) = A (M x 32 s8) * B (the 8-row digit
+// cores of the same 32 inputs), exact s32, not accumulated: every block keeps its own sums. M = 64
+// for passes of at most 64 rows (~32 cycles of tensor core per MMA, ~48 for M = 128, whatever the
+// row count). Issued by lane 0 of each compute warp w for blocks w, w + 4, ... (four issuers keep
+// the tensor core fed), descriptors advanced in place.
 SP_DEVINL void unit_i8_issue(uint32_t tmem, uint32_t unit, int rows_p, int nb, uint32_t dgb, int b0) {
+    const uint32_t idesc = rows_p <= 64 ? kIdescI8M64N8 : kIdescI8M128N8;
     uint64_t ad = smem_desc(unit + (uint32_t)(b0 * rows_p * 32), (uint32_t)(rows_p * 16), 128);
     uint64_t bd = smem_desc(dgb + (uint32_t)(b0 * 128), 64, 128);
     const uint64_t da = (uint64_t)((4 * rows_p * 32) >> 4), db = (uint64_t)((4 * 128) >> 4);
     uint32_t t = tmem + (uint32_t)(8 * b0);
     for (int b = b0; b < nb; b += 4) {
-        mma_i8(t, ad, bd);
+        mma_i8(t, ad, bd, idesc);
         ad += da;                                           // start-address field (bits 0-13) only
         bd += db;
         t += 32;
@@ -557,6 +558,9 @@ SP_DEVINL void stamp_clk(unsigned long long *tr, int k, int C, int c, int i) {
 // (u + 1) & 1) while every thread reads unit u's sums out of TMEM; a unit's stage goes back to the
 // producer once its MMAs are done and its row scales are in registers. Out of line: the loop gets
 // its own register budget instead of the step kernel's. Returns this thread's row sum.
+SP_DEVINL int i8_row_of_thread(int rows_p, int tid) {
+    return rows_p <= 64 ? ((tid & 31) < 16 ? 16 * (tid >> 5) + (tid & 31) : -1) : tid;
+}
 struct I8Ring {
     uint8_t *ring;
     uint64_t *full, *empty, *accb;
@@ -567,6 +571,9 @@ struct I8Ring {
 __device__ __noinline__ float i8_pass(I8Ring &rg, uint32_t tmem, const int8_t *dg, const float *bsc, int rows_p, int K,
                                       int chunk_w, const Abort ab) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // this thread's row (its TMEM lane): M = 128 tiles put row r at lane r, M = 64 tiles (passes of
+    // at most 64 rows) at lane r % 16 + 32 (r / 16)
+    const int row = i8_row_of_thread(rows_p, tid);
     const int S = rg.S, SB = rg.SB, s0 = rg.s, round0 = rg.round;
     uint32_t acc_par = rg.acc_par;
     const int nun = (K + chunk_w - 1) / chunk_w;
@@ -591,7 +598,7 @@ __device__ __noinline__ float i8_pass(I8Ring &rg, uint32_t tmem, const int8_t *d
         // this row's scales: [row][block] fp16 after the unit's weights
         uint32_t sc2[kUnitBlocksI8 / 2];
         const uint32_t *sr = reinterpret_cast<const uint32_t *>(rg.ring + (size_t)su * SB + (size_t)rows_p * wq) +
-                             (size_t)min(tid, rows_p - 1) * (nb >> 1);
+                             (size_t)max(0, min(row, rows_p - 1)) * (nb >> 1);
 #pragma unroll
         for (int j = 0; j < kUnitBlocksI8 / 2; ++j) sc2[j] = 2 * j < nb ? sr[j] : 0u;
         epi_sync();                                             // the stage is read
@@ -1349,7 +1356,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 // row sums: lanes 4i hold rows i and i + 8 of each tile (columns 0 = hi, 1 = lo);
                 // tile rt's U accumulator slots are summed in slot order
                 if (q8) {
-                    if (tid < rows_p) (&red[0][0])[tid] = yrow;     // row tid of the pass (<= 128 rows)
+                    const int r8 = i8_row_of_thread(rows_p, tid);    // this thread's row (<= 128 rows)
+                    if (r8 >= 0 && r8 < rows_p) (&red[0][0])[r8] = yrow;
                 } else if ((lane & 3) == 0) {
                     if (nrt == 1)
                         rows_from_acc<4>(d, red[warp], nrt, lane);

@@ -76,14 +76,16 @@ SP_DEVINL void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
 SP_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---- kind::i8 (the step kernel's int8 units) ---------------------------------------------------
-// D s32, A and B signed 8-bit, both K-major, M = 128, N = 8; one MMA covers K = 32 (32 bytes a row).
+// D s32, A and B signed 8-bit, both K-major, N = 8; one MMA covers K = 32 (32 bytes a row).
+// M = 64 (rows r at TMEM lanes r % 16 + 32 (r / 16)) costs about two thirds of M = 128 per MMA.
 constexpr uint32_t kIdescI8M128N8 = (2u << 4) | (1u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescI8M64N8 = (2u << 4) | (1u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((64u >> 4) << 24);
 
-SP_DEVINL void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
+SP_DEVINL void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc = kIdescI8M128N8) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdescI8M128N8), "r"(0u));
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0u));
 }
 // 4 consecutive TMEM columns of this thread's lane (no wait).
 SP_DEVINL void tmem_ld4_nowait(uint32_t taddr, uint32_t (&r)[4]) {
