@@ -1045,26 +1045,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             const uint64_t pol = policy_evict_first();
             UnitCursor ic{p.ops, p.n_ops, c};
             ic.seek(0);
-            UnitCursor pc = ic;
-            int pc_idx = 0;                     // units the prefetch cursor has passed
-            uint32_t ahead = 0;                 // bytes prefetched beyond the issue point
+            // the warm-ahead cursor walks the same units on its own; pf_pos / is_pos are the bytes
+            // of the CTA's stream it has passed / that have been issued
+            UnitCursor pc{p.ops, p.n_ops, c};
+            pc.seek(0);
+            unsigned long long pf_pos = 0, is_pos = 0;
             bool pf_more = p.l2_ahead > 0;
             const uint8_t *u;
             uint32_t nb;
             while (!ab.on() && ic.next(u, nb)) {
-                if (pc_idx <= issued) {         // the prefetch cursor restarts right after this unit
-                    pc = ic;
-                    pc_idx = issued + 1;
-                    ahead = 0;
-                } else {
-                    ahead -= nb;                // this unit was prefetched
-                }
+                is_pos += nb;
                 if (round > 0) {
                     const uint32_t par = (uint32_t)(round - 1) & 1u;
                     bool ok = false;
                     for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
-                        // with prefetch budget left, probe without blocking and prefetch in between
-                        const bool pf = pf_more && ahead < (uint32_t)p.l2_ahead;
+                        // with warm-ahead budget left, probe without blocking and prefetch in between
+                        const bool pf = pf_more && pf_pos < is_pos + (unsigned long long)p.l2_ahead;
                         if (pf ? mbar_test_wait(&empty[s], par) : mbar_try_wait(&empty[s], par)) {
                             ok = true;
                             break;
@@ -1073,9 +1069,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                             const uint8_t *pu;
                             uint32_t pnb;
                             if (pc.next(pu, pnb)) {
-                                prefetch_l2(pu, pnb);
-                                ahead += pnb;
-                                ++pc_idx;
+                                if (pf_pos >= is_pos) prefetch_l2(pu, pnb);     // units not issued yet only
+                                pf_pos += pnb;
                             } else {
                                 pf_more = false;
                             }
