@@ -62,6 +62,7 @@ constexpr int kMergeBatch = 32;            // attention chunks merged per batch 
 constexpr uint32_t kDepSpinLimit = 1u << 22;
 constexpr int kOpWords = (int)(sizeof(StepOp) / 16);
 static_assert(kLLBatch <= 32, "poll masks are 32-bit");
+static_assert(kStepAttnRows <= kEpiThreads - 32, "attention scores run on threads 32 ..");
 
 SP_DEVINL void ldmatrix_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -526,6 +527,22 @@ SP_DEVINL void stage_rows(uint8_t *am, const __half *kb, const __half *vb, int b
     }
 }
 
+// The K (V = false, chunks XOR-permuted by row like stage_rows) or V rows [lo, hi) of a sub-chunk
+// starting at position `base`, with cp.async.
+template <int HD, bool V>
+SP_DEVINL void stage_half(uint8_t *am, const __half *src, int base, int lo, int hi, int tid) {
+    using L = AttnRegion<HD>;
+    constexpr int kChunks = HD / 8;
+    for (int i = tid; i < (hi - lo) * kChunks; i += kEpiThreads) {
+        const int j = lo + i / kChunks, ch = i % kChunks;
+        if (V)
+            cp_async16(am + L::vOff + (size_t)(j - base) * L::kRow + ch * 16, src + (size_t)j * HD + ch * 8);
+        else
+            cp_async16(am + L::kOff + (size_t)(j - base) * L::kRow + (ch ^ ((j - base) & 7)) * 16, src + (size_t)j * HD + ch * 8);
+    }
+}
+SP_DEVINL void cp_async_wait_but1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 template <int DL>
 SP_DEVINL void load_dims(const uint8_t *q, float (&f)[DL]) {
     if constexpr (DL == 4) {
@@ -639,8 +656,8 @@ __device__ void attn_prestage(const StepParams &p, const StepOp &qkv, const Step
 }
 
 // One q head over one chunk of the context, in sub-chunks of up to kStepAttnRows positions:
-//   scores  warp = position (four in flight), lane = HD/32 dims, q in registers, warp sum
-//   softmax one warp, running max / sum across sub-chunks (fp32)
+//   scores  thread 32 + t = position t, a full HD-dim dot product against q in shared memory
+//   softmax warp 1, running max / sum across sub-chunks (fp32)
 //   values  warp = every fourth position, lane = HD/32 dims; the four warps' sums meet in shared
 //           memory and thread t < HD keeps output dim t
 // Publishes the chunk's unnormalised partial (max, sum, acc[HD]) as LL words.
@@ -661,14 +678,33 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     __shared__ float s_corr;
     const int slot = ss.slot;
     const int s1 = min(j1, j0 + kStepAttnRows);
+    // the step's own position (the last of the context) is the one K / V row this step writes: it
+    // comes from the QKV projection's LL words (thread t < HD / 2 holds one pair of each), never
+    // from the cache, wherever it falls in the chunk
+    const bool has_slot = slot >= j0 && slot < j1;
+    uint32_t kvw[2] = {0u, 0u};
+    auto put_slot = [&](int base) {
+        if (tid < HD / 2) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int i = 2 * tid + e, which = i / (HD / 2), dd = i - which * (HD / 2);
+                const int r = slot - base;
+                __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)r * L::kRow);
+                // dims dd and dd + HD/2; K chunks permuted like stage_rows'
+                const int d0 = which ? dd : ((((dd >> 3) ^ (r & 7)) << 3) | (dd & 7));
+                const int d1 = which ? dd + HD / 2 : (((((dd + HD / 2) >> 3) ^ (r & 7)) << 3) | (dd & 7));
+                row[d0] = __ushort_as_half((unsigned short)(kvw[e] & 0xffffu));
+                row[d1] = __ushort_as_half((unsigned short)(kvw[e] >> 16));
+            }
+        }
+    };
     {
-        // q of the head and, when the first sub-chunk holds the step's position, its new K / V
-        // row: LL words of the QKV projection (thread t < HD / 2: one pair of each)
+        // q of the head and, when the chunk holds the step's position, its new K / V row
         const bool cur = slot >= j0 && slot < s1;
         const uint64_t *qw = op.lin + (size_t)h * HD + 2 * tid;
         const uint64_t *kw = op.lkv + (size_t)g * HD + 2 * tid;
         uint64_t w[2][2];
-        const uint32_t valid = tid < HD / 2 ? (cur ? 3u : 1u) : 0u;
+        const uint32_t valid = tid < HD / 2 ? (has_slot ? 3u : 1u) : 0u;
         stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 0);
         ll_poll<2>(w, valid, [&](int j) { return j == 0 ? qw : kw; }, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
         stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
@@ -676,21 +712,10 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
         if (tid < HD / 2) {
             qs[2 * tid] = ll_f(w[0][0]);
             qs[2 * tid + 1] = ll_f(w[0][1]);
-            if (cur) {
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int i = 2 * tid + e, which = i / (HD / 2), dd = i - which * (HD / 2);
-                    const int r = slot - j0;
-                    __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)r * L::kRow);
-                    const uint32_t u = (uint32_t)w[1][e];
-                    // dims dd and dd + HD/2; K chunks permuted like stage_rows'
-                    const int d0 = which ? dd : ((((dd >> 3) ^ (r & 7)) << 3) | (dd & 7));
-                    const int d1 = which ? dd + HD / 2 : (((((dd + HD / 2) >> 3) ^ (r & 7)) << 3) | (dd & 7));
-                    row[d0] = __ushort_as_half((unsigned short)(u & 0xffffu));
-                    row[d1] = __ushort_as_half((unsigned short)(u >> 16));
-                }
-            }
+            kvw[0] = (uint32_t)w[1][0];
+            kvw[1] = (uint32_t)w[1][1];
         }
+        if (cur) put_slot(j0);
     }
     cp_async_wait_all();
     epi_sync();
@@ -701,27 +726,31 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     float qr[DL];
 #pragma unroll
     for (int i = 0; i < DL; ++i) qr[i] = qs[DL * lane + i];
-    float m_run = -INFINITY, l_run = 0.f;       // warp 0 (lane-uniform)
+    float m_run = -INFINITY, l_run = 0.f;       // warp 1 (lane-uniform)
     float acc = 0.f;                            // thread t < HD: output dim t
 
+    // Sub-chunks are pipelined: the next sub-chunk's K rows load while this one's softmax and
+    // values run, its V rows while its own scores run (cp.async groups complete in order).
     for (int a = j0; a < j1; a += kStepAttnRows) {
         const int b = min(j1, a + kStepAttnRows), nj = b - a;
+        const int a2 = b, b2 = min(j1, b + kStepAttnRows);  // the next sub-chunk (a2 < j1: exists)
         if (a != j0) {
-            epi_sync();                         // everyone is done with the previous sub-chunk
-            stage_rows<HD>(am, kb, vb, a, a, b, tid);
-            cp_async_commit();
-            cp_async_wait_all();
+            cp_async_wait_but1();               // K rows of [a, b) (its V rows may still load)
+            if (slot >= a && slot < b) put_slot(a);
             epi_sync();
         }
-        // scores: thread t = position t of the sub-chunk (nj <= kStepAttnRows <= kEpiThreads), a
-        // full dot product over HD dims: 16-byte K chunks (permuted by row, conflict-free) against
-        // q from shared memory (the same address in every lane: a broadcast). No shuffles.
-        if (tid < nj) {
-            const uint8_t *kr = am + L::kOff + (size_t)tid * L::kRow;
+        // scores: thread 32 + t = position t of the sub-chunk (nj <= kStepAttnRows <= 96), a full
+        // dot product over HD dims: 16-byte K chunks (permuted by row, conflict-free) against q from
+        // shared memory (the same address in every lane: a broadcast). No shuffles. Warps 1-3 do
+        // the scores and the softmax: warp 0 shares its scheduler with the producer warp, and the
+        // softmax ran ~5x slower there in some builds.
+        const int sp = tid - 32;
+        if (sp >= 0 && sp < nj) {
+            const uint8_t *kr = am + L::kOff + (size_t)sp * L::kRow;
             float sv = 0.f;
 #pragma unroll
             for (int c = 0; c < HD / 8; ++c) {
-                const uint4 kq = *reinterpret_cast<const uint4 *>(kr + ((c ^ (tid & 7)) << 4));
+                const uint4 kq = *reinterpret_cast<const uint4 *>(kr + ((c ^ (sp & 7)) << 4));
                 const float4 qa = *reinterpret_cast<const float4 *>(qs + 8 * c);
                 const float4 qb = *reinterpret_cast<const float4 *>(qs + 8 * c + 4);
                 const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.x));
@@ -737,16 +766,20 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
                 sv = fmaf(qb.z, k3.x, sv);
                 sv = fmaf(qb.w, k3.y, sv);
             }
-            const int jj = a + tid;
+            const int jj = a + sp;
             const bool vis = !(jj >= ss.tree_base && !((ss.mask >> (jj - ss.tree_base)) & 1ull));
-            sc[tid] = vis ? sv * p.scale : -INFINITY;
+            sc[sp] = vis ? sv * p.scale : -INFINITY;
         }
-        epi_sync();
+        epi_sync();                             // the K rows are free
+        if (a2 < j1) {
+            stage_half<HD, false>(am, kb, a2, a2, min(b2, slot), tid);
+            cp_async_commit();
+        }
         if (a == j0) {
             stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
             stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 3);
         }
-        if (warp == 0) {                        // softmax statistics over the sub-chunk
+        if (warp == 1) {                        // softmax statistics over the sub-chunk
             __syncwarp();
             const float v0 = lane < nj ? sc[lane] : -INFINITY;
             const float v1 = lane + 32 < nj ? sc[lane + 32] : -INFINITY;
@@ -760,6 +793,12 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
             if (lane < nj) sc[lane] = p0;
             if (lane + 32 < nj) sc[lane + 32] = p1;
             if (lane == 0) s_corr = corr;
+        }
+        if (a != j0) {                          // the V rows of [a, b)
+            if (a2 < j1)
+                cp_async_wait_but1();           // (the next K rows may still load)
+            else
+                cp_async_wait_all();
         }
         epi_sync();
         if (a == j0) stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 4);
@@ -777,7 +816,11 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
         }
 #pragma unroll
         for (int i = 0; i < DL; ++i) rd[warp * HD + DL * lane + i] = pa[i];
-        epi_sync();
+        epi_sync();                             // the V rows are free
+        if (a2 < j1) {
+            stage_half<HD, true>(am, vb, a2, a2, min(b2, slot), tid);
+            cp_async_commit();
+        }
         if (tid < HD) acc = fmaf(acc, s_corr, ((rd[tid] + rd[HD + tid]) + rd[2 * HD + tid]) + rd[3 * HD + tid]);
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
@@ -785,7 +828,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     uint64_t *pw = op.lpart + ((size_t)h * p.max_chunks + ch) * (HD + 2);
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
     if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc, tag));
-    if (tid == 0) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
+    if (tid == 32) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
 }
 
 // The chunk-0 item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
