@@ -117,7 +117,6 @@ struct sp_engine {
     StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (row blocks)
     StepLayout step_lay{};                  // shared memory of the step kernel
     int step_xmax = 0, step_max_chunks = 0;
-    int step_max_chunks_g = 0, step_part_chunks = 0, step_group_ctx = 1 << 30;
     int step_inflight = 0;                  // ring copies in flight at most (0: all stages)
     int step_l2_ahead = 0;                  // bytes per CTA prefetched into L2 ahead of the ring
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
@@ -218,7 +217,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const size_t H = c.hidden, I = c.intermediate, HD = c.head_dim;
     const size_t nq = (size_t)c.heads * HD, nkv = (size_t)c.kv_heads * HD;
-    const size_t npart = (size_t)c.heads * e->step_part_chunks * (HD + 2);
+    const size_t npart = (size_t)c.heads * e->step_max_chunks * (HD + 2);
     std::vector<StepOp> ops;
     auto gemv = [&](const StepOp &plan, const uint8_t *w, int pro, int epi) {
         StepOp o = plan;
@@ -334,9 +333,6 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.vocab = c.vocab;
         p.hidden = c.hidden;
         p.max_chunks = e->step_max_chunks;
-        p.max_chunks_g = e->step_max_chunks_g;
-        p.part_chunks = e->step_part_chunks;
-        p.group_ctx = e->step_group_ctx;
         p.evict_first = e->evict_first ? 1 : 0;
         p.max_inflight = e->step_inflight;
         p.l2_ahead = e->step_l2_ahead;
@@ -907,26 +903,16 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     auto wtake = [&](size_t bytes) { size_t o = woff; woff = align_up(woff + bytes, 256); return o; };
     // counters and split-strip state first: a device error clears exactly this prefix
     e->n_cnt = 5 * c.layers;
-    // attention chunks per head at most (SEEDPLANE_ATTN_MAX_CHUNKS lowers the cap: longer items,
+    // attention chunks per q head at most (SEEDPLANE_ATTN_MAX_CHUNKS lowers the cap: longer items,
     // e.g. to exercise many sub-chunks per item at small contexts)
     const int chunk_cap = (int)std::max(1L, env_long("SEEDPLANE_ATTN_MAX_CHUNKS", kStepMaxChunks));
     e->step_max_chunks = std::min({kStepMaxChunks, chunk_cap, e->num_sms / c.heads});
-    e->step_max_chunks_g = std::min({kStepMaxChunks, chunk_cap, e->num_sms / c.kv_heads});
-    e->step_part_chunks = std::max(e->step_max_chunks, e->step_max_chunks_g);
-    // grouped attention items (one kv head, all its q heads) from this context length on, when the
-    // attention region holds them
-    if (e->step_kernel) {
-        const long gc = env_long("SEEDPLANE_ATTN_GROUP_CTX", 1L << 30);
-        const bool fits = (size_t)e->step_lay.attn_off + step_attn_group_smem_bytes((int)HD, c.heads / c.kv_heads) <=
-                          (size_t)e->step_lay.vec_bytes;
-        e->step_group_ctx = fits ? (int)std::min<long>(std::max<long>(gc, 0), 1L << 30) : (1 << 30);
-    }
     const size_t w_cnt = wtake((size_t)e->n_cnt * 8), w_epoch = wtake(8);
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
     const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
     // step hand-off words (a step after a device error must not see tags of the failed one)
-    const size_t n_part = (size_t)c.heads * e->step_part_chunks * (HD + 2);
+    const size_t n_part = (size_t)c.heads * e->step_max_chunks * (HD + 2);
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
@@ -1016,11 +1002,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
                              c.heads));
         SP_TRY(prepare_step((int)HD, e->step_lay.smem, i8));
         if (env_flag("SEEDPLANE_VERBOSE", false))
-            fprintf(stderr,
-                    "[seedplane] step kernel: grid=%d stages=%d x %d B xmax=%d smem=%zu max_chunks=%d grouped "
-                    "attention: max_chunks=%d from ctx %d\n",
+            fprintf(stderr, "[seedplane] step kernel: grid=%d stages=%d x %d B xmax=%d smem=%zu max_chunks=%d\n",
                     e->num_sms, e->step_lay.stages, e->step_lay.stage_bytes, e->step_xmax, e->step_lay.smem,
-                    e->step_max_chunks, e->step_max_chunks_g, e->step_group_ctx);
+                    e->step_max_chunks);
     }
     for (const GemvParams *p : {&e->g_qkv, &e->g_o, &e->g_gu, &e->g_down, &e->g_head})
         if (!e->tc && gemv_smem_bytes(*p) > 227 * 1024) return bail(fail(SP_ERR_UNSUPPORTED, "GEMV needs %zu bytes of shared memory", gemv_smem_bytes(*p)));

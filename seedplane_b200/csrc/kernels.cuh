@@ -212,9 +212,6 @@ struct StepParams {
     int attn_off;            // attention staging offset in it (after the QKV projection's input)
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
     int max_chunks;          // attention chunks per q head at most (nh * max_chunks <= grid)
-    int max_chunks_g;        // grouped attention: chunks per kv head at most (nkv * max_chunks_g <= grid)
-    int part_chunks;         // chunk stride of the attention partials (>= both limits)
-    int group_ctx;           // contexts of at least this many positions use the grouped attention
     int evict_first;         // ring copies carry an L2 evict-first hint
     int max_inflight;        // ring copies in flight at most (0: stages)
     int l2_ahead;            // bytes of its next units a CTA prefetches into L2 while its ring is full
@@ -247,8 +244,6 @@ cudaError_t launch_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __
 cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
                                 const __half *bs, const int *row_of, const StepOp &plan, cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
-// Shared memory of a grouped attention item (one kv head, G q heads), from the attention offset.
-size_t step_attn_group_smem_bytes(int hd, int group);
 // xmax: the largest GEMV input (multiple of 8); hidden: the QKV projection's input; i8: inputs
 // of int8 matrices are digit rows (see digitize4 in step.cu).
 StepLayout step_layout(int hidden, int xmax, int hd, int stages, bool i8);

@@ -645,9 +645,9 @@ struct StepState {
 // input is ready; `qkv` is that projection's op (same layer caches).
 template <int HD>
 __device__ void attn_prestage(const StepParams &p, const StepOp &qkv, const StepState &ss, uint8_t *am, int item,
-                              int n_chunks, int rows_per, int ctx, bool grouped) {
+                              int n_chunks, int rows_per, int ctx) {
     const int G = p.nh / p.nkv;
-    const int u = item / n_chunks, ch = item - u * n_chunks, g = grouped ? u : u / G;
+    const int h = item / n_chunks, ch = item - h * n_chunks, g = h / G;
     const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
     const int s1 = min(j1, j0 + kStepAttnRows);
     stage_rows<HD>(am, qkv.kc + (size_t)g * p.cap * HD, qkv.vc + (size_t)g * p.cap * HD, j0, j0, min(s1, ss.slot),
@@ -825,209 +825,10 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
     stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
-    uint64_t *pw = op.lpart + ((size_t)h * p.part_chunks + ch) * (HD + 2);
+    uint64_t *pw = op.lpart + ((size_t)h * p.max_chunks + ch) * (HD + 2);
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
     if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc, tag));
     if (tid == 32) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
-}
-
-// ---- grouped attention item: (kv head g, context chunk ch) for all G q heads of the group -------
-// For long contexts: each K/V sub-chunk is staged once for the G heads (the per-head items stage it
-// G times), and the per-sub-chunk barriers are shared by the G heads.
-//   scores  thread 32 + t = position t, HD-dim dot products against the G heads' q
-//   softmax warps 1-3, head h on warp 1 + h % 3: running max / sum per head in shared memory
-//   values  thread d < HD = output dim d of every head (no cross-warp sums)
-// Sub-chunks are pipelined as in attention_item. Publishes the same per (q head, chunk) partials.
-// Shared memory after the K / V rows: scores [G][R], q [G][HD], running max, sum and correction.
-template <int HD>
-__device__ void attention_group(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int item,
-                                int n_chunks, int rows_per, int ctx, const Abort &ab, int k) {
-    using L = AttnRegion<HD>;
-    constexpr int R = kStepAttnRows;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = p.nh / p.nkv;
-    const int g = item / n_chunks, ch = item - g * n_chunks;
-    const int j0 = ch * rows_per, j1 = min(ctx, j0 + rows_per);
-    const __half *kb = op.kc + (size_t)g * p.cap * HD;
-    const __half *vb = op.vc + (size_t)g * p.cap * HD;
-    float *sg = reinterpret_cast<float *>(am + 2 * (size_t)R * L::kRow);
-    float *qg = sg + G * R;
-    float *sm = qg + G * HD, *sl = sm + kGroup, *scr = sl + kGroup;
-    const int slot = ss.slot;
-    const int s1 = min(j1, j0 + R);
-    const bool has_slot = slot >= j0 && slot < j1;
-    uint32_t kvw[2] = {0u, 0u};
-    auto put_slot = [&](int base) {                 // the step's own K / V row, from the LL words
-        if (tid < HD / 2) {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int i = 2 * tid + e, which = i / (HD / 2), dd = i - which * (HD / 2);
-                const int r = slot - base;
-                __half *row = reinterpret_cast<__half *>(am + (which ? L::vOff : L::kOff) + (size_t)r * L::kRow);
-                const int d0 = which ? dd : ((((dd >> 3) ^ (r & 7)) << 3) | (dd & 7));
-                const int d1 = which ? dd + HD / 2 : (((((dd + HD / 2) >> 3) ^ (r & 7)) << 3) | (dd & 7));
-                row[d0] = __ushort_as_half((unsigned short)(kvw[e] & 0xffffu));
-                row[d1] = __ushort_as_half((unsigned short)(kvw[e] >> 16));
-            }
-        }
-    };
-    {
-        // q of the G heads (contiguous LL words) and, when the chunk holds it, the new K / V row
-        constexpr int kQP = (kGroup * HD / 2 + kEpiThreads - 1) / kEpiThreads;   // q word pairs a thread
-        const int nqp = G * HD / 2;
-        const uint64_t *qw = op.lin + (size_t)g * G * HD;
-        const uint64_t *kw = op.lkv + (size_t)g * HD + 2 * tid;
-        uint64_t w[kQP + 1][2];
-        uint32_t valid = 0u;
-#pragma unroll
-        for (int j = 0; j < kQP; ++j)
-            if (tid + j * kEpiThreads < nqp) valid |= 1u << j;
-        if (has_slot && tid < HD / 2) valid |= 1u << kQP;
-        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 0);
-        ll_poll<kQP + 1>(w, valid, [&](int j) { return j < kQP ? qw + 2 * (tid + j * kEpiThreads) : kw; },
-                         ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
-        stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
-        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 1);
-#pragma unroll
-        for (int j = 0; j < kQP; ++j) {
-            if ((valid >> j) & 1u) {
-                const int e = 2 * (tid + j * kEpiThreads);
-                qg[e] = ll_f(w[j][0]);
-                qg[e + 1] = ll_f(w[j][1]);
-            }
-        }
-        if ((valid >> kQP) & 1u) {
-            kvw[0] = (uint32_t)w[kQP][0];
-            kvw[1] = (uint32_t)w[kQP][1];
-        }
-        if (tid < G) {
-            sm[tid] = -INFINITY;
-            sl[tid] = 0.f;
-        }
-        if (slot >= j0 && slot < s1) put_slot(j0);
-    }
-    cp_async_wait_all();
-    epi_sync();
-    stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 2);
-    float acc[kGroup];                              // thread d < HD: dim d of every head
-#pragma unroll
-    for (int h = 0; h < kGroup; ++h) acc[h] = 0.f;
-    for (int a = j0; a < j1; a += R) {
-        const int b = min(j1, a + R), nj = b - a;
-        const int a2 = b, b2 = min(j1, b + R);
-        if (a != j0) {
-            cp_async_wait_but1();                   // K rows of [a, b)
-            if (slot >= a && slot < b) put_slot(a);
-            epi_sync();
-        }
-        const int sp = tid - 32;
-        if (sp >= 0 && sp < nj) {
-            const uint8_t *kr = am + L::kOff + (size_t)sp * L::kRow;
-            float sv[kGroup];
-#pragma unroll
-            for (int h = 0; h < kGroup; ++h) sv[h] = 0.f;
-#pragma unroll
-            for (int c = 0; c < HD / 8; ++c) {
-                const uint4 kq = *reinterpret_cast<const uint4 *>(kr + ((c ^ (sp & 7)) << 4));
-                const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.x));
-                const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.y));
-                const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.z));
-                const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kq.w));
-#pragma unroll
-                for (int h = 0; h < kGroup; ++h) {
-                    if (h < G) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(qg + h * HD + 8 * c);
-                        const float4 qb = *reinterpret_cast<const float4 *>(qg + h * HD + 8 * c + 4);
-                        float t = sv[h];
-                        t = fmaf(qa.x, k0.x, t);
-                        t = fmaf(qa.y, k0.y, t);
-                        t = fmaf(qa.z, k1.x, t);
-                        t = fmaf(qa.w, k1.y, t);
-                        t = fmaf(qb.x, k2.x, t);
-                        t = fmaf(qb.y, k2.y, t);
-                        t = fmaf(qb.z, k3.x, t);
-                        t = fmaf(qb.w, k3.y, t);
-                        sv[h] = t;
-                    }
-                }
-            }
-            const int jj = a + sp;
-            const bool vis = !(jj >= ss.tree_base && !((ss.mask >> (jj - ss.tree_base)) & 1ull));
-#pragma unroll
-            for (int h = 0; h < kGroup; ++h)
-                if (h < G) sg[h * R + sp] = vis ? sv[h] * p.scale : -INFINITY;
-        }
-        epi_sync();                                 // the K rows are free
-        if (a2 < j1) {
-            stage_half<HD, false>(am, kb, a2, a2, min(b2, slot), tid);
-            cp_async_commit();
-        }
-        if (a == j0) {
-            stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
-            stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 3);
-        }
-        if (warp >= 1) {                            // softmax statistics, one head per warp at a time
-            for (int h = warp - 1; h < G; h += 3) {
-                __syncwarp();
-                const float m_run = sm[h];
-                float *sh = sg + h * R;
-                const float v0 = lane < nj ? sh[lane] : -INFINITY;
-                const float v1 = lane + 32 < nj ? sh[lane + 32] : -INFINITY;
-                const float mnew = fmaxf(m_run, warp_max(fmaxf(v0, v1)));
-                const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
-                const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
-                const float ls = warp_sum((lane < nj ? p0 : 0.f) + (lane + 32 < nj ? p1 : 0.f));
-                const float corr = m_run == -INFINITY ? 0.f : expf(m_run - mnew);
-                if (lane < nj) sh[lane] = p0;
-                if (lane + 32 < nj) sh[lane + 32] = p1;
-                __syncwarp();
-                if (lane == 0) {
-                    sl[h] = sl[h] * corr + ls;
-                    sm[h] = mnew;
-                    scr[h] = corr;
-                }
-            }
-        }
-        if (a != j0) {                              // the V rows of [a, b)
-            if (a2 < j1)
-                cp_async_wait_but1();
-            else
-                cp_async_wait_all();
-        }
-        epi_sync();
-        if (a == j0) stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 4);
-        if (tid < HD) {
-            float cr[kGroup];
-#pragma unroll
-            for (int h = 0; h < kGroup; ++h) cr[h] = h < G ? scr[h] : 0.f;
-#pragma unroll
-            for (int h = 0; h < kGroup; ++h) acc[h] *= cr[h];
-            const __half *vcol = reinterpret_cast<const __half *>(am + L::vOff) + tid;
-            for (int j = 0; j < nj; ++j) {
-                const float v = __half2float(vcol[(size_t)j * HD]);
-#pragma unroll
-                for (int h = 0; h < kGroup; ++h)
-                    if (h < G) acc[h] = fmaf(sg[h * R + j], v, acc[h]);
-            }
-        }
-        epi_sync();                                 // the V rows and the probabilities are free
-        if (a2 < j1) {
-            stage_half<HD, true>(am, vb, a2, a2, min(b2, slot), tid);
-            cp_async_commit();
-        }
-    }
-    stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
-    const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
-#pragma unroll
-    for (int h = 0; h < kGroup; ++h) {
-        if (h < G) {
-            uint64_t *pw = op.lpart + ((size_t)(g * G + h) * p.part_chunks + ch) * (HD + 2);
-            if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc[h], tag));
-            if (tid == h) ll_st2(pw, ll_wordf(sm[h], tag), ll_wordf(sl[h], tag));
-        }
-    }
 }
 
 // The chunk-0 item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
@@ -1043,7 +844,7 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
     constexpr int kW = HD + 2;                  // words per chunk
     const int tid = threadIdx.x;
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
-    const uint64_t *base = op.lpart + (size_t)h * p.part_chunks * kW;
+    const uint64_t *base = op.lpart + (size_t)h * p.max_chunks * kW;
     static_assert((size_t)kMergeBatch * kW * 4 <= L::sOff, "a merge batch fits the K/V staging rows");
     float *mp = reinterpret_cast<float *>(am + L::kOff);
     float M = -INFINITY, Ls = 0.f, A = 0.f;
@@ -1365,11 +1166,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             ss.token = 0;
         }
         const int ctx = min(ss.slot + 1, p.cap);
-        // attention items: per kv head (all its q heads) for long contexts, else per q head
-        const bool grouped = ctx >= p.group_ctx;
-        const int n_chunks = attn_chunks(ctx, grouped ? p.max_chunks_g : p.max_chunks);
+        const int n_chunks = attn_chunks(ctx, p.max_chunks);
         const int rows_per = (ctx + n_chunks - 1) / n_chunks;
-        const int n_items = (grouped ? p.nkv : p.nh) * n_chunks;
         const int half_hd = HD / 2;
         int s = 0, round = 0, consumed = 0;       // ring position of the compute warps
 
@@ -1384,18 +1182,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             stamp(p.trace, k, C, c, 0);
             const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
             if (op.kind == OP_ATTN) {
-                // items on the last CTAs: (q head or kv head, context chunk), one per CTA
-                const int item = C - 1 - c;
-                if (grouped && item < n_items && !ab.on()) {
-                    attention_group<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
-                    // head g G + hh is merged by chunk hh % n_chunks of its kv head's items
-                    const int G = p.nh / p.nkv, g = item / n_chunks, chh = item - g * n_chunks;
-                    stamp(p.trace, k, C, c, 6);
-                    stamp_clk(p.trace, k, C, c, 6);
-                    for (int hh = chh; hh < G; hh += n_chunks) merge_head<HD>(p, op, ss, am, g * G + hh, n_chunks, k, ab);
-                    stamp(p.trace, k, C, c, 7);
-                    stamp_clk(p.trace, k, C, c, 7);
-                } else if (item < n_items && !ab.on()) {
+                // items on the last CTAs: (q head, context chunk), one per CTA
+                const int items = p.nh * n_chunks, item = C - 1 - c;
+                if (item < items && !ab.on()) {
                     attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
                     const int h = item / n_chunks;
                     if (item == h * n_chunks) {          // chunk 0 of the head: merge all of them
@@ -1412,7 +1201,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             if (op.epi == EPI_QKV) {
                 // this CTA's attention item of the layer: stage its immutable K/V rows now
                 const int item = C - 1 - c;
-                if (item < n_items) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, grouped);
+                if (item < p.nh * n_chunks) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             stamp_clk(p.trace, k, C, c, 0);
@@ -1845,11 +1634,6 @@ bool step_gemv_supported(const StepOp &o, int stage_bytes) {
 
 size_t step_attn_smem_bytes(int hd) { return hd == 64 ? AttnRegion<64>::bytes : AttnRegion<128>::bytes; }
 
-size_t step_attn_group_smem_bytes(int hd, int group) {
-    return 2 * (size_t)kStepAttnRows * hd * 2 + (size_t)group * kStepAttnRows * 4 + (size_t)group * hd * 4 +
-           3 * (size_t)kGroup * 4;
-}
-
 static size_t step_static_reserve() { return 2048; }   // static shared memory of k_step, rounded up
 
 // Dynamic shared memory: ring [stages x stage_bytes] | vector region | ops k, k + 1 | barriers.
@@ -1933,10 +1717,6 @@ cudaError_t prepare_step(int hd, size_t smem, bool q8) {
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8) {
     if (p.stages < 2 || p.stage_bytes < 1024 || p.stage_bytes % 1024 || p.stage_bytes > kMaxStageBytes ||
         p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks || p.attn_off % 128 ||
-        p.nkv * p.max_chunks_g > grid || p.max_chunks_g > kStepMaxChunks || p.max_chunks_g < 1 ||
-        p.part_chunks < std::max(p.max_chunks, p.max_chunks_g) ||
-        (p.group_ctx < (1 << 30) &&
-         (size_t)p.attn_off + step_attn_group_smem_bytes(hd, p.nh / p.nkv) > (size_t)p.vec_bytes) ||
         p.vec_bytes % 128 || (size_t)p.attn_off + step_attn_smem_bytes(hd) > (size_t)p.vec_bytes)
         return cudaErrorInvalidValue;
     return q8 ? step_launch_hd<true>(hd, &p, grid, smem, s, pdl) : step_launch_hd<false>(hd, &p, grid, smem, s, pdl);
