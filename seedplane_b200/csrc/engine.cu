@@ -1363,8 +1363,10 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
     int32_t *dtok = reinterpret_cast<int32_t *>(e->acc_scratch + e->acc_vocab);
     int32_t *dpar = dtok + kSmallNodes, *dout = dpar + kSmallNodes;
     int32_t host[2 * kSmallNodes];
-    memcpy(host, tokens_host, n * 4);
-    memcpy(host + kSmallNodes, parents_host, n * 4);
+    if (n > 0) {
+        memcpy(host, tokens_host, n * 4);
+        memcpy(host + kSmallNodes, parents_host, n * 4);
+    }
     SP_CUDA(cudaMemcpyAsync(dtok, host, sizeof(host), cudaMemcpyHostToDevice, s));
     SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, temperature, seed,
                                      counter, e->acc_scratch, dout, s));

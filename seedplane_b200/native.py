@@ -14,8 +14,11 @@ types: a failed request raises `RuntimeError(message)`, a missing engine `FileNo
 * Greedy decoding runs on the device in blocks (the argmax is fed back without a host round trip);
   the host sees each block's tokens, cuts at a stop token and rolls the cache back to it. The
   token sequence is the same as one-at-a-time decoding.
-* Only full attention (`mode` None / "full") and greedy decoding (temperature 0) are built; shard
-  windows and GPU sampling are the next rows of the plan and raise `RuntimeError` here.
+* Only full attention (`mode` None / "full") is built; shard windows raise `RuntimeError`.
+* Sampling: temperature > 0 draws each token on the device from softmax(logits / temperature) with
+  a counter-based RNG (`seed`, then one counter step per token), so a seed reproduces a run; the
+  distribution is the reference's, the random stream is not its mt19937_64 (`sampler.hpp`).
+  `top_k` / `top_p` other than off (0 / 1.0) raise `RuntimeError`.
 
 `last` (`qwen_vk.cpp:848-850`): {done, reason in {stop, length, context}, generated, prompt_tokens,
 prefill_s, decode_s, decode_tok_s, position}.
@@ -161,8 +164,11 @@ class NativeEngine:
             raise RuntimeError(f"unknown request field(s): {sorted(unknown)}")
         opt = {k: v for k, v in self.defaults.items()}
         opt.update({k: v for k, v in sampling.items() if v is not None})
-        if opt.get("temperature") not in (None, 0, 0.0):
-            raise RuntimeError("sampling (temperature > 0) is not built on this engine yet; use greedy decoding")
+        if opt.get("top_k") not in (None, 0) or opt.get("top_p") not in (None, 1, 1.0):
+            raise RuntimeError("top_k / top_p sampling is not built on this engine; use temperature alone")
+        temp = float(opt.get("temperature") or 0.0)
+        if temp < 0.0:
+            raise RuntimeError("temperature must be >= 0")
         stops = set(self._stop_ids)
         for s in opt.get("stop") or ():
             if isinstance(s, int):
@@ -171,7 +177,7 @@ class NativeEngine:
                 i = self._tok.token_to_id(str(s))
                 if i is not None:
                     stops.add(int(i))
-        return int(opt["max_new_tokens"]), stops
+        return int(opt["max_new_tokens"]), stops, temp, int(opt.get("seed") or 0)
 
     def _feed(self, ids: List[int]):
         """Prefill ids into the cache; returns the argmax after the last one."""
@@ -180,7 +186,7 @@ class NativeEngine:
         return int(am[-1])
 
     def _run(self, prompt: List[int], sampling) -> Iterable[str]:
-        max_new, stops = self._options(sampling)
+        max_new, stops, temp, seed = self._options(sampling)
         self.last_tokens = []
         self.last = None
         if not prompt:
@@ -192,6 +198,9 @@ class NativeEngine:
                          "prefill_s": 0.0, "decode_s": 0.0, "decode_tok_s": 0.0, "position": self._kv.length}
             return
         dev = self._engine.device
+        if temp > 0.0:
+            yield from self._run_sampled(prompt, max_new, stops, temp, seed)
+            return
         t0 = time.perf_counter()
         queue = [self._feed(prompt)]            # generated tokens not yet checked (none is in the cache)
         torch.cuda.synchronize(dev)
@@ -234,6 +243,48 @@ class NativeEngine:
             queue = out.tolist()
             self._history.append(token)
             self._history.extend(queue[:-1])
+        decode_s = time.perf_counter() - t1
+        gen = len(produced)
+        self.last = {"done": True, "reason": reason, "generated": gen, "prompt_tokens": len(prompt),
+                     "prefill_s": prefill_s, "decode_s": decode_s,
+                     "decode_tok_s": (gen - 1) / decode_s if gen > 1 and decode_s > 0 else 0.0,
+                     "position": self._kv.length}
+
+    def _run_sampled(self, prompt: List[int], max_new: int, stops, temp: float, seed: int) -> Iterable[str]:
+        """Temperature sampling: one decode step with logits per token, the draw on the device."""
+        from .speculative import sample_token
+        dev = self._engine.device
+        t0 = time.perf_counter()
+        logits, _ = self._engine.forward(self._kv, torch.tensor(prompt, dtype=torch.int32))
+        self._history.extend(prompt)
+        counter = 0
+        tok = sample_token(self._engine, logits, temp, seed, counter)
+        prefill_s = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        produced: List[int] = []
+        shown = ""
+        reason = "length"
+        while True:
+            if tok in stops:
+                reason = "stop"
+                break
+            produced.append(tok)
+            self.last_tokens.append(tok)
+            if self._tok is not None:
+                full = self._tok.decode(produced)
+                if not full.endswith("\ufffd") and len(full) > len(shown):
+                    piece, shown = full[len(shown):], full
+                    yield piece
+            if len(produced) >= max_new:
+                break
+            if self.capacity - self._kv.length < 1:
+                reason = "context"
+                break
+            _, lg = self._engine.decode(self._kv, tok, self._kv.length, 1, want_logits=True)
+            self._history.append(tok)
+            counter += 1
+            tok = sample_token(self._engine, lg, temp, seed, counter)
+        torch.cuda.synchronize(dev)
         decode_s = time.perf_counter() - t1
         gen = len(produced)
         self.last = {"done": True, "reason": reason, "generated": gen, "prompt_tokens": len(prompt),

@@ -218,6 +218,17 @@ def accept_stochastic(engine, flat: FlatForest, target_logits, draft_logits, tem
     return Verification(emitted, n_acc, n_out > n_acc, n_out, path), nodes
 
 
+def sample_token(engine, logits_row, temperature: float, seed: int, counter: int) -> int:
+    """One draw from softmax(logits / temperature) on the device: the stochastic acceptance of an
+    empty tree (`sp_accept_stochastic` with no nodes draws from the target distribution), with the
+    same fp64 arithmetic and counter-based RNG, so (seed, counter) reproduce the token. `logits_row`:
+    fp32 [1, V] (or [V]) on the engine's device."""
+    row = logits_row.reshape(1, -1)
+    empty = FlatForest(tokens=(), parents=(), depths=(), node_paths=(), paths=())
+    v, _ = accept_stochastic(engine, empty, row, row, temperature, seed, counter)
+    return int(v.emitted[0])
+
+
 def commit_tree(engine, kv, result: TreeResult) -> int:
     """Keep the K/V of the accepted draft nodes (they were written at scratch slots len + i) and
     advance the cache length by their number. Returns the new length."""

@@ -1,5 +1,6 @@
 """`NativeEngine` and the per-GPU HIVE executor on the GPU: greedy tokens identical to the oracle,
-the reference's `last` fields, stop-token cut with cache rollback, reset."""
+the reference's `last` fields, stop-token cut with cache rollback, reset; temperature sampling
+(the device draw bit-exact with its CPU restatement, runs reproducible from the seed)."""
 import pytest
 import torch
 
@@ -43,7 +44,7 @@ def test_native_engine_generate_matches_oracle(bundle):
         list(eng.generate(ids=prompt, max_new_tokens=7))
         assert eng.last_tokens == want[:7]
         with pytest.raises(RuntimeError):
-            list(eng.generate(ids=prompt, temperature=0.7))
+            list(eng.generate(ids=prompt, temperature=0.7, top_k=40))
         with pytest.raises(RuntimeError):
             eng.tokenize("hello")
 
@@ -61,3 +62,39 @@ def test_gpu_agent_executor_matches_oracle(bundle):
         want = o.greedy(prompt, 9)[0]
         assert r["tokens"] == want and r["token_sha256"] == token_sha256(want)
     eng.close()
+
+
+def test_device_temperature_draw_matches_restatement(bundle):
+    """One draw from softmax(logits / T) on the device equals the CPU restatement's on the same logits."""
+    from oracle import speculative_oracle as so
+    from seedplane_b200.engine import CudaQwen2
+    from seedplane_b200.speculative import sample_token
+    d, cfg, w = bundle
+    eng = CudaQwen2(cfg, w, device="cuda:0")
+    kv = eng.new_kv(64)
+    logits, _ = eng.forward(kv, random_prompt(cfg.vocab, 9, seed=2))
+    host = logits.cpu().numpy()
+    for temp in (0.5, 1.0, 3.0):
+        for seed, counter in [(0, 0), (1, 0), (7, 3), (12345, 99), (2 ** 40 + 5, 7)]:
+            got = sample_token(eng, logits, temp, seed, counter)
+            emitted, _ = so.accept_stochastic([], [], host, host, temp, seed, counter)
+            assert got == emitted[0], (temp, seed, counter)
+    eng.close()
+
+
+def test_native_engine_temperature_sampling(bundle):
+    from seedplane_b200.native import NativeEngine
+    d, cfg, w = bundle
+    prompt = random_prompt(cfg.vocab, 11, seed=5)
+    with NativeEngine(d, ctx=256) as eng:
+        list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11))
+        a = list(eng.last_tokens)
+        assert len(a) == 24 and all(0 <= t < cfg.vocab for t in a)
+        assert eng.last["reason"] == "length" and eng.last["position"] == len(prompt) + 23
+        list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11))
+        assert eng.last_tokens == a                      # the seed reproduces the run
+        list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=12))
+        assert eng.last_tokens != a                      # another seed, another run
+        # a stop token ends the run before it
+        list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11, stop=[a[4]]))
+        assert eng.last_tokens == a[:a.index(a[4])] and eng.last["reason"] == "stop"
