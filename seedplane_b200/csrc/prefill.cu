@@ -118,9 +118,10 @@ __global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, 
 // before slot0 and, among the block's own slots, [slot0, slot0 + t] (causal, mask == null) or the
 // slots slot0 + j whose bit j its ancestor mask holds (tree, T <= 64). CTA = (q head, 16 queries),
 // warp = 4 queries; keys in tiles of 32 staged
-// in shared memory (K rows padded by 4 bytes: lane j reads row j without bank conflicts). Scores,
-// online softmax (running max / sum per query) and the value sums in fp32; the output goes out as
-// fp16 hi / lo halves (the O projection's input).
+// in shared memory (K rows padded by 8 bytes: lane j reads row j without bank conflicts). Scores,
+// online softmax (running max / sum per query) and the value sums in fp32 (the tile's
+// probabilities go through shared memory: each lane then sums its dims over the keys); the output
+// goes out as fp16 hi / lo halves (the O projection's input).
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, const float *q, const __half *kc,
                                                       const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
@@ -128,10 +129,11 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
                                                       DevState *st) {
     const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     constexpr int DL = HD / 32;                       // output dims per lane
-    constexpr int KROW = HD * 2 + 4;                  // padded K row (bytes)
+    constexpr int KROW = HD * 2 + 8;                  // padded K row (bytes): 8-byte reads, lanes on distinct banks
     __shared__ __align__(16) float qs[kAttnQ][HD];
     __shared__ __align__(16) uint8_t ks[kAttnKeys * KROW];
     __shared__ __align__(16) __half vs[kAttnKeys][HD];
+    __shared__ float ps[kAttnQ][kAttnKeys];            // this tile's probabilities
     const int h = blockIdx.x, q0 = blockIdx.y * kAttnQ;
     const int g = h / (nh / nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,17 +169,21 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
         }
         __syncthreads();
         __syncwarp();                                     // reconverged before the shuffles below
-        // scores: lane = key k0 + lane, four queries of this warp
+        // scores: lane = key k0 + lane, four queries of this warp, four dims per step
         float s[4] = {0.f, 0.f, 0.f, 0.f};
         const uint8_t *kr = ks + (size_t)lane * KROW;
 #pragma unroll 8
-        for (int d = 0; d < HD; d += 2) {
-            const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(kr + d * 2));
+        for (int d = 0; d < HD; d += 4) {
+            const uint2 kk = *reinterpret_cast<const uint2 *>(kr + d * 2);
+            const float2 ka = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
+            const float2 kb2 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 qf = *reinterpret_cast<const float2 *>(&qs[warp * 4 + i][d]);
-                s[i] = fmaf(qf.x, kf.x, s[i]);
-                s[i] = fmaf(qf.y, kf.y, s[i]);
+                const float4 qf = *reinterpret_cast<const float4 *>(&qs[warp * 4 + i][d]);
+                s[i] = fmaf(qf.x, ka.x, s[i]);
+                s[i] = fmaf(qf.y, ka.y, s[i]);
+                s[i] = fmaf(qf.z, kb2.x, s[i]);
+                s[i] = fmaf(qf.w, kb2.y, s[i]);
             }
         }
 #pragma unroll
@@ -194,14 +200,33 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
             m[i] = mnew;
 #pragma unroll
             for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
-            for (int j = 0; j < kAttnKeys; ++j) {
-                const float pj = __shfl_sync(0xffffffffu, p, j);
-                if (pj != 0.f) {
+            ps[warp * 4 + i][lane] = p;
+        }
+        __syncwarp();
+        // values: lane = DL dims, keys in order, the warp's four queries per key (probabilities from
+        // shared memory, a broadcast; no shuffles, no branches)
+        for (int j = 0; j < kAttnKeys; ++j) {
+            float vf[DL];
+            if constexpr (DL == 4) {
+                const uint2 vv = *reinterpret_cast<const uint2 *>(&vs[j][lane * 4]);
+                const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                const float2 v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                vf[0] = v0.x;
+                vf[1] = v0.y;
+                vf[2] = v1.x;
+                vf[3] = v1.y;
+            } else {
 #pragma unroll
-                    for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, __half2float(vs[j][lane * DL + d]), acc[i][d]);
-                }
+                for (int d = 0; d < DL; ++d) vf[d] = __half2float(vs[j][lane * DL + d]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pj = ps[warp * 4 + i][j];
+#pragma unroll
+                for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, vf[d], acc[i][d]);
             }
         }
+        __syncwarp();                                     // ps is rewritten by the next tile
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
