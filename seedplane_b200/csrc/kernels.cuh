@@ -245,7 +245,7 @@ cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as,
                                 const __half *bs, const int *row_of, const StepOp &plan, cudaStream_t s);
 size_t step_attn_smem_bytes(int hd);
 // xmax: the largest GEMV input (multiple of 8); hidden: the QKV projection's input; i8: inputs
-// of int8 matrices are digit rows (see digitize4 in step.cu).
+// of int8 matrices are digit rows (see digitize4_n in step.cu).
 StepLayout step_layout(int hidden, int xmax, int hd, int stages, bool i8);
 cudaError_t prepare_step(int hd, size_t smem, bool q8);   // q8: the build with the int8 unit path
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be

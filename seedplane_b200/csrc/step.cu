@@ -135,34 +135,47 @@ SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int ro
 // 64 + c * 16 + k % 16): each 16-input half is a K-major 8-row core matrix whose rows 0-3 are the
 // digits (rows 4-7, the next 64 bytes, give output columns that are not read). The block's scale
 // goes to bsc[k / 32]. The 32 inputs of a block are the float4s of 8 consecutive lanes (lane & 7 =
-// position in the block); the whole warp calls this.
-SP_DEVINL void digitize4(float4 x, int k, int8_t *dg, float *bsc) {
-    float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
-    __syncwarp();                   // a warp left split by earlier divergent code pays ~8x per shuffle
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    // biased exponent of m, at least 26 (blocks below 2^-101 become zero: multiplier 2^127)
-    const int eb = max((int)((__float_as_uint(m) >> 23) & 0xffu), 26);
-    const float mul = __uint_as_float((uint32_t)(280 - eb) << 23);           // 2^(153 - eb)
-    if ((threadIdx.x & 7) == 0) bsc[k >> 5] = __uint_as_float((uint32_t)(eb - 26) << 23);   // 2^(eb - 153)
-    uint32_t sp[4];
-    const float xv[4] = {x.x, x.y, x.z, x.w};
+// position in the block); the whole warp calls digitize4_n.
+// This thread's N float4s, x[u] = inputs k0 + u * kstride .. + 3 for u < nvalid (warp-uniform),
+// into digits: the N block maxima first (N shuffle chains interleaved after one reconvergence),
+// then the N conversions; one float4 at a time would serialise N latency chains.
+template <int N>
+SP_DEVINL void digitize4_n(const float4 (&x)[N], int k0, int kstride, int nvalid, int8_t *dg, float *bsc) {
+    float m[N];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const int q = __float2int_rn(xv[e] * mul);
-        // bytes (low to high): d3, d2, d1, d0 = q's 7-bit groups, the top one signed
-        sp[e] = ((uint32_t)q & 0x7fu) | (((uint32_t)q << 1) & 0x7f00u) | (((uint32_t)q << 2) & 0x7f0000u) |
-                (((uint32_t)q << 3) & 0xff000000u);
+    for (int u = 0; u < N; ++u) m[u] = fmaxf(fmaxf(fabsf(x[u].x), fabsf(x[u].y)), fmaxf(fabsf(x[u].z), fabsf(x[u].w)));
+    __syncwarp();                   // a warp left split by earlier divergent code pays ~8x per shuffle
+#pragma unroll
+    for (int sh = 1; sh <= 4; sh <<= 1)
+#pragma unroll
+        for (int u = 0; u < N; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], sh));
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        if (u < nvalid) {
+            const int k = k0 + u * kstride;
+            // biased exponent of m, at least 26 (blocks below 2^-101 become zero: multiplier 2^127)
+            const int eb = max((int)((__float_as_uint(m[u]) >> 23) & 0xffu), 26);
+            const float mul = __uint_as_float((uint32_t)(280 - eb) << 23);       // 2^(153 - eb)
+            if ((threadIdx.x & 7) == 0) bsc[k >> 5] = __uint_as_float((uint32_t)(eb - 26) << 23);   // 2^(eb - 153)
+            uint32_t sp[4];
+            const float xv[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int q = __float2int_rn(xv[e] * mul);
+                // bytes (low to high): d3, d2, d1, d0 = q's 7-bit groups, the top one signed
+                sp[e] = ((uint32_t)q & 0x7fu) | (((uint32_t)q << 1) & 0x7f00u) | (((uint32_t)q << 2) & 0x7f0000u) |
+                        (((uint32_t)q << 3) & 0xff000000u);
+            }
+            // transpose: word c = byte (3 - c) of the four inputs (c = 0: the top digit)
+            const uint32_t t0 = __byte_perm(sp[0], sp[1], 0x5140), t1 = __byte_perm(sp[0], sp[1], 0x7362);
+            const uint32_t t2 = __byte_perm(sp[2], sp[3], 0x5140), t3 = __byte_perm(sp[2], sp[3], 0x7362);
+            int8_t *w = dg + (k >> 5) * 128 + ((k >> 4) & 1) * 64 + (k & 15);
+            *reinterpret_cast<uint32_t *>(w) = __byte_perm(t1, t3, 0x7632);
+            *reinterpret_cast<uint32_t *>(w + 16) = __byte_perm(t1, t3, 0x5410);
+            *reinterpret_cast<uint32_t *>(w + 32) = __byte_perm(t0, t2, 0x7632);
+            *reinterpret_cast<uint32_t *>(w + 48) = __byte_perm(t0, t2, 0x5410);
+        }
     }
-    // transpose: word c = byte (3 - c) of the four inputs (c = 0: the top digit)
-    const uint32_t t0 = __byte_perm(sp[0], sp[1], 0x5140), t1 = __byte_perm(sp[0], sp[1], 0x7362);
-    const uint32_t t2 = __byte_perm(sp[2], sp[3], 0x5140), t3 = __byte_perm(sp[2], sp[3], 0x7362);
-    int8_t *w = dg + (k >> 5) * 128 + ((k >> 4) & 1) * 64 + (k & 15);
-    *reinterpret_cast<uint32_t *>(w) = __byte_perm(t1, t3, 0x7632);
-    *reinterpret_cast<uint32_t *>(w + 16) = __byte_perm(t1, t3, 0x5410);
-    *reinterpret_cast<uint32_t *>(w + 32) = __byte_perm(t0, t2, 0x7632);
-    *reinterpret_cast<uint32_t *>(w + 48) = __byte_perm(t0, t2, 0x5410);
 }
 
 // The MMAs of one int8 unit. A unit of rows_p rows x 32 nb inputs holds, per 32-input
@@ -456,42 +469,58 @@ __device__ __noinline__ void attn_digits(const uint64_t *lin, int K, uint32_t ta
     if (!ll_poll<2 * kNormRegs>(w, valid, [&](int j) { return lin + 4 * (tid + (j >> 1) * kEpiThreads) + 2 * (j & 1); },
                                 tag, ab))
         return;
-    __syncwarp();
+    float4 xs[kNormRegs];
+    int nvalid = 0;
 #pragma unroll
-    for (int q = 0; q < kNormRegs; ++q)
-        if (4 * (tid + q * kEpiThreads) < K)
-            digitize4(make_float4(ll_x(w[2 * q][0], true), ll_x(w[2 * q][1], true), ll_x(w[2 * q + 1][0], true),
-                                  ll_x(w[2 * q + 1][1], true)),
-                      4 * (tid + q * kEpiThreads), dg, bsc);
+    for (int q = 0; q < kNormRegs; ++q) {
+        xs[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (4 * (tid + q * kEpiThreads) < K) {                   // warp-uniform (K % 128 == 0)
+            xs[q] = make_float4(ll_x(w[2 * q][0], true), ll_x(w[2 * q][1], true), ll_x(w[2 * q + 1][0], true),
+                                ll_x(w[2 * q + 1][1], true));
+            nvalid = q + 1;
+        }
+    }
+    digitize4_n<kNormRegs>(xs, 4 * tid, 4 * kEpiThreads, nvalid, dg, bsc);
 }
 
 // PRO_PLAIN into digits: the fp16 hi / lo vectors behind the counter (written by other CTAs in
-// this launch: loads through L2), kPlainBatch float4s (2 kPlainBatch loads) in flight per thread:
-// the round trip to L2, not the arithmetic, bounds this prologue.
+// this launch). The digits of a 32-input block take 128 bytes, as many as its fp16 hi and lo
+// halves: every 16-byte piece of the input goes in flight at once (cp.async through L2) into its
+// block's own 128 bytes (hi at +0, lo at +64), one wait, then each block turns into digits in
+// place. One round trip to L2 instead of one per batch of registers: under the weight stream a
+// round trip takes microseconds. A block's 8 threads sit in one warp and read all of it before the
+// warp barrier inside digitize4_n; its digit stores come after.
 constexpr int kPlainBatch = 12;
 __device__ __noinline__ void plain_digits(const __half *xin_h, const __half *xin_l, int K, int8_t *dg, float *bsc) {
     const int tid = threadIdx.x;
+    for (int i = tid; i < K / 8; i += kEpiThreads) {                // piece i = inputs 8i .. 8i + 7
+        int8_t *d = dg + 128 * (i >> 2) + 16 * (i & 3);
+        cp_async16(d, reinterpret_cast<const uint4 *>(xin_h) + i);
+        cp_async16(d + 64, reinterpret_cast<const uint4 *>(xin_l) + i);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    epi_sync();
     for (int i0 = tid; 4 * i0 < K; i0 += kPlainBatch * kEpiThreads) {
-        uint2 h[kPlainBatch], l[kPlainBatch];
+        float4 xs[kPlainBatch];
+        int nvalid = 0;
 #pragma unroll
         for (int u = 0; u < kPlainBatch; ++u) {
-            const int i = i0 + u * kEpiThreads;
-            if (4 * i < K) {
-                h[u] = __ldcg(reinterpret_cast<const uint2 *>(xin_h) + i);
-                l[u] = __ldcg(reinterpret_cast<const uint2 *>(xin_l) + i);
+            const int k = 4 * (i0 + u * kEpiThreads);
+            xs[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < K) {                                            // warp-uniform (K % 128 == 0)
+                const int8_t *s = dg + 128 * (k >> 5) + 2 * (k & 31);
+                const uint2 h = *reinterpret_cast<const uint2 *>(s);
+                const uint2 l = *reinterpret_cast<const uint2 *>(s + 64);
+                const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+                const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&h.y));
+                const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&l.x));
+                const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&l.y));
+                xs[u] = make_float4(h0.x + l0.x, h0.y + l0.y, h1.x + l1.x, h1.y + l1.y);
+                nvalid = u + 1;
             }
         }
-#pragma unroll
-        for (int u = 0; u < kPlainBatch; ++u) {
-            const int i = i0 + u * kEpiThreads;
-            if (4 * i < K) {                                        // warp-uniform (K % 128 == 0)
-                const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&h[u].x));
-                const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&h[u].y));
-                const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&l[u].x));
-                const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&l[u].y));
-                digitize4(make_float4(h0.x + l0.x, h0.y + l0.y, h1.x + l1.x, h1.y + l1.y), 4 * i, dg, bsc);
-            }
-        }
+        digitize4_n<kPlainBatch>(xs, 4 * i0, 4 * kEpiThreads, nvalid, dg, bsc);
     }
 }
 
@@ -1302,16 +1331,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 if (lane == 0) s_val[warp] = sq;
                 epi_sync();
                 const float inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
+                if (Q8 && q8) {
+                    int nvalid = 0;
 #pragma unroll
-                for (int q = 0; q < kNormRegs; ++q) {
-                    const int i = tid + q * kEpiThreads;
-                    if (4 * i < K) {                                // warp-uniform (K % 128 == 0 for int8)
-                        const float4 xn = make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
-                                                      (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w);
-                        if (q8)
-                            digitize4(xn, 4 * i, dg, bsc);
-                        else
-                            store_hilo4(xh, xl, 4 * i, xn);
+                    for (int q = 0; q < kNormRegs; ++q) {
+                        if (4 * (tid + q * kEpiThreads) < K) {      // warp-uniform (K % 128 == 0 for int8)
+                            v[q] = make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
+                                               (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w);
+                            nvalid = q + 1;
+                        }
+                    }
+                    digitize4_n<kNormRegs>(v, 4 * tid, 4 * kEpiThreads, nvalid, dg, bsc);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < kNormRegs; ++q) {
+                        const int i = tid + q * kEpiThreads;
+                        if (4 * i < K)
+                            store_hilo4(xh, xl, 4 * i,
+                                        make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
+                                                    (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w));
                     }
                 }
             } else if (q8 && op.pro == PRO_ATTN) {

@@ -12,7 +12,7 @@ import numpy as np
 
 
 def digits(x):
-    """Restatement of digitize4 for one 32-input block: (d[4, 32] int64, scale 2^(E - 26))."""
+    """Restatement of digitize4_n for one 32-input block: (d[4, 32] int64, scale 2^(E - 26))."""
     x = np.asarray(x, dtype=np.float32)
     m = np.float32(np.abs(x).max())
     eb = max(int((m.view(np.uint32) >> 23) & 0xFF), 26)               # biased exponent, clamped
