@@ -126,6 +126,7 @@ struct sp_engine {
     // after down (xd), q, the new K/V rows, attention partials and output; the SwiGLU activation
     uint64_t *ll_xo = nullptr, *ll_xd = nullptr, *ll_q = nullptr, *ll_kv = nullptr, *ll_part = nullptr,
              *ll_attn = nullptr;
+    uint64_t *ll_ksp = nullptr;             // split-K down projection: the second CTA's row partials
     __half *act_h = nullptr, *act_l = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
@@ -282,6 +283,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.lres = e->ll_xo + par * H;
         o.lres_k = 5 * l + 2;
         o.lout = e->ll_xd + par * H;
+        o.lksp = e->ll_ksp + par * H;
         ops.push_back(o);
     }
     StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD);
@@ -579,7 +581,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             o.N = (int)N;
             o.K = (int)K;
             o.n_valid = (int)n_valid;
-            plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes);
+            plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes, (int)env_long("SEEDPLANE_STEP_KSPLIT", 2));
             return o;
         };
         e->s_qkv = sbase(QRp, H, QR, PRO_NORM, i8);
@@ -867,8 +869,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
         int k = 0;
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            fprintf(stderr, "[seedplane] step gemv %-8s %s N=%d K=%d grid=%d pass_rows=%d chunk=%d\n", names[k++],
-                    o->fmt == WF_I8 ? "i8" : "f16", o->N, o->K, o->grid, o->pass_rows, o->chunk_w);
+            fprintf(stderr, "[seedplane] step gemv %-8s %s N=%d K=%d grid=%d ksplit=%d pass_rows=%d chunk=%d\n",
+                    names[k++], o->fmt == WF_I8 ? "i8" : "f16", o->N, o->K, o->grid, o->ksplit, o->pass_rows,
+                    o->chunk_w);
     }
     if (env_flag("SEEDPLANE_VERBOSE", false) && e->tc && !e->step_kernel) {
         const char *names[] = {"qkv", "o", "gate_up", "down", "lm_head"};
@@ -916,6 +919,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
+    const size_t w_llksp = wtake(2 * H * 8);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);
@@ -957,6 +961,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     e->ll_kv = (uint64_t *)(e->ws + w_llkv);
     e->ll_part = (uint64_t *)(e->ws + w_llpart);
     e->ll_attn = (uint64_t *)(e->ws + w_llattn);
+    e->ll_ksp = (uint64_t *)(e->ws + w_llksp);
     e->act_h = (__half *)(e->ws + w_acth);        // parity p: hi at [2p I, 2p I + I), lo right after
     e->act_l = e->act_h + I;
     e->g_head.w = e->head;

@@ -192,7 +192,7 @@ struct StepOp {
     int kind;                // StepOpKind
     int pro, epi;
     int N, K, n_valid;       // N even: rows come in pairs
-    int grid;                // CTAs owning rows: CTA c owns pairs [P c / grid, P (c + 1) / grid)
+    int grid;                // CTAs owning rows (see gemv_share)
     int pass_rows;           // rows per pass (even, <= kStepPassRows)
     int chunk_w;             // inputs per unit (f16: multiple of 256, i8: of 128; or all of K)
     int lin_k, lres_k;       // ops whose tags lin / lres carry
@@ -200,8 +200,27 @@ struct StepOp {
     int sig;                 // cnt[sig] += 1 per CTA; < 0: none
     int fmt;                 // WeightFmt of w
     int cta_bytes;           // WF_I8: bytes of one CTA's rows (CTA c's units start at c * cta_bytes)
+    int ksplit;              // CTAs sharing a row group, each over K / ksplit inputs (WF_I8, EPI_RESID)
+    int pad_;
+    uint64_t *lksp;          // ksplit 2: the second CTA's row partials for the first, LL words [N]
 };
 static_assert(sizeof(StepOp) % 16 == 0, "ops are copied to shared memory in 16-byte words");
+
+// The share of CTA c in a step GEMV of N rows (P = N / 2 row pairs) and K inputs: the grid /
+// ksplit row groups own pairs [P g / G, P (g + 1) / G); CTA c works on group g = c / ksplit over
+// inputs [K0, K0 + Kc), Kc = K / ksplit, K0 = (c % ksplit) Kc.
+struct GemvShare {
+    int R0, R, K0, Kc;
+};
+__host__ __device__ inline GemvShare gemv_share(int N, int K, int grid, int ksplit, int c) {
+    const int ks = ksplit > 1 ? ksplit : 1, G = grid / ks, g = c / ks, P = N / 2;
+    GemvShare s;
+    s.R0 = 2 * (int)((long long)P * g / G);
+    s.R = 2 * (int)((long long)P * (g + 1) / G) - s.R0;
+    s.Kc = K / ks;
+    s.K0 = (c - g * ks) * s.Kc;
+    return s;
+}
 
 struct StepParams {
     const StepOp *ops;
@@ -232,7 +251,8 @@ struct StepLayout {
     size_t smem = 0;         // dynamic shared memory; stage_bytes == 0: does not fit
 };
 
-void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes);   // fills grid, pass_rows, chunk_w from N, K
+// fills grid, ksplit, pass_rows, chunk_w from N, K (ksplit 2 only for int8 PRO_PLAIN ops, at most max_ksplit)
+void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit = 1);
 bool step_gemv_supported(const StepOp &o, int stage_bytes);
 size_t step_gemv_bytes(const StepOp &o);                           // packed bytes of a planned GEMV
 // Pack an fp16 N x K matrix (packed row r = source row row_of[r] of a / b as in

@@ -1015,11 +1015,11 @@ struct UnitCursor {
             if (__ldg(&o->kind) != OP_GEMV) continue;
             const int grid = __ldg(&o->grid);
             if (c >= grid) continue;
-            const int P = __ldg(&o->N) / 2;
-            const int R0 = 2 * (int)((long long)P * c / grid);
-            R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+            const GemvShare sh = gemv_share(__ldg(&o->N), __ldg(&o->K), grid, __ldg(&o->ksplit), c);
+            const int R0 = sh.R0;
+            R = sh.R;
             if (R <= 0) continue;
-            K = __ldg(&o->K);
+            K = sh.Kc;
             cw = __ldg(&o->chunk_w);
             prw = __ldg(&o->pass_rows);
             fmt = __ldg(&o->fmt);
@@ -1234,16 +1234,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             stamp_clk(p.trace, k, C, c, 0);
-            const int K = op.K;
+            const GemvShare sh = gemv_share(op.N, op.K, op.grid, op.ksplit, c);
+            const int K = sh.Kc;                 // this CTA's inputs: [sh.K0, sh.K0 + K) of op.K
+            const bool fin = sh.K0 == 0;         // finishes its rows (ksplit 2: adds the partner's partials)
             __half *xl = xh + K;
             // int8 weights: the input's digit rows (stride K + 16 bytes) and block scales instead
             int8_t *dg = reinterpret_cast<int8_t *>(vec);
             float *bsc = reinterpret_cast<float *>(vec + 4 * (K + 16));
             const bool q8 = Q8 && op.fmt == WF_I8;
             const bool norm = op.pro == PRO_NORM || op.pro == PRO_EMBED_NORM;
-            const int P = op.N / 2;
-            const int R0 = 2 * (int)((long long)P * c / op.grid);
-            const int R = 2 * (int)((long long)P * (c + 1) / op.grid) - R0;
+            const int R0 = sh.R0, R = sh.R;
             // epilogue operands that do not depend on the products (residual rows, bias, RoPE
             // factors): thread t < npairs finishes pair t (rows 2t, 2t + 1) of a pass. Pass 0's are
             // loaded before the input wait, where their round trip costs nothing.
@@ -1256,7 +1256,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 psn = 0.f;
                 if (tid < rows_p / 2 && row < op.n_valid) {
                     if (op.epi == EPI_RESID) {
-                        if (op.lres == nullptr) {                   // layer 0: the token's embedding row
+                        if (!fin) {                                 // the partner adds the residual
+                        } else if (op.lres == nullptr) {                   // layer 0: the token's embedding row
                             const __half2 e2 = *reinterpret_cast<const __half2 *>(p.embed + (size_t)ss.token * p.hidden + row);
                             pre0 = __low2float(e2);
                             pre1 = __high2float(e2);
@@ -1357,7 +1358,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             } else if (op.pro == PRO_ATTN) {
                 ll_hilo_input(xh, xl, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
             } else if (q8) {
-                plain_digits(op.xin_h, op.xin_l, K, dg, bsc);
+                plain_digits(op.xin_h + sh.K0, op.xin_l + sh.K0, K, dg, bsc);
             } else {
                 // PRO_PLAIN: fp16 hi / lo vectors behind the dependency counter: every 16-byte piece
                 // in flight at once (cp.async through L2), one wait
@@ -1447,7 +1448,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 const float y1 =
                     q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
                 if (op.epi == EPI_RESID) {
-                    ll_st2(op.lout + row, ll_wordf(pre0 + y0, tag), ll_wordf(pre1 + y1, tag));
+                    if (!fin) {
+                        ll_st2(op.lksp + row, ll_wordf(y0, tag), ll_wordf(y1, tag));
+                    } else {
+                        float s0 = 0.f, s1 = 0.f;
+                        if (op.ksplit > 1) {                        // the partner CTA's partials
+                            uint64_t w[1][2];
+                            ll_poll<1>(w, 1u, [&](int) { return op.lksp + row; }, tag, ab);
+                            s0 = ll_f(w[0][0]);
+                            s1 = ll_f(w[0][1]);
+                        }
+                        ll_st2(op.lout + row, ll_wordf(pre0 + (y0 + s0), tag), ll_wordf(pre1 + (y1 + s1), tag));
+                    }
                 } else if (op.epi == EPI_LMHEAD) {
                     if (lg) lg[row] = y0;
                     if (y0 > bv) {
@@ -1566,32 +1578,34 @@ __global__ void k_pack_rows(uint8_t *dst, const __half *a, int rows_a, const __h
 }
 
 // Pack a blockwise-int8 N x K matrix (an fp16 scale per row and 32 inputs) into the step kernel's
-// int8 units; rows map as in k_pack_rows. CTA c's units start at c * cta_bytes, in (pass, chunk)
-// order. A unit of rows_p rows x wq inputs holds, per 32-input block, [half][row][16 bytes] (the
+// int8 units; CTA c holds its share (gemv_share: its row group's rows over its part of the inputs)
+// from c * cta_bytes, in (pass, chunk) order. A unit of rows_p rows x wq inputs holds, per 32-input block, [half][row][16 bytes] (the
 // tensor core's K-major core matrices, see unit_i8_issue), then the scales [row][block]. One
 // thread per row and 32-input block.
 __global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, int rows_a, const int8_t *b,
-                               const __half *bs, const int *row_of, int N, int K, int grid, int pass_rows,
-                               int chunk_w, int cta_bytes) {
+                               const __half *bs, const int *row_of, int N, int K, int grid, int ksplit,
+                               int pass_rows, int chunk_w, int cta_bytes) {
     const int nbk = K / 32;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)N * nbk) return;
     const int row = (int)(idx / nbk);
-    const int k = (int)(idx - (long long)row * nbk) * 32;
-    const int P = N / 2, pair = row / 2;
-    int c = (int)(((long long)pair * grid) / P);
-    while (c > 0 && (long long)P * c / grid > pair) --c;
-    while (c + 1 < grid && (long long)P * (c + 1) / grid <= pair) ++c;
-    const int R0 = 2 * (int)((long long)P * c / grid);
-    const int R = 2 * (int)((long long)P * (c + 1) / grid) - R0;
+    const int kg = (int)(idx - (long long)row * nbk) * 32;  // input of the whole row
+    const int P = N / 2, pair = row / 2, G = grid / ksplit;
+    int g = (int)(((long long)pair * G) / P);               // the row group owning the pair
+    while (g > 0 && (long long)P * g / G > pair) --g;
+    while (g + 1 < G && (long long)P * (g + 1) / G <= pair) ++g;
+    const int Kc = K / ksplit, c = g * ksplit + kg / Kc;     // the CTA owning the input's part
+    const int k = kg - (kg / Kc) * Kc;                       // input within the CTA's part
+    const GemvShare sh = gemv_share(N, K, grid, ksplit, c);
+    const int R0 = sh.R0, R = sh.R;
     const int lr = row - R0;
     const int pi = lr / pass_rows;
     const int rows_p = min(pass_rows, R - pi * pass_rows);
     const int qi = k / chunk_w;
-    const int wq = min(chunk_w, K - qi * chunk_w);
+    const int wq = min(chunk_w, Kc - qi * chunk_w);
     const int r = lr - pi * pass_rows;
     size_t pass_full = 0;                                  // bytes of a full pass (pass_rows rows)
-    for (int q0 = 0; q0 < K; q0 += chunk_w) pass_full += step_unit_bytes(WF_I8, pass_rows, min(chunk_w, K - q0));
+    for (int q0 = 0; q0 < Kc; q0 += chunk_w) pass_full += step_unit_bytes(WF_I8, pass_rows, min(chunk_w, Kc - q0));
     uint8_t *unit = dst + (size_t)c * cta_bytes + (size_t)pi * pass_full +
                     (size_t)qi * step_unit_bytes(WF_I8, rows_p, chunk_w);
     const int bl = (k - qi * chunk_w) / 32;                // block within the unit
@@ -1600,9 +1614,9 @@ __global__ void k_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as, 
     const int src = row_of[row];
     if (src >= 0) {
         const int8_t *rp = src < rows_a ? a + (size_t)src * K : b + (size_t)(src - rows_a) * K;
-        sc = src < rows_a ? as[(size_t)src * nbk + k / 32] : bs[(size_t)(src - rows_a) * nbk + k / 32];
-        v0 = *reinterpret_cast<const uint4 *>(rp + k);
-        v1 = *reinterpret_cast<const uint4 *>(rp + k + 16);
+        sc = src < rows_a ? as[(size_t)src * nbk + kg / 32] : bs[(size_t)(src - rows_a) * nbk + kg / 32];
+        v0 = *reinterpret_cast<const uint4 *>(rp + kg);
+        v1 = *reinterpret_cast<const uint4 *>(rp + kg + 16);
     }
     uint8_t *blk = unit + (size_t)bl * rows_p * 32;
     *reinterpret_cast<uint4 *>(blk + (size_t)r * 16) = v0;
@@ -1625,22 +1639,34 @@ static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
 }
 
 // Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
-// pass), each unit at most one stage.
-void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
+// pass), each unit at most one stage. An int8 op with a plain input whose CTAs would hold few rows
+// (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
+// MMA covers twice the rows and a CTA issues and reads back half the block MMAs and digitizes half
+// the input; the second CTA hands its row partials to the first.
+void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
     const int P = o.N / 2;
-    o.grid = std::max(1, std::min(num_sms, P));
-    const int rmax = 2 * ((P + o.grid - 1) / o.grid);                       // rows of the busiest CTA
     const bool i8 = o.fmt == WF_I8;
+    o.ksplit = 1;
+    o.grid = std::max(1, std::min(num_sms, P));
+    if (i8 && max_ksplit >= 2 && o.pro == PRO_PLAIN && o.K % 256 == 0 && num_sms >= 2) {
+        const int G = std::min(num_sms / 2, P);
+        if (2 * ((P + G - 1) / G) <= 64) {
+            o.ksplit = 2;
+            o.grid = 2 * G;
+        }
+    }
+    const int G = o.grid / o.ksplit, Kc = o.K / o.ksplit;
+    const int rmax = 2 * ((P + G - 1) / G);                                 // rows of the busiest CTA
     const int gran = i8 ? 64 : 256;                                          // chunk_w granule (int8: even blocks)
     long long best = -1;
     for (int pr = std::min(i8 ? kPassRowsI8 : kPassRows, rmax); pr >= 2; pr -= 2) {
         // widest unit within a stage (int8: at most kUnitBlocksI8 blocks, one TMEM column group each)
         int w = i8 ? std::min((stage_bytes - 16) / (pr + pr / 16 + 1), 32 * kUnitBlocksI8) : stage_bytes / (pr * 2);
         w = w / gran * gran;
-        if (w >= o.K) w = o.K;
-        if (w < gran && w != o.K) continue;
+        if (w >= Kc) w = Kc;
+        if (w < gran && w != Kc) continue;
         while (i8 && w > gran && step_unit_bytes(WF_I8, pr, w) > (uint32_t)stage_bytes) w -= gran;
-        const long long units = (long long)((rmax + pr - 1) / pr) * ((o.K + w - 1) / w);
+        const long long units = (long long)((rmax + pr - 1) / pr) * ((Kc + w - 1) / w);
         if (best < 0 || units < best) {
             best = units;
             o.pass_rows = pr;
@@ -1651,7 +1677,7 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes) {
         o.pass_rows = 2;
         o.chunk_w = gran;
     }
-    const size_t cb = i8 ? i8_rows_bytes(rmax, o.K, o.pass_rows, o.chunk_w) : 0;
+    const size_t cb = i8 ? i8_rows_bytes(rmax, Kc, o.pass_rows, o.chunk_w) : 0;
     o.cta_bytes = cb <= (size_t)INT_MAX ? (int)cb : -1;
 }
 
@@ -1661,6 +1687,8 @@ size_t step_gemv_bytes(const StepOp &o) {
 
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
     const bool i8 = o.fmt == WF_I8;
+    const int ks = std::max(o.ksplit, 1);
+    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || o.pro != PRO_PLAIN || o.K % (128 * ks)))) return false;
     if (i8 && (o.K % 128 || o.chunk_w % 64 || o.chunk_w > 32 * kUnitBlocksI8 || o.cta_bytes <= 0)) return false;
     if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
     return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 &&
@@ -1707,8 +1735,8 @@ cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as,
     if (plan.fmt != WF_I8 || plan.N % 2 || plan.K % 128 || plan.cta_bytes <= 0) return cudaErrorInvalidValue;
     const long long total = (long long)plan.N * (plan.K / 32);
     k_pack_rows_i8<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(dst, a, as, rows_a, b, bs, row_of, plan.N, plan.K,
-                                                                   plan.grid, plan.pass_rows, plan.chunk_w,
-                                                                   plan.cta_bytes);
+                                                                   plan.grid, std::max(plan.ksplit, 1),
+                                                                   plan.pass_rows, plan.chunk_w, plan.cta_bytes);
     return cudaGetLastError();
 }
 

@@ -111,6 +111,24 @@ def test_int8_qwen2_0_5b_shape_greedy():
     assert d is None, f"first divergence at {d}: margin there {margins[d]:.5f}"
 
 
+@pytest.mark.parametrize("ksplit", ["1", "2"])
+def test_int8_step_kernel_split_k_down(monkeypatch, ksplit):
+    """The down projection of the 0.5B shape with its inputs split over two CTAs (the second CTA's
+    row partials handed to the first as tagged words; the default) and unsplit, through the step
+    kernel on every prompt token, against the oracle's logits."""
+    from seedplane_b200.engine import CudaQwen2
+    monkeypatch.setenv("SEEDPLANE_PREFILL", "steps")
+    monkeypatch.setenv("SEEDPLANE_STEP_KSPLIT", ksplit)
+    cfg = QWEN2_0_5B
+    w = make_int8_blockwise(cfg, seed=1)
+    prompt = random_prompt(cfg.vocab, 6, seed=4)
+    eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
+    kv = eng.new_kv(32)
+    stepped, _ = eng.forward(kv, prompt, all_logits=True)
+    eng.close()
+    want, _ = OracleQwen2(cfg, w, kv_fp16=True).forward(prompt, None, all_logits=True)
+    assert_logits_close(stepped, want)
+
 
 def test_int8_prompt_through_step_kernel_matches_batched(monkeypatch):
     """The same prompt through the step kernel (one launch per token) and through the batched pass."""
