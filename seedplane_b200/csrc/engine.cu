@@ -126,7 +126,7 @@ struct sp_engine {
     // after down (xd), q, the new K/V rows, attention partials and output; the SwiGLU activation
     uint64_t *ll_xo = nullptr, *ll_xd = nullptr, *ll_q = nullptr, *ll_kv = nullptr, *ll_part = nullptr,
              *ll_attn = nullptr;
-    uint64_t *ll_ksp = nullptr;             // split-K down projection: the second CTA's row partials
+    uint64_t *ll_ksp = nullptr;             // split-K O / down projections: the second CTAs' row partials
     __half *act_h = nullptr, *act_l = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
@@ -266,6 +266,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
             o.lres_k = 5 * (l - 1) + 4;
         }
         o.lout = e->ll_xo + par * H;
+        o.lksp = e->ll_ksp + (2 * par) * H;
         ops.push_back(o);
         o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU);
         o.lin = e->ll_xo + par * H;
@@ -283,7 +284,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.lres = e->ll_xo + par * H;
         o.lres_k = 5 * l + 2;
         o.lout = e->ll_xd + par * H;
-        o.lksp = e->ll_ksp + par * H;
+        o.lksp = e->ll_ksp + (2 * par + 1) * H;
         ops.push_back(o);
     }
     StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD);
@@ -919,7 +920,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
-    const size_t w_llksp = wtake(2 * H * 8);
+    const size_t w_llksp = wtake(4 * H * 8);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);

@@ -251,7 +251,8 @@ struct StepLayout {
     size_t smem = 0;         // dynamic shared memory; stage_bytes == 0: does not fit
 };
 
-// fills grid, ksplit, pass_rows, chunk_w from N, K (ksplit 2 only for int8 PRO_PLAIN ops, at most max_ksplit)
+// fills grid, ksplit, pass_rows, chunk_w from N, K (ksplit 2 only for int8 PRO_PLAIN / PRO_ATTN ops,
+// at most max_ksplit)
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit = 1);
 bool step_gemv_supported(const StepOp &o, int stage_bytes);
 size_t step_gemv_bytes(const StepOp &o);                           // packed bytes of a planned GEMV

@@ -1354,7 +1354,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     }
                 }
             } else if (q8 && op.pro == PRO_ATTN) {
-                attn_digits(op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab, dg, bsc);
+                attn_digits(op.lin + sh.K0, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab, dg, bsc);
             } else if (op.pro == PRO_ATTN) {
                 ll_hilo_input(xh, xl, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
             } else if (q8) {
@@ -1639,8 +1639,8 @@ static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
 }
 
 // Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
-// pass), each unit at most one stage. An int8 op with a plain input whose CTAs would hold few rows
-// (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
+// pass), each unit at most one stage. An int8 op with a plain or attention input whose CTAs would
+// hold few rows (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
 // MMA covers twice the rows and a CTA issues and reads back half the block MMAs and digitizes half
 // the input; the second CTA hands its row partials to the first.
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
@@ -1648,7 +1648,7 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
     const bool i8 = o.fmt == WF_I8;
     o.ksplit = 1;
     o.grid = std::max(1, std::min(num_sms, P));
-    if (i8 && max_ksplit >= 2 && o.pro == PRO_PLAIN && o.K % 256 == 0 && num_sms >= 2) {
+    if (i8 && max_ksplit >= 2 && (o.pro == PRO_PLAIN || o.pro == PRO_ATTN) && o.K % 256 == 0 && num_sms >= 2) {
         const int G = std::min(num_sms / 2, P);
         if (2 * ((P + G - 1) / G) <= 64) {
             o.ksplit = 2;
@@ -1688,7 +1688,8 @@ size_t step_gemv_bytes(const StepOp &o) {
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
     const bool i8 = o.fmt == WF_I8;
     const int ks = std::max(o.ksplit, 1);
-    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || o.pro != PRO_PLAIN || o.K % (128 * ks)))) return false;
+    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || (o.pro != PRO_PLAIN && o.pro != PRO_ATTN) || o.K % (128 * ks))))
+        return false;
     if (i8 && (o.K % 128 || o.chunk_w % 64 || o.chunk_w > 32 * kUnitBlocksI8 || o.cta_bytes <= 0)) return false;
     if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
     return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 &&
