@@ -126,7 +126,8 @@ struct sp_engine {
     // after down (xd), q, the new K/V rows, attention partials and output; the SwiGLU activation
     uint64_t *ll_xo = nullptr, *ll_xd = nullptr, *ll_q = nullptr, *ll_kv = nullptr, *ll_part = nullptr,
              *ll_attn = nullptr;
-    uint64_t *ll_ksp = nullptr;             // split-K O / down projections: the second CTAs' row partials
+    uint64_t *ll_ksp = nullptr;             // split-K GEMVs: the second CTAs' row partials, per parity
+                                            // [O: H][down: H][QKV: q + k + v rows][gate_up: 2 I]
     __half *act_h = nullptr, *act_l = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
@@ -243,6 +244,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.bias = L.qkv_b;
         o.lout = e->ll_q + par * nq;
         o.lkv = e->ll_kv + par * nkv;
+        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + 2 * H;
         o.kc = kc;
         o.vc = vc;
         ops.push_back(o);
@@ -266,7 +268,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
             o.lres_k = 5 * (l - 1) + 4;
         }
         o.lout = e->ll_xo + par * H;
-        o.lksp = e->ll_ksp + (2 * par) * H;
+        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I);
         ops.push_back(o);
         o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU);
         o.lin = e->ll_xo + par * H;
@@ -274,6 +276,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.gain = L.post_norm;
         o.out_h = e->act_h + par * 2 * I;
         o.out_l = e->act_l + par * 2 * I;
+        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + 2 * H + nq + 2 * nkv;
         o.sig = 5 * l + 3;
         ops.push_back(o);
         o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID);
@@ -284,7 +287,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.lres = e->ll_xo + par * H;
         o.lres_k = 5 * l + 2;
         o.lout = e->ll_xd + par * H;
-        o.lksp = e->ll_ksp + (2 * par + 1) * H;
+        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + H;
         ops.push_back(o);
     }
     StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD);
@@ -302,6 +305,9 @@ int ensure_step_ops(sp_engine *e, sp_kv *kv, StepOp **out) {
         return SP_OK;
     }
     const std::vector<StepOp> ops = build_step_ops(e, kv);
+    for (const StepOp &o : ops)            // a split GEMV's second CTAs store their partials through lksp
+        if (o.kind == OP_GEMV && o.ksplit > 1 && o.lksp == nullptr)
+            return fail(SP_ERR_UNSUPPORTED, "step op table: a split GEMV (N=%d K=%d) has no partials buffer", o.N, o.K);
     StepOp *d = nullptr;
     SP_CUDA(cudaMalloc(&d, ops.size() * sizeof(StepOp)));
     cudaError_t ce = cudaMemcpy(d, ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice);
@@ -574,22 +580,23 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             return fail(SP_ERR_UNSUPPORTED, "step kernel: the input vector of %d floats leaves no room for the ring",
                         e->step_xmax);
         }
-        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, bool q8) {
+        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, int epi, bool q8) {
             StepOp o{};
             o.kind = OP_GEMV;
             o.fmt = q8 ? WF_I8 : WF_F16;
             o.pro = pro;
+            o.epi = epi;
             o.N = (int)N;
             o.K = (int)K;
             o.n_valid = (int)n_valid;
             plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes, (int)env_long("SEEDPLANE_STEP_KSPLIT", 2));
             return o;
         };
-        e->s_qkv = sbase(QRp, H, QR, PRO_NORM, i8);
-        e->s_o = sbase(Hp, H, H, PRO_ATTN, i8);
-        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM, i8);
-        e->s_down = sbase(Hp, I, H, PRO_PLAIN, i8);
-        e->s_head = sbase(VP, H, V, PRO_NORM, i8 && !c.tied_embeddings);   // a tied head is the fp16 embedding
+        e->s_qkv = sbase(QRp, H, QR, PRO_NORM, EPI_QKV, i8);
+        e->s_o = sbase(Hp, H, H, PRO_ATTN, EPI_RESID, i8);
+        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM, EPI_SWIGLU, i8);
+        e->s_down = sbase(Hp, I, H, PRO_PLAIN, EPI_RESID, i8);
+        e->s_head = sbase(VP, H, V, PRO_NORM, EPI_LMHEAD, i8 && !c.tied_embeddings);   // a tied head is the fp16 embedding
         for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
             if (!step_gemv_supported(*o, e->step_lay.stage_bytes)) {
                 delete e;
@@ -920,7 +927,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
-    const size_t w_llksp = wtake(4 * H * 8);
+    const size_t w_llksp = wtake(2 * (2 * H + (size_t)(c.heads + 2 * c.kv_heads) * HD + 2 * I) * 8);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);

@@ -136,11 +136,11 @@ SP_DEVINL void unit_mma(float (&d)[4][4], uint32_t unit, int rs, int nks, int ro
 // digits (rows 4-7, the next 64 bytes, give output columns that are not read). The block's scale
 // goes to bsc[k / 32]. The 32 inputs of a block are the float4s of 8 consecutive lanes (lane & 7 =
 // position in the block); the whole warp calls digitize4_n.
-// This thread's N float4s, x[u] = inputs k0 + u * kstride .. + 3 for u < nvalid (warp-uniform),
-// into digits: the N block maxima first (N shuffle chains interleaved after one reconvergence),
+// This thread's N float4s, x[u] = inputs k0 + u * kstride .. + 3 for the u with bit u of vmask set
+// (warp-uniform), into digits: the N block maxima first (N shuffle chains interleaved after one reconvergence),
 // then the N conversions; one float4 at a time would serialise N latency chains.
 template <int N>
-SP_DEVINL void digitize4_n(const float4 (&x)[N], int k0, int kstride, int nvalid, int8_t *dg, float *bsc) {
+SP_DEVINL void digitize4_n(const float4 (&x)[N], int k0, int kstride, uint32_t vmask, int8_t *dg, float *bsc) {
     float m[N];
 #pragma unroll
     for (int u = 0; u < N; ++u) m[u] = fmaxf(fmaxf(fabsf(x[u].x), fabsf(x[u].y)), fmaxf(fabsf(x[u].z), fabsf(x[u].w)));
@@ -151,7 +151,7 @@ SP_DEVINL void digitize4_n(const float4 (&x)[N], int k0, int kstride, int nvalid
         for (int u = 0; u < N; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], sh));
 #pragma unroll
     for (int u = 0; u < N; ++u) {
-        if (u < nvalid) {
+        if ((vmask >> u) & 1u) {
             const int k = k0 + u * kstride;
             // biased exponent of m, at least 26 (blocks below 2^-101 become zero: multiplier 2^127)
             const int eb = max((int)((__float_as_uint(m[u]) >> 23) & 0xffu), 26);
@@ -480,7 +480,7 @@ __device__ __noinline__ void attn_digits(const uint64_t *lin, int K, uint32_t ta
             nvalid = q + 1;
         }
     }
-    digitize4_n<kNormRegs>(xs, 4 * tid, 4 * kEpiThreads, nvalid, dg, bsc);
+    digitize4_n<kNormRegs>(xs, 4 * tid, 4 * kEpiThreads, (1u << nvalid) - 1u, dg, bsc);
 }
 
 // PRO_PLAIN into digits: the fp16 hi / lo vectors behind the counter (written by other CTAs in
@@ -520,7 +520,7 @@ __device__ __noinline__ void plain_digits(const __half *xin_h, const __half *xin
                 nvalid = u + 1;
             }
         }
-        digitize4_n<kPlainBatch>(xs, 4 * i0, 4 * kEpiThreads, nvalid, dg, bsc);
+        digitize4_n<kPlainBatch>(xs, 4 * i0, 4 * kEpiThreads, (1u << nvalid) - 1u, dg, bsc);
     }
 }
 
@@ -1236,6 +1236,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             stamp_clk(p.trace, k, C, c, 0);
             const GemvShare sh = gemv_share(op.N, op.K, op.grid, op.ksplit, c);
             const int K = sh.Kc;                 // this CTA's inputs: [sh.K0, sh.K0 + K) of op.K
+            const int KF = op.K;                 // the whole input (a norm prologue normalizes all of it)
             const bool fin = sh.K0 == 0;         // finishes its rows (ksplit 2: adds the partner's partials)
             __half *xl = xh + K;
             // int8 weights: the input's digit rows (stride K + 16 bytes) and block scales instead
@@ -1287,7 +1288,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
 #pragma unroll
                 for (int q = 0; q < kNormRegs; ++q) {
                     const int i = tid + q * kEpiThreads;
-                    gn[q] = 4 * i < K ? __ldg(reinterpret_cast<const float4 *>(op.gain) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    gn[q] = 4 * i < KF ? __ldg(reinterpret_cast<const float4 *>(op.gain) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
             if (op.dep >= 0) {
@@ -1307,21 +1308,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
 #pragma unroll
                     for (int q = 0; q < kNormRegs; ++q) {
                         const int i = tid + q * kEpiThreads;
-                        if (4 * i < K) {
-                            const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(p.embed + (size_t)ss.token * K) + i);
+                        if (4 * i < KF) {
+                            const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(p.embed + (size_t)ss.token * KF) + i);
                             const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
                             const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
                             v[q] = make_float4(a.x, a.y, b.x, b.y);
                         }
                     }
                 } else {
-                    ll_norm_input<false>(v, op.lin, K, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
+                    ll_norm_input<false>(v, op.lin, KF, ll_tag(ss.epoch, p.n_ops, op.lin_k), ab);
                 }
                 __syncwarp();
                 float sq = 0.f;
 #pragma unroll
                 for (int q = 0; q < kNormRegs; ++q) {
-                    if (4 * (tid + q * kEpiThreads) < K) {
+                    if (4 * (tid + q * kEpiThreads) < KF) {
                         sq = fmaf(v[q].x, v[q].x, sq);
                         sq = fmaf(v[q].y, v[q].y, sq);
                         sq = fmaf(v[q].z, v[q].z, sq);
@@ -1331,18 +1332,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 sq = warp_sum(sq);
                 if (lane == 0) s_val[warp] = sq;
                 epi_sync();
-                const float inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)K + p.eps);
+                const float inv = 1.0f / sqrtf((s_val[0] + s_val[1] + s_val[2] + s_val[3]) / (float)KF + p.eps);
                 if (Q8 && q8) {
-                    int nvalid = 0;
+                    // the whole vector is normalized; this CTA's inputs [sh.K0, sh.K0 + K) become digits
+                    uint32_t vm = 0u;
 #pragma unroll
                     for (int q = 0; q < kNormRegs; ++q) {
-                        if (4 * (tid + q * kEpiThreads) < K) {      // warp-uniform (K % 128 == 0 for int8)
+                        const int i4 = 4 * (tid + q * kEpiThreads) - sh.K0;
+                        if (i4 >= 0 && i4 < K) {                    // warp-uniform (K0, K multiples of 128)
                             v[q] = make_float4((v[q].x * inv) * gn[q].x, (v[q].y * inv) * gn[q].y,
                                                (v[q].z * inv) * gn[q].z, (v[q].w * inv) * gn[q].w);
-                            nvalid = q + 1;
+                            vm |= 1u << q;
                         }
                     }
-                    digitize4_n<kNormRegs>(v, 4 * tid, 4 * kEpiThreads, nvalid, dg, bsc);
+                    digitize4_n<kNormRegs>(v, 4 * tid - sh.K0, 4 * kEpiThreads, vm, dg, bsc);
                 } else {
 #pragma unroll
                     for (int q = 0; q < kNormRegs; ++q) {
@@ -1444,22 +1447,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 epi_sync();
                 if (!mine) continue;
                 const int r2 = 2 * tid;
-                const float y0 = q8 ? (&red[0][0])[r2] : ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
-                const float y1 =
-                    q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
-                if (op.epi == EPI_RESID) {
+                float y0 = q8 ? (&red[0][0])[r2] : ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
+                float y1 = q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
+                if (op.ksplit > 1) {
+                    // split inputs: the second CTA of the pair hands its row partials to the first,
+                    // which adds them and runs the epilogue
                     if (!fin) {
                         ll_st2(op.lksp + row, ll_wordf(y0, tag), ll_wordf(y1, tag));
-                    } else {
-                        float s0 = 0.f, s1 = 0.f;
-                        if (op.ksplit > 1) {                        // the partner CTA's partials
-                            uint64_t w[1][2];
-                            ll_poll<1>(w, 1u, [&](int) { return op.lksp + row; }, tag, ab);
-                            s0 = ll_f(w[0][0]);
-                            s1 = ll_f(w[0][1]);
-                        }
-                        ll_st2(op.lout + row, ll_wordf(pre0 + (y0 + s0), tag), ll_wordf(pre1 + (y1 + s1), tag));
+                        continue;
                     }
+                    uint64_t w[1][2];
+                    ll_poll<1>(w, 1u, [&](int) { return op.lksp + row; }, tag, ab);
+                    y0 += ll_f(w[0][0]);
+                    y1 += ll_f(w[0][1]);
+                }
+                if (op.epi == EPI_RESID) {
+                    ll_st2(op.lout + row, ll_wordf(pre0 + y0, tag), ll_wordf(pre1 + y1, tag));
                 } else if (op.epi == EPI_LMHEAD) {
                     if (lg) lg[row] = y0;
                     if (y0 > bv) {
@@ -1639,8 +1642,8 @@ static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
 }
 
 // Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
-// pass), each unit at most one stage. An int8 op with a plain or attention input whose CTAs would
-// hold few rows (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
+// pass), each unit at most one stage. An int8 op (not the LM head) whose CTAs would hold few rows
+// (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
 // MMA covers twice the rows and a CTA issues and reads back half the block MMAs and digitizes half
 // the input; the second CTA hands its row partials to the first.
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
@@ -1648,7 +1651,7 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
     const bool i8 = o.fmt == WF_I8;
     o.ksplit = 1;
     o.grid = std::max(1, std::min(num_sms, P));
-    if (i8 && max_ksplit >= 2 && (o.pro == PRO_PLAIN || o.pro == PRO_ATTN) && o.K % 256 == 0 && num_sms >= 2) {
+    if (i8 && max_ksplit >= 2 && o.epi != EPI_LMHEAD && o.K % 256 == 0 && num_sms >= 2) {
         const int G = std::min(num_sms / 2, P);
         if (2 * ((P + G - 1) / G) <= 64) {
             o.ksplit = 2;
@@ -1688,8 +1691,7 @@ size_t step_gemv_bytes(const StepOp &o) {
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
     const bool i8 = o.fmt == WF_I8;
     const int ks = std::max(o.ksplit, 1);
-    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || (o.pro != PRO_PLAIN && o.pro != PRO_ATTN) || o.K % (128 * ks))))
-        return false;
+    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || o.epi == EPI_LMHEAD || o.K % (128 * ks)))) return false;
     if (i8 && (o.K % 128 || o.chunk_w % 64 || o.chunk_w > 32 * kUnitBlocksI8 || o.cta_bytes <= 0)) return false;
     if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
     return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 &&
