@@ -567,9 +567,27 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t padq = e->step_kernel ? rowpad : 1;
     const size_t QRp = align_up(QR, padq), Hp = align_up(H, padq), GUp = align_up(2 * I, padq);
     if (e->step_kernel) {
-        // shared-memory layout first (its stage size bounds the units), then the row-block plans
-        // (the packing depends on them)
-        e->step_xmax = (int)align_up(std::max({H, I, (size_t)c.heads * HD}), 8);
+        // the input splits first (they depend on the shapes only), then the shared-memory layout
+        // (a CTA's share of the largest input sizes its vector region; the stage size bounds the
+        // units), then the row-block plans (the packing depends on them)
+        const int max_ks = (int)env_long("SEEDPLANE_STEP_KSPLIT", 2);
+        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, int epi, bool q8, int stage_bytes) {
+            StepOp o{};
+            o.kind = OP_GEMV;
+            o.fmt = q8 ? WF_I8 : WF_F16;
+            o.pro = pro;
+            o.epi = epi;
+            o.N = (int)N;
+            o.K = (int)K;
+            o.n_valid = (int)n_valid;
+            plan_step_gemv(o, e->num_sms, stage_bytes, max_ks);
+            return o;
+        };
+        auto share_k = [&](size_t N, size_t K, int pro, int epi) {
+            return K / (size_t)std::max(sbase(N, K, N, pro, epi, i8, 64 * 1024).ksplit, 1);   // any stage size
+        };
+        e->step_xmax = (int)align_up(std::max({H, share_k(Hp, I, PRO_PLAIN, EPI_RESID),
+                                               share_k(Hp, (size_t)c.heads * HD, PRO_ATTN, EPI_RESID)}), 8);
         const int want = (int)env_long("SEEDPLANE_STEP_STAGES", 3);
         e->step_inflight = (int)env_long("SEEDPLANE_STEP_INFLIGHT", 0);
         e->step_l2_ahead = (int)env_long("SEEDPLANE_STEP_L2_KB", 0) * 1024;
@@ -580,28 +598,21 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
             return fail(SP_ERR_UNSUPPORTED, "step kernel: the input vector of %d floats leaves no room for the ring",
                         e->step_xmax);
         }
-        auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, int epi, bool q8) {
-            StepOp o{};
-            o.kind = OP_GEMV;
-            o.fmt = q8 ? WF_I8 : WF_F16;
-            o.pro = pro;
-            o.epi = epi;
-            o.N = (int)N;
-            o.K = (int)K;
-            o.n_valid = (int)n_valid;
-            plan_step_gemv(o, e->num_sms, e->step_lay.stage_bytes, (int)env_long("SEEDPLANE_STEP_KSPLIT", 2));
-            return o;
-        };
-        e->s_qkv = sbase(QRp, H, QR, PRO_NORM, EPI_QKV, i8);
-        e->s_o = sbase(Hp, H, H, PRO_ATTN, EPI_RESID, i8);
-        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM, EPI_SWIGLU, i8);
-        e->s_down = sbase(Hp, I, H, PRO_PLAIN, EPI_RESID, i8);
-        e->s_head = sbase(VP, H, V, PRO_NORM, EPI_LMHEAD, i8 && !c.tied_embeddings);   // a tied head is the fp16 embedding
-        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head})
-            if (!step_gemv_supported(*o, e->step_lay.stage_bytes)) {
+        const int sb = e->step_lay.stage_bytes;
+        e->s_qkv = sbase(QRp, H, QR, PRO_NORM, EPI_QKV, i8, sb);
+        e->s_o = sbase(Hp, H, H, PRO_ATTN, EPI_RESID, i8, sb);
+        e->s_gu = sbase(GUp, H, 2 * I, PRO_NORM, EPI_SWIGLU, i8, sb);
+        e->s_down = sbase(Hp, I, H, PRO_PLAIN, EPI_RESID, i8, sb);
+        e->s_head = sbase(VP, H, V, PRO_NORM, EPI_LMHEAD, i8 && !c.tied_embeddings, sb);   // a tied head is the fp16 embedding
+        for (const StepOp *o : {&e->s_qkv, &e->s_o, &e->s_gu, &e->s_down, &e->s_head}) {
+            // a CTA's input share in the vector region: int8 digits and block scales, or fp16 halves
+            const size_t kc = (size_t)o->K / std::max(o->ksplit, 1);
+            const size_t in = o->fmt == WF_I8 ? 4 * (kc + 16) + kc / 8 : 4 * (size_t)o->K;
+            if (!step_gemv_supported(*o, e->step_lay.stage_bytes) || in > (size_t)e->step_lay.vec_bytes) {
                 delete e;
                 return fail(SP_ERR_UNSUPPORTED, "step GEMV of N=%d K=%d is not supported", o->N, o->K);
             }
+        }
     }
     // ---- arena: [weight stream][embed][small tensors] ------------------------------------------
     size_t off = 0;
