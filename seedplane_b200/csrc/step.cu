@@ -1641,8 +1641,9 @@ static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
     return b;
 }
 
-// Rows per pass and inputs per unit: the fewest units for the busiest CTA (ties: more rows per
-// pass), each unit at most one stage. An int8 op (not the LM head) whose CTAs would hold few rows
+// Rows per pass and inputs per unit, each unit at most one stage: for fp16 the fewest units for
+// the busiest CTA (ties: more rows per pass); for int8 the least tensor-core time, every 32-input
+// block of a pass one MMA (~48 cycles at M = 128, ~32 at M = 64) plus ~1,000 cycles a unit. An int8 op (not the LM head) whose CTAs would hold few rows
 // (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
 // MMA covers twice the rows and a CTA issues and reads back half the block MMAs and digitizes half
 // the input; the second CTA hands its row partials to the first.
@@ -1669,9 +1670,10 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
         if (w >= Kc) w = Kc;
         if (w < gran && w != Kc) continue;
         while (i8 && w > gran && step_unit_bytes(WF_I8, pr, w) > (uint32_t)stage_bytes) w -= gran;
-        const long long units = (long long)((rmax + pr - 1) / pr) * ((Kc + w - 1) / w);
-        if (best < 0 || units < best) {
-            best = units;
+        const long long passes = (rmax + pr - 1) / pr, units = passes * ((Kc + w - 1) / w);
+        const long long cost = i8 ? passes * (Kc / 32) * (pr > 64 ? 48 : 32) + units * 1000 : units;
+        if (best < 0 || cost < best) {
+            best = cost;
             o.pass_rows = pr;
             o.chunk_w = w;
         }
