@@ -1234,7 +1234,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             stamp_clk(p.trace, k, C, c, 0);
-            const GemvShare sh = gemv_share(op.N, op.K, op.grid, op.ksplit, c);
+            // split inputs exist for int8 units only: the fp16 build keeps the unsplit code (the split
+            // branches cost its decode step ~4.5 %)
+            const GemvShare sh = gemv_share(op.N, op.K, op.grid, Q8 ? op.ksplit : 1, c);
             const int K = sh.Kc;                 // this CTA's inputs: [sh.K0, sh.K0 + K) of op.K
             const int KF = op.K;                 // the whole input (a norm prologue normalizes all of it)
             const bool fin = sh.K0 == 0;         // finishes its rows (ksplit 2: adds the partner's partials)
@@ -1449,7 +1451,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 const int r2 = 2 * tid;
                 float y0 = q8 ? (&red[0][0])[r2] : ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
                 float y1 = q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
-                if (op.ksplit > 1) {
+                if (Q8 && op.ksplit > 1) {
                     // split inputs: the second CTA of the pair hands its row partials to the first,
                     // which adds them and runs the epilogue
                     if (!fin) {
