@@ -126,8 +126,8 @@ struct sp_engine {
     // after down (xd), q, the new K/V rows, attention partials and output; the SwiGLU activation
     uint64_t *ll_xo = nullptr, *ll_xd = nullptr, *ll_q = nullptr, *ll_kv = nullptr, *ll_part = nullptr,
              *ll_attn = nullptr;
-    uint64_t *ll_ksp = nullptr;             // split-K GEMVs: the second CTAs' row partials, per parity
-                                            // [O: H][down: H][QKV: q + k + v rows][gate_up: 2 I]
+    uint64_t *ll_ksp = nullptr;             // split GEMVs' row partials, per parity: for O, down, QKV,
+                                            // gate_up kMaxKsplit - 1 regions of the op's N words
     __half *act_h = nullptr, *act_l = nullptr;
     std::map<sp_kv *, StepOp *> step_ops;   // device op table per cache (its K/V pointers)
     int n_step_ops = 0;
@@ -221,6 +221,11 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
     const size_t nq = (size_t)c.heads * HD, nkv = (size_t)c.kv_heads * HD;
     const size_t npart = (size_t)c.heads * e->step_max_chunks * (HD + 2);
     std::vector<StepOp> ops;
+    // split-GEMV partials, per layer parity: kMaxKsplit - 1 regions of N words for each op kind
+    const size_t ksp_o = 0, ksp_down = ksp_o + (kMaxKsplit - 1) * (size_t)e->s_o.N;
+    const size_t ksp_qkv = ksp_down + (kMaxKsplit - 1) * (size_t)e->s_down.N;
+    const size_t ksp_gu = ksp_qkv + (kMaxKsplit - 1) * (size_t)e->s_qkv.N;
+    const size_t ksp_par = ksp_gu + (kMaxKsplit - 1) * (size_t)e->s_gu.N;
     auto gemv = [&](const StepOp &plan, const uint8_t *w, int pro, int epi) {
         StepOp o = plan;
         o.kind = OP_GEMV;
@@ -244,7 +249,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.bias = L.qkv_b;
         o.lout = e->ll_q + par * nq;
         o.lkv = e->ll_kv + par * nkv;
-        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + 2 * H;
+        o.lksp = e->ll_ksp + par * ksp_par + ksp_qkv;
         o.kc = kc;
         o.vc = vc;
         ops.push_back(o);
@@ -268,7 +273,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
             o.lres_k = 5 * (l - 1) + 4;
         }
         o.lout = e->ll_xo + par * H;
-        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I);
+        o.lksp = e->ll_ksp + par * ksp_par + ksp_o;
         ops.push_back(o);
         o = gemv(e->s_gu, L.gate_up, PRO_NORM, EPI_SWIGLU);
         o.lin = e->ll_xo + par * H;
@@ -276,7 +281,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.gain = L.post_norm;
         o.out_h = e->act_h + par * 2 * I;
         o.out_l = e->act_l + par * 2 * I;
-        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + 2 * H + nq + 2 * nkv;
+        o.lksp = e->ll_ksp + par * ksp_par + ksp_gu;
         o.sig = 5 * l + 3;
         ops.push_back(o);
         o = gemv(e->s_down, L.down, PRO_PLAIN, EPI_RESID);
@@ -287,7 +292,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
         o.lres = e->ll_xo + par * H;
         o.lres_k = 5 * l + 2;
         o.lout = e->ll_xd + par * H;
-        o.lksp = e->ll_ksp + par * (2 * H + nq + 2 * nkv + 2 * I) + H;
+        o.lksp = e->ll_ksp + par * ksp_par + ksp_down;
         ops.push_back(o);
     }
     StepOp o = gemv(e->s_head, e->head, PRO_NORM, EPI_LMHEAD);
@@ -570,7 +575,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         // the input splits first (they depend on the shapes only), then the shared-memory layout
         // (a CTA's share of the largest input sizes its vector region; the stage size bounds the
         // units), then the row-block plans (the packing depends on them)
-        const int max_ks = (int)env_long("SEEDPLANE_STEP_KSPLIT", 2);
+        const int max_ks = (int)env_long("SEEDPLANE_STEP_KSPLIT", kMaxKsplit);
         auto sbase = [&](size_t N, size_t K, size_t n_valid, int pro, int epi, bool q8, int stage_bytes) {
             StepOp o{};
             o.kind = OP_GEMV;
@@ -938,7 +943,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
-    const size_t w_llksp = wtake(2 * (2 * H + (size_t)(c.heads + 2 * c.kv_heads) * HD + 2 * I) * 8);
+    const size_t w_llksp = wtake(2 * (kMaxKsplit - 1) *
+                                 ((size_t)e->s_o.N + e->s_down.N + e->s_qkv.N + e->s_gu.N) * 8);
     e->ws_clear_bytes = woff;
     const size_t w_x = wtake(H * 4), w_q = wtake((size_t)c.heads * HD * 4);
     const size_t w_attn = wtake((size_t)c.heads * HD * 4), w_act = wtake(I * 4);

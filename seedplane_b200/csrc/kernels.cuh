@@ -200,9 +200,9 @@ struct StepOp {
     int sig;                 // cnt[sig] += 1 per CTA; < 0: none
     int fmt;                 // WeightFmt of w
     int cta_bytes;           // WF_I8: bytes of one CTA's rows (CTA c's units start at c * cta_bytes)
-    int ksplit;              // CTAs sharing a row group, each over K / ksplit inputs (WF_I8, EPI_RESID)
+    int ksplit;              // CTAs sharing a row group, each over K / ksplit inputs (WF_I8; 1, 2 or 4)
     int pad_;
-    uint64_t *lksp;          // ksplit 2: the second CTA's row partials for the first, LL words [N]
+    uint64_t *lksp;          // split: CTA h > 0's row partials for CTA 0, LL words [ksplit - 1][N]
 };
 static_assert(sizeof(StepOp) % 16 == 0, "ops are copied to shared memory in 16-byte words");
 
@@ -251,8 +251,9 @@ struct StepLayout {
     size_t smem = 0;         // dynamic shared memory; stage_bytes == 0: does not fit
 };
 
-// fills grid, ksplit, pass_rows, chunk_w from N, K (ksplit 2 only for int8 PRO_PLAIN / PRO_ATTN ops,
-// at most max_ksplit)
+constexpr int kMaxKsplit = 4;            // CTAs a row group of a split int8 GEMV at most
+// fills grid, ksplit, pass_rows, chunk_w from N, K (ksplit > 1 only for int8 ops other than the LM
+// head, at most max_ksplit)
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit = 1);
 bool step_gemv_supported(const StepOp &o, int stage_bytes);
 size_t step_gemv_bytes(const StepOp &o);                           // packed bytes of a planned GEMV

@@ -1239,7 +1239,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             const GemvShare sh = gemv_share(op.N, op.K, op.grid, Q8 ? op.ksplit : 1, c);
             const int K = sh.Kc;                 // this CTA's inputs: [sh.K0, sh.K0 + K) of op.K
             const int KF = op.K;                 // the whole input (a norm prologue normalizes all of it)
-            const bool fin = sh.K0 == 0;         // finishes its rows (ksplit 2: adds the partner's partials)
+            const bool fin = sh.K0 == 0;         // finishes its rows (split: adds the partners' partials)
             __half *xl = xh + K;
             // int8 weights: the input's digit rows (stride K + 16 bytes) and block scales instead
             int8_t *dg = reinterpret_cast<int8_t *>(vec);
@@ -1452,16 +1452,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                 float y0 = q8 ? (&red[0][0])[r2] : ((red[0][r2] + red[1][r2]) + red[2][r2]) + red[3][r2];
                 float y1 = q8 ? (&red[0][0])[r2 + 1] : ((red[0][r2 + 1] + red[1][r2 + 1]) + red[2][r2 + 1]) + red[3][r2 + 1];
                 if (Q8 && op.ksplit > 1) {
-                    // split inputs: the second CTA of the pair hands its row partials to the first,
-                    // which adds them and runs the epilogue
+                    // split inputs: CTA h > 0 of the row group hands its row partials to CTA 0
+                    // (region h - 1 of lksp, op.N words each), which adds them in h order and runs
+                    // the epilogue
                     if (!fin) {
-                        ll_st2(op.lksp + row, ll_wordf(y0, tag), ll_wordf(y1, tag));
+                        ll_st2(op.lksp + (size_t)(sh.K0 / K - 1) * op.N + row, ll_wordf(y0, tag), ll_wordf(y1, tag));
                         continue;
                     }
-                    uint64_t w[1][2];
-                    ll_poll<1>(w, 1u, [&](int) { return op.lksp + row; }, tag, ab);
-                    y0 += ll_f(w[0][0]);
-                    y1 += ll_f(w[0][1]);
+                    uint64_t w[kMaxKsplit - 1][2];
+                    ll_poll<kMaxKsplit - 1>(w, (1u << (op.ksplit - 1)) - 1u,
+                                            [&](int j) { return op.lksp + (size_t)j * op.N + row; }, tag, ab);
+#pragma unroll
+                    for (int j = 0; j < kMaxKsplit - 1; ++j)
+                        if (j < op.ksplit - 1) {
+                            y0 += ll_f(w[j][0]);
+                            y1 += ll_f(w[j][1]);
+                        }
                 }
                 if (op.epi == EPI_RESID) {
                     ll_st2(op.lout + row, ll_wordf(pre0 + y0, tag), ll_wordf(pre1 + y1, tag));
@@ -1645,10 +1651,12 @@ static size_t i8_rows_bytes(int R, int K, int pass_rows, int chunk_w) {
 
 // Rows per pass and inputs per unit, each unit at most one stage: for fp16 the fewest units for
 // the busiest CTA (ties: more rows per pass); for int8 the least tensor-core time, every 32-input
-// block of a pass one MMA (~48 cycles at M = 128, ~32 at M = 64) plus ~1,000 cycles a unit. An int8 op (not the LM head) whose CTAs would hold few rows
-// (<= 32) is split over its inputs: two CTAs share a row group, each over half of K, so a block
-// MMA covers twice the rows and a CTA issues and reads back half the block MMAs and digitizes half
-// the input; the second CTA hands its row partials to the first.
+// block of a pass one MMA (~48 cycles at M = 128, ~32 at M = 64) plus ~1,000 cycles a unit.
+// An int8 op (not the LM head) whose CTAs would hold few rows (<= 32) is split over its inputs:
+// two CTAs share a row group, each over half of K, so a block MMA covers twice the rows and a CTA
+// issues and reads back half the block MMAs and digitizes half the input; the second CTA hands
+// its row partials to the first. A long input (K >= 16,384, or any K when max_ksplit >= 8) is
+// split four ways when a row group then fits one M = 128 pass.
 void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
     const int P = o.N / 2;
     const bool i8 = o.fmt == WF_I8;
@@ -1659,6 +1667,13 @@ void plan_step_gemv(StepOp &o, int num_sms, int stage_bytes, int max_ksplit) {
         if (2 * ((P + G - 1) / G) <= 64) {
             o.ksplit = 2;
             o.grid = 2 * G;
+        }
+    }
+    if (o.ksplit == 2 && max_ksplit >= 4 && o.K % 512 == 0 && num_sms >= 4 && (o.K >= 16384 || max_ksplit >= 8)) {
+        const int G = std::min(num_sms / 4, P);
+        if (2 * ((P + G - 1) / G) <= kPassRowsI8) {
+            o.ksplit = 4;
+            o.grid = 4 * G;
         }
     }
     const int G = o.grid / o.ksplit, Kc = o.K / o.ksplit;
@@ -1695,7 +1710,8 @@ size_t step_gemv_bytes(const StepOp &o) {
 bool step_gemv_supported(const StepOp &o, int stage_bytes) {
     const bool i8 = o.fmt == WF_I8;
     const int ks = std::max(o.ksplit, 1);
-    if (ks > 2 || o.grid % ks || (ks == 2 && (!i8 || o.epi == EPI_LMHEAD || o.K % (128 * ks)))) return false;
+    if (ks > kMaxKsplit || (ks & (ks - 1)) || o.grid % ks || (ks > 1 && (!i8 || o.epi == EPI_LMHEAD || o.K % (128 * ks))))
+        return false;
     if (i8 && (o.K % 128 || o.chunk_w % 64 || o.chunk_w > 32 * kUnitBlocksI8 || o.cta_bytes <= 0)) return false;
     if (!i8 && (o.fmt != WF_F16 || (o.chunk_w != o.K && o.chunk_w % 256))) return false;
     return o.N % 2 == 0 && o.K % 64 == 0 && o.pass_rows % 2 == 0 && o.pass_rows >= 2 &&

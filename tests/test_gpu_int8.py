@@ -111,15 +111,16 @@ def test_int8_qwen2_0_5b_shape_greedy():
     assert d is None, f"first divergence at {d}: margin there {margins[d]:.5f}"
 
 
-@pytest.mark.parametrize("ksplit", ["1", "2"])
-def test_int8_step_kernel_split_k_down(monkeypatch, ksplit):
-    """The down projection of the 0.5B shape with its inputs split over two CTAs (the second CTA's
-    row partials handed to the first as tagged words; the default) and unsplit, through the step
-    kernel on every prompt token, against the oracle's logits."""
+@pytest.mark.parametrize("model,ksplit", [("qwen2-0.5b", "1"), ("qwen2-0.5b", "2"), ("tiny-hd64", "8")])
+def test_int8_step_kernel_split_k_down(monkeypatch, model, ksplit):
+    """Split inputs through the step kernel on every prompt token, against the oracle's logits: the
+    0.5B shape's down projection unsplit and over two CTAs (the second CTA's row partials handed to
+    the first as tagged words; the default), and the tiny model's down projection forced over four
+    CTAs (three partners' partials; by default only inputs of 16,384 or more are split four ways)."""
     from seedplane_b200.engine import CudaQwen2
     monkeypatch.setenv("SEEDPLANE_PREFILL", "steps")
     monkeypatch.setenv("SEEDPLANE_STEP_KSPLIT", ksplit)
-    cfg = QWEN2_0_5B
+    cfg = PRESETS[model]
     w = make_int8_blockwise(cfg, seed=1)
     prompt = random_prompt(cfg.vocab, 6, seed=4)
     eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
