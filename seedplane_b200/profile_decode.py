@@ -170,8 +170,7 @@ def main():
     ap.add_argument("--evict-first", default="1", help="comma list of 0/1: stream weights with evict-first")
     ap.add_argument("--trace", action="store_true", help="print the kernel timeline of the last decode step")
     ap.add_argument("--step", default="step", help="comma list of step implementations: step (persistent), chain")
-    ap.add_argument("--l2-ahead", default="0", help="comma list: weight tiles the step kernel warms L2 with ahead")
-    ap.add_argument("--min-tiles", default="4", help="comma list: weight tiles per CTA at least (step kernel)")
+    ap.add_argument("--l2-kb", default="0", help="comma list: KB per CTA the step kernel warms L2 with ahead of its ring")
     ap.add_argument("--int8", action="store_true", help="blockwise-int8 random weights (drawn on the device)")
     a = ap.parse_args()
     from .engine import CudaQwen2
@@ -183,18 +182,16 @@ def main():
     fmt = "i8" if a.int8 else "f16"
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
     results = {}
-    variants = [(m, pf, ev, sk, la, mt) for sk in a.step.split(",") for m in a.modes.split(",")
-                for pf in a.prefetch_mb.split(",") for ev in a.evict_first.split(",") for la in a.l2_ahead.split(",")
-                for mt in a.min_tiles.split(",")]
-    for mode, pf, ev, sk, la, mt in variants:
+    variants = [(m, pf, ev, sk, la) for sk in a.step.split(",") for m in a.modes.split(",")
+                for pf in a.prefetch_mb.split(",") for ev in a.evict_first.split(",") for la in a.l2_kb.split(",")]
+    for mode, pf, ev, sk, la in variants:
         graph, pdl = MODES[mode]
         os.environ["SEEDPLANE_GRAPH"], os.environ["SEEDPLANE_PDL"] = graph, pdl
         os.environ["SEEDPLANE_STEP"] = sk
-        os.environ["SEEDPLANE_L2_AHEAD"] = la
-        os.environ["SEEDPLANE_STEP_MIN_TILES"] = mt
+        os.environ["SEEDPLANE_STEP_L2_KB"] = la
         os.environ["SEEDPLANE_L2_PREFETCH_MB"], os.environ["SEEDPLANE_EVICT_FIRST"] = pf, ev
         os.environ["SEEDPLANE_TRACE"] = "1" if a.trace else "0"
-        label = f"{sk} {mode} l2_ahead={la} min_tiles={mt} evict_first={ev}" if sk == "step" else f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
+        label = f"{sk} {mode} l2_kb={la} evict_first={ev}" if sk == "step" else f"{sk} {mode} prefetch={pf}MB evict_first={ev}"
         eng = CudaQwen2(cfg, w, weight_format=fmt)
         kv = eng.new_kv(a.capacity)
         _, am = eng.forward(kv, prompt, want_logits=False)
