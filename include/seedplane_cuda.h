@@ -152,6 +152,17 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
                          int32_t vocab, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
                          double temperature, uint64_t seed, uint64_t counter, int32_t *out_host, void *stream);
 
+/* Top-k / top-p filter of one logits row before a draw (replaces the masking steps of
+ * seedplane/qwen_engine.py:147-156, Qwen2Engine.sample): z_dev[j] = logits_dev[j] / temperature
+ * (fp32); then, if top_k > 0, -inf below the top_k-th largest z (ties at the cut kept); then, if
+ * top_p < 1, -inf for every entry whose preceding probability mass in descending order (softmax
+ * over the entries still kept) exceeds top_p (a group of equal values at the cut is kept whole).
+ * Draw from z_dev with sp_accept_stochastic (n = 0, temperature 1). One launch of one CTA on
+ * `stream`, no engine, no allocation. vocab in [1, 524288], temperature > 0, top_k >= 0,
+ * top_p in [0, 1], else SP_ERR_INVALID. */
+int sp_sample_filter(const float *logits_dev, int32_t vocab, double temperature, int32_t top_k, double top_p,
+                     float *z_dev, void *stream);
+
 /* sp_argmax without an engine and without any allocation (no reference counterpart: the
  * reference allocates nothing on this path; this entry point exists for callers that must not
  * allocate device memory, e.g. inside a memory-capped serving process or before an engine

@@ -261,10 +261,51 @@ def accept_stochastic(tokens, parents, target_logits, draft_logits, temperature:
                     if run > target:
                         pick, found = j, True
                         break
-                if not found:
-                    pick, found = min(V - 1, t * B + B - 1), True
+                if not found:                      # rounding: the last positive index up to the block's end
+                    j = min(V - 1, t * B + B - 1)
+                    while j > 0 and not float(P[j]) > 0.0:
+                        j -= 1
+                    pick, found = (j if float(P[j]) > 0.0 else min(V - 1, t * B + B - 1)), True
             else:
                 run = run + float(blocks[t])
         emitted.append(int(pick))
         break
     return emitted, accepted
+
+
+# ---- top-k / top-p filter (restatement of the reference's sample(), qwen_engine.py:147-156) ------
+def sample_filter(logits, temperature: float, top_k: int = 0, top_p: float = 1.0):
+    """The reference's masking before its multinomial draw, in fp32 as torch computes it:
+    z = logits / T; top_k > 0: -inf where z < the top_k-th largest z; top_p < 1: sort descending
+    (stable), probs = softmax in fp32, -inf where cumsum(probs) - probs > top_p. Returns z (fp32)."""
+    import numpy as np
+    z = (np.asarray(logits, dtype=np.float32) / np.float32(temperature)).astype(np.float32)
+    V = z.shape[0]
+    if top_k > 0:
+        cutoff = np.partition(z, V - min(top_k, V))[V - min(top_k, V)]
+        z = np.where(z < cutoff, np.float32(-np.inf), z).astype(np.float32)
+    if top_p < 1:
+        order = np.argsort(-z, kind="stable")
+        values = z[order]
+        e = np.exp(values - values[0], dtype=np.float32)
+        probs = (e / e.sum(dtype=np.float32)).astype(np.float32)
+        drop = (np.cumsum(probs, dtype=np.float32) - probs) > np.float32(top_p)
+        values = np.where(drop, np.float32(-np.inf), values).astype(np.float32)
+        z = np.full_like(z, -np.inf)
+        z[order] = values
+    return z
+
+
+def sample_filter_margin(logits, temperature: float, top_k: int = 0, top_p: float = 1.0) -> float:
+    """How far the top-p decision is from flipping: min |exclusive mass - top_p| over the entries
+    kept by top-k, in fp64 (inf when top_p >= 1). Cases with a margin below fp32 rounding are
+    ambiguous between implementations that sum in different orders."""
+    import numpy as np
+    if top_p >= 1:
+        return float("inf")
+    z = sample_filter(logits, temperature, top_k, 1.0).astype(np.float64)
+    v = np.sort(z[np.isfinite(z)])[::-1]
+    e = np.exp(v - v[0])
+    excl = (np.cumsum(e) - e) / e.sum()
+    # the first entry's exclusive mass is exactly 0 everywhere: it never flips
+    return float(np.min(np.abs(excl[1:] - top_p))) if excl.size > 1 else float("inf")

@@ -1370,6 +1370,17 @@ int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, i
     return SP_OK;
 }
 
+int sp_sample_filter(const float *logits_dev, int32_t vocab, double temperature, int32_t top_k, double top_p,
+                     float *z_dev, void *stream) {
+    if (!logits_dev || !z_dev) return fail(SP_ERR_INVALID, "null argument");
+    if (vocab <= 0 || vocab > kSampleFilterMaxVocab)
+        return fail(SP_ERR_INVALID, "vocab %d outside [1, %d]", vocab, kSampleFilterMaxVocab);
+    if (!(temperature > 0.0)) return fail(SP_ERR_INVALID, "temperature must be positive");
+    if (top_k < 0 || !(top_p >= 0.0 && top_p <= 1.0)) return fail(SP_ERR_INVALID, "top_k < 0 or top_p outside [0, 1]");
+    SP_CUDA(launch_sample_filter(logits_dev, vocab, temperature, top_k, top_p, z_dev, (cudaStream_t)stream));
+    return SP_OK;
+}
+
 int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const float *draft_logits_dev, int64_t ld,
                          int32_t vocab, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
                          double temperature, uint64_t seed, uint64_t counter, int32_t *out_host, void *stream) {

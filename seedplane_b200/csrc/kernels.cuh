@@ -341,6 +341,10 @@ cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long 
 // Stochastic acceptance of a draft tree (sample.cu): target / drafter logits [n + 1][ld] (row 0:
 // after the committed prefix, row i + 1: after node i), nodes (token, parent), fp64 scratch [V].
 // out [2n + 3]: emitted count, accepted count, emitted tokens [n + 1], accepted nodes [n].
+// top-k / top-p filter of one logits row (z = logits / T, dropped entries -inf); one CTA
+constexpr int kSampleFilterMaxVocab = 1 << 19;      // fixed-point mass sums stay below 2^63
+cudaError_t launch_sample_filter(const float *logits, int V, double temperature, int top_k, double top_p, float *z,
+                                 cudaStream_t s);
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
                                      const int *parent, int n, double temperature, unsigned long long seed,
                                      unsigned long long counter, double *scratch, int *out, cudaStream_t s);

@@ -302,8 +302,10 @@ __global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *
                             break;
                         }
                     }
-                    if (!found) {                             // rounding: the block's last index
-                        pick = min(V - 1, t * B + B - 1);
+                    if (!found) {                             // rounding: the last index of positive
+                        int j = min(V - 1, t * B + B - 1);    // probability up to the block's end
+                        while (j > 0 && !(P[j] > 0.0)) --j;
+                        pick = P[j] > 0.0 ? j : min(V - 1, t * B + B - 1);
                         found = true;
                     }
                 } else {
@@ -324,7 +326,108 @@ __global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *
     }
 }
 
+// ---- top-k / top-p filter of one row (the masking steps of the reference's sample()) ----------
+// z = logits / T in fp32. top_k > 0 keeps z >= the k-th largest z (ties at the cut kept, as
+// `z < cutoff` drops only smaller values). top_p < 1 then keeps, in descending order, every value
+// whose preceding probability mass (softmax over what top-k kept) is at most top_p: the cut is the
+// value at which the inclusive mass first exceeds top_p * S (a tie group at the cut stays whole).
+// Dropped entries become -inf. One CTA; both cuts are radix selects over order-preserving 32-bit
+// keys, 8 bits a pass: by count for top-k, by mass for top-p. Masses are exp(z - max) in fixed
+// point (2^44 units, 64-bit integer sums: exact and independent of the atomics' order, so the cut
+// is deterministic; the rounding moves a mass by at most V 2^-45 of the largest entry's).
+constexpr int kFiltThreads = 1024;
+constexpr double kMassScale = 17592186044416.0;      // 2^44
+
+SP_DEVINL uint32_t order_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kFiltThreads) k_sample_filter(const float *logits, int V, float temp, int top_k,
+                                                                double top_p, float *z) {
+    __shared__ unsigned long long s_bin[256];
+    __shared__ unsigned long long s_red[kFiltThreads / 32];
+    __shared__ float s_fmax[kFiltThreads / 32];
+    __shared__ uint32_t s_digit;
+    __shared__ unsigned long long s_rest;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int j = tid; j < V; j += kFiltThreads) z[j] = __fdiv_rn(logits[j], temp);
+    __syncthreads();
+
+    // radix select over the keys of the kept entries (key >= lo): the key at which the running
+    // weight from the top first reaches `need` (weight 1 per entry: rank; mass: strictly exceeds)
+    auto select = [&](uint32_t lo, bool by_mass, float mx, unsigned long long need) -> uint32_t {
+        uint32_t prefix = 0u, pmask = 0u;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int b = tid; b < 256; b += kFiltThreads) s_bin[b] = 0ull;
+            __syncthreads();
+            for (int j = tid; j < V; j += kFiltThreads) {
+                const float v = z[j];
+                const uint32_t key = order_key(v);
+                if (key >= lo && (key & pmask) == prefix) {
+                    const unsigned long long w =
+                        by_mass ? __double2ull_rn(exp((double)v - (double)mx) * kMassScale) : 1ull;
+                    if (w) atomicAdd(&s_bin[(key >> shift) & 255u], w);
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {
+                unsigned long long acc = 0ull;
+                int d = 255;
+                for (; d > 0; --d) {
+                    const unsigned long long nx = acc + s_bin[d];
+                    if (by_mass ? nx > need : nx >= need) break;
+                    acc = nx;
+                }
+                s_digit = (uint32_t)d;
+                s_rest = need - acc;
+            }
+            __syncthreads();
+            prefix |= s_digit << shift;
+            pmask |= 255u << shift;
+            need = s_rest;
+            __syncthreads();
+        }
+        return prefix;
+    };
+
+    uint32_t cut = 0u;                                    // keep keys >= cut
+    if (top_k > 0 && top_k < V) cut = select(0u, false, 0.f, (unsigned long long)top_k);
+    if (top_p < 1.0) {
+        float m = -INFINITY;
+        for (int j = tid; j < V; j += kFiltThreads)
+            if (order_key(z[j]) >= cut) m = fmaxf(m, z[j]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_fmax[warp] = m;
+        __syncthreads();
+        m = s_fmax[0];
+        for (int w = 1; w < kFiltThreads / 32; ++w) m = fmaxf(m, s_fmax[w]);
+        unsigned long long tot = 0ull;
+        for (int j = tid; j < V; j += kFiltThreads)
+            if (order_key(z[j]) >= cut) tot += __double2ull_rn(exp((double)z[j] - (double)m) * kMassScale);
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        if (lane == 0) s_red[warp] = tot;
+        __syncthreads();
+        tot = 0ull;
+        for (int w = 0; w < kFiltThreads / 32; ++w) tot += s_red[w];
+        __syncthreads();
+        // mass above the cut at most top_p * S: the cut is where the inclusive mass first exceeds it
+        const unsigned long long need = (unsigned long long)fmax(0.0, floor(top_p * (double)tot));
+        if (need < tot) cut = max(cut, select(cut, true, m, need));
+    }
+    for (int j = tid; j < V; j += kFiltThreads)
+        if (order_key(z[j]) < cut) z[j] = -INFINITY;
+}
+
 }  // namespace
+
+cudaError_t launch_sample_filter(const float *logits, int V, double temperature, int top_k, double top_p, float *z,
+                                 cudaStream_t s) {
+    if (V <= 0 || V > kSampleFilterMaxVocab || !(temperature > 0.0) || top_k < 0 || !(top_p >= 0.0 && top_p <= 1.0))
+        return cudaErrorInvalidValue;
+    k_sample_filter<<<1, kFiltThreads, 0, s>>>(logits, V, (float)temperature, top_k, top_p, z);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
                                      const int *parent, int n, double temperature, unsigned long long seed,

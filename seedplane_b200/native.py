@@ -18,7 +18,9 @@ types: a failed request raises `RuntimeError(message)`, a missing engine `FileNo
 * Sampling: temperature > 0 draws each token on the device from softmax(logits / temperature) with
   a counter-based RNG (`seed`, then one counter step per token), so a seed reproduces a run; the
   distribution is the reference's, the random stream is not its mt19937_64 (`sampler.hpp`).
-  `top_k` / `top_p` other than off (0 / 1.0) raise `RuntimeError`.
+  `top_k` (> 0) / `top_p` (< 1) filter the row on the device first (`sp_sample_filter`, the
+  reference's rule of `sampler.hpp:2-3` and `qwen_engine.py:147-156`), then the same draw runs on
+  the filtered row.
 
 `last` (`qwen_vk.cpp:848-850`): {done, reason in {stop, length, context}, generated, prompt_tokens,
 prefill_s, decode_s, decode_tok_s, position}.
@@ -164,11 +166,12 @@ class NativeEngine:
             raise RuntimeError(f"unknown request field(s): {sorted(unknown)}")
         opt = {k: v for k, v in self.defaults.items()}
         opt.update({k: v for k, v in sampling.items() if v is not None})
-        if opt.get("top_k") not in (None, 0) or opt.get("top_p") not in (None, 1, 1.0):
-            raise RuntimeError("top_k / top_p sampling is not built on this engine; use temperature alone")
         temp = float(opt.get("temperature") or 0.0)
         if temp < 0.0:
             raise RuntimeError("temperature must be >= 0")
+        top_k, top_p = int(opt.get("top_k") or 0), float(1.0 if opt.get("top_p") is None else opt["top_p"])
+        if top_k < 0 or not 0.0 <= top_p <= 1.0:
+            raise RuntimeError("top_k must be >= 0 and top_p in [0, 1]")
         stops = set(self._stop_ids)
         for s in opt.get("stop") or ():
             if isinstance(s, int):
@@ -177,7 +180,7 @@ class NativeEngine:
                 i = self._tok.token_to_id(str(s))
                 if i is not None:
                     stops.add(int(i))
-        return int(opt["max_new_tokens"]), stops, temp, int(opt.get("seed") or 0)
+        return int(opt["max_new_tokens"]), stops, temp, int(opt.get("seed") or 0), top_k, top_p
 
     def _feed(self, ids: List[int]):
         """Prefill ids into the cache; returns the argmax after the last one."""
@@ -186,7 +189,7 @@ class NativeEngine:
         return int(am[-1])
 
     def _run(self, prompt: List[int], sampling) -> Iterable[str]:
-        max_new, stops, temp, seed = self._options(sampling)
+        max_new, stops, temp, seed, top_k, top_p = self._options(sampling)
         self.last_tokens = []
         self.last = None
         if not prompt:
@@ -199,7 +202,7 @@ class NativeEngine:
             return
         dev = self._engine.device
         if temp > 0.0:
-            yield from self._run_sampled(prompt, max_new, stops, temp, seed)
+            yield from self._run_sampled(prompt, max_new, stops, temp, seed, top_k, top_p)
             return
         t0 = time.perf_counter()
         queue = [self._feed(prompt)]            # generated tokens not yet checked (none is in the cache)
@@ -250,15 +253,17 @@ class NativeEngine:
                      "decode_tok_s": (gen - 1) / decode_s if gen > 1 and decode_s > 0 else 0.0,
                      "position": self._kv.length}
 
-    def _run_sampled(self, prompt: List[int], max_new: int, stops, temp: float, seed: int) -> Iterable[str]:
-        """Temperature sampling: one decode step with logits per token, the draw on the device."""
+    def _run_sampled(self, prompt: List[int], max_new: int, stops, temp: float, seed: int, top_k: int = 0,
+                     top_p: float = 1.0) -> Iterable[str]:
+        """Temperature sampling (top-k / top-p filtered when set, as the reference's sample()): one
+        decode step with logits per token, the filter and the draw on the device."""
         from .speculative import sample_token
         dev = self._engine.device
         t0 = time.perf_counter()
         logits, _ = self._engine.forward(self._kv, torch.tensor(prompt, dtype=torch.int32))
         self._history.extend(prompt)
         counter = 0
-        tok = sample_token(self._engine, logits, temp, seed, counter)
+        tok = sample_token(self._engine, logits, temp, seed, counter, top_k, top_p)
         prefill_s = time.perf_counter() - t0
         t1 = time.perf_counter()
         produced: List[int] = []
@@ -283,7 +288,7 @@ class NativeEngine:
             _, lg = self._engine.decode(self._kv, tok, self._kv.length, 1, want_logits=True)
             self._history.append(tok)
             counter += 1
-            tok = sample_token(self._engine, lg, temp, seed, counter)
+            tok = sample_token(self._engine, lg, temp, seed, counter, top_k, top_p)
         torch.cuda.synchronize(dev)
         decode_s = time.perf_counter() - t1
         gen = len(produced)

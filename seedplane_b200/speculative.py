@@ -218,12 +218,34 @@ def accept_stochastic(engine, flat: FlatForest, target_logits, draft_logits, tem
     return Verification(emitted, n_acc, n_out > n_acc, n_out, path), nodes
 
 
-def sample_token(engine, logits_row, temperature: float, seed: int, counter: int) -> int:
+def sample_filter(logits_row, temperature: float, top_k: int = 0, top_p: float = 1.0, out=None):
+    """The masking of the reference's sample() (qwen_engine.py:147-156) on the device
+    (`sp_sample_filter`): z = logits / temperature, -inf where top_k (> 0) or top_p (< 1) drops the
+    entry. `logits_row`: fp32 [V] or [1, V] on a CUDA device; returns z fp32 [1, V]."""
+    import ctypes as C
+    import torch
+    from . import _native as N
+    from .engine import _stream
+    row = logits_row.reshape(1, -1)
+    if row.dtype != torch.float32 or not row.is_cuda or not row.is_contiguous():
+        raise ValueError("logits_row must be a contiguous fp32 CUDA tensor")
+    z = torch.empty_like(row) if out is None else out
+    N.check(N.load().sp_sample_filter(C.c_void_p(row.data_ptr()), row.shape[1], float(temperature), int(top_k),
+                                      float(top_p), C.c_void_p(z.data_ptr()), C.c_void_p(_stream(row.device))))
+    return z
+
+
+def sample_token(engine, logits_row, temperature: float, seed: int, counter: int, top_k: int = 0,
+                 top_p: float = 1.0) -> int:
     """One draw from softmax(logits / temperature) on the device: the stochastic acceptance of an
     empty tree (`sp_accept_stochastic` with no nodes draws from the target distribution), with the
-    same fp64 arithmetic and counter-based RNG, so (seed, counter) reproduce the token. `logits_row`:
-    fp32 [1, V] (or [V]) on the engine's device."""
+    same fp64 arithmetic and counter-based RNG, so (seed, counter) reproduce the token. With top_k
+    (> 0) or top_p (< 1) the row first goes through `sample_filter` and the draw runs at temperature
+    1 on its output. `logits_row`: fp32 [1, V] (or [V]) on the engine's device."""
     row = logits_row.reshape(1, -1)
+    if top_k > 0 or top_p < 1.0:
+        row = sample_filter(row, temperature, top_k, top_p)
+        temperature = 1.0
     empty = FlatForest(tokens=(), parents=(), depths=(), node_paths=(), paths=())
     v, _ = accept_stochastic(engine, empty, row, row, temperature, seed, counter)
     return int(v.emitted[0])

@@ -44,7 +44,7 @@ def test_native_engine_generate_matches_oracle(bundle):
         list(eng.generate(ids=prompt, max_new_tokens=7))
         assert eng.last_tokens == want[:7]
         with pytest.raises(RuntimeError):
-            list(eng.generate(ids=prompt, temperature=0.7, top_k=40))
+            list(eng.generate(ids=prompt, temperature=0.7, top_p=1.5))
         with pytest.raises(RuntimeError):
             eng.tokenize("hello")
 
@@ -98,3 +98,22 @@ def test_native_engine_temperature_sampling(bundle):
         # a stop token ends the run before it
         list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11, stop=[a[4]]))
         assert eng.last_tokens == a[:a.index(a[4])] and eng.last["reason"] == "stop"
+
+
+def test_native_engine_top_k_top_p_sampling(bundle):
+    """top-k / top-p sampling on the device: top_k = 1 is greedy, a seed reproduces a filtered run."""
+    from seedplane_b200.native import NativeEngine
+    d, cfg, w = bundle
+    prompt = random_prompt(cfg.vocab, 11, seed=5)
+    with NativeEngine(d, ctx=256) as eng:
+        list(eng.generate(ids=prompt, max_new_tokens=12))
+        greedy = list(eng.last_tokens)
+        list(eng.generate(ids=prompt, max_new_tokens=12, temperature=3.0, top_k=1, seed=4))
+        assert eng.last_tokens == greedy
+        list(eng.generate(ids=prompt, max_new_tokens=12, temperature=3.0, top_p=0.0, seed=4))
+        assert eng.last_tokens == greedy
+        list(eng.generate(ids=prompt, max_new_tokens=16, temperature=2.0, top_k=20, top_p=0.9, seed=8))
+        a = list(eng.last_tokens)
+        assert len(a) == 16 and eng.last["reason"] == "length"
+        list(eng.generate(ids=prompt, max_new_tokens=16, temperature=2.0, top_k=20, top_p=0.9, seed=8))
+        assert eng.last_tokens == a
