@@ -96,6 +96,7 @@ class NativeEngine:
                      "window_slots": self.capacity, "weights": fmt}
         self.last = None
         self.last_tokens: List[int] = []
+        self.on_token = None                    # callable(token, text piece or "") per emitted token
 
     @staticmethod
     def _load_tokenizer(path: Path):
@@ -121,8 +122,10 @@ class NativeEngine:
         return self._tok.decode(list(ids), skip_special_tokens=skip_special)
 
     def state(self):
-        return {"position": self._kv.length, "capacity": self.capacity, "mode": "full",
-                "tokens": len(self._history)}
+        """The serve loop's `state` answer (`qwen_vk.cpp:828-831`): position, processed (every
+        position of the cache is processed here) and the token ids the cache holds."""
+        return {"position": self._kv.length, "processed": self._kv.length, "tokens": list(self._history),
+                "capacity": self.capacity, "mode": "full"}
 
     def reset(self):
         self._kv.length = 0
@@ -172,7 +175,8 @@ class NativeEngine:
         top_k, top_p = int(opt.get("top_k") or 0), float(1.0 if opt.get("top_p") is None else opt["top_p"])
         if top_k < 0 or not 0.0 <= top_p <= 1.0:
             raise RuntimeError("top_k must be >= 0 and top_p in [0, 1]")
-        stops = set(self._stop_ids)
+        # a request's stop list replaces the default stop tokens (`qwen_vk.cpp:839-840`)
+        stops = set(self._stop_ids) if opt.get("stop") is None else set()
         for s in opt.get("stop") or ():
             if isinstance(s, int):
                 stops.add(int(s))
@@ -221,11 +225,15 @@ class NativeEngine:
                 else:
                     produced.append(t)
                     self.last_tokens.append(t)
+                    piece = ""
                     if self._tok is not None:
                         full = self._tok.decode(produced)
                         if not full.endswith("\ufffd") and len(full) > len(shown):
                             piece, shown = full[len(shown):], full
-                            yield piece
+                    if self.on_token is not None:
+                        self.on_token(t, piece)
+                    if piece:
+                        yield piece
                     if len(produced) >= max_new:
                         reason, done = "length", True
                 if done:
@@ -275,11 +283,15 @@ class NativeEngine:
                 break
             produced.append(tok)
             self.last_tokens.append(tok)
+            piece = ""
             if self._tok is not None:
                 full = self._tok.decode(produced)
                 if not full.endswith("\ufffd") and len(full) > len(shown):
                     piece, shown = full[len(shown):], full
-                    yield piece
+            if self.on_token is not None:
+                self.on_token(tok, piece)
+            if piece:
+                yield piece
             if len(produced) >= max_new:
                 break
             if self.capacity - self._kv.length < 1:

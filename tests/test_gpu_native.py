@@ -117,3 +117,41 @@ def test_native_engine_top_k_top_p_sampling(bundle):
         assert len(a) == 16 and eng.last["reason"] == "length"
         list(eng.generate(ids=prompt, max_new_tokens=16, temperature=2.0, top_k=20, top_p=0.9, seed=8))
         assert eng.last_tokens == a
+
+
+def test_serve_executable_matches_in_process_engine(bundle):
+    """`seedplane_b200/qwen_serve` as the reference's client runs it (`[engine, bundle, '--serve',
+    ...]`, JSON lines): the ready line, greedy tokens equal to the in-process engine's, state."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    from seedplane_b200.native import NativeEngine
+    d, cfg, w = bundle
+    prompt = random_prompt(cfg.vocab, 10, seed=3)
+    with NativeEngine(d, ctx=128) as eng:
+        list(eng.generate(ids=prompt, max_new_tokens=9))
+        want = list(eng.last_tokens)
+    exe = Path(__file__).resolve().parents[1] / "seedplane_b200" / "qwen_serve"
+    p = subprocess.Popen([sys.executable, str(exe), str(d), "--serve", "--ctx", "128"], stdin=subprocess.PIPE,
+                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+    try:
+        ready = json.loads(p.stdout.readline())
+        assert ready["ready"] and ready["positions"] == 128
+        p.stdin.write(json.dumps({"op": "generate", "ids": prompt, "max_new_tokens": 9}) + "\n")
+        p.stdin.flush()
+        toks = []
+        while True:
+            r = json.loads(p.stdout.readline())
+            assert "error" not in r, r
+            if r.get("done"):
+                break
+            toks.append(r["token"])
+        assert toks == want and r["generated"] == 9 and r["position"] == len(prompt) + 8
+        p.stdin.write(json.dumps({"op": "state"}) + "\n")
+        p.stdin.flush()
+        st = json.loads(p.stdout.readline())
+        assert st["position"] == len(prompt) + 8 and st["tokens"] == (prompt + want)[:st["position"]]
+    finally:
+        p.stdin.close()
+        p.wait(timeout=60)
