@@ -41,9 +41,11 @@ _DECODE_BLOCK = 32
 
 
 def find_engine(explicit=None) -> str:
-    """Engine library: explicit path, $SEEDPLANE_NATIVE_ENGINE, then the in-tree build."""
+    """Engine library: explicit path, $SEEDPLANE_NATIVE_ENGINE, then the in-tree build. The variable
+    may name the serve executable instead (for the reference's subprocess client); a candidate
+    that is not a shared library is passed over."""
     for cand in (explicit, os.environ.get("SEEDPLANE_NATIVE_ENGINE"), N.LIB_PATH):
-        if cand and Path(cand).is_file():
+        if cand and Path(cand).is_file() and ".so" in Path(cand).name:
             return str(cand)
     raise FileNotFoundError("native engine not found: build it with `python -m seedplane_b200.build` "
                             "or set SEEDPLANE_NATIVE_ENGINE")
