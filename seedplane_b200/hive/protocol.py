@@ -43,18 +43,20 @@ class Frame:
 
 
 def json_payload(value) -> bytes:
-    return json.dumps(value, ensure_ascii=False, separators=(",", ":")).encode("utf-8")
+    """Compact UTF-8 JSON (no spaces after separators, non-ASCII kept as is)."""
+    return json.dumps(value, separators=(",", ":"), ensure_ascii=False).encode("utf-8")
 
 
 def parse_json(payload: bytes):
-    return json.loads(payload.decode("utf-8"))
+    return json.loads(bytes(payload).decode("utf-8"))
 
 
 def encode_frame(frame: Frame) -> bytes:
-    if len(frame.payload) > MAX_PAYLOAD:
-        raise ValueError(f"HIVE payload exceeds {MAX_PAYLOAD} bytes")
-    return HEADER.pack(MAGIC, VERSION, int(frame.kind), frame.flags, frame.request_id, frame.sequence,
-                       len(frame.payload)) + frame.payload
+    n = len(frame.payload)
+    if n > MAX_PAYLOAD:
+        raise ValueError(f"a HIVE payload of {n} bytes is over the {MAX_PAYLOAD}-byte limit")
+    head = HEADER.pack(MAGIC, VERSION, int(frame.kind), frame.flags, frame.request_id, frame.sequence, n)
+    return head + bytes(frame.payload)
 
 
 def send_frame(sock: socket.socket, frame: Frame) -> None:
@@ -69,21 +71,29 @@ def recv_exact(sock: socket.socket, size: int) -> bytes:
     while got < size:
         n = sock.recv_into(view[got:], size - got)
         if n == 0:
-            raise ConnectionError("HIVE peer closed the connection")
+            raise ConnectionError(f"the HIVE peer hung up after {got} of {size} bytes")
         got += n
     return bytes(buf)
 
 
+def _checked_kind(magic: bytes, version: int, kind: int, length: int) -> Message:
+    """The message kind of a header, after the checks that make the rest of it trustworthy."""
+    if magic != MAGIC:
+        raise ValueError(f"not a HIVE frame (magic {magic!r})")
+    if version != VERSION:
+        raise ValueError(f"HIVE protocol version {version} is not supported (this side speaks {VERSION})")
+    if length > MAX_PAYLOAD:
+        raise ValueError(f"a HIVE frame announces {length} payload bytes, over the {MAX_PAYLOAD}-byte limit")
+    if kind not in _KINDS:
+        raise ValueError(f"HIVE message kind {kind} is unknown")
+    return Message(kind)
+
+
+_KINDS = frozenset(int(m) for m in Message)
+
+
 def recv_frame(sock: socket.socket) -> Frame:
     magic, version, kind, flags, request_id, sequence, length = HEADER.unpack(recv_exact(sock, HEADER.size))
-    if magic != MAGIC:
-        raise ValueError("invalid HIVE frame magic")
-    if version != VERSION:
-        raise ValueError(f"unsupported HIVE protocol version {version}")
-    if length > MAX_PAYLOAD:
-        raise ValueError(f"HIVE payload length {length} exceeds limit")
-    try:
-        message = Message(kind)
-    except ValueError as exc:
-        raise ValueError(f"unknown HIVE message type {kind}") from exc
-    return Frame(message, request_id, sequence, recv_exact(sock, length) if length else b"", flags)
+    message = _checked_kind(magic, version, kind, length)
+    payload = recv_exact(sock, length) if length else b""
+    return Frame(message, request_id, sequence, payload, flags)

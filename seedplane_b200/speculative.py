@@ -35,6 +35,8 @@ class ForestNode:
 
 @dataclass
 class SpeculativeForest:
+    """Draft branches merged into a trie: `roots` maps a first token to its node, `paths` keeps every
+    non-empty branch as given (input order decides ties between equally good branches)."""
     roots: Dict[int, ForestNode] = field(default_factory=dict)
     paths: List[Tuple[int, ...]] = field(default_factory=list)
 
@@ -42,23 +44,29 @@ class SpeculativeForest:
     def build(cls, branches: Iterable[Iterable[int]]) -> "SpeculativeForest":
         forest = cls()
         for branch in branches:
-            path = tuple(int(token) for token in branch)
-            if not path:
-                continue
-            forest.paths.append(path)
-            children = forest.roots
-            for token in path:
-                node = children.get(token)
-                if node is None:
-                    node = children[token] = ForestNode(token)
-                children = node.children
+            forest.add(branch)
         return forest
+
+    def add(self, branch: Iterable[int]) -> None:
+        """Merge one branch into the trie (an empty branch adds nothing)."""
+        path = tuple(map(int, branch))
+        if not path:
+            return
+        self.paths.append(path)
+        level = self.roots
+        for tok in path:
+            if tok not in level:
+                level[tok] = ForestNode(tok)
+            level = level[tok].children
 
     @property
     def node_count(self) -> int:
-        def count(children):
-            return sum(1 + count(node.children) for node in children.values())
-        return count(self.roots)
+        n, todo = 0, list(self.roots.values())
+        while todo:
+            node = todo.pop()
+            n += 1
+            todo.extend(node.children.values())
+        return n
 
     def flatten(self) -> "FlatForest":
         index: Dict[Tuple[int, ...], int] = {}
@@ -100,71 +108,79 @@ class Verification:
 
 
 def _first_argmax(values: Sequence[float]) -> int:
-    return max(range(len(values)), key=values.__getitem__)
+    """Index of the largest value, the lowest index on ties (like `max` over the indices)."""
+    if not len(values):
+        raise ValueError("target returned empty logits")
+    best = 0
+    for i in range(1, len(values)):
+        if values[i] > values[best]:
+            best = i
+    return best
+
+
+def _select(flat: FlatForest, predict: Callable[[int], int]) -> Tuple[Verification, Tuple[int, ...]]:
+    """The greedy decision over a flattened forest. `predict(node)` is the target's token after
+    node `node` (-1: after the committed prefix alone); it is asked only for the nodes a walk
+    reaches, each at most once.
+
+    Each path is walked from its root while the target agrees with the draft; the first
+    disagreement emits the target's token instead and rejects the path; a fully agreed path
+    emits its draft tokens and nothing more. The decision is the path with the most accepted
+    draft tokens, then the most emitted tokens, then the earliest in input order. Returns it with
+    the node indices of its accepted draft tokens."""
+    if not flat.paths:
+        return Verification((predict(-1),), 0, False, 1, ()), ()
+    memo: Dict[int, int] = {}
+
+    def after(node: int) -> int:
+        if node not in memo:
+            memo[node] = int(predict(node))
+        return memo[node]
+
+    best_key, best = None, None
+    for order, (path, ids) in enumerate(zip(flat.paths, flat.node_paths)):
+        emitted: List[int] = []
+        prev = -1
+        for nid in ids:
+            want = after(prev)
+            if want != flat.tokens[nid]:
+                emitted.append(want)
+                break
+            emitted.append(flat.tokens[nid])
+            prev = nid
+        accepted = ids.index(prev) + 1 if prev >= 0 else 0
+        rejected = len(emitted) > accepted
+        key = (accepted, len(emitted), -order)
+        if best_key is None or key > best_key:
+            best_key = key
+            best = (Verification(tuple(emitted), accepted, rejected, len(emitted), tuple(path)), tuple(ids[:accepted]))
+    return best
 
 
 def verify_greedy(committed: Sequence[int], forest: SpeculativeForest,
                   target_logits: Callable[[Tuple[int, ...]], Sequence[float]]) -> Verification:
-    """Verify every draft path with one target call per (path, depth), then choose the longest
-    exact greedy continuation (the reference's sequential rule, kept for callers with a logits
-    callback; the GPU path is `verify_tree`)."""
+    """The reference's greedy verification with a logits callback: `target_logits(prefix)` gives the
+    target's logits for the token after `prefix`. Every distinct prefix is asked once (paths that
+    share a trie prefix share its answers); the decision is `_select`'s. The GPU path is
+    `verify_tree`."""
     base = tuple(int(t) for t in committed)
-    if not forest.paths:
-        logits = target_logits(base)
-        if not len(logits):
-            raise ValueError("target returned empty logits")
-        return Verification((_first_argmax(logits),), 0, False, 1, ())
-    best = None
-    for path in forest.paths:
-        accepted: List[int] = []
-        steps = 0
-        rejected = False
-        for draft_token in path:
-            logits = target_logits(base + tuple(accepted))
-            if not len(logits):
-                raise ValueError("target returned empty logits")
-            target_token = _first_argmax(logits)
-            steps += 1
-            if draft_token != target_token:
-                accepted.append(target_token)
-                rejected = True
-                break
-            accepted.append(draft_token)
-        result = Verification(tuple(accepted), len(accepted) - int(rejected), rejected, steps, path)
-        if best is None or (result.accepted_draft_tokens, len(result.emitted)) > \
-                (best.accepted_draft_tokens, len(best.emitted)):
-            best = result
-    return best
+    flat = forest.flatten()
+    prefix_of = {}
+    for path, ids in zip(flat.paths, flat.node_paths):
+        for d, nid in enumerate(ids):
+            prefix_of[nid] = path[:d + 1]
+
+    def predict(node: int) -> int:
+        return _first_argmax(target_logits(base + (prefix_of[node] if node >= 0 else ())))
+
+    return _select(flat, predict)[0]
 
 
 def accept_greedy(flat: FlatForest, root_pred: int, node_pred: Sequence[int]) -> Tuple[Verification, Tuple[int, ...]]:
     """`verify_greedy`'s decision from the target argmax after the committed prefix (`root_pred`)
     and after each node (`node_pred[i]`). Returns the verification and the accepted draft nodes
     of the chosen path (their K/V is what a commit keeps)."""
-    if not flat.paths:
-        return Verification((int(root_pred),), 0, False, 1, ()), ()
-    best, best_nodes = None, ()
-    for path, ids in zip(flat.paths, flat.node_paths):
-        emitted: List[int] = []
-        nodes: List[int] = []
-        steps = 0
-        rejected = False
-        prev = -1
-        for nid in ids:
-            target = int(root_pred) if prev < 0 else int(node_pred[prev])
-            steps += 1
-            if flat.tokens[nid] != target:
-                emitted.append(target)
-                rejected = True
-                break
-            emitted.append(flat.tokens[nid])
-            nodes.append(nid)
-            prev = nid
-        result = Verification(tuple(emitted), len(emitted) - int(rejected), rejected, steps, tuple(path))
-        if best is None or (result.accepted_draft_tokens, len(result.emitted)) > \
-                (best.accepted_draft_tokens, len(best.emitted)):
-            best, best_nodes = result, tuple(nodes)
-    return best, best_nodes
+    return _select(flat, lambda node: int(root_pred) if node < 0 else int(node_pred[node]))
 
 
 @dataclass(frozen=True)
@@ -262,7 +278,7 @@ def commit_tree(engine, kv, result: TreeResult) -> int:
 
 @dataclass
 class CommitLedger:
-    """Committed token frontier; speculative state never mutates it pre-commit."""
+    """The committed tokens. Only `commit` moves the frontier; speculation never touches it."""
     tokens: List[int] = field(default_factory=list)
     commits: int = 0
 
@@ -271,12 +287,12 @@ class CommitLedger:
         return len(self.tokens)
 
     def commit(self, verification: Verification) -> Tuple[int, ...]:
-        if not verification.emitted:
-            raise ValueError("cannot commit an empty verification")
-        committed = verification.emitted
-        self.tokens.extend(committed)
+        new = tuple(verification.emitted)
+        if len(new) == 0:
+            raise ValueError("a verification that emitted no token cannot be committed")
+        self.tokens += new
         self.commits += 1
-        return committed
+        return new
 
 
 # ---- tree drafting and the speculative decode loop (the cfg2 workload) ---------------------------

@@ -227,3 +227,57 @@ def test_two_rank_agents_partition_the_burst():
     assert len(res[3]) == 16 and set(res[3]) == {"gpu0", "gpu1"}   # split by measured service time
     served = sorted(m[1:] for m in msgs if m[0] == "served")
     assert all(n >= 1 and not alive for _, n, alive in served)
+
+
+# ---- the lease queue behind the broker ------------------------------------------------------------
+def test_queue_orders_by_priority_then_submission():
+    from seedplane_b200.hive.pool import LeaseQueue, WorkerInfo, WorkTile, _Ticket
+    q = LeaseQueue()
+    mk = lambda rid, prio, model="m": _Ticket(rid, WorkTile(kind="k", model=model, payload={"r": rid}, priority=prio),
+                                                time.monotonic() + 60, rid)
+    q.put([mk(1, 0), mk(2, 5), mk(3, 0, model="other"), mk(4, 5)])
+    w = WorkerInfo("w", frozenset(), frozenset({"m"}), 0.0)
+    assert [q.take(w, 0.0).request_id for _ in range(3)] == [2, 4, 1]
+    assert q.take(w, 0.01) is None                  # request 3 is for a model w does not serve
+    q.close(RuntimeError("closed"))
+
+
+def test_reserved_work_is_released_when_its_worker_leaves():
+    with HiveBroker(pull_poll_s=0.02) as broker:
+        agents, threads = _start_agents(broker, [(n, ("generate",), ("qwen",), lambda p: p) for n in ("fast", "slow")])
+        for name, ms in (("fast", 5), ("slow", 500)):
+            for _ in range(3):
+                broker.cost_model.observe(kind="decode", model="qwen", worker=name, token_budget=4, duration_ms=ms)
+        _stop(agents[:1], threads[:1])              # the fast worker leaves before the batch
+        assert _wait(lambda: set(broker.workers()) == {"slow"})
+        futs = broker.submit_batch([{"n": n} for n in range(3)], model="qwen", kind="decode", token_budget=4)
+        assert [f.result(timeout=3) for f in futs] == [{"n": 0}, {"n": 1}, {"n": 2}]
+        assert {f.worker_id for f in futs} == {"slow"}
+        _stop(agents[1:], threads[1:])
+
+
+def test_local_agent_pulls_without_tcp_and_feeds_the_cost_model():
+    with HiveBroker(pull_poll_s=0.02) as broker:
+        ag = broker.local_agent("gpu0", caps=("generate",), models=("m",), execute=lambda p: {"twice": 2 * p["x"]})
+        t = threading.Thread(target=ag.run, daemon=True)
+        t.start()
+        assert _wait(lambda: "gpu0" in broker.workers())
+        futs = [broker.submit({"x": i}, model="m") for i in range(4)]
+        assert [f.result(timeout=3) for f in futs] == [{"twice": 2 * i} for i in range(4)]
+        est = broker.cost_model.estimate(kind="throughput.generate", model="m", worker="gpu0", token_budget=0)
+        assert est is not None and est.samples == 4
+        ag.stop()
+        t.join(timeout=3)
+        assert not t.is_alive() and "gpu0" not in broker.workers()
+
+
+def test_unleased_work_expires():
+    with HiveBroker(pull_poll_s=0.02) as broker:
+        fut = broker.submit({"x": 1}, model="nobody-serves-this", timeout=0.05)
+        ag = broker.local_agent("gpu0", caps=("generate",), models=("m",), execute=lambda p: p)
+        t = threading.Thread(target=ag.run, daemon=True)
+        t.start()
+        with pytest.raises(TimeoutError):
+            fut.result(timeout=3)
+        ag.stop()
+        t.join(timeout=3)
