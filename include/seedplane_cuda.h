@@ -166,14 +166,17 @@ int sp_sample_filter(const float *logits_dev, int32_t vocab, double temperature,
 /* sp_argmax without an engine and without any allocation (no reference counterpart: the
  * reference allocates nothing on this path; this entry point exists for callers that must not
  * allocate device memory, e.g. inside a memory-capped serving process or before an engine
- * exists). Same result as sp_argmax. Runs on `device` (it calls cudaSetDevice). Its scratch is
- * a fixed 33,280-byte __device__ array of the library (one per device), so:
+ * exists). Same result as sp_argmax. Runs on `device` and sets the calling thread's current
+ * device back to what it was before returning; logits_dev and argmax_dev must be device memory
+ * of `device` (else SP_ERR_INVALID). Its scratch is a fixed 33,280-byte __device__ array of the
+ * library (one per device), so:
  *   - rows <= 128, else SP_ERR_CAPACITY (nothing is launched);
  *   - it clears the row counters it uses (a memset on `stream`) before each launch;
  *   - calls that overlap in time on one device (different streams or threads) race on the same
  *     scratch: order them on one stream;
  *   - the first call on a device looks the scratch up (cudaGetSymbolAddress): make it before any
- *     stream capture; later calls may be captured. */
+ *     stream capture. The address is kept for the life of the device's primary context; a
+ *     process that resets the device (cudaDeviceReset) must not call this entry point again. */
 int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld,
                       int32_t *argmax_dev, void *stream);
 

@@ -1424,8 +1424,23 @@ int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t
     if (rows > argmax_noalloc_max_rows())
         return fail(SP_ERR_CAPACITY, "%d rows exceed the fixed scratch (at most %d rows)", rows, argmax_noalloc_max_rows());
     if (device < 0 || device >= kMaxDevices) return fail(SP_ERR_INVALID, "device %d", device);
+    // the caller's current device is put back on every return
+    struct DeviceRestore {
+        int prev = -1;
+        ~DeviceRestore() { if (prev >= 0) cudaSetDevice(prev); }
+    } restore;
+    SP_CUDA(cudaGetDevice(&restore.prev));
     SP_CUDA(cudaSetDevice(device));
-    // Per-device address of the module's scratch array, looked up once (before any stream capture).
+    for (const void *ptr : {(const void *)logits_dev, (const void *)argmax_dev}) {
+        cudaPointerAttributes at{};
+        SP_CUDA(cudaPointerGetAttributes(&at, ptr));
+        if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+            return fail(SP_ERR_INVALID, "logits and output must be device memory");
+        if (at.device != device)
+            return fail(SP_ERR_INVALID, "a buffer lives on device %d, not on device %d", at.device, device);
+    }
+    // Per-device address of the module's scratch array, looked up once (before any stream capture);
+    // it stays valid for the life of the device's primary context.
     static std::mutex mu;
     static void *base[kMaxDevices] = {};
     void *b = nullptr;

@@ -12,8 +12,14 @@ types: a failed request raises `RuntimeError(message)`, a missing engine `FileNo
 * `engine`: the engine library (`libseedplane_cuda.so`) in place of the reference's executable:
   the explicit path, `$SEEDPLANE_NATIVE_ENGINE`, or the in-tree build.
 * Greedy decoding runs on the device in blocks (the argmax is fed back without a host round trip);
-  the host sees each block's tokens, cuts at a stop token and rolls the cache back to it. The
-  token sequence is the same as one-at-a-time decoding.
+  the host sees each block's tokens, cuts at a stop token or the length limit and rolls the cache
+  back to it. The token sequence is the same as one-at-a-time decoding.
+* Run semantics are the reference engine's (`qwen_vk.cpp:588-613`): every sampled token, a stop
+  token included, is emitted (a stop token with empty text) and counted in `generated`; the last
+  sampled token stays in the session unprocessed (so `state()` reports position = processed + 1
+  and a chat turn's `<|im_end|>` becomes history); text still held by the incremental decoder at
+  the end is flushed as one more emission with token -1, and the reference's client appends that
+  -1 to `last_tokens`, as this class does.
 * Only full attention (`mode` None / "full") is built; shard windows raise `RuntimeError`.
 * Sampling: temperature > 0 draws each token on the device from softmax(logits / temperature) with
   a counter-based RNG (`seed`, then one counter step per token), so a seed reproduces a run; the
@@ -36,8 +42,42 @@ import torch
 
 from . import _native as N
 
-QWEN_STOP_TOKENS = ("<|endoftext|>", "<|im_end|>")
+QWEN_STOP_TOKENS = ("<|im_end|>", "<|endoftext|>")
+DEFAULT_SYSTEM = "You are a helpful assistant."      # qwen_vk.cpp:664
 _DECODE_BLOCK = 32
+
+
+class _TextStream:
+    """Incremental detokenizer: `push(id)` returns the text that became complete (nothing while a
+    multi-byte character is still open), `flush()` whatever is left. Special tokens add no text."""
+
+    def __init__(self, tok):
+        self.tok = tok
+        self.ids: List[int] = []
+        self.shown = ""
+
+    def push(self, t: int) -> str:
+        if self.tok is None:
+            return ""
+        self.ids.append(int(t))
+        full = self.tok.decode(self.ids, skip_special_tokens=True)
+        if full.endswith("\ufffd") or len(full) <= len(self.shown):
+            return ""
+        piece, self.shown = full[len(self.shown):], full
+        return piece
+
+    def flush(self) -> str:
+        if self.tok is None or not self.ids:
+            return ""
+        full = self.tok.decode(self.ids, skip_special_tokens=True)
+        rest = full[len(self.shown):] if full.startswith(self.shown) else ""
+        self.shown = full
+        return rest
+
+
+def _sync(dev) -> None:
+    if getattr(dev, "type", None) == "cuda":
+        torch.cuda.synchronize(dev)
 
 
 def find_engine(explicit=None) -> str:
@@ -90,8 +130,10 @@ class NativeEngine:
                     self._stop_ids.add(int(i))
         self.defaults = {"temperature": temperature, "top_k": top_k, "top_p": top_p, "seed": seed,
                          "max_new_tokens": max_new_tokens if max_new_tokens is not None else 256}
-        self.system = system
-        self._history: List[int] = []           # token ids whose K/V the cache holds
+        self.system = DEFAULT_SYSTEM if system is None else system
+        # the session's token sequence; the cache holds the K/V of its first `_kv.length` tokens
+        # (after a run, every token but the last sampled one)
+        self._history: List[int] = []
         dev = self._engine.device
         self.info = {"ready": True, "device": torch.cuda.get_device_name(dev), "engine": "seedplane-b200",
                      "mode": "full", "plan": plan_of(self.bundle), "positions": self.capacity,
@@ -114,19 +156,24 @@ class NativeEngine:
 
     # ---- requests --------------------------------------------------------------------------
     def tokenize(self, text, special=True):
-        """Token ids of `text`; special tokens written in the text are recognised (the tokenizer's
-        added tokens), as the reference engine's `special=True` default does."""
+        """Token ids of `text`. With `special` (the default), special tokens written in the text
+        (`<|im_start|>`, ...) become their ids; without it they are encoded as plain text, like
+        the reference engine's `encode(text, allow_special)`."""
         self._need_tokenizer()
-        return self._tok.encode(text, add_special_tokens=False).ids
+        self._tok.encode_special_tokens = not special
+        try:
+            return self._tok.encode(text, add_special_tokens=False).ids
+        finally:
+            self._tok.encode_special_tokens = False
 
     def detokenize(self, ids, skip_special=False):
         self._need_tokenizer()
         return self._tok.decode(list(ids), skip_special_tokens=skip_special)
 
     def state(self):
-        """The serve loop's `state` answer (`qwen_vk.cpp:828-831`): position, processed (every
-        position of the cache is processed here) and the token ids the cache holds."""
-        return {"position": self._kv.length, "processed": self._kv.length, "tokens": list(self._history),
+        """The serve loop's `state` answer (`qwen_vk.cpp:828-831`): position = tokens in the
+        session, processed = tokens whose K/V the cache holds, and the token ids."""
+        return {"position": len(self._history), "processed": self._kv.length, "tokens": list(self._history),
                 "capacity": self.capacity, "mode": "full"}
 
     def reset(self):
@@ -141,27 +188,20 @@ class NativeEngine:
         yield from self._run(prompt, sampling)
 
     def chat(self, content, system=None, reset=False, **sampling):
-        """One user turn in ChatML; the conversation stays in the cache."""
+        """One user turn in ChatML (`qwen_vk.cpp:615-620`); the conversation stays in the session.
+        The first turn opens with the system block; a later one closes the previous assistant turn
+        (with `<|im_end|>` unless that was its last token) before the user block."""
         self._need_tokenizer()
         if reset:
             self.reset()
-        text = ""
-        sys_prompt = system if system is not None else self.system
-        if not self._history and sys_prompt:
-            text += f"<|im_start|>system\n{sys_prompt}<|im_end|>\n"
-        elif self._history:
-            text += "\n"                        # closes the previous assistant turn's <|im_end|>
-        text += f"<|im_start|>user\n{content}<|im_end|>\n<|im_start|>assistant\n"
+        tail = f"<|im_start|>user\n{content}<|im_end|>\n<|im_start|>assistant\n"
+        if not self._history:
+            sys_prompt = system if system is not None else self.system
+            text = f"<|im_start|>system\n{sys_prompt}<|im_end|>\n" + tail
+        else:
+            closed = self._history[-1] == self._tok.token_to_id("<|im_end|>")
+            text = ("" if closed else "<|im_end|>") + "\n" + tail
         yield from self._run(self.tokenize(text), sampling)
-        # close the assistant turn in the cache: its last token (when cut by length) and <|im_end|>
-        tail = []
-        if self.last and self.last["reason"] == "length" and self.last_tokens:
-            tail.append(self.last_tokens[-1])
-        end = self._tok.token_to_id("<|im_end|>")
-        if end is not None:
-            tail.append(int(end))
-        if tail and self._kv.length + len(tail) < self.capacity:
-            self._feed(tail)
 
     # ---- the loop ----------------------------------------------------------------------------
     def _options(self, sampling):
@@ -180,68 +220,84 @@ class NativeEngine:
         # a request's stop list replaces the default stop tokens (`qwen_vk.cpp:839-840`)
         stops = set(self._stop_ids) if opt.get("stop") is None else set()
         for s in opt.get("stop") or ():
-            if isinstance(s, int):
-                stops.add(int(s))
+            if isinstance(s, (int, float)) and not isinstance(s, bool):
+                stops.add(int(s))             # JSON numbers (151645 or 151645.0), as qwen_vk.cpp:844 casts them
             elif self._tok is not None:
                 i = self._tok.token_to_id(str(s))
                 if i is not None:
                     stops.add(int(i))
         return int(opt["max_new_tokens"]), stops, temp, int(opt.get("seed") or 0), top_k, top_p
 
-    def _feed(self, ids: List[int]):
-        """Prefill ids into the cache; returns the argmax after the last one."""
-        _, am = self._engine.forward(self._kv, torch.tensor(ids, dtype=torch.int32), want_logits=False)
-        self._history.extend(ids)
-        return int(am[-1])
+    def _catch_up(self, ids: List[int], want_logits: bool = False):
+        """Append `ids` to the session and process every pending token (the previous run's last
+        sampled token, then `ids`); returns (logits of the last or None, its argmax)."""
+        self._history.extend(int(t) for t in ids)
+        pending = self._history[self._kv.length:]
+        logits, am = self._engine.forward(self._kv, torch.tensor(pending, dtype=torch.int32), want_logits=want_logits)
+        return logits, int(am[-1])
+
+    def _emit(self, t: int, piece: str):
+        self.last_tokens.append(int(t))
+        if self.on_token is not None:
+            self.on_token(int(t), piece)
+
+    def _finish(self, reason, generated, n_prompt, prefill_s, decode_s, stream: _TextStream):
+        rest = stream.flush()
+        if rest:
+            self._emit(-1, rest)
+        self.last = {"done": True, "reason": reason, "generated": generated, "prompt_tokens": n_prompt,
+                     "prefill_s": prefill_s, "decode_s": decode_s,
+                     "decode_tok_s": generated / max(decode_s, 1e-9), "position": len(self._history)}
+        return rest
+
+    def _check_prompt(self, prompt: List[int]) -> bool:
+        if not prompt:
+            raise RuntimeError("empty prompt")
+        if any(t < 0 or t >= self.cfg.vocab for t in prompt):
+            raise RuntimeError("token id outside the vocabulary")
+        if len(self._history) + len(prompt) > self.capacity:
+            self.last = {"done": True, "reason": "context", "generated": 0, "prompt_tokens": len(prompt),
+                         "prefill_s": 0.0, "decode_s": 0.0, "decode_tok_s": 0.0, "position": len(self._history)}
+            return False
+        return True
 
     def _run(self, prompt: List[int], sampling) -> Iterable[str]:
         max_new, stops, temp, seed, top_k, top_p = self._options(sampling)
         self.last_tokens = []
         self.last = None
-        if not prompt:
-            raise RuntimeError("empty prompt")
-        if any(t < 0 or t >= self.cfg.vocab for t in prompt):
-            raise RuntimeError("token id outside the vocabulary")
-        if self._kv.length + len(prompt) >= self.capacity:
-            self.last = {"done": True, "reason": "context", "generated": 0, "prompt_tokens": len(prompt),
-                         "prefill_s": 0.0, "decode_s": 0.0, "decode_tok_s": 0.0, "position": self._kv.length}
+        if not self._check_prompt(prompt):
             return
-        dev = self._engine.device
         if temp > 0.0:
             yield from self._run_sampled(prompt, max_new, stops, temp, seed, top_k, top_p)
             return
+        dev = self._engine.device
+        stream = _TextStream(self._tok)
         t0 = time.perf_counter()
-        queue = [self._feed(prompt)]            # generated tokens not yet checked (none is in the cache)
-        torch.cuda.synchronize(dev)
+        _, first = self._catch_up(prompt)
+        _sync(dev)
         prefill_s = time.perf_counter() - t0
         t1 = time.perf_counter()
-        produced: List[int] = []
-        shown = ""
-        reason = "length"
+        queue = [first]                         # sampled tokens not emitted yet (the first is unprocessed)
         fed_at = None                           # cache slot of the token fed to the last decode block
+        generated, reason = 0, "length"
         while True:
             done = False
             for i, t in enumerate(queue):
-                if t in stops:
+                self._history.append(t)
+                generated += 1
+                is_stop = t in stops
+                piece = "" if is_stop else stream.push(t)
+                self._emit(t, piece)
+                if piece:
+                    yield piece
+                if is_stop:
                     reason, done = "stop", True
-                else:
-                    produced.append(t)
-                    self.last_tokens.append(t)
-                    piece = ""
-                    if self._tok is not None:
-                        full = self._tok.decode(produced)
-                        if not full.endswith("\ufffd") and len(full) > len(shown):
-                            piece, shown = full[len(shown):], full
-                    if self.on_token is not None:
-                        self.on_token(t, piece)
-                    if piece:
-                        yield piece
-                    if len(produced) >= max_new:
-                        reason, done = "length", True
+                elif generated >= max_new:
+                    reason, done = "length", True
                 if done:
-                    if fed_at is not None:      # the cache holds the fed token and queue[:-1]: keep queue[:i]
+                    # the block's cache holds the fed token and queue[:-1]; keep it up to queue[i - 1]
+                    if fed_at is not None:
                         self._kv.length = fed_at + 1 + i
-                        del self._history[self._kv.length:]
                     break
             if done:
                 break
@@ -249,19 +305,14 @@ class NativeEngine:
             if room < 1:
                 reason = "context"
                 break
-            token = queue[-1]
-            n = min(_DECODE_BLOCK, max_new - len(produced), room)
+            n = min(_DECODE_BLOCK, max_new - generated, room)
             fed_at = self._kv.length
-            out, _ = self._engine.decode(self._kv, token, fed_at, n)
+            out, _ = self._engine.decode(self._kv, self._history[-1], fed_at, n)
             queue = out.tolist()
-            self._history.append(token)
-            self._history.extend(queue[:-1])
         decode_s = time.perf_counter() - t1
-        gen = len(produced)
-        self.last = {"done": True, "reason": reason, "generated": gen, "prompt_tokens": len(prompt),
-                     "prefill_s": prefill_s, "decode_s": decode_s,
-                     "decode_tok_s": (gen - 1) / decode_s if gen > 1 and decode_s > 0 else 0.0,
-                     "position": self._kv.length}
+        rest = self._finish(reason, generated, len(prompt), prefill_s, decode_s, stream)
+        if rest:
+            yield rest
 
     def _run_sampled(self, prompt: List[int], max_new: int, stops, temp: float, seed: int, top_k: int = 0,
                      top_p: float = 1.0) -> Iterable[str]:
@@ -269,47 +320,38 @@ class NativeEngine:
         decode step with logits per token, the filter and the draw on the device."""
         from .speculative import sample_token
         dev = self._engine.device
+        stream = _TextStream(self._tok)
         t0 = time.perf_counter()
-        logits, _ = self._engine.forward(self._kv, torch.tensor(prompt, dtype=torch.int32))
-        self._history.extend(prompt)
+        logits, _ = self._catch_up(prompt, want_logits=True)
         counter = 0
-        tok = sample_token(self._engine, logits, temp, seed, counter, top_k, top_p)
+        tok = sample_token(self._engine, logits[-1:], temp, seed, counter, top_k, top_p)
         prefill_s = time.perf_counter() - t0
         t1 = time.perf_counter()
-        produced: List[int] = []
-        shown = ""
-        reason = "length"
+        generated, reason = 0, "length"
         while True:
-            if tok in stops:
-                reason = "stop"
-                break
-            produced.append(tok)
-            self.last_tokens.append(tok)
-            piece = ""
-            if self._tok is not None:
-                full = self._tok.decode(produced)
-                if not full.endswith("\ufffd") and len(full) > len(shown):
-                    piece, shown = full[len(shown):], full
-            if self.on_token is not None:
-                self.on_token(tok, piece)
+            self._history.append(tok)
+            generated += 1
+            is_stop = tok in stops
+            piece = "" if is_stop else stream.push(tok)
+            self._emit(tok, piece)
             if piece:
                 yield piece
-            if len(produced) >= max_new:
+            if is_stop:
+                reason = "stop"
+                break
+            if generated >= max_new:
                 break
             if self.capacity - self._kv.length < 1:
                 reason = "context"
                 break
             _, lg = self._engine.decode(self._kv, tok, self._kv.length, 1, want_logits=True)
-            self._history.append(tok)
             counter += 1
             tok = sample_token(self._engine, lg, temp, seed, counter, top_k, top_p)
-        torch.cuda.synchronize(dev)
+        _sync(dev)
         decode_s = time.perf_counter() - t1
-        gen = len(produced)
-        self.last = {"done": True, "reason": reason, "generated": gen, "prompt_tokens": len(prompt),
-                     "prefill_s": prefill_s, "decode_s": decode_s,
-                     "decode_tok_s": (gen - 1) / decode_s if gen > 1 and decode_s > 0 else 0.0,
-                     "position": self._kv.length}
+        rest = self._finish(reason, generated, len(prompt), prefill_s, decode_s, stream)
+        if rest:
+            yield rest
 
     # ---- lifetime ----------------------------------------------------------------------------
     def close(self):

@@ -1,6 +1,8 @@
 """`NativeEngine` and the per-GPU HIVE executor on the GPU: greedy tokens identical to the oracle,
-the reference's `last` fields, stop-token cut with cache rollback, reset; temperature sampling
-(the device draw bit-exact with its CPU restatement, runs reproducible from the seed)."""
+the reference engine's run semantics (`qwen_vk.cpp:588-613`: the stop token emitted and counted,
+the last sampled token kept unprocessed in the session and processed by the next request), reset;
+temperature sampling (the device draw bit-exact with its CPU restatement, runs reproducible from
+the seed)."""
 import pytest
 import torch
 
@@ -35,11 +37,19 @@ def test_native_engine_generate_matches_oracle(bundle):
         assert eng.last_tokens == want
         last = eng.last
         assert last["done"] and last["reason"] == "length" and last["generated"] == 40
-        assert last["prompt_tokens"] == len(prompt) and last["position"] == len(prompt) + 39
-        # a stop token cuts the output and rolls the cache back to the emitted tokens
+        assert last["prompt_tokens"] == len(prompt) and last["position"] == len(prompt) + 40
+        st = eng.state()
+        assert st["position"] == len(prompt) + 40 and st["processed"] == len(prompt) + 39
+        # a stop token ends the run: emitted and counted, kept in the session unprocessed
+        k = want.index(want[5])
         list(eng.generate(ids=prompt, max_new_tokens=40, stop=[want[5]]))
-        assert eng.last_tokens == want[:5] and eng.last["reason"] == "stop"
-        assert eng.state()["position"] == len(prompt) + 5
+        assert eng.last_tokens == want[:k + 1] and eng.last["reason"] == "stop" and eng.last["generated"] == k + 1
+        st = eng.state()
+        assert st["tokens"] == prompt + want[:k + 1] and st["processed"] == len(prompt) + k
+        # a request without reset continues the session: the pending stop token is processed first
+        more = random_prompt(cfg.vocab, 3, seed=9)
+        list(eng.generate(ids=more, reset=False, max_new_tokens=6))
+        assert eng.last_tokens == OracleQwen2(cfg, w, kv_fp16=True).greedy(prompt + want[:k + 1] + more, 6)[0]
         # reset=True starts over: same tokens again
         list(eng.generate(ids=prompt, max_new_tokens=7))
         assert eng.last_tokens == want[:7]
@@ -90,14 +100,14 @@ def test_native_engine_temperature_sampling(bundle):
         list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11))
         a = list(eng.last_tokens)
         assert len(a) == 24 and all(0 <= t < cfg.vocab for t in a)
-        assert eng.last["reason"] == "length" and eng.last["position"] == len(prompt) + 23
+        assert eng.last["reason"] == "length" and eng.last["position"] == len(prompt) + 24
         list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11))
         assert eng.last_tokens == a                      # the seed reproduces the run
         list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=12))
         assert eng.last_tokens != a                      # another seed, another run
-        # a stop token ends the run before it
+        # a stop token ends the run with it
         list(eng.generate(ids=prompt, max_new_tokens=24, temperature=5.0, seed=11, stop=[a[4]]))
-        assert eng.last_tokens == a[:a.index(a[4])] and eng.last["reason"] == "stop"
+        assert eng.last_tokens == a[:a.index(a[4]) + 1] and eng.last["reason"] == "stop"
 
 
 def test_native_engine_top_k_top_p_sampling(bundle):
@@ -147,11 +157,12 @@ def test_serve_executable_matches_in_process_engine(bundle):
             if r.get("done"):
                 break
             toks.append(r["token"])
-        assert toks == want and r["generated"] == 9 and r["position"] == len(prompt) + 8
+        assert toks == want and r["generated"] == 9 and r["position"] == len(prompt) + 9
         p.stdin.write(json.dumps({"op": "state"}) + "\n")
         p.stdin.flush()
         st = json.loads(p.stdout.readline())
-        assert st["position"] == len(prompt) + 8 and st["tokens"] == (prompt + want)[:st["position"]]
+        assert st["position"] == len(prompt) + 9 and st["processed"] == len(prompt) + 8
+        assert st["tokens"] == prompt + want
     finally:
         p.stdin.close()
         p.wait(timeout=60)

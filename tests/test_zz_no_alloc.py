@@ -55,3 +55,17 @@ def test_noalloc_rejects_oversize_without_launching(engine):
     # still usable afterwards
     x[:, 3] = 1.0
     assert (argmax_noalloc(x[:128]) == 3).all()
+
+
+def test_noalloc_rejects_host_buffers_and_keeps_the_current_device(engine):
+    """Host memory is refused before anything is launched, and the calling thread's current device
+    is the same after a call as before it."""
+    import ctypes as C
+    from seedplane_b200 import _native as N
+    before = torch.cuda.current_device()
+    host = torch.zeros((2, 16), dtype=torch.float32)
+    out = torch.zeros(2, dtype=torch.int32, device=engine.device)
+    rc = N.load().sp_argmax_noalloc(engine.device.index or 0, C.c_void_p(host.data_ptr()), 2, 16, 16,
+                                    C.c_void_p(out.data_ptr()), None)
+    assert rc != 0 and "device memory" in N.load().sp_last_error().decode()
+    assert torch.cuda.current_device() == before
