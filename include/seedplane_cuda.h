@@ -152,6 +152,20 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
                          int32_t vocab, const int32_t *tokens_host, const int32_t *parents_host, int32_t n,
                          double temperature, uint64_t seed, uint64_t counter, int32_t *out_host, void *stream);
 
+/* The batched pass's projection on its own: y[t][n] = alpha * W[n, :] . (x[t] + x[lo_row0 + t]),
+ * t < t, n < n, over k inputs, on the tcgen05 multi-column GEMM of the engine's device (no reference
+ * counterpart: it is the contraction under sp_forward's prompt chunks and sp_verify_tree, which
+ * replace qwen_vk.cpp:417-436's gemm_b.comp batch and speculative.py:55-92's per-prefix target calls;
+ * exposed for callers and tests of that contraction). W: row-major fp16 [n, k] (w_lo_dev: optional
+ * second fp16 half, W = w + w_lo); x: fp16 rows [x_rows, k], token t's hi half at row t, its lo
+ * half at row lo_row0 + t. mode 0: y[t * ldy + n] = ...; 1: y[t * ldy + n] += ...; 2 (SwiGLU): rows
+ * 2i, 2i + 1 are gate i, up i, and a = SiLU(gate) * up goes to act_hi[t * ld_act + i] = fp16(a),
+ * act_lo[...] = fp16(a - hi). t <= 512; k a multiple of 8; the engine's GEMM workspace is used,
+ * so calls on one engine are ordered on one stream. */
+int sp_mcol_gemm(sp_engine *e, int32_t mode, const void *w_dev, const void *w_lo_dev, float alpha, int32_t n, int32_t k,
+                 const void *x_dev, int32_t x_rows, int32_t lo_row0, int32_t t, float *y_dev, int32_t ldy,
+                 void *act_hi_dev, void *act_lo_dev, int32_t ld_act, void *stream);
+
 /* Top-k / top-p filter of one logits row before a draw (replaces the masking steps of
  * seedplane/qwen_engine.py:147-156, Qwen2Engine.sample): z_dev[j] = logits_dev[j] / temperature
  * (fp32); then, if top_k > 0, -inf below the top_k-th largest z (ties at the cut kept); then, if

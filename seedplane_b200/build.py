@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libseedplane_cuda.so"
-SOURCES = ["kernels.cu", "gemv_tc.cu", "attention.cu", "argmax.cu", "step.cu", "prefill.cu", "sample.cu", "engine.cu"]
+SOURCES = ["kernels.cu", "gemv_tc.cu", "attention.cu", "argmax.cu", "step.cu", "prefill.cu", "mcol.cu", "sample.cu", "engine.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -62,9 +62,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags=()) -> Path:
             sys.stderr.write(r.stderr)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cuda_lib = Path(nvcc).resolve().parent.parent / "lib64"
-    cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-cudart", "static", f"-L{cuda_lib}", "-lcublas",
-           "-Xlinker", f"-rpath={cuda_lib}"]
+    cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-cudart", "static"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc link failed:\n{r.stdout}\n{r.stderr}")

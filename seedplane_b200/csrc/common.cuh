@@ -68,6 +68,10 @@ SP_DEVINL void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
+SP_DEVINL void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Non-blocking probe of a phase (mbarrier.try_wait may suspend the thread for a while; this never does).
 SP_DEVINL bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;

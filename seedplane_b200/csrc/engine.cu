@@ -142,7 +142,6 @@ struct sp_engine {
     std::map<sp_kv *, cudaGraphExec_t> graphs;
     // batched prompt pass (prefill.cu); off with SEEDPLANE_PREFILL=steps
     bool prefill = false;
-    void *blas = nullptr;                   // cublasHandle_t
     PrefillDims pf_dims{};
     PrefillScratch pf{};
     uint8_t *pf_mem = nullptr;
@@ -152,7 +151,6 @@ struct sp_engine {
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
     int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
-    void *blas_ws = nullptr;
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
     std::vector<sp_kv *> caches;
 };
@@ -706,10 +704,12 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     std::vector<int> head_rows(VP);
     for (size_t i = 0; i < VP; ++i) head_rows[i] = i < V ? (int)i : -1;
     idx.insert(idx.end(), head_rows.begin(), head_rows.end());
+    for (size_t i = 0; i < I; ++i) idx.push_back((int)i);
     SP_TRY(cudaMalloc(&d_idx, idx.size() * 4));
     SP_TRY(cudaMemcpy(d_idx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice));
     const int *d_head_rows = d_idx + QRp + GUp + n_iota;
     const int *d_perm = d_idx, *d_gu = d_idx + QRp, *d_iota = d_idx + QRp + GUp;
+    const int *d_seq = d_idx + QRp + GUp + n_iota + VP;      // 0, 1, .., I - 1
     SP_TRY(cudaMemcpyAsync(A + o_embed, w->embed, V * H * 2, cudaMemcpyDeviceToDevice, s));
     const __half *head_src = (const __half *)(c.tied_embeddings ? w->embed : w->lm_head);
     auto pack = [&](uint8_t *dst, const void *a, const void *as, int rows_a, const void *b, const void *bs,
@@ -731,6 +731,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // (fp16 range, and the lo halves of the large weights stay normal); one alpha = 2^-k per matrix
     auto dequant = [&](size_t hi_off, size_t lo_off, const void *q1, const void *s1, int rows1, const void *q2,
                        const void *s2, int rows2, int K, PrefillMat &m) -> cudaError_t {
+        // with a second matrix (gate_up: gate, then up) the rows are interleaved: 2i = q1 row i, 2i + 1 = q2 row i
         float mx = 0.f, mx2 = 0.f;
         cudaError_t er = launch_int8_absmax(d_absmax, (const __half *)s1, (long long)rows1 * (K / 32), s);
         if (er == cudaSuccess) er = cudaMemcpyAsync(&mx, d_absmax, 4, cudaMemcpyDeviceToHost, s);
@@ -742,10 +743,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         int k = 0;
         if (mx > 0.f && std::isfinite(mx)) k = std::min(30, std::max(-30, (int)std::floor(std::log2(32768.0 / mx))));
         __half *hi = (__half *)(A + hi_off), *lw = (__half *)(A + lo_off);
-        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, s);
+        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, q2 ? 2 : 1, 0, s);
         if (er == cudaSuccess && q2)
-            er = launch_dequant_hilo(hi + (size_t)rows1 * K, lw + (size_t)rows1 * K, (const int8_t *)q2,
-                                     (const __half *)s2, rows2, K, k, s);
+            er = launch_dequant_hilo(hi, lw, (const int8_t *)q2, (const __half *)s2, rows2, K, k, 2, 1, s);
         m.hi = hi;
         m.lo = lw;
         m.alpha = ldexpf(1.0f, -k);
@@ -783,8 +783,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         } else if (e->prefill) {
             SP_TRY(cudaMemcpyAsync(A + lo[l].rqkv, Lw.qkv_w, QR * H * 2, cudaMemcpyDeviceToDevice, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].ro, Lw.o_w, H * (size_t)c.heads * HD * 2, cudaMemcpyDeviceToDevice, s));
-            SP_TRY(cudaMemcpyAsync(A + lo[l].rgu, Lw.gate_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
-            SP_TRY(cudaMemcpyAsync(A + lo[l].rgu + I * H * 2, Lw.up_w, I * H * 2, cudaMemcpyDeviceToDevice, s));
+            // gate and up rows interleaved (2i = gate i, 2i + 1 = up i): the GEMM's SwiGLU epilogue pairs them
+            SP_TRY(launch_gather_rows(A + lo[l].rgu, (const uint8_t *)Lw.gate_w, d_seq, (int)I, (int)H * 2, 2, 0, s));
+            SP_TRY(launch_gather_rows(A + lo[l].rgu, (const uint8_t *)Lw.up_w, d_seq, (int)I, (int)H * 2, 2, 1, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].rdn, Lw.down_w, H * I * 2, cudaMemcpyDeviceToDevice, s));
             L.pf.qkv = PrefillMat{(const __half *)(A + lo[l].rqkv), nullptr, 1.0f};
             L.pf.o = PrefillMat{(const __half *)(A + lo[l].ro), nullptr, 1.0f};
@@ -962,8 +963,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->pf_bytes = prefill_scratch_bytes(e->pf_dims);
         SP_TRY(cudaMalloc(&e->pf_mem, e->pf_bytes));
         e->pf = prefill_scratch_at(e->pf_mem, e->pf_dims);
-        SP_TRY(cudaMalloc(&e->blas_ws, kPrefillBlasWorkspace));
-        SP_TRY(prefill_blas_create(&e->blas, e->blas_ws, kPrefillBlasWorkspace));
+        SP_TRY(cudaMemset(e->pf.cnt, 0, (size_t)e->pf.cnt_count * sizeof(unsigned)));   // the GEMM keeps them zero
         SP_TRY(cudaMalloc(&e->vt, sizeof(VerifyIn) + kSmallNodes * sizeof(int32_t)));
         e->vt_argmax = reinterpret_cast<int32_t *>(e->vt + 1);
     }
@@ -1069,8 +1069,6 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->pf_mem);
     cudaFree(e->vt);
     cudaFree(e->acc_scratch);
-    prefill_blas_destroy(e->blas);
-    cudaFree(e->blas_ws);
     delete e;
 }
 
@@ -1162,7 +1160,6 @@ static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const in
     const sp_config &c = e->c;
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const float scale = 1.0f / sqrtf((float)c.head_dim);
-    SP_CUDA(prefill_blas_stream(e->blas, s));
     for (int32_t b0 = 0; b0 < n; b0 += kPrefillMaxTokens) {
         const int T = std::min<int32_t>(kPrefillMaxTokens, n - b0);
         SP_CUDA(launch_prefill_embed(e->pf_dims, e->pf, e->embed, tok + b0, T, e->st, s));
@@ -1170,13 +1167,13 @@ static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const in
             const PrefillLayer &L = e->layers[l].pf;
             SP_CUDA(launch_prefill_layer_front(e->pf_dims, L, e->pf, T, pos ? pos + b0 : nullptr,
                                                mask ? mask + b0 : nullptr, kv->k + l * kv_layer, kv->v + l * kv_layer,
-                                               kv->capacity, slot_base, b0, scale, e->rope, e->st, e->blas, s));
-            SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->blas, s));
+                                               kv->capacity, slot_base, b0, scale, e->rope, e->st, s));
+            SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->st, s));
         }
         for (int r0 = 0; r0 < T; r0 += kPrefillLogitRows) {
             const int rows = std::min(kPrefillLogitRows, T - r0);
             float *out = all_logits && logits ? logits + (size_t)(b0 + r0) * c.vocab : e->pf.logits;
-            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_pf, r0, rows, out, e->blas, s));
+            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_pf, r0, rows, out, e->st, s));
             SP_CUDA(launch_argmax_rows(out, rows, c.vocab, c.vocab, argmax + b0 + r0, e->am, s));
             if (!all_logits && logits && b0 + r0 + rows == n)
                 SP_CUDA(cudaMemcpyAsync(logits, out + (size_t)(rows - 1) * c.vocab, (size_t)c.vocab * 4,
@@ -1357,6 +1354,44 @@ int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols,
         SP_CUDA(launch_argmax_rows(logits_dev + (size_t)r0 * ld, n, cols, ld, argmax_dev + r0, e->am,
                                    (cudaStream_t)stream));
     }
+    return SP_OK;
+}
+
+int sp_mcol_gemm(sp_engine *e, int32_t mode, const void *w_dev, const void *w_lo_dev, float alpha, int32_t n, int32_t k,
+                 const void *x_dev, int32_t x_rows, int32_t lo_row0, int32_t t, float *y_dev, int32_t ldy,
+                 void *act_hi_dev, void *act_lo_dev, int32_t ld_act, void *stream) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    if (!e->prefill) return fail(SP_ERR_UNSUPPORTED, "the engine was created without the batched pass");
+    if (!w_dev || !x_dev || n <= 0 || k <= 0 || t <= 0 || t > x_rows || lo_row0 < t || lo_row0 + t > x_rows)
+        return fail(SP_ERR_INVALID, "bad GEMM shape n=%d k=%d t=%d x_rows=%d lo_row0=%d", n, k, t, x_rows, lo_row0);
+    if (t > kPrefillMaxTokens) return fail(SP_ERR_CAPACITY, "%d tokens exceed %d", t, kPrefillMaxTokens);
+    if (mode < MC_STORE || mode > MC_SWIGLU) return fail(SP_ERR_INVALID, "mode %d", mode);
+    if (mode == MC_SWIGLU ? (!act_hi_dev || !act_lo_dev || n % 2 || ld_act < n / 2) : (!y_dev || ldy < n))
+        return fail(SP_ERR_INVALID, "bad GEMM output");
+    SP_CUDA(cudaSetDevice(e->device));
+    McolOp op{};
+    op.mode = mode;
+    op.w = (const __half *)w_dev;
+    op.w_lo = (const __half *)w_lo_dev;
+    op.alpha = alpha;
+    op.N = n;
+    op.K = k;
+    op.x = (const __half *)x_dev;
+    op.x_rows = x_rows;
+    op.lo_row0 = lo_row0;
+    op.T = t;
+    op.y = y_dev;
+    op.ldy = ldy;
+    op.act_h = (__half *)act_hi_dev;
+    op.act_l = (__half *)act_lo_dev;
+    op.ld_act = ld_act;
+    op.ws = e->pf.ws;
+    op.ws_bytes = e->pf.ws_bytes;
+    op.cnt = e->pf.cnt;
+    op.cnt_count = e->pf.cnt_count;
+    op.max_ctas = kPrefillMaxCtas;
+    op.st = e->st;
+    SP_CUDA(launch_mcol(op, (cudaStream_t)stream, false));
     return SP_OK;
 }
 

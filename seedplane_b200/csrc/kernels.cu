@@ -52,10 +52,6 @@ SP_DEVINL uint32_t pack_half2(__half lo, __half hi) {
     return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
-SP_DEVINL void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // The CTA whose unit range [floor(U*c/C), floor(U*(c+1)/C)) contains unit u.
 SP_DEVINL int cta_of(int u, int U, int C) {
     int c = (int)(((long long)u * C) / U);

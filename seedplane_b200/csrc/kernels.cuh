@@ -275,12 +275,13 @@ cudaError_t prepare_step(int hd, size_t smem, bool q8);   // q8: the build with 
 cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8);
 
 // ---- batched prompt pass: prefill.cu ------------------------------------------------------------
-// T prompt tokens per chunk through all layers at once: cuBLAS GEMMs (fp16 x fp16 -> fp32) on
-// row-major weight copies with the activation split into fp16 hi / lo halves, and this engine's
-// kernels for the norms, RoPE + K/V write, causal attention and SwiGLU.
+// T prompt tokens per chunk through all layers at once: the multi-column tcgen05 GEMM (mcol.cu)
+// on row-major weight copies with the activation split into fp16 hi / lo halves, and this engine's
+// kernels for the norms, RoPE + K/V write and causal attention.
 constexpr int kPrefillMin = 8;           // shorter inputs run as step launches
-constexpr int kPrefillMaxTokens = 512;   // tokens per chunk (scratch size)
+constexpr int kPrefillMaxTokens = 512;   // tokens per chunk (scratch size; a multiple of 128)
 constexpr int kPrefillLogitRows = 64;    // logits rows per head GEMM (argmax scratch rows)
+constexpr int kPrefillMaxCtas = 148;     // GEMM CTAs at most (one per SM; workspace slots)
 
 struct PrefillDims {
     int hidden, inter, heads, kv_heads, head_dim, vocab, max_pos, max_tokens;
@@ -294,29 +295,31 @@ struct PrefillMat {                      // row-major fp16 weights W = alpha * (
 struct PrefillLayer {
     PrefillMat qkv;                      // [(heads + 2 kv_heads) * head_dim, hidden], natural row order
     PrefillMat o;                        // [hidden, heads * head_dim]
-    PrefillMat gate_up;                  // [2 inter, hidden]: gate rows, then up rows
+    PrefillMat gate_up;                  // [2 inter, hidden]: rows interleaved, 2i = gate i, 2i + 1 = up i
     PrefillMat down;                     // [hidden, inter]
     const float *qkv_b, *in_norm, *post_norm;
 };
 // Dequantize blockwise int8 rows (q [rows][K], fp16 scales [rows][K / 32]) into fp16 hi / lo halves
-// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi).
+// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi); source row r goes to row r * dst_mul + dst_add.
 cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                cudaStream_t s);
+                                int dst_mul, int dst_add, cudaStream_t s);
 // Largest |scale| * 127 of a blockwise-int8 matrix (n fp16 scales), into *out (device float).
 cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cudaStream_t s);
 struct PrefillScratch {
     float *x;                            // [T, hidden] residual stream
-    __half *xh, *xl;                     // GEMM inputs [2T, K]: hi rows then lo rows (xl unused)
-    float *y;                            // [2T, max(qkv rows, 2 inter)] GEMM outputs (hi rows, lo rows)
+    __half *xa;                          // GEMM inputs of norms and attention: hi rows [0, max_tokens), lo
+                                         // rows [max_tokens, 2 max_tokens), row stride = the GEMM's K
+    __half *xb;                          // the down projection's input (SwiGLU), same layout
+    float *y;                            // [T, qkv rows] QKV projection
     float *q;                            // [T, heads * head_dim]
     float *logits;                       // [kPrefillLogitRows, vocab]
+    float *ws;                           // multi-column GEMM split-K partials
+    size_t ws_bytes;
+    unsigned *cnt;                       // its per-tile counters (zero between launches)
+    long long cnt_count;
 };
 size_t prefill_scratch_bytes(const PrefillDims &d);
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d);
-constexpr size_t kPrefillBlasWorkspace = 32u << 20;
-cudaError_t prefill_blas_create(void **handle, void *workspace, size_t workspace_bytes);
-cudaError_t prefill_blas_stream(void *handle, cudaStream_t s);
-void prefill_blas_destroy(void *handle);
 cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,
                                  const int32_t *tok, int T, DevState *st, cudaStream_t stream);
 // RMSNorm, QKV GEMM, bias + RoPE + K/V write at slots *slot_base + slot_off .., attention
@@ -324,13 +327,54 @@ cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, 
 cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
                                        const int32_t *pos, const uint64_t *mask, __half *kc, __half *vc, int cap,
                                        const int *slot_base, int slot_off, float scale, const float *rope,
-                                       DevState *st, void *cublas, cudaStream_t stream);
-// RMSNorm, gate_up GEMM, SwiGLU, down GEMM (+= x)
+                                       DevState *st, cudaStream_t stream);
+// RMSNorm, gate_up GEMM with SwiGLU, down GEMM (+= x)
 cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
-                                     void *cublas, cudaStream_t stream);
+                                     DevState *st, cudaStream_t stream);
 // final RMSNorm of rows [r0, r0 + n) and the head GEMM into out [n, vocab]
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
-                                  const PrefillMat &head, int r0, int n, float *out, void *cublas, cudaStream_t stream);
+                                  const PrefillMat &head, int r0, int n, float *out, DevState *st, cudaStream_t stream);
+
+// ---- multi-column GEMM of the batched pass: mcol.cu ----------------------------------------------
+// Y[t][n] = alpha * W[n, :] . (x_hi[t] + x_lo[t]) on tcgen05 (weights = the M 128 operand, tokens'
+// hi / lo rows = the N operand), fused epilogue by mode. x: fp16 rows [x_rows, K], token t's hi row
+// at t, its lo row at lo_row0 + t. W: row-major fp16 [N, K], or two halves (w + w_lo).
+enum { MC_STORE = 0, MC_RESID = 1, MC_SWIGLU = 2 };
+struct McolOp {
+    int mode;                    // MC_STORE: y[t ldy + n] = ..; MC_RESID: += ..; MC_SWIGLU: see act_*
+    const __half *w, *w_lo;      // w_lo: second weight half or null
+    float alpha;
+    int N, K;
+    const __half *x;
+    int x_rows, lo_row0, T;
+    float *y;
+    int ldy;
+    __half *act_h, *act_l;       // MC_SWIGLU: rows 2i = gate i, 2i + 1 = up i; act[t ld_act + i] = hi / lo
+    int ld_act;
+    float *ws;                   // split-K partials (mcol_workspace_bytes) and per-tile counters (zeroed
+    size_t ws_bytes;             // once; the kernel leaves them zero)
+    unsigned *cnt;
+    long long cnt_count;
+    int max_ctas;
+    DevState *st;
+};
+struct McolParams {
+    int N, K, T, tn, lo_row0, two_w, split, stages, tmem_cols;
+    float alpha;
+    float *y;
+    int ldy;
+    __half *act_h, *act_l;
+    int ld_act;
+    float *ws;
+    unsigned *cnt;
+    DevState *st;
+};
+size_t mcol_max_smem();
+int mcol_tile_tokens(int T);
+size_t mcol_workspace_bytes(int max_ctas, int max_tokens);
+size_t mcol_counter_count(int max_rows, int max_tokens);
+// pdl: programmatic dependent launch after the previous kernel in the stream
+cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl);
 
 // Per-row top-k (k <= kTopkMax; larger value first, lower index on ties) and log-sum-exp of fp32
 // logits (sample.cu): idx / val [rows][k], lse [rows].

@@ -1,19 +1,17 @@
 // Batched prompt pass (prefill) for sm_100a: T prompt tokens per chunk through all layers at once.
 //
-// The projections of T tokens are plain GEMMs, [T, K] x [K, N], compute-bound at prompt lengths,
-// so they go to cuBLAS (fp16 operands, fp32 accumulation and output) on row-major copies of the
-// weights. Everything around them is this file's kernels: embedding gather, RMSNorm to fp16
-// hi / lo halves, bias + RoPE + K/V cache write, causal GQA attention over the cache, SwiGLU.
-// The activation of every GEMM is split like the decode step's: hi = fp16(x), lo = fp16(x - hi),
-// stacked as 2T columns [hi rows; lo rows] so ONE GEMM reads the weights once, and the epilogues
-// add the two halves (W x = W hi + W lo): the products carry ~22 bits of the fp32 activation
-// against the fp16 weights — the decode step's precision, which greedy token identity with the
-// fp32 reference depends on. The residual stream stays fp32.
+// The projections of T tokens go to the multi-column tcgen05 GEMM of mcol.cu (weights as the
+// M = 128 operand, the tokens as the N operand) with fused epilogues: the O and down projections
+// add into the fp32 residual stream, gate_up (rows interleaved gate / up) writes SwiGLU straight
+// into the down projection's input, QKV and the LM head store fp32. Around them: embedding gather,
+// RMSNorm to fp16 hi / lo halves, bias + RoPE + K/V cache write, causal GQA attention over the
+// cache. Every GEMM input is split like the decode step's: hi = fp16(x), lo = fp16(x - hi), token
+// t's hi row at t and its lo row at kPrefillMaxTokens + t of the input buffer, so the products carry
+// ~22 bits of the fp32 activation against the fp16 weights (the precision greedy token identity
+// with the fp32 reference depends on). The residual stream stays fp32.
 //
 // The same pass verifies a draft tree: the T tokens are tree nodes (K/V at scratch slots) and
 // node t attends to the committed prefix and to the nodes whose bits its ancestor mask holds.
-#include <cublas_v2.h>
-
 #include <algorithm>
 #include <cmath>
 
@@ -76,8 +74,9 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __hal
     }
 }
 
-// y[t] = [q heads | k heads | v heads] (natural row order): bias, RoPE on q and k with the
-// position of token t, q -> fp32, k and v -> the fp16 cache at slot slot0 + t.
+// y[t] = [q heads | k heads | v heads] (natural row order, hi + lo already summed by the GEMM):
+// bias, RoPE on q and k with the position of token t, q -> fp32, k and v -> the fp16 cache at slot
+// slot0 + t.
 __global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, const float *bias, const float *rope,
                               const int32_t *pos, int T, int nh, int nkv, int hd, int cap, const int *slot_base,
                               int slot_off, int max_pos, DevState *st) {
@@ -88,12 +87,12 @@ __global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, 
         if (threadIdx.x == 0) set_err(st, kErrBadSlot);
         p = min(max(p, 0), max_pos - 1);
     }
-    const float *yr = y + (size_t)t * heads * hd, *yl = y + (size_t)(T + t) * heads * hd;
+    const float *yr = y + (size_t)t * heads * hd;
     const int slot = slot0 + t;
     for (int i = threadIdx.x; i < heads * half_hd; i += blockDim.x) {
         const int hh = i / half_hd, d = i - hh * half_hd;
         const int lo = hh * hd + d, hi = lo + half_hd;
-        const float a0 = (yr[lo] + yl[lo]) + bias[lo], a1 = (yr[hi] + yl[hi]) + bias[hi];
+        const float a0 = yr[lo] + bias[lo], a1 = yr[hi] + bias[hi];
         if (hh < nh + nkv) {
             const float cs = rope[((size_t)p * half_hd + d) * 2], sn = rope[((size_t)p * half_hd + d) * 2 + 1];
             const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
@@ -243,73 +242,16 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
     }
 }
 
-// act = SiLU(gate) * up as fp16 hi / lo; rows t and T + t of y are the two halves of [gate | up]
-__global__ void k_swiglu_hilo(__half *ah, __half *al, const float *y, int T, int I) {
-    const int t = blockIdx.x;
-    const float *g = y + (size_t)t * 2 * I, *u = g + I;
-    const float *gl = y + (size_t)(T + t) * 2 * I, *ul = gl + I;
-    for (int j = threadIdx.x; j < I; j += blockDim.x) {
-        const float y0 = g[j] + gl[j], y1 = u[j] + ul[j];
-        const float a = (y0 / (1.0f + expf(-y0))) * y1;
-        const __half hv = __float2half_rn(a);
-        ah[(size_t)t * I + j] = hv;
-        al[(size_t)t * I + j] = __float2half_rn(a - __half2float(hv));
-    }
-}
-
-// out[t] = y[t] + y[n + t] (rows of `cols`); in place when out == y
-__global__ void k_sum_halves(float *out, const float *y, int n, int cols) {
-    const int t = blockIdx.y;
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += gridDim.x * blockDim.x)
-        out[(size_t)t * cols + j] = y[(size_t)t * cols + j] + y[(size_t)(n + t) * cols + j];
-}
-
-// x[t] += y[t] + y[T + t]: the two halves of a projection into the residual stream
-__global__ void k_resid_add(float *x, const float *y, int T, int H) {
-    const int t = blockIdx.x;
-    for (int j = threadIdx.x; j < H; j += blockDim.x)
-        x[(size_t)t * H + j] += y[(size_t)t * H + j] + y[(size_t)(T + t) * H + j];
-}
-
-// Y2[2T, N] (row-major) = W[N, K] (row-major) . X2[2T, K]^T, X2 = [hi rows; lo rows]: one GEMM per
-// weight half (W = alpha (hi + lo); fp16 checkpoints have no lo half)
-cublasStatus_t gemm_stacked(cublasHandle_t hb, const PrefillMat &w, int N, int K, const __half *x2, int T, float *y2) {
-    const float zero = 0.0f, one = 1.0f;
-    cublasStatus_t st = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &w.alpha, w.hi, CUDA_R_16F, K, x2,
-                                     CUDA_R_16F, K, &zero, y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    if (st != CUBLAS_STATUS_SUCCESS || w.lo == nullptr) return st;
-    return cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &w.alpha, w.lo, CUDA_R_16F, K, x2, CUDA_R_16F, K,
-                        &one, y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-}
-
-// Y[T, N] (row-major, ldy) = beta * Y + W[N, K] (row-major) . (Xh + Xl)[T, K]^T, one GEMM per input
-// half and weight half
-cublasStatus_t gemm_hilo(cublasHandle_t hb, const PrefillMat &w, int N, int K, const __half *xh, const __half *xl, int T,
-                         float *y, int ldy, float beta) {
-    const float one = 1.0f;
-    const __half *wh[2] = {w.hi, w.lo};
-    const __half *xs[2] = {xh, xl};
-    bool first = true;
-    for (int i = 0; i < 2; ++i) {
-        if (wh[i] == nullptr) continue;
-        for (int j = 0; j < 2; ++j) {
-            cublasStatus_t st = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &w.alpha, wh[i], CUDA_R_16F, K,
-                                             xs[j], CUDA_R_16F, K, first ? &beta : &one, y, CUDA_R_32F, ldy,
-                                             CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-            if (st != CUBLAS_STATUS_SUCCESS) return st;
-            first = false;
-        }
-    }
-    return CUBLAS_STATUS_SUCCESS;
-}
-
 // w = q * scale (exact in fp32), times 2^k (exact), split into fp16 hi = fp16(w') and lo =
 // fp16(w' - hi): hi + lo = w' exactly while w' and its remainder stay in fp16's normal range, which
 // the caller's k arranges for the matrix's largest weights. One thread per 8 inputs of a row.
-__global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, float p2) {
+__global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, float p2,
+                               int dst_mul, int dst_add) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)rows * (K / 8)) return;
     const long long e0 = idx * 8;
+    const long long r = e0 / K;
+    const long long d0 = (r * dst_mul + dst_add) * K + (e0 - r * K);   // destination row r * dst_mul + dst_add
     const float sc = __half2float(scales[e0 / 32]) * p2;
     const uint2 raw = *reinterpret_cast<const uint2 *>(q + e0);
     const int8_t *b = reinterpret_cast<const int8_t *>(&raw);
@@ -320,8 +262,8 @@ __global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __
         h[j] = __float2half_rn(w);
         l[j] = __float2half_rn(w - __half2float(h[j]));
     }
-    *reinterpret_cast<uint4 *>(hi + e0) = *reinterpret_cast<const uint4 *>(h);
-    *reinterpret_cast<uint4 *>(lo + e0) = *reinterpret_cast<const uint4 *>(l);
+    *reinterpret_cast<uint4 *>(hi + d0) = *reinterpret_cast<const uint4 *>(h);
+    *reinterpret_cast<uint4 *>(lo + d0) = *reinterpret_cast<const uint4 *>(l);
 }
 
 // max |scale| over n fp16 scales, times 127, into *out (non-negative floats compare as unsigned)
@@ -335,66 +277,111 @@ __global__ void k_int8_absmax(float *out, const __half *scales, long long n) {
 
 }  // namespace
 
+namespace {
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+size_t kmax_of(const PrefillDims &d) {
+    return std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
+}
+size_t qrows_of(const PrefillDims &d) { return (size_t)(d.heads + 2 * d.kv_heads) * d.head_dim; }
+}  // namespace
+
 size_t prefill_scratch_bytes(const PrefillDims &d) {
     const size_t T = d.max_tokens;
-    const size_t kmax = std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
-    const size_t nmax = std::max((size_t)(d.heads + 2 * d.kv_heads) * d.head_dim, 2 * (size_t)d.inter);
-    return T * d.hidden * 4 + 2 * T * kmax * 2 + 2 * T * nmax * 4 + T * d.heads * d.head_dim * 4 +
-           (size_t)kPrefillLogitRows * d.vocab * 4 + 5 * 256;
+    return up256(T * d.hidden * 4) + up256(2 * T * kmax_of(d) * 2) + up256(2 * T * d.inter * 2) +
+           up256(T * qrows_of(d) * 4) + up256(T * d.heads * d.head_dim * 4) + up256((size_t)kPrefillLogitRows * d.vocab * 4) +
+           up256(mcol_workspace_bytes(kPrefillMaxCtas, d.max_tokens)) + up256(kPrefillMaxCtas * sizeof(unsigned));
 }
 
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
-    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
     const size_t T = d.max_tokens;
-    const size_t kmax = std::max({(size_t)d.hidden, (size_t)d.inter, (size_t)d.heads * d.head_dim});
-    const size_t nmax = std::max((size_t)(d.heads + 2 * d.kv_heads) * d.head_dim, 2 * (size_t)d.inter);
     uint8_t *p = static_cast<uint8_t *>(base);
     PrefillScratch s{};
-    s.x = reinterpret_cast<float *>(p);
-    p += up(T * d.hidden * 4);
-    s.xh = reinterpret_cast<__half *>(p);      // [2T, kmax] halves: hi rows, then lo rows
-    p += up(2 * T * kmax * 2);
-    s.xl = nullptr;
-    s.y = reinterpret_cast<float *>(p);
-    p += up(2 * T * nmax * 4);
-    s.q = reinterpret_cast<float *>(p);
-    p += up(T * d.heads * d.head_dim * 4);
-    s.logits = reinterpret_cast<float *>(p);
+    auto take = [&](size_t bytes) { uint8_t *q = p; p += up256(bytes); return q; };
+    s.x = reinterpret_cast<float *>(take(T * d.hidden * 4));
+    s.xa = reinterpret_cast<__half *>(take(2 * T * kmax_of(d) * 2));
+    s.xb = reinterpret_cast<__half *>(take(2 * T * d.inter * 2));
+    s.y = reinterpret_cast<float *>(take(T * qrows_of(d) * 4));
+    s.q = reinterpret_cast<float *>(take(T * d.heads * d.head_dim * 4));
+    s.logits = reinterpret_cast<float *>(take((size_t)kPrefillLogitRows * d.vocab * 4));
+    s.ws_bytes = mcol_workspace_bytes(kPrefillMaxCtas, d.max_tokens);
+    s.ws = reinterpret_cast<float *>(take(s.ws_bytes));
+    s.cnt = reinterpret_cast<unsigned *>(take(kPrefillMaxCtas * sizeof(unsigned)));
+    s.cnt_count = kPrefillMaxCtas;
     return s;
 }
+
+namespace {
+// One projection of the chunk: x = rows of `in` (hi at t, lo at max_tokens + t, row stride K).
+McolOp proj(const PrefillDims &d, const PrefillScratch &s, const PrefillMat &w, int mode, int N, int K, const __half *in,
+            int T, DevState *st) {
+    McolOp op{};
+    op.mode = mode;
+    op.w = w.hi;
+    op.w_lo = w.lo;
+    op.alpha = w.alpha;
+    op.N = N;
+    op.K = K;
+    op.x = in;
+    op.x_rows = 2 * d.max_tokens;
+    op.lo_row0 = d.max_tokens;
+    op.T = T;
+    op.ws = s.ws;
+    op.ws_bytes = s.ws_bytes;
+    op.cnt = s.cnt;
+    op.cnt_count = s.cnt_count;
+    op.max_ctas = kPrefillMaxCtas;
+    op.st = st;
+    return op;
+}
+}  // namespace
 
 cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
                                        const int32_t *pos, const uint64_t *mask, __half *kc, __half *vc, int cap,
                                        const int *slot_base, int slot_off, float scale, const float *rope,
-                                       DevState *st, void *cublas, cudaStream_t stream) {
-    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
-    const int H = d.hidden, QR = (d.heads + 2 * d.kv_heads) * d.head_dim, A = d.heads * d.head_dim;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)T * H, s.x, L.in_norm, H, d.eps);
-    if (gemm_stacked(hb, L.qkv, QR, H, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+                                       DevState *st, cudaStream_t stream) {
+    const int H = d.hidden, QR = (int)qrows_of(d), A = d.heads * d.head_dim;
+    const size_t lo = (size_t)d.max_tokens;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xa, s.xa + lo * H, s.x, L.in_norm, H, d.eps);
+    McolOp qkv = proj(d, s, L.qkv, MC_STORE, QR, H, s.xa, T, st);
+    qkv.y = s.y;
+    qkv.ldy = QR;
+    cudaError_t e = launch_mcol(qkv, stream, false);
+    if (e != cudaSuccess) return e;
     k_qkv_rope_kv<<<T, 256, 0, stream>>>(s.q, kc, vc, s.y, L.qkv_b, rope, pos, T, d.heads, d.kv_heads, d.head_dim,
                                          cap, slot_base, slot_off, d.max_pos, st);
     const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
     if (d.head_dim == 128)
-        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xh, s.xh + (size_t)T * A, s.q, kc, vc, mask, T, d.heads,
-                                                      d.kv_heads, cap, slot_base, slot_off, scale, st);
+        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xa, s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads,
+                                                      cap, slot_base, slot_off, scale, st);
     else
-        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xh, s.xh + (size_t)T * A, s.q, kc, vc, mask, T, d.heads,
-                                                     d.kv_heads, cap, slot_base, slot_off, scale, st);
+        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xa, s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads,
+                                                     cap, slot_base, slot_off, scale, st);
     // O projection into the residual stream
-    if (gemm_stacked(hb, L.o, H, A, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-    k_resid_add<<<T, 256, 0, stream>>>(s.x, s.y, T, H);
+    McolOp o = proj(d, s, L.o, MC_RESID, H, A, s.xa, T, st);
+    o.y = s.x;
+    o.ldy = H;
+    e = launch_mcol(o, stream, false);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
-                                     void *cublas, cudaStream_t stream) {
-    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
+                                     DevState *st, cudaStream_t stream) {
     const int H = d.hidden, I = d.inter;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)T * H, s.x, L.post_norm, H, d.eps);
-    if (gemm_stacked(hb, L.gate_up, 2 * I, H, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-    k_swiglu_hilo<<<T, 256, 0, stream>>>(s.xh, s.xh + (size_t)T * I, s.y, T, I);
-    if (gemm_stacked(hb, L.down, H, I, s.xh, T, s.y) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-    k_resid_add<<<T, 256, 0, stream>>>(s.x, s.y, T, H);
+    const size_t lo = (size_t)d.max_tokens;
+    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xa, s.xa + lo * H, s.x, L.post_norm, H, d.eps);
+    // gate_up (rows interleaved: 2i gate, 2i + 1 up) -> SiLU(gate) * up as the down projection's input
+    McolOp gu = proj(d, s, L.gate_up, MC_SWIGLU, 2 * I, H, s.xa, T, st);
+    gu.act_h = s.xb;
+    gu.act_l = s.xb + lo * I;
+    gu.ld_act = I;
+    cudaError_t e = launch_mcol(gu, stream, false);
+    if (e != cudaSuccess) return e;
+    McolOp dn = proj(d, s, L.down, MC_RESID, H, I, s.xb, T, st);
+    dn.y = s.x;
+    dn.ldy = H;
+    e = launch_mcol(dn, stream, false);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -407,27 +394,24 @@ cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, 
 // Logits of rows [r0, r0 + n) of the chunk (n <= kPrefillLogitRows) into `out` (row stride vocab):
 // final RMSNorm, then the head GEMM.
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
-                                  const PrefillMat &head, int r0, int n, float *out, void *cublas, cudaStream_t stream) {
-    cublasHandle_t hb = static_cast<cublasHandle_t>(cublas);
+                                  const PrefillMat &head, int r0, int n, float *out, DevState *st, cudaStream_t stream) {
     const int H = d.hidden;
-    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xh, s.xh + (size_t)n * H, s.x + (size_t)r0 * H, final_norm, H,
-                                                    d.eps);
-    if (2 * n <= kPrefillLogitRows) {
-        // one pass over the head: [hi rows; lo rows] into the scratch, then the halves summed
-        if (gemm_stacked(hb, head, d.vocab, H, s.xh, n, s.logits) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-        k_sum_halves<<<dim3(64, n), 256, 0, stream>>>(out, s.logits, n, d.vocab);
-    } else if (gemm_hilo(hb, head, d.vocab, H, s.xh, s.xh + (size_t)n * H, n, out, d.vocab, 0.0f) !=
-               CUBLAS_STATUS_SUCCESS) {
-        return cudaErrorUnknown;
-    }
+    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xa, s.xa + (size_t)d.max_tokens * H, s.x + (size_t)r0 * H,
+                                                    final_norm, H, d.eps);
+    McolOp hd = proj(d, s, head, MC_STORE, d.vocab, H, s.xa, n, st);
+    hd.y = out;
+    hd.ldy = d.vocab;
+    cudaError_t e = launch_mcol(hd, stream, false);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                cudaStream_t s) {
-    if (K % 32 || k < -30 || k > 30) return cudaErrorInvalidValue;
+                                int dst_mul, int dst_add, cudaStream_t s) {
+    if (K % 32 || k < -30 || k > 30 || dst_mul < 1 || dst_add < 0 || dst_add >= dst_mul) return cudaErrorInvalidValue;
     const long long n = (long long)rows * (K / 8);
-    k_dequant_hilo<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(hi, lo, q, scales, rows, K, ldexpf(1.0f, k));
+    k_dequant_hilo<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(hi, lo, q, scales, rows, K, ldexpf(1.0f, k), dst_mul,
+                                                               dst_add);
     return cudaGetLastError();
 }
 
@@ -436,27 +420,6 @@ cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cu
     if (e != cudaSuccess) return e;
     k_int8_absmax<<<256, 256, 0, s>>>(out, scales, n);
     return cudaGetLastError();
-}
-
-cudaError_t prefill_blas_create(void **handle, void *workspace, size_t workspace_bytes) {
-    cublasHandle_t h = nullptr;
-    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-    // a fixed workspace: no allocation inside a captured graph
-    if (cublasSetWorkspace(h, workspace, workspace_bytes) != CUBLAS_STATUS_SUCCESS) {
-        cublasDestroy(h);
-        return cudaErrorUnknown;
-    }
-    *handle = h;
-    return cudaSuccess;
-}
-
-cudaError_t prefill_blas_stream(void *handle, cudaStream_t s) {
-    return cublasSetStream(static_cast<cublasHandle_t>(handle), s) == CUBLAS_STATUS_SUCCESS ? cudaSuccess
-                                                                                             : cudaErrorUnknown;
-}
-
-void prefill_blas_destroy(void *handle) {
-    if (handle) cublasDestroy(static_cast<cublasHandle_t>(handle));
 }
 
 }  // namespace sp

@@ -201,14 +201,6 @@ SP_DEVINL void unit_i8_issue(uint32_t tmem, uint32_t unit, int rows_p, int nb, u
     }
 }
 
-// 16 consecutive TMEM columns of this thread's lane (no wait).
-SP_DEVINL void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-                 : "r"(taddr));
-}
-
 // This thread's row (its TMEM lane) of one int8 unit of nb blocks (nb even): sum over blocks b of
 // row scale (sc2: fp16 pairs of blocks 2j, 2j + 1) * input block scale * (2^14 (128 d0 + d1) +
 // (128 d2 + d3)), the d's the block's digit columns 0-3 (the pairs are exact in s32), in fp32 and
@@ -263,10 +255,6 @@ SP_DEVINL void argmax_merge(float &v, int &i, float ov, int oi) {
         v = ov;
         i = oi;
     }
-}
-
-SP_DEVINL void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // The compute warps' barrier. A warp can leave bar.sync with its lanes still split (they arrived

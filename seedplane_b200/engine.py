@@ -267,6 +267,33 @@ class CudaQwen2:
         return out
 
 
+    def mcol_gemm(self, w: torch.Tensor, x: torch.Tensor, *, mode: str = "store", w_lo: Optional[torch.Tensor] = None,
+                  alpha: float = 1.0, y: Optional[torch.Tensor] = None, act: Optional[tuple] = None) -> torch.Tensor:
+        """The batched pass's projection (`sp_mcol_gemm`): alpha * W . x^T on the tcgen05 multi-column
+        GEMM, x split into fp16 hi / lo halves here. w: fp16 [N, K] (w_lo: a second half, W = w + w_lo);
+        x: fp32 [T, K]. mode "store" returns y [T, N]; "resid" adds into the given y [T, N]; "swiglu"
+        (rows 2i gate, 2i + 1 up) writes SiLU(gate) * up as fp16 hi / lo into act = (hi, lo) [T, N / 2]
+        and returns their sum as fp32."""
+        T, K = x.shape
+        Nrows = w.shape[0]
+        xs = torch.zeros((2 * T, K), dtype=torch.float16, device=self.device)
+        xf = x.to(self.device, torch.float32)
+        xs[:T] = xf.half()
+        xs[T:] = (xf - xs[:T].float()).half()
+        modes = {"store": 0, "resid": 1, "swiglu": 2}
+        if mode == "store":
+            y = torch.empty((T, Nrows), dtype=torch.float32, device=self.device)
+        elif mode == "swiglu":
+            act = act or (torch.empty((T, Nrows // 2), dtype=torch.float16, device=self.device),
+                          torch.empty((T, Nrows // 2), dtype=torch.float16, device=self.device))
+        ptr = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+        N.check(N.load().sp_mcol_gemm(self.handle, modes[mode], ptr(w), ptr(w_lo), float(alpha), Nrows, K, ptr(xs),
+                                      2 * T, T, T, ptr(y), Nrows, ptr(act[0]) if act else None,
+                                      ptr(act[1]) if act else None, Nrows // 2, C.c_void_p(_stream(self.device))))
+        if mode == "swiglu":
+            return act[0].float() + act[1].float()
+        return y
+
 def argmax_noalloc(logits: torch.Tensor) -> torch.Tensor:
     """Row-wise greedy argmax of fp32 logits [rows <= 128, V] through `sp_argmax_noalloc`: no engine
     and no device allocation in the library (its scratch is a fixed device array). Calls on one
