@@ -10,18 +10,29 @@ rolled back to 512 before each step, so every step does identical work). The met
 tokens per second; with N GPUs every rank runs its own replica (independent requests, no
 collective on the data path) and `value` = all ranks' tokens / the slowest rank's time.
 
+The decode line also carries: `e2e` through the drop-in surface (`NativeEngine.generate(ids=...)`
+on a checkpoint written to disk: host prompt in, generated tokens out, blocks of device decode);
+`burst` (every N: the 16 x 32 HIVE burst on the same engines, tok/s over the wall-clock makespan);
+and at N = 1 `verify` (cfg2: one 16-node tree-verify pass on the Qwen2-0.5B shape), `reference_gpu`
+(the reference's own `Qwen2Engine(device='cuda')`, fp16, from `baseline/_ref`, decoding the same
+256 tokens after the same prompt on the same GPU) and `cpu_baseline` (the oracle port on the host).
+
 Workload `burst`: the 16 x 32 independent-request burst (prompt lengths uniform in [32, 128]),
 requests pulled by one agent per GPU; aggregate tokens / makespan.
 
 `--impl reference` times the reference's CPU algorithm (the oracle port of `Qwen2Engine`) on the
-host cores for a bounded sample of the same workload; under torchrun only rank 0 runs it.
+host cores: one greedy token at each of the contexts 512, 576, 640, 704 and 768 per step (the
+window the timed decode covers), at the best thread count of a sweep; under torchrun only rank 0
+runs it.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import platform
 import statistics
+import tempfile
 import subprocess
 import sys
 import threading
@@ -168,51 +179,144 @@ def physical_cores():
         return os.cpu_count()
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+def thread_counts(n_max: int):
+    out, t = [], 1
+    while t < n_max:
+        out.append(t)
+        t *= 2
+    return out + [n_max]
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
     from seedplane_b200.config import QWEN2_1_5B
     from seedplane_b200.randinit import make_weights, random_prompt
+    from oracle.qwen_oracle import OracleQwen2
     cfg = QWEN2_1_5B
-    threads = physical_cores()
+    cores = physical_cores()
     w = make_weights(cfg, seed=0, dtype=torch.float16)
     prompt = random_prompt(cfg.vocab, PROMPT, seed=0)
-    from oracle.qwen_oracle import OracleQwen2
-    torch.set_num_threads(threads)
+    torch.set_num_threads(cores)
     o = OracleQwen2(cfg, w, kv_fp16=True)
     del w
+    # the cache holds the prompt and 256 more positions (teacher-forced), so a token can be decoded
+    # at every context of the timed window; the cost of a decode step depends on its context only
     cache = o.new_cache(CAPACITY)
-    logits, cache = o.forward(prompt, cache)
-    first = int(logits[-1].argmax())
-    per_step = 4   # tokens per step: a bounded sample of the 256-token decode
+    o.forward(prompt + random_prompt(cfg.vocab, DECODE, seed=1), cache)
+    contexts = [PROMPT + i * DECODE // 4 for i in range(5)]          # 512, 576, 640, 704, 768
+    tok = 0
 
     def step():
-        cache.length = PROMPT
-        tok = first
-        lg, _ = o.forward([tok], cache)
-        for _ in range(per_step - 1):
-            tok = int(lg[-1].argmax())
-            lg, _ = o.forward([tok], cache)
+        for c in contexts:
+            cache.length = c
+            o.forward([tok], cache)
 
+    sweep = {}
+    for t in thread_counts(cores):
+        torch.set_num_threads(t)
+        step()                                                       # warm this thread count
+        t0 = time.perf_counter()
+        step()
+        sweep[t] = len(contexts) / (time.perf_counter() - t0)
+    best = max(sweep, key=sweep.get)
+    torch.set_num_threads(best)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = time.perf_counter() - t0
-    value = args.steps * per_step / dt
+    value = args.steps * len(contexts) / dt
+    model = cpu_model()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "qwen2-1.5b decode after a 512-token prompt (fp16-rounded random-init "
-                                   "weights, fp16 K/V), oracle port of Qwen2Engine on the CPU",
-                       "tokens_per_step": per_step},
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": f"{per_step} greedy tokens at context 512 per step, torch "
-                                       f"{torch.__version__} fp32 on {threads} threads"},
+            "config": {"workload": "qwen2-1.5b greedy decode at contexts 512..768 after a 512-token prompt "
+                                   "(fp16-rounded random-init weights, fp16 K/V), oracle port of Qwen2Engine on the CPU",
+                       "tokens_per_step": len(contexts), "contexts": contexts},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": best, "kind": "port",
+                             "cpu_model": model, "physical_cores": cores,
+                             "thread_sweep_tok_s": {str(k): v for k, v in sweep.items()},
+                             "sample": f"one greedy token at each context {contexts} per step (the decode window of "
+                                       f"the GPU line), torch {torch.__version__} fp32 on {best} threads (best of "
+                                       f"the sweep {sorted(sweep)})"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def write_checkpoint(cfg, weights, directory: Path) -> Path:
+    """An HF-named safetensors checkpoint with its config.json (what `NativeEngine` and the
+    reference's `Qwen2Engine` load)."""
+    from safetensors.torch import save_file
+    directory.mkdir(parents=True, exist_ok=True)
+    (directory / "config.json").write_text(json.dumps(cfg.to_hf()))
+    save_file({k: v.contiguous() for k, v in weights.items()}, str(directory / "model.safetensors"))
+    return directory
+
+
+def native_e2e(ckpt: Path, prompt, want, steps: int, dev):
+    """`NativeEngine.generate(ids=prompt)` (the drop-in surface) for DECODE tokens per step: host
+    prompt in, the prefill, greedy decode in device blocks, every block's tokens back to the host."""
+    from seedplane_b200.native import NativeEngine
+    with NativeEngine(ckpt, ctx=CAPACITY, max_new_tokens=DECODE, extra_args=("--device", str(dev))) as ne:
+        list(ne.generate(ids=prompt))                                 # warm-up (captures the graphs)
+        assert ne.last_tokens == want, "NativeEngine tokens differ from the decode loop"
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            list(ne.generate(ids=prompt))
+        dt = time.perf_counter() - t0
+        assert ne.last_tokens == want
+    return steps * DECODE / dt, dt / steps
+
+
+def reference_gpu(ckpt: Path, prompt, ours, dev):
+    """The reference's own PyTorch engine (`seedplane.qwen_engine.Qwen2Engine`, installed unmodified in
+    baseline/_ref) on the same GPU, fp16 (its default on CUDA): the prompt, then DECODE greedy tokens
+    (contexts 512..767) timed on the wall clock with the device synchronized at both ends."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "seedplane" / "qwen_engine.py").exists():
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    from seedplane.qwen_engine import Qwen2Engine
+    torch.cuda.set_device(dev)
+    e = Qwen2Engine(ckpt, device=str(dev))
+
+    def run():
+        cache = e.new_cache(CAPACITY)
+        logits, cache = e.forward(prompt, cache)
+        toks = [int(logits[-1].argmax())]
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(DECODE - 1):
+            logits, cache = e.forward([toks[-1]], cache)
+            toks.append(int(logits[-1].argmax()))
+        torch.cuda.synchronize(dev)
+        return toks, time.perf_counter() - t0
+
+    run()
+    toks, dt = run()
+    match = next((i for i, (a, b) in enumerate(zip(toks, ours)) if a != b), len(toks))
+    del e
+    torch.cuda.empty_cache()
+    return {"value": (DECODE - 1) / dt, "unit": "tok/s", "dtype": "f16 (the reference's CUDA default)",
+            "kind": "reference Qwen2Engine(device='cuda') from baseline/_ref, unmodified",
+            "sample": f"{DECODE - 1} greedy tokens after the same {PROMPT}-token prompt, one forward per token",
+            "tokens_equal_ours_prefix": match}
 
 
 # --------------------------------------------------------------------------------------------
@@ -297,37 +401,54 @@ def run_decode(args, world, rank, local):
     traffic = traffic_per_token() if not i8 else None
     step_kernel = os.environ.get("SEEDPLANE_STEP", "step") != "chain"
 
-    # e2e through the public API: host prompt (pinned) -> device, prefill, decode, tokens -> host
-    from seedplane_b200.qwen_engine import KVCache
-    host_prompt = torch.tensor(prompt, dtype=torch.int32).pin_memory()
-    host_out = torch.empty(DECODE, dtype=torch.int32).pin_memory()
-    dev_prompt = torch.empty(PROMPT, dtype=torch.int32, device=dev)
+    # e2e through the drop-in surface: NativeEngine.generate(ids=...) on a checkpoint on disk (fp16
+    # path; the int8 line keeps the engine API: NativeEngine loads fp16 bundles)
+    want = [first] + tokens_ref[:-1]
     e2e_steps = max(1, min(args.steps, 3))
+    # one checkpoint on disk for every rank of the run (rank 0 writes it)
+    workdir = Path(tempfile.gettempdir()) / f"seedplane-bench-{os.environ.get('MASTER_PORT', os.getpid())}"
+    ckpt = None
+    if not i8:
+        ckpt = workdir / "ckpt"
+        if rank == 0:
+            write_checkpoint(cfg, w, ckpt)
+        barrier(world)
+        e2e_value, e2e_s = native_e2e(ckpt, prompt, want, e2e_steps, dev)
+        e2e_h2d, e2e_d2h = PROMPT * 4, DECODE * 4 + 4
+        e2e_note = (f"NativeEngine.generate(ids=prompt) per step: host ids in, prefill, {DECODE} greedy tokens "
+                    f"(device decode blocks of 32, each block's tokens to the host), wall clock")
+    else:
+        from seedplane_b200.qwen_engine import KVCache   # noqa: F401
+        host_prompt = torch.tensor(prompt, dtype=torch.int32).pin_memory()
+        host_out = torch.empty(DECODE, dtype=torch.int32).pin_memory()
+        dev_prompt = torch.empty(PROMPT, dtype=torch.int32, device=dev)
 
-    def e2e_step():
-        kv.length = 0
-        dev_prompt.copy_(host_prompt, non_blocking=True)
-        _, am = eng.forward(kv, dev_prompt, want_logits=False)
-        # the first generated token is read back (the reference's generate yields it to the host)
-        first_tok = int(am[-1])
-        eng.decode(kv, first_tok, PROMPT, DECODE - 1, out=out[1:])
-        out[0] = first_tok
-        host_out.copy_(out, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        def e2e_step():
+            kv.length = 0
+            dev_prompt.copy_(host_prompt, non_blocking=True)
+            _, am = eng.forward(kv, dev_prompt, want_logits=False)
+            first_tok = int(am[-1])
+            eng.decode(kv, first_tok, PROMPT, DECODE - 1, out=out[1:])
+            out[0] = first_tok
+            host_out.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
 
-    e2e_step()
-    barrier(world)
-    t0 = time.perf_counter()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
         e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - t0) * 1000.0)
-    e2e_ms = max_over_ranks(e2e_ms, world, dev)
-    assert host_out.tolist() == [first] + tokens_ref[:-1], "public-API tokens differ from the decode loop"
-    e2e_value = e2e_steps * DECODE * world / (e2e_ms / 1000.0)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        assert host_out.tolist() == want, "public-API tokens differ from the decode loop"
+        e2e_value = DECODE / e2e_s
+        e2e_h2d, e2e_d2h = PROMPT * 4, DECODE * 4 + 4
+        e2e_note = f"engine API per step: pinned prompt H2D, prefill, {DECODE}-token decode, tokens D2H"
+    e2e_value = world * DECODE / max_over_ranks(DECODE / e2e_value, world, dev)
+
+    # the 16 x 32 HIVE burst on these engines (every rank; fp16 headline only)
+    burst = None
+    if not i8 and not args.no_burst:
+        from seedplane_b200.hive.burst import burst_on_engine
+        burst = burst_on_engine(eng, 2, 3, world, rank, local, ClockSampler, max_over_ranks, barrier)
 
     line = None
     if rank == 0:
@@ -348,9 +469,8 @@ def run_decode(args, world, rank, local):
                              "kernel": ("k_step: persistent per-token decode kernel, one launch per token"
                                         if step_kernel else "one decode step: the GEMV / attention kernel chain"),
                              "algorithmic_bytes_per_launch": alg_bytes, "peak_kind": peak_kind},
-                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
-                        "d2h_bytes_per_step": DECODE * 4 + 4,
-                        "note": f"public API per step: pinned prompt H2D, prefill, {DECODE}-token decode, tokens D2H"},
+                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": e2e_h2d,
+                        "d2h_bytes_per_step": e2e_d2h, "note": e2e_note, "ms_per_step": 1000.0 * e2e_s},
                 "gpu_launches": args.steps * (DECODE * (1 if step_kernel else 5 * L + 1) + 1),
                 "clocks": clocks.summary(),
                 "token_sha256": __import__("hashlib").sha256(json.dumps(tokens_ref).encode()).hexdigest()}
@@ -358,6 +478,13 @@ def run_decode(args, world, rank, local):
             line["cpu_baseline"] = None
             line["cpu_baseline_note"] = ("not run: the oracle needs the 7B checkpoint dequantized to fp32 (28 GB) "
                                          "in host memory; int8 parity is covered by the tests on smaller shapes")
+        if burst is not None:
+            line["burst"] = burst
+        if world == 1 and not i8 and not args.no_extras:
+            line["verify"] = verify_measure(dev, args)
+            line["reference_gpu"] = reference_gpu(ckpt, prompt, want, dev)
+        if i8:
+            pass
         elif world == 1 and not args.no_cpu_baseline:
             threads = physical_cores()
             n = 200    # about 10 s of CPU work on a 16-core host
@@ -365,22 +492,25 @@ def run_decode(args, world, rank, local):
             line["cpu_baseline"] = {"value": val, "unit": "tok/s", "cores": threads, "kind": "port",
                                     "sample": f"{n} greedy tokens after the same 512-token prompt (prefill "
                                               f"untimed), oracle port fp32 on {threads} threads, {dt:.1f} s",
-                                    "tokens_match_gpu": toks == [first] + tokens_ref[:n - 1]}
+                                    "tokens_match_gpu": toks == [first] + tokens_ref[:n - 1],
+                                    "cpu_model": cpu_model()}
     eng.close()
+    barrier(world)
+    if rank == 0:
+        import shutil
+        shutil.rmtree(workdir, ignore_errors=True)
     return line
 
 
-def run_verify(args, world, rank, local):
-    """Tree-verify latency (the cfg2 shapes): Qwen2-0.5B-shaped fp16 target, a 128-token prompt, a
-    16-node draft tree of depth 4 (branching 4, 2, 1, 1 cut to 16 nodes); one batched device pass
-    per verify. `value` = microseconds per verify pass (device, CUDA events on the stream); `e2e`
-    adds the host side: tree arrays to the device and the 16 argmaxes back."""
+def verify_measure(dev, args):
+    """One batched verify pass of the cfg2 tree (Qwen2-0.5B-shaped fp16 target, a 128-token prompt, 16
+    nodes of branching 4, 2, 1, 1 at depth 4): device microseconds per pass (CUDA events over the
+    replays of its graph), and the host-side figure with the tree sent and the argmaxes read back."""
     import random
     from seedplane_b200.config import QWEN2_0_5B
     from seedplane_b200.engine import CudaQwen2
     from seedplane_b200.randinit import make_weights, random_prompt
     cfg = QWEN2_0_5B
-    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = make_weights(cfg, seed=0, dtype=torch.float16)
     eng = CudaQwen2(cfg, w, device=dev)
@@ -408,7 +538,7 @@ def run_verify(args, world, rank, local):
     ref = am.cpu().tolist()
     reps = max(10, args.steps * 20)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([local]) as clocks:
+    with ClockSampler([dev.index]) as clocks:
         torch.cuda.synchronize(dev)
         e0.record(stream)
         for _ in range(reps):
@@ -424,20 +554,33 @@ def run_verify(args, world, rank, local):
     e2e_us = (time.perf_counter() - t0) * 1e6 / reps
     eng.status()
     eng.close()
+    w_bytes = cfg.weight_bytes_per_token(2)
+    flops = 2.0 * w_bytes / 2 * len(tokens)
+    return {"metric": "tree verify us (16 nodes, Qwen2-0.5B-shaped target)", "value": us, "unit": "us",
+            "e2e_us": e2e_us, "nodes": len(tokens), "prompt": len(prompt), "reps": reps,
+            "tensor_tflops": flops / (us * 1e-6) / 1e12, "weights_gbs": w_bytes / (us * 1e-6) / 1e9,
+            "kernel": "batched pass: k_mcol (tcgen05 multi-column GEMM) + norm / attention kernels, one graph",
+            "argmax": host, "clocks": clocks.summary()}
+
+
+def run_verify(args, world, rank, local):
+    """Tree-verify latency (the cfg2 shapes) as the line's own metric: `value` = microseconds per
+    verify pass (device, CUDA events on the stream); `e2e` adds the host side: tree arrays to the
+    device and the 16 argmaxes back."""
+    dev = torch.device("cuda", local)
+    v = verify_measure(dev, args)
     if rank != 0:
         return None
-    flops = 2.0 * cfg.weight_bytes_per_token(2) / 2 * len(tokens)
-    return {"metric": "tree verify us (16 nodes, Qwen2-0.5B-shaped target)", "value": us, "unit": "us",
-            "n_gpus": 1, "steps": reps, "warmup": max(3, args.warmup), "ms_per_step": us / 1000.0,
+    return {"metric": v["metric"], "value": v["value"], "unit": "us",
+            "n_gpus": 1, "steps": v["reps"], "warmup": max(3, args.warmup), "ms_per_step": v["value"] / 1000.0,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "one batched verify pass of a 16-node depth-4 draft tree (branching 4,2,1,1 cut "
                                    "to 16) after a 128-token prompt, qwen2-0.5b random-init fp16 target",
-                       "nodes": len(tokens), "prompt": len(prompt),
-                       "tensor_tflops": flops / (us * 1e-6) / 1e12,
-                       "l2": "inputs larger than L2: 0.99 GB of weights per pass"},
-            "e2e": {"value": e2e_us, "unit": "us", "h2d_bytes_per_step": len(tokens) * 16,
-                    "d2h_bytes_per_step": len(tokens) * 4},
-            "clocks": clocks.summary(), "argmax": host}
+                       "nodes": v["nodes"], "prompt": v["prompt"], "tensor_tflops": v["tensor_tflops"],
+                       "weights_gbs": v["weights_gbs"], "l2": "inputs larger than L2: 0.99 GB of weights per pass"},
+            "e2e": {"value": v["e2e_us"], "unit": "us", "h2d_bytes_per_step": v["nodes"] * 16,
+                    "d2h_bytes_per_step": v["nodes"] * 4},
+            "clocks": v["clocks"], "argmax": v["argmax"]}
 
 
 def run_speculative(args, world, rank, local):
@@ -515,6 +658,9 @@ def main():
     ap.add_argument("--workload", choices=("decode", "decode-7b-i8", "burst", "verify", "speculative"),
                     default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-burst", action="store_true", help="leave the HIVE burst out of the decode line")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="leave the verify and reference_gpu objects out of the decode line")
     args = ap.parse_args()
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -198,7 +198,9 @@ int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t
  * GEMV of the step (4 per layer, then the LM head) and each CTA, kernel-start / dependency-wait /
  * prologue / stream / epilogue stamps and per-unit issue and ready stamps of %globaltimer (ns).
  * host_out NULL: returns the number of 64-bit words; else copies them (synchronizes the device)
- * and returns the count. Returns 0 when tracing is off. The reference had no GPU timestamps
+ * and returns the count. Returns 0 when tracing is off. With SEEDPLANE_MCOL_TRACE=1 (and no step
+ * trace) it returns the last sp_mcol_gemm launch's per-CTA phase stamps instead (16 words per CTA,
+ * 148 CTAs). The reference had no GPU timestamps
  * (experiments/v18/RESULTS.md:29-30). */
 int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity);
 

@@ -30,6 +30,8 @@ SP_DEVINL void am_take(float &bv, int &bi, float v, int i) {
 
 __global__ void __launch_bounds__(kArgmaxThreads) k_argmax_rows(const float *logits, int cols, long long ld, int *out,
                                                                 const ArgmaxScratch sc) {
+    griddep_wait();               // launched after the pass's head GEMM (programmatic launch)
+    griddep_launch_dependents();
     __shared__ float s_v[kArgmaxThreads / 32];
     __shared__ int s_i[kArgmaxThreads / 32];
     const int row = blockIdx.y, cta = blockIdx.x, nct = gridDim.x;
@@ -120,7 +122,17 @@ cudaError_t argmax_noalloc_scratch(void **base) { return cudaGetSymbolAddress(ba
 cudaError_t launch_argmax_rows(const float *logits, int rows, int cols, long long ld, int *out, const ArgmaxScratch &sc,
                                cudaStream_t s) {
     if (rows <= 0 || rows > 65535 || cols <= 0 || ld < cols) return cudaErrorInvalidValue;
-    k_argmax_rows<<<dim3(argmax_ctas(cols), rows), kArgmaxThreads, 0, s>>>(logits, cols, ld, out, sc);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(argmax_ctas(cols), rows);
+    cfg.blockDim = dim3(kArgmaxThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_argmax_rows, logits, cols, ld, out, sc);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -152,6 +152,7 @@ struct sp_engine {
     int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
+    unsigned long long *mc_trace = nullptr;  // SEEDPLANE_MCOL_TRACE: stamps of the last multi-column GEMM
     std::vector<sp_kv *> caches;
 };
 
@@ -730,7 +731,7 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // int8 row-major copies: exponent k per matrix so that its largest weight times 2^k is near 2^15
     // (fp16 range, and the lo halves of the large weights stay normal); one alpha = 2^-k per matrix
     auto dequant = [&](size_t hi_off, size_t lo_off, const void *q1, const void *s1, int rows1, const void *q2,
-                       const void *s2, int rows2, int K, PrefillMat &m) -> cudaError_t {
+                       const void *s2, int rows2, int K, PrefillMat &m, int pair_hd = 0) -> cudaError_t {
         // with a second matrix (gate_up: gate, then up) the rows are interleaved: 2i = q1 row i, 2i + 1 = q2 row i
         float mx = 0.f, mx2 = 0.f;
         cudaError_t er = launch_int8_absmax(d_absmax, (const __half *)s1, (long long)rows1 * (K / 32), s);
@@ -743,9 +744,9 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         int k = 0;
         if (mx > 0.f && std::isfinite(mx)) k = std::min(30, std::max(-30, (int)std::floor(std::log2(32768.0 / mx))));
         __half *hi = (__half *)(A + hi_off), *lw = (__half *)(A + lo_off);
-        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, q2 ? 2 : 1, 0, s);
+        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, q2 ? 2 : 1, 0, pair_hd, s);
         if (er == cudaSuccess && q2)
-            er = launch_dequant_hilo(hi, lw, (const int8_t *)q2, (const __half *)s2, rows2, K, k, 2, 1, s);
+            er = launch_dequant_hilo(hi, lw, (const int8_t *)q2, (const __half *)s2, rows2, K, k, 2, 1, 0, s);
         m.hi = hi;
         m.lo = lw;
         m.alpha = ldexpf(1.0f, -k);
@@ -775,13 +776,15 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         LayerDev L;
         if (e->prefill && i8) {
             const int A_ = c.heads * (int)HD;
-            SP_TRY(dequant(lo[l].rqkv, lo[l].rqkv_lo, Lw.qkv_w, Lw.qkv_s, (int)QR, nullptr, nullptr, 0, (int)H, L.pf.qkv));
+            SP_TRY(dequant(lo[l].rqkv, lo[l].rqkv_lo, Lw.qkv_w, Lw.qkv_s, (int)QR, nullptr, nullptr, 0, (int)H, L.pf.qkv,
+                           (int)HD));
             SP_TRY(dequant(lo[l].ro, lo[l].ro_lo, Lw.o_w, Lw.o_s, (int)H, nullptr, nullptr, 0, A_, L.pf.o));
             SP_TRY(dequant(lo[l].rgu, lo[l].rgu_lo, Lw.gate_w, Lw.gate_s, (int)I, Lw.up_w, Lw.up_s, (int)I, (int)H,
                            L.pf.gate_up));
             SP_TRY(dequant(lo[l].rdn, lo[l].rdn_lo, Lw.down_w, Lw.down_s, (int)H, nullptr, nullptr, 0, (int)I, L.pf.down));
         } else if (e->prefill) {
-            SP_TRY(cudaMemcpyAsync(A + lo[l].rqkv, Lw.qkv_w, QR * H * 2, cudaMemcpyDeviceToDevice, s));
+            // QKV rows with RoPE partners adjacent (the GEMM's QKV epilogue pairs them)
+            SP_TRY(launch_gather_rows(A + lo[l].rqkv, (const uint8_t *)Lw.qkv_w, d_perm, (int)QR, (int)H * 2, 1, 0, s));
             SP_TRY(cudaMemcpyAsync(A + lo[l].ro, Lw.o_w, H * (size_t)c.heads * HD * 2, cudaMemcpyDeviceToDevice, s));
             // gate and up rows interleaved (2i = gate i, 2i + 1 = up i): the GEMM's SwiGLU epilogue pairs them
             SP_TRY(launch_gather_rows(A + lo[l].rgu, (const uint8_t *)Lw.gate_w, d_seq, (int)I, (int)H * 2, 2, 0, s));
@@ -963,7 +966,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         e->pf_bytes = prefill_scratch_bytes(e->pf_dims);
         SP_TRY(cudaMalloc(&e->pf_mem, e->pf_bytes));
         e->pf = prefill_scratch_at(e->pf_mem, e->pf_dims);
-        SP_TRY(cudaMemset(e->pf.cnt, 0, (size_t)e->pf.cnt_count * sizeof(unsigned)));   // the GEMM keeps them zero
+        if (getenv("SEEDPLANE_MCOL_TRACE") && atoi(getenv("SEEDPLANE_MCOL_TRACE")) != 0) {
+            SP_TRY(cudaMalloc(&e->mc_trace, (size_t)kPrefillMaxCtas * kMcolTraceWords * 8));
+            SP_TRY(cudaMemset(e->mc_trace, 0, (size_t)kPrefillMaxCtas * kMcolTraceWords * 8));
+        }
         SP_TRY(cudaMalloc(&e->vt, sizeof(VerifyIn) + kSmallNodes * sizeof(int32_t)));
         e->vt_argmax = reinterpret_cast<int32_t *>(e->vt + 1);
     }
@@ -1067,6 +1073,7 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->trace);
     for (auto &g : e->vgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->pf_mem);
+    cudaFree(e->mc_trace);
     cudaFree(e->vt);
     cudaFree(e->acc_scratch);
     delete e;
@@ -1385,12 +1392,9 @@ int sp_mcol_gemm(sp_engine *e, int32_t mode, const void *w_dev, const void *w_lo
     op.act_h = (__half *)act_hi_dev;
     op.act_l = (__half *)act_lo_dev;
     op.ld_act = ld_act;
-    op.ws = e->pf.ws;
-    op.ws_bytes = e->pf.ws_bytes;
-    op.cnt = e->pf.cnt;
-    op.cnt_count = e->pf.cnt_count;
     op.max_ctas = kPrefillMaxCtas;
     op.st = e->st;
+    op.trace = e->mc_trace;
     SP_CUDA(launch_mcol(op, (cudaStream_t)stream, false));
     return SP_OK;
 }
@@ -1499,14 +1503,16 @@ int sp_argmax_noalloc(int device, const float *logits_dev, int32_t rows, int32_t
 
 int64_t sp_trace_read(sp_engine *e, uint64_t *host_out, int64_t capacity) {
     if (!e) return fail(SP_ERR_INVALID, "null engine");
-    if (!e->trace && !e->step_trace) return 0;
+    if (!e->trace && !e->step_trace && !e->mc_trace) return 0;
     const int64_t n = e->step_trace ? (int64_t)(5 * e->c.layers + 1) * e->num_sms * kStepTraceWords
-                                    : (int64_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords;
+                      : e->trace ? (int64_t)(e->trace_kernels + 2) * e->num_sms * kTraceWords
+                                 : (int64_t)kPrefillMaxCtas * kMcolTraceWords;
     if (!host_out) return n;
     if (capacity < n) return fail(SP_ERR_CAPACITY, "trace needs %lld words", (long long)n);
     cudaError_t ce = cudaSetDevice(e->device);
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
-    if (ce == cudaSuccess) ce = cudaMemcpy(host_out, e->step_trace ? e->step_trace : e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost);
+    const void *src = e->step_trace ? (const void *)e->step_trace : e->trace ? (const void *)e->trace : (const void *)e->mc_trace;
+    if (ce == cudaSuccess) ce = cudaMemcpy(host_out, src, (size_t)n * 8, cudaMemcpyDeviceToHost);
     if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "trace copy: %s", cudaGetErrorString(ce));
     return n;
 }

@@ -293,16 +293,18 @@ struct PrefillMat {                      // row-major fp16 weights W = alpha * (
     float alpha;                         // fp16 halves (exact: q * scale has at most 19 significant bits)
 };
 struct PrefillLayer {
-    PrefillMat qkv;                      // [(heads + 2 kv_heads) * head_dim, hidden], natural row order
+    PrefillMat qkv;                      // [(heads + 2 kv_heads) * head_dim, hidden], RoPE partners adjacent
     PrefillMat o;                        // [hidden, heads * head_dim]
     PrefillMat gate_up;                  // [2 inter, hidden]: rows interleaved, 2i = gate i, 2i + 1 = up i
     PrefillMat down;                     // [hidden, inter]
     const float *qkv_b, *in_norm, *post_norm;
 };
 // Dequantize blockwise int8 rows (q [rows][K], fp16 scales [rows][K / 32]) into fp16 hi / lo halves
-// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi); source row r goes to row r * dst_mul + dst_add.
+// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi); source row r goes to row r * dst_mul + dst_add,
+// or, with pair_hd > 0 (the QKV projection), to its RoPE-pair position: row h * pair_hd + d goes to
+// h * pair_hd + 2 d (d < pair_hd / 2) or h * pair_hd + 2 (d - pair_hd / 2) + 1.
 cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                int dst_mul, int dst_add, cudaStream_t s);
+                                int dst_mul, int dst_add, int pair_hd, cudaStream_t s);
 // Largest |scale| * 127 of a blockwise-int8 matrix (n fp16 scales), into *out (device float).
 cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cudaStream_t s);
 struct PrefillScratch {
@@ -313,10 +315,6 @@ struct PrefillScratch {
     float *y;                            // [T, qkv rows] QKV projection
     float *q;                            // [T, heads * head_dim]
     float *logits;                       // [kPrefillLogitRows, vocab]
-    float *ws;                           // multi-column GEMM split-K partials
-    size_t ws_bytes;
-    unsigned *cnt;                       // its per-tile counters (zero between launches)
-    long long cnt_count;
 };
 size_t prefill_scratch_bytes(const PrefillDims &d);
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d);
@@ -339,7 +337,19 @@ cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s,
 // Y[t][n] = alpha * W[n, :] . (x_hi[t] + x_lo[t]) on tcgen05 (weights = the M 128 operand, tokens'
 // hi / lo rows = the N operand), fused epilogue by mode. x: fp16 rows [x_rows, K], token t's hi row
 // at t, its lo row at lo_row0 + t. W: row-major fp16 [N, K], or two halves (w + w_lo).
-enum { MC_STORE = 0, MC_RESID = 1, MC_SWIGLU = 2 };
+enum { MC_STORE = 0, MC_RESID = 1, MC_SWIGLU = 2, MC_QKV = 3 };
+// MC_QKV epilogue: the rows are the QKV projection's with RoPE partners adjacent (row 2p, 2p + 1 =
+// dims d, d + head_dim / 2 of one head, p = head * head_dim / 2 + d); adds the bias (natural order),
+// rotates q and k by the token's position (rope table [pos][head_dim / 2][cos, sin]), writes q fp32
+// [t][heads * head_dim] and k, v fp16 into the cache at slot *slot_base + slot_off + t.
+struct McolQkv {
+    const float *bias, *rope;
+    const int32_t *pos;          // per-token positions or null (= slot)
+    const int *slot_base;
+    int slot_off, cap, nh, nkv, hd, max_pos;
+    float *q;
+    __half *kc, *vc;
+};
 struct McolOp {
     int mode;                    // MC_STORE: y[t ldy + n] = ..; MC_RESID: += ..; MC_SWIGLU: see act_*
     const __half *w, *w_lo;      // w_lo: second weight half or null
@@ -351,28 +361,25 @@ struct McolOp {
     int ldy;
     __half *act_h, *act_l;       // MC_SWIGLU: rows 2i = gate i, 2i + 1 = up i; act[t ld_act + i] = hi / lo
     int ld_act;
-    float *ws;                   // split-K partials (mcol_workspace_bytes) and per-tile counters (zeroed
-    size_t ws_bytes;             // once; the kernel leaves them zero)
-    unsigned *cnt;
-    long long cnt_count;
     int max_ctas;
     DevState *st;
+    McolQkv qkv;                 // MC_QKV only
+    unsigned long long *trace;   // optional: %globaltimer stamps of the launch's phases per CTA
 };
 struct McolParams {
-    int N, K, T, tn, lo_row0, two_w, split, stages, tmem_cols;
+    int N, K, T, tn, lo_row0, two_w, cs, stages, tmem_cols;   // cs: CTAs of a cluster splitting a tile
     float alpha;
     float *y;
     int ldy;
     __half *act_h, *act_l;
     int ld_act;
-    float *ws;
-    unsigned *cnt;
     DevState *st;
+    McolQkv qkv;
+    unsigned long long *trace;   // per-CTA phase stamps (kMcolTraceWords each) or null
 };
+constexpr int kMcolTraceWords = 16;
 size_t mcol_max_smem();
 int mcol_tile_tokens(int T);
-size_t mcol_workspace_bytes(int max_ctas, int max_tokens);
-size_t mcol_counter_count(int max_rows, int max_tokens);
 // pdl: programmatic dependent launch after the previous kernel in the stream
 cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl);
 

@@ -14,22 +14,26 @@
 //   warp 5   allocates TMEM and issues tcgen05.mma (M 128, N 2 TN, K 16; four per k-block) into one
 //            of two accumulators, commits each stage back to the producer and each finished
 //            accumulator to the epilogue
-//   warps 0-3  epilogue: thread = output row (TMEM lane), tcgen05.ld of its hi / lo columns, the
-//            fused epilogue of the op: store, residual add, or SwiGLU of interleaved gate / up rows
-//            written as the down projection's fp16 hi / lo input
+//   warps 0-3  epilogue: tcgen05.ld of the hi / lo columns and the fused epilogue of the op: store,
+//            residual add, SwiGLU of interleaved gate / up rows written as the down projection's
+//            fp16 hi / lo input, or QKV bias + RoPE + K/V cache write
 //
-// Work: tiles of 128 rows x TN tokens, each over K in k-blocks of 64 inputs. With at least as many
-// tiles as CTAs, every CTA takes whole tiles. Otherwise (the small projections of a verify pass)
-// the k-blocks of all tiles are dealt out as one contiguous range per CTA (stream-K): a CTA whose
-// range covers part of a tile writes its partial sums to a workspace slot and counts itself in on
-// the tile's counter; the last contributor adds all partials in contributor order (so the result
-// does not depend on which CTA finishes last) and runs the epilogue. Every wait is bounded; an
-// expired wait records kErrMbarTimeout in DevState::err and the CTA leaves without waiting again.
+// Work: tiles of 128 rows x TN tokens, each over K in k-blocks of 64 inputs. With enough tiles to
+// keep half the SMs busy, every CTA takes whole tiles in turn (thread = output row, accumulators
+// double-buffered so a tile's epilogue overlaps the next tile's MMAs). Otherwise (the small
+// projections of a verify pass) each tile goes to a thread-block cluster of cs CTAs that split its
+// k-blocks: every CTA leaves its partial sums in its own shared memory, the cluster meets at a
+// barrier, and CTA r adds the cs partials of rows [r 128 / cs, (r + 1) 128 / cs) in rank order
+// through distributed shared memory and runs the epilogue on them. No global workspace, no atomics,
+// the same result whichever CTA finishes first. Every mbarrier wait is bounded; an expired wait
+// records kErrMbarTimeout in DevState::err and the CTA stops waiting (the cluster barriers still
+// complete: every thread reaches them).
 #include <cuda.h>
 
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -47,8 +51,17 @@ constexpr int kMcMma = 5;
 constexpr int kBK = 64;                  // inputs per k-block: one 128-byte swizzle row of fp16
 constexpr int kBM = 128;
 constexpr int kATileBytes = kBM * kBK * 2;
-constexpr int kMcMaxStages = 8;
+constexpr int kMcMaxStages = 12;
+constexpr int kMcMaxCluster = 8;         // portable cluster size
 constexpr uint32_t kMcSpin = 1u << 22;
+
+// Phase stamp i of this CTA (%globaltimer, ns) when the launch carries a trace buffer:
+// 0 entry, 1 set-up done, 2 first TMA issued, 3 dependency wait done, 4 first stage landed (MMA
+// warp), 5 first accumulator committed, 6 first accumulator seen by the epilogue, 7 partial in
+// shared memory (cluster split), 8 cluster partials reduced, 9 epilogue done, 10 exit.
+SP_DEVINL void mstamp(unsigned long long *tr, int i) {
+    if (tr) tr[(size_t)blockIdx.x * kMcolTraceWords + i] = globaltimer();
+}
 
 SP_DEVINL void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kMcEpiThreads) : "memory"); }
 
@@ -67,6 +80,28 @@ SP_DEVINL void tma_load_2d_hint(uint32_t dst, const CUtensorMap *map, int x, int
 }
 SP_DEVINL void prefetch_map(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Thread-block cluster: every thread of every CTA arrives (release) and waits (acquire). Not the
+// .aligned form: the producer and MMA warps reach it from divergent code.
+SP_DEVINL void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+SP_DEVINL uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The address of this CTA's shared-memory word `addr` in the CTA of rank `rank` of the cluster.
+SP_DEVINL uint32_t dsmem_addr(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+SP_DEVINL float ld_dsmem(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
 }
 
 // kind::f16 instruction descriptor: D fp32, A / B fp16, both K-major, M = 128, N = n.
@@ -90,13 +125,74 @@ SP_DEVINL bool wait_phase(uint64_t *bar, uint32_t parity, const Flag &f) {
     return false;
 }
 
-// The unit (k-block) range [u0, u1) of CTA c out of C over W units.
-SP_DEVINL long long unit_start(long long W, int C, int c) { return W * c / C; }
-SP_DEVINL int cta_of_unit(long long W, int C, long long u) {
-    int c = (int)((u * C) / W);
-    while (c > 0 && unit_start(W, C, c) > u) --c;
-    while (c + 1 < C && unit_start(W, C, c + 1) <= u) ++c;
-    return c;
+// The cache slot of token 0 of the block (device-side base + offset), checked against the cache.
+SP_DEVINL int qkv_slot0(const McolParams &p) {
+    const McolQkv &a = p.qkv;
+    int s0 = *a.slot_base + a.slot_off;
+    if (s0 < 0 || s0 + p.T > a.cap) {
+        if (p.st && threadIdx.x == 0) atomicCAS(&p.st->err, 0, kErrBadSlot);
+        s0 = min(max(s0, 0), max(a.cap - p.T, 0));
+    }
+    return s0;
+}
+
+// The fused epilogue of one output y = alpha * sum (row n, token t). Rows 2i and 2i + 1 are in
+// lanes 2m and 2m + 1 of one warp for the same token (every lane calls this, valid or not: the pair
+// is exchanged by shuffle).
+//   MC_STORE / MC_RESID: y[t ldy + n] = / += value
+//   MC_SWIGLU: rows 2i (gate i), 2i + 1 (up i): act[t ld_act + i] = SiLU(gate) * up as fp16 hi / lo
+//   MC_QKV: rows 2p, 2p + 1 = dims d, d + hd / 2 of one head (p = head * hd / 2 + d): bias, RoPE on
+//     q and k with the token's position, q fp32 [t][heads * hd], k / v fp16 into the cache
+//     (as the decode step's QKV epilogue computes them)
+template <int MODE>
+SP_DEVINL void epilogue_one(const McolParams &p, float v, int n, int t, int lane, int slot0) {
+    const float y = p.alpha * v;
+    const bool ok = n < p.N && t < p.T;
+    if (MODE == MC_STORE || MODE == MC_RESID) {
+        if (ok) {
+            float *dst = p.y + (size_t)t * p.ldy + n;
+            *dst = MODE == MC_RESID ? *dst + y : y;
+        }
+    } else if (MODE == MC_SWIGLU) {
+        const float up = __shfl_xor_sync(0xffffffffu, y, 1);
+        if ((lane & 1) == 0 && ok && n + 1 < p.N) {
+            const float a = (y / (1.0f + expf(-y))) * up;
+            const __half ah = __float2half_rn(a);
+            p.act_h[(size_t)t * p.ld_act + (n >> 1)] = ah;
+            p.act_l[(size_t)t * p.ld_act + (n >> 1)] = __float2half_rn(a - __half2float(ah));
+        }
+    } else {
+        const McolQkv &a = p.qkv;
+        const float other = __shfl_xor_sync(0xffffffffu, y, 1);
+        if ((lane & 1) != 0 || !ok || n + 1 >= p.N) return;
+        const int half_hd = a.hd / 2;
+        const int P2 = n >> 1, hh = P2 / half_hd, dd = P2 - hh * half_hd;
+        const float a0 = y + __ldg(a.bias + hh * a.hd + dd), a1 = other + __ldg(a.bias + hh * a.hd + dd + half_hd);
+        const int slot = slot0 + t;
+        if (hh < a.nh + a.nkv) {
+            int pos = a.pos ? a.pos[t] : slot;
+            if (pos < 0 || pos >= a.max_pos) {
+                if (p.st) atomicCAS(&p.st->err, 0, kErrBadSlot);
+                pos = min(max(pos, 0), a.max_pos - 1);
+            }
+            const float2 r2 = __ldg(reinterpret_cast<const float2 *>(a.rope + ((size_t)pos * half_hd + dd) * 2));
+            const float o0 = __fadd_rn(__fmul_rn(a0, r2.x), -__fmul_rn(a1, r2.y));
+            const float o1 = __fadd_rn(__fmul_rn(a1, r2.x), __fmul_rn(a0, r2.y));
+            if (hh < a.nh) {
+                float *qr = a.q + (size_t)t * a.nh * a.hd + hh * a.hd;
+                qr[dd] = o0;
+                qr[dd + half_hd] = o1;
+            } else {
+                __half *kr = a.kc + ((size_t)(hh - a.nh) * a.cap + slot) * a.hd;
+                kr[dd] = __float2half_rn(o0);
+                kr[dd + half_hd] = __float2half_rn(o1);
+            }
+        } else {
+            __half *vr = a.vc + ((size_t)(hh - a.nh - a.nkv) * a.cap + slot) * a.hd;
+            vr[dd] = __float2half_rn(a0);
+            vr[dd + half_hd] = __float2half_rn(a1);
+        }
+    }
 }
 
 }  // namespace
@@ -108,26 +204,29 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     extern __shared__ uint8_t mc_smem_raw[];
     __shared__ __align__(8) uint64_t full[kMcMaxStages], empty[kMcMaxStages], accf[2], acce[2], drain;
     __shared__ uint32_t s_tmem;
-    __shared__ int s_abort, s_last;
+    __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int C = gridDim.x, c = blockIdx.x;
-    const int TN = p.tn, S = p.stages;
+    const int TN = p.tn, S = p.stages, cs = p.cs;
     const int kbx = (p.K + kBK - 1) / kBK;              // k-blocks of the input
     const int kbe = p.two_w ? 2 * kbx : kbx;            // k-blocks of a tile
     const int mtiles = (p.N + kBM - 1) / kBM, ntiles = (p.T + TN - 1) / TN;
     const long long tiles = (long long)mtiles * ntiles;
-    const long long W = tiles * kbe;
+    // this CTA's k-blocks [u0, u1) of the flattened (tile, k-block) order
     long long u0, u1;
-    if (p.split) {
-        u0 = unit_start(W, C, c);
-        u1 = unit_start(W, C, c + 1);
+    int rank = 0;
+    if (cs > 1) {
+        rank = (int)cluster_rank();
+        const long long tile = blockIdx.x / cs;
+        u0 = tile * kbe + (long long)kbe * rank / cs;
+        u1 = tile * kbe + (long long)kbe * (rank + 1) / cs;
     } else {
-        u0 = tiles * c / C * kbe;
-        u1 = tiles * (c + 1) / C * kbe;
+        u0 = tiles * blockIdx.x / gridDim.x * kbe;
+        u1 = tiles * (blockIdx.x + 1) / gridDim.x * kbe;
     }
     const uint32_t base = (smem_u32(mc_smem_raw) + 1023u) & ~1023u;
     const uint32_t stage_bytes = (uint32_t)(kATileBytes + 2 * TN * kBK * 2);
     const Flag fl{&s_abort, p.st};
+    if (tid == 0) mstamp(p.trace, 0);
 
     if (tid == 0) {
         s_abort = 0;
@@ -157,6 +256,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     griddep_launch_dependents();
+    if (tid == 0) mstamp(p.trace, 1);
 
     if (warp == kMcProducer) {
         if (lane == 0) {
@@ -176,7 +276,9 @@ __global__ void __launch_bounds__(kMcThreads, 1)
                 const int kx = (second ? kb - kbx : kb) * kBK;
                 tma_load_2d_hint(st, second ? &tm_w2 : &tm_w, kx, mt * kBM, &full[s], pol);
                 if (!waited) {
+                    mstamp(p.trace, 2);
                     griddep_wait();
+                    mstamp(p.trace, 3);
                     waited = true;
                 }
                 tma_load_2d(st + kATileBytes, &tm_x, kx, nt * TN, &full[s]);
@@ -212,6 +314,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
                 bool first = true;
                 for (; u < v1; ++u) {
                     if (!wait_phase(&full[s], ph, fl)) break;
+                    if (u == u0) mstamp(p.trace, 4);
                     tc_fence_after();
                     const uint32_t st = base + (uint32_t)s * stage_bytes;
                     const uint64_t ad = smem_desc_sw128(st, 1024);
@@ -228,6 +331,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
                 }
                 if (u < v1) break;                          // aborted
                 mma_commit(&accf[buf]);
+                if (nseg == 0) mstamp(p.trace, 5);
                 ++nseg;
                 buf ^= 1;
             }
@@ -235,121 +339,98 @@ __global__ void __launch_bounds__(kMcThreads, 1)
             mma_commit(&drain);
             mbar_wait_bounded(&drain, 0u);
         }
-    } else {
-        // ---- epilogue: warps 0-3, thread = row of the tile ----------------------------------------
+    } else if (cs == 1) {
+        // ---- whole tiles: thread = output row, 16 tokens per TMEM read ------------------------------
         const int row = warp * 32 + lane;
         int buf = 0;
         uint32_t fph[2] = {0u, 0u};
-        long long u = u0;
-        while (u < u1 && !fl.on()) {
-            const int tile = (int)(u / kbe), kb0 = (int)(u % kbe);
-            const long long tile_end = (long long)(tile + 1) * kbe;
-            const long long v1 = u1 < tile_end ? u1 : tile_end;
-            const bool whole = kb0 == 0 && v1 == tile_end;
-            u = v1;
+        const int slot0 = MODE == MC_QKV ? qkv_slot0(p) : 0;
+        for (long long u = u0; u < u1 && !fl.on(); u += kbe) {
+            const int tile = (int)(u / kbe);
             const int mt = tile / ntiles, nt = tile % ntiles;
             const int n = mt * kBM + row;
             if (!wait_phase(&accf[buf], fph[buf], fl)) break;
+            if (u == u0 && tid == 0) mstamp(p.trace, 6);
             fph[buf] ^= 1u;
             tc_fence_after();
             const uint32_t tacc = tmem + (uint32_t)(buf * 2 * TN) + ((uint32_t)(warp * 32) << 16);
-            // this segment's position among the tile's contributors (split tiles only)
-            // (the host makes every CTA's range non-empty, so the contributors are consecutive CTAs)
-            int first_c = 0, nctr = 1;
-            if (!whole) {
-                first_c = cta_of_unit(W, C, (long long)tile * kbe);
-                nctr = cta_of_unit(W, C, tile_end - 1) - first_c + 1;
-            }
-            float *wsl = nullptr;
-            if (!whole) {
-                const int slot = 2 * c + ((long long)tile == unit_start(W, C, c) / kbe ? 0 : 1);
-                wsl = p.ws + (size_t)slot * kBM * TN;
-            }
-            // the tile's columns in chunks of 16 tokens: v[j] = hi + lo of token c0 + j
-            bool last = true;
-            if (!whole) {
-                for (int c0 = 0; c0 < TN; c0 += 16) {
-                    uint32_t h[16], l[16];
-                    tmem_ld16_nowait(tacc + (uint32_t)c0, h);
-                    tmem_ld16_nowait(tacc + (uint32_t)(TN + c0), l);
-                    tmem_wait_ld();
+            for (int c0 = 0; c0 < TN; c0 += 16) {
+                uint32_t h[16], l[16];
+                tmem_ld16_nowait(tacc + (uint32_t)c0, h);
+                tmem_ld16_nowait(tacc + (uint32_t)(TN + c0), l);
+                tmem_wait_ld();
+                const int t0 = nt * TN + c0;
+                if (MODE == MC_RESID) {
+                    if (n < p.N) {
+                        // all loads before the stores (a store could alias a later load for the compiler)
+                        float *dst = p.y + (size_t)t0 * p.ldy + n;
+                        float old[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) old[j] = t0 + j < p.T ? __ldcg(dst + (size_t)j * p.ldy) : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (t0 + j < p.T)
+                                dst[(size_t)j * p.ldy] = old[j] + p.alpha * (__uint_as_float(h[j]) + __uint_as_float(l[j]));
+                    }
+                } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        __stcg(wsl + (size_t)(c0 + j) * kBM + row, __uint_as_float(h[j]) + __uint_as_float(l[j]));
-                }
-                tc_fence_before();
-                __threadfence();
-                epi_bar();
-                if (tid == 0) {
-                    __threadfence();
-                    const unsigned prev = atomicAdd(p.cnt + tile, 1u);
-                    s_last = prev == (unsigned)(nctr - 1);
-                    if (s_last) p.cnt[tile] = 0u;                       // ready for the next launch
-                    __threadfence();
-                }
-                epi_bar();
-                last = s_last != 0;
-                if (tid == 0) mbar_arrive(&acce[buf]);                  // the accumulator is read out
-                if (last) __threadfence();
-            }
-            if (last) {
-                for (int c0 = 0; c0 < TN; c0 += 16) {
-                    float v[16];
-                    if (whole) {
-                        uint32_t h[16], l[16];
-                        tmem_ld16_nowait(tacc + (uint32_t)c0, h);
-                        tmem_ld16_nowait(tacc + (uint32_t)(TN + c0), l);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(h[j]) + __uint_as_float(l[j]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                        for (int q = 0; q < nctr; ++q) {             // contributors in CTA order
-                            const int cq = first_c + q;
-                            const int slot = 2 * cq + ((long long)tile == unit_start(W, C, cq) / kbe ? 0 : 1);
-                            const float *src = p.ws + (size_t)slot * kBM * TN + (size_t)c0 * kBM + row;
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)j * kBM);
-                        }
-                    }
-                    const int t0 = nt * TN + c0;
-                    if (MODE == MC_SWIGLU) {
-                        // rows 2i (gate i) and 2i + 1 (up i) sit in lanes 2m, 2m + 1 of one warp
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float y = p.alpha * v[j];
-                            const float up = __shfl_xor_sync(0xffffffffu, y, 1);
-                            const int t = t0 + j;
-                            if ((lane & 1) == 0 && t < p.T && n + 1 < p.N) {
-                                const float a = (y / (1.0f + expf(-y))) * up;
-                                const __half ah = __float2half_rn(a);
-                                p.act_h[(size_t)t * p.ld_act + (n >> 1)] = ah;
-                                p.act_l[(size_t)t * p.ld_act + (n >> 1)] = __float2half_rn(a - __half2float(ah));
-                            }
-                        }
-                    } else if (n < p.N) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int t = t0 + j;
-                            if (t < p.T) {
-                                float *dst = p.y + (size_t)t * p.ldy + n;
-                                if (MODE == MC_RESID)
-                                    *dst += p.alpha * v[j];
-                                else
-                                    *dst = p.alpha * v[j];
-                            }
-                        }
-                    }
+                        epilogue_one<MODE>(p, __uint_as_float(h[j]) + __uint_as_float(l[j]), n, t0 + j, lane, slot0);
                 }
             }
-            if (whole) {
-                tc_fence_before();
-                epi_bar();
-                if (tid == 0) mbar_arrive(&acce[buf]);
-            }
+            tc_fence_before();
+            epi_bar();
+            if (tid == 0) mbar_arrive(&acce[buf]);
             buf ^= 1;
         }
+        if (tid == 0) mstamp(p.trace, 9);
+    } else {
+        // ---- cluster split: this CTA's partial of its tile into its own shared memory ---------------
+        // P [row][TN] fp32 at the ring's start (every stage has been consumed once the accumulator is
+        // committed: this CTA has exactly one segment)
+        const int row = warp * 32 + lane;
+        if (u0 < u1 && wait_phase(&accf[0], 0u, fl)) {
+            if (tid == 0) mstamp(p.trace, 6);
+            tc_fence_after();
+            const uint32_t tacc = tmem + ((uint32_t)(warp * 32) << 16);
+            float4 *mine = reinterpret_cast<float4 *>(mc_smem_raw + (base - smem_u32(mc_smem_raw))) + (size_t)row * (TN / 4);
+            for (int c0 = 0; c0 < TN; c0 += 16) {
+                uint32_t h[16], l[16];
+                tmem_ld16_nowait(tacc + (uint32_t)c0, h);
+                tmem_ld16_nowait(tacc + (uint32_t)(TN + c0), l);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    mine[c0 / 4 + j] = make_float4(__uint_as_float(h[4 * j]) + __uint_as_float(l[4 * j]),
+                                                   __uint_as_float(h[4 * j + 1]) + __uint_as_float(l[4 * j + 1]),
+                                                   __uint_as_float(h[4 * j + 2]) + __uint_as_float(l[4 * j + 2]),
+                                                   __uint_as_float(h[4 * j + 3]) + __uint_as_float(l[4 * j + 3]));
+            }
+            tc_fence_before();
+        }
+        if (tid == 0) mstamp(p.trace, 7);
+    }
+
+    if (cs > 1) {
+        // ---- cluster split: reduce rows [rank rp, (rank + 1) rp) of the tile over the cs partials ----
+        cluster_sync();                                     // every partial of the cluster is written
+        if (warp < kMcEpiThreads / 32) {
+            const int rp = kBM / cs;
+            const long long tile = blockIdx.x / cs;
+            const int mt = (int)(tile / ntiles), nt = (int)(tile % ntiles);
+            const int slot0 = MODE == MC_QKV ? qkv_slot0(p) : 0;
+            // element e = tid + 128 i: row rank rp + e % rp, token e / rp (adjacent lanes, adjacent rows)
+            for (int e = tid; e < rp * TN; e += kMcEpiThreads) {
+                const int rl = e % rp, t = e / rp;
+                const uint32_t off = base + (uint32_t)(((rank * rp + rl) * TN + t) * 4);
+                float v = 0.f;
+                for (int q = 0; q < cs; ++q) v += ld_dsmem(dsmem_addr(off, (uint32_t)q));
+                const int n = mt * kBM + rank * rp + rl;
+                epilogue_one<MODE>(p, v, n, nt * TN + t, lane, slot0);
+            }
+            if (tid == 0) mstamp(p.trace, 8);
+        }
+        cluster_sync();                                     // no CTA leaves while its partial is read
     }
     tc_fence_before();
     __syncthreads();
@@ -357,6 +438,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)p.tmem_cols));
     }
+    if (tid == 0) mstamp(p.trace, 10);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -397,6 +479,11 @@ cudaError_t map_rows(CUtensorMap *m, const __half *ptr, int rows, int K, int box
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+int env_int(const char *name, int fallback) {
+    const char *v = getenv(name);
+    return v && *v ? atoi(v) : fallback;
+}
+
 int sm_count() {
     static int n = 0;
     if (n == 0) {
@@ -426,11 +513,22 @@ cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUten
     cfg.blockDim = dim3(kMcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (p.cs > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)p.cs;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, k_mcol<MODE>, a, a2, x, p);
 }
 
@@ -440,19 +538,16 @@ size_t mcol_max_smem() { return 227 * 1024 - 1024; }   // 1 KB for the static ba
 
 int mcol_tile_tokens(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128; }
 
-size_t mcol_workspace_bytes(int max_ctas, int max_tokens) {
-    return (size_t)2 * max_ctas * kBM * mcol_tile_tokens(max_tokens) * sizeof(float);
-}
-
-size_t mcol_counter_count(int max_rows, int max_tokens) {
-    const int tn = mcol_tile_tokens(max_tokens);
-    return (size_t)((max_rows + kBM - 1) / kBM) * ((max_tokens + tn - 1) / tn);
-}
-
 cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     if (op.T <= 0 || op.N <= 0 || op.K <= 0 || op.T > op.x_rows || op.lo_row0 < op.T) return cudaErrorInvalidValue;
     if (op.mode == MC_SWIGLU && (op.N % 2 || !op.act_h || !op.act_l)) return cudaErrorInvalidValue;
-    if (op.mode != MC_SWIGLU && !op.y) return cudaErrorInvalidValue;
+    if ((op.mode == MC_STORE || op.mode == MC_RESID) && !op.y) return cudaErrorInvalidValue;
+    if (op.mode == MC_QKV) {
+        const McolQkv &a = op.qkv;
+        if (!a.bias || !a.rope || !a.slot_base || !a.q || !a.kc || !a.vc || a.hd <= 0 || a.hd % 2 || a.nh <= 0 ||
+            a.nkv <= 0 || op.N != (a.nh + 2 * a.nkv) * a.hd || a.max_pos <= 0 || a.cap < op.T)
+            return cudaErrorInvalidValue;
+    }
     McolParams p{};
     p.N = op.N;
     p.K = op.K;
@@ -466,27 +561,29 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     p.act_h = op.act_h;
     p.act_l = op.act_l;
     p.ld_act = op.ld_act;
-    p.ws = op.ws;
-    p.cnt = op.cnt;
     p.st = op.st;
+    p.qkv = op.qkv;
+    p.trace = op.trace;
     p.tmem_cols = 4 * p.tn < 32 ? 32 : 4 * p.tn;
     const int stage_bytes = kATileBytes + 2 * p.tn * kBK * 2;
-    p.stages = std::min(kMcMaxStages, (int)((mcol_max_smem() - 1024) / stage_bytes));   // 1 KB: alignment
+    static const int stage_cap = env_int("SEEDPLANE_MCOL_STAGES", kMcMaxStages);
+    const int fit = (int)((mcol_max_smem() - 1024) / stage_bytes);          // 1 KB: alignment
+    p.stages = std::max(2, std::min(std::min(stage_cap, kMcMaxStages), fit));
     const long long mtiles = (op.N + kBM - 1) / kBM, ntiles = (op.T + p.tn - 1) / p.tn;
     const long long tiles = mtiles * ntiles;
+    const long long kbe = (long long)((op.K + kBK - 1) / kBK) * (op.w_lo ? 2 : 1);
+    // Whole tiles when they keep at least half the SMs busy; else the largest cluster (<= 8 CTAs, <= the
+    // tile's k-blocks) whose tiles x cluster CTAs fit the SMs in one wave splits each tile's k-blocks.
     const int C = std::min(sm_count(), op.max_ctas);
-    int grid;
-    if (tiles >= C) {
-        p.split = 0;
-        grid = C;
-    } else {
-        // every CTA gets at least one k-block, so a split tile's contributors are consecutive CTAs
-        p.split = 1;
-        const long long kbe = (long long)((op.K + kBK - 1) / kBK) * (op.w_lo ? 2 : 1);
-        grid = (int)std::min<long long>(C, tiles * kbe);
-        if (!op.ws || !op.cnt || tiles > op.cnt_count) return cudaErrorInvalidValue;
-    }
-    if (p.split && (size_t)2 * grid * kBM * p.tn * sizeof(float) > op.ws_bytes) return cudaErrorInvalidValue;
+    static const int cs_cap = std::max(1, std::min(kMcMaxCluster, env_int("SEEDPLANE_MCOL_CLUSTER", kMcMaxCluster)));
+    p.cs = 1;
+    if (2 * tiles <= C)
+        for (int cs = cs_cap; cs >= 2; cs /= 2)
+            if (tiles * cs <= C && cs <= kbe) {
+                p.cs = cs;
+                break;
+            }
+    const int grid = p.cs > 1 ? (int)(tiles * p.cs) : (int)std::min<long long>(C, tiles);
     CUtensorMap a, a2, x;
     cudaError_t e = map_rows(&a, op.w, op.N, op.K, kBM);
     if (e == cudaSuccess) e = map_rows(&a2, op.w_lo ? op.w_lo : op.w, op.N, op.K, kBM);
@@ -497,6 +594,7 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
         case MC_STORE: return launch_mode<MC_STORE>(a, a2, x, p, grid, smem, s, pdl);
         case MC_RESID: return launch_mode<MC_RESID>(a, a2, x, p, grid, smem, s, pdl);
         case MC_SWIGLU: return launch_mode<MC_SWIGLU>(a, a2, x, p, grid, smem, s, pdl);
+        case MC_QKV: return launch_mode<MC_QKV>(a, a2, x, p, grid, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

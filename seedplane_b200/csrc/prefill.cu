@@ -24,9 +24,30 @@ namespace {
 constexpr int kNormThreads = 256;
 constexpr int kAttnQ = 16;                  // queries per attention CTA (4 per warp)
 constexpr int kAttnKeys = 32;               // keys per staged tile (one per lane)
+constexpr int kTreeAttnMaxT = 64;           // blocks up to this many tokens use k_attn_tree
 
 __device__ __forceinline__ void set_err(DevState *st, int code) {
     if (st) atomicCAS(&st->err, 0, code);
+}
+
+// Kernels of the pass are launched with programmatic dependent launch: each may start while its
+// predecessor finishes, and waits for it (griddepcontrol.wait) before its first global access.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+SP_DEVINL void pdl_enter() {
+    griddep_wait();
+    griddep_launch_dependents();
 }
 
 // First cache slot of the block: device-side base (so a captured graph serves any cache length)
@@ -42,6 +63,7 @@ __device__ __forceinline__ int block_slot0(const int *slot_base, int slot_off, i
 
 // x[t] = embedding row of token t (ids outside the vocabulary record an error and read row 0)
 __global__ void k_embed_rows(float *x, const __half *embed, const int32_t *tok, int H, int vocab, DevState *st) {
+    pdl_enter();
     const int t = blockIdx.x;
     int id = tok[t];
     if (id < 0 || id >= vocab) {
@@ -55,6 +77,7 @@ __global__ void k_embed_rows(float *x, const __half *embed, const int32_t *tok, 
 // hi / lo halves of RMSNorm(x[t]) * gain: v = (x * inv) * g, inv = 1 / sqrt(mean(x^2) + eps)
 __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __half *xl, const float *x,
                                                                 const float *gain, int H, float eps) {
+    pdl_enter();
     const int t = blockIdx.x;
     const float *r = x + (size_t)t * H;
     __shared__ float s_part[kNormThreads / 32];
@@ -74,45 +97,6 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __hal
     }
 }
 
-// y[t] = [q heads | k heads | v heads] (natural row order, hi + lo already summed by the GEMM):
-// bias, RoPE on q and k with the position of token t, q -> fp32, k and v -> the fp16 cache at slot
-// slot0 + t.
-__global__ void k_qkv_rope_kv(float *q, __half *kc, __half *vc, const float *y, const float *bias, const float *rope,
-                              const int32_t *pos, int T, int nh, int nkv, int hd, int cap, const int *slot_base,
-                              int slot_off, int max_pos, DevState *st) {
-    const int t = blockIdx.x, half_hd = hd / 2, heads = nh + 2 * nkv;
-    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
-    int p = pos ? pos[t] : slot0 + t;
-    if (p < 0 || p >= max_pos) {
-        if (threadIdx.x == 0) set_err(st, kErrBadSlot);
-        p = min(max(p, 0), max_pos - 1);
-    }
-    const float *yr = y + (size_t)t * heads * hd;
-    const int slot = slot0 + t;
-    for (int i = threadIdx.x; i < heads * half_hd; i += blockDim.x) {
-        const int hh = i / half_hd, d = i - hh * half_hd;
-        const int lo = hh * hd + d, hi = lo + half_hd;
-        const float a0 = yr[lo] + bias[lo], a1 = yr[hi] + bias[hi];
-        if (hh < nh + nkv) {
-            const float cs = rope[((size_t)p * half_hd + d) * 2], sn = rope[((size_t)p * half_hd + d) * 2 + 1];
-            const float o0 = __fadd_rn(__fmul_rn(a0, cs), -__fmul_rn(a1, sn));
-            const float o1 = __fadd_rn(__fmul_rn(a1, cs), __fmul_rn(a0, sn));
-            if (hh < nh) {
-                q[(size_t)t * nh * hd + lo] = o0;
-                q[(size_t)t * nh * hd + hi] = o1;
-            } else {
-                __half *kr = kc + ((size_t)(hh - nh) * cap + slot) * hd;
-                kr[d] = __float2half_rn(o0);
-                kr[d + half_hd] = __float2half_rn(o1);
-            }
-        } else {
-            __half *vr = vc + ((size_t)(hh - nh - nkv) * cap + slot) * hd;
-            vr[d] = __float2half_rn(a0);
-            vr[d + half_hd] = __float2half_rn(a1);
-        }
-    }
-}
-
 // GQA attention of T queries (slots slot0 .. slot0 + T - 1) over the cache. Query t sees the slots
 // before slot0 and, among the block's own slots, [slot0, slot0 + t] (causal, mask == null) or the
 // slots slot0 + j whose bit j its ancestor mask holds (tree, T <= 64). CTA = (q head, 16 queries),
@@ -126,6 +110,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
                                                       const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
                                                       int cap, const int *slot_base, int slot_off, float scale,
                                                       DevState *st) {
+    pdl_enter();
     const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     constexpr int DL = HD / 32;                       // output dims per lane
     constexpr int KROW = HD * 2 + 8;                  // padded K row (bytes): 8-byte reads, lanes on distinct banks
@@ -242,16 +227,166 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
     }
 }
 
+// Attention of a short block (T <= kTreeAttnMaxT: a verify tree or a short prompt chunk). CTA =
+// (q head, 4 queries); its four warps split the visible keys into 32-key tiles (warp w takes tiles
+// w, w + 4, ...) and read K and V straight from L2: scores with lane = key (q broadcast from shared
+// memory), online softmax per query and warp, values with lane = HD / 32 output dims and each key's
+// probability broadcast by shuffle. The four warps' (max, sum, acc) meet in shared memory and
+// warp 0 merges them in warp order. Visibility as k_attn_prefill's.
+constexpr int kTreeQ = 4;
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const float *q, const __half *kc,
+                                                   const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
+                                                   int cap, const int *slot_base, int slot_off, float scale,
+                                                   DevState *st) {
+    pdl_enter();
+    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
+    constexpr int DL = HD / 32;
+    __shared__ __align__(16) float qs[kTreeQ][HD];
+    __shared__ float pm[4][kTreeQ], pl[4][kTreeQ];
+    __shared__ __align__(16) float pa[4][kTreeQ][HD];
+    const int h = blockIdx.x, q0 = blockIdx.y * kTreeQ;
+    const int g = h / (nh / nkv);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kTreeQ * HD; i += 128) {
+        const int qq = i / HD, d = i - qq * HD;
+        qs[qq][d] = q0 + qq < T ? q[(size_t)(q0 + qq) * nh * HD + h * HD + d] * scale : 0.f;
+    }
+    __syncthreads();
+    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
+    float m[kTreeQ], l[kTreeQ], acc[kTreeQ][DL];
+#pragma unroll
+    for (int i = 0; i < kTreeQ; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[i][d] = 0.f;
+    }
+    const int last = slot0 + min(T, q0 + kTreeQ) - 1;    // the last key any query of this CTA sees
+    for (int k0 = warp * 32; k0 <= last; k0 += 4 * 32) {
+        const int key = k0 + lane;
+        float s[kTreeQ] = {0.f, 0.f, 0.f, 0.f};
+        if (key <= last) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)key * HD);
+#pragma unroll 4
+            for (int c = 0; c < HD / 8; ++c) {
+                const uint4 kk = __ldg(kr + c);
+                const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
+                const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
+                const float2 k45 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.z));
+                const float2 k67 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.w));
+#pragma unroll
+                for (int i = 0; i < kTreeQ; ++i) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[i][8 * c]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[i][8 * c + 4]);
+                    s[i] = fmaf(qa.x, k01.x, s[i]);
+                    s[i] = fmaf(qa.y, k01.y, s[i]);
+                    s[i] = fmaf(qa.z, k23.x, s[i]);
+                    s[i] = fmaf(qa.w, k23.y, s[i]);
+                    s[i] = fmaf(qb.x, k45.x, s[i]);
+                    s[i] = fmaf(qb.y, k45.y, s[i]);
+                    s[i] = fmaf(qb.z, k67.x, s[i]);
+                    s[i] = fmaf(qb.w, k67.y, s[i]);
+                }
+            }
+        }
+        float pr[kTreeQ];
+#pragma unroll
+        for (int i = 0; i < kTreeQ; ++i) {
+            const int t = q0 + i;
+            bool vis = t < T && key <= slot0 + t;
+            if (mask && vis && key >= slot0) vis = (mask[t] >> (key - slot0)) & 1ull;
+            const float sv = vis ? s[i] : -INFINITY;
+            const float mnew = fmaxf(m[i], warp_max(sv));
+            pr[i] = mnew == -INFINITY ? 0.f : expf(sv - mnew);
+            const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
+            l[i] = l[i] * corr + warp_sum(pr[i]);
+            m[i] = mnew;
+#pragma unroll
+            for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
+        }
+        // values: key k0 + j's probability from lane j; its V row read by all lanes (DL dims each)
+        const int nk = min(32, last + 1 - k0);
+        for (int j = 0; j < nk; ++j) {
+            float vf[DL];
+            const __half *vr = vb + (size_t)(k0 + j) * HD + lane * DL;
+            if constexpr (DL == 4) {
+                const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vr));
+                const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                const float2 v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                vf[0] = v0.x;
+                vf[1] = v0.y;
+                vf[2] = v1.x;
+                vf[3] = v1.y;
+            } else {
+                const float2 v0 = __half22float2(__ldg(reinterpret_cast<const __half2 *>(vr)));
+                vf[0] = v0.x;
+                vf[1] = v0.y;
+            }
+#pragma unroll
+            for (int i = 0; i < kTreeQ; ++i) {
+                const float pj = __shfl_sync(0xffffffffu, pr[i], j);
+#pragma unroll
+                for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, vf[d], acc[i][d]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kTreeQ; ++i) {
+        if (lane == 0) {
+            pm[warp][i] = m[i];
+            pl[warp][i] = l[i];
+        }
+#pragma unroll
+        for (int d = 0; d < DL; ++d) pa[warp][i][lane * DL + d] = acc[i][d];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < kTreeQ; ++i) {
+            const int t = q0 + i;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) M = fmaxf(M, pm[w][i]);
+            float L = 0.f, o[DL];
+#pragma unroll
+            for (int d = 0; d < DL; ++d) o[d] = 0.f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float f = pm[w][i] == -INFINITY ? 0.f : expf(pm[w][i] - M);
+                L = fmaf(pl[w][i], f, L);
+#pragma unroll
+                for (int d = 0; d < DL; ++d) o[d] = fmaf(pa[w][i][lane * DL + d], f, o[d]);
+            }
+            if (t < T) {
+#pragma unroll
+                for (int d = 0; d < DL; ++d) {
+                    const float v = o[d] / L;
+                    const __half hv = __float2half_rn(v);
+                    const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
+                    oh[idx] = hv;
+                    ol[idx] = __float2half_rn(v - __half2float(hv));
+                }
+            }
+        }
+    }
+}
+
 // w = q * scale (exact in fp32), times 2^k (exact), split into fp16 hi = fp16(w') and lo =
 // fp16(w' - hi): hi + lo = w' exactly while w' and its remainder stay in fp16's normal range, which
 // the caller's k arranges for the matrix's largest weights. One thread per 8 inputs of a row.
 __global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, float p2,
-                               int dst_mul, int dst_add) {
+                               int dst_mul, int dst_add, int pair_hd) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)rows * (K / 8)) return;
     const long long e0 = idx * 8;
     const long long r = e0 / K;
-    const long long d0 = (r * dst_mul + dst_add) * K + (e0 - r * K);   // destination row r * dst_mul + dst_add
+    long long dr = r * dst_mul + dst_add;
+    if (pair_hd > 0) {                                    // RoPE partners adjacent
+        const long long hh = r / pair_hd, dd = r - hh * pair_hd;
+        dr = hh * pair_hd + (dd < pair_hd / 2 ? 2 * dd : 2 * (dd - pair_hd / 2) + 1);
+    }
+    const long long d0 = dr * K + (e0 - r * K);
     const float sc = __half2float(scales[e0 / 32]) * p2;
     const uint2 raw = *reinterpret_cast<const uint2 *>(q + e0);
     const int8_t *b = reinterpret_cast<const int8_t *>(&raw);
@@ -288,8 +423,7 @@ size_t qrows_of(const PrefillDims &d) { return (size_t)(d.heads + 2 * d.kv_heads
 size_t prefill_scratch_bytes(const PrefillDims &d) {
     const size_t T = d.max_tokens;
     return up256(T * d.hidden * 4) + up256(2 * T * kmax_of(d) * 2) + up256(2 * T * d.inter * 2) +
-           up256(T * qrows_of(d) * 4) + up256(T * d.heads * d.head_dim * 4) + up256((size_t)kPrefillLogitRows * d.vocab * 4) +
-           up256(mcol_workspace_bytes(kPrefillMaxCtas, d.max_tokens)) + up256(kPrefillMaxCtas * sizeof(unsigned));
+           up256(T * d.heads * d.head_dim * 4) + up256((size_t)kPrefillLogitRows * d.vocab * 4);
 }
 
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
@@ -300,13 +434,8 @@ PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
     s.x = reinterpret_cast<float *>(take(T * d.hidden * 4));
     s.xa = reinterpret_cast<__half *>(take(2 * T * kmax_of(d) * 2));
     s.xb = reinterpret_cast<__half *>(take(2 * T * d.inter * 2));
-    s.y = reinterpret_cast<float *>(take(T * qrows_of(d) * 4));
     s.q = reinterpret_cast<float *>(take(T * d.heads * d.head_dim * 4));
     s.logits = reinterpret_cast<float *>(take((size_t)kPrefillLogitRows * d.vocab * 4));
-    s.ws_bytes = mcol_workspace_bytes(kPrefillMaxCtas, d.max_tokens);
-    s.ws = reinterpret_cast<float *>(take(s.ws_bytes));
-    s.cnt = reinterpret_cast<unsigned *>(take(kPrefillMaxCtas * sizeof(unsigned)));
-    s.cnt_count = kPrefillMaxCtas;
     return s;
 }
 
@@ -325,10 +454,6 @@ McolOp proj(const PrefillDims &d, const PrefillScratch &s, const PrefillMat &w, 
     op.x_rows = 2 * d.max_tokens;
     op.lo_row0 = d.max_tokens;
     op.T = T;
-    op.ws = s.ws;
-    op.ws_bytes = s.ws_bytes;
-    op.cnt = s.cnt;
-    op.cnt_count = s.cnt_count;
     op.max_ctas = kPrefillMaxCtas;
     op.st = st;
     return op;
@@ -341,26 +466,29 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
                                        DevState *st, cudaStream_t stream) {
     const int H = d.hidden, QR = (int)qrows_of(d), A = d.heads * d.head_dim;
     const size_t lo = (size_t)d.max_tokens;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xa, s.xa + lo * H, s.x, L.in_norm, H, d.eps);
-    McolOp qkv = proj(d, s, L.qkv, MC_STORE, QR, H, s.xa, T, st);
-    qkv.y = s.y;
-    qkv.ldy = QR;
-    cudaError_t e = launch_mcol(qkv, stream, false);
+    cudaError_t e = launch_pdl(k_rmsnorm_hilo, T, kNormThreads, stream, s.xa, s.xa + lo * H, s.x, L.in_norm, H, d.eps);
     if (e != cudaSuccess) return e;
-    k_qkv_rope_kv<<<T, 256, 0, stream>>>(s.q, kc, vc, s.y, L.qkv_b, rope, pos, T, d.heads, d.kv_heads, d.head_dim,
-                                         cap, slot_base, slot_off, d.max_pos, st);
-    const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
-    if (d.head_dim == 128)
-        k_attn_prefill<128><<<grid, 128, 0, stream>>>(s.xa, s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads,
-                                                      cap, slot_base, slot_off, scale, st);
-    else
-        k_attn_prefill<64><<<grid, 128, 0, stream>>>(s.xa, s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads,
-                                                     cap, slot_base, slot_off, scale, st);
+    // QKV with bias, RoPE and the K/V cache write in the epilogue (q to s.q)
+    McolOp qkv = proj(d, s, L.qkv, MC_QKV, QR, H, s.xa, T, st);
+    qkv.qkv = McolQkv{L.qkv_b, rope, pos, slot_base, slot_off, cap, d.heads, d.kv_heads, d.head_dim, d.max_pos,
+                      s.q, kc, vc};
+    e = launch_mcol(qkv, stream, true);
+    if (e != cudaSuccess) return e;
+    if (T <= kTreeAttnMaxT) {
+        const dim3 grid(d.heads, (T + kTreeQ - 1) / kTreeQ);
+        e = launch_pdl(d.head_dim == 128 ? k_attn_tree<128> : k_attn_tree<64>, grid, 128, stream, s.xa,
+                       s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+    } else {
+        const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
+        e = launch_pdl(d.head_dim == 128 ? k_attn_prefill<128> : k_attn_prefill<64>, grid, 128, stream, s.xa,
+                       s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+    }
+    if (e != cudaSuccess) return e;
     // O projection into the residual stream
     McolOp o = proj(d, s, L.o, MC_RESID, H, A, s.xa, T, st);
     o.y = s.x;
     o.ldy = H;
-    e = launch_mcol(o, stream, false);
+    e = launch_mcol(o, stream, true);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -369,26 +497,26 @@ cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L
                                      DevState *st, cudaStream_t stream) {
     const int H = d.hidden, I = d.inter;
     const size_t lo = (size_t)d.max_tokens;
-    k_rmsnorm_hilo<<<T, kNormThreads, 0, stream>>>(s.xa, s.xa + lo * H, s.x, L.post_norm, H, d.eps);
+    cudaError_t e = launch_pdl(k_rmsnorm_hilo, T, kNormThreads, stream, s.xa, s.xa + lo * H, s.x, L.post_norm, H, d.eps);
+    if (e != cudaSuccess) return e;
     // gate_up (rows interleaved: 2i gate, 2i + 1 up) -> SiLU(gate) * up as the down projection's input
     McolOp gu = proj(d, s, L.gate_up, MC_SWIGLU, 2 * I, H, s.xa, T, st);
     gu.act_h = s.xb;
     gu.act_l = s.xb + lo * I;
     gu.ld_act = I;
-    cudaError_t e = launch_mcol(gu, stream, false);
+    e = launch_mcol(gu, stream, true);
     if (e != cudaSuccess) return e;
     McolOp dn = proj(d, s, L.down, MC_RESID, H, I, s.xb, T, st);
     dn.y = s.x;
     dn.ldy = H;
-    e = launch_mcol(dn, stream, false);
+    e = launch_mcol(dn, stream, true);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,
                                  const int32_t *tok, int T, DevState *st, cudaStream_t stream) {
-    k_embed_rows<<<T, 256, 0, stream>>>(s.x, embed, tok, d.hidden, d.vocab, st);
-    return cudaGetLastError();
+    return launch_pdl(k_embed_rows, T, 256, stream, s.x, embed, tok, d.hidden, d.vocab, st);
 }
 
 // Logits of rows [r0, r0 + n) of the chunk (n <= kPrefillLogitRows) into `out` (row stride vocab):
@@ -396,22 +524,25 @@ cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, 
 cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s, const float *final_norm,
                                   const PrefillMat &head, int r0, int n, float *out, DevState *st, cudaStream_t stream) {
     const int H = d.hidden;
-    k_rmsnorm_hilo<<<n, kNormThreads, 0, stream>>>(s.xa, s.xa + (size_t)d.max_tokens * H, s.x + (size_t)r0 * H,
-                                                    final_norm, H, d.eps);
+    cudaError_t e = launch_pdl(k_rmsnorm_hilo, n, kNormThreads, stream, s.xa, s.xa + (size_t)d.max_tokens * H,
+                               s.x + (size_t)r0 * H, final_norm, H, d.eps);
+    if (e != cudaSuccess) return e;
     McolOp hd = proj(d, s, head, MC_STORE, d.vocab, H, s.xa, n, st);
     hd.y = out;
     hd.ldy = d.vocab;
-    cudaError_t e = launch_mcol(hd, stream, false);
+    e = launch_mcol(hd, stream, true);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                int dst_mul, int dst_add, cudaStream_t s) {
-    if (K % 32 || k < -30 || k > 30 || dst_mul < 1 || dst_add < 0 || dst_add >= dst_mul) return cudaErrorInvalidValue;
+                                int dst_mul, int dst_add, int pair_hd, cudaStream_t s) {
+    if (K % 32 || k < -30 || k > 30 || dst_mul < 1 || dst_add < 0 || dst_add >= dst_mul || pair_hd < 0 || pair_hd % 2 ||
+        (pair_hd > 0 && (rows % pair_hd || dst_mul != 1)))
+        return cudaErrorInvalidValue;
     const long long n = (long long)rows * (K / 8);
     k_dequant_hilo<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(hi, lo, q, scales, rows, K, ldexpf(1.0f, k), dst_mul,
-                                                               dst_add);
+                                                               dst_add, pair_hd);
     return cudaGetLastError();
 }
 

@@ -7,9 +7,14 @@ times (and capture each GPU's step graph); each timed step then submits the 16 r
 `submit_batch`, which splits them by those measurements (identical GPUs: 16 / N each). Requests
 partition across GPUs; nothing is exchanged between GPUs.
 
-`value` = generated tokens / the slowest rank's device span (CUDA events around every timed request
-on that rank, first start to last end), the max over ranks; `e2e` = the same tokens over rank 0's
-wall clock from the first submit to the last result (TCP, JSON and host work included).
+`value` = generated tokens / the makespan on rank 0's wall clock, from the first submit to the last
+result (TCP, JSON and host work included: the reference's own burst measure,
+`experiments/hive_scaling/benchmark_hive_fleet.py:112`); `device_tok_s` = the same tokens over the
+slowest rank's device span (CUDA events around every timed request on that rank, first start to
+last end, the max over ranks).
+
+`burst_on_engine` runs the same burst on an engine the caller already built (the decode bench's
+replica on every rank) and returns the summary object the bench line carries.
 """
 from __future__ import annotations
 
@@ -22,26 +27,20 @@ REQUESTS, NEW_TOKENS, LOW, HIGH = 16, 32, 32, 128
 MODEL_ID = "qwen2-1.5b"
 
 
-def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barrier, peaks):
+def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_over_ranks, barrier):
+    """The 16 x 32 burst through HIVE on `eng` (this rank's engine); every rank calls it. Returns the
+    summary on rank 0 (None elsewhere)."""
     import torch
     import torch.distributed as dist
 
-    from ..config import QWEN2_1_5B
-    from ..engine import CudaQwen2
-    from ..randinit import burst_prompts, make_weights
+    from ..randinit import burst_prompts
     from .agent import GreedyExecutor
     from .pool import HiveAgent, HiveBroker
 
-    cfg = QWEN2_1_5B
-    dev = torch.device("cuda", local)
+    dev = eng.device
     torch.cuda.set_device(dev)
-    w = make_weights(cfg, seed=0, dtype=torch.float16)
-    eng = CudaQwen2(cfg, w, device=dev)
-    del w
-    prompts = burst_prompts(cfg.vocab, REQUESTS, LOW, HIGH, seed=0)
-
-    # device time of this rank's timed requests
-    spans = []
+    prompts = burst_prompts(eng.cfg.vocab, REQUESTS, LOW, HIGH, seed=0)
+    spans = []                                  # device time of this rank's timed requests
 
     def timer(start: bool):
         ev = torch.cuda.Event(enable_timing=True)
@@ -79,8 +78,7 @@ def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barr
 
     th = threading.Thread(target=run_agent, name=f"hive-agent-gpu{rank}", daemon=True)
     th.start()
-
-    line = None
+    info = None
     if rank == 0:
         t_end = time.monotonic() + 300
         while len(broker.workers()) < world and time.monotonic() < t_end:
@@ -93,24 +91,22 @@ def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barr
             return [{"ids": p, "max_new_tokens": NEW_TOKENS, "request": i, "phase": phase, "step": step}
                     for i, p in enumerate(prompts)]
 
-        # warm-up: until every worker has 3 measured leases (and at least args.warmup rounds)
+        # warm-up: until every worker has 3 measured leases (and at least `warmup` rounds)
         rounds = 0
         while True:
-            futs = broker.submit_batch(payloads("warmup", rounds)[:max(world, 2)], require_profiles=False, **kw)
-            for f in futs:
+            for f in broker.submit_batch(payloads("warmup", rounds)[:max(world, 2)], require_profiles=False, **kw):
                 f.result(timeout=600)
             rounds += 1
             have = [broker.cost_model.estimate(kind="throughput.generate", model=MODEL_ID, worker=f"gpu{r}",
                                                token_budget=NEW_TOKENS) for r in range(world)]
-            if rounds >= max(3, args.warmup) and all(h is not None for h in have):
+            if rounds >= max(3, warmup) and all(h is not None for h in have):
                 break
             if rounds > 200:
                 raise RuntimeError("warm-up could not measure every worker")
-        shas = {}
-        assigned = {}
+        shas, assigned, makespans = {}, {}, []
         with ClockSampler(list(range(world))) as clocks:
-            t0 = time.perf_counter()
-            for step in range(args.steps):
+            for step in range(steps):
+                t0 = time.perf_counter()
                 futs = broker.submit_batch(payloads("timed", step), **kw)
                 for f in futs:
                     assigned[f.planned_worker_id] = assigned.get(f.planned_worker_id, 0) + 1
@@ -118,36 +114,59 @@ def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barr
                     r = f.result(timeout=600)
                     if shas.setdefault(r["request"], r["token_sha256"]) != r["token_sha256"]:
                         raise RuntimeError(f"request {r['request']}: tokens differ between GPUs / steps")
-            wall_s = time.perf_counter() - t0
+                makespans.append(time.perf_counter() - t0)
         broker.close()
-        line = {"clocks": clocks.summary(), "wall_s": wall_s, "assigned": assigned,
+        info = {"clocks": clocks.summary(), "makespans": makespans, "assigned": assigned,
                 "token_sha256": hashlib.sha256(json.dumps([shas[i] for i in sorted(shas)]).encode()).hexdigest()}
     th.join(timeout=600)
     if errors:
         raise errors[0]
     torch.cuda.synchronize(dev)
     span_ms = spans[0][0].elapsed_time(spans[-1][1]) if spans else 0.0
-    busy_ms = sum(a.elapsed_time(b) for a, b in spans)
     barrier(world)
     span_max = max_over_ranks(span_ms, world, dev)
+    if rank != 0:
+        return None
+    tokens = steps * REQUESTS * NEW_TOKENS
+    wall = sum(info["makespans"])
+    return {"metric": "burst tok/s (16 x 32 requests, HIVE pull agent per GPU, wall-clock makespan)",
+            "value": tokens / wall, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "makespan_ms": [1000.0 * m for m in info["makespans"]],
+            "device_tok_s": tokens / (span_max / 1000.0) if span_max > 0 else None,
+            "assigned": info["assigned"], "prompt_tokens_per_step": sum(len(p) for p in prompts),
+            "token_sha256": info["token_sha256"], "clocks": info["clocks"],
+            "note": "makespan = submit_batch to the last result on rank 0 (loopback TCP broker, JSON, host work "
+                    "included); device_tok_s = the same tokens over the slowest rank's device span"}
+
+
+def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barrier, peaks):
+    """`bench.py --workload burst`: the burst as the line's own metric."""
+    import torch
+    from ..config import QWEN2_1_5B
+    from ..engine import CudaQwen2
+    from ..randinit import make_weights
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = make_weights(QWEN2_1_5B, seed=0, dtype=torch.float16)
+    eng = CudaQwen2(QWEN2_1_5B, w, device=dev)
+    del w
+    b = burst_on_engine(eng, args.steps, args.warmup, world, rank, local, ClockSampler, max_over_ranks, barrier)
     eng.close()
     if rank != 0:
         return None
     tokens = args.steps * REQUESTS * NEW_TOKENS
-    prompt_tokens = sum(len(p) for p in prompts)
+    wall_ms = sum(b["makespan_ms"])
     return {"metric": "Qwen2-1.5B burst tok/s (16 x 32 requests, HIVE pull agent per GPU)",
-            "value": tokens / (span_max / 1000.0), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": span_max / args.steps, "higher_is_better": True,
+            "value": b["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": wall_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": f"{REQUESTS} independent greedy requests x {NEW_TOKENS} new tokens per step, "
                                    f"prompts of uniform-random length in [{LOW}, {HIGH}] (seeded), qwen2-1.5b "
                                    "random-init fp16 weights, one HIVE pull agent per GPU, loopback TCP broker",
                        "parallelism": f"requests partitioned over {world} GPU(s) by measured service time, "
-                                      "no collective", "assigned": line["assigned"],
-                       "prompt_tokens_per_step": prompt_tokens,
-                       "rank0_busy_ms": busy_ms, "l2": "inputs larger than L2: 3.09 GB of weights per step launch"},
-            "e2e": {"value": tokens / line["wall_s"], "unit": "tok/s", "h2d_bytes_per_step": prompt_tokens * 4,
-                    "d2h_bytes_per_step": REQUESTS * NEW_TOKENS * 4,
-                    "note": "rank 0 wall clock: submit_batch to the last result, through the TCP broker"},
-            "gpu_launches": args.steps * sum(len(p) + NEW_TOKENS + 1 for p in prompts),
-            "clocks": line["clocks"], "token_sha256": line["token_sha256"]}
+                                      "no collective", "assigned": b["assigned"],
+                       "device_tok_s": b["device_tok_s"],
+                       "l2": "inputs larger than L2: 3.09 GB of weights per step launch"},
+            "e2e": {"value": b["value"], "unit": "tok/s", "h2d_bytes_per_step": b["prompt_tokens_per_step"] * 4,
+                    "d2h_bytes_per_step": REQUESTS * NEW_TOKENS * 4, "note": b["note"]},
+            "gpu_launches": None, "clocks": b["clocks"], "token_sha256": b["token_sha256"]}
