@@ -139,6 +139,21 @@ int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols,
 int sp_topk(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t k,
             int32_t *idx_dev, float *val_dev, float *lse_dev, void *stream);
 
+/* Greedy acceptance of a verified draft tree on the device (replaces the selection loop of
+ * seedplane/speculative.py:55-92, verify_greedy, fed by one batched pass instead of per-prefix target
+ * calls). node_pred_dev: int32 [n] on the engine's device, the target's argmax after each node (the
+ * argmax output of sp_verify_tree); root_pred: its argmax after the committed prefix. tokens /
+ * parents (host, parents[i] < i, -1 = child of the prefix); path_ends (host, [n_paths]): the last
+ * node of each draft branch in input order. Each branch is walked from its root while the target
+ * agrees; the first disagreement emits the target's token and rejects the branch; the chosen
+ * branch has the most accepted draft tokens, then the most emitted tokens, then the earliest input
+ * position; no paths: the one token root_pred. out_host [2n + 5]: emitted count, accepted count,
+ * chosen branch (-1: none), the target's token after a fully accepted branch (else -1), emitted
+ * tokens [n + 1], accepted node indices [n]. n <= 64, n_paths <= 1024. Synchronises `stream`. */
+int sp_accept_greedy(sp_engine *e, const int32_t *node_pred_dev, int32_t root_pred, const int32_t *tokens_host,
+                     const int32_t *parents_host, int32_t n, const int32_t *path_ends_host, int32_t n_paths,
+                     int32_t *out_host, void *stream);
+
 /* Stochastic acceptance of a draft tree at `temperature` with a counter-based RNG (seed, counter):
  * recursive rejection sampling (children tried in node order, accept with min(1, p/q), residual
  * max(p - q, 0) after a rejection, a draw from the residual when every child is rejected). The

@@ -22,7 +22,7 @@ SP_WEIGHTS_I8_B32 = 1
 EXPORTED = ("sp_last_error", "sp_version", "sp_engine_create", "sp_engine_destroy", "sp_engine_device_bytes",
             "sp_kv_create", "sp_kv_destroy", "sp_kv_length", "sp_kv_capacity", "sp_kv_set_length",
             "sp_forward", "sp_decode", "sp_verify_tree", "sp_kv_commit", "sp_argmax", "sp_argmax_noalloc", "sp_mcol_gemm", "sp_topk",
-            "sp_accept_stochastic", "sp_sample_filter",
+            "sp_accept_stochastic", "sp_accept_greedy", "sp_sample_filter",
             "sp_device_status",
             "sp_trace_read")
 
@@ -82,6 +82,7 @@ def load(path: Path = LIB_PATH):
         "sp_topk": (C.c_int, [vp, vp, i32, i32, i64, i32, vp, vp, vp, vp]),
         "sp_accept_stochastic": (C.c_int, [vp, vp, vp, i64, i32, pi32, pi32, i32, C.c_double, C.c_uint64,
                                            C.c_uint64, pi32, vp]),
+        "sp_accept_greedy": (C.c_int, [vp, vp, i32, pi32, pi32, i32, pi32, i32, pi32, vp]),
         "sp_sample_filter": (C.c_int, [vp, i32, C.c_double, i32, C.c_double, vp, vp]),
         "sp_device_status": (C.c_int, [vp, vp]),
         "sp_trace_read": (i64, [vp, C.POINTER(C.c_uint64), i64]),

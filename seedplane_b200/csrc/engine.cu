@@ -149,6 +149,7 @@ struct sp_engine {
     PrefillMat head_pf{};                   // row-major LM head for the batched pass (the embedding when tied)
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
+    int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
     int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
@@ -1076,6 +1077,7 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->mc_trace);
     cudaFree(e->vt);
     cudaFree(e->acc_scratch);
+    cudaFree(e->gr_buf);
     delete e;
 }
 
@@ -1451,6 +1453,38 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
     SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, temperature, seed,
                                      counter, e->acc_scratch, dout, s));
     SP_CUDA(cudaMemcpyAsync(out_host, dout, (size_t)(2 * n + 3) * 4, cudaMemcpyDeviceToHost, s));
+    SP_CUDA(cudaStreamSynchronize(s));
+    return SP_OK;
+}
+
+int sp_accept_greedy(sp_engine *e, const int32_t *node_pred_dev, int32_t root_pred, const int32_t *tokens_host,
+                     const int32_t *parents_host, int32_t n, const int32_t *path_ends_host, int32_t n_paths,
+                     int32_t *out_host, void *stream) {
+    if (!e || !out_host || (n > 0 && (!node_pred_dev || !tokens_host || !parents_host)) ||
+        (n_paths > 0 && !path_ends_host))
+        return fail(SP_ERR_INVALID, "null argument");
+    if (n < 0 || n > kSmallNodes) return fail(SP_ERR_CAPACITY, "tree of %d nodes exceeds %d", n, kSmallNodes);
+    if (n_paths < 0 || n_paths > kGreedyMaxPaths)
+        return fail(SP_ERR_CAPACITY, "%d paths exceed %d", n_paths, kGreedyMaxPaths);
+    if (n_paths > 0 && n == 0) return fail(SP_ERR_INVALID, "paths without nodes");
+    for (int i = 0; i < n; ++i)
+        if (parents_host[i] >= i || parents_host[i] < -1) return fail(SP_ERR_INVALID, "node %d: bad parent", i);
+    for (int j = 0; j < n_paths; ++j)
+        if (path_ends_host[j] < 0 || path_ends_host[j] >= n) return fail(SP_ERR_INVALID, "path %d: bad end node", j);
+    SP_CUDA(cudaSetDevice(e->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    constexpr int kIn = 2 * kSmallNodes + kGreedyMaxPaths, kOut = 2 * kSmallNodes + 5;
+    if (!e->gr_buf) SP_CUDA(cudaMalloc(&e->gr_buf, (size_t)(kIn + kOut) * sizeof(int32_t)));
+    std::vector<int32_t> host(2 * kSmallNodes + n_paths, 0);
+    if (n > 0) {
+        memcpy(host.data(), tokens_host, n * 4);
+        memcpy(host.data() + kSmallNodes, parents_host, n * 4);
+    }
+    if (n_paths > 0) memcpy(host.data() + 2 * kSmallNodes, path_ends_host, n_paths * 4);
+    int32_t *dtok = e->gr_buf, *dpar = dtok + kSmallNodes, *dend = dpar + kSmallNodes, *dout = e->gr_buf + kIn;
+    SP_CUDA(cudaMemcpyAsync(dtok, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s));
+    SP_CUDA(launch_accept_greedy(node_pred_dev, root_pred, dtok, dpar, n, dend, n_paths, dout, s));
+    SP_CUDA(cudaMemcpyAsync(out_host, dout, (size_t)(2 * n + 5) * 4, cudaMemcpyDeviceToHost, s));
     SP_CUDA(cudaStreamSynchronize(s));
     return SP_OK;
 }

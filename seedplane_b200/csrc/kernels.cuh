@@ -399,6 +399,13 @@ cudaError_t launch_sample_filter(const float *logits, int V, double temperature,
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
                                      const int *parent, int n, double temperature, unsigned long long seed,
                                      unsigned long long counter, double *scratch, int *out, cudaStream_t s);
+// Greedy acceptance of a verified tree (one warp): pred [n] = target argmax after each node, ends
+// [n_paths] = last node of each draft path in input order; out [2 n + 5]: emitted count, accepted
+// count, chosen path, target token after a fully accepted path (else -1), emitted tokens (n + 1
+// slots), accepted node indices (n slots).
+constexpr int kGreedyMaxPaths = 1024;
+cudaError_t launch_accept_greedy(const int *pred, int root_pred, const int *tok, const int *parent, int n,
+                                 const int *ends, int n_paths, int *out, cudaStream_t s);
 
 // Row-wise greedy argmax (argmax.cu). A row is split over argmax_ctas(cols) CTAs whose partial
 // (max, index) pairs meet in the scratch: val / idx [rows][kArgmaxMaxCtas] and one counter per

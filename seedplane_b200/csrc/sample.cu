@@ -438,4 +438,79 @@ cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long 
     return cudaGetLastError();
 }
 
+// ---- greedy acceptance of a verified tree ----------------------------------------------------
+// The reference's rule (seedplane/speculative.py:55-92) over per-node target argmaxes: every draft
+// path is walked from its root while the target's token after the previous node (after the
+// committed prefix for the root) equals the node's token; the first disagreement emits the
+// target's token and ends the path; a fully agreed path emits its draft tokens only. The chosen
+// path has the most accepted draft tokens, then the most emitted tokens, then the lowest input
+// position. One warp: lane j walks paths j, j + 32, ...; the keys (accepted, emitted, -position)
+// meet in a warp maximum; lane 0 writes the chosen path's result.
+namespace {
+
+SP_DEVINL int greedy_walk(const int *pred, int root_pred, const int *tok, const int *parent, int end, int *chain,
+                          int &emitted) {
+    int d = 0;
+    for (int v = end; v >= 0 && d < kSmallNodes; v = parent[v]) chain[d++] = v;   // end .. root
+    int prev = -1, acc = 0;
+    emitted = 0;
+    for (int i = d - 1; i >= 0; --i) {
+        const int nid = chain[i];
+        const int want = prev < 0 ? root_pred : pred[prev];
+        ++emitted;
+        if (want != tok[nid]) return acc;
+        ++acc;
+        prev = nid;
+    }
+    return acc;
+}
+
+__global__ void __launch_bounds__(32) k_accept_greedy(const int *pred, int root_pred, const int *tok, const int *parent,
+                                                      int n, const int *ends, int n_paths, int *out) {
+    const int lane = threadIdx.x;
+    int chain[kSmallNodes];
+    unsigned best = 0u;                     // (accepted << 20) | (emitted << 10) | (1023 - position), + 1
+    for (int p = lane; p < n_paths; p += 32) {
+        int em = 0;
+        const int acc = greedy_walk(pred, root_pred, tok, parent, ends[p], chain, em);
+        best = max(best, (((unsigned)acc << 20) | ((unsigned)em << 10) | (unsigned)(1023 - p)) + 1u);
+    }
+    best = __reduce_max_sync(0xffffffffu, best);
+    if (lane != 0) return;
+    int *emit = out + 4, *nodes = out + 4 + n + 1;
+    if (n_paths == 0) {                     // no draft: one target token
+        out[0] = 1;
+        out[1] = 0;
+        out[2] = -1;
+        out[3] = -1;
+        emit[0] = root_pred;
+        return;
+    }
+    const int p = 1023 - (int)((best - 1u) & 1023u);
+    int d = 0;
+    for (int v = ends[p]; v >= 0 && d < kSmallNodes; v = parent[v]) chain[d++] = v;
+    int prev = -1, acc = 0, em = 0;
+    for (int i = d - 1; i >= 0; --i) {
+        const int nid = chain[i];
+        const int want = prev < 0 ? root_pred : pred[prev];
+        emit[em++] = want;
+        if (want != tok[nid]) break;
+        nodes[acc++] = nid;
+        prev = nid;
+    }
+    out[0] = em;
+    out[1] = acc;
+    out[2] = p;
+    out[3] = (acc == d && acc > 0) ? pred[prev] : -1;    // the target's token after a fully accepted path
+}
+
+}  // namespace
+
+cudaError_t launch_accept_greedy(const int *pred, int root_pred, const int *tok, const int *parent, int n,
+                                 const int *ends, int n_paths, int *out, cudaStream_t s) {
+    if (n < 0 || n > kSmallNodes || n_paths < 0 || n_paths > kGreedyMaxPaths) return cudaErrorInvalidValue;
+    k_accept_greedy<<<1, 32, 0, s>>>(pred, root_pred, tok, parent, n, ends, n_paths, out);
+    return cudaGetLastError();
+}
+
 }  // namespace sp

@@ -183,19 +183,44 @@ def accept_greedy(flat: FlatForest, root_pred: int, node_pred: Sequence[int]) ->
     return _select(flat, lambda node: int(root_pred) if node < 0 else int(node_pred[node]))
 
 
+def accept_greedy_device(engine, flat: FlatForest, root_pred: int, node_pred_dev
+                         ) -> Tuple[Verification, Tuple[int, ...], Optional[int]]:
+    """`accept_greedy` on the device (`sp_accept_greedy`): the same decision from the per-node
+    argmaxes that stay in device memory (int32 [n] on the engine's device); only the decision comes
+    back. Returns the verification, the accepted draft nodes and the target's token after a fully
+    accepted path (None otherwise)."""
+    import ctypes as C
+    from . import _native as N
+    from .engine import _stream
+    n = len(flat.tokens)
+    ends = [ids[-1] for ids in flat.node_paths]
+    out = (C.c_int32 * (2 * n + 5))()
+    ptr = C.c_void_p(node_pred_dev.data_ptr()) if n else C.c_void_p(None)
+    N.check(N.load().sp_accept_greedy(engine.handle, ptr, int(root_pred), N.int_array(flat.tokens),
+                                      N.int_array(flat.parents), n, N.int_array(ends), len(ends), out,
+                                      C.c_void_p(_stream(engine.device))))
+    n_out, n_acc, chosen, nxt = out[0], out[1], out[2], out[3]
+    emitted = tuple(out[4 + i] for i in range(n_out))
+    nodes = tuple(out[4 + n + 1 + i] for i in range(n_acc))
+    path = tuple(flat.paths[chosen]) if chosen >= 0 else ()
+    rejected = chosen >= 0 and n_out > n_acc          # no draft: the target's token, nothing rejected
+    return Verification(emitted, n_acc, rejected, n_out, path), nodes, (nxt if nxt >= 0 else None)
+
+
 @dataclass(frozen=True)
 class TreeResult:
     verification: Verification
     accepted_nodes: Tuple[int, ...]  # node indices of the accepted draft tokens, in order
-    node_pred: Tuple[int, ...]       # target argmax after every node
+    node_pred: Optional[Tuple[int, ...]]   # target argmax after every node (None: decided on the device)
     next_pred: Optional[int]         # target argmax after the emitted tokens, when known (full acceptance)
     flat: FlatForest
 
 
 def verify_tree(engine, kv, forest: SpeculativeForest, root_pred: int, base_pos: int,
-                want_logits: bool = False) -> TreeResult:
+                want_logits: bool = False, on_device: bool = True) -> TreeResult:
     """One batched target pass over the whole forest (`sp_verify_tree`) and the reference's
-    selection rule on its argmaxes.
+    selection rule on its argmaxes: on the device (`sp_accept_greedy`, only the decision is read
+    back) or, with on_device=False, on the host over the argmaxes read back.
 
     `root_pred` is the target's greedy token after the committed prefix (the caller has it from
     the previous step); `base_pos` is the position of the first draft token. The cache length is
@@ -204,6 +229,9 @@ def verify_tree(engine, kv, forest: SpeculativeForest, root_pred: int, base_pos:
     if not flat.tokens:
         return TreeResult(Verification((int(root_pred),), 0, False, 1, ()), (), (), None, flat)
     argmax, _ = engine.verify_tree(kv, list(flat.tokens), list(flat.parents), base_pos, want_logits=want_logits)
+    if on_device:
+        ver, nodes, next_pred = accept_greedy_device(engine, flat, root_pred, argmax)
+        return TreeResult(ver, nodes, None, next_pred, flat)
     node_pred = tuple(int(t) for t in argmax.cpu().tolist())
     ver, nodes = accept_greedy(flat, root_pred, node_pred)
     next_pred = node_pred[nodes[-1]] if (nodes and not ver.rejected) else None

@@ -149,3 +149,40 @@ def test_int8_prompt_through_step_kernel_matches_batched(monkeypatch):
     want, _ = OracleQwen2(cfg, w, kv_fp16=True).forward(prompt, None, all_logits=True)
     assert_logits_close(batched, want)
     assert_logits_close(stepped, want)
+
+
+@pytest.mark.slow
+def test_int8_7b_shape_long_context_decode():
+    """cfg5's long context on the 7B int8 shape (hidden 3584, 28 q / 4 kv heads, untied int8 LM
+    head), truncated to one layer so the CPU oracle finishes: a 4,100-token prompt, then 8 greedy
+    step-kernel tokens at contexts 4,100-4,107 with the attention items the kernel picks itself
+    (no chunk cap: 28 heads x 5 chunks of ~820 positions, many sub-chunks per item). Tokens equal
+    the oracle's; the last step's logits within the int8 tolerance."""
+    from dataclasses import replace
+    from seedplane_b200.config import QWEN2_5_7B
+    from seedplane_b200.engine import CudaQwen2
+    cfg = replace(QWEN2_5_7B, layers=1, max_positions=8192, name="qwen2.5-7b-1l")
+    w = make_int8_blockwise(cfg, seed=0, std=0.02)
+    prompt = random_prompt(cfg.vocab, 4100, seed=0)
+    eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
+    kv = eng.new_kv(4160)
+    _, argmax = eng.forward(kv, prompt, want_logits=False)
+    first = int(argmax[-1])
+    toks, logits = eng.decode(kv, first, len(prompt), 8, want_logits=True)
+    got = [first] + toks.cpu().tolist()
+    eng.status()
+    eng.close()
+    o = OracleQwen2(cfg, w, kv_fp16=True)
+    del w
+    cache = o.new_cache(4160)
+    lg, cache = o.forward(prompt, cache)
+    want, margins = [int(lg[-1].argmax())], []
+    for i in range(8):
+        top = torch.topk(lg[-1], 2).values
+        margins.append(float(top[0] - top[1]))
+        lg, cache = o.forward([want[-1]], cache)
+        if i < 7:
+            want.append(int(lg[-1].argmax()))
+    # the engine's last step produced the logits after token got[7] (= want[7] when all match)
+    assert got[:8] == want[:8], (got, want, margins)
+    assert_logits_close(logits, lg[-1])

@@ -54,3 +54,20 @@ def test_qwen2_1_5b_greedy_512_plus_256():
     want, margins = OracleQwen2(QWEN2_1_5B, w, kv_fp16=True).greedy(prompt, 256)
     d = _first_divergence(got, want)
     assert d is None, f"first divergence at {d}: margin there {margins[d]:.5f}, min margin {min(margins):.5f}"
+
+
+@pytest.mark.parametrize("gemv", ["tc", "hmma"])
+def test_chain_path_greedy_tokens(golden_dir, monkeypatch, gemv):
+    """The kernel-per-op decode chain (SEEDPLANE_STEP=chain: one GEMV launch per projection, the
+    standalone decode attention kernel; SEEDPLANE_GEMV=hmma: its mma.sync GEMV instead of the
+    tcgen05 one) gives the oracle's tokens on the Qwen2-0.5B shape, like the persistent step kernel."""
+    from seedplane_b200.engine import CudaQwen2
+    gold = json.loads((golden_dir / "qwen2-0.5b.json").read_text())
+    w = make_weights(QWEN2_0_5B, seed=0, dtype=torch.float16)
+    monkeypatch.setenv("SEEDPLANE_STEP", "chain")
+    if gemv == "hmma":
+        monkeypatch.setenv("SEEDPLANE_GEMV", "hmma")
+    eng = CudaQwen2(QWEN2_0_5B, w)        # the switches are read when the engine is created
+    got = _engine_greedy(eng, gold["prompt"], 32, 96)
+    eng.close()
+    assert got == gold["fp16_weights"]["tokens"], _first_divergence(got, gold["fp16_weights"]["tokens"])

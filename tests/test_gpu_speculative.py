@@ -100,3 +100,44 @@ def test_stochastic_accept_matches_oracle(pair, V):
             assert list(ver.emitted) == want_tokens and list(nodes) == want_nodes
             cases += 1
     assert cases == 16
+
+
+def test_accept_greedy_device_matches_host_rule(pair):
+    """sp_accept_greedy (the decision on the device from device-resident argmaxes) equals the host
+    selection and the oracle's restatement of verify_greedy (speculative.py:55-92) on random
+    forests: shared prefixes, duplicate branches, branches that are prefixes of others, ties."""
+    import random
+    from oracle import speculative_oracle as so
+    from seedplane_b200.speculative import SpeculativeForest, accept_greedy, accept_greedy_device
+    cfg, w, target, drafter = pair
+    rng = random.Random(7)
+    for case in range(300):
+        vocab = rng.choice((3, 5, 50))
+        branches = []
+        for _ in range(rng.randint(0, 8)):
+            b = [rng.randrange(vocab) for _ in range(rng.randint(0, 5))]
+            if branches and rng.random() < 0.3:
+                b = list(rng.choice(branches))[:rng.randint(0, 5)]      # a duplicate or a prefix
+            branches.append(b)
+        forest = SpeculativeForest.build(branches)
+        flat = forest.flatten()
+        if len(flat.tokens) > 64:
+            continue
+        root = rng.randrange(vocab)
+        # predictions that often agree with a child so that paths get accepted
+        pred = []
+        for i in range(len(flat.tokens)):
+            kids = [j for j, p in enumerate(flat.parents) if p == i]
+            pred.append(flat.tokens[rng.choice(kids)] if kids and rng.random() < 0.7 else rng.randrange(vocab))
+        if flat.tokens and rng.random() < 0.7:
+            root = rng.choice([flat.tokens[j] for j, p in enumerate(flat.parents) if p < 0])
+        dev = torch.tensor(pred if pred else [0], dtype=torch.int32, device="cuda:0")
+        ver_d, nodes_d, nxt = accept_greedy_device(target, flat, root, dev)
+        ver_h, nodes_h = accept_greedy(flat, root, pred)
+        assert (ver_d, nodes_d) == (ver_h, nodes_h), case
+        want_next = pred[nodes_h[-1]] if nodes_h and not ver_h.rejected else None
+        assert nxt == want_next, case
+        want = so.accept_from_predictions(list(flat.paths), [list(p) for p in flat.node_paths], list(flat.tokens),
+                                          root, pred)
+        assert (tuple(ver_h.emitted), ver_h.accepted_draft_tokens, ver_h.rejected, ver_h.target_steps,
+                tuple(ver_h.branch)) == tuple(want), case
