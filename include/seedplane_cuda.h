@@ -124,6 +124,14 @@ int sp_verify_tree(sp_engine *e, sp_kv *kv, const int32_t *tokens_host, const in
  * rollback by truncation (benchmark_speculative.py:119,127) for tree-shaped drafts. */
 int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stream);
 
+/* Copy the K/V of n consecutive slots, every layer and kv head, from src slots [src_slot0,
+ * src_slot0 + n) to dst slots [dst_slot0, dst_slot0 + n). The caches belong to one engine; they may
+ * differ in capacity, or be the same cache with disjoint ranges. Lengths are not changed. Replaces
+ * the native session's Engine::copy_slots (native/vulkan_decode/qwen_vk.cpp:440-453): a shard
+ * window is seeded with the sink tokens' K/V and, in the approximate reuse mode, the halo's
+ * (qwen_vk.cpp:512-542). */
+int sp_kv_copy(sp_kv *src, int32_t src_slot0, sp_kv *dst, int32_t dst_slot0, int32_t n, void *stream);
+
 /* Greedy argmax of each row of fp32 logits [rows][ld] (device) over the first `cols` columns:
  * argmax_dev[rows] int32, lowest index on ties (NaN is never selected). For logits produced
  * outside the fused LM head, e.g. all-logits verification. Replaces `Qwen2Engine.sample`

@@ -18,7 +18,7 @@ from __future__ import annotations
 import hashlib
 import json
 from pathlib import Path
-from typing import Dict, Tuple
+from typing import Dict, Optional, Tuple
 
 import numpy as np
 import torch
@@ -78,11 +78,17 @@ def load_bundle_v2(path, verify_sha256: bool = False) -> Tuple[Qwen2Config, Dict
     return cfg, out, "f16"
 
 
-def plan_of(path) -> dict:
-    """The shard plan of a bundle (`seedplane.json` `plan`), or the reference default."""
+def bundle_plan(path) -> Optional[dict]:
+    """The shard plan a SeedPlane bundle carries (`seedplane.json` `plan`), or None."""
     p = Path(path)
     if (p / "seedplane.json").exists():
         meta = json.loads((p / "seedplane.json").read_text())
         if "plan" in meta:
             return dict(meta["plan"])
-    return {"shard": 512, "halo": 256, "sinks": 4}
+    return None
+
+
+def plan_of(path) -> dict:
+    """The shard plan of a bundle (`seedplane.json` `plan`), or the reference default."""
+    plan = bundle_plan(path)
+    return plan if plan is not None else {"shard": 512, "halo": 256, "sinks": 4}

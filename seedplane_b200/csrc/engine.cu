@@ -1350,6 +1350,30 @@ int sp_kv_commit(sp_kv *kv, const int32_t *src_slots_host, int32_t n, void *stre
     return SP_OK;
 }
 
+int sp_kv_copy(sp_kv *src, int32_t src_slot0, sp_kv *dst, int32_t dst_slot0, int32_t n, void *stream) {
+    if (!src || !dst || !src->e || !dst->e) return fail(SP_ERR_INVALID, "null or orphaned cache");
+    if (src->e != dst->e) return fail(SP_ERR_INVALID, "caches of different engines");
+    if (n < 0 || src_slot0 < 0 || dst_slot0 < 0) return fail(SP_ERR_INVALID, "negative slot or count");
+    if (n == 0) return SP_OK;
+    if ((int64_t)src_slot0 + n > src->capacity || (int64_t)dst_slot0 + n > dst->capacity)
+        return fail(SP_ERR_CAPACITY, "slots [%d, %d) -> [%d, %d) outside the capacities %d / %d", src_slot0, src_slot0 + n,
+                    dst_slot0, dst_slot0 + n, src->capacity, dst->capacity);
+    if (src == dst && src_slot0 < dst_slot0 + n && dst_slot0 < src_slot0 + n)
+        return fail(SP_ERR_INVALID, "overlapping slot ranges in one cache");
+    sp_engine *e = src->e;
+    SP_CUDA(cudaSetDevice(e->device));
+    // layout [layer][kv head][capacity][head_dim]: one row of n slots per (layer, kv head)
+    const size_t row = (size_t)e->c.head_dim * sizeof(__half);
+    const size_t rows = (size_t)e->c.layers * e->c.kv_heads;
+    for (int which = 0; which < 2; ++which) {
+        const __half *s = (which ? src->v : src->k) + (size_t)src_slot0 * e->c.head_dim;
+        __half *d = (which ? dst->v : dst->k) + (size_t)dst_slot0 * e->c.head_dim;
+        SP_CUDA(cudaMemcpy2DAsync(d, row * dst->capacity, s, row * src->capacity, row * n, rows, cudaMemcpyDeviceToDevice,
+                                  (cudaStream_t)stream));
+    }
+    return SP_OK;
+}
+
 int sp_argmax(sp_engine *e, const float *logits_dev, int32_t rows, int32_t cols, int64_t ld, int32_t *argmax_dev,
               void *stream) {
     if (!e) return fail(SP_ERR_INVALID, "null engine");

@@ -242,6 +242,12 @@ class CudaQwen2:
         N.check(N.load().sp_kv_commit(kv.handle, N.int_array(src_slots), len(src_slots),
                                       C.c_void_p(_stream(self.device))))
 
+    def kv_copy(self, src: DeviceKV, src_slot0: int, dst: DeviceKV, dst_slot0: int, n: int):
+        """K/V of slots [src_slot0, src_slot0 + n) of `src` into [dst_slot0, ...) of `dst` (every
+        layer; lengths unchanged): `sp_kv_copy`."""
+        N.check(N.load().sp_kv_copy(src.handle, int(src_slot0), dst.handle, int(dst_slot0), int(n),
+                                    C.c_void_p(_stream(self.device))))
+
     def topk(self, logits: torch.Tensor, k: int):
         """Per-row top-k of fp32 logits on the device: (indices int32 [rows, k], values [rows, k],
         log-sum-exp [rows]); larger value first, lower index on ties."""

@@ -20,7 +20,11 @@ types: a failed request raises `RuntimeError(message)`, a missing engine `FileNo
   and a chat turn's `<|im_end|>` becomes history); text still held by the incremental decoder at
   the end is flushed as one more emission with token -1, and the reference's client appends that
   -1 to `last_tokens`, as this class does.
-* Only full attention (`mode` None / "full") is built; shard windows raise `RuntimeError`.
+* Attention follows the reference's modes (`qwen_vk.cpp:235,257,285-301`): `full=True` or
+  `mode="full"` is one window over all positions (default `ctx` 8192); otherwise the bundle's shard
+  plan (`seedplane.json`, overridable by `--shard/--halo/--sinks` in `extra_args`) with `mode` one
+  of rebuild, rebuild-batch, shadow, shadow-batch (the default) or reuse, and `ctx` positions
+  (default: the checkpoint's maximum) over windows of S + H + sinks slots (`windows.py`).
 * Sampling: temperature > 0 draws each token on the device from softmax(logits / temperature) with
   a counter-based RNG (`seed`, then one counter step per token), so a seed reproduces a run; the
   distribution is the reference's, the random stream is not its mt19937_64 (`sampler.hpp`).
@@ -41,6 +45,7 @@ from typing import Iterable, List, Optional
 import torch
 
 from . import _native as N
+from .windows import DEFAULT_MODE, MODES, ShardPlan, WindowSession
 
 QWEN_STOP_TOKENS = ("<|im_end|>", "<|endoftext|>")
 DEFAULT_SYSTEM = "You are a helpful assistant."      # qwen_vk.cpp:664
@@ -98,6 +103,7 @@ class NativeEngine:
         if Path(lib_path).resolve() != N.LIB_PATH.resolve() and N._lib is None:
             N.load(Path(lib_path))
         device = "cuda"
+        overrides = {}
         args = list(extra_args)
         while args:
             flag = args.pop(0)
@@ -105,22 +111,36 @@ class NativeEngine:
                 device = args.pop(0)
             elif flag == "--shaders" and args:
                 args.pop(0)                      # the Vulkan build's shader directory: nothing to load here
+            elif flag in ("--shard", "--halo", "--sinks") and args:
+                try:
+                    overrides[flag[2:]] = int(args.pop(0))
+                except ValueError as exc:
+                    raise RuntimeError(f"engine failed to start: {flag} needs an integer") from exc
             else:
                 raise RuntimeError(f"engine failed to start: unknown argument {flag!r}")
-        if mode not in (None, "full") and not full:
-            raise RuntimeError(f"engine failed to start: attention mode {mode!r} is not built (full attention only)")
-        from .bundle import load_checkpoint, plan_of
+        from .bundle import bundle_plan, load_checkpoint, plan_of
+        # a SeedPlane bundle decodes under its plan (shadow-batch unless told otherwise, as the
+        # reference engine); a plain checkpoint without a plan defaults to full attention
+        mode = "full" if full else (mode or (DEFAULT_MODE if bundle_plan(bundle) is not None else "full"))
+        if mode not in MODES:
+            raise RuntimeError(f"engine failed to start: bad --mode {mode!r}")
         from .engine import CudaQwen2
         self.bundle = Path(bundle)
         try:
             cfg, weights, fmt = load_checkpoint(self.bundle)
-        except (OSError, ValueError, KeyError) as exc:
+            plan = ShardPlan(**{**plan_of(self.bundle), **overrides})
+        except (OSError, ValueError, KeyError, TypeError) as exc:
             raise RuntimeError(f"engine failed to start: {exc}") from exc
         self.cfg = cfg
+        # positions: qwen_vk.cpp:785 (full attention defaults to 8192, windows to the model's maximum)
+        self.capacity = int(min(ctx or (8192 if mode == "full" else cfg.max_positions), cfg.max_positions))
         self._engine = CudaQwen2(cfg, weights, device=device, weight_format=fmt)
         del weights
-        self.capacity = int(min(ctx or 4096, cfg.max_positions))
-        self._kv = self._engine.new_kv(self.capacity)
+        try:
+            self._session = WindowSession(self._engine, mode, plan, self.capacity)
+        except ValueError as exc:
+            self._engine.close()
+            raise RuntimeError(f"engine failed to start: {exc}") from exc
         self._tok = self._load_tokenizer(self.bundle)
         self._stop_ids = set()
         if self._tok is not None:
@@ -131,13 +151,10 @@ class NativeEngine:
         self.defaults = {"temperature": temperature, "top_k": top_k, "top_p": top_p, "seed": seed,
                          "max_new_tokens": max_new_tokens if max_new_tokens is not None else 256}
         self.system = DEFAULT_SYSTEM if system is None else system
-        # the session's token sequence; the cache holds the K/V of its first `_kv.length` tokens
-        # (after a run, every token but the last sampled one)
-        self._history: List[int] = []
         dev = self._engine.device
+        ses = self._session
         self.info = {"ready": True, "device": torch.cuda.get_device_name(dev), "engine": "seedplane-b200",
-                     "mode": "full", "plan": plan_of(self.bundle), "positions": self.capacity,
-                     "window_slots": self.capacity, "weights": fmt}
+                     "mode": ses.mode, "plan": ses.plan, "positions": ses.P, "window_slots": ses.W, "weights": fmt}
         self.last = None
         self.last_tokens: List[int] = []
         self.on_token = None                    # callable(token, text piece or "") per emitted token
@@ -170,15 +187,20 @@ class NativeEngine:
         self._need_tokenizer()
         return self._tok.decode(list(ids), skip_special_tokens=skip_special)
 
+    @property
+    def _history(self) -> List[int]:
+        """The session's token sequence; the first `_session.done` of them are processed (after a
+        run, every token but the last sampled one)."""
+        return self._session.seq
+
     def state(self):
         """The serve loop's `state` answer (`qwen_vk.cpp:828-831`): position = tokens in the
-        session, processed = tokens whose K/V the cache holds, and the token ids."""
-        return {"position": len(self._history), "processed": self._kv.length, "tokens": list(self._history),
-                "capacity": self.capacity, "mode": "full"}
+        session, processed = tokens whose K/V the windows hold, and the token ids."""
+        return {"position": len(self._history), "processed": self._session.done, "tokens": list(self._history),
+                "capacity": self.capacity, "mode": self._session.mode}
 
     def reset(self):
-        self._kv.length = 0
-        self._history = []
+        self._session.reset()
 
     def generate(self, text=None, ids=None, reset=True, **sampling):
         """Raw continuation of `text` or of token `ids`; yields text pieces."""
@@ -232,9 +254,7 @@ class NativeEngine:
         """Append `ids` to the session and process every pending token (the previous run's last
         sampled token, then `ids`); returns (logits of the last or None, its argmax)."""
         self._history.extend(int(t) for t in ids)
-        pending = self._history[self._kv.length:]
-        logits, am = self._engine.forward(self._kv, torch.tensor(pending, dtype=torch.int32), want_logits=want_logits)
-        return logits, int(am[-1])
+        return self._session.catch_up(want_logits)
 
     def _emit(self, t: int, piece: str):
         self.last_tokens.append(int(t))
@@ -277,11 +297,12 @@ class NativeEngine:
         _sync(dev)
         prefill_s = time.perf_counter() - t0
         t1 = time.perf_counter()
+        ses = self._session
         queue = [first]                         # sampled tokens not emitted yet (the first is unprocessed)
-        fed_at = None                           # cache slot of the token fed to the last decode block
+        in_block = False                        # queue came from a device decode block
         generated, reason = 0, "length"
         while True:
-            done = False
+            done, kept = False, len(queue)
             for i, t in enumerate(queue):
                 self._history.append(t)
                 generated += 1
@@ -295,20 +316,19 @@ class NativeEngine:
                 elif generated >= max_new:
                     reason, done = "length", True
                 if done:
-                    # the block's cache holds the fed token and queue[:-1]; keep it up to queue[i - 1]
-                    if fed_at is not None:
-                        self._kv.length = fed_at + 1 + i
+                    kept = i + 1
                     break
+            if in_block:
+                # the block processed the fed token and queue[:-1]; keep them up to queue[kept - 2]
+                ses.commit_block(kept)
             if done:
                 break
-            room = self.capacity - self._kv.length
+            room = ses.P - ses.done
             if room < 1:
                 reason = "context"
                 break
-            n = min(_DECODE_BLOCK, max_new - generated, room)
-            fed_at = self._kv.length
-            out, _ = self._engine.decode(self._kv, self._history[-1], fed_at, n)
-            queue = out.tolist()
+            out, _ = ses.decode_block(min(_DECODE_BLOCK, max_new - generated, room))
+            queue, in_block = out.tolist(), True
         decode_s = time.perf_counter() - t1
         rest = self._finish(reason, generated, len(prompt), prefill_s, decode_s, stream)
         if rest:
@@ -341,10 +361,11 @@ class NativeEngine:
                 break
             if generated >= max_new:
                 break
-            if self.capacity - self._kv.length < 1:
+            if self._session.P - self._session.done < 1:
                 reason = "context"
                 break
-            _, lg = self._engine.decode(self._kv, tok, self._kv.length, 1, want_logits=True)
+            _, lg = self._session.decode_block(1, want_logits=True)
+            self._session.commit_block(1)
             counter += 1
             tok = sample_token(self._engine, lg, temp, seed, counter, top_k, top_p)
         _sync(dev)
@@ -355,9 +376,9 @@ class NativeEngine:
 
     # ---- lifetime ----------------------------------------------------------------------------
     def close(self):
-        if getattr(self, "_kv", None) is not None:
-            self._kv.close()
-            self._kv = None
+        if getattr(self, "_session", None) is not None:
+            self._session.close()
+            self._session = None
         if getattr(self, "_engine", None) is not None:
             self._engine.close()
             self._engine = None

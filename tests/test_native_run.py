@@ -20,11 +20,18 @@ class FakeKV:
     def __init__(self, capacity):
         self.capacity, self.length, self.cache = capacity, 0, []
 
+    def close(self):
+        pass
+
 
 class FakeEngine:
     device = torch.device("cpu")
+    cfg = type("C", (), {"vocab": V, "max_positions": 4096})()
 
-    def forward(self, kv, ids, want_logits=False):
+    def new_kv(self, capacity):
+        return FakeKV(capacity)
+
+    def forward(self, kv, ids, positions=None, want_logits=False):
         ids = [int(t) for t in ids]
         del kv.cache[kv.length:]
         out = []
@@ -34,7 +41,7 @@ class FakeEngine:
         kv.length = len(kv.cache)
         return None, torch.tensor(out)
 
-    def decode(self, kv, token, pos, n):
+    def decode(self, kv, token, pos, n, want_logits=False):
         assert pos == kv.length
         out = []
         for _ in range(n):
@@ -72,15 +79,16 @@ class FakeTok:
         return e
 
 
-def bare(tok=None, capacity=64):
+def bare(tok=None, capacity=64, engine=None):
     eng = nat.NativeEngine.__new__(nat.NativeEngine)
     eng.cfg = type("C", (), {"vocab": V})()
-    eng._engine, eng._kv, eng._tok = FakeEngine(), FakeKV(capacity), tok
+    eng._engine, eng._tok = engine or FakeEngine(), tok
+    eng._session = nat.WindowSession(eng._engine, "full", None, capacity)
     eng.capacity = capacity
     eng._stop_ids = {95, 96} if tok is not None else set()
     eng.defaults = {"temperature": None, "top_k": None, "top_p": None, "seed": None, "max_new_tokens": 256}
     eng.system = nat.DEFAULT_SYSTEM
-    eng._history, eng.last, eng.last_tokens, eng.on_token, eng.bundle = [], None, [], None, "fake"
+    eng.last, eng.last_tokens, eng.on_token, eng.bundle = None, [], None, "fake"
     return eng
 
 
@@ -127,14 +135,13 @@ def test_stop_token_is_emitted_counted_and_processed_by_the_next_request():
 def test_decoder_flush_is_a_token_minus_one_emission():
     s = nat._TextStream(FakeTok())
     assert s.push(90) == "" and s.push(91) == "é" and s.flush() == ""
-    eng = bare(FakeTok())
 
     class OpenChars(FakeEngine):        # every greedy token opens a character that never closes
-        def forward(self, kv, ids, want_logits=False):
-            _, am = super().forward(kv, ids, want_logits)
+        def forward(self, kv, ids, positions=None, want_logits=False):
+            _, am = super().forward(kv, ids, positions, want_logits)
             return None, torch.full_like(am, 90)
 
-    eng._engine = OpenChars()
+    eng = bare(FakeTok(), engine=OpenChars())
     seen = []
     eng.on_token = lambda t, piece: seen.append((t, piece))
     pieces = list(eng.generate(ids=[1, 2, 3], max_new_tokens=4))
