@@ -12,7 +12,9 @@ collective on the data path) and `value` = all ranks' tokens / the slowest rank'
 
 The decode line also carries: `e2e` through the drop-in surface (`NativeEngine.generate(ids=...)`
 on a checkpoint written to disk: host prompt in, generated tokens out, blocks of device decode);
-`burst` (every N: the 16 x 32 HIVE burst on the same engines, tok/s over the wall-clock makespan);
+`burst` (every N: the 16 x 32 HIVE burst on the same engines, tok/s over the wall-clock makespan,
+one request per lease, and `burst.batched`: the same burst with each GPU's share decoded as one
+batch, runtime request batching);
 and at N = 1 `verify` (cfg2: one 16-node tree-verify pass on the Qwen2-0.5B shape), `reference_gpu`
 (the reference's own `Qwen2Engine(device='cuda')`, fp16, from `baseline/_ref`, decoding the same
 256 tokens after the same prompt on the same GPU) and `cpu_baseline` (the oracle port on the host).
@@ -449,6 +451,14 @@ def run_decode(args, world, rank, local):
     if not i8 and not args.no_burst:
         from seedplane_b200.hive.burst import burst_on_engine
         burst = burst_on_engine(eng, 2, 3, world, rank, local, ClockSampler, max_over_ranks, barrier)
+        # the same burst with runtime request batching: each GPU's share decoded as one batch
+        batched = burst_on_engine(eng, 3, 3, world, rank, local, ClockSampler, max_over_ranks, barrier, batched=True)
+        if burst is not None:
+            # requests whose tokens equal the one-request-per-lease run (a request may part from it at
+            # a near-tie of the oracle's logits: the two paths sum in different orders)
+            batched["requests_equal_one_per_lease"] = sum(
+                x == y for x, y in zip(batched["request_sha256"], burst["request_sha256"]))
+            burst["batched"] = batched
 
     line = None
     if rank == 0:

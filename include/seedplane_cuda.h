@@ -110,6 +110,18 @@ int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t
 int sp_decode(sp_engine *e, sp_kv *kv, int32_t token, int32_t pos, int32_t n_steps,
               int32_t *out_tokens_dev, float *logits_dev, void *stream);
 
+/* Greedy decode of B independent requests in one batched pass per step (runtime request batching;
+ * the reference has none: README.md:67-68, its HIVE agents report batch_size 1, hive/pool.py:465-466).
+ * Request b feeds tokens_host[b] at RoPE position positions_host[b] into its own cache kvs[b] (slot =
+ * that cache's length, attention over that cache alone), then each step's argmax is fed back on the
+ * device for n_steps steps; the weights are streamed once per step for all B requests.
+ * out_tokens_dev[n_steps][B] receives every step's argmaxes (row i = the tokens after step i).
+ * 1 <= B <= 64, distinct caches of this engine, each with room for n_steps more slots. Advances every
+ * cache's length by n_steps. Replaces, for a batch, B calls of sp_decode (the reference's per-request
+ * Session::step loop, qwen_vk.cpp:519-565,588-613). */
+int sp_decode_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *tokens_host,
+                    const int32_t *positions_host, int32_t n_steps, int32_t *out_tokens_dev, void *stream);
+
 /* Speculative tree verification (no counterpart kernel in the reference; semantics of
  * seedplane/speculative.py:55-92). n nodes in an ancestor-closed order (parent index < own index;
  * -1 = child of the committed prefix). Node i is written to scratch slot len+i at RoPE position

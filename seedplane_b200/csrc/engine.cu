@@ -55,6 +55,17 @@ struct VerifyIn {
     uint64_t mask[kSmallNodes];             // ancestor-or-self bits of node i
 };
 
+// Inputs of a batched decode step (sp_decode_batch) that its captured graph reads from fixed device
+// memory; the step's last kernel advances them (each request's argmax becomes its next token).
+constexpr int kBatchMax = 64;
+struct BatchIn {
+    BatchLane lanes[kBatchMax];
+    int32_t tok[kBatchMax];
+    int32_t pos[kBatchMax];
+    int32_t argmax[kBatchMax];
+    int32_t out[kBatchMax];
+};
+
 struct LayerDev {
     const uint8_t *qkv, *o, *gate_up, *down;       // fragment-packed fp16, contiguous in the stream
     const float *qkv_b, *in_norm, *post_norm;
@@ -150,6 +161,8 @@ struct sp_engine {
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
     int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
+    BatchIn *bt = nullptr;                  // batched decode inputs
+    std::map<int, cudaGraphExec_t> bgraphs; // batched decode step per batch size
     int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
@@ -1078,6 +1091,8 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->vt);
     cudaFree(e->acc_scratch);
     cudaFree(e->gr_buf);
+    for (auto &g : e->bgraphs) cudaGraphExecDestroy(g.second);
+    cudaFree(e->bt);
     delete e;
 }
 
@@ -1272,6 +1287,95 @@ int sp_decode(sp_engine *e, sp_kv *kv, int32_t token, int32_t pos, int32_t n_ste
     rc = run_steps(e, kv, d, n_steps, (cudaStream_t)stream);
     if (rc) return rc;
     kv->length += n_steps;
+    return SP_OK;
+}
+
+// One greedy step of a batch of independent requests (e->bt): the batched pass over B tokens, each
+// writing and attending to its own cache, every row's LM head and argmax, then the advance.
+static int batch_step(sp_engine *e, int B, cudaStream_t s) {
+    const sp_config &c = e->c;
+    const float scale = 1.0f / sqrtf((float)c.head_dim);
+    SP_CUDA(launch_prefill_embed(e->pf_dims, e->pf, e->embed, e->bt->tok, B, e->st, s));
+    for (int l = 0; l < c.layers; ++l) {
+        const PrefillLayer &L = e->layers[l].pf;
+        SP_CUDA(launch_batch_layer_front(e->pf_dims, L, e->pf, B, e->bt->pos, e->bt->lanes, l, scale, e->rope, e->st, s));
+        SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, B, e->st, s));
+    }
+    SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_pf, 0, B, e->pf.logits, e->st, s));
+    SP_CUDA(launch_argmax_rows(e->pf.logits, B, c.vocab, c.vocab, e->bt->argmax, e->am, s));
+    SP_CUDA(launch_batch_advance(e->bt->lanes, e->bt->tok, e->bt->pos, e->bt->argmax, e->bt->out, B, c.max_positions,
+                                 e->st, s));
+    return SP_OK;
+}
+
+static int batch_graph(sp_engine *e, int B, cudaGraphExec_t *out) {
+    auto it = e->bgraphs.find(B);
+    if (it != e->bgraphs.end()) {
+        *out = it->second;
+        return SP_OK;
+    }
+    cudaGraph_t g = nullptr;
+    SP_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = batch_step(e, B, e->cap_stream);
+    cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
+    if (rc != SP_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "batch graph capture: %s", cudaGetErrorString(ce));
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "batch graph instantiate: %s", cudaGetErrorString(ce));
+    e->bgraphs[B] = ex;
+    *out = ex;
+    return SP_OK;
+}
+
+int sp_decode_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *tokens_host,
+                    const int32_t *positions_host, int32_t n_steps, int32_t *out_tokens_dev, void *stream) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    if (!kvs || !tokens_host || !positions_host || !out_tokens_dev) return fail(SP_ERR_INVALID, "null argument");
+    if (B <= 0 || B > kBatchMax) return fail(SP_ERR_CAPACITY, "batch of %d requests (1..%d)", B, kBatchMax);
+    if (n_steps <= 0) return fail(SP_ERR_INVALID, "n_steps must be positive");
+    if (!e->prefill) return fail(SP_ERR_UNSUPPORTED, "batched decode needs the batched pass (SEEDPLANE_PREFILL=steps)");
+    BatchIn in;
+    memset(&in, 0, sizeof(in));
+    for (int b = 0; b < B; ++b) {
+        sp_kv *kv = kvs[b];
+        if (!kv || kv->e != e) return fail(SP_ERR_INVALID, "request %d: null cache or a cache of another engine", b);
+        for (int j = 0; j < b; ++j)
+            if (kvs[j] == kv) return fail(SP_ERR_INVALID, "request %d: cache shared with request %d", b, j);
+        if (kv->length + n_steps > kv->capacity)
+            return fail(SP_ERR_CAPACITY, "request %d: KV cache capacity %d exceeded", b, kv->capacity);
+        if (tokens_host[b] < 0 || tokens_host[b] >= e->c.vocab)
+            return fail(SP_ERR_INVALID, "request %d: token %d outside the vocabulary", b, tokens_host[b]);
+        if (positions_host[b] < 0 || positions_host[b] + n_steps > e->c.max_positions)
+            return fail(SP_ERR_CAPACITY, "request %d: positions outside the RoPE table", b);
+        in.lanes[b] = BatchLane{kv->k, kv->v, kv->capacity, kv->length};
+        in.tok[b] = tokens_host[b];
+        in.pos[b] = positions_host[b];
+    }
+    SP_CUDA(cudaSetDevice(e->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (!e->bt) SP_CUDA(cudaMalloc(&e->bt, sizeof(BatchIn)));
+    SP_CUDA(cudaMemcpyAsync(e->bt, &in, sizeof(in), cudaMemcpyHostToDevice, s));
+    cudaGraphExec_t ex = nullptr;
+    if (e->use_graph) {
+        int rc = batch_graph(e, B, &ex);
+        if (rc) return rc;
+    }
+    for (int i = 0; i < n_steps; ++i) {
+        if (ex) {
+            SP_CUDA(cudaGraphLaunch(ex, s));
+        } else {
+            int rc = batch_step(e, B, s);
+            if (rc) return rc;
+        }
+        SP_CUDA(cudaMemcpyAsync(out_tokens_dev + (size_t)i * B, e->bt->out, (size_t)B * sizeof(int32_t),
+                                cudaMemcpyDeviceToDevice, s));
+    }
+    for (int b = 0; b < B; ++b) kvs[b]->length += n_steps;
     return SP_OK;
 }
 

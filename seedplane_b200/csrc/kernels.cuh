@@ -283,6 +283,14 @@ constexpr int kPrefillMaxTokens = 512;   // tokens per chunk (scratch size; a mu
 constexpr int kPrefillLogitRows = 64;    // logits rows per head GEMM (argmax scratch rows)
 constexpr int kPrefillMaxCtas = 148;     // GEMM CTAs at most (one per SM; workspace slots)
 
+// One request of a batched decode step (sp_decode_batch): its own cache (layer-0 K / V bases and
+// capacity, layout [layer][kv head][cap][head_dim]) and the slot its token's K / V go to (= the
+// cache length before the step). The token attends to slots [0, slot] of that cache.
+struct BatchLane {
+    __half *k, *v;
+    int cap;
+    int slot;
+};
 struct PrefillDims {
     int hidden, inter, heads, kv_heads, head_dim, vocab, max_pos, max_tokens;
     float eps;
@@ -326,6 +334,15 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
                                        const int32_t *pos, const uint64_t *mask, __half *kc, __half *vc, int cap,
                                        const int *slot_base, int slot_off, float scale, const float *rope,
                                        DevState *st, cudaStream_t stream);
+// The same front for a batched decode step: token t belongs to request lanes[t] (its cache, slot;
+// positions pos[t]) and attends to that cache alone (k_attn_batch)
+cudaError_t launch_batch_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int B,
+                                     const int32_t *pos, const BatchLane *lanes, int layer, float scale,
+                                     const float *rope, DevState *st, cudaStream_t stream);
+// after a batched decode step: each request's argmax becomes its next token (pos + 1, slot + 1) and
+// is stored at out[b]
+cudaError_t launch_batch_advance(BatchLane *lanes, int32_t *tok, int32_t *pos, const int32_t *argmax, int32_t *out,
+                                 int B, int max_pos, DevState *st, cudaStream_t stream);
 // RMSNorm, gate_up GEMM with SwiGLU, down GEMM (+= x)
 cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,
                                      DevState *st, cudaStream_t stream);
@@ -349,6 +366,8 @@ struct McolQkv {
     int slot_off, cap, nh, nkv, hd, max_pos;
     float *q;
     __half *kc, *vc;
+    const BatchLane *lanes;      // batched decode: token t writes its K / V into lanes[t]'s cache (layer
+    int layer;                   // `layer`), kc / vc / cap / slot_base unused
 };
 struct McolOp {
     int mode;                    // MC_STORE: y[t ldy + n] = ..; MC_RESID: += ..; MC_SWIGLU: see act_*

@@ -128,6 +128,7 @@ SP_DEVINL bool wait_phase(uint64_t *bar, uint32_t parity, const Flag &f) {
 // The cache slot of token 0 of the block (device-side base + offset), checked against the cache.
 SP_DEVINL int qkv_slot0(const McolParams &p) {
     const McolQkv &a = p.qkv;
+    if (a.lanes) return 0;               // batched decode: every token's slot comes from its lane
     int s0 = *a.slot_base + a.slot_off;
     if (s0 < 0 || s0 + p.T > a.cap) {
         if (p.st && threadIdx.x == 0) atomicCAS(&p.st->err, 0, kErrBadSlot);
@@ -168,7 +169,18 @@ SP_DEVINL void epilogue_one(const McolParams &p, float v, int n, int t, int lane
         const int half_hd = a.hd / 2;
         const int P2 = n >> 1, hh = P2 / half_hd, dd = P2 - hh * half_hd;
         const float a0 = y + __ldg(a.bias + hh * a.hd + dd), a1 = other + __ldg(a.bias + hh * a.hd + dd + half_hd);
-        const int slot = slot0 + t;
+        const int slot = a.lanes ? a.lanes[t].slot : slot0 + t;
+        __half *kbase = a.kc, *vbase = a.vc;
+        int cap = a.cap;
+        if (a.lanes) {                    // batched decode: the token's own cache, this layer
+            cap = a.lanes[t].cap;
+            kbase = a.lanes[t].k + (size_t)a.layer * a.nkv * cap * a.hd;
+            vbase = a.lanes[t].v + (size_t)a.layer * a.nkv * cap * a.hd;
+            if (slot < 0 || slot >= cap) {
+                if (p.st) atomicCAS(&p.st->err, 0, kErrBadSlot);
+                return;
+            }
+        }
         if (hh < a.nh + a.nkv) {
             int pos = a.pos ? a.pos[t] : slot;
             if (pos < 0 || pos >= a.max_pos) {
@@ -183,12 +195,12 @@ SP_DEVINL void epilogue_one(const McolParams &p, float v, int n, int t, int lane
                 qr[dd] = o0;
                 qr[dd + half_hd] = o1;
             } else {
-                __half *kr = a.kc + ((size_t)(hh - a.nh) * a.cap + slot) * a.hd;
+                __half *kr = kbase + ((size_t)(hh - a.nh) * cap + slot) * a.hd;
                 kr[dd] = __float2half_rn(o0);
                 kr[dd + half_hd] = __float2half_rn(o1);
             }
         } else {
-            __half *vr = a.vc + ((size_t)(hh - a.nh - a.nkv) * a.cap + slot) * a.hd;
+            __half *vr = vbase + ((size_t)(hh - a.nh - a.nkv) * cap + slot) * a.hd;
             vr[dd] = __float2half_rn(a0);
             vr[dd + half_hd] = __float2half_rn(a1);
         }
@@ -423,8 +435,16 @@ __global__ void __launch_bounds__(kMcThreads, 1)
             for (int e = tid; e < rp * TN; e += kMcEpiThreads) {
                 const int rl = e % rp, t = e / rp;
                 const uint32_t off = base + (uint32_t)(((rank * rp + rl) * TN + t) * 4);
+                // every partial is loaded before the first add (the remote loads overlap), then the
+                // sum runs in rank order
+                float part[kMcMaxCluster];
+#pragma unroll
+                for (int q = 0; q < kMcMaxCluster; ++q)
+                    part[q] = q < cs ? ld_dsmem(dsmem_addr(off, (uint32_t)q)) : 0.f;
                 float v = 0.f;
-                for (int q = 0; q < cs; ++q) v += ld_dsmem(dsmem_addr(off, (uint32_t)q));
+#pragma unroll
+                for (int q = 0; q < kMcMaxCluster; ++q)
+                    if (q < cs) v += part[q];
                 const int n = mt * kBM + rank * rp + rl;
                 epilogue_one<MODE>(p, v, n, nt * TN + t, lane, slot0);
             }
@@ -544,9 +564,11 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     if ((op.mode == MC_STORE || op.mode == MC_RESID) && !op.y) return cudaErrorInvalidValue;
     if (op.mode == MC_QKV) {
         const McolQkv &a = op.qkv;
-        if (!a.bias || !a.rope || !a.slot_base || !a.q || !a.kc || !a.vc || a.hd <= 0 || a.hd % 2 || a.nh <= 0 ||
-            a.nkv <= 0 || op.N != (a.nh + 2 * a.nkv) * a.hd || a.max_pos <= 0 || a.cap < op.T)
+        if (!a.bias || !a.rope || !a.q || a.hd <= 0 || a.hd % 2 || a.nh <= 0 || a.nkv <= 0 ||
+            op.N != (a.nh + 2 * a.nkv) * a.hd || a.max_pos <= 0)
             return cudaErrorInvalidValue;
+        if (!a.lanes && (!a.slot_base || !a.kc || !a.vc || a.cap < op.T)) return cudaErrorInvalidValue;
+        if (a.lanes && (!a.pos || a.layer < 0)) return cudaErrorInvalidValue;
     }
     McolParams p{};
     p.N = op.N;

@@ -13,6 +13,7 @@
 // The same pass verifies a draft tree: the T tokens are tree nodes (K/V at scratch slots) and
 // node t attends to the committed prefix and to the nodes whose bits its ancestor mask holds.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "kernels.cuh"
@@ -37,6 +38,35 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStre
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+// The same with dynamic shared memory; the kernel's limit is raised once per device when the size
+// is above the default 48 KB.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args... args) {
+    if (smem > 48 * 1024) {
+        static std::atomic<unsigned long long> raised{0};     // one bit per device, per kernel
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const unsigned long long bit = 1ull << (dev & 63);
+        if (!(raised.load() & bit)) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            raised.fetch_or(bit);
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -228,148 +258,305 @@ __global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, co
 }
 
 // Attention of a short block (T <= kTreeAttnMaxT: a verify tree or a short prompt chunk). CTA =
-// (q head, 4 queries); its four warps split the visible keys into 32-key tiles (warp w takes tiles
-// w, w + 4, ...) and read K and V straight from L2: scores with lane = key (q broadcast from shared
-// memory), online softmax per query and warp, values with lane = HD / 32 output dims and each key's
-// probability broadcast by shuffle. The four warps' (max, sum, acc) meet in shared memory and
-// warp 0 merges them in warp order. Visibility as k_attn_prefill's.
+// (q head, 4 queries), warp w = query q0 + w. The visible keys go through shared memory in tiles of
+// 64 (K and V rows padded by 16 bytes, so the lanes of a quarter warp reading 16 bytes of 8
+// different rows hit distinct banks), two tiles in flight: tile i + 1 is copied with cp.async while
+// tile i is used. Per tile and warp: lane = keys lane and lane + 32 (full dot products over the
+// row), online softmax of the query (running max / sum in fp32), then lane = HD / 32 output dims
+// summed over the tile's keys in order with the probabilities broadcast from shared memory.
+// Visibility as k_attn_prefill's. The output goes out as fp16 hi / lo halves.
 constexpr int kTreeQ = 4;
+constexpr int kTreeKeys = 64;
+template <int HD>
+struct TreeSmem {
+    static constexpr int kRow = HD * 2 + 16;                       // bytes of a padded K / V row
+    static constexpr int kTile = kTreeKeys * kRow;                 // one tile of K (or V)
+    static constexpr int kBytes = 2 * 2 * kTile;                   // two stages of K and V
+};
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const float *q, const __half *kc,
                                                    const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
                                                    int cap, const int *slot_base, int slot_off, float scale,
                                                    DevState *st) {
+    using L = TreeSmem<HD>;
+    extern __shared__ __align__(16) uint8_t tsm[];
+    __shared__ __align__(16) float qs[kTreeQ][HD];
+    __shared__ float ps[kTreeQ][kTreeKeys];
     pdl_enter();
     const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     constexpr int DL = HD / 32;
-    __shared__ __align__(16) float qs[kTreeQ][HD];
-    __shared__ float pm[4][kTreeQ], pl[4][kTreeQ];
-    __shared__ __align__(16) float pa[4][kTreeQ][HD];
+    constexpr int CH = HD / 8;                                     // 16-byte chunks per row
     const int h = blockIdx.x, q0 = blockIdx.y * kTreeQ;
     const int g = h / (nh / nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = q0 + warp;                                       // this warp's query
+    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
+    const int last = slot0 + min(T, q0 + kTreeQ) - 1;              // the last key any query of this CTA sees
+    const int ntiles = last / kTreeKeys + 1;
+    auto stage = [&](int tile) {                                   // cp.async of tile `tile` into its stage
+        uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
+        const int k0 = tile * kTreeKeys;
+        for (int i = threadIdx.x; i < kTreeKeys * CH; i += 128) {
+            const int j = i / CH, c = i - j * CH;
+            if (k0 + j <= last) {
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ks + j * L::kRow + c * 16)),
+                             "l"(kb + (size_t)(k0 + j) * HD + c * 8) : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(vs + j * L::kRow + c * 16)),
+                             "l"(vb + (size_t)(k0 + j) * HD + c * 8) : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0);
     for (int i = threadIdx.x; i < kTreeQ * HD; i += 128) {
         const int qq = i / HD, d = i - qq * HD;
         qs[qq][d] = q0 + qq < T ? q[(size_t)(q0 + qq) * nh * HD + h * HD + d] * scale : 0.f;
     }
-    __syncthreads();
-    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
-    float m[kTreeQ], l[kTreeQ], acc[kTreeQ][DL];
+    float m = -INFINITY, l = 0.f, acc[DL];
 #pragma unroll
-    for (int i = 0; i < kTreeQ; ++i) {
+    for (int d = 0; d < DL; ++d) acc[d] = 0.f;
+    const uint64_t tmask = (mask && t < T) ? mask[t] : 0ull;
+    for (int tile = 0; tile < ntiles; ++tile) {
+        if (tile + 1 < ntiles) {
+            stage(tile + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();                                           // tile `tile` (and q) visible to all
+        const uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
+        const int k0 = tile * kTreeKeys;
+        // scores of keys k0 + lane and k0 + 32 + lane
+        float s0 = 0.f, s1 = 0.f;
+        const uint8_t *r0 = ks + lane * L::kRow, *r1 = ks + (lane + 32) * L::kRow;
+#pragma unroll 4
+        for (int c = 0; c < CH; ++c) {
+            const uint4 a = *reinterpret_cast<const uint4 *>(r0 + c * 16);
+            const uint4 b = *reinterpret_cast<const uint4 *>(r1 + c * 16);
+            const float4 qa = *reinterpret_cast<const float4 *>(&qs[warp][8 * c]);
+            const float4 qb = *reinterpret_cast<const float4 *>(&qs[warp][8 * c + 4]);
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&aw[e]));
+                const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&bw[e]));
+                s0 = fmaf(qv[2 * e], fa.x, s0);
+                s0 = fmaf(qv[2 * e + 1], fa.y, s0);
+                s1 = fmaf(qv[2 * e], fb.x, s1);
+                s1 = fmaf(qv[2 * e + 1], fb.y, s1);
+            }
+        }
+        auto visible = [&](int key) {
+            bool vis = t < T && key <= slot0 + t;
+            if (mask && vis && key >= slot0) vis = (tmask >> (key - slot0)) & 1ull;
+            return vis;
+        };
+        const float v0 = visible(k0 + lane) ? s0 : -INFINITY;
+        const float v1 = visible(k0 + 32 + lane) ? s1 : -INFINITY;
+        __syncwarp();
+        const float mnew = fmaxf(m, warp_max(fmaxf(v0, v1)));
+        const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
+        const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
+        const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
+        l = l * corr + warp_sum(p0 + p1);
+        m = mnew;
+        ps[warp][lane] = p0;
+        ps[warp][lane + 32] = p1;
+        __syncwarp();
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[d] *= corr;
+        const int nk = min(kTreeKeys, last + 1 - k0);              // keys of the tile that were copied
+#pragma unroll 8
+        for (int j = 0; j < nk; ++j) {
+            const float pj = ps[warp][j];
+            const uint8_t *vr = vs + j * L::kRow + lane * DL * 2;
+            if constexpr (DL == 4) {
+                const uint2 vv = *reinterpret_cast<const uint2 *>(vr);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                acc[0] = fmaf(pj, a.x, acc[0]);
+                acc[1] = fmaf(pj, a.y, acc[1]);
+                acc[2] = fmaf(pj, b.x, acc[2]);
+                acc[3] = fmaf(pj, b.y, acc[3]);
+            } else {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(vr));
+                acc[0] = fmaf(pj, a.x, acc[0]);
+                acc[1] = fmaf(pj, a.y, acc[1]);
+            }
+        }
+        __syncthreads();                                           // the stage is rewritten two tiles on
+    }
+    if (t < T) {
+#pragma unroll
+        for (int d = 0; d < DL; ++d) {
+            const float o = acc[d] / l;
+            const __half hv = __float2half_rn(o);
+            const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
+            oh[idx] = hv;
+            ol[idx] = __float2half_rn(o - __half2float(hv));
+        }
+    }
+}
+
+// Attention of a batched decode step: token b of request lanes[b] attends to slots [0, slot] of
+// its own cache. CTA = (kv head g, token b): the group's G = nh / nkv query heads share the K / V
+// tiles, which go through shared memory as in k_attn_tree (64 keys per tile, two in flight, padded
+// rows); warp w takes heads g G + w and g G + w + 4 (G <= 8). Output as fp16 hi / lo halves.
+constexpr int kBatchHeadsPerWarp = 2;
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_batch(__half *oh, __half *ol, const float *q, const BatchLane *lanes,
+                                                    int layer, int nh, int nkv, float scale, DevState *st) {
+    using L = TreeSmem<HD>;
+    extern __shared__ __align__(16) uint8_t tsm[];
+    __shared__ __align__(16) float qs[4 * kBatchHeadsPerWarp][HD];
+    __shared__ float ps[4 * kBatchHeadsPerWarp][kTreeKeys];
+    pdl_enter();
+    constexpr int DL = HD / 32;
+    constexpr int CH = HD / 8;
+    const int g = blockIdx.x, b = blockIdx.y, G = nh / nkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const BatchLane ln = lanes[b];
+    int last = ln.slot;
+    if (last < 0 || last >= ln.cap) {
+        if (threadIdx.x == 0) set_err(st, kErrBadSlot);
+        last = min(max(last, 0), ln.cap - 1);
+    }
+    const size_t head_off = ((size_t)layer * nkv + g) * ln.cap * HD;
+    const __half *kb = ln.k + head_off, *vb = ln.v + head_off;
+    const int ntiles = last / kTreeKeys + 1;
+    auto stage = [&](int tile) {
+        uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
+        const int k0 = tile * kTreeKeys;
+        for (int i = threadIdx.x; i < kTreeKeys * CH; i += 128) {
+            const int j = i / CH, c = i - j * CH;
+            if (k0 + j <= last) {
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ks + j * L::kRow + c * 16)),
+                             "l"(kb + (size_t)(k0 + j) * HD + c * 8) : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(vs + j * L::kRow + c * 16)),
+                             "l"(vb + (size_t)(k0 + j) * HD + c * 8) : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0);
+    for (int i = threadIdx.x; i < 4 * kBatchHeadsPerWarp * HD; i += 128) {
+        const int r = i / HD, d = i - r * HD;               // row r: head g G + (r % 4) + 4 (r / 4)
+        const int hl = (r & 3) + 4 * (r >> 2);
+        qs[r][d] = hl < G ? q[(size_t)b * nh * HD + (g * G + hl) * HD + d] * scale : 0.f;
+    }
+    float m[kBatchHeadsPerWarp], l[kBatchHeadsPerWarp], acc[kBatchHeadsPerWarp][DL];
+#pragma unroll
+    for (int i = 0; i < kBatchHeadsPerWarp; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.f;
 #pragma unroll
         for (int d = 0; d < DL; ++d) acc[i][d] = 0.f;
     }
-    const int last = slot0 + min(T, q0 + kTreeQ) - 1;    // the last key any query of this CTA sees
-    for (int k0 = warp * 32; k0 <= last; k0 += 4 * 32) {
-        const int key = k0 + lane;
-        float s[kTreeQ] = {0.f, 0.f, 0.f, 0.f};
-        if (key <= last) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)key * HD);
-#pragma unroll 4
-            for (int c = 0; c < HD / 8; ++c) {
-                const uint4 kk = __ldg(kr + c);
-                const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
-                const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
-                const float2 k45 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.z));
-                const float2 k67 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.w));
+    for (int tile = 0; tile < ntiles; ++tile) {
+        if (tile + 1 < ntiles) {
+            stage(tile + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
+        const int k0 = tile * kTreeKeys;
+        const bool in0 = k0 + lane <= last, in1 = k0 + 32 + lane <= last;
+        const uint8_t *r0 = ks + lane * L::kRow, *r1 = ks + (lane + 32) * L::kRow;
 #pragma unroll
-                for (int i = 0; i < kTreeQ; ++i) {
-                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[i][8 * c]);
-                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[i][8 * c + 4]);
-                    s[i] = fmaf(qa.x, k01.x, s[i]);
-                    s[i] = fmaf(qa.y, k01.y, s[i]);
-                    s[i] = fmaf(qa.z, k23.x, s[i]);
-                    s[i] = fmaf(qa.w, k23.y, s[i]);
-                    s[i] = fmaf(qb.x, k45.x, s[i]);
-                    s[i] = fmaf(qb.y, k45.y, s[i]);
-                    s[i] = fmaf(qb.z, k67.x, s[i]);
-                    s[i] = fmaf(qb.w, k67.y, s[i]);
+        for (int i = 0; i < kBatchHeadsPerWarp; ++i) {
+            const int r = warp + 4 * i;
+            if (warp + 4 * i >= G) break;                   // warp-uniform
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < CH; ++c) {
+                const uint4 a = *reinterpret_cast<const uint4 *>(r0 + c * 16);
+                const uint4 bb = *reinterpret_cast<const uint4 *>(r1 + c * 16);
+                const float4 qa = *reinterpret_cast<const float4 *>(&qs[r][8 * c]);
+                const float4 qb = *reinterpret_cast<const float4 *>(&qs[r][8 * c + 4]);
+                const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {bb.x, bb.y, bb.z, bb.w};
+                const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&aw[e]));
+                    const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&bw[e]));
+                    s0 = fmaf(qv[2 * e], fa.x, s0);
+                    s0 = fmaf(qv[2 * e + 1], fa.y, s0);
+                    s1 = fmaf(qv[2 * e], fb.x, s1);
+                    s1 = fmaf(qv[2 * e + 1], fb.y, s1);
                 }
             }
-        }
-        float pr[kTreeQ];
-#pragma unroll
-        for (int i = 0; i < kTreeQ; ++i) {
-            const int t = q0 + i;
-            bool vis = t < T && key <= slot0 + t;
-            if (mask && vis && key >= slot0) vis = (mask[t] >> (key - slot0)) & 1ull;
-            const float sv = vis ? s[i] : -INFINITY;
-            const float mnew = fmaxf(m[i], warp_max(sv));
-            pr[i] = mnew == -INFINITY ? 0.f : expf(sv - mnew);
+            const float v0 = in0 ? s0 : -INFINITY, v1 = in1 ? s1 : -INFINITY;
+            __syncwarp();
+            const float mnew = fmaxf(m[i], warp_max(fmaxf(v0, v1)));
+            const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
+            const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
             const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
-            l[i] = l[i] * corr + warp_sum(pr[i]);
+            l[i] = l[i] * corr + warp_sum(p0 + p1);
             m[i] = mnew;
+            ps[r][lane] = p0;
+            ps[r][lane + 32] = p1;
 #pragma unroll
             for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
         }
-        // values: key k0 + j's probability from lane j; its V row read by all lanes (DL dims each)
-        const int nk = min(32, last + 1 - k0);
+        __syncwarp();
+        const int nk = min(kTreeKeys, last + 1 - k0);
+#pragma unroll 4
         for (int j = 0; j < nk; ++j) {
+            const uint8_t *vr = vs + j * L::kRow + lane * DL * 2;
             float vf[DL];
-            const __half *vr = vb + (size_t)(k0 + j) * HD + lane * DL;
             if constexpr (DL == 4) {
-                const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vr));
-                const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-                const float2 v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
-                vf[0] = v0.x;
-                vf[1] = v0.y;
-                vf[2] = v1.x;
-                vf[3] = v1.y;
+                const uint2 vv = *reinterpret_cast<const uint2 *>(vr);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                vf[0] = a.x;
+                vf[1] = a.y;
+                vf[2] = c.x;
+                vf[3] = c.y;
             } else {
-                const float2 v0 = __half22float2(__ldg(reinterpret_cast<const __half2 *>(vr)));
-                vf[0] = v0.x;
-                vf[1] = v0.y;
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(vr));
+                vf[0] = a.x;
+                vf[1] = a.y;
             }
 #pragma unroll
-            for (int i = 0; i < kTreeQ; ++i) {
-                const float pj = __shfl_sync(0xffffffffu, pr[i], j);
+            for (int i = 0; i < kBatchHeadsPerWarp; ++i) {
+                if (warp + 4 * i >= G) break;
+                const float pj = ps[warp + 4 * i][j];
 #pragma unroll
                 for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, vf[d], acc[i][d]);
             }
         }
+        __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < kTreeQ; ++i) {
-        if (lane == 0) {
-            pm[warp][i] = m[i];
-            pl[warp][i] = l[i];
-        }
+    for (int i = 0; i < kBatchHeadsPerWarp; ++i) {
+        const int hl = warp + 4 * i;
+        if (hl >= G) break;
 #pragma unroll
-        for (int d = 0; d < DL; ++d) pa[warp][i][lane * DL + d] = acc[i][d];
-    }
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-        for (int i = 0; i < kTreeQ; ++i) {
-            const int t = q0 + i;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) M = fmaxf(M, pm[w][i]);
-            float L = 0.f, o[DL];
-#pragma unroll
-            for (int d = 0; d < DL; ++d) o[d] = 0.f;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const float f = pm[w][i] == -INFINITY ? 0.f : expf(pm[w][i] - M);
-                L = fmaf(pl[w][i], f, L);
-#pragma unroll
-                for (int d = 0; d < DL; ++d) o[d] = fmaf(pa[w][i][lane * DL + d], f, o[d]);
-            }
-            if (t < T) {
-#pragma unroll
-                for (int d = 0; d < DL; ++d) {
-                    const float v = o[d] / L;
-                    const __half hv = __float2half_rn(v);
-                    const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
-                    oh[idx] = hv;
-                    ol[idx] = __float2half_rn(v - __half2float(hv));
-                }
-            }
+        for (int d = 0; d < DL; ++d) {
+            const float o = acc[i][d] / l[i];
+            const __half hv = __float2half_rn(o);
+            const size_t idx = (size_t)b * nh * HD + (g * G + hl) * HD + lane * DL + d;
+            oh[idx] = hv;
+            ol[idx] = __float2half_rn(o - __half2float(hv));
         }
     }
+}
+
+__global__ void k_batch_advance(BatchLane *lanes, int32_t *tok, int32_t *pos, const int32_t *argmax, int32_t *out,
+                                int B, int max_pos, DevState *st) {
+    pdl_enter();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int t = argmax[b];
+    out[b] = t;
+    tok[b] = t;
+    const int np = pos[b] + 1, ns = lanes[b].slot + 1;
+    if (np >= max_pos || ns >= lanes[b].cap) set_err(st, kErrBadSlot);
+    pos[b] = min(np, max_pos - 1);
+    lanes[b].slot = min(ns, lanes[b].cap - 1);
 }
 
 // w = q * scale (exact in fp32), times 2^k (exact), split into fp16 hi = fp16(w') and lo =
@@ -476,8 +663,12 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
     if (e != cudaSuccess) return e;
     if (T <= kTreeAttnMaxT) {
         const dim3 grid(d.heads, (T + kTreeQ - 1) / kTreeQ);
-        e = launch_pdl(d.head_dim == 128 ? k_attn_tree<128> : k_attn_tree<64>, grid, 128, stream, s.xa,
-                       s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+        if (d.head_dim == 128)
+            e = launch_pdl_smem(k_attn_tree<128>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
+                                kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+        else
+            e = launch_pdl_smem(k_attn_tree<64>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
+                                kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
     } else {
         const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
         e = launch_pdl(d.head_dim == 128 ? k_attn_prefill<128> : k_attn_prefill<64>, grid, 128, stream, s.xa,
@@ -491,6 +682,41 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
     e = launch_mcol(o, stream, true);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
+}
+
+cudaError_t launch_batch_layer_front(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int B,
+                                     const int32_t *pos, const BatchLane *lanes, int layer, float scale,
+                                     const float *rope, DevState *st, cudaStream_t stream) {
+    const int H = d.hidden, QR = (int)qrows_of(d), A = d.heads * d.head_dim;
+    const size_t lo = (size_t)d.max_tokens;
+    if (B <= 0 || B > d.max_tokens || !lanes || !pos || d.heads / d.kv_heads > 4 * kBatchHeadsPerWarp)
+        return cudaErrorInvalidValue;
+    cudaError_t e = launch_pdl(k_rmsnorm_hilo, B, kNormThreads, stream, s.xa, s.xa + lo * H, s.x, L.in_norm, H, d.eps);
+    if (e != cudaSuccess) return e;
+    McolOp qkv = proj(d, s, L.qkv, MC_QKV, QR, H, s.xa, B, st);
+    qkv.qkv = McolQkv{L.qkv_b, rope, pos, nullptr, 0, 0, d.heads, d.kv_heads, d.head_dim, d.max_pos,
+                      s.q, nullptr, nullptr, lanes, layer};
+    e = launch_mcol(qkv, stream, true);
+    if (e != cudaSuccess) return e;
+    const dim3 grid(d.kv_heads, B);
+    if (d.head_dim == 128)
+        e = launch_pdl_smem(k_attn_batch<128>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
+                            lanes, layer, d.heads, d.kv_heads, scale, st);
+    else
+        e = launch_pdl_smem(k_attn_batch<64>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
+                            lanes, layer, d.heads, d.kv_heads, scale, st);
+    if (e != cudaSuccess) return e;
+    McolOp o = proj(d, s, L.o, MC_RESID, H, A, s.xa, B, st);
+    o.y = s.x;
+    o.ldy = H;
+    e = launch_mcol(o, stream, true);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_batch_advance(BatchLane *lanes, int32_t *tok, int32_t *pos, const int32_t *argmax, int32_t *out,
+                                 int B, int max_pos, DevState *st, cudaStream_t stream) {
+    return launch_pdl(k_batch_advance, (B + 127) / 128, 128, stream, lanes, tok, pos, argmax, out, B, max_pos, st);
 }
 
 cudaError_t launch_prefill_layer_ffn(const PrefillDims &d, const PrefillLayer &L, const PrefillScratch &s, int T,

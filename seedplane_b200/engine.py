@@ -227,6 +227,18 @@ class CudaQwen2:
                                    C.c_void_p(_stream(self.device))))
         return out, logits
 
+    def decode_batch(self, kvs: Sequence[DeviceKV], tokens: Sequence[int], positions: Sequence[int], n_steps: int,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Greedy decode of len(kvs) independent requests together (`sp_decode_batch`): request b feeds
+        tokens[b] at positions[b] into kvs[b]; returns the argmaxes int32 [n_steps, B]."""
+        B = len(kvs)
+        if out is None:
+            out = torch.empty((n_steps, B), dtype=torch.int32, device=self.device)
+        handles = (C.c_void_p * B)(*[kv.handle for kv in kvs])
+        N.check(N.load().sp_decode_batch(self.handle, handles, B, N.int_array(tokens), N.int_array(positions),
+                                         int(n_steps), C.c_void_p(out.data_ptr()), C.c_void_p(_stream(self.device))))
+        return out
+
     def verify_tree(self, kv: DeviceKV, tokens: Sequence[int], parents: Sequence[int], base_pos: int,
                     want_logits: bool = False):
         """One batched pass over a draft tree; returns (argmax int32 [n], logits [n, V] or None)."""

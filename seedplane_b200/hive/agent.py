@@ -40,16 +40,43 @@ class GreedyExecutor:
     """`execute` of a GPU agent over an engine in this process: greedy generation of token ids.
 
     Payload: {"ids": [...], "max_new_tokens": n}. Prefill, then the device decode loop (argmax fed
-    back on the GPU); one host sync per request, to read the first token. Optional `timer`
-    (callable(start: bool)) brackets the device work of each request."""
+    back on the GPU); one host sync per request, to read the first token. A grouped lease,
+    {"batch": [payload, ...]}, runs its requests together (`batch.generate_batch`: one batched pass
+    per decode step for all of them) and answers {"batch": [result, ...]}. Optional `timer`
+    (callable(start: bool)) brackets the device work of each lease."""
 
     def __init__(self, engine, capacity: int, timer=None):
         self.engine = engine
+        self.capacity = capacity
         self.kv = engine.new_kv(capacity)
+        self.batch_kvs = []
         self.timer = timer
+
+    def _batch(self, items) -> dict:
+        from ..batch import MAX_BATCH, generate_batch
+        prompts, limits = [], []
+        for it in items:
+            ids = [int(t) for t in it["ids"]]
+            n = int(it.get("max_new_tokens", 32))
+            if not ids or n < 1:
+                raise ValueError("a request needs prompt ids and max_new_tokens >= 1")
+            if len(ids) + n > self.capacity:
+                raise ValueError("request exceeds the agent's KV capacity")
+            prompts.append(ids)
+            limits.append(n)
+        while len(self.batch_kvs) < min(len(items), MAX_BATCH):
+            self.batch_kvs.append(self.engine.new_kv(self.capacity))
+        out = []
+        for c0 in range(0, len(items), MAX_BATCH):
+            out += generate_batch(self.engine, prompts[c0:c0 + MAX_BATCH], limits[c0:c0 + MAX_BATCH],
+                                  kvs=self.batch_kvs, timer=self.timer)
+        dev = str(self.engine.device)
+        return {"batch": [{"tokens": t, "token_sha256": token_sha256(t), "device": dev} for t in out]}
 
     def __call__(self, payload: dict) -> dict:
         import torch
+        if "batch" in payload:
+            return self._batch(payload["batch"])
         ids = [int(t) for t in payload["ids"]]
         n = int(payload.get("max_new_tokens", 32))
         if not ids or n < 1:

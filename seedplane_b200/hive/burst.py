@@ -27,9 +27,11 @@ REQUESTS, NEW_TOKENS, LOW, HIGH = 16, 32, 32, 128
 MODEL_ID = "qwen2-1.5b"
 
 
-def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_over_ranks, barrier):
+def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_over_ranks, barrier, batched=False):
     """The 16 x 32 burst through HIVE on `eng` (this rank's engine); every rank calls it. Returns the
-    summary on rank 0 (None elsewhere)."""
+    summary on rank 0 (None elsewhere). `batched`: each GPU's share of a timed step goes out as one
+    grouped lease that its agent decodes as one batch (runtime request batching); warm-up leases
+    stay single requests, which is what the planner measures."""
     import torch
     import torch.distributed as dist
 
@@ -53,9 +55,15 @@ def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_ov
     base = GreedyExecutor(eng, HIGH + NEW_TOKENS + 1)
 
     def execute(payload):
-        base.timer = timer if payload.get("phase") == "timed" else None
+        items = payload.get("batch")
+        phase = (items[0] if items else payload).get("phase")
+        base.timer = timer if phase == "timed" else None
         r = base(payload)
-        r["request"] = payload.get("request")
+        if items is not None:
+            for it, res in zip(items, r["batch"]):
+                res["request"] = it.get("request")
+        else:
+            r["request"] = payload.get("request")
         return r
 
     broker = None
@@ -107,7 +115,7 @@ def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_ov
         with ClockSampler(list(range(world))) as clocks:
             for step in range(steps):
                 t0 = time.perf_counter()
-                futs = broker.submit_batch(payloads("timed", step), **kw)
+                futs = broker.submit_batch(payloads("timed", step), group_per_worker=batched, **kw)
                 for f in futs:
                     assigned[f.planned_worker_id] = assigned.get(f.planned_worker_id, 0) + 1
                 for f in futs:
@@ -117,7 +125,8 @@ def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_ov
                 makespans.append(time.perf_counter() - t0)
         broker.close()
         info = {"clocks": clocks.summary(), "makespans": makespans, "assigned": assigned,
-                "token_sha256": hashlib.sha256(json.dumps([shas[i] for i in sorted(shas)]).encode()).hexdigest()}
+                "token_sha256": hashlib.sha256(json.dumps([shas[i] for i in sorted(shas)]).encode()).hexdigest(),
+                "request_sha256": [shas[i] for i in sorted(shas)]}
     th.join(timeout=600)
     if errors:
         raise errors[0]
@@ -130,11 +139,12 @@ def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_ov
     tokens = steps * REQUESTS * NEW_TOKENS
     wall = sum(info["makespans"])
     return {"metric": "burst tok/s (16 x 32 requests, HIVE pull agent per GPU, wall-clock makespan)",
+            "batched": bool(batched),
             "value": tokens / wall, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "makespan_ms": [1000.0 * m for m in info["makespans"]],
             "device_tok_s": tokens / (span_max / 1000.0) if span_max > 0 else None,
             "assigned": info["assigned"], "prompt_tokens_per_step": sum(len(p) for p in prompts),
-            "token_sha256": info["token_sha256"], "clocks": info["clocks"],
+            "token_sha256": info["token_sha256"], "request_sha256": info["request_sha256"], "clocks": info["clocks"],
             "note": "makespan = submit_batch to the last result on rank 0 (loopback TCP broker, JSON, host work "
                     "included); device_tok_s = the same tokens over the slowest rank's device span"}
 
@@ -150,7 +160,9 @@ def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barr
     w = make_weights(QWEN2_1_5B, seed=0, dtype=torch.float16)
     eng = CudaQwen2(QWEN2_1_5B, w, device=dev)
     del w
-    b = burst_on_engine(eng, args.steps, args.warmup, world, rank, local, ClockSampler, max_over_ranks, barrier)
+    single = burst_on_engine(eng, args.steps, args.warmup, world, rank, local, ClockSampler, max_over_ranks, barrier)
+    b = burst_on_engine(eng, args.steps, args.warmup, world, rank, local, ClockSampler, max_over_ranks, barrier,
+                        batched=True)
     eng.close()
     if rank != 0:
         return None
@@ -162,7 +174,13 @@ def run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barr
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": f"{REQUESTS} independent greedy requests x {NEW_TOKENS} new tokens per step, "
                                    f"prompts of uniform-random length in [{LOW}, {HIGH}] (seeded), qwen2-1.5b "
-                                   "random-init fp16 weights, one HIVE pull agent per GPU, loopback TCP broker",
+                                   "random-init fp16 weights, one HIVE pull agent per GPU, loopback TCP broker; "
+                                   "each GPU's share as one grouped lease decoded as a batch",
+                       "one_request_per_lease": {"value": single["value"], "makespan_ms": single["makespan_ms"],
+                                                 "token_sha256": single["token_sha256"],
+                                                 "requests_with_equal_tokens": sum(
+                                                     x == y for x, y in zip(single["request_sha256"],
+                                                                            b["request_sha256"]))},
                        "parallelism": f"requests partitioned over {world} GPU(s) by measured service time, "
                                       "no collective", "assigned": b["assigned"],
                        "device_tok_s": b["device_tok_s"],

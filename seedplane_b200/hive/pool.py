@@ -155,6 +155,22 @@ class WorkFuture:
         self._t.future.add_done_callback(fn)
 
 
+class BatchMemberFuture(WorkFuture):
+    """One request of a grouped lease (`submit_batch(..., group_per_worker=True)`): its result is
+    element `index` of the group's `{"batch": [...]}` result."""
+
+    def __init__(self, ticket: _Ticket, index: int):
+        super().__init__(ticket)
+        self.index = index
+
+    def result(self, timeout=None):
+        res = self._t.future.result(timeout)
+        items = res.get("batch") if isinstance(res, dict) else None
+        if not isinstance(items, list) or len(items) != len(self._t.tile.payload["batch"]):
+            raise RuntimeError("the agent's batch result does not match the batch it was given")
+        return items[self.index]
+
+
 class LeaseQueue:
     """Ready tickets in heaps by work class and by reserved worker; see the module docstring."""
 
@@ -388,11 +404,17 @@ class HiveBroker:
 
     def submit_batch(self, payloads, *, model, required_caps=("generate",), priority=0, timeout=300,
                      kind="throughput.generate", token_budget=0, predicted_cost=None,
-                     require_profiles=True) -> List[WorkFuture]:
+                     require_profiles=True, group_per_worker=False) -> List[WorkFuture]:
         """Queue interchangeable, independent tiles split over the capable workers so that the
         predicted makespan (by measured median service times) is least; a slow worker may get
         none. With `require_profiles`, every capable worker must have been measured. Requests are
-        never split."""
+        never split.
+
+        `group_per_worker`: each worker's share goes out as ONE lease whose payload is
+        `{"batch": [payload, ...]}` (kind `<kind>.batch`), for agents that run a batch of requests
+        together (runtime request batching, one set of decode steps for all of them); the agent
+        answers `{"batch": [result, ...]}` in the same order and reports the batch size in its
+        metrics. The returned futures are still one per request, in payload order."""
         payloads = list(payloads)
         if not payloads:
             return []
@@ -415,6 +437,18 @@ class HiveBroker:
             plan = plan_homogeneous_batch(len(tiles), measured)
             fastest_first = sorted(plan.assignments, key=lambda w: (measured[w], w))
             owners = [w for w in fastest_first for _ in range(plan.assignments[w])]
+        if group_per_worker:
+            futures: List[WorkFuture] = []
+            tickets = []
+            for owner, idx in _runs(owners):
+                group = WorkTile(kind=kind + ".batch", model=model, payload={"batch": [payloads[i] for i in idx]},
+                                 required_caps=frozenset(required_caps), token_budget=token_budget,
+                                 predicted_cost=dict(predicted_cost or {}), deadline_s=timeout, priority=priority)
+                t = self._ticket(group, owner)
+                tickets.append(t)
+                futures += [BatchMemberFuture(t, j) for j in range(len(idx))]
+            self._queue.put(tickets)
+            return futures
         tickets = [self._ticket(tile, owner) for tile, owner in zip(tiles, owners)]
         self._queue.put(tickets)
         return [WorkFuture(t) for t in tickets]
@@ -552,6 +586,18 @@ class _Session(threading.Thread):
                 pass
 
 
+def _runs(owners: List[Optional[str]]):
+    """(owner, indices) of each maximal run of equal owners (a batch plan lists every worker's share
+    contiguously)."""
+    out: List[Tuple[Optional[str], List[int]]] = []
+    for i, w in enumerate(owners):
+        if out and out[-1][0] == w:
+            out[-1][1].append(i)
+        else:
+            out.append((w, [i]))
+    return out
+
+
 def _run_task(execute: Callable, payload) -> dict:
     """Run one payload; a failure becomes the lease's error and leaves the agent alive."""
     t0 = time.perf_counter()
@@ -559,8 +605,9 @@ def _run_task(execute: Callable, payload) -> dict:
         result = execute(payload)
     except Exception as exc:  # noqa: BLE001 - any task failure belongs to its lease
         return {"ok": False, "error": f"{type(exc).__name__}: {exc}"}
+    batch = payload.get("batch") if isinstance(payload, dict) else None
     return {"ok": True, "result": result, "metrics": {"duration_ms": (time.perf_counter() - t0) * 1e3,
-                                                      "batch_size": 1}}
+                                                      "batch_size": len(batch) if isinstance(batch, list) else 1}}
 
 
 class LocalAgent:

@@ -281,3 +281,41 @@ def test_unleased_work_expires():
             fut.result(timeout=3)
         ag.stop()
         t.join(timeout=3)
+
+
+def test_grouped_leases_send_each_workers_share_as_one_batch():
+    """submit_batch(group_per_worker=True): each planned worker gets ONE lease carrying its share as
+    {"batch": [...]}; the agent answers {"batch": [...]} and every request's future resolves to its
+    own element; the broker records the batch size the agent reports."""
+    seen = {}
+
+    def make(name):
+        def execute(p):
+            items = p["batch"]
+            seen.setdefault(name, []).append(len(items))
+            return {"batch": [{"twice": 2 * it["x"]} for it in items]}
+        return execute
+
+    with HiveBroker(pull_poll_s=0.02) as broker:
+        agents, threads = _start_agents(broker, [(n, ("generate",), ("qwen",), make(n)) for n in ("gpu0", "gpu1")])
+        for name in ("gpu0", "gpu1"):
+            for _ in range(3):
+                broker.cost_model.observe(kind="decode", model="qwen", worker=name, token_budget=4, duration_ms=10)
+        futs = broker.submit_batch([{"x": n} for n in range(10)], model="qwen", required_caps=("generate",),
+                                   kind="decode", token_budget=4, group_per_worker=True)
+        assert [f.result(timeout=3) for f in futs] == [{"twice": 2 * n} for n in range(10)]
+        assert sorted(sum(seen.values(), [])) == [5, 5]
+        assert {f.planned_worker_id for f in futs} == {"gpu0", "gpu1"}
+        est = broker.cost_model.estimate(kind="decode.batch", model="qwen", worker="gpu0", token_budget=4,
+                                         batch_size=5)
+        assert est is None or est.samples >= 1
+        _stop(agents, threads)
+    # a malformed batch answer fails every member of that lease
+    with HiveBroker(pull_poll_s=0.02) as broker:
+        agents, threads = _start_agents(broker, [("bad", ("generate",), ("other",), lambda p: {"batch": []})])
+        futs = broker.submit_batch([{"x": 1}, {"x": 2}], model="other", required_caps=("generate",),
+                                   require_profiles=False, group_per_worker=True)
+        for f in futs:
+            with pytest.raises(RuntimeError, match="does not match"):
+                f.result(timeout=3)
+        _stop(agents, threads)
