@@ -97,8 +97,11 @@ int sp_kv_set_length(sp_kv *kv, int32_t length);
 /* Run `n` tokens through the model at cache slots [len, len+n), exactly Qwen2Engine.forward
  * (qwen_engine.py:105-144): tokens_dev[n] int32, positions_dev[n] int32 RoPE positions (NULL =
  * the slots). Token i attends to slots [0, len+i]. Advances the cache length by n.
- * logits_dev: NULL, or fp32 [n][vocab] when all_logits else [vocab] (last token only).
- * argmax_dev: NULL, or int32 [n] greedy token after each input token (lowest index on ties). */
+ * all_logits = 0: logits_dev NULL or fp32 [vocab] of the last token; argmax_dev NULL or int32 [n],
+ *   the greedy token after each input token (lowest index on ties).
+ * all_logits = 1: logits_dev fp32 [n][vocab] and argmax_dev [n] for every token.
+ * all_logits = 2: the last token only (a prompt whose other tokens only fill the cache): logits_dev
+ *   [vocab], argmax_dev[0]; the batched pass runs the LM head for that one token. */
 int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t *positions_dev,
                int32_t n, float *logits_dev, int32_t all_logits, int32_t *argmax_dev, void *stream);
 

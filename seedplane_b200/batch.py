@@ -47,7 +47,7 @@ def generate_batch(engine, prompts: Sequence[Sequence[int]], max_new_tokens, sto
         firsts = []
         for p, kv in zip(prompts, kvs):
             kv.length = 0
-            _, am = engine.forward(kv, torch.tensor(p, dtype=torch.int32), want_logits=False)
+            _, am = engine.forward(kv, torch.tensor(p, dtype=torch.int32), want_logits=False, last_only=True)
             firsts.append(am[-1:])
         out = [[t] for t in torch.cat(firsts).cpu().tolist()]
         done = [o[0] in stops or m == 1 for o, m in zip(out, limits)]

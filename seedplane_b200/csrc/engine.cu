@@ -162,6 +162,8 @@ struct sp_engine {
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
     int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
     BatchIn *bt = nullptr;                  // batched decode inputs
+    int32_t *last_only_buf = nullptr;       // sp_forward(all_logits = 2) through the step path: per-step argmaxes
+    int32_t last_only_cap = 0;
     std::map<int, cudaGraphExec_t> bgraphs; // batched decode step per batch size
     int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
@@ -1093,6 +1095,7 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->gr_buf);
     for (auto &g : e->bgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->bt);
+    cudaFree(e->last_only_buf);
     delete e;
 }
 
@@ -1180,7 +1183,7 @@ static int check_engine_kv(sp_engine *e, sp_kv *kv) {
 // ancestor masks (n <= kSmallNodes), else causal.
 static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const int32_t *pos, const uint64_t *mask,
                            const int32_t *slot_base, int32_t n, float *logits, bool all_logits, int32_t *argmax,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool last_only = false) {
     const sp_config &c = e->c;
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const float scale = 1.0f / sqrtf((float)c.head_dim);
@@ -1193,6 +1196,15 @@ static int forward_batched(sp_engine *e, sp_kv *kv, const int32_t *tok, const in
                                                mask ? mask + b0 : nullptr, kv->k + l * kv_layer, kv->v + l * kv_layer,
                                                kv->capacity, slot_base, b0, scale, e->rope, e->st, s));
             SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->st, s));
+        }
+        // last_only: the head of the last token alone (argmax[0], logits [vocab])
+        if (last_only) {
+            if (b0 + T < n) continue;
+            SP_CUDA(launch_prefill_logits(e->pf_dims, e->pf, e->final_norm, e->head_pf, T - 1, 1, e->pf.logits, e->st, s));
+            if (argmax) SP_CUDA(launch_argmax_rows(e->pf.logits, 1, c.vocab, c.vocab, argmax, e->am, s));
+            if (logits)
+                SP_CUDA(cudaMemcpyAsync(logits, e->pf.logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToDevice, s));
+            continue;
         }
         for (int r0 = 0; r0 < T; r0 += kPrefillLogitRows) {
             const int rows = std::min(kPrefillLogitRows, T - r0);
@@ -1241,12 +1253,13 @@ int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t
     if (rc) return rc;
     if (n <= 0 || !tokens_dev) return fail(SP_ERR_INVALID, "input_ids cannot be empty");
     if (kv->length + n > kv->capacity) return fail(SP_ERR_CAPACITY, "KV cache capacity %d exceeded", kv->capacity);
+    if (all_logits < 0 || all_logits > 2) return fail(SP_ERR_INVALID, "all_logits must be 0, 1 or 2");
     if (e->prefill && n >= kPrefillMin) {
         cudaStream_t s = (cudaStream_t)stream;
         const int32_t base = kv->length;
         SP_CUDA(cudaMemcpyAsync(&e->vt->slot0, &base, sizeof(base), cudaMemcpyHostToDevice, s));
-        rc = forward_batched(e, kv, tokens_dev, positions_dev, nullptr, &e->vt->slot0, n, logits_dev, all_logits != 0,
-                             argmax_dev, s);
+        rc = forward_batched(e, kv, tokens_dev, positions_dev, nullptr, &e->vt->slot0, n, logits_dev, all_logits == 1,
+                             argmax_dev, s, all_logits == 2);
         if (rc) return rc;
         kv->length += n;
         return SP_OK;
@@ -1258,10 +1271,24 @@ int sp_forward(sp_engine *e, sp_kv *kv, const int32_t *tokens_dev, const int32_t
     d.f_tok = tokens_dev;
     d.f_pos = positions_dev;
     d.logits = logits_dev;
-    d.logits_stride = all_logits ? (long long)e->c.vocab : 0;
-    d.logits_from = all_logits ? 0 : n - 1;
+    d.logits_stride = all_logits == 1 ? (long long)e->c.vocab : 0;
+    d.logits_from = all_logits == 1 ? 0 : n - 1;
     d.out_tokens = argmax_dev;
+    if (all_logits == 2 && argmax_dev && n > 1) {
+        // the last token's argmax alone, at argmax_dev[0]: the steps write theirs to the engine's scratch
+        if (e->last_only_cap < n) {
+            cudaFree(e->last_only_buf);
+            e->last_only_buf = nullptr;
+            e->last_only_cap = 0;
+            SP_CUDA(cudaMalloc(&e->last_only_buf, (size_t)n * sizeof(int32_t)));
+            e->last_only_cap = n;
+        }
+        d.out_tokens = e->last_only_buf;
+    }
     rc = run_steps(e, kv, d, n, (cudaStream_t)stream);
+    if (!rc && all_logits == 2 && argmax_dev && n > 1)
+        SP_CUDA(cudaMemcpyAsync(argmax_dev, e->last_only_buf + n - 1, sizeof(int32_t), cudaMemcpyDeviceToDevice,
+                                (cudaStream_t)stream));
     if (rc) return rc;
     kv->length += n;
     return SP_OK;

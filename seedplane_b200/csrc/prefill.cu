@@ -23,9 +23,7 @@ namespace sp {
 namespace {
 
 constexpr int kNormThreads = 256;
-constexpr int kAttnQ = 16;                  // queries per attention CTA (4 per warp)
-constexpr int kAttnKeys = 32;               // keys per staged tile (one per lane)
-constexpr int kTreeAttnMaxT = 64;           // blocks up to this many tokens use k_attn_tree
+constexpr int kShortBlockT = 64;            // blocks up to this many tokens: one query per warp
 
 __device__ __forceinline__ void set_err(DevState *st, int code) {
     if (st) atomicCAS(&st->err, 0, code);
@@ -127,145 +125,17 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __hal
     }
 }
 
-// GQA attention of T queries (slots slot0 .. slot0 + T - 1) over the cache. Query t sees the slots
-// before slot0 and, among the block's own slots, [slot0, slot0 + t] (causal, mask == null) or the
-// slots slot0 + j whose bit j its ancestor mask holds (tree, T <= 64). CTA = (q head, 16 queries),
-// warp = 4 queries; keys in tiles of 32 staged
-// in shared memory (K rows padded by 8 bytes: lane j reads row j without bank conflicts). Scores,
-// online softmax (running max / sum per query) and the value sums in fp32 (the tile's
-// probabilities go through shared memory: each lane then sums its dims over the keys); the output
-// goes out as fp16 hi / lo halves (the O projection's input).
-template <int HD>
-__global__ void __launch_bounds__(128) k_attn_prefill(__half *oh, __half *ol, const float *q, const __half *kc,
-                                                      const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
-                                                      int cap, const int *slot_base, int slot_off, float scale,
-                                                      DevState *st) {
-    pdl_enter();
-    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
-    constexpr int DL = HD / 32;                       // output dims per lane
-    constexpr int KROW = HD * 2 + 8;                  // padded K row (bytes): 8-byte reads, lanes on distinct banks
-    __shared__ __align__(16) float qs[kAttnQ][HD];
-    __shared__ __align__(16) uint8_t ks[kAttnKeys * KROW];
-    __shared__ __align__(16) __half vs[kAttnKeys][HD];
-    __shared__ float ps[kAttnQ][kAttnKeys];            // this tile's probabilities
-    const int h = blockIdx.x, q0 = blockIdx.y * kAttnQ;
-    const int g = h / (nh / nkv);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < kAttnQ * HD; i += 128) {
-        const int qq = i / HD, d = i - qq * HD;
-        qs[qq][d] = q0 + qq < T ? q[(size_t)(q0 + qq) * nh * HD + h * HD + d] * scale : 0.f;
-    }
-    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
-    float m[4], l[4], acc[4][DL];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-#pragma unroll
-        for (int d = 0; d < DL; ++d) acc[i][d] = 0.f;
-    }
-    const int last = slot0 + min(T, q0 + kAttnQ) - 1;    // the last key any query of this CTA sees
-    for (int k0 = 0; k0 <= last; k0 += kAttnKeys) {
-        __syncthreads();                                  // previous tile consumed (and q staged)
-        for (int i = threadIdx.x; i < kAttnKeys * (HD / 8); i += 128) {
-            const int j = i / (HD / 8), c = i - j * (HD / 8);
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
-            if (k0 + j <= last) {
-                kv = *reinterpret_cast<const uint4 *>(kb + (size_t)(k0 + j) * HD + c * 8);
-                vv = *reinterpret_cast<const uint4 *>(vb + (size_t)(k0 + j) * HD + c * 8);
-            }
-            uint32_t *kd = reinterpret_cast<uint32_t *>(ks + (size_t)j * KROW + c * 16);
-            kd[0] = kv.x;
-            kd[1] = kv.y;
-            kd[2] = kv.z;
-            kd[3] = kv.w;
-            *reinterpret_cast<uint4 *>(&vs[j][c * 8]) = vv;
-        }
-        __syncthreads();
-        __syncwarp();                                     // reconverged before the shuffles below
-        // scores: lane = key k0 + lane, four queries of this warp, four dims per step
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint8_t *kr = ks + (size_t)lane * KROW;
-#pragma unroll 8
-        for (int d = 0; d < HD; d += 4) {
-            const uint2 kk = *reinterpret_cast<const uint2 *>(kr + d * 2);
-            const float2 ka = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
-            const float2 kb2 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float4 qf = *reinterpret_cast<const float4 *>(&qs[warp * 4 + i][d]);
-                s[i] = fmaf(qf.x, ka.x, s[i]);
-                s[i] = fmaf(qf.y, ka.y, s[i]);
-                s[i] = fmaf(qf.z, kb2.x, s[i]);
-                s[i] = fmaf(qf.w, kb2.y, s[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int t = q0 + warp * 4 + i;
-            const int key = k0 + lane;
-            bool vis = t < T && key <= slot0 + t;
-            if (mask && vis && key >= slot0) vis = (mask[t] >> (key - slot0)) & 1ull;
-            const float sv = vis ? s[i] : -INFINITY;
-            const float mnew = fmaxf(m[i], warp_max(sv));
-            const float p = mnew == -INFINITY ? 0.f : expf(sv - mnew);
-            const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
-            l[i] = l[i] * corr + warp_sum(p);
-            m[i] = mnew;
-#pragma unroll
-            for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
-            ps[warp * 4 + i][lane] = p;
-        }
-        __syncwarp();
-        // values: lane = DL dims, keys in order, the warp's four queries per key (probabilities from
-        // shared memory, a broadcast; no shuffles, no branches)
-        for (int j = 0; j < kAttnKeys; ++j) {
-            float vf[DL];
-            if constexpr (DL == 4) {
-                const uint2 vv = *reinterpret_cast<const uint2 *>(&vs[j][lane * 4]);
-                const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-                const float2 v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
-                vf[0] = v0.x;
-                vf[1] = v0.y;
-                vf[2] = v1.x;
-                vf[3] = v1.y;
-            } else {
-#pragma unroll
-                for (int d = 0; d < DL; ++d) vf[d] = __half2float(vs[j][lane * DL + d]);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float pj = ps[warp * 4 + i][j];
-#pragma unroll
-                for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, vf[d], acc[i][d]);
-            }
-        }
-        __syncwarp();                                     // ps is rewritten by the next tile
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int t = q0 + warp * 4 + i;
-        if (t >= T) continue;
-#pragma unroll
-        for (int d = 0; d < DL; ++d) {
-            const float o = acc[i][d] / l[i];
-            const __half hv = __float2half_rn(o);
-            const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
-            oh[idx] = hv;
-            ol[idx] = __float2half_rn(o - __half2float(hv));
-        }
-    }
-}
-
-// Attention of a short block (T <= kTreeAttnMaxT: a verify tree or a short prompt chunk). CTA =
-// (q head, 4 queries), warp w = query q0 + w. The visible keys go through shared memory in tiles of
-// 64 (K and V rows padded by 16 bytes, so the lanes of a quarter warp reading 16 bytes of 8
-// different rows hit distinct banks), two tiles in flight: tile i + 1 is copied with cp.async while
-// tile i is used. Per tile and warp: lane = keys lane and lane + 32 (full dot products over the
-// row), online softmax of the query (running max / sum in fp32), then lane = HD / 32 output dims
-// summed over the tile's keys in order with the probabilities broadcast from shared memory.
-// Visibility as k_attn_prefill's. The output goes out as fp16 hi / lo halves.
-constexpr int kTreeQ = 4;
+// Attention of a block of T queries over the cache (a prompt chunk or a verify tree). CTA =
+// (q head, 4 QW queries), warp w = queries q0 + w QW .. + QW - 1 (QW = 1 for short blocks, 4 for
+// prompt chunks). The visible keys go through shared memory in tiles of 64 (K and V rows padded by
+// 16 bytes, so the lanes of a quarter warp reading 16 bytes of 8 different rows hit distinct
+// banks), two tiles in flight: tile i + 1 is copied with cp.async while tile i is used. Per tile
+// and warp: lane = keys lane and lane + 32 (full dot products over the row, each K chunk read once
+// for the warp's QW queries), online softmax per query (running max / sum in fp32), then lane =
+// HD / 32 output dims summed over the tile's keys in order with the probabilities broadcast from
+// shared memory. Query t sees the slots before slot0 and, among the block's own slots,
+// [slot0, slot0 + t] (causal, mask == null) or the slots slot0 + j whose bit j its ancestor mask
+// holds (tree, T <= 64). The output goes out as fp16 hi / lo halves (the O projection's input).
 constexpr int kTreeKeys = 64;
 template <int HD>
 struct TreeSmem {
@@ -273,25 +143,26 @@ struct TreeSmem {
     static constexpr int kTile = kTreeKeys * kRow;                 // one tile of K (or V)
     static constexpr int kBytes = 2 * 2 * kTile;                   // two stages of K and V
 };
-template <int HD>
-__global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const float *q, const __half *kc,
-                                                   const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
-                                                   int cap, const int *slot_base, int slot_off, float scale,
-                                                   DevState *st) {
+template <int HD, int QW>
+__global__ void __launch_bounds__(128) k_attn_block(__half *oh, __half *ol, const float *q, const __half *kc,
+                                                    const __half *vc, const uint64_t *mask, int T, int nh, int nkv,
+                                                    int cap, const int *slot_base, int slot_off, float scale,
+                                                    DevState *st) {
     using L = TreeSmem<HD>;
+    constexpr int QC = 4 * QW;                                     // queries per CTA
     extern __shared__ __align__(16) uint8_t tsm[];
-    __shared__ __align__(16) float qs[kTreeQ][HD];
-    __shared__ float ps[kTreeQ][kTreeKeys];
+    __shared__ __align__(16) float qs[QC][HD];
+    __shared__ float ps[QC][kTreeKeys];
     pdl_enter();
     const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
     constexpr int DL = HD / 32;
     constexpr int CH = HD / 8;                                     // 16-byte chunks per row
-    const int h = blockIdx.x, q0 = blockIdx.y * kTreeQ;
+    const int h = blockIdx.x, q0 = blockIdx.y * QC;
     const int g = h / (nh / nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = q0 + warp;                                       // this warp's query
+    const int tw = q0 + warp * QW;                                 // this warp's first query
     const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
-    const int last = slot0 + min(T, q0 + kTreeQ) - 1;              // the last key any query of this CTA sees
+    const int last = slot0 + min(T, q0 + QC) - 1;                  // the last key any query of this CTA sees
     const int ntiles = last / kTreeKeys + 1;
     auto stage = [&](int tile) {                                   // cp.async of tile `tile` into its stage
         uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
@@ -308,14 +179,22 @@ __global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     stage(0);
-    for (int i = threadIdx.x; i < kTreeQ * HD; i += 128) {
+    for (int i = threadIdx.x; i < QC * HD; i += 128) {
         const int qq = i / HD, d = i - qq * HD;
         qs[qq][d] = q0 + qq < T ? q[(size_t)(q0 + qq) * nh * HD + h * HD + d] * scale : 0.f;
     }
-    float m = -INFINITY, l = 0.f, acc[DL];
+    float m[QW], l[QW], acc[QW][DL];
+    uint64_t tmask[QW];
 #pragma unroll
-    for (int d = 0; d < DL; ++d) acc[d] = 0.f;
-    const uint64_t tmask = (mask && t < T) ? mask[t] : 0ull;
+    for (int i = 0; i < QW; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+        tmask[i] = (mask && tw + i < T) ? mask[tw + i] : 0ull;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[i][d] = 0.f;
+    }
+    // the last key any query of this warp sees: tiles past it are skipped by the warp
+    const int wlast = slot0 + min(T - 1, tw + QW - 1);
     for (int tile = 0; tile < ntiles; ++tile) {
         if (tile + 1 < ntiles) {
             stage(tile + 1);
@@ -326,71 +205,96 @@ __global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const
         __syncthreads();                                           // tile `tile` (and q) visible to all
         const uint8_t *ks = tsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
         const int k0 = tile * kTreeKeys;
-        // scores of keys k0 + lane and k0 + 32 + lane
-        float s0 = 0.f, s1 = 0.f;
-        const uint8_t *r0 = ks + lane * L::kRow, *r1 = ks + (lane + 32) * L::kRow;
-#pragma unroll 4
-        for (int c = 0; c < CH; ++c) {
-            const uint4 a = *reinterpret_cast<const uint4 *>(r0 + c * 16);
-            const uint4 b = *reinterpret_cast<const uint4 *>(r1 + c * 16);
-            const float4 qa = *reinterpret_cast<const float4 *>(&qs[warp][8 * c]);
-            const float4 qb = *reinterpret_cast<const float4 *>(&qs[warp][8 * c + 4]);
-            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        if (k0 <= wlast && tw < T) {                               // warp-uniform
+            float s0[QW], s1[QW];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&aw[e]));
-                const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&bw[e]));
-                s0 = fmaf(qv[2 * e], fa.x, s0);
-                s0 = fmaf(qv[2 * e + 1], fa.y, s0);
-                s1 = fmaf(qv[2 * e], fb.x, s1);
-                s1 = fmaf(qv[2 * e + 1], fb.y, s1);
+            for (int i = 0; i < QW; ++i) s0[i] = s1[i] = 0.f;
+            const uint8_t *r0 = ks + lane * L::kRow, *r1 = ks + (lane + 32) * L::kRow;
+#pragma unroll 2
+            for (int c = 0; c < CH; ++c) {
+                const uint4 a = *reinterpret_cast<const uint4 *>(r0 + c * 16);
+                const uint4 b = *reinterpret_cast<const uint4 *>(r1 + c * 16);
+                const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+                float fa[8], fb[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 x = __half22float2(*reinterpret_cast<const __half2 *>(&aw[e]));
+                    const float2 y = __half22float2(*reinterpret_cast<const __half2 *>(&bw[e]));
+                    fa[2 * e] = x.x;
+                    fa[2 * e + 1] = x.y;
+                    fb[2 * e] = y.x;
+                    fb[2 * e + 1] = y.y;
+                }
+#pragma unroll
+                for (int i = 0; i < QW; ++i) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[warp * QW + i][8 * c]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[warp * QW + i][8 * c + 4]);
+                    const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        s0[i] = fmaf(qv[e], fa[e], s0[i]);
+                        s1[i] = fmaf(qv[e], fb[e], s1[i]);
+                    }
+                }
             }
-        }
-        auto visible = [&](int key) {
-            bool vis = t < T && key <= slot0 + t;
-            if (mask && vis && key >= slot0) vis = (tmask >> (key - slot0)) & 1ull;
-            return vis;
-        };
-        const float v0 = visible(k0 + lane) ? s0 : -INFINITY;
-        const float v1 = visible(k0 + 32 + lane) ? s1 : -INFINITY;
-        __syncwarp();
-        const float mnew = fmaxf(m, warp_max(fmaxf(v0, v1)));
-        const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
-        const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
-        const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
-        l = l * corr + warp_sum(p0 + p1);
-        m = mnew;
-        ps[warp][lane] = p0;
-        ps[warp][lane + 32] = p1;
-        __syncwarp();
+            __syncwarp();
 #pragma unroll
-        for (int d = 0; d < DL; ++d) acc[d] *= corr;
-        const int nk = min(kTreeKeys, last + 1 - k0);              // keys of the tile that were copied
-#pragma unroll 8
-        for (int j = 0; j < nk; ++j) {
-            const float pj = ps[warp][j];
-            const uint8_t *vr = vs + j * L::kRow + lane * DL * 2;
-            if constexpr (DL == 4) {
-                const uint2 vv = *reinterpret_cast<const uint2 *>(vr);
-                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
-                acc[0] = fmaf(pj, a.x, acc[0]);
-                acc[1] = fmaf(pj, a.y, acc[1]);
-                acc[2] = fmaf(pj, b.x, acc[2]);
-                acc[3] = fmaf(pj, b.y, acc[3]);
-            } else {
-                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(vr));
-                acc[0] = fmaf(pj, a.x, acc[0]);
-                acc[1] = fmaf(pj, a.y, acc[1]);
+            for (int i = 0; i < QW; ++i) {
+                const int t = tw + i;
+                auto visible = [&](int key) {
+                    bool vis = t < T && key <= slot0 + t;
+                    if (mask && vis && key >= slot0) vis = (tmask[i] >> (key - slot0)) & 1ull;
+                    return vis;
+                };
+                const float v0 = visible(k0 + lane) ? s0[i] : -INFINITY;
+                const float v1 = visible(k0 + 32 + lane) ? s1[i] : -INFINITY;
+                const float mnew = fmaxf(m[i], warp_max(fmaxf(v0, v1)));
+                const float p0 = mnew == -INFINITY ? 0.f : expf(v0 - mnew);
+                const float p1 = mnew == -INFINITY ? 0.f : expf(v1 - mnew);
+                const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
+                l[i] = l[i] * corr + warp_sum(p0 + p1);
+                m[i] = mnew;
+                ps[warp * QW + i][lane] = p0;
+                ps[warp * QW + i][lane + 32] = p1;
+#pragma unroll
+                for (int d = 0; d < DL; ++d) acc[i][d] *= corr;
+            }
+            __syncwarp();
+            const int nk = min(kTreeKeys, wlast + 1 - k0);         // keys of the tile this warp may see
+#pragma unroll 4
+            for (int j = 0; j < nk; ++j) {
+                const uint8_t *vr = vs + j * L::kRow + lane * DL * 2;
+                float vf[DL];
+                if constexpr (DL == 4) {
+                    const uint2 vv = *reinterpret_cast<const uint2 *>(vr);
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                    vf[0] = a.x;
+                    vf[1] = a.y;
+                    vf[2] = b.x;
+                    vf[3] = b.y;
+                } else {
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(vr));
+                    vf[0] = a.x;
+                    vf[1] = a.y;
+                }
+#pragma unroll
+                for (int i = 0; i < QW; ++i) {
+                    const float pj = ps[warp * QW + i][j];
+#pragma unroll
+                    for (int d = 0; d < DL; ++d) acc[i][d] = fmaf(pj, vf[d], acc[i][d]);
+                }
             }
         }
         __syncthreads();                                           // the stage is rewritten two tiles on
     }
-    if (t < T) {
+#pragma unroll
+    for (int i = 0; i < QW; ++i) {
+        const int t = tw + i;
+        if (t >= T) continue;
 #pragma unroll
         for (int d = 0; d < DL; ++d) {
-            const float o = acc[d] / l;
+            const float o = acc[i][d] / l[i];
             const __half hv = __float2half_rn(o);
             const size_t idx = (size_t)t * nh * HD + h * HD + lane * DL + d;
             oh[idx] = hv;
@@ -401,7 +305,7 @@ __global__ void __launch_bounds__(128) k_attn_tree(__half *oh, __half *ol, const
 
 // Attention of a batched decode step: token b of request lanes[b] attends to slots [0, slot] of
 // its own cache. CTA = (kv head g, token b): the group's G = nh / nkv query heads share the K / V
-// tiles, which go through shared memory as in k_attn_tree (64 keys per tile, two in flight, padded
+// tiles, which go through shared memory as in k_attn_block (64 keys per tile, two in flight, padded
 // rows); warp w takes heads g G + w and g G + w + 4 (G <= 8). Output as fp16 hi / lo halves.
 constexpr int kBatchHeadsPerWarp = 2;
 template <int HD>
@@ -661,18 +565,23 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
                       s.q, kc, vc};
     e = launch_mcol(qkv, stream, true);
     if (e != cudaSuccess) return e;
-    if (T <= kTreeAttnMaxT) {
-        const dim3 grid(d.heads, (T + kTreeQ - 1) / kTreeQ);
+    if (T <= kShortBlockT) {
+        const dim3 grid(d.heads, (T + 3) / 4);
         if (d.head_dim == 128)
-            e = launch_pdl_smem(k_attn_tree<128>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
-                                kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+            e = launch_pdl_smem(k_attn_block<128, 1>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A,
+                                s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
         else
-            e = launch_pdl_smem(k_attn_tree<64>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A, s.q,
-                                kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+            e = launch_pdl_smem(k_attn_block<64, 1>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A,
+                                s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
     } else {
-        const dim3 grid(d.heads, (T + kAttnQ - 1) / kAttnQ);
-        e = launch_pdl(d.head_dim == 128 ? k_attn_prefill<128> : k_attn_prefill<64>, grid, 128, stream, s.xa,
-                       s.xa + lo * A, s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+        if (mask) return cudaErrorInvalidValue;                    // trees have at most 64 nodes
+        const dim3 grid(d.heads, (T + 15) / 16);
+        if (d.head_dim == 128)
+            e = launch_pdl_smem(k_attn_block<128, 4>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A,
+                                s.q, kc, vc, nullptr, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+        else
+            e = launch_pdl_smem(k_attn_block<64, 4>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A,
+                                s.q, kc, vc, nullptr, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
     }
     if (e != cudaSuccess) return e;
     // O projection into the residual stream

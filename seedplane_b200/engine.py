@@ -196,22 +196,27 @@ class CudaQwen2:
         t = torch.as_tensor(ids, dtype=torch.int32).flatten()
         return t.to(self.device, non_blocking=True)
 
-    def forward(self, kv: DeviceKV, ids, positions=None, all_logits: bool = False, want_logits: bool = True):
-        """Qwen2Engine.forward semantics: logits fp32 [n or 1, V] (or None) and argmax int32 [n]."""
+    def forward(self, kv: DeviceKV, ids, positions=None, all_logits: bool = False, want_logits: bool = True,
+                last_only: bool = False):
+        """Qwen2Engine.forward semantics: logits fp32 [n or 1, V] (or None) and argmax int32 [n].
+        `last_only`: the LM head for the last token alone (argmax int32 [1]); the others only fill
+        the cache."""
         tok = ids if (isinstance(ids, torch.Tensor) and ids.device == self.device and ids.dtype == torch.int32) \
             else self._ids(ids)
         n = int(tok.numel())
         pos = None if positions is None else self._ids(positions)
         if pos is not None and pos.numel() != n:
             raise ValueError("positions must match input_ids")
+        if last_only and all_logits:
+            raise ValueError("last_only excludes all_logits")
         logits = None
         if want_logits:
             logits = torch.empty((n if all_logits else 1, self.cfg.vocab), dtype=torch.float32, device=self.device)
-        argmax = torch.empty(n, dtype=torch.int32, device=self.device)
+        argmax = torch.empty(1 if last_only else n, dtype=torch.int32, device=self.device)
         N.check(N.load().sp_forward(self.handle, kv.handle, C.c_void_p(tok.data_ptr()),
                                     C.c_void_p(pos.data_ptr() if pos is not None else None), n,
                                     C.c_void_p(logits.data_ptr() if logits is not None else None),
-                                    int(all_logits), C.c_void_p(argmax.data_ptr()),
+                                    2 if last_only else int(all_logits), C.c_void_p(argmax.data_ptr()),
                                     C.c_void_p(_stream(self.device))))
         return logits, argmax
 

@@ -88,7 +88,7 @@ class GreedyExecutor:
         self.kv.length = 0
         if self.timer:
             self.timer(True)
-        _, am = self.engine.forward(self.kv, torch.tensor(ids, dtype=torch.int32), want_logits=False)
+        _, am = self.engine.forward(self.kv, torch.tensor(ids, dtype=torch.int32), want_logits=False, last_only=True)
         first = int(am[-1])
         tokens = [first]
         if n > 1:

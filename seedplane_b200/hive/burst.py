@@ -111,6 +111,9 @@ def burst_on_engine(eng, steps, warmup, world, rank, local, ClockSampler, max_ov
                 break
             if rounds > 200:
                 raise RuntimeError("warm-up could not measure every worker")
+        if batched:                             # the grouped path once (captures each GPU's batch graph)
+            for f in broker.submit_batch(payloads("warmup", rounds), group_per_worker=True, **kw):
+                f.result(timeout=600)
         shas, assigned, makespans = {}, {}, []
         with ClockSampler(list(range(world))) as clocks:
             for step in range(steps):

@@ -129,7 +129,7 @@ class WindowSession:
     def _forward(self, kv, ids: Sequence[int], positions: Sequence[int], slot: int, want_logits=False):
         kv.length = slot
         logits, am = self.engine.forward(kv, torch.tensor(list(ids), dtype=torch.int32),
-                                         positions=list(positions), want_logits=want_logits)
+                                         positions=list(positions), want_logits=want_logits, last_only=True)
         return logits, am
 
     def _copy(self, src, s0: int, dst, d0: int, n: int):

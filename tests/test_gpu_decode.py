@@ -240,3 +240,23 @@ def test_speculative_surface_verify_tree_and_commit(tiny):
             want, _ = o.greedy(prompt + emitted + [res.next_pred], 2, capacity=64)
         assert toks.cpu().tolist() == want
         kv.close()
+
+
+@pytest.mark.parametrize("n", [1, 5, 12, 70])
+def test_last_only_forward_gives_the_last_tokens_head(tiny, n):
+    """sp_forward with all_logits = 2 (the last token's LM head alone) gives the same logits and
+    argmax as the full forward's last row, through the step path (n < 8) and the batched pass."""
+    cfg, w, eng, o = tiny
+    prompt = random_prompt(cfg.vocab, n, seed=3)
+    kv1, kv2 = eng.new_kv(96), eng.new_kv(96)
+    try:
+        lg_all, am_all = eng.forward(kv1, prompt, all_logits=True)
+        lg, am = eng.forward(kv2, prompt, last_only=True)
+        assert am.numel() == 1 and int(am[0]) == int(am_all[-1])
+        assert_logits_close(lg[0], lg_all[-1], rel=1e-6)
+        assert kv2.length == n
+        want, _ = o.forward(prompt, o.new_cache(96))
+        assert_logits_close(lg[0], want[-1])
+    finally:
+        kv1.close()
+        kv2.close()

@@ -31,7 +31,7 @@ class FakeEngine:
     def new_kv(self, capacity):
         return FakeKV(capacity)
 
-    def forward(self, kv, ids, positions=None, want_logits=False):
+    def forward(self, kv, ids, positions=None, want_logits=False, last_only=False):
         ids = [int(t) for t in ids]
         del kv.cache[kv.length:]
         out = []
@@ -137,7 +137,7 @@ def test_decoder_flush_is_a_token_minus_one_emission():
     assert s.push(90) == "" and s.push(91) == "é" and s.flush() == ""
 
     class OpenChars(FakeEngine):        # every greedy token opens a character that never closes
-        def forward(self, kv, ids, positions=None, want_logits=False):
+        def forward(self, kv, ids, positions=None, want_logits=False, last_only=False):
             _, am = super().forward(kv, ids, positions, want_logits)
             return None, torch.full_like(am, 90)
 

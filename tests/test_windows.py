@@ -106,7 +106,7 @@ class FakeEngine:
         assert s0 + n <= src.capacity and d0 + n <= dst.capacity and None not in src.slots[s0:s0 + n]
         dst.slots[d0:d0 + n] = src.slots[s0:s0 + n]
 
-    def forward(self, kv, ids, positions=None, want_logits=False):
+    def forward(self, kv, ids, positions=None, want_logits=False, last_only=False):
         ids = [int(t) for t in ids]
         pos = list(positions) if positions is not None else list(range(kv.length, kv.length + len(ids)))
         self.calls.append(("forward", len(ids)))
