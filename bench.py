@@ -654,6 +654,80 @@ def run_speculative(args, world, rank, local):
             "clocks": clocks.summary()}
 
 
+def run_speculative_7b(args, world, rank, local):
+    """cfg5: greedy speculative decoding on the Qwen2.5-7B blockwise-int8 target after an 8,192-token
+    prompt, with a Qwen2-0.5B-shaped fp16 drafter (its own random init, the target's vocabulary)
+    proposing 32-node trees (branching 4, 2, 2, 1, 1, depth 5, kept by cumulative drafter
+    log-probability), 128 output tokens. `value` = output tokens per second of the loop (wall clock,
+    host included); the line also carries the device time of the 32-node verify passes at this
+    context, the accepted draft tokens per round (random weights: ~0, so this measures the loop, not
+    a speed-up), whether the tokens equal the target's own greedy decoding, and that decoding's rate
+    at the same context."""
+    from dataclasses import replace
+    from seedplane_b200.config import QWEN2_0_5B, QWEN2_5_7B
+    from seedplane_b200.engine import CudaQwen2
+    from seedplane_b200.randinit import make_int8_blockwise, make_weights, random_prompt
+    from seedplane_b200.speculative import speculative_generate
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = QWEN2_5_7B
+    w = make_int8_blockwise(cfg, seed=0, device=str(dev))
+    target = CudaQwen2(cfg, w, device=dev, weight_format="i8")
+    del w
+    dcfg = replace(QWEN2_0_5B, vocab=cfg.vocab, name="qwen2-0.5b-shaped-drafter")
+    dw = make_weights(dcfg, seed=1, dtype=torch.float16)
+    drafter = CudaQwen2(dcfg, dw, device=dev)
+    del dw
+    P, n_out, nodes, branching = 8192, 128, 32, (4, 2, 2, 1, 1)
+    prompt = random_prompt(cfg.vocab, P, seed=0)
+    cap = P + n_out + 8 * nodes
+    # the target's own greedy tokens, and its plain decode rate at this context
+    kv = target.new_kv(cap)
+    _, am = target.forward(kv, prompt, want_logits=False, last_only=True)
+    first = int(am[-1])
+    target.decode(kv, first, P, 8)                    # warm the step graph
+    kv.length = P
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rest, _ = target.decode(kv, first, P, n_out - 1)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    decode_ms = e0.elapsed_time(e1) / (n_out - 1)
+    greedy = [first] + rest.tolist()
+    kv.close()
+    speculative_generate(target, drafter, prompt, 8, branching=branching, max_nodes=nodes, capacity=cap)   # warm-up
+    torch.cuda.synchronize(dev)
+    with ClockSampler([local]) as clocks:
+        t0 = time.perf_counter()
+        toks, stats = speculative_generate(target, drafter, prompt, n_out, branching=branching, max_nodes=nodes,
+                                           capacity=cap)
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    target.status()
+    drafter.status()
+    target.close()
+    drafter.close()
+    if rank != 0:
+        return None
+    return {"metric": "Qwen2.5-7B int8 speculative greedy tok/s (32-node depth-5 tree verify, 0.5B-shaped drafter, "
+                      "8,192-token prompt)",
+            "value": n_out / wall, "unit": "tok/s", "n_gpus": 1, "steps": 1, "warmup": 1,
+            "ms_per_step": 1000 * wall, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": "cfg5: qwen2.5-7b blockwise-int8 target (random-init seed 0), qwen2-0.5b-shaped "
+                                   "fp16 drafter (seed 1, the target's vocabulary), 8,192-token prompt (prefill and "
+                                   "the drafter's prefill inside the timed loop), 32-node draft trees, 128 greedy "
+                                   "output tokens",
+                       "rounds": stats.rounds, "accepted_per_round": stats.accepted / max(1, stats.rounds),
+                       "verify_us_mean": 1000.0 * statistics.mean(stats.verify_ms),
+                       "verify_us_median": 1000.0 * statistics.median(stats.verify_ms),
+                       "tokens_equal_target_greedy": toks == greedy,
+                       "target_decode_ms_per_token_at_8k": decode_ms,
+                       "l2": "inputs larger than L2: 7.5 GB of int8 weights per decode step"},
+            "e2e": {"value": n_out / wall, "unit": "tok/s", "h2d_bytes_per_step": P * 4, "d2h_bytes_per_step": n_out * 4},
+            "clocks": clocks.summary()}
+
+
 def run_burst(args, world, rank, local):
     from seedplane_b200.hive.burst import run_burst_bench
     return run_burst_bench(args, world, rank, local, ClockSampler, max_over_ranks, barrier, peaks)
@@ -665,7 +739,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "decode-7b-i8", "burst", "verify", "speculative"),
+    ap.add_argument("--workload", choices=("decode", "decode-7b-i8", "burst", "verify", "speculative",
+                                           "speculative-7b-i8"),
                     default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-burst", action="store_true", help="leave the HIVE burst out of the decode line")
@@ -679,7 +754,8 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        run = {"burst": run_burst, "verify": run_verify, "speculative": run_speculative}.get(args.workload, run_decode)
+        run = {"burst": run_burst, "verify": run_verify, "speculative": run_speculative,
+               "speculative-7b-i8": run_speculative_7b}.get(args.workload, run_decode)
         line = run(args, world, rank, local)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)

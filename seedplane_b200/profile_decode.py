@@ -158,6 +158,82 @@ def trace_summary(eng, layers_shown=(0, 1, 13)):
     return {"step_span_us": round(total, 1), "kernels": out, "attention": attn}
 
 
+def tree_of(n: int, vocab: int, seed: int = 0, widths=(4, 2)):
+    """A draft tree of n nodes in breadth-first order (tokens, parents): every node of level d gets
+    widths[d] children (1 past the listed levels) until there are n nodes."""
+    import random
+    rng = random.Random(seed)
+    tokens, parents, level, d = [], [], [-1], 0
+    while len(tokens) < n:
+        w = widths[d] if d < len(widths) else 1
+        nxt = []
+        for par in level:
+            for _ in range(w):
+                if len(tokens) < n:
+                    tokens.append(rng.randrange(vocab))
+                    parents.append(par)
+                    nxt.append(len(tokens) - 1)
+        level, d = nxt, d + 1
+    return tokens, parents
+
+
+def prompt_passes(eng, prompt, repeat: int, capacity: int) -> dict:
+    """Prompt passes (device milliseconds per pass over `repeat` passes), then one more inside the
+    profiler range."""
+    kv = eng.new_kv(max(capacity, len(prompt)))
+    for _ in range(2):
+        kv.length = 0
+        eng.forward(kv, prompt, want_logits=False, last_only=True)
+    torch.cuda.synchronize()
+    ms = None
+    if repeat:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(repeat):
+            kv.length = 0
+            eng.forward(kv, prompt, want_logits=False, last_only=True)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / repeat
+    kv.length = 0
+    torch.cuda.cudart().cudaProfilerStart()
+    _, am = eng.forward(kv, prompt, want_logits=False, last_only=True)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    eng.status()
+    out = {"model": eng.cfg.name, "prompt": len(prompt), "prompt_pass_ms": ms, "argmax": int(am[-1])}
+    eng.close()
+    return out
+
+
+def verify_passes(eng, prompt, nodes: int, repeat: int, capacity: int) -> dict:
+    """Batched verify passes over an n-node tree after the prompt: device microseconds per pass
+    (CUDA events over `repeat` graph replays), then one more pass inside the profiler range."""
+    tokens, parents = tree_of(nodes, eng.cfg.vocab)
+    kv = eng.new_kv(capacity)
+    eng.forward(kv, prompt, want_logits=False, last_only=True)
+    for _ in range(3):
+        am, _ = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+    torch.cuda.synchronize()
+    us = None
+    if repeat:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(repeat):
+            eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) * 1000.0 / repeat
+    torch.cuda.cudart().cudaProfilerStart()
+    am, _ = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt))
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    eng.status()
+    out = {"model": eng.cfg.name, "prompt": len(prompt), "nodes": nodes, "verify_us": us, "argmax": am.cpu().tolist()}
+    eng.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model", default="qwen2-1.5b", choices=sorted(PRESETS))
@@ -172,6 +248,13 @@ def main():
     ap.add_argument("--step", default="step", help="comma list of step implementations: step (persistent), chain")
     ap.add_argument("--l2-kb", default="0", help="comma list: KB per CTA the step kernel warms L2 with ahead of its ring")
     ap.add_argument("--int8", action="store_true", help="blockwise-int8 random weights (drawn on the device)")
+    ap.add_argument("--verify", type=int, default=0,
+                    help="instead of decoding: after the prompt, `--repeat` + 1 batched verify passes of a tree of this "
+                         "many nodes (branching 4, 2, 1, 1, ... breadth first); the last pass runs between "
+                         "cudaProfilerStart / Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--prefill-pass", action="store_true",
+                    help="instead of decoding: `--repeat` + 1 prompt passes of `--prompt` tokens (the batched pass, "
+                         "last token's head only); the last runs between cudaProfilerStart / Stop")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
@@ -181,6 +264,12 @@ def main():
         w = make_weights(cfg, seed=0, dtype=torch.float16)
     fmt = "i8" if a.int8 else "f16"
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
+    if a.verify:
+        print(json.dumps(verify_passes(CudaQwen2(cfg, w, weight_format=fmt), prompt, a.verify, a.repeat, a.capacity)))
+        return
+    if a.prefill_pass:
+        print(json.dumps(prompt_passes(CudaQwen2(cfg, w, weight_format=fmt), prompt, a.repeat, a.capacity)))
+        return
     results = {}
     variants = [(m, pf, ev, sk, la) for sk in a.step.split(",") for m in a.modes.split(",")
                 for pf in a.prefetch_mb.split(",") for ev in a.evict_first.split(",") for la in a.l2_kb.split(",")]

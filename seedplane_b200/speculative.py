@@ -396,9 +396,9 @@ def speculative_generate(target, drafter, prompt: Sequence[int], n_new: int, bra
     import torch
     cap = capacity or len(prompt) + n_new + 8 * max_nodes
     tkv, dkv = target.new_kv(cap), drafter.new_kv(cap)
-    _, am = target.forward(tkv, list(prompt), want_logits=False)
+    _, am = target.forward(tkv, list(prompt), want_logits=False, last_only=True)
     root_pred = int(am[-1])
-    d_logits, _ = drafter.forward(dkv, list(prompt))
+    d_logits, _ = drafter.forward(dkv, list(prompt), last_only=True)
     d_root = d_logits[-1]
     out: List[int] = []
     stats = SpecStats()
@@ -427,7 +427,7 @@ def speculative_generate(target, drafter, prompt: Sequence[int], n_new: int, bra
             _, am = target.forward(tkv, [emitted[-1]], want_logits=False)
             root_pred = int(am[-1])
         dkv.length = base
-        d_logits, _ = drafter.forward(dkv, emitted)
+        d_logits, _ = drafter.forward(dkv, emitted, last_only=True)
         d_root = d_logits[-1]
         out.extend(emitted)
     tkv.close()
