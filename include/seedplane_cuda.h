@@ -125,6 +125,17 @@ int sp_decode(sp_engine *e, sp_kv *kv, int32_t token, int32_t pos, int32_t n_ste
 int sp_decode_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *tokens_host,
                     const int32_t *positions_host, int32_t n_steps, int32_t *out_tokens_dev, void *stream);
 
+/* The prompts of B independent requests in packed batched passes (runtime request batching; see
+ * sp_decode_batch): request b appends lens_host[b] tokens (tokens_dev holds the B prompts one after
+ * another) to its own cache kvs[b] at slots len .. len + lens_host[b] - 1, RoPE positions = the slots,
+ * every token attending to its own cache up to itself. argmax_dev[B]: the greedy token after each
+ * prompt's last token (the LM head runs for those rows only). Whole prompts are packed into passes
+ * of at most 512 tokens; a longer prompt runs alone through the chunked pass. 1 <= B <= 256,
+ * distinct caches of this engine. Advances every cache's length by its prompt's length. Replaces,
+ * for a batch, B prompt calls of sp_forward (Qwen2Engine.forward(prompt), qwen_engine.py:105-144). */
+int sp_prefill_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *tokens_dev, const int32_t *lens_host,
+                     int32_t *argmax_dev, void *stream);
+
 /* Speculative tree verification (no counterpart kernel in the reference; semantics of
  * seedplane/speculative.py:55-92). n nodes in an ancestor-closed order (parent index < own index;
  * -1 = child of the committed prefix). Node i is written to scratch slot len+i at RoPE position

@@ -21,7 +21,7 @@ SP_WEIGHTS_I8_B32 = 1
 # Every symbol the header declares (the CPU tests check the library exports all of them).
 EXPORTED = ("sp_last_error", "sp_version", "sp_engine_create", "sp_engine_destroy", "sp_engine_device_bytes",
             "sp_kv_create", "sp_kv_destroy", "sp_kv_length", "sp_kv_capacity", "sp_kv_set_length",
-            "sp_forward", "sp_decode", "sp_decode_batch", "sp_verify_tree", "sp_kv_commit", "sp_kv_copy", "sp_argmax", "sp_argmax_noalloc", "sp_mcol_gemm", "sp_topk",
+            "sp_forward", "sp_decode", "sp_decode_batch", "sp_prefill_batch", "sp_verify_tree", "sp_kv_commit", "sp_kv_copy", "sp_argmax", "sp_argmax_noalloc", "sp_mcol_gemm", "sp_topk",
             "sp_accept_stochastic", "sp_accept_greedy", "sp_sample_filter",
             "sp_device_status",
             "sp_trace_read")
@@ -75,6 +75,7 @@ def load(path: Path = LIB_PATH):
         "sp_forward": (C.c_int, [vp, vp, vp, vp, i32, vp, i32, vp, vp]),
         "sp_decode": (C.c_int, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "sp_decode_batch": (C.c_int, [vp, C.POINTER(vp), i32, pi32, pi32, i32, vp, vp]),
+        "sp_prefill_batch": (C.c_int, [vp, C.POINTER(vp), i32, vp, pi32, vp, vp]),
         "sp_verify_tree": (C.c_int, [vp, vp, pi32, pi32, i32, i32, vp, vp, vp]),
         "sp_kv_commit": (C.c_int, [vp, pi32, i32, vp]),
         "sp_kv_copy": (C.c_int, [vp, i32, vp, i32, i32, vp]),

@@ -7,9 +7,10 @@ batched pass per step over the batch's tokens, each reading and writing its own 
 weights stream from HBM once per step for all of them. Every request's tokens are its own greedy
 continuation, the same as decoding it alone.
 
-`generate_batch` prefills each request (the batched prompt pass), then decodes the batch in device
-blocks (each block's argmaxes are fed back on the GPU); after a block the host cuts each request
-at its stop token or length limit and drops finished requests from the batch.
+`generate_batch` packs the requests' prompts into batched passes (`sp_prefill_batch`: every token
+writes and reads its own request's cache), then decodes the batch in device blocks (each block's
+argmaxes are fed back on the GPU); after a block the host cuts each request at its stop token or
+length limit and drops finished requests from the batch.
 """
 from __future__ import annotations
 
@@ -18,6 +19,7 @@ from typing import Iterable, List, Optional, Sequence
 import torch
 
 MAX_BATCH = 64                          # requests per sp_decode_batch call
+MAX_PREFILL_BATCH = 256                 # prompts per sp_prefill_batch call
 
 
 def generate_batch(engine, prompts: Sequence[Sequence[int]], max_new_tokens, stop: Iterable[int] = (),
@@ -45,10 +47,10 @@ def generate_batch(engine, prompts: Sequence[Sequence[int]], max_new_tokens, sto
         if timer:
             timer(True)
         firsts = []
-        for p, kv in zip(prompts, kvs):
+        for kv in kvs[:n_req]:
             kv.length = 0
-            _, am = engine.forward(kv, torch.tensor(p, dtype=torch.int32), want_logits=False, last_only=True)
-            firsts.append(am[-1:])
+        for c0 in range(0, n_req, MAX_PREFILL_BATCH):      # the prompts packed into batched passes
+            firsts.append(engine.prefill_batch(kvs[c0:c0 + MAX_PREFILL_BATCH], prompts[c0:c0 + MAX_PREFILL_BATCH]))
         out = [[t] for t in torch.cat(firsts).cpu().tolist()]
         done = [o[0] in stops or m == 1 for o, m in zip(out, limits)]
         while True:

@@ -66,6 +66,15 @@ struct BatchIn {
     int32_t out[kBatchMax];
 };
 
+// Inputs of one packed pass of several requests' prompts (sp_prefill_batch): every token's lane
+// (its request's cache and slot) and position, and the rows of the prompts' last tokens.
+constexpr int kPrefillBatchMax = 256;      // requests per sp_prefill_batch call
+struct PrefillBatchIn {
+    BatchLane lanes[kPrefillMaxTokens];
+    int32_t pos[kPrefillMaxTokens];
+    int32_t last[kPrefillMaxTokens];
+};
+
 struct LayerDev {
     const uint8_t *qkv, *o, *gate_up, *down;       // fragment-packed fp16, contiguous in the stream
     const float *qkv_b, *in_norm, *post_norm;
@@ -162,6 +171,7 @@ struct sp_engine {
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
     int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
     BatchIn *bt = nullptr;                  // batched decode inputs
+    PrefillBatchIn *bp = nullptr;           // packed prompt pass inputs
     int32_t *last_only_buf = nullptr;       // sp_forward(all_logits = 2) through the step path: per-step argmaxes
     int32_t last_only_cap = 0;
     std::map<int, cudaGraphExec_t> bgraphs; // batched decode step per batch size
@@ -1095,6 +1105,7 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->gr_buf);
     for (auto &g : e->bgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->bt);
+    cudaFree(e->bp);
     cudaFree(e->last_only_buf);
     delete e;
 }
@@ -1403,6 +1414,100 @@ int sp_decode_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *t
                                 cudaMemcpyDeviceToDevice, s));
     }
     for (int b = 0; b < B; ++b) kvs[b]->length += n_steps;
+    return SP_OK;
+}
+
+// One packed pass: requests [r0, r1) whose prompts are the tokens [off, off + T) of tokens_dev.
+static int prefill_pack(sp_engine *e, sp_kv *const *kvs, const int32_t *lens, int r0, int r1, const int32_t *tokens_dev,
+                        int64_t off, int T, int32_t *argmax_dev, cudaStream_t s) {
+    const sp_config &c = e->c;
+    PrefillBatchIn in;
+    int t = 0;
+    for (int r = r0; r < r1; ++r) {
+        sp_kv *kv = kvs[r];
+        for (int i = 0; i < lens[r]; ++i, ++t) {
+            in.lanes[t] = BatchLane{kv->k, kv->v, kv->capacity, kv->length + i};
+            in.pos[t] = kv->length + i;
+        }
+        in.last[r - r0] = t - 1;
+    }
+    // only the filled part of the struct goes over (the lanes, positions and rows in use)
+    SP_CUDA(cudaMemcpyAsync(e->bp->lanes, in.lanes, (size_t)T * sizeof(BatchLane), cudaMemcpyHostToDevice, s));
+    SP_CUDA(cudaMemcpyAsync(e->bp->pos, in.pos, (size_t)T * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    SP_CUDA(cudaMemcpyAsync(e->bp->last, in.last, (size_t)(r1 - r0) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    const float scale = 1.0f / sqrtf((float)c.head_dim);
+    SP_CUDA(launch_prefill_embed(e->pf_dims, e->pf, e->embed, tokens_dev + off, T, e->st, s));
+    for (int l = 0; l < c.layers; ++l) {
+        const PrefillLayer &L = e->layers[l].pf;
+        SP_CUDA(launch_batch_layer_front(e->pf_dims, L, e->pf, T, e->bp->pos, e->bp->lanes, l, scale, e->rope, e->st, s));
+        SP_CUDA(launch_prefill_layer_ffn(e->pf_dims, L, e->pf, T, e->st, s));
+    }
+    // the prompts' last rows, gathered: the LM head and argmax for them alone
+    PrefillScratch g = e->pf;
+    g.x = e->pf.q;                         // free after the last layer's attention
+    const int n = r1 - r0;
+    SP_CUDA(launch_gather_rows(reinterpret_cast<uint8_t *>(g.x), reinterpret_cast<const uint8_t *>(e->pf.x), e->bp->last,
+                               n, c.hidden * 4, 1, 0, s));
+    for (int b0 = 0; b0 < n; b0 += kPrefillLogitRows) {
+        const int rows = std::min(kPrefillLogitRows, n - b0);
+        SP_CUDA(launch_prefill_logits(e->pf_dims, g, e->final_norm, e->head_pf, b0, rows, e->pf.logits, e->st, s));
+        SP_CUDA(launch_argmax_rows(e->pf.logits, rows, c.vocab, c.vocab, argmax_dev + r0 + b0, e->am, s));
+    }
+    for (int r = r0; r < r1; ++r) kvs[r]->length += lens[r];
+    return SP_OK;
+}
+
+int sp_prefill_batch(sp_engine *e, sp_kv *const *kvs, int32_t B, const int32_t *tokens_dev, const int32_t *lens_host,
+                     int32_t *argmax_dev, void *stream) {
+    if (!e) return fail(SP_ERR_INVALID, "null engine");
+    if (!kvs || !tokens_dev || !lens_host || !argmax_dev) return fail(SP_ERR_INVALID, "null argument");
+    if (B <= 0 || B > kPrefillBatchMax) return fail(SP_ERR_CAPACITY, "batch of %d prompts (1..%d)", B, kPrefillBatchMax);
+    if (!e->prefill) return fail(SP_ERR_UNSUPPORTED, "packed prompts need the batched pass (SEEDPLANE_PREFILL=steps)");
+    for (int b = 0; b < B; ++b) {
+        sp_kv *kv = kvs[b];
+        if (!kv || kv->e != e) return fail(SP_ERR_INVALID, "request %d: null cache or a cache of another engine", b);
+        for (int j = 0; j < b; ++j)
+            if (kvs[j] == kv) return fail(SP_ERR_INVALID, "request %d: cache shared with request %d", b, j);
+        if (lens_host[b] <= 0) return fail(SP_ERR_INVALID, "request %d: empty prompt", b);
+        if (kv->length + lens_host[b] > kv->capacity)
+            return fail(SP_ERR_CAPACITY, "request %d: KV cache capacity %d exceeded", b, kv->capacity);
+        if (kv->length + lens_host[b] > e->c.max_positions)
+            return fail(SP_ERR_CAPACITY, "request %d: positions outside the RoPE table", b);
+    }
+    SP_CUDA(cudaSetDevice(e->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (!e->bp) SP_CUDA(cudaMalloc(&e->bp, sizeof(PrefillBatchIn)));
+    // pack whole prompts into passes of at most kPrefillMaxTokens tokens; a longer prompt runs alone
+    int64_t off = 0, pack_off = 0;
+    int r0 = 0, T = 0;
+    for (int b = 0; b <= B; ++b) {
+        const int len = b < B ? lens_host[b] : 0;
+        if (b == B || T + len > kPrefillMaxTokens) {
+            if (T > 0) {
+                int rc = prefill_pack(e, kvs, lens_host, r0, b, tokens_dev, pack_off, T, argmax_dev, s);
+                if (rc) return rc;
+            }
+            r0 = b;
+            pack_off = off;
+            T = 0;
+        }
+        if (b == B) break;
+        if (len > kPrefillMaxTokens) {                  // alone, through the chunked pass
+            sp_kv *kv = kvs[b];
+            const int32_t base = kv->length;
+            SP_CUDA(cudaMemcpyAsync(&e->vt->slot0, &base, sizeof(base), cudaMemcpyHostToDevice, s));
+            int rc = forward_batched(e, kv, tokens_dev + off, nullptr, nullptr, &e->vt->slot0, len, nullptr, false,
+                                     argmax_dev + b, s, true);
+            if (rc) return rc;
+            kv->length += len;
+            off += len;
+            r0 = b + 1;
+            pack_off = off;
+            continue;
+        }
+        T += len;
+        off += len;
+    }
     return SP_OK;
 }
 

@@ -244,6 +244,18 @@ class CudaQwen2:
                                          int(n_steps), C.c_void_p(out.data_ptr()), C.c_void_p(_stream(self.device))))
         return out
 
+    def prefill_batch(self, kvs: Sequence[DeviceKV], prompts: Sequence[Sequence[int]]) -> torch.Tensor:
+        """The prompts of len(kvs) requests in packed batched passes (`sp_prefill_batch`): prompt b is
+        appended to kvs[b]; returns the greedy token after each prompt, int32 [B]."""
+        B = len(kvs)
+        flat = torch.tensor([int(t) for p in prompts for t in p], dtype=torch.int32).to(self.device, non_blocking=True)
+        out = torch.empty(B, dtype=torch.int32, device=self.device)
+        handles = (C.c_void_p * B)(*[kv.handle for kv in kvs])
+        N.check(N.load().sp_prefill_batch(self.handle, handles, B, C.c_void_p(flat.data_ptr()),
+                                          N.int_array([len(p) for p in prompts]), C.c_void_p(out.data_ptr()),
+                                          C.c_void_p(_stream(self.device))))
+        return out
+
     def verify_tree(self, kv: DeviceKV, tokens: Sequence[int], parents: Sequence[int], base_pos: int,
                     want_logits: bool = False):
         """One batched pass over a draft tree; returns (argmax int32 [n], logits [n, V] or None)."""

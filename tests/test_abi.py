@@ -45,6 +45,8 @@ def test_null_arguments_are_rejected_with_messages(lib):
     assert lib.sp_kv_set_length(None, 0) == N.SP_ERR_INVALID
     assert lib.sp_kv_commit(None, None, 0, None) == N.SP_ERR_INVALID
     assert lib.sp_kv_copy(None, 0, None, 0, 1, None) == N.SP_ERR_INVALID
+    assert lib.sp_decode_batch(None, None, 1, None, None, 1, None, None) == N.SP_ERR_INVALID
+    assert lib.sp_prefill_batch(None, None, 1, None, None, None, None) == N.SP_ERR_INVALID
     assert lib.sp_device_status(None, None) == N.SP_ERR_INVALID
     assert lib.sp_argmax(None, None, 1, 1, 1, None, None) == N.SP_ERR_INVALID
     assert lib.sp_argmax_noalloc(0, None, 1, 1, 1, None, None) == N.SP_ERR_INVALID

@@ -94,6 +94,29 @@ def test_more_requests_than_one_pass_and_decode_batch_rows(tiny):
             kv.close()
 
 
+def test_packed_prompts_match_prompts_alone(tiny):
+    """sp_prefill_batch packs whole prompts into passes of at most 512 tokens (a longer prompt runs
+    alone); each request's first token and K/V equal its own prompt pass: the decode that follows
+    gives the same tokens."""
+    eng, cfg, w = tiny
+    lens = [1, 7, 130, 3, 200, 90, 500, 17, 64]            # 130 + 200 + 90 > 512: several packs; 500 alone
+    prompts = [random_prompt(cfg.vocab, n, seed=300 + i) for i, n in enumerate(lens)]
+    kvs = [eng.new_kv(n + 8) for n in lens]
+    try:
+        firsts = eng.prefill_batch(kvs, prompts).cpu().tolist()
+        assert [kv.length for kv in kvs] == lens
+        for p, kv, f in zip(prompts, kvs, firsts):
+            want = _alone(eng, p, 6)
+            assert f == want[0]
+            out, _ = eng.decode(kv, f, len(p), 5)
+            assert [f] + out.cpu().tolist() == want
+        with pytest.raises(Exception):
+            eng.prefill_batch([kvs[0], kvs[0]], [[1], [2]])           # one cache twice
+    finally:
+        for kv in kvs:
+            kv.close()
+
+
 def test_bad_batches_are_rejected(tiny):
     eng, cfg, w = tiny
     a, b = eng.new_kv(8), eng.new_kv(8)
@@ -121,10 +144,10 @@ def test_qwen2_0_5b_batch_gives_the_reference_tokens(golden_dir):
     w = make_weights(QWEN2_0_5B, seed=0, dtype=torch.float16)
     eng = CudaQwen2(QWEN2_0_5B, w)
     try:
-        prompts = [random_prompt(QWEN2_0_5B.vocab, n, seed=7 + n) for n in (17, 90, 3, 128)]
+        prompts = [random_prompt(QWEN2_0_5B.vocab, n, seed=7 + n) for n in (17, 90, 3, 128, 600)]
         got = generate_batch(eng, [gold["prompt"]] + prompts, 32)
         assert got[0] == gold["fp16_weights"]["tokens"]
-        for p, g in zip(prompts, got[1:]):
+        for p, g in zip(prompts, got[1:]):                  # the 600-token prompt runs alone (> 512)
             assert g == _alone(eng, p, 32)
     finally:
         eng.close()
@@ -132,10 +155,12 @@ def test_qwen2_0_5b_batch_gives_the_reference_tokens(golden_dir):
 
 def test_qwen2_1_5b_burst_batch_matches_requests_alone_or_the_oracle():
     """The cfg4 burst: 16 requests (prompts 32..128 tokens) x 32 tokens as one batch on the
-    Qwen2-1.5B shape. Each request's tokens equal the same request decoded alone (the step kernel);
-    where the two paths part (their fp32 sums differ in order), the oracle decides: up to the parting
-    token both equal the oracle, and there the oracle's two best logits are a near-tie (margin
-    < 1e-3) between exactly the two paths' tokens."""
+    Qwen2-1.5B shape (the prompts packed into batched passes, then batched decode steps). Each
+    request's tokens equal the same request decoded alone (its own prompt pass, then the step
+    kernel), except where the two paths part because their fp32 sums differ in order (random-init
+    weights leave the two best logits very close): there the oracle decides, up to the parting token
+    both equal the oracle, and at it the oracle's two best logits are a near-tie (margin < 1e-3)
+    between exactly the two paths' tokens."""
     from seedplane_b200.batch import generate_batch
     from seedplane_b200.engine import CudaQwen2
     w = make_weights(QWEN2_1_5B, seed=0, dtype=torch.float16)
@@ -147,7 +172,7 @@ def test_qwen2_1_5b_burst_batch_matches_requests_alone_or_the_oracle():
     finally:
         eng.close()
     parted = [i for i in range(16) if got[i] != alone[i]]
-    assert len(parted) <= 2, parted
+    assert len(parted) <= 4, parted
     if parted:
         oracle = OracleQwen2(QWEN2_1_5B, w, kv_fp16=True)
         for i in parted:
