@@ -177,6 +177,38 @@ def tree_of(n: int, vocab: int, seed: int = 0, widths=(4, 2)):
     return tokens, parents
 
 
+def batch_steps(eng, B: int, repeat: int) -> dict:
+    """B requests (the burst's prompt lengths) prefilled together, then batched decode steps: device
+    milliseconds per step over `repeat` steps, then one more inside the profiler range."""
+    from .randinit import burst_prompts
+    prompts = burst_prompts(eng.cfg.vocab, B, 32, 128, seed=0)
+    kvs = [eng.new_kv(len(p) + repeat + 8) for p in prompts]
+    first = eng.prefill_batch(kvs, prompts).cpu().tolist()
+    pos = [len(p) for p in prompts]
+    out = eng.decode_batch(kvs, first, pos, 2)               # captures the step's graph
+    toks, pos = out[-1].cpu().tolist(), [q + 2 for q in pos]
+    torch.cuda.synchronize()
+    ms = None
+    if repeat:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = eng.decode_batch(kvs, toks, pos, repeat)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / repeat
+        toks, pos = out[-1].cpu().tolist(), [q + repeat for q in pos]
+    torch.cuda.cudart().cudaProfilerStart()
+    out = eng.decode_batch(kvs, toks, pos, 1)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    eng.status()
+    for kv in kvs:
+        kv.close()
+    res = {"model": eng.cfg.name, "requests": B, "decode_step_ms": ms, "tokens": out[-1].cpu().tolist()}
+    eng.close()
+    return res
+
+
 def prompt_passes(eng, prompt, repeat: int, capacity: int) -> dict:
     """Prompt passes (device milliseconds per pass over `repeat` passes), then one more inside the
     profiler range."""
@@ -255,6 +287,10 @@ def main():
     ap.add_argument("--prefill-pass", action="store_true",
                     help="instead of decoding: `--repeat` + 1 prompt passes of `--prompt` tokens (the batched pass, "
                          "last token's head only); the last runs between cudaProfilerStart / Stop")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="instead of decoding one request: this many requests (prompts of 32..128 tokens, packed "
+                         "into batched passes), then `--repeat` batched decode steps (sp_decode_batch) and one more "
+                         "between cudaProfilerStart / Stop")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
@@ -266,6 +302,9 @@ def main():
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
     if a.verify:
         print(json.dumps(verify_passes(CudaQwen2(cfg, w, weight_format=fmt), prompt, a.verify, a.repeat, a.capacity)))
+        return
+    if a.batch:
+        print(json.dumps(batch_steps(CudaQwen2(cfg, w, weight_format=fmt), a.batch, a.repeat)))
         return
     if a.prefill_pass:
         print(json.dumps(prompt_passes(CudaQwen2(cfg, w, weight_format=fmt), prompt, a.repeat, a.capacity)))
