@@ -35,7 +35,9 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "kernels.cuh"
 #include "tc.cuh"
@@ -515,19 +517,27 @@ int sm_count() {
     return n;
 }
 
+// The kernel's dynamic shared-memory limit, raised once per device.
 template <int MODE>
-cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &x, const McolParams &p,
-                        int grid, size_t smem, cudaStream_t s, bool pdl) {
+cudaError_t set_max_smem(int dev) {
     static std::atomic<unsigned long long> configured{0};       // one bit per device
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(configured.load() & bit)) {
-        e = cudaFuncSetAttribute(k_mcol<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mcol_max_smem());
+        cudaError_t e = cudaFuncSetAttribute(k_mcol<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mcol_max_smem());
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
+    return cudaSuccess;
+}
+
+template <int MODE>
+cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &x, const McolParams &p,
+                        int grid, size_t smem, cudaStream_t s, bool pdl) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = set_max_smem<MODE>(dev);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kMcThreads);
@@ -550,6 +560,47 @@ cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUten
     cfg.attrs = attr;
     cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, k_mcol<MODE>, a, a2, x, p);
+}
+
+// Clusters of cs CTAs of k_mcol<mode> with `smem` bytes of dynamic shared memory that can be resident
+// at once on this device (cudaOccupancyMaxActiveClusters), cached per (device, mode, cs, smem).
+int max_active_clusters(int mode, int cs, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, size_t>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const auto key = std::make_tuple(dev, mode, cs, smem);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs * kPrefillMaxCtas);
+    cfg.blockDim = dim3(kMcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cudaError_t e = cudaSuccess;
+    switch (mode) {
+        case MC_STORE: e = set_max_smem<MC_STORE>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_STORE>, &cfg); break;
+        case MC_RESID: e = set_max_smem<MC_RESID>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_RESID>, &cfg); break;
+        case MC_SWIGLU: e = set_max_smem<MC_SWIGLU>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_SWIGLU>, &cfg); break;
+        default: e = set_max_smem<MC_QKV>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_QKV>, &cfg); break;
+    }
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;                                  // unknown: no cluster split
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = n;
+    return n;
 }
 
 }  // namespace
@@ -595,13 +646,16 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     const long long tiles = mtiles * ntiles;
     const long long kbe = (long long)((op.K + kBK - 1) / kBK) * (op.w_lo ? 2 : 1);
     // Whole tiles when they keep at least half the SMs busy; else the largest cluster (<= 8 CTAs, <= the
-    // tile's k-blocks) whose tiles x cluster CTAs fit the SMs in one wave splits each tile's k-blocks.
+    // tile's k-blocks) whose tiles x cluster CTAs fit the SMs in one wave splits each tile's k-blocks:
+    // the clusters must all be resident at once (a cluster's CTAs share one GPC, so fewer clusters
+    // of 8 fit than 148 / 8), which the occupancy query of the launch says.
     const int C = std::min(sm_count(), op.max_ctas);
     static const int cs_cap = std::max(1, std::min(kMcMaxCluster, env_int("SEEDPLANE_MCOL_CLUSTER", kMcMaxCluster)));
+    const size_t smem = (size_t)p.stages * stage_bytes + 1024;
     p.cs = 1;
     if (2 * tiles <= C)
         for (int cs = cs_cap; cs >= 2; cs /= 2)
-            if (tiles * cs <= C && cs <= kbe) {
+            if (tiles * cs <= C && cs <= kbe && tiles <= max_active_clusters(op.mode, cs, smem)) {
                 p.cs = cs;
                 break;
             }
@@ -611,7 +665,6 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     if (e == cudaSuccess) e = map_rows(&a2, op.w_lo ? op.w_lo : op.w, op.N, op.K, kBM);
     if (e == cudaSuccess) e = map_rows(&x, op.x, op.x_rows, op.K, p.tn);
     if (e != cudaSuccess) return e;
-    const size_t smem = (size_t)p.stages * stage_bytes + 1024;
     switch (op.mode) {
         case MC_STORE: return launch_mode<MC_STORE>(a, a2, x, p, grid, smem, s, pdl);
         case MC_RESID: return launch_mode<MC_RESID>(a, a2, x, p, grid, smem, s, pdl);
