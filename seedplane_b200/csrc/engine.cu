@@ -9,6 +9,7 @@
 // pre-recorded one-token command buffer (native/vulkan_decode/qwen_vk.cpp:349-412) and its
 // per-token submit + fence wait (qwen_vk.cpp:141-147, 519-565).
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstdarg>
@@ -137,6 +138,7 @@ struct sp_engine {
     StepOp s_qkv{}, s_o{}, s_gu{}, s_down{}, s_head{};     // planned step GEMVs (row blocks)
     StepLayout step_lay{};                  // shared memory of the step kernel
     int step_xmax = 0, step_max_chunks = 0;
+    int step_group_chunks = 0, step_group_ctx = 0, step_part_stride = 0;   // grouped attention items
     int step_inflight = 0;                  // ring copies in flight at most (0: all stages)
     int step_l2_ahead = 0;                  // bytes per CTA prefetched into L2 ahead of the ring
     unsigned long long *cnt = nullptr;      // dependency counters [5 * layers]
@@ -159,7 +161,7 @@ struct sp_engine {
     GemvParams g_qkv{}, g_o{}, g_gu{}, g_down{}, g_head{};
     TcGemvParams t_qkv{}, t_o{}, t_gu{}, t_down{}, t_head{};
     cudaStream_t cap_stream = nullptr;
-    std::map<sp_kv *, cudaGraphExec_t> graphs;
+    std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> graphs;   // step per (cache, grouped attention)
     // batched prompt pass (prefill.cu); off with SEEDPLANE_PREFILL=steps
     bool prefill = false;
     PrefillDims pf_dims{};
@@ -244,7 +246,7 @@ std::vector<StepOp> build_step_ops(const sp_engine *e, const sp_kv *kv) {
     const size_t kv_layer = (size_t)c.kv_heads * kv->capacity * c.head_dim;
     const size_t H = c.hidden, I = c.intermediate, HD = c.head_dim;
     const size_t nq = (size_t)c.heads * HD, nkv = (size_t)c.kv_heads * HD;
-    const size_t npart = (size_t)c.heads * e->step_max_chunks * (HD + 2);
+    const size_t npart = (size_t)c.heads * e->step_part_stride * (HD + 2);
     std::vector<StepOp> ops;
     // split-GEMV partials, per layer parity: kMaxKsplit - 1 regions of N words for each op kind
     const size_t ksp_o = 0, ksp_down = ksp_o + (kMaxKsplit - 1) * (size_t)e->s_o.N;
@@ -351,7 +353,8 @@ int ensure_step_ops(sp_engine *e, sp_kv *kv, StepOp **out) {
     return SP_OK;
 }
 
-int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
+// grouped: the step kernel's grouped attention items (one per kv head and chunk)
+int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s, bool grouped) {
     const sp_config &c = e->c;
     if (e->step_kernel) {
         StepOp *ops = nullptr;
@@ -372,6 +375,8 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.vocab = c.vocab;
         p.hidden = c.hidden;
         p.max_chunks = e->step_max_chunks;
+        p.group_chunks = e->step_group_chunks;
+        p.part_stride = e->step_part_stride;
         p.evict_first = e->evict_first ? 1 : 0;
         p.max_inflight = e->step_inflight;
         p.l2_ahead = e->step_l2_ahead;
@@ -386,7 +391,8 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
         p.epoch = e->epoch;
         p.st = e->st;
         p.trace = e->step_trace;
-        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_lay.smem, s, e->pdl, e->c.weight_format == SP_WEIGHTS_I8_B32));
+        SP_CUDA(launch_step(c.head_dim, p, e->num_sms, e->step_lay.smem, s, e->pdl,
+                            e->c.weight_format == SP_WEIGHTS_I8_B32, grouped));
         return SP_OK;
     }
     int kidx = 0;       // GEMV index within the step (trace slot)
@@ -462,15 +468,16 @@ int record_step(sp_engine *e, sp_kv *kv, cudaStream_t s) {
     return SP_OK;
 }
 
-int get_graph(sp_engine *e, sp_kv *kv, cudaGraphExec_t *out) {
-    auto it = e->graphs.find(kv);
+int get_graph(sp_engine *e, sp_kv *kv, bool grouped, cudaGraphExec_t *out) {
+    const auto key = std::make_pair(kv, grouped ? 1 : 0);
+    auto it = e->graphs.find(key);
     if (it != e->graphs.end()) {
         *out = it->second;
         return SP_OK;
     }
     cudaGraph_t g = nullptr;
     SP_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
-    int rc = record_step(e, kv, e->cap_stream);
+    int rc = record_step(e, kv, e->cap_stream, grouped);
     cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
     if (rc != SP_OK) {
         if (g) cudaGraphDestroy(g);
@@ -481,7 +488,7 @@ int get_graph(sp_engine *e, sp_kv *kv, cudaGraphExec_t *out) {
     ce = cudaGraphInstantiate(&ex, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return fail(SP_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
-    e->graphs[kv] = ex;
+    e->graphs[key] = ex;
     *out = ex;
     return SP_OK;
 }
@@ -493,14 +500,16 @@ int run_steps(sp_engine *e, sp_kv *kv, const DevState &init, int n, cudaStream_t
         if (rc != SP_OK) return rc;
     }
     SP_CUDA(launch_set_state(e->st, init, s));
+    // the first step's visible context decides the attention items of the whole block
+    const bool grouped = e->step_kernel && (long)init.slot + 1 >= (long)e->step_group_ctx;
     if (e->use_graph) {
         cudaGraphExec_t ex;
-        int rc = get_graph(e, kv, &ex);
+        int rc = get_graph(e, kv, grouped, &ex);
         if (rc != SP_OK) return rc;
         for (int i = 0; i < n; ++i) SP_CUDA(cudaGraphLaunch(ex, s));
     } else {
         for (int i = 0; i < n; ++i) {
-            int rc = record_step(e, kv, s);
+            int rc = record_step(e, kv, s, grouped);
             if (rc != SP_OK) return rc;
         }
     }
@@ -964,12 +973,25 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
     // e.g. to exercise many sub-chunks per item at small contexts)
     const int chunk_cap = (int)std::max(1L, env_long("SEEDPLANE_ATTN_MAX_CHUNKS", kStepMaxChunks));
     e->step_max_chunks = std::min({kStepMaxChunks, chunk_cap, e->num_sms / c.heads});
+    // grouped items (one per kv head and chunk, all q heads of the group at once) from
+    // SEEDPLANE_ATTN_GROUP_CTX visible positions on (0: always; a value above every context: never)
+    // chunks: as many as leave one CTA per q head free for the merges (which then poll while the
+    // items run instead of after them), SEEDPLANE_ATTN_GROUP_CHUNKS at most
+    const int group_cap = (int)std::max(1L, env_long("SEEDPLANE_ATTN_GROUP_CHUNKS", kStepMaxChunks));
+    const int group_fit = e->num_sms - c.heads >= c.kv_heads ? (e->num_sms - c.heads) / c.kv_heads
+                                                             : e->num_sms / c.kv_heads;
+    e->step_group_chunks = std::max(1, std::min({kStepMaxChunks, group_cap, group_fit}));
+    // default: grouped items when the per-head items get fewer than 8 chunks per head (long
+    // contexts then leave each per-head item hundreds of positions: 28 q heads on 148 SMs)
+    const long group_dflt = e->num_sms / c.heads < 8 ? 0L : (long)kStepGroupCtx;
+    e->step_group_ctx = (int)std::max(0L, std::min<long>(INT_MAX, env_long("SEEDPLANE_ATTN_GROUP_CTX", group_dflt)));
+    e->step_part_stride = std::max(e->step_max_chunks, e->step_group_chunks);
     const size_t w_cnt = wtake((size_t)e->n_cnt * 8), w_epoch = wtake(8);
     const size_t w_scnt = wtake(std::max<size_t>(n_strips, 1) * 4);
     const size_t w_lmcnt = wtake(4);
     const size_t w_am = wtake(argmax_scratch_bytes(kArgmaxChunkRows));
     // step hand-off words (a step after a device error must not see tags of the failed one)
-    const size_t n_part = (size_t)c.heads * e->step_max_chunks * (HD + 2);
+    const size_t n_part = (size_t)c.heads * e->step_part_stride * (HD + 2);
     const size_t w_llxo = wtake(2 * H * 8), w_llxd = wtake(2 * H * 8);
     const size_t w_llq = wtake(2 * (size_t)c.heads * HD * 8), w_llkv = wtake(2 * (size_t)c.kv_heads * HD * 8);
     const size_t w_llpart = wtake(2 * n_part * 8), w_llattn = wtake(2 * (size_t)c.heads * HD * 8);
@@ -1059,7 +1081,8 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         SP_TRY(prepare_gemv_tc(PRO_NORM, EPI_LMHEAD, e->t_head));
     }
     if (e->step_kernel) {
-        if (e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms)
+        if (e->step_max_chunks < 1 || c.heads * e->step_max_chunks > e->num_sms ||
+            c.kv_heads * e->step_group_chunks > e->num_sms)
             return bail(fail(SP_ERR_UNSUPPORTED, "step kernel: %d q heads do not fit one attention item per CTA",
                              c.heads));
         SP_TRY(prepare_step((int)HD, e->step_lay.smem, i8));
@@ -1143,10 +1166,13 @@ void sp_kv_destroy(sp_kv *kv) {
     if (kv->e) {
         sp_engine *e = kv->e;
         cudaSetDevice(e->device);
-        auto it = e->graphs.find(kv);
-        if (it != e->graphs.end()) {
-            cudaGraphExecDestroy(it->second);
-            e->graphs.erase(it);
+        for (auto g = e->graphs.begin(); g != e->graphs.end();) {
+            if (g->first.first == kv) {
+                cudaGraphExecDestroy(g->second);
+                g = e->graphs.erase(g);
+            } else {
+                ++g;
+            }
         }
         auto so = e->step_ops.find(kv);
         if (so != e->step_ops.end()) {

@@ -170,6 +170,7 @@ enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged attention output
 constexpr int kStepAttnRows = 48;        // attention positions staged per sub-chunk
 constexpr int kStepMaxChunks = 64;       // attention chunks per q head
+constexpr int kStepGroupCtx = 1 << 30;   // a context no step reaches: grouped attention items off
 constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
 constexpr int kStepTraceWords = 16;      // per op and CTA: [0..7] %globaltimer: reached, dep met, input
                                          // ready, done, first unit available, rows finished, merge
@@ -231,6 +232,8 @@ struct StepParams {
     int attn_off;            // attention staging offset in it (after the QKV projection's input)
     int nh, nkv, hd, cap, max_pos, vocab, hidden;
     int max_chunks;          // attention chunks per q head at most (nh * max_chunks <= grid)
+    int group_chunks;        // grouped items: chunks per kv head at most (nkv * group_chunks <= grid)
+    int part_stride;         // attention partial slots per q head (>= both chunk counts)
     int evict_first;         // ring copies carry an L2 evict-first hint
     int max_inflight;        // ring copies in flight at most (0: stages)
     int l2_ahead;            // bytes of its next units a CTA prefetches into L2 while its ring is full
@@ -269,10 +272,12 @@ size_t step_attn_smem_bytes(int hd);
 // xmax: the largest GEMV input (multiple of 8); hidden: the QKV projection's input; i8: inputs
 // of int8 matrices are digit rows (see digitize4_n in step.cu).
 StepLayout step_layout(int hidden, int xmax, int hd, int stages, bool i8);
-cudaError_t prepare_step(int hd, size_t smem, bool q8);   // q8: the build with the int8 unit path
+cudaError_t prepare_step(int hd, size_t smem, bool q8);   // q8: the builds with the int8 unit path
 // pdl: programmatic dependent launch after the previous kernel in the stream; the grid must be
 // resident at once (one CTA per SM), so the launch is cooperative.
-cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8);
+// grouped: the build with grouped attention items (one per kv head and chunk) instead of per-head ones
+cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8,
+                        bool grouped);
 
 // ---- batched prompt pass: prefill.cu ------------------------------------------------------------
 // T prompt tokens per chunk through all layers at once: the multi-column tcgen05 GEMM (mcol.cu)

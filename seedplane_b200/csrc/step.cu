@@ -37,6 +37,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "tc.cuh"
@@ -56,6 +57,7 @@ constexpr int kUnitBlocksI8 = 32;           // int8 32-input blocks per unit: 8 
 constexpr uint32_t kStepTmemCols = 2 * 8 * kUnitBlocksI8;   // two unit buffers
 static_assert(kPassRowsI8 <= 4 * kPassRows, "int8 pass rows go through red[]");
 constexpr int kGroup = 8;                   // q heads per kv head at most
+constexpr int kGroupTileRows = 32;          // grouped attention items: positions per chunk at least
 constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
 constexpr int kLLBatch = 7;                 // LL word pairs per thread in flight (plain prologues, merge)
 constexpr int kMergeBatch = 32;            // attention chunks merged per batch (staged in shared memory)
@@ -842,7 +844,7 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     }
     stamp(p.trace, k, gridDim.x, blockIdx.x, 4);
     stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
-    uint64_t *pw = op.lpart + ((size_t)h * p.max_chunks + ch) * (HD + 2);
+    uint64_t *pw = op.lpart + ((size_t)h * p.part_stride + ch) * (HD + 2);
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
     if (tid < HD) ll_st1(pw + 2 + tid, ll_wordf(acc, tag));
     if (tid == 32) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
@@ -861,7 +863,7 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
     constexpr int kW = HD + 2;                  // words per chunk
     const int tid = threadIdx.x;
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
-    const uint64_t *base = op.lpart + (size_t)h * p.max_chunks * kW;
+    const uint64_t *base = op.lpart + (size_t)h * p.part_stride * kW;
     static_assert((size_t)kMergeBatch * kW * 4 <= L::sOff, "a merge batch fits the K/V staging rows");
     float *mp = reinterpret_cast<float *>(am + L::kOff);
     float M = -INFINITY, Ls = 0.f, A = 0.f;
@@ -906,6 +908,267 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
         epi_sync();                             // the staging rows are reused by the next batch
     }
     if (tid < HD) ll_st1(op.lout + (size_t)h * HD + tid, ll_word(hilo_bits(A / Ls), tag));
+}
+
+// ---- grouped attention item: (kv head g, context chunk ch), all G <= 8 q heads of the group -----
+// The K/V rows of a chunk are read from HBM once for the whole group (the per-head items read them
+// once per q head) and the products run on the tensor cores, with fp32-grade sums:
+//   scores  S (16 x 8 positions) = Q (16 x HD) K^T, mma.sync m16n8k16: A row r < 8 = fp16 hi of
+//           q_r * scale, row 8 + r = its fp16 lo (q - hi); B = the K rows. Score of head r =
+//           D[r] + D[8 + r].
+//   values  O (16 x HD) += P (16 x 8 positions) V, mma.sync m16n8k8: A row r = fp16 hi of the
+//           head's probabilities, row 8 + r = their lo; B = the V rows transposed with movmatrix.
+//           Output of head r = O[r] + O[8 + r].
+// All four warps walk all tiles of 8 positions: each computes the same scores and softmax (the
+// same instructions on the same operands: the same bits) and the values for its quarter of the
+// output dims, so a thread holds 16 accumulators, not 64, and the item needs no cross-warp merge:
+// every warp publishes its dims of the partial directly. The contraction index is permuted so that
+// thread (row g, quad t) reads whole 16-byte pieces of the K row of position g: pieces t, t + 4, ...
+// (8 dims each; the quad reads 64 contiguous bytes per load). Its j-th dim is dim
+// 32 (j / 8) + 8 t + j % 8 of the row, and logical k = 16 kk + 2 t + 8 h + e is its dim
+// j = 4 kk + 2 h + e, in q and in K alike; output n-tile nn, column 2 t + e is its dim 2 nn + e,
+// so warp w reads V in the pieces of its dims. K/V go straight from global memory (L2) into
+// registers, D tiles in flight while one computes (the first ones issued before q is polled); no
+// shared-memory staging and no barriers inside the loop. The item publishes one partial
+// (max, sum, acc[HD]) per q head in the per-head items' format, so the same merge follows.
+template <int HD>
+struct GroupRegion {
+    static constexpr size_t qOff = 0;                                    // q [8][HD] fp32 (scaled)
+    static constexpr size_t sOff = qOff + (size_t)kGroup * HD * 4;       // own K / V row [2][HD] fp16
+    static constexpr size_t fOff = sOff + (size_t)2 * HD * 2;            // q fragments [HD / 16][32] uint4
+    static constexpr size_t bytes = fOff + (size_t)HD / 16 * 32 * 16;
+};
+static_assert(GroupRegion<64>::bytes <= AttnRegion<64>::bytes && GroupRegion<128>::bytes <= AttnRegion<128>::bytes,
+              "grouped items use the per-head items' staging region");
+
+// D (16x8 fp32) += A (16x8 fp16, row-major) * B (8x8 fp16, column-major)
+SP_DEVINL void mma_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0));
+}
+// 8x8 fp16 transpose across the warp (lane 4 r + t holds elements (r, 2t), (r, 2t + 1))
+SP_DEVINL uint32_t movmatrix_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+SP_DEVINL uint32_t pack_half2(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// L2 prefetch of [src, src + bytes) (16-byte aligned, bytes a multiple of 16)
+SP_DEVINL void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Chunk ch = item % n_chunks of kv head g = item / n_chunks: positions [j0, j1) of that head's rows.
+struct GroupRows {
+    const __half *kb, *vb;
+    int g, ch, j0, j1;
+};
+template <int HD>
+SP_DEVINL GroupRows group_rows(const StepParams &p, const StepOp &op, int item, int n_chunks, int rows_per, int ctx) {
+    GroupRows r;
+    r.g = item / n_chunks;
+    r.ch = item - r.g * n_chunks;
+    r.kb = op.kc + (size_t)r.g * p.cap * HD;
+    r.vb = op.vc + (size_t)r.g * p.cap * HD;
+    r.j0 = r.ch * rows_per;
+    r.j1 = min(ctx, r.j0 + rows_per);
+    return r;
+}
+
+// The item's K and V rows other than the step's own, into L2 while the QKV projection runs.
+template <int HD>
+SP_DEVINL void group_prefetch(const GroupRows &r, int slot) {
+    constexpr uint32_t kPiece = 4096;
+    const int hi = min(r.j1, slot);
+    if (hi <= r.j0) return;
+    const uint32_t bytes = (uint32_t)(hi - r.j0) * HD * 2, n = (bytes + kPiece - 1) / kPiece;
+    for (uint32_t i = threadIdx.x; i < 2 * n; i += kEpiThreads) {
+        const uint32_t piece = i % n, off = piece * kPiece;
+        const __half *base = (i < n ? r.kb : r.vb) + (size_t)r.j0 * HD;
+        bulk_prefetch_l2(reinterpret_cast<const uint8_t *>(base) + off, min(kPiece, bytes - off));
+    }
+}
+
+template <int HD>
+__device__ __noinline__ void group_attention(const StepParams &p, const StepOp &op, int item, int n_chunks, int rows_per,
+                                             int ctx, int slot, int tree_base, unsigned long long mask, uint32_t qtag,
+                                             uint32_t tag, uint8_t *am, const Abort ab, int k) {
+    using L = GroupRegion<HD>;
+    const GroupRows gr = group_rows<HD>(p, op, item, n_chunks, rows_per, ctx);
+    const int G = p.nh / p.nkv;
+    const int j0 = gr.j0, j1 = gr.j1;
+    const __half *kb = gr.kb, *vb = gr.vb;
+    constexpr int KS = HD / 16;             // k-steps of a score MMA
+    constexpr int KP = HD / 32;             // 16-byte K pieces of a thread per row
+    constexpr int NW = HD / 32;             // output n-tiles of a warp (= V words of a thread per row)
+    constexpr int D = 1;                    // K / V tiles in flight per warp beyond the current one
+                                            // (deeper pipelines spill: measured slower)
+    using VW = typename std::conditional<NW == 4, uint4, uint2>::type;
+    static_assert(NW == 4 || NW == 2, "HD 64 or 128");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+    float *qs = reinterpret_cast<float *>(am + L::qOff);
+    __half *srow = reinterpret_cast<__half *>(am + L::sOff);
+    const bool has_slot = slot >= j0 && slot < j1;
+    const int ntiles = max(0, (j1 - j0 + 7) / 8);
+    // warp w's output dims are the threads' dims 2 NW w .. 2 NW (w + 1) - 1: at this row offset
+    const int jw = 2 * NW * warp;
+    const int voff = 32 * (jw >> 3) + 8 * tq + (jw & 7);
+    // row of position gq of tile t (past the chunk: a valid row, masked)
+    const auto row_at = [&](int t) { return (size_t)min(j0 + 8 * t + gq, j1 - 1) * HD; };
+    uint4 kq[D][KP];
+    VW vq[D];
+    const auto load = [&](int t, uint4 (&kr)[KP], VW &vr) {
+        const size_t r = row_at(t);
+#pragma unroll
+        for (int i = 0; i < KP; ++i) kr[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + r + 32 * i + 8 * tq));
+        vr = __ldcg(reinterpret_cast<const VW *>(vb + r + voff));
+    };
+    // the first tiles go in flight before q is polled (the step's own row is replaced later)
+#pragma unroll
+    for (int u = 0; u < D; ++u)
+        if (u < ntiles) load(u, kq[u], vq[u]);
+    {
+        // q of the group's heads (rows G.. are zero) and, when the chunk holds the step's position,
+        // its K / V row; word pairs: q first (8 HD / 2), then K / V (HD / 2)
+        constexpr int QP = kGroup * HD / 2, NPAIR = QP + HD / 2;
+        constexpr int NP = (NPAIR + kEpiThreads - 1) / kEpiThreads;
+        const uint64_t *lq = op.lin + (size_t)gr.g * G * HD, *lkv = op.lkv + (size_t)gr.g * HD;
+        uint64_t w[NP][2];
+        uint32_t valid = 0u;
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+            const int i = tid + j * kEpiThreads;
+            if (i < QP ? 2 * i < G * HD : (i < NPAIR && has_slot)) valid |= 1u << j;
+        }
+        const auto addr = [&](int j) {
+            const int i = tid + j * kEpiThreads;
+            return i < QP ? lq + 2 * i : lkv + 2 * (i - QP);
+        };
+        // one tag: q and the K / V rows come from the same QKV projection
+        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 0);
+        if (!ll_poll<NP>(w, valid, addr, qtag, ab)) valid = 0u;
+        stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
+        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 1);
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+            const int i = tid + j * kEpiThreads;
+            if (i < QP) {
+                const bool v = (valid >> j) & 1u;
+                qs[2 * i] = v ? ll_f(w[j][0]) * p.scale : 0.f;
+                qs[2 * i + 1] = v ? ll_f(w[j][1]) * p.scale : 0.f;
+            } else if ((valid >> j) & 1u) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {     // word = (dim dd, dim dd + HD / 2) of K (which 0) or V
+                    const int wi = 2 * (i - QP) + e, which = wi / (HD / 2), dd = wi - which * (HD / 2);
+                    const uint32_t u = (uint32_t)w[j][e];
+                    srow[which * HD + dd] = __ushort_as_half((unsigned short)(u & 0xffffu));
+                    srow[which * HD + dd + HD / 2] = __ushort_as_half((unsigned short)(u >> 16));
+                }
+            }
+        }
+    }
+    epi_sync();
+    // q fragments of lane l: row l / 4 hi / lo at its dims 4 kk + {0, 1} (columns 2 (l % 4) + {0, 1})
+    // and 4 kk + {2, 3}; the same for every warp, built once into [kk][lane] uint4
+    uint4 *qf = reinterpret_cast<uint4 *>(am + L::fOff);
+    for (int i = tid; i < KS * 32; i += kEpiThreads) {
+        const int kk = i >> 5, l = i & 31;
+        const float4 x = *reinterpret_cast<const float4 *>(qs + (l >> 2) * HD + 32 * (kk >> 1) + 8 * (l & 3) + 4 * (kk & 1));
+        const __half h0 = __float2half_rn(x.x), h1 = __float2half_rn(x.y), h2 = __float2half_rn(x.z),
+                     h3 = __float2half_rn(x.w);
+        qf[i] = make_uint4(pack_half2(h0, h1),
+                           pack_half2(__float2half_rn(x.x - __half2float(h0)), __float2half_rn(x.y - __half2float(h1))),
+                           pack_half2(h2, h3),
+                           pack_half2(__float2half_rn(x.z - __half2float(h2)), __float2half_rn(x.w - __half2float(h3))));
+    }
+    epi_sync();
+    stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 2);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 3);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 4);
+    float o[NW][4];
+#pragma unroll
+    for (int n = 0; n < NW; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_run = -INFINITY, l_part = 0.f;  // head gq (m quad-uniform; l this thread's positions)
+    const auto tile = [&](int t, uint4 (&kc)[KP], VW &vc) {
+        const int a = j0 + 8 * t;
+        const bool own = a + gq == slot;    // the step's own row: from the QKV projection's words
+        if (own) {
+#pragma unroll
+            for (int i = 0; i < KP; ++i) kc[i] = *reinterpret_cast<const uint4 *>(srow + 32 * i + 8 * tq);
+            vc = *reinterpret_cast<const VW *>(srow + HD + voff);
+        }
+        const uint32_t *kw = reinterpret_cast<const uint32_t *>(kc);
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};   // even / odd k-steps
+#pragma unroll
+        for (int kk = 0; kk < KS; kk += 2) {
+            const uint4 f0 = qf[kk * 32 + lane], f1 = qf[(kk + 1) * 32 + lane];
+            mma_16816(sa, f0.x, f0.y, f0.z, f0.w, kw[2 * kk], kw[2 * kk + 1]);
+            mma_16816(sb, f1.x, f1.y, f1.z, f1.w, kw[2 * kk + 2], kw[2 * kk + 3]);
+        }
+        // positions a + 2 tq, a + 2 tq + 1
+        float s0 = (sa[0] + sb[0]) + (sa[2] + sb[2]), s1 = (sa[1] + sb[1]) + (sa[3] + sb[3]);
+        const auto vis = [&](int jj) {
+            if (jj >= j1) return false;
+            const int d = jj - tree_base;
+            return !(d >= 0 && (d >= 64 || !((mask >> d) & 1ull)));
+        };
+        if (!vis(a + 2 * tq)) s0 = -INFINITY;
+        if (!vis(a + 2 * tq + 1)) s1 = -INFINITY;
+        float mt = fmaxf(s0, s1);
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+        const float mn = fmaxf(m_run, mt);
+        const float corr = m_run == -INFINITY ? 0.f : expf(m_run - mn);
+        const float e0 = s0 == -INFINITY ? 0.f : expf(s0 - mn), e1 = s1 == -INFINITY ? 0.f : expf(s1 - mn);
+        l_part = fmaf(l_part, corr, e0 + e1);
+        m_run = mn;
+        const __half p0 = __float2half_rn(e0), p1 = __float2half_rn(e1);
+        const uint32_t pa0 = pack_half2(p0, p1);
+        const uint32_t pa1 = pack_half2(__float2half_rn(e0 - __half2float(p0)), __float2half_rn(e1 - __half2float(p1)));
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(&vc);
+#pragma unroll
+        for (int n = 0; n < NW; ++n) {
+            o[n][0] *= corr;
+            o[n][1] *= corr;
+            o[n][2] *= corr;
+            o[n][3] *= corr;
+            mma_1688(o[n], pa0, pa1, movmatrix_t(vw[n]));
+        }
+    };
+    for (int t0 = 0; t0 < ntiles; t0 += D) {
+#pragma unroll
+        for (int u = 0; u < D; ++u) {
+            const int t = t0 + u;
+            if (t < ntiles) {               // uniform
+                uint4 kc[KP];
+#pragma unroll
+                for (int i = 0; i < KP; ++i) kc[i] = kq[u][i];
+                VW vc = vq[u];
+                if (t + D < ntiles) load(t + D, kq[u], vq[u]);
+                tile(t, kc, vc);
+            }
+        }
+    }
+    stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
+    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
+    // this warp's dims of the partial of head gq: thread dims jw + 2 n + e
+    float l = l_part + __shfl_xor_sync(0xffffffffu, l_part, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (gq < G) {
+        uint64_t *pw = op.lpart + ((size_t)(gr.g * G + gq) * p.part_stride + gr.ch) * (HD + 2);
+#pragma unroll
+        for (int n = 0; n < NW; ++n) {
+            const int j = jw + 2 * n;
+            uint64_t *q = pw + 2 + 32 * (j >> 3) + 8 * tq + (j & 7);
+            ll_st2(q, ll_wordf(o[n][0] + o[n][2], tag), ll_wordf(o[n][1] + o[n][3], tag));
+        }
+        if (warp == 0 && tq == 0) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l, tag));
+    }
+    epi_sync();                             // the region is reused by the merge
 }
 
 // The LM head's argmax across CTAs (last arriver) and the device state of the next step; once
@@ -1041,7 +1304,7 @@ struct UnitCursor {
 
 // Q8: the build with the blockwise-int8 unit path (a separate instantiation, so the fp16-only
 // kernel keeps its register allocation).
-template <int HD, bool Q8>
+template <int HD, bool Q8, bool GR>
 __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ float s_val[4];
@@ -1183,8 +1446,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             ss.token = 0;
         }
         const int ctx = min(ss.slot + 1, p.cap);
-        const int n_chunks = attn_chunks(ctx, p.max_chunks);
+        // attention items: per (q head, chunk), or (GR) per (kv head, chunk)
+        const int n_chunks = GR ? max(1, min(p.group_chunks, (ctx + kGroupTileRows - 1) / kGroupTileRows))
+                                : attn_chunks(ctx, p.max_chunks);
         const int rows_per = (ctx + n_chunks - 1) / n_chunks;
+        const int n_items = (GR ? p.nkv : p.nh) * n_chunks;
         const int half_hd = HD / 2;
         int s = 0, round = 0, consumed = 0;       // ring position of the compute warps
 
@@ -1198,9 +1464,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             cp_async_commit();
             stamp(p.trace, k, C, c, 0);
             const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
-            if (op.kind == OP_ATTN) {
+            if (GR && op.kind == OP_ATTN) {
+                // items on the last CTAs, one per CTA; head h's merge on the CTA before them (or on
+                // the CTA of item h, after its item, when the grid has no room)
+                const int item = C - 1 - c;
+                if (item < n_items && !ab.on()) {
+                    group_attention<HD>(p, op, item, n_chunks, rows_per, ctx, ss.slot, ss.tree_base, ss.mask,
+                                        ll_tag(ss.epoch, p.n_ops, op.lin_k), tag, am, ab, k);
+                    stamp(p.trace, k, C, c, 4);
+                }
+                const int h = n_items + p.nh <= C ? C - 1 - n_items - c : item;
+                if (h >= 0 && h < p.nh && !ab.on()) {
+                    stamp(p.trace, k, C, c, 6);
+                    stamp_clk(p.trace, k, C, c, 6);
+                    merge_head<HD>(p, op, ss, am, h, n_chunks, k, ab);
+                    stamp(p.trace, k, C, c, 7);
+                    stamp_clk(p.trace, k, C, c, 7);
+                }
+                stamp(p.trace, k, C, c, 3);
+                continue;
+            }
+            if (!GR && op.kind == OP_ATTN) {
                 // items on the last CTAs: (q head, context chunk), one per CTA
-                const int items = p.nh * n_chunks, item = C - 1 - c;
+                const int items = n_items, item = C - 1 - c;
                 if (item < items && !ab.on()) {
                     attention_item<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx, ab, k);
                     const int h = item / n_chunks;
@@ -1218,7 +1504,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             if (op.epi == EPI_QKV) {
                 // this CTA's attention item of the layer: stage its immutable K/V rows now
                 const int item = C - 1 - c;
-                if (item < p.nh * n_chunks) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
+                if (item < n_items) {
+                    if constexpr (GR)
+                        group_prefetch<HD>(group_rows<HD>(p, op, item, n_chunks, rows_per, ctx), ss.slot);
+                    else
+                        attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
+                }
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             stamp_clk(p.trace, k, C, c, 0);
@@ -1751,12 +2042,12 @@ cudaError_t launch_pack_rows_i8(uint8_t *dst, const int8_t *a, const __half *as,
     return cudaGetLastError();
 }
 
-template <int HD, bool Q8>
+template <int HD, bool Q8, bool GR>
 static cudaError_t step_launch_t(const StepParams *p, int grid, size_t smem, cudaStream_t s, bool pdl) {
     if (p == nullptr) {
-        cudaError_t e = cudaFuncSetAttribute(k_step<HD, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_step<HD, Q8, GR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        return cudaFuncSetAttribute(k_step<HD, Q8>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        return cudaFuncSetAttribute(k_step<HD, Q8, GR>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     (int)cudaSharedmemCarveoutMaxShared);
     }
     cudaLaunchConfig_t cfg = {};
@@ -1776,27 +2067,39 @@ static cudaError_t step_launch_t(const StepParams *p, int grid, size_t smem, cud
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, k_step<HD, Q8>, *p);
+    return cudaLaunchKernelEx(&cfg, k_step<HD, Q8, GR>, *p);
 }
 
-template <bool Q8>
+template <bool Q8, bool GR>
 static cudaError_t step_launch_hd(int hd, const StepParams *p, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    if (hd == 128) return step_launch_t<128, Q8>(p, grid, smem, s, pdl);
-    if (hd == 64) return step_launch_t<64, Q8>(p, grid, smem, s, pdl);
+    if (hd == 128) return step_launch_t<128, Q8, GR>(p, grid, smem, s, pdl);
+    if (hd == 64) return step_launch_t<64, Q8, GR>(p, grid, smem, s, pdl);
     return cudaErrorInvalidValue;
 }
 
 cudaError_t prepare_step(int hd, size_t smem, bool q8) {
-    return q8 ? step_launch_hd<true>(hd, nullptr, 0, smem, nullptr, false)
-              : step_launch_hd<false>(hd, nullptr, 0, smem, nullptr, false);
+    for (const bool gr : {false, true}) {
+        const cudaError_t e = q8 ? (gr ? step_launch_hd<true, true>(hd, nullptr, 0, smem, nullptr, false)
+                                       : step_launch_hd<true, false>(hd, nullptr, 0, smem, nullptr, false))
+                                 : (gr ? step_launch_hd<false, true>(hd, nullptr, 0, smem, nullptr, false)
+                                       : step_launch_hd<false, false>(hd, nullptr, 0, smem, nullptr, false));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
-cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8) {
+cudaError_t launch_step(int hd, const StepParams &p, int grid, size_t smem, cudaStream_t s, bool pdl, bool q8,
+                        bool grouped) {
     if (p.stages < 2 || p.stage_bytes < 1024 || p.stage_bytes % 1024 || p.stage_bytes > kMaxStageBytes ||
         p.nh / p.nkv > kGroup || p.nh * p.max_chunks > grid || p.max_chunks > kStepMaxChunks || p.attn_off % 128 ||
+        p.group_chunks < 1 || p.nkv * p.group_chunks > grid || p.group_chunks > kStepMaxChunks ||
+        p.part_stride < std::max(p.max_chunks, p.group_chunks) ||
         p.vec_bytes % 128 || (size_t)p.attn_off + step_attn_smem_bytes(hd) > (size_t)p.vec_bytes)
         return cudaErrorInvalidValue;
-    return q8 ? step_launch_hd<true>(hd, &p, grid, smem, s, pdl) : step_launch_hd<false>(hd, &p, grid, smem, s, pdl);
+    if (q8) return grouped ? step_launch_hd<true, true>(hd, &p, grid, smem, s, pdl)
+                           : step_launch_hd<true, false>(hd, &p, grid, smem, s, pdl);
+    return grouped ? step_launch_hd<false, true>(hd, &p, grid, smem, s, pdl)
+                   : step_launch_hd<false, false>(hd, &p, grid, smem, s, pdl);
 }
 
 }  // namespace sp

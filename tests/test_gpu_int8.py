@@ -152,26 +152,31 @@ def test_int8_prompt_through_step_kernel_matches_batched(monkeypatch):
 
 
 @pytest.mark.slow
-def test_int8_7b_shape_long_context_decode():
+def test_int8_7b_shape_long_context_decode(monkeypatch):
     """cfg5's long context on the 7B int8 shape (hidden 3584, 28 q / 4 kv heads, untied int8 LM
     head), truncated to one layer so the CPU oracle finishes: a 4,100-token prompt, then 8 greedy
     step-kernel tokens at contexts 4,100-4,107 with the attention items the kernel picks itself
-    (no chunk cap: 28 heads x 5 chunks of ~820 positions, many sub-chunks per item). Tokens equal
-    the oracle's; the last step's logits within the int8 tolerance."""
+    (no chunk cap), once with per-head items (28 heads x 5 chunks of ~820 positions, many
+    sub-chunks per item) and once with grouped items (4 kv heads x 37 chunks, all 7 q heads of a
+    group on the tensor cores). Tokens equal the oracle's; the last step's logits within the int8
+    tolerance."""
     from dataclasses import replace
     from seedplane_b200.config import QWEN2_5_7B
     from seedplane_b200.engine import CudaQwen2
     cfg = replace(QWEN2_5_7B, layers=1, max_positions=8192, name="qwen2.5-7b-1l")
     w = make_int8_blockwise(cfg, seed=0, std=0.02)
     prompt = random_prompt(cfg.vocab, 4100, seed=0)
-    eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
-    kv = eng.new_kv(4160)
-    _, argmax = eng.forward(kv, prompt, want_logits=False)
-    first = int(argmax[-1])
-    toks, logits = eng.decode(kv, first, len(prompt), 8, want_logits=True)
-    got = [first] + toks.cpu().tolist()
-    eng.status()
-    eng.close()
+    runs = []
+    for group_ctx in (str(1 << 30), "0"):
+        monkeypatch.setenv("SEEDPLANE_ATTN_GROUP_CTX", group_ctx)
+        eng = CudaQwen2(cfg, w, device="cuda:0", weight_format="i8")
+        kv = eng.new_kv(4160)
+        _, argmax = eng.forward(kv, prompt, want_logits=False)
+        first = int(argmax[-1])
+        toks, logits = eng.decode(kv, first, len(prompt), 8, want_logits=True)
+        runs.append(([first] + toks.cpu().tolist(), logits.float().cpu()))
+        eng.status()
+        eng.close()
     o = OracleQwen2(cfg, w, kv_fp16=True)
     del w
     cache = o.new_cache(4160)
@@ -184,5 +189,6 @@ def test_int8_7b_shape_long_context_decode():
         if i < 7:
             want.append(int(lg[-1].argmax()))
     # the engine's last step produced the logits after token got[7] (= want[7] when all match)
-    assert got[:8] == want[:8], (got, want, margins)
-    assert_logits_close(logits, lg[-1])
+    for got, logits in runs:
+        assert got[:8] == want[:8], (got, want, margins)
+        assert_logits_close(logits, lg[-1])
