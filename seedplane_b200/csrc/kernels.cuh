@@ -170,7 +170,6 @@ enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 constexpr int PRO_ATTN = 3;              // O-projection prologue: the merged attention output
 constexpr int kStepAttnRows = 48;        // attention positions staged per sub-chunk
 constexpr int kStepMaxChunks = 64;       // attention chunks per q head
-constexpr int kStepGroupCtx = 1 << 30;   // a context no step reaches: grouped attention items off
 constexpr int kStepPassRows = 64;        // GEMV rows per pass (16 per compute warp)
 constexpr int kStepTraceWords = 16;      // per op and CTA: [0..7] %globaltimer: reached, dep met, input
                                          // ready, done, first unit available, rows finished, merge

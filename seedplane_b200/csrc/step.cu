@@ -57,7 +57,7 @@ constexpr int kUnitBlocksI8 = 32;           // int8 32-input blocks per unit: 8 
 constexpr uint32_t kStepTmemCols = 2 * 8 * kUnitBlocksI8;   // two unit buffers
 static_assert(kPassRowsI8 <= 4 * kPassRows, "int8 pass rows go through red[]");
 constexpr int kGroup = 8;                   // q heads per kv head at most
-constexpr int kGroupTileRows = 32;          // grouped attention items: positions per chunk at least
+constexpr int kGroupTileRows = 64;          // grouped attention items: positions per chunk at least
 constexpr int kNormRegs = 8;                // float4s per thread in the RMSNorm prologue: K <= 4096
 constexpr int kLLBatch = 7;                 // LL word pairs per thread in flight (plain prologues, merge)
 constexpr int kMergeBatch = 32;            // attention chunks merged per batch (staged in shared memory)
@@ -588,6 +588,13 @@ SP_DEVINL void stamp(unsigned long long *tr, int k, int C, int c, int i) {
 SP_DEVINL void stamp_clk(unsigned long long *tr, int k, int C, int c, int i) {
     if (tr && threadIdx.x == 0) tr[((size_t)k * C + c) * kStepTraceWords + 8 + i] = clock64();
 }
+// The same two from the calling thread (the attention warps' first thread)
+SP_DEVINL void stamp_lead(unsigned long long *tr, int k, int C, int c, int i) {
+    if (tr) tr[((size_t)k * C + c) * kStepTraceWords + i] = globaltimer();
+}
+SP_DEVINL void stamp_clk_lead(unsigned long long *tr, int k, int C, int c, int i) {
+    if (tr) tr[((size_t)k * C + c) * kStepTraceWords + 8 + i] = clock64();
+}
 
 // One int8 pass (rows_p rows, all K inputs in units of chunk_w) on the 5th-generation tensor cores,
 // pipelined: lane 0 of each compute warp issues its share of unit u + 1's block MMAs (TMEM buffer
@@ -850,67 +857,91 @@ __device__ void attention_item(const StepParams &p, const StepOp &op, const Step
     if (tid == 32) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l_run, tag));
 }
 
-// The chunk-0 item of q head h merges the head's chunks: out[d] = sum_c w_c acc_c[d] with
+// A merge CTA folds q head h's chunks: out[d] = sum_c w_c acc_c[d] with
 // w_c = exp(m_c - M) / sum_c l_c exp(m_c - M), chunks in a fixed order. In batches of up to
-// kMergeBatch chunks, all epilogue threads poll the batch's LL words (max, sum, acc[HD] per
-// chunk; one round trip) into the free K staging rows, then thread d < HD folds the batch into a
-// running (M, sum, acc[d]). The output goes out as LL words whose payload is the fp16 hi / lo pair
-// the O projection multiplies.
-template <int HD>
+// kMergeBatch chunks, the NTH threads of the group (thread index t, their barrier) poll the batch's
+// LL words (max, sum, acc[HD] per chunk; one round trip) into the free K staging rows, then the
+// thread of output d folds the batch into a running (M, sum, acc[d]). The output goes out as LL
+// words whose payload is the fp16 hi / lo pair the O projection multiplies.
+template <int NTH>
+SP_DEVINL void group_sync() {
+    if constexpr (NTH == kEpiThreads)
+        epi_sync();
+    else
+        asm volatile("bar.sync 2, %0;" ::"n"(NTH) : "memory");
+}
+// NB: word pairs a thread polls per round trip; MB: chunks staged per batch.
+template <int HD, int NTH, int NB, int MB>
 __device__ void merge_head(const StepParams &p, const StepOp &op, const StepState &ss, uint8_t *am, int h,
-                           int n_chunks, int k, const Abort &ab) {
+                           int n_chunks, int k, const Abort &ab, int t) {
     using L = AttnRegion<HD>;
     constexpr int kW = HD + 2;                  // words per chunk
-    const int tid = threadIdx.x;
+    constexpr int ND = (HD + NTH - 1) / NTH;    // outputs per thread
     const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
     const uint64_t *base = op.lpart + (size_t)h * p.part_stride * kW;
-    static_assert((size_t)kMergeBatch * kW * 4 <= L::sOff, "a merge batch fits the K/V staging rows");
+    static_assert((size_t)MB * (kW + 1) * 4 <= L::sOff, "a merge batch and its weights fit the K/V staging rows");
+    static_assert(MB <= NTH, "a thread per chunk weight");
     float *mp = reinterpret_cast<float *>(am + L::kOff);
-    float M = -INFINITY, Ls = 0.f, A = 0.f;
-    for (int c0 = 0; c0 < n_chunks; c0 += kMergeBatch) {
-        const int nc = min(kMergeBatch, n_chunks - c0);
+    float *fw = mp + (size_t)MB * kW;             // chunk weights of the batch
+    float M = -INFINITY, Ls = 0.f, A[ND];
+#pragma unroll
+    for (int i = 0; i < ND; ++i) A[i] = 0.f;
+    for (int c0 = 0; c0 < n_chunks; c0 += MB) {
+        const int nc = min(MB, n_chunks - c0);
         const int nw = nc * kW;                 // even
         const uint64_t *bw = base + (size_t)c0 * kW;
-        for (int b0 = 0; b0 < nw; b0 += 2 * kEpiThreads * kLLBatch) {
-            uint64_t w[kLLBatch][2];
+        for (int b0 = 0; b0 < nw; b0 += 2 * NTH * NB) {
+            uint64_t w[NB][2];
             uint32_t valid = 0u;
 #pragma unroll
-            for (int j = 0; j < kLLBatch; ++j)
-                if (b0 + 2 * (tid + j * kEpiThreads) < nw) valid |= 1u << j;
+            for (int j = 0; j < NB; ++j)
+                if (b0 + 2 * (t + j * NTH) < nw) valid |= 1u << j;
             // on abort every thread still passes the barriers below (the results are then unused)
-            if (!ll_poll<kLLBatch>(w, valid, [&](int j) { return bw + b0 + 2 * (tid + j * kEpiThreads); }, tag, ab))
+            if (!ll_poll<NB>(w, valid, [&](int j) { return bw + b0 + 2 * (t + j * NTH); }, tag, ab))
                 valid = 0u;
 #pragma unroll
-            for (int j = 0; j < kLLBatch; ++j) {
+            for (int j = 0; j < NB; ++j) {
                 if ((valid >> j) & 1u) {
-                    const int e = b0 + 2 * (tid + j * kEpiThreads);
+                    const int e = b0 + 2 * (t + j * NTH);
                     *reinterpret_cast<float2 *>(mp + e) = make_float2(ll_f(w[j][0]), ll_f(w[j][1]));
                 }
             }
         }
-        epi_sync();
-        if (tid < HD) {
-            float Mb = M;
-            for (int cc = 0; cc < nc; ++cc) Mb = fmaxf(Mb, mp[cc * kW]);
-            if (Mb != -INFINITY) {
-                const float r = M == -INFINITY ? 0.f : expf(M - Mb);
-                Ls *= r;
-                A *= r;
-                for (int cc = 0; cc < nc; ++cc) {
-                    const float mc = mp[cc * kW];
-                    const float f = mc == -INFINITY ? 0.f : expf(mc - Mb);
-                    Ls = fmaf(mp[cc * kW + 1], f, Ls);
-                    A = fmaf(mp[cc * kW + 2 + tid], f, A);
-                }
-                M = Mb;
+        group_sync<NTH>();
+        // the batch's running max, then one weight exp(m_c - max) per chunk (thread c) for everyone
+        float Mb = M;
+        for (int cc = 0; cc < nc; ++cc) Mb = fmaxf(Mb, mp[cc * kW]);
+        if (t < nc) {
+            const float mc = mp[t * kW];
+            fw[t] = (mc == -INFINITY || Mb == -INFINITY) ? 0.f : expf(mc - Mb);
+        }
+        group_sync<NTH>();
+        if (t < HD && Mb != -INFINITY) {
+            const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+            Ls *= r;
+#pragma unroll
+            for (int i = 0; i < ND; ++i) A[i] *= r;
+            for (int cc = 0; cc < nc; ++cc) {
+                const float f = fw[cc];
+                Ls = fmaf(mp[cc * kW + 1], f, Ls);
+#pragma unroll
+                for (int i = 0; i < ND; ++i)
+                    if (t + i * NTH < HD) A[i] = fmaf(mp[cc * kW + 2 + t + i * NTH], f, A[i]);
             }
         }
-        epi_sync();                             // the staging rows are reused by the next batch
+        M = Mb;
+        group_sync<NTH>();                      // the staging rows are reused by the next batch
     }
-    if (tid < HD) ll_st1(op.lout + (size_t)h * HD + tid, ll_word(hilo_bits(A / Ls), tag));
+#pragma unroll
+    for (int i = 0; i < ND; ++i)
+        if (t + i * NTH < HD) ll_st1(op.lout + (size_t)h * HD + t + i * NTH, ll_word(hilo_bits(A[i] / Ls), tag));
 }
 
-// ---- grouped attention item: (kv head g, context chunk ch), all G <= 8 q heads of the group -----
+// ---- grouped attention: items (kv head g, context chunk ch), all G <= 8 q heads of the group ----
+// In the grouped build the attention runs on three warps of its own (warps 5-7), which walk the
+// step's attention ops while warps 0-3 do the GEMVs: the attention code keeps its registers out of
+// the GEMV loop's budget, and a CTA's attention warps start each layer early (L2 prefetch of the
+// item's K/V rows, its first tiles in flight) and wait for q.
 // The K/V rows of a chunk are read from HBM once for the whole group (the per-head items read them
 // once per q head) and the products run on the tensor cores, with fp32-grade sums:
 //   scores  S (16 x 8 positions) = Q (16 x HD) K^T, mma.sync m16n8k16: A row r < 8 = fp16 hi of
@@ -919,24 +950,32 @@ __device__ void merge_head(const StepParams &p, const StepOp &op, const StepStat
 //   values  O (16 x HD) += P (16 x 8 positions) V, mma.sync m16n8k8: A row r = fp16 hi of the
 //           head's probabilities, row 8 + r = their lo; B = the V rows transposed with movmatrix.
 //           Output of head r = O[r] + O[8 + r].
-// All four warps walk all tiles of 8 positions: each computes the same scores and softmax (the
-// same instructions on the same operands: the same bits) and the values for its quarter of the
-// output dims, so a thread holds 16 accumulators, not 64, and the item needs no cross-warp merge:
-// every warp publishes its dims of the partial directly. The contraction index is permuted so that
-// thread (row g, quad t) reads whole 16-byte pieces of the K row of position g: pieces t, t + 4, ...
-// (8 dims each; the quad reads 64 contiguous bytes per load). Its j-th dim is dim
-// 32 (j / 8) + 8 t + j % 8 of the row, and logical k = 16 kk + 2 t + 8 h + e is its dim
-// j = 4 kk + 2 h + e, in q and in K alike; output n-tile nn, column 2 t + e is its dim 2 nn + e,
-// so warp w reads V in the pieces of its dims. K/V go straight from global memory (L2) into
-// registers, D tiles in flight while one computes (the first ones issued before q is polled); no
-// shared-memory staging and no barriers inside the loop. The item publishes one partial
-// (max, sum, acc[HD]) per q head in the per-head items' format, so the same merge follows.
+// The contraction index is permuted so that thread (row g, quad t) reads whole 16-byte pieces of
+// the K row of position g: pieces t, t + 4, ... (8 dims each; the quad reads 64 contiguous bytes
+// per load). Its j-th dim is dim 32 (j / 8) + 8 t + j % 8 of the row, and logical k =
+// 16 kk + 2 t + 8 h + e is its dim j = 4 kk + 2 h + e, in q and in K alike; output n-tile nn,
+// column 2 t + e is its dim 2 nn + e, so V is read in the same pieces. K/V go straight from
+// global memory (L2) into registers, D tiles in flight while one computes; no shared-memory
+// staging and no barriers inside the loop. Warp w takes tiles w, w + 3, ... of the chunk with its
+// own running max / sum per head; the warps' partials meet once in shared memory and the item
+// publishes one partial (max, sum, acc[HD]) per q head in the per-head items' format, so the same
+// merge follows.
+constexpr int kAttnWarps = 3;
+constexpr int kAttnThreads = 32 * kAttnWarps;
+constexpr int kAttnWarp0 = kProducerWarp + 1;
+constexpr int kThreadsGR = kThreads + kAttnThreads;
+static_assert(kThreadsGR * 255 <= 65536, "the grouped build keeps 255 registers a thread");
+constexpr int kAttnMergePairs = 12;         // the attention warps' merge: word pairs in flight a thread
+template <int HD>
+constexpr int kAttnMergeChunks = HD == 128 ? 46 : 45;   // chunks staged per merge batch (region size)
 template <int HD>
 struct GroupRegion {
     static constexpr size_t qOff = 0;                                    // q [8][HD] fp32 (scaled)
     static constexpr size_t sOff = qOff + (size_t)kGroup * HD * 4;       // own K / V row [2][HD] fp16
     static constexpr size_t fOff = sOff + (size_t)2 * HD * 2;            // q fragments [HD / 16][32] uint4
-    static constexpr size_t bytes = fOff + (size_t)HD / 16 * 32 * 16;
+    static constexpr size_t oOff = fOff + (size_t)HD / 16 * 32 * 16;     // warps' outputs [3][8][HD] fp32
+    static constexpr size_t mOff = oOff + (size_t)kAttnWarps * kGroup * HD * 4;   // (max, sum) [3][8]
+    static constexpr size_t bytes = mOff + (size_t)kAttnWarps * kGroup * 2 * 4;
 };
 static_assert(GroupRegion<64>::bytes <= AttnRegion<64>::bytes && GroupRegion<128>::bytes <= AttnRegion<128>::bytes,
               "grouped items use the per-head items' staging region");
@@ -978,83 +1017,103 @@ SP_DEVINL GroupRows group_rows(const StepParams &p, const StepOp &op, int item, 
     return r;
 }
 
-// The item's K and V rows other than the step's own, into L2 while the QKV projection runs.
+// The item's K and V rows other than the step's own into L2 (threads t of nth), ahead of the item.
 template <int HD>
-SP_DEVINL void group_prefetch(const GroupRows &r, int slot) {
+SP_DEVINL void group_prefetch_t(const GroupRows &r, int slot, int t, int nth) {
     constexpr uint32_t kPiece = 4096;
     const int hi = min(r.j1, slot);
     if (hi <= r.j0) return;
     const uint32_t bytes = (uint32_t)(hi - r.j0) * HD * 2, n = (bytes + kPiece - 1) / kPiece;
-    for (uint32_t i = threadIdx.x; i < 2 * n; i += kEpiThreads) {
+    for (uint32_t i = (uint32_t)t; i < 2 * n; i += (uint32_t)nth) {
         const uint32_t piece = i % n, off = piece * kPiece;
         const __half *base = (i < n ? r.kb : r.vb) + (size_t)r.j0 * HD;
         bulk_prefetch_l2(reinterpret_cast<const uint8_t *>(base) + off, min(kPiece, bytes - off));
     }
 }
 
+// One pair of LL words (16-byte aligned) until both carry `tag`, with a back-off: the attention
+// warps reach a layer long before its q exists and must not take issue slots from the GEMV warps.
+// Bounded; false on abort.
+SP_DEVINL bool ll_wait_pair(const uint64_t *w2, uint32_t tag, const Abort &ab) {
+    for (uint32_t it = 0; it < kDepSpinLimit; ++it) {
+        uint64_t a, b;
+        ll_ld2(w2, a, b);
+        if (ll_ok(a, tag) && ll_ok(b, tag)) return true;
+        if ((it & 15u) == 15u && (ab.on() || *reinterpret_cast<volatile int *>(&ab.st->err) != 0)) {
+            *ab.flag = 1;
+            return false;
+        }
+        __nanosleep(200);
+    }
+    ab.raise(kErrDepTimeout);
+    return false;
+}
+
+// The attention warps' item; t = thread index among them.
 template <int HD>
-__device__ __noinline__ void group_attention(const StepParams &p, const StepOp &op, int item, int n_chunks, int rows_per,
-                                             int ctx, int slot, int tree_base, unsigned long long mask, uint32_t qtag,
-                                             uint32_t tag, uint8_t *am, const Abort ab, int k) {
+SP_DEVINL void group_item(const StepParams &p, const StepOp &op, int item, int n_chunks, int rows_per, int ctx,
+                          const StepState &ss, uint32_t tag, uint8_t *am, const Abort &ab, int k, int t) {
     using L = GroupRegion<HD>;
     const GroupRows gr = group_rows<HD>(p, op, item, n_chunks, rows_per, ctx);
     const int G = p.nh / p.nkv;
-    const int j0 = gr.j0, j1 = gr.j1;
+    const int j0 = gr.j0, j1 = gr.j1, slot = ss.slot;
     const __half *kb = gr.kb, *vb = gr.vb;
     constexpr int KS = HD / 16;             // k-steps of a score MMA
-    constexpr int KP = HD / 32;             // 16-byte K pieces of a thread per row
-    constexpr int NW = HD / 32;             // output n-tiles of a warp (= V words of a thread per row)
-    constexpr int D = 1;                    // K / V tiles in flight per warp beyond the current one
-                                            // (deeper pipelines spill: measured slower)
-    using VW = typename std::conditional<NW == 4, uint4, uint2>::type;
-    static_assert(NW == 4 || NW == 2, "HD 64 or 128");
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+    constexpr int NT = HD / 8;              // output n-tiles
+    constexpr int LD = HD / 32;             // 16-byte pieces of a thread per row
+    constexpr int D = HD == 128 ? 1 : 3;    // K / V tiles in flight per warp beyond the current one
+    const int warp = t >> 5, lane = t & 31, gq = lane >> 2, tq = lane & 3;
+    const bool lead = t == 0;
+    const int C = gridDim.x, c = blockIdx.x;
     float *qs = reinterpret_cast<float *>(am + L::qOff);
     __half *srow = reinterpret_cast<__half *>(am + L::sOff);
     const bool has_slot = slot >= j0 && slot < j1;
     const int ntiles = max(0, (j1 - j0 + 7) / 8);
-    // warp w's output dims are the threads' dims 2 NW w .. 2 NW (w + 1) - 1: at this row offset
-    const int jw = 2 * NW * warp;
-    const int voff = 32 * (jw >> 3) + 8 * tq + (jw & 7);
-    // row of position gq of tile t (past the chunk: a valid row, masked)
-    const auto row_at = [&](int t) { return (size_t)min(j0 + 8 * t + gq, j1 - 1) * HD; };
-    uint4 kq[D][KP];
-    VW vq[D];
-    const auto load = [&](int t, uint4 (&kr)[KP], VW &vr) {
-        const size_t r = row_at(t);
+    group_prefetch_t<HD>(gr, slot, t, kAttnThreads);
+    // row of position gq of tile tt (past the chunk: a valid row, masked)
+    const auto row_at = [&](int tt) { return (size_t)min(j0 + 8 * tt + gq, j1 - 1) * HD; };
+    uint4 kq[D][LD], vq[D][LD];
+    const auto load = [&](int tt, uint4 (&kr)[LD], uint4 (&vr)[LD]) {
+        const size_t r = row_at(tt);
 #pragma unroll
-        for (int i = 0; i < KP; ++i) kr[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + r + 32 * i + 8 * tq));
-        vr = __ldcg(reinterpret_cast<const VW *>(vb + r + voff));
+        for (int i = 0; i < LD; ++i) {
+            kr[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + r + 32 * i + 8 * tq));
+            vr[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + r + 32 * i + 8 * tq));
+        }
     };
-    // the first tiles go in flight before q is polled (the step's own row is replaced later)
+    // the first tiles go in flight before q exists (the step's own row is replaced later)
 #pragma unroll
     for (int u = 0; u < D; ++u)
-        if (u < ntiles) load(u, kq[u], vq[u]);
+        if (warp + kAttnWarps * u < ntiles) load(warp + kAttnWarps * u, kq[u], vq[u]);
+    const uint32_t qtag = ll_tag(ss.epoch, p.n_ops, op.lin_k);
+    const uint64_t *lq = op.lin + (size_t)gr.g * G * HD, *lkv = op.lkv + (size_t)gr.g * HD;
+    if (lead) stamp_clk_lead(p.trace, k, C, c, 0);
+    ll_wait_pair(lq, qtag, ab);
     {
         // q of the group's heads (rows G.. are zero) and, when the chunk holds the step's position,
         // its K / V row; word pairs: q first (8 HD / 2), then K / V (HD / 2)
         constexpr int QP = kGroup * HD / 2, NPAIR = QP + HD / 2;
-        constexpr int NP = (NPAIR + kEpiThreads - 1) / kEpiThreads;
-        const uint64_t *lq = op.lin + (size_t)gr.g * G * HD, *lkv = op.lkv + (size_t)gr.g * HD;
+        constexpr int NP = (NPAIR + kAttnThreads - 1) / kAttnThreads;
         uint64_t w[NP][2];
         uint32_t valid = 0u;
 #pragma unroll
         for (int j = 0; j < NP; ++j) {
-            const int i = tid + j * kEpiThreads;
+            const int i = t + j * kAttnThreads;
             if (i < QP ? 2 * i < G * HD : (i < NPAIR && has_slot)) valid |= 1u << j;
         }
         const auto addr = [&](int j) {
-            const int i = tid + j * kEpiThreads;
+            const int i = t + j * kAttnThreads;
             return i < QP ? lq + 2 * i : lkv + 2 * (i - QP);
         };
         // one tag: q and the K / V rows come from the same QKV projection
-        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 0);
         if (!ll_poll<NP>(w, valid, addr, qtag, ab)) valid = 0u;
-        stamp(p.trace, k, gridDim.x, blockIdx.x, 1);
-        stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 1);
+        if (lead) {
+            stamp_lead(p.trace, k, C, c, 1);
+            stamp_clk_lead(p.trace, k, C, c, 1);
+        }
 #pragma unroll
         for (int j = 0; j < NP; ++j) {
-            const int i = tid + j * kEpiThreads;
+            const int i = t + j * kAttnThreads;
             if (i < QP) {
                 const bool v = (valid >> j) & 1u;
                 qs[2 * i] = v ? ll_f(w[j][0]) * p.scale : 0.f;
@@ -1070,11 +1129,11 @@ __device__ __noinline__ void group_attention(const StepParams &p, const StepOp &
             }
         }
     }
-    epi_sync();
+    group_sync<kAttnThreads>();
     // q fragments of lane l: row l / 4 hi / lo at its dims 4 kk + {0, 1} (columns 2 (l % 4) + {0, 1})
     // and 4 kk + {2, 3}; the same for every warp, built once into [kk][lane] uint4
     uint4 *qf = reinterpret_cast<uint4 *>(am + L::fOff);
-    for (int i = tid; i < KS * 32; i += kEpiThreads) {
+    for (int i = t; i < KS * 32; i += kAttnThreads) {
         const int kk = i >> 5, l = i & 31;
         const float4 x = *reinterpret_cast<const float4 *>(qs + (l >> 2) * HD + 32 * (kk >> 1) + 8 * (l & 3) + 4 * (kk & 1));
         const __half h0 = __float2half_rn(x.x), h1 = __float2half_rn(x.y), h2 = __float2half_rn(x.z),
@@ -1084,22 +1143,26 @@ __device__ __noinline__ void group_attention(const StepParams &p, const StepOp &
                            pack_half2(h2, h3),
                            pack_half2(__float2half_rn(x.z - __half2float(h2)), __float2half_rn(x.w - __half2float(h3))));
     }
-    epi_sync();
-    stamp(p.trace, k, gridDim.x, blockIdx.x, 2);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 2);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 3);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 4);
-    float o[NW][4];
+    group_sync<kAttnThreads>();
+    if (lead) {
+        stamp_lead(p.trace, k, C, c, 2);
+        stamp_clk_lead(p.trace, k, C, c, 2);
+        stamp_clk_lead(p.trace, k, C, c, 3);
+        stamp_clk_lead(p.trace, k, C, c, 4);
+    }
+    float o[NT][4];
 #pragma unroll
-    for (int n = 0; n < NW; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int nn = 0; nn < NT; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
     float m_run = -INFINITY, l_part = 0.f;  // head gq (m quad-uniform; l this thread's positions)
-    const auto tile = [&](int t, uint4 (&kc)[KP], VW &vc) {
-        const int a = j0 + 8 * t;
+    const auto tile = [&](int tt, uint4 (&kc)[LD], uint4 (&vc)[LD]) {
+        const int a = j0 + 8 * tt;
         const bool own = a + gq == slot;    // the step's own row: from the QKV projection's words
         if (own) {
 #pragma unroll
-            for (int i = 0; i < KP; ++i) kc[i] = *reinterpret_cast<const uint4 *>(srow + 32 * i + 8 * tq);
-            vc = *reinterpret_cast<const VW *>(srow + HD + voff);
+            for (int i = 0; i < LD; ++i) {
+                kc[i] = *reinterpret_cast<const uint4 *>(srow + 32 * i + 8 * tq);
+                vc[i] = *reinterpret_cast<const uint4 *>(srow + HD + 32 * i + 8 * tq);
+            }
         }
         const uint32_t *kw = reinterpret_cast<const uint32_t *>(kc);
         float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};   // even / odd k-steps
@@ -1113,8 +1176,8 @@ __device__ __noinline__ void group_attention(const StepParams &p, const StepOp &
         float s0 = (sa[0] + sb[0]) + (sa[2] + sb[2]), s1 = (sa[1] + sb[1]) + (sa[3] + sb[3]);
         const auto vis = [&](int jj) {
             if (jj >= j1) return false;
-            const int d = jj - tree_base;
-            return !(d >= 0 && (d >= 64 || !((mask >> d) & 1ull)));
+            const int d = jj - ss.tree_base;
+            return !(d >= 0 && (d >= 64 || !((ss.mask >> d) & 1ull)));
         };
         if (!vis(a + 2 * tq)) s0 = -INFINITY;
         if (!vis(a + 2 * tq + 1)) s1 = -INFINITY;
@@ -1129,46 +1192,70 @@ __device__ __noinline__ void group_attention(const StepParams &p, const StepOp &
         const __half p0 = __float2half_rn(e0), p1 = __float2half_rn(e1);
         const uint32_t pa0 = pack_half2(p0, p1);
         const uint32_t pa1 = pack_half2(__float2half_rn(e0 - __half2float(p0)), __float2half_rn(e1 - __half2float(p1)));
-        const uint32_t *vw = reinterpret_cast<const uint32_t *>(&vc);
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(vc);
 #pragma unroll
-        for (int n = 0; n < NW; ++n) {
-            o[n][0] *= corr;
-            o[n][1] *= corr;
-            o[n][2] *= corr;
-            o[n][3] *= corr;
-            mma_1688(o[n], pa0, pa1, movmatrix_t(vw[n]));
+        for (int nn = 0; nn < NT; ++nn) {
+            o[nn][0] *= corr;
+            o[nn][1] *= corr;
+            o[nn][2] *= corr;
+            o[nn][3] *= corr;
+            mma_1688(o[nn], pa0, pa1, movmatrix_t(vw[nn]));
         }
     };
-    for (int t0 = 0; t0 < ntiles; t0 += D) {
+    for (int t0 = warp; t0 < ntiles; t0 += kAttnWarps * D) {
 #pragma unroll
         for (int u = 0; u < D; ++u) {
-            const int t = t0 + u;
-            if (t < ntiles) {               // uniform
-                uint4 kc[KP];
+            const int tt = t0 + kAttnWarps * u;
+            if (tt < ntiles) {              // warp-uniform
+                uint4 kc[LD], vc[LD];
 #pragma unroll
-                for (int i = 0; i < KP; ++i) kc[i] = kq[u][i];
-                VW vc = vq[u];
-                if (t + D < ntiles) load(t + D, kq[u], vq[u]);
-                tile(t, kc, vc);
+                for (int i = 0; i < LD; ++i) {
+                    kc[i] = kq[u][i];
+                    vc[i] = vq[u][i];
+                }
+                if (tt + kAttnWarps * D < ntiles) load(tt + kAttnWarps * D, kq[u], vq[u]);
+                tile(tt, kc, vc);
             }
         }
     }
-    stamp(p.trace, k, gridDim.x, blockIdx.x, 5);
-    stamp_clk(p.trace, k, gridDim.x, blockIdx.x, 5);
-    // this warp's dims of the partial of head gq: thread dims jw + 2 n + e
+    // the warp's partial of head gq (the thread's dims 2 nn + e)
     float l = l_part + __shfl_xor_sync(0xffffffffu, l_part, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
-    if (gq < G) {
-        uint64_t *pw = op.lpart + ((size_t)(gr.g * G + gq) * p.part_stride + gr.ch) * (HD + 2);
+    float *ow = reinterpret_cast<float *>(am + L::oOff) + ((size_t)warp * kGroup + gq) * HD + 8 * tq;
 #pragma unroll
-        for (int n = 0; n < NW; ++n) {
-            const int j = jw + 2 * n;
-            uint64_t *q = pw + 2 + 32 * (j >> 3) + 8 * tq + (j & 7);
-            ll_st2(q, ll_wordf(o[n][0] + o[n][2], tag), ll_wordf(o[n][1] + o[n][3], tag));
-        }
-        if (warp == 0 && tq == 0) ll_st2(pw, ll_wordf(m_run, tag), ll_wordf(l, tag));
+    for (int nn = 0; nn < NT; ++nn)
+        *reinterpret_cast<float2 *>(ow + 32 * (nn >> 2) + 2 * (nn & 3)) =
+            make_float2(o[nn][0] + o[nn][2], o[nn][1] + o[nn][3]);
+    float *mw = reinterpret_cast<float *>(am + L::mOff);
+    if (tq == 0) *reinterpret_cast<float2 *>(mw + 2 * (warp * kGroup + gq)) = make_float2(m_run, l);
+    group_sync<kAttnThreads>();
+    if (lead) {
+        stamp_lead(p.trace, k, C, c, 5);
+        stamp_clk_lead(p.trace, k, C, c, 5);
     }
-    epi_sync();                             // the region is reused by the merge
+    // the warps' partials -> one per q head, in the per-head items' format
+    const float *oo = reinterpret_cast<const float *>(am + L::oOff);
+    uint64_t *part = op.lpart + ((size_t)gr.g * G * p.part_stride + gr.ch) * (HD + 2);
+    for (int i = t; i < G * HD; i += kAttnThreads) {
+        const int r = i / HD, d = i - r * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, mw[2 * (w * kGroup + r)]);
+        float Ls = 0.f, A = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float mwr = mw[2 * (w * kGroup + r)];
+                const float f = mwr == -INFINITY ? 0.f : expf(mwr - M);
+                Ls = fmaf(mw[2 * (w * kGroup + r) + 1], f, Ls);
+                A = fmaf(oo[((size_t)w * kGroup + r) * HD + d], f, A);
+            }
+        }
+        uint64_t *pw = part + (size_t)r * p.part_stride * (HD + 2);
+        ll_st1(pw + 2 + d, ll_wordf(A, tag));
+        if (d == 0) ll_st2(pw, ll_wordf(M, tag), ll_wordf(Ls, tag));
+    }
+    group_sync<kAttnThreads>();             // the region is reused by the merge
 }
 
 // The LM head's argmax across CTAs (last arriver) and the device state of the next step; once
@@ -1305,7 +1392,7 @@ struct UnitCursor {
 // Q8: the build with the blockwise-int8 unit path (a separate instantiation, so the fp16-only
 // kernel keeps its register allocation).
 template <int HD, bool Q8, bool GR>
-__global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
+__global__ void __launch_bounds__(GR ? kThreadsGR : kThreads, 1) k_step(const StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ float s_val[4];
     __shared__ int s_abort;
@@ -1424,6 +1511,45 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             }
             s_issued = issued;
         }
+    } else if (GR && warp >= kAttnWarp0) {
+        // ---- grouped build, warps 5-7: the step's attention ops, one layer after the other -------
+        griddep_wait();
+        const int t = tid - kAttnWarp0 * 32;
+        DevState *st = p.st;
+        StepState ss;
+        ss.epoch = *p.epoch;
+        ss.slot = min(max(st->slot, 0), p.cap - 1);          // warps 0-3 report bad slots
+        ss.tree_base = st->tree_base;
+        ss.mask = ss.slot >= ss.tree_base ? st->small_mask[ss.slot - ss.tree_base] : 0ull;
+        ss.token = 0;
+        ss.pos = 0;
+        const int ctx = min(ss.slot + 1, p.cap);
+        const int n_chunks = max(1, min(p.group_chunks, (ctx + kGroupTileRows - 1) / kGroupTileRows));
+        const int rows_per = (ctx + n_chunks - 1) / n_chunks;
+        const int n_items = p.nkv * n_chunks;
+        // items on the last CTAs, one per CTA; head h's merge on the CTA before them (or on the CTA
+        // of item h, after its item, when the grid has no room)
+        const int item = C - 1 - c;
+        const int mh = n_items + p.nh <= C ? C - 1 - n_items - c : item;
+        for (int k = 0; k < p.n_ops; ++k) {
+            const StepOp &op = p.ops[k];
+            if (op.kind != OP_ATTN) continue;
+            if (ab.on()) break;
+            const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
+            if (item < n_items) {
+                group_item<HD>(p, op, item, n_chunks, rows_per, ctx, ss, tag, am, ab, k, t);
+                if (t == 0) stamp_lead(p.trace, k, C, c, 4);
+            }
+            if (mh >= 0 && mh < p.nh && !ab.on()) {
+                if (t == 0) stamp_lead(p.trace, k, C, c, 6);
+                ll_wait_pair(op.lpart + (size_t)mh * p.part_stride * (HD + 2), tag, ab);   // back-off first
+                merge_head<HD, kAttnThreads, kAttnMergePairs, kAttnMergeChunks<HD>>(p, op, ss, am, mh, n_chunks, k, ab, t);
+                if (t == 0) {
+                    stamp_lead(p.trace, k, C, c, 7);
+                    stamp_clk_lead(p.trace, k, C, c, 7);
+                }
+            }
+        }
     } else {
         // ---- warps 0-3: hand-offs, prologues, GEMV compute, epilogues, attention ------------------
         griddep_wait();
@@ -1464,23 +1590,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             cp_async_commit();
             stamp(p.trace, k, C, c, 0);
             const uint32_t tag = ll_tag(ss.epoch, p.n_ops, k);
-            if (GR && op.kind == OP_ATTN) {
-                // items on the last CTAs, one per CTA; head h's merge on the CTA before them (or on
-                // the CTA of item h, after its item, when the grid has no room)
-                const int item = C - 1 - c;
-                if (item < n_items && !ab.on()) {
-                    group_attention<HD>(p, op, item, n_chunks, rows_per, ctx, ss.slot, ss.tree_base, ss.mask,
-                                        ll_tag(ss.epoch, p.n_ops, op.lin_k), tag, am, ab, k);
-                    stamp(p.trace, k, C, c, 4);
-                }
-                const int h = n_items + p.nh <= C ? C - 1 - n_items - c : item;
-                if (h >= 0 && h < p.nh && !ab.on()) {
-                    stamp(p.trace, k, C, c, 6);
-                    stamp_clk(p.trace, k, C, c, 6);
-                    merge_head<HD>(p, op, ss, am, h, n_chunks, k, ab);
-                    stamp(p.trace, k, C, c, 7);
-                    stamp_clk(p.trace, k, C, c, 7);
-                }
+            if (GR && op.kind == OP_ATTN) {       // the attention warps' op
                 stamp(p.trace, k, C, c, 3);
                 continue;
             }
@@ -1493,7 +1603,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
                     if (item == h * n_chunks) {          // chunk 0 of the head: merge all of them
                         stamp(p.trace, k, C, c, 6);
                         stamp_clk(p.trace, k, C, c, 6);
-                        merge_head<HD>(p, op, ss, am, h, n_chunks, k, ab);
+                        merge_head<HD, kEpiThreads, kLLBatch, kMergeBatch>(p, op, ss, am, h, n_chunks, k, ab, tid);
                         stamp(p.trace, k, C, c, 7);
                         stamp_clk(p.trace, k, C, c, 7);
                     }
@@ -1504,12 +1614,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams p) {
             if (op.epi == EPI_QKV) {
                 // this CTA's attention item of the layer: stage its immutable K/V rows now
                 const int item = C - 1 - c;
-                if (item < n_items) {
-                    if constexpr (GR)
-                        group_prefetch<HD>(group_rows<HD>(p, op, item, n_chunks, rows_per, ctx), ss.slot);
-                    else
-                        attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
-                }
+                if (!GR && item < n_items) attn_prestage<HD>(p, op, ss, am, item, n_chunks, rows_per, ctx);
             }
             if (c >= op.grid) continue;          // no rows of this GEMV
             stamp_clk(p.trace, k, C, c, 0);
@@ -2052,7 +2157,7 @@ static cudaError_t step_launch_t(const StepParams *p, int grid, size_t smem, cud
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(GR ? kThreadsGR : kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
