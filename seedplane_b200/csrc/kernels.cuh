@@ -327,7 +327,9 @@ struct PrefillScratch {
     float *y;                            // [T, qkv rows] QKV projection
     float *q;                            // [T, heads * head_dim]
     float *logits;                       // [kPrefillLogitRows, vocab]
+    float *part;                         // attention partials per (query, head, key chunk): kAttnPartBytes
 };
+constexpr size_t kAttnPartBytes = (size_t)64 << 20;
 size_t prefill_scratch_bytes(const PrefillDims &d);
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d);
 cudaError_t launch_prefill_embed(const PrefillDims &d, const PrefillScratch &s, const __half *embed,

@@ -125,9 +125,9 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_hilo(__half *xh, __hal
     }
 }
 
-// Attention of a block of T queries over the cache (a prompt chunk or a verify tree). CTA =
-// (q head, 4 QW queries), warp w = queries q0 + w QW .. + QW - 1 (QW = 1 for short blocks, 4 for
-// prompt chunks). The visible keys go through shared memory in tiles of 64 (K and V rows padded by
+// Attention of a block of T queries over the cache (a short verify tree or prompt chunk over a
+// short cache; k_attn_gqa below takes the rest). CTA = (q head, 4 QW queries), warp w = queries
+// q0 + w QW .. + QW - 1 (the pass uses QW = 1). The visible keys go through shared memory in tiles of 64 (K and V rows padded by
 // 16 bytes, so the lanes of a quarter warp reading 16 bytes of 8 different rows hit distinct
 // banks), two tiles in flight: tile i + 1 is copied with cp.async while tile i is used. Per tile
 // and warp: lane = keys lane and lane + 32 (full dot products over the row, each K chunk read once
@@ -301,6 +301,270 @@ __global__ void __launch_bounds__(128) k_attn_block(__half *oh, __half *ol, cons
             ol[idx] = __float2half_rn(o - __half2float(hv));
         }
     }
+}
+
+// Attention of a block of T queries on the tensor cores, by GQA group and context chunk (the long-
+// context form of k_attn_block, same visibility rule and output). Rows are (query t, head r) pairs
+// of kv head g's group, pair p = t G + r; an m-tile of the MMAs is 8 pairs: row i < 8 = fp16 hi
+// of pair i's q * scale, row 8 + i = its fp16 lo, so
+//   scores  S (16 x 8 keys) = Q K^T, mma.sync m16n8k16 (B = K rows by ldmatrix), pair i's score
+//           = D[i] + D[8 + i];
+//   values  O (16 x HD) += P V, mma.sync m16n8k16 with A = the probabilities' fp16 hi (rows i) and
+//           lo (rows 8 + i) taken straight from the score accumulators, B = V rows by
+//           ldmatrix.trans; pair i's output = O[i] + O[8 + i].
+// CTA = (kv head g, 32 pairs = one m-tile per warp, key chunk z): the chunk's keys go through
+// shared memory in tiles of 64 (rows XOR-swizzled in 16-byte pieces, two tiles in flight), and
+// every warp multiplies its m-tile with each tile; online softmax per pair in fp32. Chunks: the
+// visible keys [0, slot0 + T) are cut into nz pieces of >= 256 keys (nz <= gridDim.z, computed on
+// the device from slot0, so one captured graph serves any cache length). One chunk: the output as
+// fp16 hi / lo halves; several: an unnormalised partial (max, sum, acc[HD]) per (pair, chunk) that
+// k_attn_merge folds in chunk order.
+constexpr int kGqaKeys = 64;                // keys per shared-memory tile
+constexpr int kGqaChunkKeys = 256;          // keys per chunk at least
+constexpr int kShortCacheKeys = 1024;       // caches this short: verify blocks use k_attn_block
+constexpr int kGqaPairs = 32;               // (query, head) pairs per CTA: 8 a warp
+constexpr int kGqaMaxChunks = 64;           // chunks of the keys at most
+template <int HD>
+struct GqaSmem {
+    static constexpr int kRow = HD * 2;                            // bytes of a K / V row
+    static constexpr int kTile = kGqaKeys * kRow;
+    static constexpr int kBytes = 2 * 2 * kTile;                   // two stages of K and V
+};
+SP_DEVINL void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+SP_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+SP_DEVINL void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+SP_DEVINL uint32_t h2bits(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// byte offset of 16-byte piece c of row r in a swizzled tile (pieces XOR-permuted by r within each
+// 128-byte segment: the 8 rows an ldmatrix reads hit 8 different bank groups)
+template <int HD>
+SP_DEVINL uint32_t gqa_off(int r, int c) {
+    return (uint32_t)(r * GqaSmem<HD>::kRow + (((c & ~7) | ((c & 7) ^ (r & 7))) << 4));
+}
+// Chunk size and count for `keys` visible keys over at most zmax chunks (the same in every kernel).
+SP_DEVINL void gqa_chunks(int keys, int zmax, int &chunk, int &nz) {
+    chunk = max(kGqaChunkKeys, (keys + zmax - 1) / zmax);
+    chunk = (chunk + kGqaKeys - 1) / kGqaKeys * kGqaKeys;
+    nz = (keys + chunk - 1) / chunk;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_gqa(__half *oh, __half *ol, float *part, const float *q,
+                                                  const __half *kc, const __half *vc, const uint64_t *mask, int T,
+                                                  int nh, int nkv, int cap, const int *slot_base, int slot_off,
+                                                  float scale, DevState *st) {
+    using L = GqaSmem<HD>;
+    constexpr int KS = HD / 16;             // k-steps of a score MMA
+    constexpr int NT = HD / 8;              // output n-tiles
+    constexpr int CH = HD / 8;              // 16-byte pieces of a row
+    extern __shared__ __align__(128) uint8_t gsm[];
+    pdl_enter();
+    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
+    const int G = nh / nkv, g = blockIdx.x, z = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    const int keys = slot0 + T;             // every key any query sees is below this
+    int chunk, nz;
+    gqa_chunks(keys, (int)gridDim.z, chunk, nz);
+    if (z >= nz) return;                    // uniform: this chunk holds no key
+    const int np = T * G, p0 = blockIdx.y * kGqaPairs;
+    // the last key the CTA's pairs see, and this chunk's keys
+    const int last = slot0 + min(T - 1, (min(np, p0 + kGqaPairs) - 1) / G);
+    const int k_lo = z * chunk, k_hi = min(keys, min(k_lo + chunk, last + 1));
+    // this thread's pair (row gq of the warp's m-tile): query, head, visibility
+    const int pr = p0 + warp * 8 + gq;
+    const bool live = pr < np;
+    const int tr = live ? pr / G : 0, hr = g * G + (live ? pr % G : 0);
+    const uint64_t tm = (mask && live) ? mask[tr] : 0ull;
+    const __half *kb = kc + (size_t)g * cap * HD, *vb = vc + (size_t)g * cap * HD;
+    const int ntiles = k_hi > k_lo ? (k_hi - k_lo + kGqaKeys - 1) / kGqaKeys : 0;
+    auto stage = [&](int tile) {
+        uint8_t *ks = gsm + (tile & 1) * 2 * L::kTile, *vs = ks + L::kTile;
+        const int j0 = k_lo + tile * kGqaKeys;
+        for (int i = threadIdx.x; i < kGqaKeys * CH; i += 128) {
+            const int r = i / CH, c = i - r * CH;
+            const int j = min(j0 + r, keys - 1);     // past the chunk: a valid row, masked
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ks + gqa_off<HD>(r, c))),
+                         "l"(kb + (size_t)j * HD + c * 8) : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(vs + gqa_off<HD>(r, c))),
+                         "l"(vb + (size_t)j * HD + c * 8) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (ntiles > 0) stage(0);
+    // q fragments of the warp's m-tile: row gq hi / lo at dims 16 kk + 2 tq + {0, 1} and + 8
+    uint32_t qa[KS][4];
+    {
+        const float *qr = q + (size_t)tr * nh * HD + (size_t)hr * HD;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const float2 x = live ? *reinterpret_cast<const float2 *>(qr + 16 * kk + 8 * hf + 2 * tq)
+                                      : make_float2(0.f, 0.f);
+                const float a = x.x * scale, b = x.y * scale;
+                const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+                qa[kk][2 * hf] = h2bits(ha, hb);
+                qa[kk][2 * hf + 1] = h2bits(__float2half_rn(a - __half2float(ha)), __float2half_rn(b - __half2float(hb)));
+            }
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_run = -INFINITY, l_part = 0.f;
+    const int wlast = slot0 + min(T - 1, (min(np, p0 + warp * 8 + 8) - 1) / G);   // the warp's last key
+    const auto visible = [&](int j) {
+        if (!live || j >= keys) return false;
+        if (j < slot0) return true;
+        return mask ? (((tm >> (j - slot0)) & 1ull) != 0ull) : j <= slot0 + tr;
+    };
+    for (int tile = 0; tile < ntiles; ++tile) {
+        if (tile + 1 < ntiles) {
+            stage(tile + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();                    // tile `tile` visible to all
+        const uint32_t ks = smem_u32(gsm + (tile & 1) * 2 * L::kTile), vs = ks + L::kTile;
+        const int j0 = k_lo + tile * kGqaKeys;
+        if (j0 <= wlast && pr - gq < np) {  // warp-uniform
+            // scores of the tile: 8 n-tiles of 8 keys
+            float s[8][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < KS; kk += 2) {
+                    uint32_t b0, b1, b2, b3;   // keys 8 nt .. + 7, pieces 2 kk .. 2 kk + 3
+                    ldsm_x4(ks + gqa_off<HD>(8 * nt + (lane & 7), 2 * kk + (lane >> 3)), b0, b1, b2, b3);
+                    mma16816(s[nt], qa[kk], b0, b1);
+                    mma16816(s[nt], qa[kk + 1], b2, b3);
+                }
+            }
+            float mt = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float v = s[nt][e] + s[nt][2 + e];
+                    if (!visible(j0 + 8 * nt + 2 * tq + e)) v = -INFINITY;
+                    s[nt][e] = v;
+                    mt = fmaxf(mt, v);
+                }
+            }
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+            const float mn = fmaxf(m_run, mt);
+            const float corr = m_run == -INFINITY ? 0.f : expf(m_run - mn);
+            m_run = mn;
+            float ls = 0.f;
+            uint32_t pa[4][4];                // P as the A operand: 4 k-steps of 16 keys
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                float pe[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    pe[e] = s[nt][e] == -INFINITY ? 0.f : expf(s[nt][e] - mn);
+                    ls += pe[e];
+                }
+                const __half h0 = __float2half_rn(pe[0]), h1 = __float2half_rn(pe[1]);
+                pa[nt >> 1][2 * (nt & 1)] = h2bits(h0, h1);
+                pa[nt >> 1][2 * (nt & 1) + 1] =
+                    h2bits(__float2half_rn(pe[0] - __half2float(h0)), __float2half_rn(pe[1] - __half2float(h1)));
+            }
+            l_part = fmaf(l_part, corr, ls);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                o[n][0] *= corr;
+                o[n][1] *= corr;
+                o[n][2] *= corr;
+                o[n][3] *= corr;
+            }
+            // values: 4 k-steps of 16 keys x NT n-tiles of 8 dims
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                for (int n = 0; n < NT; n += 2) {
+                    uint32_t b0, b1, b2, b3;   // keys 16 kk + {0..7, 8..15} x dims 8 n .. 8 n + 15
+                    const int mtx = lane >> 3;
+                    ldsm_x4_t(vs + gqa_off<HD>(16 * kk + 8 * (mtx & 1) + (lane & 7), n + (mtx >> 1)), b0, b1, b2, b3);
+                    mma16816(o[n], pa[kk], b0, b1);
+                    mma16816(o[n + 1], pa[kk], b2, b3);
+                }
+            }
+        }
+        __syncthreads();                    // the stage is rewritten two tiles on
+    }
+    // pair gq of the warp: dims 8 n + 2 tq + e
+    float l = l_part + __shfl_xor_sync(0xffffffffu, l_part, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (!live) return;
+    if (nz == 1) {
+        const float inv = 1.f / l;
+        const size_t base = (size_t)tr * nh * HD + (size_t)hr * HD + 2 * tq;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float v = (o[n][e] + o[n][2 + e]) * inv;
+                const __half hv = __float2half_rn(v);
+                oh[base + 8 * n + e] = hv;
+                ol[base + 8 * n + e] = __float2half_rn(v - __half2float(hv));
+            }
+        }
+    } else {
+        float *pp = part + (((size_t)tr * nh + hr) * gridDim.z + z) * (HD + 2);
+        if (tq == 0) {
+            pp[0] = m_run;
+            pp[1] = l;
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+            *reinterpret_cast<float2 *>(pp + 2 + 8 * n + 2 * tq) = make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
+    }
+}
+
+// The chunks' partials of each (query, head) -> the attention output as fp16 hi / lo halves, chunks
+// folded in order (log-sum-exp). CTA = one (query, head), thread d = output dim d.
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_merge(__half *oh, __half *ol, const float *part, int T, int nh, int cap,
+                                                   const int *slot_base, int slot_off, int zmax, DevState *st) {
+    pdl_enter();
+    const int slot0 = block_slot0(slot_base, slot_off, T, cap, st);
+    int chunk, nz;
+    gqa_chunks(slot0 + T, zmax, chunk, nz);
+    if (nz == 1) return;                    // k_attn_gqa wrote the output
+    const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const float *pp = part + ((size_t)t * nh + h) * zmax * (HD + 2);
+    float M = -INFINITY;
+    for (int z = 0; z < nz; ++z) M = fmaxf(M, pp[(size_t)z * (HD + 2)]);
+    float Ls = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+        for (int z = 0; z < nz; ++z) {
+            const float *q = pp + (size_t)z * (HD + 2);
+            const float f = q[0] == -INFINITY ? 0.f : expf(q[0] - M);
+            Ls = fmaf(q[1], f, Ls);
+            A = fmaf(q[2 + d], f, A);
+        }
+    }
+    const float v = A / Ls;
+    const __half hv = __float2half_rn(v);
+    const size_t idx = (size_t)t * nh * HD + (size_t)h * HD + d;
+    oh[idx] = hv;
+    ol[idx] = __float2half_rn(v - __half2float(hv));
 }
 
 // Attention of a batched decode step: token b of request lanes[b] attends to slots [0, slot] of
@@ -514,7 +778,7 @@ size_t qrows_of(const PrefillDims &d) { return (size_t)(d.heads + 2 * d.kv_heads
 size_t prefill_scratch_bytes(const PrefillDims &d) {
     const size_t T = d.max_tokens;
     return up256(T * d.hidden * 4) + up256(2 * T * kmax_of(d) * 2) + up256(2 * T * d.inter * 2) +
-           up256(T * d.heads * d.head_dim * 4) + up256((size_t)kPrefillLogitRows * d.vocab * 4);
+           up256(T * d.heads * d.head_dim * 4) + up256((size_t)kPrefillLogitRows * d.vocab * 4) + kAttnPartBytes;
 }
 
 PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
@@ -527,6 +791,7 @@ PrefillScratch prefill_scratch_at(void *base, const PrefillDims &d) {
     s.xb = reinterpret_cast<__half *>(take(2 * T * d.inter * 2));
     s.q = reinterpret_cast<float *>(take(T * d.heads * d.head_dim * 4));
     s.logits = reinterpret_cast<float *>(take((size_t)kPrefillLogitRows * d.vocab * 4));
+    s.part = reinterpret_cast<float *>(take(kAttnPartBytes));
     return s;
 }
 
@@ -565,7 +830,10 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
                       s.q, kc, vc};
     e = launch_mcol(qkv, stream, true);
     if (e != cudaSuccess) return e;
-    if (T <= kShortBlockT) {
+    if (mask && T > kShortBlockT) return cudaErrorInvalidValue;    // trees have at most 64 nodes
+    if (T <= kShortBlockT && cap <= kShortCacheKeys) {
+        // short blocks over a short cache (the cfg2 verify): per (head, 4 queries) CTAs keep more of the
+        // GPU busy than the grouped kernel's few CTAs (1.17 against 1.26 ms a 0.5B verify pass)
         const dim3 grid(d.heads, (T + 3) / 4);
         if (d.head_dim == 128)
             e = launch_pdl_smem(k_attn_block<128, 1>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A,
@@ -574,14 +842,27 @@ cudaError_t launch_prefill_layer_front(const PrefillDims &d, const PrefillLayer 
             e = launch_pdl_smem(k_attn_block<64, 1>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A,
                                 s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
     } else {
-        if (mask) return cudaErrorInvalidValue;                    // trees have at most 64 nodes
-        const dim3 grid(d.heads, (T + 15) / 16);
-        if (d.head_dim == 128)
-            e = launch_pdl_smem(k_attn_block<128, 4>, grid, 128, TreeSmem<128>::kBytes, stream, s.xa, s.xa + lo * A,
-                                s.q, kc, vc, nullptr, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
-        else
-            e = launch_pdl_smem(k_attn_block<64, 4>, grid, 128, TreeSmem<64>::kBytes, stream, s.xa, s.xa + lo * A,
-                                s.q, kc, vc, nullptr, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+        // chunks of the visible keys (at most zmax; the kernels cut the keys on the device): one per
+        // 256 keys the cache holds, within the partials' scratch
+        const size_t per_chunk = (size_t)T * d.heads * (d.head_dim + 2) * 4;
+        const int groups = (T * (d.heads / d.kv_heads) + kGqaPairs - 1) / kGqaPairs;
+        const int zmax = (int)std::max<size_t>(1, std::min<size_t>({(size_t)(cap + kGqaChunkKeys - 1) / kGqaChunkKeys,
+                                                                     (size_t)kGqaMaxChunks, kAttnPartBytes / per_chunk}));
+        const dim3 grid(d.kv_heads, groups, zmax);
+        const dim3 mgrid(T, d.heads);
+        if (d.head_dim == 128) {
+            e = launch_pdl_smem(k_attn_gqa<128>, grid, 128, GqaSmem<128>::kBytes, stream, s.xa, s.xa + lo * A, s.part,
+                                s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+            if (e == cudaSuccess && zmax > 1)
+                e = launch_pdl(k_attn_merge<128>, mgrid, 128, stream, s.xa, s.xa + lo * A, s.part, T, d.heads, cap,
+                               slot_base, slot_off, zmax, st);
+        } else {
+            e = launch_pdl_smem(k_attn_gqa<64>, grid, 128, GqaSmem<64>::kBytes, stream, s.xa, s.xa + lo * A, s.part,
+                                s.q, kc, vc, mask, T, d.heads, d.kv_heads, cap, slot_base, slot_off, scale, st);
+            if (e == cudaSuccess && zmax > 1)
+                e = launch_pdl(k_attn_merge<64>, mgrid, 64, stream, s.xa, s.xa + lo * A, s.part, T, d.heads, cap,
+                               slot_base, slot_off, zmax, st);
+        }
     }
     if (e != cudaSuccess) return e;
     // O projection into the residual stream

@@ -1,6 +1,9 @@
-"""The step kernel's grouped attention items: one item per (kv head, context chunk) computing all q
+"""GQA attention on the tensor cores, in both passes.
+
+The step kernel's grouped attention items: one item per (kv head, context chunk) computing all q
 heads of the GQA group on the tensor cores (scores and values as m16n8 MMAs with fp16 hi / lo
-rows), selected from `SEEDPLANE_ATTN_GROUP_CTX` visible positions on.
+rows), selected from `SEEDPLANE_ATTN_GROUP_CTX` visible positions on. The batched pass's attention
+(prompt chunks and verify trees) by GQA group and key chunk, with the chunks' partials merged.
 
 Every case runs the prompt through the step kernel too (`SEEDPLANE_PREFILL=steps`), so each prompt
 token is one step with its own context length: chunks of one tile, partial tiles, the step's own
@@ -107,3 +110,37 @@ def test_grouped_and_per_head_items_agree_on_qwen2_0_5b(monkeypatch):
     (g_tok, g_last), (h_tok, h_last) = runs["0"], runs[str(1 << 30)]
     assert g_tok == h_tok
     _close(g_last, h_last)
+
+
+@pytest.mark.parametrize("name", ["tiny-hd64", "tiny-hd128"])
+def test_batched_pass_attention_over_several_key_chunks(name):
+    """A 400-token prompt in one batched pass (causal; 400 keys cut into two chunks of 256 and the
+    partials merged) and a 12-node tree verified after it (keys of the prefix in two chunks, the
+    nodes' ancestor masks; a cache of 1,100 slots, so the tree takes the grouped kernel too):
+    every prompt row's logits and every node's logits and argmax against the oracle."""
+    from seedplane_b200.engine import CudaQwen2
+    cfg = PRESETS[name]
+    w = make_weights(cfg, seed=0, dtype=torch.float16, **TEST_INIT)
+    o = OracleQwen2(cfg, w, kv_fp16=True)
+    eng = CudaQwen2(cfg, w, device="cuda:0")
+    try:
+        prompt = random_prompt(cfg.vocab, 400, seed=9)
+        kv = eng.new_kv(1100)
+        logits, _ = eng.forward(kv, prompt, all_logits=True)
+        want_all, _ = o.forward(prompt, o.new_cache(512), all_logits=True)
+        _close(logits, want_all)
+        rng = np.random.default_rng(5)
+        parents = [-1] + [int(rng.integers(-1, i)) for i in range(1, 12)]
+        tokens = [int(t) for t in rng.integers(0, cfg.vocab, size=12)]
+        argmax, tl = eng.verify_tree(kv, tokens, parents, base_pos=len(prompt), want_logits=True)
+        for i in range(12):
+            path, j = [], i
+            while j >= 0:
+                path.append(tokens[j])
+                j = parents[j]
+            want = o.prefix_logits(prompt + path[::-1])
+            _close(tl[i], want)
+            assert int(argmax[i]) == int(want.argmax())
+        eng.status()
+    finally:
+        eng.close()
