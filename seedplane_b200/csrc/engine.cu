@@ -677,25 +677,28 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         lo[l].post = take(H * 4);
     }
     // row-major copies for the batched prompt pass: the fp16 weights, or for int8 checkpoints the
-    // dequantized weights times a power of two as exact fp16 hi / lo halves (4 bytes a weight)
+    // int8 rows and their block scales times a power of two (the GEMM dequantizes them on the chip
+    // into exact fp16 hi / lo halves): 1 + 1/16 bytes a weight
     e->prefill = !(getenv("SEEDPLANE_PREFILL") && strcmp(getenv("SEEDPLANE_PREFILL"), "steps") == 0);
     size_t o_head_rm = 0, o_head_rm_lo = 0;
+    auto kb64 = [](size_t K) { return (K + 63) / 64; };
     if (e->prefill) {
+        const size_t AQ = (size_t)c.heads * HD;
         for (int l = 0; l < c.layers; ++l) {
-            lo[l].rqkv = take(QR * H * 2);
-            lo[l].ro = take(H * (size_t)c.heads * HD * 2);
-            lo[l].rgu = take(2 * I * H * 2);
-            lo[l].rdn = take(H * I * 2);
-            if (i8) {
-                lo[l].rqkv_lo = take(QR * H * 2);
-                lo[l].ro_lo = take(H * (size_t)c.heads * HD * 2);
-                lo[l].rgu_lo = take(2 * I * H * 2);
-                lo[l].rdn_lo = take(H * I * 2);
+            lo[l].rqkv = take(QR * H * (i8 ? 1 : 2));
+            lo[l].ro = take(H * AQ * (i8 ? 1 : 2));
+            lo[l].rgu = take(2 * I * H * (i8 ? 1 : 2));
+            lo[l].rdn = take(H * I * (i8 ? 1 : 2));
+            if (i8) {                                   // scales [ceil(K / 64)][N][2] fp16
+                lo[l].rqkv_lo = take(kb64(H) * QR * 4);
+                lo[l].ro_lo = take(kb64(AQ) * H * 4);
+                lo[l].rgu_lo = take(kb64(H) * 2 * I * 4);
+                lo[l].rdn_lo = take(kb64(I) * H * 4);
             }
         }
         if (!c.tied_embeddings) {
-            o_head_rm = take(V * H * 2);
-            if (i8) o_head_rm_lo = take(V * H * 2);
+            o_head_rm = take(V * H * (i8 ? 1 : 2));
+            if (i8) o_head_rm_lo = take(kb64(H) * V * 4);
         }
     }
     e->arena_bytes = off;
@@ -778,12 +781,19 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
         mx = std::max(mx, mx2);
         int k = 0;
         if (mx > 0.f && std::isfinite(mx)) k = std::min(30, std::max(-30, (int)std::floor(std::log2(32768.0 / mx))));
-        __half *hi = (__half *)(A + hi_off), *lw = (__half *)(A + lo_off);
-        er = launch_dequant_hilo(hi, lw, (const int8_t *)q1, (const __half *)s1, rows1, K, k, q2 ? 2 : 1, 0, pair_hd, s);
+        if (k < 0) return cudaErrorInvalidValue;      // block scales above 2^15 / 127: not this format
+        int8_t *dq = (int8_t *)(A + hi_off);
+        __half *dsc = (__half *)(A + lo_off);
+        const int N = q2 ? rows1 + rows2 : rows1;
+        er = cudaMemsetAsync(dsc, 0, (size_t)((K + 63) / 64) * N * 4, s);
+        if (er == cudaSuccess)
+            er = launch_repack_i8(dq, dsc, (const int8_t *)q1, (const __half *)s1, rows1, N, K, k, q2 ? 2 : 1, 0,
+                                  pair_hd, s);
         if (er == cudaSuccess && q2)
-            er = launch_dequant_hilo(hi, lw, (const int8_t *)q2, (const __half *)s2, rows2, K, k, 2, 1, 0, s);
-        m.hi = hi;
-        m.lo = lw;
+            er = launch_repack_i8(dq, dsc, (const int8_t *)q2, (const __half *)s2, rows2, N, K, k, 2, 1, 0, s);
+        m = PrefillMat{};
+        m.q = dq;
+        m.sc = dsc;
         m.alpha = ldexpf(1.0f, -k);
         return er;
     };

@@ -299,10 +299,13 @@ struct PrefillDims {
     int hidden, inter, heads, kv_heads, head_dim, vocab, max_pos, max_tokens;
     float eps;
 };
-struct PrefillMat {                      // row-major fp16 weights W = alpha * (hi + lo)
+struct PrefillMat {                      // row-major weights W = alpha * (hi + lo), or alpha * q * sc
     const __half *hi;                    // fp16 checkpoints: the weights (alpha 1, no lo)
-    const __half *lo;                    // int8 checkpoints: the dequantized weights times 2^k split in two
-    float alpha;                         // fp16 halves (exact: q * scale has at most 19 significant bits)
+    const __half *lo;
+    float alpha;
+    const int8_t *q;                     // int8 checkpoints: the int8 rows [N][K] (hi, lo null) and their
+    const __half *sc;                    // 32-input block scales times 2^k, [ceil(K / 64)][N][2] fp16
+                                         // (exact); the GEMM splits q * sc into exact fp16 halves on the chip
 };
 struct PrefillLayer {
     PrefillMat qkv;                      // [(heads + 2 kv_heads) * head_dim, hidden], RoPE partners adjacent
@@ -311,12 +314,12 @@ struct PrefillLayer {
     PrefillMat down;                     // [hidden, inter]
     const float *qkv_b, *in_norm, *post_norm;
 };
-// Dequantize blockwise int8 rows (q [rows][K], fp16 scales [rows][K / 32]) into fp16 hi / lo halves
-// of w * 2^k: hi = fp16(w 2^k), lo = fp16(w 2^k - hi); source row r goes to row r * dst_mul + dst_add,
-// or, with pair_hd > 0 (the QKV projection), to its RoPE-pair position: row h * pair_hd + d goes to
-// h * pair_hd + 2 d (d < pair_hd / 2) or h * pair_hd + 2 (d - pair_hd / 2) + 1.
-cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                int dst_mul, int dst_add, int pair_hd, cudaStream_t s);
+// Blockwise int8 rows (q [rows][K], fp16 scales [rows][K / 32]) into the batched pass's int8 form:
+// source row r to row r * dst_mul + dst_add (or its RoPE-pair position, pair_hd > 0) of dq [N][K],
+// and the scales times 2^k (fp16; exact for k >= 0 below overflow) to dsc [ceil(K / 64)][N][2]
+// (zeroed first by the caller).
+cudaError_t launch_repack_i8(int8_t *dq, __half *dsc, const int8_t *q, const __half *scales, int rows, int N, int K,
+                             int k, int dst_mul, int dst_add, int pair_hd, cudaStream_t s);
 // Largest |scale| * 127 of a blockwise-int8 matrix (n fp16 scales), into *out (device float).
 cudaError_t launch_int8_absmax(float *out, const __half *scales, long long n, cudaStream_t s);
 struct PrefillScratch {
@@ -378,6 +381,8 @@ struct McolQkv {
 struct McolOp {
     int mode;                    // MC_STORE: y[t ldy + n] = ..; MC_RESID: += ..; MC_SWIGLU: see act_*
     const __half *w, *w_lo;      // w_lo: second weight half or null
+    const int8_t *wq;            // or int8 weights [N][K] with block scales wsc (PrefillMat::q, sc)
+    const __half *wsc;
     float alpha;
     int N, K;
     const __half *x;
@@ -393,6 +398,8 @@ struct McolOp {
 };
 struct McolParams {
     int N, K, T, tn, lo_row0, two_w, cs, stages, tmem_cols;   // cs: CTAs of a cluster splitting a tile
+    int i8w;                     // int8 weights: tiles dequantized into fp16 hi / lo on the chip
+    const __half *wsc;
     float alpha;
     float *y;
     int ldy;

@@ -53,6 +53,10 @@ constexpr int kMcMma = 5;
 constexpr int kBK = 64;                  // inputs per k-block: one 128-byte swizzle row of fp16
 constexpr int kBM = 128;
 constexpr int kATileBytes = kBM * kBK * 2;
+constexpr int kI8TileBytes = kBM * kBK;  // an int8 weight tile (rows of 64 bytes, no swizzle)
+constexpr int kABufs = 2;                // int8 weights: fp16 hi / lo tile buffers (the MMA's A operand)
+constexpr int kABufBytes = 2 * kATileBytes;
+constexpr int kScaleBytes = 1024;        // int8 weights: a stage's block scales (128 rows x 2 fp16), padded
 constexpr int kMcMaxStages = 12;
 constexpr int kMcMaxCluster = 8;         // portable cluster size
 constexpr uint32_t kMcSpin = 1u << 22;
@@ -216,7 +220,8 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     k_mcol(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
            const __grid_constant__ CUtensorMap tm_x, const McolParams p) {
     extern __shared__ uint8_t mc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[kMcMaxStages], empty[kMcMaxStages], accf[2], acce[2], drain;
+    __shared__ __align__(8) uint64_t full[kMcMaxStages], empty[kMcMaxStages], conv[kABufs], aempty[kABufs], accf[2],
+        acce[2], drain;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -238,7 +243,16 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         u1 = tiles * (blockIdx.x + 1) / gridDim.x * kbe;
     }
     const uint32_t base = (smem_u32(mc_smem_raw) + 1023u) & ~1023u;
-    const uint32_t stage_bytes = (uint32_t)(kATileBytes + 2 * TN * kBK * 2);
+    // a stage of the ring: the weight tile and the token tile. int8 weights: the token tile and the
+    // TMA's int8 tile, which the epilogue warps turn into fp16 hi / lo tiles in one of kABufs
+    // buffers ahead of the ring (a deep ring of 1-byte weights; the 4-byte tiles only where the MMA
+    // reads them)
+    const bool i8w = p.i8w != 0;
+    const uint32_t qbase = base + (i8w ? (uint32_t)(kABufs * kABufBytes) : 0u);
+    const uint32_t boff = i8w ? 0u : (uint32_t)kATileBytes;
+    const uint32_t qoff = boff + (uint32_t)(2 * TN * kBK * 2);
+    const uint32_t soff = qoff + (uint32_t)kI8TileBytes;              // int8: the tile's block scales
+    const uint32_t stage_bytes = i8w ? soff + (uint32_t)kScaleBytes : qoff;
     const Flag fl{&s_abort, p.st};
     if (tid == 0) mstamp(p.trace, 0);
 
@@ -247,6 +261,10 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < kABufs; ++i) {
+            mbar_init(&conv[i], kMcEpiThreads / 32);
+            mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&accf[i], 1);
@@ -272,6 +290,76 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     griddep_launch_dependents();
     if (tid == 0) mstamp(p.trace, 1);
 
+    // int8 weights, epilogue warps: the k-blocks [ua, ub) of the CTA's order, in the ring order of
+    // the producer and the MMA warp. Per stage: wait for the TMA, turn the int8 tile into the fp16
+    // hi / lo tiles, make the writes visible to the tensor core (fence.proxy.async) and arrive on
+    // conv[stage]. w = q * sc with sc the block scale times 2^k (fp16, exact): hi = fp16(q sc) and
+    // lo = fp16(q sc - hi), both single roundings of exact values (HMUL2 / HFMA2 on q as fp16, exact
+    // for an int8), the same halves fp32 arithmetic gives. q to fp16 two at a time: the bytes
+    // biased by 128 go into the mantissas of 1024.0 (0x64xx), then 1152 is subtracted (exact). The
+    // tiles are 128-byte swizzled like a TMA tile: 16-byte piece j of row r at
+    // r * 128 + ((j ^ (r & 7)) << 4). Thread item i of 512: row i / 4, inputs 16 (i % 4) .. + 15
+    // (a warp reads 512 contiguous bytes of the int8 tile).
+    int cv_s = 0, cv_a = 0;
+    uint32_t cv_ph = 0u, cv_aph[kABufs] = {0u, 0u};
+    long long cv_n = 0;
+    uint8_t *const gbase = mc_smem_raw + (base - smem_u32(mc_smem_raw));
+    const auto convert = [&](long long ua, long long ub) -> bool {
+        const __half2 bias = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
+        for (long long u = ua; u < ub; ++u) {
+            if (!wait_phase(&full[cv_s], cv_ph, fl)) return false;
+            if (cv_n >= kABufs) {                      // the MMAs that read this buffer are done
+                if (!wait_phase(&aempty[cv_a], cv_aph[cv_a], fl)) return false;
+                cv_aph[cv_a] ^= 1u;
+            }
+            const int mt = (int)(u / kbe) / ntiles;
+            const uint8_t *stg = gbase + (qbase - base) + (size_t)cv_s * stage_bytes;
+            uint8_t *abuf = gbase + (size_t)cv_a * kABufBytes;
+#pragma unroll
+            for (int j = 0; j < kBM * 4 / kMcEpiThreads; ++j) {
+                const int i = tid + j * kMcEpiThreads, r = i >> 2, c = i & 3;
+                const int n = mt * kBM + r;
+                const uint4 raw = *reinterpret_cast<const uint4 *>(stg + qoff + r * kBK + c * 16);
+                // the two block scales of the row's k-block (staged with the tile); this item's block is c / 2
+                const uint32_t sw = n < p.N ? *reinterpret_cast<const uint32_t *>(stg + soff + r * 4) : 0u;
+                const uint32_t sbits = __byte_perm(sw, 0u, (c >> 1) ? 0x3232u : 0x1010u);
+                const __half2 s2 = *reinterpret_cast<const __half2 *>(&sbits);
+                const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+                uint32_t hw[8], lw[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t x = words[e] ^ 0x80808080u;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t pb = __byte_perm(x, 0x64646464u, h ? 0x7362u : 0x5140u);
+                        const __half2 q2 = __hsub2(*reinterpret_cast<const __half2 *>(&pb), bias);
+                        const __half2 hi2 = __hmul2(q2, s2);
+                        const __half2 lo2 = __hfma2(q2, s2, __hneg2(hi2));
+                        hw[2 * e + h] = *reinterpret_cast<const uint32_t *>(&hi2);
+                        lw[2 * e + h] = *reinterpret_cast<const uint32_t *>(&lo2);
+                    }
+                }
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const uint32_t off = (uint32_t)(r * 128 + (((2 * c + hh) ^ (r & 7)) << 4));
+                    *reinterpret_cast<uint4 *>(abuf + off) = make_uint4(hw[4 * hh], hw[4 * hh + 1], hw[4 * hh + 2], hw[4 * hh + 3]);
+                    *reinterpret_cast<uint4 *>(abuf + kATileBytes + off) =
+                        make_uint4(lw[4 * hh], lw[4 * hh + 1], lw[4 * hh + 2], lw[4 * hh + 3]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[cv_a]);
+            if (++cv_s == S) {
+                cv_s = 0;
+                cv_ph ^= 1u;
+            }
+            cv_a = (cv_a + 1) % kABufs;
+            ++cv_n;
+        }
+        return true;
+    };
+
     if (warp == kMcProducer) {
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
@@ -284,19 +372,25 @@ __global__ void __launch_bounds__(kMcThreads, 1)
                 const int tile = (int)(u / kbe), kb = (int)(u % kbe);
                 const int mt = tile / ntiles, nt = tile % ntiles;
                 if (issued >= S && !wait_phase(&empty[s], ph ^ 1u, fl)) break;
-                const uint32_t st = base + (uint32_t)s * stage_bytes;
-                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                const uint32_t st = qbase + (uint32_t)s * stage_bytes;
+                // int8: the scales of the tile's rows below N (a multiple of 4 rows: 16-byte pieces)
+                const uint32_t sc_bytes = i8w ? (uint32_t)min(kBM, p.N - mt * kBM) * 4u : 0u;
+                mbar_arrive_expect_tx(&full[s], i8w ? qoff + (uint32_t)kI8TileBytes + sc_bytes : stage_bytes);
                 const bool second = kb >= kbx;
                 const int kx = (second ? kb - kbx : kb) * kBK;
-                tma_load_2d_hint(st, second ? &tm_w2 : &tm_w, kx, mt * kBM, &full[s], pol);
+                tma_load_2d_hint(i8w ? st + qoff : st, second ? &tm_w2 : &tm_w, kx, mt * kBM, &full[s], pol);
+                if (i8w)
+                    bulk_g2s_hint(mc_smem_raw + (st + soff - smem_u32(mc_smem_raw)),
+                                  reinterpret_cast<const uint8_t *>(p.wsc) + ((size_t)kb * p.N + (size_t)mt * kBM) * 4, sc_bytes,
+                                  &full[s], pol);
                 if (!waited) {
                     mstamp(p.trace, 2);
                     griddep_wait();
                     mstamp(p.trace, 3);
                     waited = true;
                 }
-                tma_load_2d(st + kATileBytes, &tm_x, kx, nt * TN, &full[s]);
-                tma_load_2d(st + kATileBytes + (uint32_t)(TN * kBK * 2), &tm_x, kx, p.lo_row0 + nt * TN, &full[s]);
+                tma_load_2d(st + boff, &tm_x, kx, nt * TN, &full[s]);
+                tma_load_2d(st + boff + (uint32_t)(TN * kBK * 2), &tm_x, kx, p.lo_row0 + nt * TN, &full[s]);
                 ++issued;
                 if (++s == S) {
                     s = 0;
@@ -311,8 +405,8 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     } else if (warp == kMcMma) {
         if (lane == 0) {
             const uint32_t idesc = idesc_m128(2 * TN);
-            int s = 0, buf = 0;
-            uint32_t ph = 0, eph[2] = {0u, 0u};
+            int s = 0, buf = 0, ab = 0;
+            uint32_t ph = 0, eph[2] = {0u, 0u}, cph[kABufs] = {0u, 0u};
             int nseg = 0;
             long long u = u0;
             while (u < u1 && !fl.on()) {
@@ -328,14 +422,27 @@ __global__ void __launch_bounds__(kMcThreads, 1)
                 bool first = true;
                 for (; u < v1; ++u) {
                     if (!wait_phase(&full[s], ph, fl)) break;
+                    if (i8w) {                              // and the stage's weights as fp16 hi / lo
+                        if (!wait_phase(&conv[ab], cph[ab], fl)) break;
+                        cph[ab] ^= 1u;
+                    }
                     if (u == u0) mstamp(p.trace, 4);
                     tc_fence_after();
-                    const uint32_t st = base + (uint32_t)s * stage_bytes;
-                    const uint64_t ad = smem_desc_sw128(st, 1024);
-                    const uint64_t bd = smem_desc_sw128(st + kATileBytes, 1024);
+                    const uint32_t st = qbase + (uint32_t)s * stage_bytes;
+                    const uint32_t at = i8w ? base + (uint32_t)(ab * kABufBytes) : st;
+                    const uint64_t ad = smem_desc_sw128(at, 1024);
+                    const uint64_t bd = smem_desc_sw128(st + boff, 1024);
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
                         mma_f16_id(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, first && k == 0 ? 0u : 1u);
+                    if (i8w) {                              // the lo tile into the same sums
+                        const uint64_t ad2 = smem_desc_sw128(at + kATileBytes, 1024);
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; ++k)
+                            mma_f16_id(acc, ad2 + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, 1u);
+                        mma_commit(&aempty[ab]);
+                        ab = (ab + 1) % kABufs;
+                    }
                     first = false;
                     mma_commit(&empty[s]);
                     if (++s == S) {
@@ -359,7 +466,11 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         int buf = 0;
         uint32_t fph[2] = {0u, 0u};
         const int slot0 = MODE == MC_QKV ? qkv_slot0(p) : 0;
+        // int8 weights: the next tile's k-blocks are dequantized before this tile's epilogue, so the
+        // MMAs of the next tile run while it is written
+        if (i8w && !convert(u0, min(u1, u0 + kbe))) u1 = u0;
         for (long long u = u0; u < u1 && !fl.on(); u += kbe) {
+            if (i8w && u + kbe < u1 && !convert(u + kbe, min(u1, u + 2 * kbe))) break;
             const int tile = (int)(u / kbe);
             const int mt = tile / ntiles, nt = tile % ntiles;
             const int n = mt * kBM + row;
@@ -403,6 +514,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         // P [row][TN] fp32 at the ring's start (every stage has been consumed once the accumulator is
         // committed: this CTA has exactly one segment)
         const int row = warp * 32 + lane;
+        if (i8w && !convert(u0, u1)) u1 = u0;
         if (u0 < u1 && wait_phase(&accf[0], 0u, fl)) {
             if (tid == 0) mstamp(p.trace, 6);
             tc_fence_after();
@@ -497,6 +609,22 @@ cudaError_t map_rows(CUtensorMap *m, const __half *ptr, int rows, int K, int box
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(ptr), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// A row-major int8 [rows, K] matrix as 64-input x box_rows tiles of 64-byte rows (no swizzle: the
+// epilogue warps read it and write the swizzled fp16 tiles), zeros outside.
+cudaError_t map_rows_i8(CUtensorMap *m, const int8_t *ptr, int rows, int K, int box_rows) {
+    EncodeTiled enc = encoder();
+    if (!enc) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) || K % 16 || box_rows < 8 || box_rows > 256) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
@@ -621,6 +749,10 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
         if (!a.lanes && (!a.slot_base || !a.kc || !a.vc || a.cap < op.T)) return cudaErrorInvalidValue;
         if (a.lanes && (!a.pos || a.layer < 0)) return cudaErrorInvalidValue;
     }
+    // int8: N a multiple of 4 (the block scales of a tile go by 16-byte bulk copies)
+    if (op.wq && (op.w || op.w_lo || !op.wsc || op.N % 4 || (reinterpret_cast<uintptr_t>(op.wsc) & 15u)))
+        return cudaErrorInvalidValue;
+    if (!op.wq && !op.w) return cudaErrorInvalidValue;
     McolParams p{};
     p.N = op.N;
     p.K = op.K;
@@ -628,6 +760,8 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     p.tn = mcol_tile_tokens(op.T);
     p.lo_row0 = op.lo_row0;
     p.two_w = op.w_lo != nullptr;
+    p.i8w = op.wq != nullptr;
+    p.wsc = op.wsc;
     p.alpha = op.alpha;
     p.y = op.y;
     p.ldy = op.ldy;
@@ -638,9 +772,10 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     p.qkv = op.qkv;
     p.trace = op.trace;
     p.tmem_cols = 4 * p.tn < 32 ? 32 : 4 * p.tn;
-    const int stage_bytes = kATileBytes + 2 * p.tn * kBK * 2;
+    const int stage_bytes = (p.i8w ? kI8TileBytes + kScaleBytes : kATileBytes) + 2 * p.tn * kBK * 2;
+    const size_t abytes = p.i8w ? (size_t)kABufs * kABufBytes : 0;       // int8: the hi / lo tile buffers
     static const int stage_cap = env_int("SEEDPLANE_MCOL_STAGES", kMcMaxStages);
-    const int fit = (int)((mcol_max_smem() - 1024) / stage_bytes);          // 1 KB: alignment
+    const int fit = (int)((mcol_max_smem() - 1024 - abytes) / stage_bytes);          // 1 KB: alignment
     p.stages = std::max(2, std::min(std::min(stage_cap, kMcMaxStages), fit));
     const long long mtiles = (op.N + kBM - 1) / kBM, ntiles = (op.T + p.tn - 1) / p.tn;
     const long long tiles = mtiles * ntiles;
@@ -651,7 +786,7 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     // of 8 fit than 148 / 8), which the occupancy query of the launch says.
     const int C = std::min(sm_count(), op.max_ctas);
     static const int cs_cap = std::max(1, std::min(kMcMaxCluster, env_int("SEEDPLANE_MCOL_CLUSTER", kMcMaxCluster)));
-    const size_t smem = (size_t)p.stages * stage_bytes + 1024;
+    const size_t smem = abytes + (size_t)p.stages * stage_bytes + 1024;
     p.cs = 1;
     if (2 * tiles <= C)
         for (int cs = cs_cap; cs >= 2; cs /= 2)
@@ -661,8 +796,13 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
             }
     const int grid = p.cs > 1 ? (int)(tiles * p.cs) : (int)std::min<long long>(C, tiles);
     CUtensorMap a, a2, x;
-    cudaError_t e = map_rows(&a, op.w, op.N, op.K, kBM);
-    if (e == cudaSuccess) e = map_rows(&a2, op.w_lo ? op.w_lo : op.w, op.N, op.K, kBM);
+    cudaError_t e = p.i8w ? map_rows_i8(&a, op.wq, op.N, op.K, kBM) : map_rows(&a, op.w, op.N, op.K, kBM);
+    if (e == cudaSuccess) {
+        if (p.i8w)
+            a2 = a;
+        else
+            e = map_rows(&a2, op.w_lo ? op.w_lo : op.w, op.N, op.K, kBM);
+    }
     if (e == cudaSuccess) e = map_rows(&x, op.x, op.x_rows, op.K, p.tn);
     if (e != cudaSuccess) return e;
     switch (op.mode) {

@@ -727,33 +727,23 @@ __global__ void k_batch_advance(BatchLane *lanes, int32_t *tok, int32_t *pos, co
     lanes[b].slot = min(ns, lanes[b].cap - 1);
 }
 
-// w = q * scale (exact in fp32), times 2^k (exact), split into fp16 hi = fp16(w') and lo =
-// fp16(w' - hi): hi + lo = w' exactly while w' and its remainder stay in fp16's normal range, which
-// the caller's k arranges for the matrix's largest weights. One thread per 8 inputs of a row.
-__global__ void k_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, float p2,
-                               int dst_mul, int dst_add, int pair_hd) {
+// The int8 rows and their scales for the batched pass (launch_repack_i8): one thread per 8 inputs
+// of a row; the thread of a 32-input block's first 8 writes its scale times 2^k.
+__global__ void k_repack_i8(int8_t *dq, __half *dsc, const int8_t *q, const __half *scales, int rows, int N, int K,
+                            float p2, int dst_mul, int dst_add, int pair_hd) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)rows * (K / 8)) return;
     const long long e0 = idx * 8;
     const long long r = e0 / K;
+    const int k0 = (int)(e0 - r * K);
     long long dr = r * dst_mul + dst_add;
     if (pair_hd > 0) {                                    // RoPE partners adjacent
         const long long hh = r / pair_hd, dd = r - hh * pair_hd;
         dr = hh * pair_hd + (dd < pair_hd / 2 ? 2 * dd : 2 * (dd - pair_hd / 2) + 1);
     }
-    const long long d0 = dr * K + (e0 - r * K);
-    const float sc = __half2float(scales[e0 / 32]) * p2;
-    const uint2 raw = *reinterpret_cast<const uint2 *>(q + e0);
-    const int8_t *b = reinterpret_cast<const int8_t *>(&raw);
-    __align__(16) __half h[8], l[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float w = (float)b[j] * sc;
-        h[j] = __float2half_rn(w);
-        l[j] = __float2half_rn(w - __half2float(h[j]));
-    }
-    *reinterpret_cast<uint4 *>(hi + d0) = *reinterpret_cast<const uint4 *>(h);
-    *reinterpret_cast<uint4 *>(lo + d0) = *reinterpret_cast<const uint4 *>(l);
+    *reinterpret_cast<uint2 *>(dq + dr * K + k0) = *reinterpret_cast<const uint2 *>(q + e0);
+    if ((k0 & 31) == 0)
+        dsc[((size_t)(k0 >> 6) * N + dr) * 2 + ((k0 >> 5) & 1)] = __float2half_rn(__half2float(scales[e0 / 32]) * p2);
 }
 
 // max |scale| over n fp16 scales, times 127, into *out (non-negative floats compare as unsigned)
@@ -803,6 +793,8 @@ McolOp proj(const PrefillDims &d, const PrefillScratch &s, const PrefillMat &w, 
     op.mode = mode;
     op.w = w.hi;
     op.w_lo = w.lo;
+    op.wq = w.q;
+    op.wsc = w.sc;
     op.alpha = w.alpha;
     op.N = N;
     op.K = K;
@@ -951,14 +943,14 @@ cudaError_t launch_prefill_logits(const PrefillDims &d, const PrefillScratch &s,
     return cudaGetLastError();
 }
 
-cudaError_t launch_dequant_hilo(__half *hi, __half *lo, const int8_t *q, const __half *scales, int rows, int K, int k,
-                                int dst_mul, int dst_add, int pair_hd, cudaStream_t s) {
-    if (K % 32 || k < -30 || k > 30 || dst_mul < 1 || dst_add < 0 || dst_add >= dst_mul || pair_hd < 0 || pair_hd % 2 ||
-        (pair_hd > 0 && (rows % pair_hd || dst_mul != 1)))
+cudaError_t launch_repack_i8(int8_t *dq, __half *dsc, const int8_t *q, const __half *scales, int rows, int N, int K,
+                             int k, int dst_mul, int dst_add, int pair_hd, cudaStream_t s) {
+    if (K % 32 || k < 0 || k > 30 || dst_mul < 1 || dst_add < 0 || dst_add >= dst_mul || pair_hd < 0 || pair_hd % 2 ||
+        (pair_hd > 0 && (rows % pair_hd || dst_mul != 1)) || (long long)(rows - 1) * dst_mul + dst_add >= N)
         return cudaErrorInvalidValue;
     const long long n = (long long)rows * (K / 8);
-    k_dequant_hilo<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(hi, lo, q, scales, rows, K, ldexpf(1.0f, k), dst_mul,
-                                                               dst_add, pair_hd);
+    k_repack_i8<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dq, dsc, q, scales, rows, N, K, ldexpf(1.0f, k), dst_mul,
+                                                            dst_add, pair_hd);
     return cudaGetLastError();
 }
 
