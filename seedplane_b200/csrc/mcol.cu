@@ -14,6 +14,7 @@
 //   warp 5   allocates TMEM and issues tcgen05.mma (M 128, N 2 TN, K 16; four per k-block) into one
 //            of two accumulators, commits each stage back to the producer and each finished
 //            accumulator to the epilogue
+//   warps 6-9  int8 weights only: each k-block's int8 tile and block scales into fp16 hi / lo tiles
 //   warps 0-3  epilogue: tcgen05.ld of the hi / lo columns and the fused epilogue of the op: store,
 //            residual add, SwiGLU of interleaved gate / up rows written as the down projection's
 //            fp16 hi / lo input, or QKV bias + RoPE + K/V cache write
@@ -46,7 +47,9 @@ namespace sp {
 
 namespace {
 
-constexpr int kMcThreads = 192;
+constexpr int kMcThreads = 320;         // warps 0-3 epilogue, 4 producer, 5 MMA, 6-9 int8 dequantization
+constexpr int kMcThreadsF16 = 192;      // fp16 weights: no dequantization warps
+constexpr int kMcConv0 = 6;
 constexpr int kMcEpiThreads = 128;
 constexpr int kMcProducer = 4;
 constexpr int kMcMma = 5;
@@ -215,8 +218,8 @@ SP_DEVINL void epilogue_one(const McolParams &p, float v, int n, int t, int lane
 
 }  // namespace
 
-template <int MODE>
-__global__ void __launch_bounds__(kMcThreads, 1)
+template <int MODE, bool I8>
+__global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
     k_mcol(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
            const __grid_constant__ CUtensorMap tm_x, const McolParams p) {
     extern __shared__ uint8_t mc_smem_raw[];
@@ -247,7 +250,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     // TMA's int8 tile, which the epilogue warps turn into fp16 hi / lo tiles in one of kABufs
     // buffers ahead of the ring (a deep ring of 1-byte weights; the 4-byte tiles only where the MMA
     // reads them)
-    const bool i8w = p.i8w != 0;
+    constexpr bool i8w = I8;               // the int8-weight build (dequantization warps 6-9)
     const uint32_t qbase = base + (i8w ? (uint32_t)(kABufs * kABufBytes) : 0u);
     const uint32_t boff = i8w ? 0u : (uint32_t)kATileBytes;
     const uint32_t qoff = boff + (uint32_t)(2 * TN * kBK * 2);
@@ -290,7 +293,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
     griddep_launch_dependents();
     if (tid == 0) mstamp(p.trace, 1);
 
-    // int8 weights, epilogue warps: the k-blocks [ua, ub) of the CTA's order, in the ring order of
+    // int8 weights, warps 6-9: the k-blocks [ua, ub) of the CTA's order, in the ring order of
     // the producer and the MMA warp. Per stage: wait for the TMA, turn the int8 tile into the fp16
     // hi / lo tiles, make the writes visible to the tensor core (fence.proxy.async) and arrive on
     // conv[stage]. w = q * sc with sc the block scale times 2^k (fp16, exact): hi = fp16(q sc) and
@@ -317,7 +320,7 @@ __global__ void __launch_bounds__(kMcThreads, 1)
             uint8_t *abuf = gbase + (size_t)cv_a * kABufBytes;
 #pragma unroll
             for (int j = 0; j < kBM * 4 / kMcEpiThreads; ++j) {
-                const int i = tid + j * kMcEpiThreads, r = i >> 2, c = i & 3;
+                const int i = (tid - kMcConv0 * 32) + j * kMcEpiThreads, r = i >> 2, c = i & 3;
                 const int n = mt * kBM + r;
                 const uint4 raw = *reinterpret_cast<const uint4 *>(stg + qoff + r * kBK + c * 16);
                 // the two block scales of the row's k-block (staged with the tile); this item's block is c / 2
@@ -460,17 +463,16 @@ __global__ void __launch_bounds__(kMcThreads, 1)
             mma_commit(&drain);
             mbar_wait_bounded(&drain, 0u);
         }
+    } else if (warp >= kMcConv0) {
+        // ---- int8 weights: every k-block of the CTA, as the ring brings them --------------------------
+        if constexpr (I8) convert(u0, u1);
     } else if (cs == 1) {
         // ---- whole tiles: thread = output row, 16 tokens per TMEM read ------------------------------
         const int row = warp * 32 + lane;
         int buf = 0;
         uint32_t fph[2] = {0u, 0u};
         const int slot0 = MODE == MC_QKV ? qkv_slot0(p) : 0;
-        // int8 weights: the next tile's k-blocks are dequantized before this tile's epilogue, so the
-        // MMAs of the next tile run while it is written
-        if (i8w && !convert(u0, min(u1, u0 + kbe))) u1 = u0;
         for (long long u = u0; u < u1 && !fl.on(); u += kbe) {
-            if (i8w && u + kbe < u1 && !convert(u + kbe, min(u1, u + 2 * kbe))) break;
             const int tile = (int)(u / kbe);
             const int mt = tile / ntiles, nt = tile % ntiles;
             const int n = mt * kBM + row;
@@ -514,7 +516,6 @@ __global__ void __launch_bounds__(kMcThreads, 1)
         // P [row][TN] fp32 at the ring's start (every stage has been consumed once the accumulator is
         // committed: this CTA has exactly one segment)
         const int row = warp * 32 + lane;
-        if (i8w && !convert(u0, u1)) u1 = u0;
         if (u0 < u1 && wait_phase(&accf[0], 0u, fl)) {
             if (tid == 0) mstamp(p.trace, 6);
             tc_fence_after();
@@ -646,29 +647,29 @@ int sm_count() {
 }
 
 // The kernel's dynamic shared-memory limit, raised once per device.
-template <int MODE>
+template <int MODE, bool I8>
 cudaError_t set_max_smem(int dev) {
     static std::atomic<unsigned long long> configured{0};       // one bit per device
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(configured.load() & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(k_mcol<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mcol_max_smem());
+        cudaError_t e = cudaFuncSetAttribute(k_mcol<MODE, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mcol_max_smem());
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
     return cudaSuccess;
 }
 
-template <int MODE>
+template <int MODE, bool I8>
 cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &x, const McolParams &p,
                         int grid, size_t smem, cudaStream_t s, bool pdl) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    e = set_max_smem<MODE>(dev);
+    e = set_max_smem<MODE, I8>(dev);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kMcThreads);
+    cfg.blockDim = dim3(I8 ? kMcThreads : kMcThreadsF16);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -687,17 +688,20 @@ cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &a2, const CUten
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, k_mcol<MODE>, a, a2, x, p);
+    return cudaLaunchKernelEx(&cfg, k_mcol<MODE, I8>, a, a2, x, p);
 }
 
-// Clusters of cs CTAs of k_mcol<mode> with `smem` bytes of dynamic shared memory that can be resident
-// at once on this device (cudaOccupancyMaxActiveClusters), cached per (device, mode, cs, smem).
-int max_active_clusters(int mode, int cs, size_t smem) {
+// Clusters of cs CTAs of k_mcol<mode> (`threads` a CTA) with `smem` bytes of dynamic shared memory that
+// can be resident at once on this device (cudaOccupancyMaxActiveClusters), cached per (device, mode,
+// cs, smem, threads).
+template <bool I8>
+int max_active_clusters_t(int mode, int cs, size_t smem) {
+    const int threads = I8 ? kMcThreads : kMcThreadsF16;
     static std::mutex mu;
-    static std::map<std::tuple<int, int, int, size_t>, int> cache;
+    static std::map<std::tuple<int, int, int, size_t, int>, int> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    const auto key = std::make_tuple(dev, mode, cs, smem);
+    const auto key = std::make_tuple(dev, mode, cs, smem, threads);
     {
         std::lock_guard<std::mutex> lk(mu);
         auto it = cache.find(key);
@@ -705,7 +709,7 @@ int max_active_clusters(int mode, int cs, size_t smem) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cs * kPrefillMaxCtas);
-    cfg.blockDim = dim3(kMcThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -717,10 +721,10 @@ int max_active_clusters(int mode, int cs, size_t smem) {
     int n = 0;
     cudaError_t e = cudaSuccess;
     switch (mode) {
-        case MC_STORE: e = set_max_smem<MC_STORE>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_STORE>, &cfg); break;
-        case MC_RESID: e = set_max_smem<MC_RESID>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_RESID>, &cfg); break;
-        case MC_SWIGLU: e = set_max_smem<MC_SWIGLU>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_SWIGLU>, &cfg); break;
-        default: e = set_max_smem<MC_QKV>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_QKV>, &cfg); break;
+        case MC_STORE: e = set_max_smem<MC_STORE, I8>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_STORE, I8>, &cfg); break;
+        case MC_RESID: e = set_max_smem<MC_RESID, I8>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_RESID, I8>, &cfg); break;
+        case MC_SWIGLU: e = set_max_smem<MC_SWIGLU, I8>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_SWIGLU, I8>, &cfg); break;
+        default: e = set_max_smem<MC_QKV, I8>(dev); if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, k_mcol<MC_QKV, I8>, &cfg); break;
     }
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
@@ -729,6 +733,9 @@ int max_active_clusters(int mode, int cs, size_t smem) {
     std::lock_guard<std::mutex> lk(mu);
     cache[key] = n;
     return n;
+}
+int max_active_clusters(int mode, int cs, size_t smem, bool i8) {
+    return i8 ? max_active_clusters_t<true>(mode, cs, smem) : max_active_clusters_t<false>(mode, cs, smem);
 }
 
 }  // namespace
@@ -790,7 +797,8 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     p.cs = 1;
     if (2 * tiles <= C)
         for (int cs = cs_cap; cs >= 2; cs /= 2)
-            if (tiles * cs <= C && cs <= kbe && tiles <= max_active_clusters(op.mode, cs, smem)) {
+            if (tiles * cs <= C && cs <= kbe &&
+                tiles <= max_active_clusters(op.mode, cs, smem, p.i8w != 0)) {
                 p.cs = cs;
                 break;
             }
@@ -805,11 +813,20 @@ cudaError_t launch_mcol(const McolOp &op, cudaStream_t s, bool pdl) {
     }
     if (e == cudaSuccess) e = map_rows(&x, op.x, op.x_rows, op.K, p.tn);
     if (e != cudaSuccess) return e;
+    if (p.i8w) {
+        switch (op.mode) {
+            case MC_STORE: return launch_mode<MC_STORE, true>(a, a2, x, p, grid, smem, s, pdl);
+            case MC_RESID: return launch_mode<MC_RESID, true>(a, a2, x, p, grid, smem, s, pdl);
+            case MC_SWIGLU: return launch_mode<MC_SWIGLU, true>(a, a2, x, p, grid, smem, s, pdl);
+            case MC_QKV: return launch_mode<MC_QKV, true>(a, a2, x, p, grid, smem, s, pdl);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (op.mode) {
-        case MC_STORE: return launch_mode<MC_STORE>(a, a2, x, p, grid, smem, s, pdl);
-        case MC_RESID: return launch_mode<MC_RESID>(a, a2, x, p, grid, smem, s, pdl);
-        case MC_SWIGLU: return launch_mode<MC_SWIGLU>(a, a2, x, p, grid, smem, s, pdl);
-        case MC_QKV: return launch_mode<MC_QKV>(a, a2, x, p, grid, smem, s, pdl);
+        case MC_STORE: return launch_mode<MC_STORE, false>(a, a2, x, p, grid, smem, s, pdl);
+        case MC_RESID: return launch_mode<MC_RESID, false>(a, a2, x, p, grid, smem, s, pdl);
+        case MC_SWIGLU: return launch_mode<MC_SWIGLU, false>(a, a2, x, p, grid, smem, s, pdl);
+        case MC_QKV: return launch_mode<MC_QKV, false>(a, a2, x, p, grid, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
