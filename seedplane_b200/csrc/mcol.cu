@@ -47,7 +47,9 @@ namespace sp {
 
 namespace {
 
-constexpr int kMcThreads = 320;         // warps 0-3 epilogue, 4 producer, 5 MMA, 6-9 int8 dequantization
+constexpr int kMcConvWarps = 4;         // int8 weights: dequantization warps (8 measured no faster)
+constexpr int kMcConvThreads = 32 * kMcConvWarps;
+constexpr int kMcThreads = 192 + kMcConvThreads;   // warps 0-3 epilogue, 4 producer, 5 MMA, 6.. dequantization
 constexpr int kMcThreadsF16 = 192;      // fp16 weights: no dequantization warps
 constexpr int kMcConv0 = 6;
 constexpr int kMcEpiThreads = 128;
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kABufs; ++i) {
-            mbar_init(&conv[i], kMcEpiThreads / 32);
+            mbar_init(&conv[i], kMcConvWarps);
             mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -306,7 +308,6 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
     int cv_s = 0, cv_a = 0;
     uint32_t cv_ph = 0u, cv_aph[kABufs] = {0u, 0u};
     long long cv_n = 0;
-    uint8_t *const gbase = mc_smem_raw + (base - smem_u32(mc_smem_raw));
     const auto convert = [&](long long ua, long long ub) -> bool {
         const __half2 bias = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
         for (long long u = ua; u < ub; ++u) {
@@ -316,18 +317,29 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
                 cv_aph[cv_a] ^= 1u;
             }
             const int mt = (int)(u / kbe) / ntiles;
-            const uint8_t *stg = gbase + (qbase - base) + (size_t)cv_s * stage_bytes;
-            uint8_t *abuf = gbase + (size_t)cv_a * kABufBytes;
+            const uint32_t stg = qbase + (uint32_t)cv_s * stage_bytes;     // shared-space addresses
+            const uint32_t abuf = base + (uint32_t)(cv_a * kABufBytes);
+            constexpr int NI = kBM * 4 / kMcConvThreads;         // items a thread
+            uint4 raw[NI];
+            uint32_t sw[NI];
 #pragma unroll
-            for (int j = 0; j < kBM * 4 / kMcEpiThreads; ++j) {
-                const int i = (tid - kMcConv0 * 32) + j * kMcEpiThreads, r = i >> 2, c = i & 3;
+            for (int j = 0; j < NI; ++j) {                       // every load first, then the math
+                const int i = (tid - kMcConv0 * 32) + j * kMcConvThreads, r = i >> 2, c = i & 3;
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(raw[j].x), "=r"(raw[j].y), "=r"(raw[j].z), "=r"(raw[j].w)
+                             : "r"(stg + qoff + (uint32_t)(r * kBK + c * 16)));
+                // the two block scales of the row's k-block (staged with the tile)
+                asm volatile("ld.shared.u32 %0, [%1];" : "=r"(sw[j]) : "r"(stg + soff + (uint32_t)(r * 4)));
+            }
+#pragma unroll
+            for (int j = 0; j < NI; ++j) {
+                const int i = (tid - kMcConv0 * 32) + j * kMcConvThreads, r = i >> 2, c = i & 3;
                 const int n = mt * kBM + r;
-                const uint4 raw = *reinterpret_cast<const uint4 *>(stg + qoff + r * kBK + c * 16);
-                // the two block scales of the row's k-block (staged with the tile); this item's block is c / 2
-                const uint32_t sw = n < p.N ? *reinterpret_cast<const uint32_t *>(stg + soff + r * 4) : 0u;
-                const uint32_t sbits = __byte_perm(sw, 0u, (c >> 1) ? 0x3232u : 0x1010u);
+                // this item's block is c / 2; rows past N read stale scale bytes: their int8 are zeros
+                // from the TMA, and a zero scale keeps them zero
+                const uint32_t sbits = n < p.N ? __byte_perm(sw[j], 0u, (c >> 1) ? 0x3232u : 0x1010u) : 0u;
                 const __half2 s2 = *reinterpret_cast<const __half2 *>(&sbits);
-                const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+                const uint32_t words[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
                 uint32_t hw[8], lw[8];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -345,9 +357,10 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const uint32_t off = (uint32_t)(r * 128 + (((2 * c + hh) ^ (r & 7)) << 4));
-                    *reinterpret_cast<uint4 *>(abuf + off) = make_uint4(hw[4 * hh], hw[4 * hh + 1], hw[4 * hh + 2], hw[4 * hh + 3]);
-                    *reinterpret_cast<uint4 *>(abuf + kATileBytes + off) =
-                        make_uint4(lw[4 * hh], lw[4 * hh + 1], lw[4 * hh + 2], lw[4 * hh + 3]);
+                    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(abuf + off), "r"(hw[4 * hh]),
+                                 "r"(hw[4 * hh + 1]), "r"(hw[4 * hh + 2]), "r"(hw[4 * hh + 3]) : "memory");
+                    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(abuf + (uint32_t)kATileBytes + off),
+                                 "r"(lw[4 * hh]), "r"(lw[4 * hh + 1]), "r"(lw[4 * hh + 2]), "r"(lw[4 * hh + 3]) : "memory");
                 }
             }
             fence_proxy_async_smem();
