@@ -206,21 +206,22 @@ SP_DEVINL void unit_i8_issue(uint32_t tmem, uint32_t unit, int rows_p, int nb, u
 // This thread's row (its TMEM lane) of one int8 unit of nb blocks (nb even): sum over blocks b of
 // row scale (sc2: fp16 pairs of blocks 2j, 2j + 1) * input block scale * (2^14 (128 d0 + d1) +
 // (128 d2 + d3)), the d's the block's digit columns 0-3 (the pairs are exact in s32), in fp32 and
-// block order. Whole warp (tcgen05.ld is warp-wide).
+// block order. Whole warp (tcgen05.ld is warp-wide): one 32-column load per 4 blocks (the
+// readout's cost follows the number of load instructions: x16 pairs were 2 % slower). A last pair
+// of blocks reads 16 columns past them, inside the unit's buffer.
 SP_DEVINL float unit_i8_row(uint32_t tmem_lane, const uint32_t (&sc2)[kUnitBlocksI8 / 2], int nb, const float *bsc) {
     float y = 0.f;
 #pragma unroll
     for (int b0 = 0; b0 < kUnitBlocksI8; b0 += 4) {
         if (b0 < nb) {                                          // warp-uniform
-            uint32_t v[2][16];
-            tmem_ld16_nowait(tmem_lane + (uint32_t)(8 * b0), v[0]);
-            if (b0 + 2 < nb) tmem_ld16_nowait(tmem_lane + (uint32_t)(8 * b0 + 16), v[1]);
+            uint32_t v[32];
+            tmem_ld32_nowait(tmem_lane + (uint32_t)(8 * b0), v);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int b = b0 + e;
                 if (b < nb) {
-                    const uint32_t *r = &v[e >> 1][8 * (e & 1)];
+                    const uint32_t *r = &v[8 * e];
                     const int hi = (int)r[0] * 128 + (int)r[1], lo = (int)r[2] * 128 + (int)r[3];
                     const float ds = fmaf(16384.f, (float)hi, (float)lo);
                     const __half2 s2 = *reinterpret_cast<const __half2 *>(&sc2[b >> 1]);
