@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
         }
     } else if (warp == kMcMma) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_m128(2 * TN);
+            const uint32_t idesc = idesc_m128(2 * TN), idesc_lo = idesc_m128(TN);
             int s = 0, buf = 0, ab = 0;
             uint32_t ph = 0, eph[2] = {0u, 0u}, cph[kABufs] = {0u, 0u};
             int nseg = 0;
@@ -451,11 +451,13 @@ __global__ void __launch_bounds__(I8 ? kMcThreads : kMcThreadsF16, 1)
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k)
                         mma_f16_id(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, first && k == 0 ? 0u : 1u);
-                    if (i8w) {                              // the lo tile into the same sums
+                    if (i8w) {
+                        // the lo tile times the tokens' hi rows only (N = TN: columns 0 .. TN - 1); lo x lo
+                        // is below 2^-22 of a product and is left out (a quarter of the MMA work)
                         const uint64_t ad2 = smem_desc_sw128(at + kATileBytes, 1024);
 #pragma unroll
                         for (int k = 0; k < kBK / 16; ++k)
-                            mma_f16_id(acc, ad2 + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, 1u);
+                            mma_f16_id(acc, ad2 + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc_lo, 1u);
                         mma_commit(&aempty[ab]);
                         ab = (ab + 1) % kABufs;
                     }
