@@ -992,10 +992,10 @@ int sp_engine_create(const sp_config *cfg, const sp_weights *w, int device, sp_e
                                                              : e->num_sms / c.kv_heads;
     e->step_group_chunks = std::max(1, std::min({kStepMaxChunks, group_cap, group_fit}));
     // default (measured on the Qwen2 shapes): grouped items from the first position when a group
-    // has 7 or more q heads (per-head items read every K/V row 7 times), else from 1,024 visible
-    // positions on (Qwen2-1.5B's 6-head groups: per-head items are 1 % faster at 512 positions,
-    // grouped ones 2 % at 1,024 and 13 % at 4,096)
-    const long group_dflt = c.heads / c.kv_heads >= 7 ? 0L : 1024L;
+    // has 7 or more q heads (per-head items read every K/V row 7 times), else from 640 visible
+    // positions on (Qwen2-1.5B's 6-head groups: per-head items are 0.3 % faster at 512-640
+    // positions, grouped ones 1.5 % at 768-896, 2 % at 1,024 and 13 % at 4,096)
+    const long group_dflt = c.heads / c.kv_heads >= 7 ? 0L : 640L;
     e->step_group_ctx = (int)std::max(0L, std::min<long>(INT_MAX, env_long("SEEDPLANE_ATTN_GROUP_CTX", group_dflt)));
     e->step_part_stride = std::max(e->step_max_chunks, e->step_group_chunks);
     const size_t w_cnt = wtake((size_t)e->n_cnt * 8), w_epoch = wtake(8);
