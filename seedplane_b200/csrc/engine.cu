@@ -171,6 +171,8 @@ struct sp_engine {
     PrefillMat head_pf{};                   // row-major LM head for the batched pass (the embedding when tied)
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
     double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
+    double *acc_rows = nullptr;             // stochastic acceptance: the visited rows' (max, S) and e_j, fp64
+    size_t acc_rows_bytes = 0;
     int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
     BatchIn *bt = nullptr;                  // batched decode inputs
     PrefillBatchIn *bp = nullptr;           // packed prompt pass inputs
@@ -1137,6 +1139,7 @@ void sp_engine_destroy(sp_engine *e) {
     cudaFree(e->mc_trace);
     cudaFree(e->vt);
     cudaFree(e->acc_scratch);
+    cudaFree(e->acc_rows);
     cudaFree(e->gr_buf);
     for (auto &g : e->bgraphs) cudaGraphExecDestroy(g.second);
     cudaFree(e->bt);
@@ -1737,19 +1740,40 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
     if (e->acc_vocab < vocab) {
         cudaFree(e->acc_scratch);
         e->acc_scratch = nullptr;
-        SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)vocab * 8 + (size_t)(4 * kSmallNodes + 8) * 4));
+        SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)vocab * 8 + (size_t)(6 * kSmallNodes + 16) * 4));
         e->acc_vocab = vocab;
     }
-    int32_t *dtok = reinterpret_cast<int32_t *>(e->acc_scratch + e->acc_vocab);
-    int32_t *dpar = dtok + kSmallNodes, *dout = dpar + kSmallNodes;
-    int32_t host[2 * kSmallNodes];
-    if (n > 0) {
-        memcpy(host, tokens_host, n * 4);
-        memcpy(host + kSmallNodes, parents_host, n * 4);
+    // the rows the walk can visit: the root's (0) and row i + 1 of every node i with children
+    int32_t host[4 * kSmallNodes + 2];
+    int32_t *h_tok = host, *h_par = host + kSmallNodes, *h_rows = h_par + kSmallNodes, *h_slot = h_rows + kSmallNodes + 1;
+    for (int r = 0; r <= n; ++r) h_slot[r] = -1;
+    int nr = 0;
+    h_slot[0] = nr;
+    h_rows[nr++] = 0;
+    for (int i = 0; i < n; ++i) {
+        h_tok[i] = tokens_host[i];
+        h_par[i] = parents_host[i];
+        const int row = parents_host[i] + 1;
+        if (h_slot[row] < 0) {
+            h_slot[row] = nr;
+            h_rows[nr++] = row;
+        }
     }
+    const size_t rows_bytes = ((size_t)4 * nr + (size_t)2 * nr * vocab) * 8;
+    if (e->acc_rows_bytes < rows_bytes) {
+        cudaFree(e->acc_rows);
+        e->acc_rows = nullptr;
+        e->acc_rows_bytes = 0;
+        SP_CUDA(cudaMalloc(&e->acc_rows, rows_bytes));
+        e->acc_rows_bytes = rows_bytes;
+    }
+    int32_t *dtok = reinterpret_cast<int32_t *>(e->acc_scratch + e->acc_vocab);
+    int32_t *dpar = dtok + kSmallNodes, *drows = dpar + kSmallNodes, *dslot = drows + kSmallNodes + 1;
+    int32_t *dout = dslot + kSmallNodes + 1;
     SP_CUDA(cudaMemcpyAsync(dtok, host, sizeof(host), cudaMemcpyHostToDevice, s));
-    SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, temperature, seed,
-                                     counter, e->acc_scratch, dout, s));
+    double *ms = e->acc_rows, *ev = e->acc_rows + 4 * nr;
+    SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, drows, dslot, nr,
+                                     temperature, seed, counter, e->acc_scratch, ms, ev, dout, s));
     SP_CUDA(cudaMemcpyAsync(out_host, dout, (size_t)(2 * n + 3) * 4, cudaMemcpyDeviceToHost, s));
     SP_CUDA(cudaStreamSynchronize(s));
     return SP_OK;

@@ -428,9 +428,13 @@ cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long 
 constexpr int kSampleFilterMaxVocab = 1 << 19;      // fixed-point mass sums stay below 2^63
 cudaError_t launch_sample_filter(const float *logits, int V, double temperature, int top_k, double top_p, float *z,
                                  cudaStream_t s);
+// Stochastic acceptance, launch arguments: rows [nr] = the logits rows the walk can visit (row 0
+// and the rows i + 1 of nodes i with children), slot [n + 1] = a row's index in rows (-1 if not
+// listed); fp64 scratch P [V], MS [2][nr][2], E [2][nr][V].
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
-                                     const int *parent, int n, double temperature, unsigned long long seed,
-                                     unsigned long long counter, double *scratch, int *out, cudaStream_t s);
+                                     const int *parent, int n, const int *rows, const int *slot, int nr,
+                                     double temperature, unsigned long long seed, unsigned long long counter,
+                                     double *P, double *MS, double *E, int *out, cudaStream_t s);
 // Greedy acceptance of a verified tree (one warp): pred [n] = target argmax after each node, ends
 // [n_paths] = last node of each draft path in input order; out [2 n + 5]: emitted count, accepted
 // count, chosen path, target token after a fully accepted path (else -1), emitted tokens (n + 1

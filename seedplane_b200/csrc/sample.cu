@@ -4,6 +4,7 @@
 // elements and an online (max, sum of exp) pair; the CTA merges the threads' lists by k rounds of
 // a block-wide argmax over the list heads. Order: larger value first, lower index on ties (the
 // greedy argmax's rule); NaN never enters a list.
+#include <algorithm>
 #include <cfloat>
 #include <climits>
 #include <cmath>
@@ -226,9 +227,44 @@ SP_DEVINL double block_max(const float *row, int V, double inv_t, double *s_part
     return mx;
 }
 
-__global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *tlog, const float *dlog, long long ld,
-                                                                   int V, const int *tok, const int *parent, int n,
-                                                                   double inv_t, unsigned long long seed,
+// ---- the rows' distributions ahead of the walk, over the whole GPU ---------------------------
+// The walk can visit the root's row and the rows of nodes with children (nr rows, rows[r] = the
+// logits row). For each and for both models (w = 0 target, 1 drafter): MS[w][r] = (max, S) and
+// E[w][r][j] = e_j, with the walk's own arithmetic (the same max, exponentials and block-ordered
+// sum), so every number the walk reads is the one it would have computed itself.
+SP_DEVINL const float *stoch_row(const float *tlog, const float *dlog, long long ld, const int *rows, int nr, int wr) {
+    return (wr < nr ? tlog : dlog) + (size_t)rows[wr % nr] * ld;
+}
+
+__global__ void __launch_bounds__(kAccThreads) k_stoch_max(const float *tlog, const float *dlog, long long ld, int V,
+                                                           const int *rows, int nr, double inv_t, double *MS) {
+    __shared__ double s_part[kAccThreads];
+    const double m = block_max(stoch_row(tlog, dlog, ld, rows, nr, blockIdx.x), V, inv_t, s_part);
+    if (threadIdx.x == 0) MS[2 * blockIdx.x] = m;
+}
+
+// grid (2 nr) x chunks: e_j of chunk c of row wr
+__global__ void __launch_bounds__(kAccThreads) k_stoch_exp(const float *tlog, const float *dlog, long long ld, int V,
+                                                           const int *rows, int nr, double inv_t, const double *MS,
+                                                           double *E) {
+    const int wr = blockIdx.y;
+    const float *row = stoch_row(tlog, dlog, ld, rows, nr, wr);
+    const double m = MS[2 * wr];
+    double *e = E + (size_t)wr * V;
+    for (int j = blockIdx.x * kAccThreads + threadIdx.x; j < V; j += gridDim.x * kAccThreads)
+        e[j] = dexp_ref(__dadd_rn(__dmul_rn((double)row[j], inv_t), -m));
+}
+
+__global__ void __launch_bounds__(kAccThreads) k_stoch_sum(int V, const double *E, double *MS) {
+    __shared__ double s_part[kAccThreads];
+    const double *e = E + (size_t)blockIdx.x * V;
+    const double S = block_sum([&](int j) { return e[j]; }, V, s_part);
+    if (threadIdx.x == 0) MS[2 * blockIdx.x + 1] = S;
+}
+
+__global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(int V, const int *tok, const int *parent, int n,
+                                                                   const int *slot, int nr, const double *MS,
+                                                                   const double *E, unsigned long long seed,
                                                                    unsigned long long counter, double *P, int *out) {
     __shared__ double s_part[kAccThreads];
     __shared__ int s_tok;
@@ -236,12 +272,10 @@ __global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *
     int cur = -1;                                         // -1: the root
     int n_out = 0, n_acc = 0;
     for (int depth = 0; depth <= n; ++depth) {
-        const float *tr = tlog + (size_t)(cur + 1) * ld, *dr = dlog + (size_t)(cur + 1) * ld;
-        const double mt = block_max(tr, V, inv_t, s_part), md = block_max(dr, V, inv_t, s_part);
-        const double St = block_sum([&](int j) { return dexp_ref(__dadd_rn(__dmul_rn((double)tr[j], inv_t), -mt)); }, V, s_part);
-        const double Sd = block_sum([&](int j) { return dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)); }, V, s_part);
-        for (int j = threadIdx.x; j < V; j += kAccThreads)
-            P[j] = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)tr[j], inv_t), -mt)), St);
+        const int r = slot[cur + 1];                          // a row the host listed (the root or a parent)
+        const double *et = E + (size_t)r * V, *ed = E + (size_t)(nr + r) * V;
+        const double St = MS[2 * r + 1], Sd = MS[2 * (nr + r) + 1];
+        for (int j = threadIdx.x; j < V; j += kAccThreads) P[j] = __ddiv_rn(et[j], St);
         __syncthreads();
         int next = -1;
         bool any_child = false;
@@ -249,19 +283,19 @@ __global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(const float *
             if (parent[c] != cur) continue;
             any_child = true;
             const int x = tok[c];
-            const double q = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[x], inv_t), -md)), Sd);
+            const double q = __ddiv_rn(ed[x], Sd);
             const double u = uniform53(rng);                  // the same in every thread
             const double px = P[x];
             if (u < __ddiv_rn(px, q)) {
                 next = c;
             } else {                                          // residual max(p - q, 0), normalised
                 const double Z = block_sum([&](int j) {
-                    const double qj = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)), Sd);
+                    const double qj = __ddiv_rn(ed[j], Sd);
                     return fmax(__dadd_rn(P[j], -qj), 0.0);
                 }, V, s_part);
                 if (Z > 0.0) {
                     for (int j = threadIdx.x; j < V; j += kAccThreads) {
-                        const double qj = __ddiv_rn(dexp_ref(__dadd_rn(__dmul_rn((double)dr[j], inv_t), -md)), Sd);
+                        const double qj = __ddiv_rn(ed[j], Sd);
                         P[j] = __ddiv_rn(fmax(__dadd_rn(P[j], -qj), 0.0), Z);
                     }
                 }
@@ -361,14 +395,31 @@ __global__ void __launch_bounds__(kFiltThreads) k_sample_filter(const float *log
         for (int shift = 24; shift >= 0; shift -= 8) {
             for (int b = tid; b < 256; b += kFiltThreads) s_bin[b] = 0ull;
             __syncthreads();
-            for (int j = tid; j < V; j += kFiltThreads) {
-                const float v = z[j];
-                const uint32_t key = order_key(v);
-                if (key >= lo && (key & pmask) == prefix) {
-                    const unsigned long long w =
-                        by_mass ? __double2ull_rn(exp((double)v - (double)mx) * kMassScale) : 1ull;
-                    if (w) atomicAdd(&s_bin[(key >> shift) & 255u], w);
+            // a warp's entries of one bin go in as one atomic (most entries share a few top bins, whose
+            // per-entry atomics serialised): the bin's lanes meet by __match_any_sync, the lowest adds
+            // their weights (integers: the sum does not depend on the order)
+            for (int j = tid; j - lane < V; j += kFiltThreads) {
+                uint32_t bin = 256u;
+                unsigned long long w = 0ull;
+                if (j < V) {
+                    const float v = z[j];
+                    const uint32_t key = order_key(v);
+                    if (key >= lo && (key & pmask) == prefix) {
+                        w = by_mass ? __double2ull_rn(exp((double)v - (double)mx) * kMassScale) : 1ull;
+                        if (w) bin = (key >> shift) & 255u;
+                    }
                 }
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                unsigned long long sum = 0ull;
+                if (by_mass) {
+                    for (int i = 0; i < 32; ++i) {
+                        const unsigned long long wi = __shfl_sync(0xffffffffu, w, i);
+                        if ((peers >> i) & 1u) sum += wi;
+                    }
+                } else {
+                    sum = (unsigned long long)__popc(peers);
+                }
+                if (bin < 256u && lane == __ffs(peers) - 1) atomicAdd(&s_bin[bin], sum);
             }
             __syncthreads();
             if (tid == 0) {
@@ -430,11 +481,16 @@ cudaError_t launch_sample_filter(const float *logits, int V, double temperature,
 }
 
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
-                                     const int *parent, int n, double temperature, unsigned long long seed,
-                                     unsigned long long counter, double *scratch, int *out, cudaStream_t s) {
-    if (V <= 0 || n < 0 || !(temperature > 0.0)) return cudaErrorInvalidValue;
-    k_accept_stochastic<<<1, kAccThreads, 0, s>>>(tlog, dlog, ld, V, tok, parent, n, 1.0 / temperature, seed, counter,
-                                                  scratch, out);
+                                     const int *parent, int n, const int *rows, const int *slot, int nr,
+                                     double temperature, unsigned long long seed, unsigned long long counter,
+                                     double *P, double *MS, double *E, int *out, cudaStream_t s) {
+    if (V <= 0 || n < 0 || nr < 1 || nr > n + 1 || !(temperature > 0.0)) return cudaErrorInvalidValue;
+    const double inv_t = 1.0 / temperature;
+    k_stoch_max<<<2 * nr, kAccThreads, 0, s>>>(tlog, dlog, ld, V, rows, nr, inv_t, MS);
+    const int chunks = std::max(1, std::min(64, (V + 8 * kAccThreads - 1) / (8 * kAccThreads)));
+    k_stoch_exp<<<dim3(chunks, 2 * nr), kAccThreads, 0, s>>>(tlog, dlog, ld, V, rows, nr, inv_t, MS, E);
+    k_stoch_sum<<<2 * nr, kAccThreads, 0, s>>>(V, E, MS);
+    k_accept_stochastic<<<1, kAccThreads, 0, s>>>(V, tok, parent, n, slot, nr, MS, E, seed, counter, P, out);
     return cudaGetLastError();
 }
 

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import argparse
 import json
+from dataclasses import replace
 import os
 import time
 
@@ -177,6 +178,51 @@ def tree_of(n: int, vocab: int, seed: int = 0, widths=(4, 2)):
     return tokens, parents
 
 
+def sampling_steps(eng, nodes: int, repeat: int, top_k: int = 50, top_p: float = 0.9, temperature: float = 0.8) -> dict:
+    """The device sampling path of one stochastic speculative round at the model's vocabulary, on
+    seeded random logits: the top-k / top-p filter of the root row (`sp_sample_filter`) and the
+    stochastic acceptance of a `nodes`-node tree (`sp_accept_stochastic`, target and drafter logits
+    [nodes + 1, V]). Device milliseconds per round over `repeat` rounds (CUDA events), then one
+    more round between cudaProfilerStart / Stop."""
+    from .speculative import FlatForest, accept_stochastic, sample_filter
+    V = eng.cfg.vocab
+    g = torch.Generator(device=eng.device).manual_seed(0)
+    tl = torch.randn((nodes + 1, V), generator=g, device=eng.device) * 3.0
+    dl = tl + 0.5 * torch.randn((nodes + 1, V), generator=g, device=eng.device)
+    tokens, parents = tree_of(nodes, V)
+    depths, node_paths = [], []
+    for t, par in zip(tokens, parents):
+        depths.append(1 if par < 0 else depths[par] + 1)
+        node_paths.append((node_paths[par] if par >= 0 else ()) + (t,))
+    leaves = [i for i in range(nodes) if i not in set(parents)]
+    flat = FlatForest(tuple(tokens), tuple(parents), tuple(depths), tuple(node_paths),
+                      tuple(node_paths[i] for i in leaves))
+    z = torch.empty((1, V), dtype=torch.float32, device=eng.device)
+
+    def round_(counter):
+        sample_filter(tl[0], temperature, top_k, top_p, out=z)
+        return accept_stochastic(eng, flat, tl, dl, temperature, seed=7, counter=counter)
+
+    first = round_(0)
+    torch.cuda.synchronize()
+    ms = None
+    if repeat:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(repeat):
+            round_(1 + i)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / repeat
+    torch.cuda.cudart().cudaProfilerStart()
+    round_(repeat + 1)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    eng.status()
+    return {"vocab": V, "nodes": nodes, "top_k": top_k, "top_p": top_p, "temperature": temperature,
+            "ms_per_round": ms, "first_round_emitted": list(first[0].emitted)}
+
+
 def batch_steps(eng, B: int, repeat: int) -> dict:
     """B requests (the burst's prompt lengths) prefilled together, then batched decode steps: device
     milliseconds per step over `repeat` steps, then one more inside the profiler range."""
@@ -291,6 +337,10 @@ def main():
                     help="instead of decoding one request: this many requests (prompts of 32..128 tokens, packed "
                          "into batched passes), then `--repeat` batched decode steps (sp_decode_batch) and one more "
                          "between cudaProfilerStart / Stop")
+    ap.add_argument("--sampling", type=int, default=0,
+                    help="instead of decoding: the device sampling path of a stochastic speculative round with a tree "
+                         "of this many nodes at the model's vocabulary (seeded random logits): `--repeat` rounds "
+                         "timed, one more between cudaProfilerStart / Stop")
     a = ap.parse_args()
     from .engine import CudaQwen2
     cfg = PRESETS[a.model]
@@ -300,6 +350,11 @@ def main():
         w = make_weights(cfg, seed=0, dtype=torch.float16)
     fmt = "i8" if a.int8 else "f16"
     prompt = random_prompt(cfg.vocab, a.prompt, seed=0)
+    if a.sampling:
+        tiny = PRESETS["tiny-hd64"]
+        eng = CudaQwen2(replace(tiny, vocab=cfg.vocab), make_weights(replace(tiny, vocab=cfg.vocab), seed=0, dtype=torch.float16))
+        print(json.dumps(sampling_steps(eng, a.sampling, a.repeat)))
+        return
     if a.verify:
         print(json.dumps(verify_passes(CudaQwen2(cfg, w, weight_format=fmt), prompt, a.verify, a.repeat, a.capacity)))
         return
