@@ -170,8 +170,8 @@ struct sp_engine {
     size_t pf_bytes = 0;
     PrefillMat head_pf{};                   // row-major LM head for the batched pass (the embedding when tied)
     VerifyIn *vt = nullptr;                 // device copy of the block inputs (tree verify, slot base)
-    double *acc_scratch = nullptr;          // stochastic acceptance: fp64 [vocab] + tree inputs / outputs
-    double *acc_rows = nullptr;             // stochastic acceptance: the visited rows' (max, S) and e_j, fp64
+    int32_t *acc_scratch = nullptr;         // stochastic acceptance: tree inputs / outputs
+    double *acc_rows = nullptr;             // stochastic acceptance: the visited rows' (max, S) and p / q, fp64
     size_t acc_rows_bytes = 0;
     int32_t *gr_buf = nullptr;              // greedy acceptance: tree, path ends and result
     BatchIn *bt = nullptr;                  // batched decode inputs
@@ -179,7 +179,6 @@ struct sp_engine {
     int32_t *last_only_buf = nullptr;       // sp_forward(all_logits = 2) through the step path: per-step argmaxes
     int32_t last_only_cap = 0;
     std::map<int, cudaGraphExec_t> bgraphs; // batched decode step per batch size
-    int acc_vocab = 0;
     int32_t *vt_argmax = nullptr;           // [kSmallNodes] argmax of a captured verify pass
     std::map<std::pair<sp_kv *, int>, cudaGraphExec_t> vgraphs;   // verify pass per (cache, nodes)
     unsigned long long *mc_trace = nullptr;  // SEEDPLANE_MCOL_TRACE: stamps of the last multi-column GEMM
@@ -1737,12 +1736,7 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
     }
     SP_CUDA(cudaSetDevice(e->device));
     cudaStream_t s = (cudaStream_t)stream;
-    if (e->acc_vocab < vocab) {
-        cudaFree(e->acc_scratch);
-        e->acc_scratch = nullptr;
-        SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)vocab * 8 + (size_t)(6 * kSmallNodes + 16) * 4));
-        e->acc_vocab = vocab;
-    }
+    if (!e->acc_scratch) SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)(6 * kSmallNodes + 16) * 4));
     // the rows the walk can visit: the root's (0) and row i + 1 of every node i with children
     int32_t host[4 * kSmallNodes + 2];
     int32_t *h_tok = host, *h_par = host + kSmallNodes, *h_rows = h_par + kSmallNodes, *h_slot = h_rows + kSmallNodes + 1;
@@ -1767,13 +1761,13 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
         SP_CUDA(cudaMalloc(&e->acc_rows, rows_bytes));
         e->acc_rows_bytes = rows_bytes;
     }
-    int32_t *dtok = reinterpret_cast<int32_t *>(e->acc_scratch + e->acc_vocab);
+    int32_t *dtok = e->acc_scratch;
     int32_t *dpar = dtok + kSmallNodes, *drows = dpar + kSmallNodes, *dslot = drows + kSmallNodes + 1;
     int32_t *dout = dslot + kSmallNodes + 1;
     SP_CUDA(cudaMemcpyAsync(dtok, host, sizeof(host), cudaMemcpyHostToDevice, s));
     double *ms = e->acc_rows, *ev = e->acc_rows + 4 * nr;
     SP_CUDA(launch_accept_stochastic(target_logits_dev, draft_logits_dev, ld, vocab, dtok, dpar, n, drows, dslot, nr,
-                                     temperature, seed, counter, e->acc_scratch, ms, ev, dout, s));
+                                     temperature, seed, counter, ms, ev, dout, s));
     SP_CUDA(cudaMemcpyAsync(out_host, dout, (size_t)(2 * n + 3) * 4, cudaMemcpyDeviceToHost, s));
     SP_CUDA(cudaStreamSynchronize(s));
     return SP_OK;

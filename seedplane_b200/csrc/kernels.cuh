@@ -421,20 +421,20 @@ constexpr int kTopkMax = 8;
 cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long ld, int k, int *idx, float *val,
                              float *lse, cudaStream_t s);
 
-// Stochastic acceptance of a draft tree (sample.cu): target / drafter logits [n + 1][ld] (row 0:
-// after the committed prefix, row i + 1: after node i), nodes (token, parent), fp64 scratch [V].
-// out [2n + 3]: emitted count, accepted count, emitted tokens [n + 1], accepted nodes [n].
 // top-k / top-p filter of one logits row (z = logits / T, dropped entries -inf); one CTA
 constexpr int kSampleFilterMaxVocab = 1 << 19;      // fixed-point mass sums stay below 2^63
 cudaError_t launch_sample_filter(const float *logits, int V, double temperature, int top_k, double top_p, float *z,
                                  cudaStream_t s);
-// Stochastic acceptance, launch arguments: rows [nr] = the logits rows the walk can visit (row 0
-// and the rows i + 1 of nodes i with children), slot [n + 1] = a row's index in rows (-1 if not
-// listed); fp64 scratch P [V], MS [2][nr][2], E [2][nr][V].
+// Stochastic acceptance of a draft tree (sample.cu): target / drafter logits [n + 1][ld] (row 0:
+// after the committed prefix, row i + 1: after node i), nodes (token, parent); out [2n + 3]:
+// emitted count, accepted count, emitted tokens [n + 1], accepted nodes [n]. rows [nr]: the logits
+// rows the walk can visit (row 0 and the rows i + 1 of nodes i with children); slot [n + 1]: a
+// row's index in rows (-1 if not listed); fp64 scratch MS [2][nr][2], E [2][nr][V] (the rows' p,
+// then q).
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
                                      const int *parent, int n, const int *rows, const int *slot, int nr,
                                      double temperature, unsigned long long seed, unsigned long long counter,
-                                     double *P, double *MS, double *E, int *out, cudaStream_t s);
+                                     double *MS, double *E, int *out, cudaStream_t s);
 // Greedy acceptance of a verified tree (one warp): pred [n] = target argmax after each node, ends
 // [n_paths] = last node of each draft path in input order; out [2 n + 5]: emitted count, accepted
 // count, chosen path, target token after a fully accepted path (else -1), emitted tokens (n + 1

@@ -262,42 +262,65 @@ __global__ void __launch_bounds__(kAccThreads) k_stoch_sum(int V, const double *
     if (threadIdx.x == 0) MS[2 * blockIdx.x + 1] = S;
 }
 
-__global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(int V, const int *tok, const int *parent, int n,
-                                                                   const int *slot, int nr, const double *MS,
-                                                                   const double *E, unsigned long long seed,
-                                                                   unsigned long long counter, double *P, int *out) {
+// the rows' probabilities in place: p_j = e_j / S (target rows), q_j = e_j / S (drafter rows)
+__global__ void __launch_bounds__(kAccThreads) k_stoch_div(int V, const double *MS, double *E) {
+    const int wr = blockIdx.y;
+    const double S = MS[2 * wr + 1];
+    double *e = E + (size_t)wr * V;
+    for (int j = blockIdx.x * kAccThreads + threadIdx.x; j < V; j += gridDim.x * kAccThreads) e[j] = __ddiv_rn(e[j], S);
+}
+
+// The walk's sums: the block structure of block_sum (256 contiguous blocks, each in index order, then
+// the block sums in order) with a CTA of kWalkThreads (threads 0-255 sum the blocks).
+constexpr int kWalkThreads = 1024;
+template <typename F>
+SP_DEVINL double walk_sum(F f, int V, double *s_part) {
+    if (threadIdx.x < kAccThreads) {
+        const int B = (V + kAccThreads - 1) / kAccThreads;
+        double acc = 0.0;
+        for (int i = 0; i < B; ++i) {
+            const int j = threadIdx.x * B + i;
+            if (j < V) acc = __dadd_rn(acc, f(j));
+        }
+        s_part[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    double tot = 0.0;
+    for (int t = 0; t < kAccThreads; ++t) tot = __dadd_rn(tot, s_part[t]);
+    __syncthreads();
+    return tot;
+}
+
+__global__ void __launch_bounds__(kWalkThreads) k_accept_stochastic(int V, const int *tok, const int *parent, int n,
+                                                                    const int *slot, int nr, double *E,
+                                                                    unsigned long long seed, unsigned long long counter,
+                                                                    int *out) {
     __shared__ double s_part[kAccThreads];
     __shared__ int s_tok;
     unsigned long long rng = seed ^ (counter * 0x9E3779B97F4A7C15ull);
     int cur = -1;                                         // -1: the root
     int n_out = 0, n_acc = 0;
     for (int depth = 0; depth <= n; ++depth) {
+        // the row's p (updated in place on rejections: a row is visited once) and q
         const int r = slot[cur + 1];                          // a row the host listed (the root or a parent)
-        const double *et = E + (size_t)r * V, *ed = E + (size_t)(nr + r) * V;
-        const double St = MS[2 * r + 1], Sd = MS[2 * (nr + r) + 1];
-        for (int j = threadIdx.x; j < V; j += kAccThreads) P[j] = __ddiv_rn(et[j], St);
-        __syncthreads();
+        double *P = E + (size_t)r * V;
+        const double *Q = E + (size_t)(nr + r) * V;
         int next = -1;
         bool any_child = false;
         for (int c = 0; c < n && next < 0; ++c) {
             if (parent[c] != cur) continue;
             any_child = true;
             const int x = tok[c];
-            const double q = __ddiv_rn(ed[x], Sd);
+            const double q = Q[x];
             const double u = uniform53(rng);                  // the same in every thread
             const double px = P[x];
             if (u < __ddiv_rn(px, q)) {
                 next = c;
             } else {                                          // residual max(p - q, 0), normalised
-                const double Z = block_sum([&](int j) {
-                    const double qj = __ddiv_rn(ed[j], Sd);
-                    return fmax(__dadd_rn(P[j], -qj), 0.0);
-                }, V, s_part);
+                const double Z = walk_sum([&](int j) { return fmax(__dadd_rn(P[j], -Q[j]), 0.0); }, V, s_part);
                 if (Z > 0.0) {
-                    for (int j = threadIdx.x; j < V; j += kAccThreads) {
-                        const double qj = __ddiv_rn(ed[j], Sd);
-                        P[j] = __ddiv_rn(fmax(__dadd_rn(P[j], -qj), 0.0), Z);
-                    }
+                    for (int j = threadIdx.x; j < V; j += kWalkThreads)
+                        P[j] = __ddiv_rn(fmax(__dadd_rn(P[j], -Q[j]), 0.0), Z);
                 }
                 __syncthreads();
             }
@@ -317,7 +340,7 @@ __global__ void __launch_bounds__(kAccThreads) k_accept_stochastic(int V, const 
         }
         // every child rejected (or none): draw from p
         const double u = uniform53(rng);
-        const double S = block_sum([&](int j) { return P[j]; }, V, s_part);
+        const double S = walk_sum([&](int j) { return P[j]; }, V, s_part);
         if (threadIdx.x == 0) {
             const double target = __dmul_rn(u, S);
             const int B = (V + kAccThreads - 1) / kAccThreads;
@@ -483,14 +506,15 @@ cudaError_t launch_sample_filter(const float *logits, int V, double temperature,
 cudaError_t launch_accept_stochastic(const float *tlog, const float *dlog, long long ld, int V, const int *tok,
                                      const int *parent, int n, const int *rows, const int *slot, int nr,
                                      double temperature, unsigned long long seed, unsigned long long counter,
-                                     double *P, double *MS, double *E, int *out, cudaStream_t s) {
+                                     double *MS, double *E, int *out, cudaStream_t s) {
     if (V <= 0 || n < 0 || nr < 1 || nr > n + 1 || !(temperature > 0.0)) return cudaErrorInvalidValue;
     const double inv_t = 1.0 / temperature;
     k_stoch_max<<<2 * nr, kAccThreads, 0, s>>>(tlog, dlog, ld, V, rows, nr, inv_t, MS);
     const int chunks = std::max(1, std::min(64, (V + 8 * kAccThreads - 1) / (8 * kAccThreads)));
     k_stoch_exp<<<dim3(chunks, 2 * nr), kAccThreads, 0, s>>>(tlog, dlog, ld, V, rows, nr, inv_t, MS, E);
     k_stoch_sum<<<2 * nr, kAccThreads, 0, s>>>(V, E, MS);
-    k_accept_stochastic<<<1, kAccThreads, 0, s>>>(V, tok, parent, n, slot, nr, MS, E, seed, counter, P, out);
+    k_stoch_div<<<dim3(chunks, 2 * nr), kAccThreads, 0, s>>>(V, MS, E);
+    k_accept_stochastic<<<1, kWalkThreads, 0, s>>>(V, tok, parent, n, slot, nr, E, seed, counter, out);
     return cudaGetLastError();
 }
 
