@@ -167,6 +167,10 @@ cudaError_t launch_topk_rows(const float *logits, int rows, int cols, long long 
 //   u: splitmix64 (Vigna) of seed ^ (counter * 0x9E3779B97F4A7C15) advanced once per draw, the
 //   top 53 bits times 2^-53; a draw from p walks the same blocks: the first index whose running
 //   sum exceeds u * S.
+// Launches: four grid-wide kernels give every row the walk can visit (the root's, and those of
+// nodes with children) its max, e_j, S and then p (target) or q (drafter) in place; the walk is
+// one CTA that reads them. It modifies a row's p in place when a child is rejected, which is safe
+// because it visits each row once.
 // ---------------------------------------------------------------------------------------------
 namespace {
 
