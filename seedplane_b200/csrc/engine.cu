@@ -1738,7 +1738,7 @@ int sp_accept_stochastic(sp_engine *e, const float *target_logits_dev, const flo
     cudaStream_t s = (cudaStream_t)stream;
     if (!e->acc_scratch) SP_CUDA(cudaMalloc(&e->acc_scratch, (size_t)(6 * kSmallNodes + 16) * 4));
     // the rows the walk can visit: the root's (0) and row i + 1 of every node i with children
-    int32_t host[4 * kSmallNodes + 2];
+    int32_t host[4 * kSmallNodes + 2] = {};
     int32_t *h_tok = host, *h_par = host + kSmallNodes, *h_rows = h_par + kSmallNodes, *h_slot = h_rows + kSmallNodes + 1;
     for (int r = 0; r <= n; ++r) h_slot[r] = -1;
     int nr = 0;
