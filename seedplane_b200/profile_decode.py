@@ -190,13 +190,14 @@ def sampling_steps(eng, nodes: int, repeat: int, top_k: int = 50, top_p: float =
     tl = torch.randn((nodes + 1, V), generator=g, device=eng.device) * 3.0
     dl = tl + 0.5 * torch.randn((nodes + 1, V), generator=g, device=eng.device)
     tokens, parents = tree_of(nodes, V)
-    depths, node_paths = [], []
-    for t, par in zip(tokens, parents):
+    # the tree as FlatForest fields: each root-to-leaf path as node ids and as tokens
+    depths, chains = [], []
+    for i, par in enumerate(parents):
         depths.append(1 if par < 0 else depths[par] + 1)
-        node_paths.append((node_paths[par] if par >= 0 else ()) + (t,))
+        chains.append((chains[par] if par >= 0 else ()) + (i,))
     leaves = [i for i in range(nodes) if i not in set(parents)]
-    flat = FlatForest(tuple(tokens), tuple(parents), tuple(depths), tuple(node_paths),
-                      tuple(node_paths[i] for i in leaves))
+    flat = FlatForest(tuple(tokens), tuple(parents), tuple(depths), tuple(chains[i] for i in leaves),
+                      tuple(tuple(tokens[j] for j in chains[i]) for i in leaves))
     z = torch.empty((1, V), dtype=torch.float32, device=eng.device)
 
     def round_(counter):
